@@ -1,0 +1,425 @@
+"""igllm_b200 - the B200 backend of the speculative verify round.
+
+Python face of libigllm_cuda (include/igllm_cuda.h), mirroring the reference
+engine's public API (iamhaymc/igllm app_core.c:158-425): the same entry
+names (model_load, session_open, prime, step, guess, guess_keep,
+guess_taste, pick, hold, scout_*), the same argument meaning and the same
+refusals.  A refused call raises IgcError carrying the reference's app_code.
+
+The library is built in-tree by igllm_b200/build.py; importing this module
+does not build it, and every entry fails loudly if it is missing.
+"""
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libigllm_cuda.so")
+
+OKAY = 0
+FAIL_ARGUMENT = -1
+FAIL_MEMORY = -2
+FAIL_FILE = -3
+FAIL_FORMAT = -4
+FAIL_MISSING = -5
+FAIL_SUPPORT = -6
+FAIL_STATE = -7
+FAIL_DEVICE = -8
+LANE_LIMIT = 16
+
+_CODE_TEXT = {  # app_core.c:12406 app_code_text
+    0: "okay", -1: "bad argument", -2: "out of memory", -3: "file not readable",
+    -4: "malformed data", -5: "required piece missing", -6: "unsupported configuration",
+    -7: "invalid state", -8: "device failure",
+}
+
+
+class IgcError(RuntimeError):
+    def __init__(self, code, where=""):
+        self.code = code
+        detail = _lib().igc_last_error().decode() if code == FAIL_DEVICE else ""
+        super().__init__(f"{where}: {_CODE_TEXT.get(code, code)} ({code}) {detail}".strip())
+
+
+class Setup(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int), ("window_limit", ctypes.c_int),
+                ("verbose_level", ctypes.c_int), ("cache_bits", ctypes.c_int)]
+
+
+class Taste(ctypes.Structure):  # app_core.c:60-67 app_taste
+    _fields_ = [("heat_value", ctypes.c_float), ("top_count", ctypes.c_int),
+                ("top_portion", ctypes.c_float), ("echo_penalty", ctypes.c_float),
+                ("echo_window", ctypes.c_int), ("seed_value", ctypes.c_uint64)]
+
+
+def taste_plain():
+    """app_core.c:12426 app_taste_plain."""
+    return Taste(1.0, 64, 0.95, 1.0, 64, 0x2545F4914F6CDD1D)
+
+
+class SynthSpec(ctypes.Structure):
+    _fields_ = [("vocab", ctypes.c_int), ("hidden", ctypes.c_int), ("layers", ctypes.c_int),
+                ("heads", ctypes.c_int), ("kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("inner", ctypes.c_int), ("ple_dim", ctypes.c_int), ("slide_span", ctypes.c_int),
+                ("share_count", ctypes.c_int), ("global_every", ctypes.c_int),
+                ("window_limit", ctypes.c_int), ("norm_offset", ctypes.c_float),
+                ("with_layer_scalar", ctypes.c_int), ("seed", ctypes.c_uint64)]
+
+
+def spec_e2b(norm_offset=0.0, seed=1, window_limit=32768):
+    """The benchmark shape: Gemma-4-E2B text stack with BASELINE's overrides
+    (global head 256, single-width feed-forward)."""
+    return SynthSpec(vocab=262144, hidden=1536, layers=35, heads=8, kv_heads=1, head_dim=256,
+                     inner=6144, ple_dim=256, slide_span=512, share_count=20, global_every=5,
+                     window_limit=window_limit, norm_offset=norm_offset, with_layer_scalar=0,
+                     seed=seed)
+
+
+class IgcPlane(ctypes.Structure):  # app_core.c:1775 plane
+    _fields_ = [("form", ctypes.c_int), ("row_count", ctypes.c_int), ("col_count", ctypes.c_int),
+                ("real_data", ctypes.c_void_p), ("real_type", ctypes.c_int),
+                ("code_data", ctypes.c_void_p), ("row_stride", ctypes.c_size_t),
+                ("gain_data", ctypes.c_void_p), ("gain_type", ctypes.c_int),
+                ("bias_data", ctypes.c_void_p), ("bit_count", ctypes.c_int),
+                ("code_bias", ctypes.c_int), ("code_flip", ctypes.c_int),
+                ("group_size", ctypes.c_int), ("group_count", ctypes.c_int),
+                ("enter_gain", ctypes.c_float), ("leave_gain", ctypes.c_float)]
+
+
+class _Desk(ctypes.Structure):
+    pass
+
+
+_P = ctypes.POINTER
+_f = _P(ctypes.c_float)
+_MATVEC = ctypes.CFUNCTYPE(None, _P(_Desk), _P(IgcPlane), _f, _f)
+_MATMAT = ctypes.CFUNCTYPE(None, _P(_Desk), _P(IgcPlane), _f, ctypes.c_int, ctypes.c_int, _f, ctypes.c_int)
+_NORM = ctypes.CFUNCTYPE(None, _P(_Desk), _f, _f, ctypes.c_int, ctypes.c_float, _f)
+_SOFT = ctypes.CFUNCTYPE(None, _P(_Desk), _f, ctypes.c_int)
+_GELU = ctypes.CFUNCTYPE(None, _P(_Desk), _f, _f, ctypes.c_int)
+_ROPE = ctypes.CFUNCTYPE(None, _P(_Desk), _f, ctypes.c_int, _f, _f)
+_Desk._fields_ = [("name_text", ctypes.c_char_p), ("state", ctypes.c_void_p), ("mat_vec", _MATVEC),
+                  ("mat_mat", _MATMAT), ("norm_rms", _NORM), ("soft_max", _SOFT), ("gelu_gate", _GELU),
+                  ("rope_turn", _ROPE)]
+
+_LIB = None
+
+
+def _lib():
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python igllm_b200/build.py`")
+    lib = ctypes.CDLL(LIB_PATH)
+    vp, i, i32p, fp = ctypes.c_void_p, ctypes.c_int, _P(ctypes.c_int32), _f
+    sig = {
+        "igc_model_load": (i, [ctypes.c_char_p, _P(Setup), _P(vp)]),
+        "igc_model_synth": (i, [_P(SynthSpec), _P(Setup), _P(vp)]),
+        "igc_model_free": (None, [vp]),
+        "igc_model_vocab_count": (i, [vp]),
+        "igc_model_layer_count": (i, [vp]),
+        "igc_model_state_size": (i, [vp]),
+        "igc_model_window_limit": (i, [vp]),
+        "igc_model_decode_bytes": (ctypes.c_size_t, [vp]),
+        "igc_model_device_bytes": (ctypes.c_size_t, [vp]),
+        "igc_session_open": (i, [vp, _P(vp)]),
+        "igc_session_close": (None, [vp]),
+        "igc_session_reset": (None, [vp]),
+        "igc_session_hold": (i, [vp, i]),
+        "igc_session_prime": (i, [vp, i32p, i]),
+        "igc_session_step": (i, [vp, ctypes.c_int32, fp, i32p]),
+        "igc_session_guess": (i, [vp, i32p, i, fp]),
+        "igc_session_guess_top": (i, [vp, i32p]),
+        "igc_session_guess_keep": (i, [vp, i]),
+        "igc_session_guess_taste": (i, [vp, i32p, i, _P(Taste), i32p]),
+        "igc_session_pick": (ctypes.c_int32, [vp, _P(Taste)]),
+        "igc_session_fill": (i, [vp]),
+        "igc_session_guess_span": (i, [vp]),
+        "igc_session_guess_limit": (i, [vp]),
+        "igc_session_round": (i, [vp, i32p, i, _P(Taste), i32p, i32p]),
+        "igc_session_serve_seconds": (ctypes.c_double, [vp]),
+        "igc_session_serve_tokens": (ctypes.c_size_t, [vp]),
+        "igc_scout_open": (i, [_P(vp)]),
+        "igc_scout_close": (None, [vp]),
+        "igc_scout_clear": (None, [vp]),
+        "igc_scout_note": (i, [vp, i32p, i]),
+        "igc_scout_span": (i, [vp]),
+        "igc_scout_draw": (i, [vp, i32p, i]),
+        "igc_synth_fill": (i, [ctypes.c_uint64, ctypes.c_uint64, i, ctypes.c_float, ctypes.c_size_t, vp, i]),
+        "igc_synth_write": (i, [_P(SynthSpec), ctypes.c_char_p, i]),
+        "igc_synth_stream": (ctypes.c_uint64, [ctypes.c_char_p]),
+        "igc_back_open": (i, [_P(_Desk), i]),
+        "igc_back_close": (None, [_P(_Desk)]),
+        "igc_desk_status": (i, [_P(_Desk)]),
+        "igc_last_error": (ctypes.c_char_p, []),
+        "igc_launch_count": (ctypes.c_long, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def exported_symbols():
+    """Names the library must export (every entry of include/igllm_cuda.h)."""
+    return [
+        "igc_back_open", "igc_back_close", "igc_desk_status", "igc_model_load", "igc_model_free",
+        "igc_model_vocab_count", "igc_model_layer_count", "igc_model_state_size",
+        "igc_model_window_limit", "igc_model_decode_bytes", "igc_model_device_bytes",
+        "igc_session_open", "igc_session_close", "igc_session_reset", "igc_session_hold",
+        "igc_session_prime", "igc_session_step", "igc_session_guess", "igc_session_guess_top",
+        "igc_session_guess_keep", "igc_session_guess_taste", "igc_session_pick", "igc_session_fill",
+        "igc_session_guess_span", "igc_session_guess_limit", "igc_session_round",
+        "igc_session_serve_seconds", "igc_session_serve_tokens", "igc_scout_open", "igc_scout_close",
+        "igc_scout_clear", "igc_scout_note", "igc_scout_span", "igc_scout_draw", "igc_synth_fill",
+        "igc_synth_write", "igc_model_synth", "igc_last_error", "igc_launch_count",
+    ]
+
+
+def _check(code, where):
+    if code != OKAY:
+        raise IgcError(code, where)
+
+
+def _ids(ids):
+    a = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
+    return a, a.ctypes.data_as(_P(ctypes.c_int32))
+
+
+def launch_count():
+    """Kernels this library launched on this thread since the last call."""
+    return _lib().igc_launch_count()
+
+
+class Model:
+    """app_core.c:12439 model_load (or a synthetic spec built straight in HBM)."""
+
+    def __init__(self, folder=None, spec=None, device=0, window_limit=0):
+        lib = _lib()
+        self._h = ctypes.c_void_p()
+        setup = Setup(device, window_limit, 0, 0)
+        if spec is not None:
+            _check(lib.igc_model_synth(ctypes.byref(spec), ctypes.byref(setup), ctypes.byref(self._h)),
+                   "model_synth")
+        else:
+            _check(lib.igc_model_load(str(folder).encode(), ctypes.byref(setup), ctypes.byref(self._h)),
+                   "model_load")
+
+    @property
+    def vocab(self):
+        return _lib().igc_model_vocab_count(self._h)
+
+    @property
+    def layers(self):
+        return _lib().igc_model_layer_count(self._h)
+
+    @property
+    def window_limit(self):
+        return _lib().igc_model_window_limit(self._h)
+
+    def decode_bytes(self):
+        return _lib().igc_model_decode_bytes(self._h)
+
+    def device_bytes(self):
+        return _lib().igc_model_device_bytes(self._h)
+
+    def close(self):
+        if self._h:
+            _lib().igc_model_free(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    """app_core.c:14219 session_open and the calls on a session."""
+
+    def __init__(self, model):
+        self.model = model
+        self._h = ctypes.c_void_p()
+        _check(_lib().igc_session_open(model._h, ctypes.byref(self._h)), "session_open")
+
+    def close(self):
+        if self._h:
+            _lib().igc_session_close(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def reset(self):
+        _lib().igc_session_reset(self._h)
+
+    @property
+    def fill(self):
+        return _lib().igc_session_fill(self._h)
+
+    def hold(self, keep):
+        _check(_lib().igc_session_hold(self._h, int(keep)), "session_hold")
+
+    def prime(self, ids):
+        a, p = _ids(ids)
+        _check(_lib().igc_session_prime(self._h, p, len(a)), "session_prime")
+
+    def step(self, id_value, want_logits=True):
+        """One id; returns (argmax id, logit row or None)."""
+        top = ctypes.c_int32()
+        row = np.empty(self.model.vocab, np.float32) if want_logits else None
+        rp = row.ctypes.data_as(_f) if want_logits else None
+        _check(_lib().igc_session_step(self._h, int(id_value), rp, ctypes.byref(top)), "session_step")
+        return top.value, row
+
+    def guess(self, ids, want_logits=True):
+        """A block of ids; returns the rows (K x vocab) or None."""
+        a, p = _ids(ids)
+        rows = np.empty((len(a), self.model.vocab), np.float32) if want_logits else None
+        rp = rows.ctypes.data_as(_f) if want_logits else None
+        _check(_lib().igc_session_guess(self._h, p, len(a), rp), "session_guess")
+        return rows
+
+    def guess_top(self):
+        out = np.empty(_lib().igc_session_guess_span(self._h), np.int32)
+        _check(_lib().igc_session_guess_top(self._h, out.ctypes.data_as(_P(ctypes.c_int32))), "guess_top")
+        return out
+
+    def guess_keep(self, keep):
+        _check(_lib().igc_session_guess_keep(self._h, int(keep)), "session_guess_keep")
+
+    def guess_taste(self, ids, taste):
+        a, p = _ids(ids)
+        made = ctypes.c_int32()
+        take = _lib().igc_session_guess_taste(self._h, p, len(a), ctypes.byref(taste), ctypes.byref(made))
+        if take < 0:
+            raise IgcError(FAIL_STATE, "session_guess_taste")
+        return take, made.value
+
+    def pick(self, taste):
+        return _lib().igc_session_pick(self._h, ctypes.byref(taste))
+
+    def round(self, ids, taste=None):
+        """guess + verify + keep; returns (take, made)."""
+        a, p = _ids(ids)
+        take, made = ctypes.c_int32(), ctypes.c_int32()
+        tp = ctypes.byref(taste) if taste is not None else None
+        n = _lib().igc_session_round(self._h, p, len(a), tp, ctypes.byref(take), ctypes.byref(made))
+        if n < 0:
+            raise IgcError(n, "session_round")
+        return take.value, made.value
+
+    def serve_seconds(self):
+        return _lib().igc_session_serve_seconds(self._h)
+
+    def serve_tokens(self):
+        return _lib().igc_session_serve_tokens(self._h)
+
+
+class Scout:
+    """app_core.c:12277-12361 the n-gram proposer (host C)."""
+
+    def __init__(self):
+        self._h = ctypes.c_void_p()
+        _check(_lib().igc_scout_open(ctypes.byref(self._h)), "scout_open")
+
+    def __del__(self):
+        try:
+            if self._h:
+                _lib().igc_scout_close(self._h)
+        except Exception:
+            pass
+
+    def clear(self):
+        _lib().igc_scout_clear(self._h)
+
+    def note(self, ids):
+        a, p = _ids(ids)
+        _check(_lib().igc_scout_note(self._h, p, len(a)), "scout_note")
+
+    @property
+    def span(self):
+        return _lib().igc_scout_span(self._h)
+
+    def draw(self, want):
+        out = np.zeros(max(int(want), 1), np.int32)
+        n = _lib().igc_scout_draw(self._h, out.ctypes.data_as(_P(ctypes.c_int32)), int(want))
+        return out[:n]
+
+
+class Desk:
+    """app_core.c:5222 back_desk on the GPU: host pointers in and out."""
+
+    def __init__(self, device=0):
+        self._d = _Desk()
+        _check(_lib().igc_back_open(ctypes.byref(self._d), device), "back_open")
+
+    def close(self):
+        if self._d.state:
+            _lib().igc_back_close(ctypes.byref(self._d))
+
+    def status(self):
+        return _lib().igc_desk_status(ctypes.byref(self._d))
+
+    def mat_mat(self, plane, act, lanes, out_rows):
+        act = np.ascontiguousarray(act, np.float32)
+        out = np.zeros((lanes, out_rows), np.float32)
+        self._d.mat_mat(ctypes.byref(self._d), ctypes.byref(plane), act.ctypes.data_as(_f),
+                        act.shape[-1], lanes, out.ctypes.data_as(_f), out_rows)
+        _check(self.status(), "desk.mat_mat")
+        return out
+
+    def norm_rms(self, x, w, eps):
+        x = np.ascontiguousarray(x, np.float32)
+        out = np.zeros_like(x)
+        wp = np.ascontiguousarray(w, np.float32).ctypes.data_as(_f) if w is not None else None
+        self._d.norm_rms(ctypes.byref(self._d), x.ctypes.data_as(_f), wp, len(x), eps, out.ctypes.data_as(_f))
+        _check(self.status(), "desk.norm_rms")
+        return out
+
+    def soft_max(self, x):
+        x = np.array(x, np.float32)
+        self._d.soft_max(ctypes.byref(self._d), x.ctypes.data_as(_f), len(x))
+        _check(self.status(), "desk.soft_max")
+        return x
+
+    def gelu_gate(self, gate, rise):
+        g = np.array(gate, np.float32)
+        r = np.ascontiguousarray(rise, np.float32)
+        self._d.gelu_gate(ctypes.byref(self._d), g.ctypes.data_as(_f), r.ctypes.data_as(_f), len(g))
+        _check(self.status(), "desk.gelu_gate")
+        return g
+
+    def rope_turn(self, x, cs, sn):
+        x = np.array(x, np.float32)
+        c = np.ascontiguousarray(cs, np.float32)
+        s = np.ascontiguousarray(sn, np.float32)
+        self._d.rope_turn(ctypes.byref(self._d), x.ctypes.data_as(_f), len(x), c.ctypes.data_as(_f),
+                          s.ctypes.data_as(_f))
+        _check(self.status(), "desk.rope_turn")
+        return x
+
+
+def synth_write(spec, folder, threads=8):
+    """Writes config.json, tokenizer.json and model.safetensors for `spec`."""
+    os.makedirs(folder, exist_ok=True)
+    _check(_lib().igc_synth_write(ctypes.byref(spec), str(folder).encode(), int(threads)), "synth_write")
+
+
+def synth_fill(seed, name, kind, count, offset=0.0, threads=1):
+    """The values of one synthetic tensor stream (kind 0 bytes, else u16 bits)."""
+    lib = _lib()
+    out = np.empty(count, np.uint8 if kind == 0 else np.uint16)
+    stream = lib.igc_synth_stream(name.encode())
+    _check(lib.igc_synth_fill(seed, stream, kind, offset, count, out.ctypes.data_as(ctypes.c_void_p), threads),
+           "synth_fill")
+    return out

@@ -1,0 +1,248 @@
+// igc_desk.cu - the device backend table: the six entries of the reference's
+// back_desk (app_core.c:5222-5245) with host pointers in and out.
+//
+// A code plane is uploaded the first time a product names it, keyed by its
+// code pointer, and reused afterwards: the "device handle beside each plane"
+// the reference's design notes ask for.  Each entry copies its activations
+// in, runs the same kernel the session pass runs, and copies the result out,
+// synchronously, so a reference build can swap its table for this one and
+// compare entry by entry.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/igllm_cuda.h"
+#include "igc_kernels.h"
+
+using namespace igc;
+
+namespace {
+
+struct DeskPlane {
+  uint4 *tiles = nullptr;
+  uint2 *scales = nullptr;
+  int n_rb = 0, n_cc = 0, rows = 0, cols = 0, split = 1, grid = 1;
+};
+
+struct DeskState {
+  int device = 0;
+  int sm_count = 148;
+  int smem_limit = 200 * 1024;
+  int status = IGC_OKAY;
+  cudaStream_t st = nullptr;
+  std::unordered_map<const void *, DeskPlane> planes;
+  float *buf_a = nullptr, *buf_b = nullptr, *buf_c = nullptr;
+  size_t buf_floats = 0;
+  float *arg_val = nullptr;
+  int *arg_idx = nullptr;
+};
+
+DeskState *state_of(igc_desk *d) { return static_cast<DeskState *>(d->state); }
+
+bool note(DeskState *s, int code) {
+  if (code != IGC_OKAY && s->status == IGC_OKAY) s->status = code;
+  return code == IGC_OKAY;
+}
+
+bool ok(DeskState *s, cudaError_t e) { return note(s, e == cudaSuccess ? IGC_OKAY : IGC_FAIL_DEVICE); }
+
+bool grow(DeskState *s, size_t floats) {
+  if (floats <= s->buf_floats) return true;
+  cudaFree(s->buf_a);
+  cudaFree(s->buf_b);
+  cudaFree(s->buf_c);
+  s->buf_a = s->buf_b = s->buf_c = nullptr;
+  if (!ok(s, cudaMalloc(&s->buf_a, floats * 4)) || !ok(s, cudaMalloc(&s->buf_b, floats * 4)) ||
+      !ok(s, cudaMalloc(&s->buf_c, floats * 4)))
+    return false;
+  s->buf_floats = floats;
+  return true;
+}
+
+// app_core.c:1775 plane, restricted to what the kernels read: 4-bit codes,
+// no flip, no zero points, groups of 32, f16 scales.
+const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
+  auto it = s->planes.find(p->code_data);
+  if (it != s->planes.end()) return &it->second;
+  if (p->form != 2 || p->bit_count != 4 || p->code_flip != 0 || p->bias_data || p->group_size != 32 ||
+      p->gain_type != 2 || p->code_bias != 8) {
+    note(s, IGC_FAIL_SUPPORT);
+    return nullptr;
+  }
+  DeskPlane dp;
+  dp.rows = p->row_count;
+  dp.cols = p->col_count;
+  dp.n_rb = (p->row_count + 15) / 16;
+  dp.n_cc = (p->col_count + 63) / 64;
+  size_t cb = (size_t)p->row_count * p->row_stride, sb = (size_t)p->row_count * p->group_count * 2;
+  uint8_t *dc = nullptr;
+  uint16_t *ds = nullptr;
+  if (!ok(s, cudaMalloc(&dp.tiles, (size_t)dp.n_rb * dp.n_cc * 512)) ||
+      !ok(s, cudaMalloc(&dp.scales, (size_t)dp.n_rb * dp.n_cc * 64)) || !ok(s, cudaMalloc(&dc, cb)) ||
+      !ok(s, cudaMalloc(&ds, sb)))
+    return nullptr;
+  bool good = ok(s, cudaMemcpy(dc, p->code_data, cb, cudaMemcpyHostToDevice)) &&
+              ok(s, cudaMemcpy(ds, p->gain_data, sb, cudaMemcpyHostToDevice)) &&
+              ok(s, igc_launch_repack(dc, p->row_stride, ds, p->group_count, p->row_count, p->col_count, dp.n_rb,
+                                      dp.n_cc, 1, 0, dp.tiles, dp.scales, s->st)) &&
+              ok(s, cudaStreamSynchronize(s->st));
+  cudaFree(dc);
+  cudaFree(ds);
+  if (!good) return nullptr;
+  int target = s->sm_count * GEMV_WARPS * 2;
+  while (dp.split < 8 && dp.split * 2 <= dp.n_cc && dp.n_rb * dp.split < target) dp.split *= 2;
+  int per_iter = GEMV_WARPS / dp.split;
+  dp.grid = (dp.n_rb + per_iter - 1) / per_iter;
+  if (dp.grid > s->sm_count * 4) dp.grid = s->sm_count * 4;
+  return &(s->planes[p->code_data] = dp);
+}
+
+void desk_mat_mat(igc_desk *d, const igc_plane *sheet, const float *act, int act_stride, int lanes, float *out,
+                  int out_stride) {
+  DeskState *s = state_of(d);
+  if (cudaSetDevice(s->device) != cudaSuccess) return void(note(s, IGC_FAIL_DEVICE));
+  const DeskPlane *p = plane_of(s, sheet);
+  if (!p) return;
+  for (int done = 0; done < lanes;) {  // app_core.c:5250: chunks of 16 lanes
+    int k = lanes - done < IGC_LANE_LIMIT ? lanes - done : IGC_LANE_LIMIT;
+    if (!grow(s, (size_t)IGC_LANE_LIMIT * (size_t)(p->cols > p->rows ? p->cols : p->rows))) return;
+    for (int j = 0; j < k; ++j)
+      if (!ok(s, cudaMemcpyAsync(s->buf_a + (size_t)j * p->cols, act + (size_t)(done + j) * act_stride,
+                                 sizeof(float) * p->cols, cudaMemcpyHostToDevice, s->st)))
+        return;
+    GemvArgs a;
+    memset(&a, 0, sizeof(a));
+    a.pl = GemvPlane{p->tiles, p->scales, p->n_rb, p->n_cc, p->rows, p->cols};
+    a.lanes = k;
+    a.split = p->split;
+    a.x = s->buf_a;
+    a.x_stride = p->cols;
+    a.out = s->buf_b;
+    a.out_stride = p->rows;
+    a.out_scale = 1.0f;
+    a.part_val = s->arg_val;
+    a.part_idx = s->arg_idx;
+    if (igc_gemv_smem(&a) > (size_t)s->smem_limit) {
+      // wide planes stage at most eight lanes at a time
+      int k8 = k < 8 ? k : 8;
+      for (int j0 = 0; j0 < k; j0 += k8) {
+        GemvArgs b = a;
+        b.lanes = k - j0 < k8 ? k - j0 : k8;
+        b.x = s->buf_a + (size_t)j0 * p->cols;
+        b.out = s->buf_b + (size_t)j0 * p->rows;
+        if (igc_gemv_smem(&b) > (size_t)s->smem_limit) return void(note(s, IGC_FAIL_SUPPORT));
+        if (!ok(s, igc_launch_gemv(&b, 0, PRO_F32, EPI_STORE, p->grid, s->st))) return;
+      }
+    } else if (!ok(s, igc_launch_gemv(&a, 0, PRO_F32, EPI_STORE, p->grid, s->st))) {
+      return;
+    }
+    for (int j = 0; j < k; ++j)
+      if (!ok(s, cudaMemcpyAsync(out + (size_t)(done + j) * out_stride, s->buf_b + (size_t)j * p->rows,
+                                 sizeof(float) * p->rows, cudaMemcpyDeviceToHost, s->st)))
+        return;
+    if (!ok(s, cudaStreamSynchronize(s->st))) return;
+    done += k;
+  }
+}
+
+void desk_mat_vec(igc_desk *d, const igc_plane *sheet, const float *act, float *out) {
+  desk_mat_mat(d, sheet, act, 0, 1, out, 0);
+}
+
+void desk_norm_rms(igc_desk *d, const float *x, const float *w, int n, float eps, float *out) {
+  DeskState *s = state_of(d);
+  if (cudaSetDevice(s->device) != cudaSuccess || !grow(s, (size_t)n)) return;
+  if (!ok(s, cudaMemcpyAsync(s->buf_a, x, sizeof(float) * n, cudaMemcpyHostToDevice, s->st))) return;
+  if (w && !ok(s, cudaMemcpyAsync(s->buf_c, w, sizeof(float) * n, cudaMemcpyHostToDevice, s->st))) return;
+  if (!ok(s, igc_launch_desk_norm(s->buf_a, w ? s->buf_c : nullptr, n, eps, s->buf_b, s->st))) return;
+  if (!ok(s, cudaMemcpyAsync(out, s->buf_b, sizeof(float) * n, cudaMemcpyDeviceToHost, s->st))) return;
+  ok(s, cudaStreamSynchronize(s->st));
+}
+
+void desk_soft_max(igc_desk *d, float *x, int n) {
+  DeskState *s = state_of(d);
+  if (cudaSetDevice(s->device) != cudaSuccess || !grow(s, (size_t)n)) return;
+  if (!ok(s, cudaMemcpyAsync(s->buf_a, x, sizeof(float) * n, cudaMemcpyHostToDevice, s->st))) return;
+  if (!ok(s, igc_launch_desk_softmax(s->buf_a, n, s->st))) return;
+  if (!ok(s, cudaMemcpyAsync(x, s->buf_a, sizeof(float) * n, cudaMemcpyDeviceToHost, s->st))) return;
+  ok(s, cudaStreamSynchronize(s->st));
+}
+
+void desk_gelu_gate(igc_desk *d, float *gate, const float *rise, int n) {
+  DeskState *s = state_of(d);
+  if (cudaSetDevice(s->device) != cudaSuccess || !grow(s, (size_t)n)) return;
+  if (!ok(s, cudaMemcpyAsync(s->buf_a, gate, sizeof(float) * n, cudaMemcpyHostToDevice, s->st))) return;
+  if (!ok(s, cudaMemcpyAsync(s->buf_b, rise, sizeof(float) * n, cudaMemcpyHostToDevice, s->st))) return;
+  if (!ok(s, igc_launch_desk_gelu(s->buf_a, s->buf_b, n, s->st))) return;
+  if (!ok(s, cudaMemcpyAsync(gate, s->buf_a, sizeof(float) * n, cudaMemcpyDeviceToHost, s->st))) return;
+  ok(s, cudaStreamSynchronize(s->st));
+}
+
+void desk_rope_turn(igc_desk *d, float *x, int head, const float *cs, const float *sn) {
+  DeskState *s = state_of(d);
+  int half = head / 2;
+  if (cudaSetDevice(s->device) != cudaSuccess || !grow(s, (size_t)head)) return;
+  if (!ok(s, cudaMemcpyAsync(s->buf_a, x, sizeof(float) * head, cudaMemcpyHostToDevice, s->st))) return;
+  if (!ok(s, cudaMemcpyAsync(s->buf_b, cs, sizeof(float) * half, cudaMemcpyHostToDevice, s->st))) return;
+  if (!ok(s, cudaMemcpyAsync(s->buf_c, sn, sizeof(float) * half, cudaMemcpyHostToDevice, s->st))) return;
+  if (!ok(s, igc_launch_desk_rope(s->buf_a, head, s->buf_b, s->buf_c, s->st))) return;
+  if (!ok(s, cudaMemcpyAsync(x, s->buf_a, sizeof(float) * head, cudaMemcpyDeviceToHost, s->st))) return;
+  ok(s, cudaStreamSynchronize(s->st));
+}
+
+}  // namespace
+
+extern "C" int igc_back_open(igc_desk *desk, int device) {
+  if (!desk) return IGC_FAIL_ARGUMENT;
+  memset(desk, 0, sizeof(*desk));
+  if (cudaSetDevice(device) != cudaSuccess) return IGC_FAIL_DEVICE;
+  DeskState *s = new DeskState();
+  s->device = device;
+  if (cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
+      cudaDeviceGetAttribute(&s->smem_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess ||
+      igc_kernels_configure(227 * 1024) != cudaSuccess ||
+      cudaMalloc(&s->arg_val, (size_t)s->sm_count * 4 * 16 * 4) != cudaSuccess ||
+      cudaMalloc(&s->arg_idx, (size_t)s->sm_count * 4 * 16 * 4) != cudaSuccess) {
+    delete s;
+    return IGC_FAIL_DEVICE;
+  }
+  s->smem_limit -= 2048;
+  desk->name_text = "cuda/sm_100a";
+  desk->state = s;
+  desk->mat_vec = desk_mat_vec;
+  desk->mat_mat = desk_mat_mat;
+  desk->norm_rms = desk_norm_rms;
+  desk->soft_max = desk_soft_max;
+  desk->gelu_gate = desk_gelu_gate;
+  desk->rope_turn = desk_rope_turn;
+  return IGC_OKAY;
+}
+
+extern "C" void igc_back_close(igc_desk *desk) {
+  if (!desk || !desk->state) return;
+  DeskState *s = state_of(desk);
+  cudaSetDevice(s->device);
+  for (auto &kv : s->planes) {
+    cudaFree(kv.second.tiles);
+    cudaFree(kv.second.scales);
+  }
+  cudaFree(s->buf_a);
+  cudaFree(s->buf_b);
+  cudaFree(s->buf_c);
+  cudaFree(s->arg_val);
+  cudaFree(s->arg_idx);
+  if (s->st) cudaStreamDestroy(s->st);
+  delete s;
+  desk->state = nullptr;
+}
+
+extern "C" int igc_desk_status(igc_desk *desk) {
+  if (!desk || !desk->state) return IGC_FAIL_ARGUMENT;
+  DeskState *s = state_of(desk);
+  int c = s->status;
+  s->status = IGC_OKAY;
+  return c;
+}

@@ -1,0 +1,97 @@
+// igc_device.cuh - device-side building blocks shared by the kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace igc {
+
+// One m16n8k16 tensor-core product, f16 inputs, f32 accumulate.
+// A: 16 weight rows x 16 input columns (4 regs of f16x2 per thread),
+// B: 16 input columns x 8 lanes (2 regs), C/D: 16 rows x 8 lanes (4 floats).
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1, const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%11,%12,%13};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+        "f"(c[2]), "f"(c[3]));
+}
+
+// Eight 4-bit codes (one 32-bit word, laid out by the upload repack) to the
+// four f16x2 A-fragment registers of one m16n8k16 product, each value being
+// code - 8 exactly.  Register k takes nibbles k and k+4 (bits 4k and 4k+16).
+// The lop3 masks put a nibble under the f16 exponent of 1024 (0x6400): the
+// low nibble of each half reads 1024 + n, the high one 1024 + 16 n; one
+// subtract or one fused multiply-add then leaves n - 8 with no rounding
+// (the integer-to-float construction of Kim et al., "Who Says Elephants
+// Can't Run", 2022).
+__device__ __forceinline__ void dequant_i4(uint32_t w, uint32_t (&a)[4]) {
+  const uint32_t lo_mask = 0x000f000fu, hi_mask = 0x00f000f0u, magic = 0x64006400u;
+  uint32_t w8 = w >> 8;
+  uint32_t t0, t1, t2, t3;
+  // (x & mask) | magic in one lop3: immLut = (0xF0 & 0xCC) | 0xAA = 0xEA
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(t0) : "r"(w), "r"(lo_mask), "r"(magic));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(t1) : "r"(w), "r"(hi_mask), "r"(magic));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(t2) : "r"(w8), "r"(lo_mask), "r"(magic));
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;\n" : "=r"(t3) : "r"(w8), "r"(hi_mask), "r"(magic));
+  const uint32_t sub_lo = 0x64086408u;  // 1032 = 1024 + 8
+  const uint32_t mul_hi = 0x2c002c00u;  // 1/16
+  const uint32_t add_hi = 0xd480d480u;  // -72 = -(64 + 8)
+  asm("sub.f16x2 %0, %1, %2;\n" : "=r"(a[0]) : "r"(t0), "r"(sub_lo));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(a[1]) : "r"(t1), "r"(mul_hi), "r"(add_hi));
+  asm("sub.f16x2 %0, %1, %2;\n" : "=r"(a[2]) : "r"(t2), "r"(sub_lo));
+  asm("fma.rn.f16x2 %0, %1, %2, %3;\n" : "=r"(a[3]) : "r"(t3), "r"(mul_hi), "r"(add_hi));
+}
+
+// Streaming 16-byte load that does not allocate in L1: every weight byte is
+// read exactly once per pass.
+__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint2 ld_stream2(const uint2 *p) {
+  uint2 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];\n"
+               : "=r"(r.x), "=r"(r.y)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// app_core.c:5109 kern_gelu_tanh: x * t / (t + 1), t = e^{2y}, y the tanh
+// argument; zero below the clamp, the clamp caps t above.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float root = 0.7978845608028654f, bend = 0.044715f, reach = 30.0f;
+  float cube = x * x * x;
+  float turn = 2.0f * root * (x + bend * cube);
+  if (!(turn > -reach)) return x * 0.0f;
+  if (turn > reach) turn = reach;
+  float rise = expf(turn);
+  return x * (rise / (rise + 1.0f));
+}
+
+// app_core.c:5016 kern_logit_cap_one
+__device__ __forceinline__ float logit_cap(float x, float cap) {
+  float t = x * (1.0f / cap);
+  t = fminf(fmaxf(t, -10.0f), 10.0f);
+  return cap * (1.0f - 2.0f / (expf(t + t) + 1.0f));
+}
+
+}  // namespace igc

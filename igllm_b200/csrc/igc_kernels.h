@@ -1,0 +1,43 @@
+// igc_kernels.h - host-side launchers of igc_kernels.cu.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "igc_gemv.cuh"
+
+extern "C" {
+
+cudaError_t igc_kernels_configure(int bytes);
+
+cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint16_t *scale, int groups,
+                              int rows, int cols, int n_rb, int n_cc, int out_mul, int out_add, uint4 *tiles,
+                              uint2 *scales, cudaStream_t st);
+
+cudaError_t igc_launch_gemv(const igc::GemvArgs *a, int pair, int pro, int epi, int grid, cudaStream_t st);
+size_t igc_gemv_smem(const igc::GemvArgs *a);
+
+cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
+                             const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
+                             float *x_out, float *seed_out, cudaStream_t st);
+cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes, int layers, int ple_dim,
+                                  const float *w, float eps, float blend, float *out, cudaStream_t st);
+cudaError_t igc_launch_attn_prep(float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
+                                 const float *k_norm, const float *cs, const float *sn, int owner, float eps,
+                                 const int *d_p0, int lanes, float *kc, float *vc, cudaStream_t st);
+size_t igc_attn_smem(int heads, int hd, int kv_w);
+cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int hd, const float *kc, const float *vc,
+                            int kv_w, int group, int sliding, int span, const int *d_p0, int lanes, int n_chunks,
+                            float *part_ml, float *part_acc, float *out, int out_stride, cudaStream_t st);
+cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
+                              cudaStream_t st);
+cudaError_t igc_launch_rope_table(const float *steps, int half, int window, float *cs, float *sn,
+                                  cudaStream_t st);
+cudaError_t igc_launch_topk(const float *logits, int vocab, int lanes, int keep, const int32_t *echo_ids,
+                            const int *echo_from, const int *echo_upto, float penalty, float *cand_v, int *cand_i,
+                            float *top_v, int *top_i, cudaStream_t st);
+cudaError_t igc_launch_desk_norm(const float *x, const float *w, int n, float eps, float *out, cudaStream_t st);
+cudaError_t igc_launch_desk_softmax(float *x, int n, cudaStream_t st);
+cudaError_t igc_launch_desk_gelu(float *gate, const float *rise, int n, cudaStream_t st);
+cudaError_t igc_launch_desk_rope(float *x, int head, const float *cs, const float *sn, cudaStream_t st);
+}

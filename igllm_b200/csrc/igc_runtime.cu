@@ -1,0 +1,1359 @@
+// igc_runtime.cu - model load and upload, sessions, the verify-round pass and
+// the C ABI of include/igllm_cuda.h.
+//
+// The pass follows app_core.c:11843 session_pass: embedding rows, the
+// per-layer-embedding lift, 35 layers of (attention, feed-forward,
+// per-layer-embedding feed), final norm, output head, logit cap.  Every step
+// is a kernel of igc_kernels.cu; norms and residual adds ride inside the
+// prologue of the projection that consumes them, so the residual stream is
+// read and written by the projections themselves.  The position a pass starts
+// at lives in device memory, which lets one captured CUDA graph per lane
+// count serve every position.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/igllm_cuda.h"
+#include "igc_json.h"
+#include "igc_kernels.h"
+#include "igc_synth.h"
+
+using namespace igc;
+
+// ---------------------------------------------------------------------------
+// errors and counters
+
+static thread_local std::string g_last_error;
+static thread_local long g_launches = 0;
+
+static int fail_device(cudaError_t e, const char *where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return IGC_FAIL_DEVICE;
+}
+
+#define CK(call)                                       \
+  do {                                                 \
+    cudaError_t e_ = (call);                           \
+    if (e_ != cudaSuccess) return fail_device(e_, #call); \
+  } while (0)
+
+#define CKL(call)                                      \
+  do {                                                 \
+    cudaError_t e_ = (call);                           \
+    ++g_launches;                                      \
+    if (e_ != cudaSuccess) return fail_device(e_, #call); \
+  } while (0)
+
+extern "C" const char *igc_last_error(void) { return g_last_error.c_str(); }
+extern "C" long igc_launch_count(void) {
+  long n = g_launches;
+  g_launches = 0;
+  return n;
+}
+
+// ---------------------------------------------------------------------------
+// tensor sources: a safetensors folder (mmap) or a synthetic spec
+
+enum { T_F32 = 1, T_F16 = 2, T_BF16 = 3, T_F64 = 4, T_I8 = 5, T_U8 = 6, T_I16 = 7, T_I32 = 8, T_I64 = 9 };
+
+struct Tensor {
+  int dtype = 0;
+  int rank = 0;
+  int64_t shape[4] = {0, 0, 0, 0};
+  const uint8_t *data = nullptr;
+  size_t bytes = 0;
+};
+
+static int dtype_of(const std::string &s) {
+  if (s == "F32") return T_F32;
+  if (s == "F16") return T_F16;
+  if (s == "BF16") return T_BF16;
+  if (s == "F64") return T_F64;
+  if (s == "I8") return T_I8;
+  if (s == "U8") return T_U8;
+  if (s == "I16") return T_I16;
+  if (s == "I32" || s == "U32") return T_I32;
+  if (s == "I64" || s == "U64") return T_I64;
+  return 0;
+}
+
+static size_t dtype_bytes(int t) {
+  switch (t) {
+    case T_F32: case T_I32: return 4;
+    case T_F16: case T_BF16: case T_I16: return 2;
+    case T_F64: case T_I64: return 8;
+    default: return 1;
+  }
+}
+
+static float f16_to_f32(uint16_t h) { return __half2float(*reinterpret_cast<const __half *>(&h)); }
+static float bf16_to_f32(uint16_t h) {
+  uint32_t u = (uint32_t)h << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+static float real_at(const Tensor &t, size_t i) { /* app_core.c:1719 real_read */
+  switch (t.dtype) {
+    case T_F32: { float f; memcpy(&f, t.data + 4 * i, 4); return f; }
+    case T_F16: { uint16_t h; memcpy(&h, t.data + 2 * i, 2); return f16_to_f32(h); }
+    case T_BF16: { uint16_t h; memcpy(&h, t.data + 2 * i, 2); return bf16_to_f32(h); }
+    case T_F64: { double d; memcpy(&d, t.data + 8 * i, 8); return (float)d; }
+    case T_I8: return (float)(int8_t)t.data[i];
+    case T_U8: return (float)t.data[i];
+    default: return 0.0f;
+  }
+}
+
+struct Source {
+  virtual ~Source() {}
+  virtual const Tensor *find(const std::string &name) = 0;
+  virtual void release(const std::string &) {}
+};
+
+struct FileMap {
+  void *base = nullptr;
+  size_t size = 0;
+  ~FileMap() {
+    if (base) munmap(base, size);
+  }
+};
+
+static bool slurp(const std::string &path, std::string &out) {
+  FILE *f = fopen(path.c_str(), "rb");
+  if (!f) return false;
+  fseek(f, 0, SEEK_END);
+  long n = ftell(f);
+  fseek(f, 0, SEEK_SET);
+  out.resize((size_t)(n > 0 ? n : 0));
+  size_t got = n > 0 ? fread(&out[0], 1, (size_t)n, f) : 0;
+  fclose(f);
+  return got == (size_t)(n > 0 ? n : 0);
+}
+
+// app_core.c:1634 store_open: model.safetensors, or every shard the index
+// names; tensors are views into the mapped files.
+struct SafeSource : Source {
+  std::vector<std::unique_ptr<FileMap>> maps;
+  std::unordered_map<std::string, Tensor> tensors;
+
+  int open_file(const std::string &path) {
+    int fd = ::open(path.c_str(), O_RDONLY);
+    if (fd < 0) return IGC_FAIL_FILE;
+    struct stat st;
+    if (fstat(fd, &st) != 0 || st.st_size < 8) { ::close(fd); return IGC_FAIL_FORMAT; }
+    auto fm = std::make_unique<FileMap>();
+    fm->size = (size_t)st.st_size;
+    fm->base = mmap(nullptr, fm->size, PROT_READ, MAP_PRIVATE, fd, 0);
+    ::close(fd);
+    if (fm->base == MAP_FAILED) { fm->base = nullptr; return IGC_FAIL_FILE; }
+    const uint8_t *b = (const uint8_t *)fm->base;
+    uint64_t hl;
+    memcpy(&hl, b, 8);
+    if (hl > fm->size - 8) return IGC_FAIL_FORMAT;
+    Json head;
+    JsonReader rd((const char *)b + 8, (size_t)hl);
+    if (!rd.parse(head) || head.kind != Json::OBJ) return IGC_FAIL_FORMAT;
+    const uint8_t *data = b + 8 + hl;
+    size_t data_size = fm->size - 8 - hl;
+    for (auto &kv : head.obj) {
+      if (kv.first == "__metadata__") continue;
+      const Json &j = kv.second;
+      Tensor t;
+      t.dtype = dtype_of(j.text("dtype", ""));
+      const Json *sh = j.get("shape");
+      const Json *off = j.get("data_offsets");
+      if (!t.dtype || !sh || !off || off->kind != Json::ARR || off->arr.size() != 2) return IGC_FAIL_FORMAT;
+      t.rank = (int)sh->arr.size();
+      if (t.rank > 4) return IGC_FAIL_SUPPORT;
+      for (int i = 0; i < t.rank; ++i) t.shape[i] = (int64_t)sh->arr[i].num;
+      size_t a = (size_t)off->arr[0].num, e = (size_t)off->arr[1].num;
+      if (e < a || e > data_size) return IGC_FAIL_FORMAT;
+      t.data = data + a;
+      t.bytes = e - a;
+      tensors[kv.first] = t;
+    }
+    maps.push_back(std::move(fm));
+    return IGC_OKAY;
+  }
+
+  int open(const std::string &folder) {
+    std::string index;
+    if (slurp(folder + "/model.safetensors.index.json", index)) {
+      Json j;
+      JsonReader rd(index.data(), index.size());
+      if (!rd.parse(j)) return IGC_FAIL_FORMAT;
+      const Json *wm = j.get("weight_map");
+      if (!wm || wm->kind != Json::OBJ) return IGC_FAIL_FORMAT;
+      std::map<std::string, int> files;
+      for (auto &kv : wm->obj) files[kv.second.str] = 1;
+      for (auto &f : files) {
+        int c = open_file(folder + "/" + f.first);
+        if (c != IGC_OKAY) return c;
+      }
+      return IGC_OKAY;
+    }
+    return open_file(folder + "/model.safetensors");
+  }
+
+  const Tensor *find(const std::string &name) override {
+    auto it = tensors.find(name);
+    return it == tensors.end() ? nullptr : &it->second;
+  }
+};
+
+// A synthetic checkpoint: tensors generated on first use, dropped on release.
+struct SynthSource : Source {
+  igc_synth_spec spec;
+  std::unordered_map<std::string, igc_synth_tensor> list;
+  std::unordered_map<std::string, std::pair<std::vector<uint8_t>, Tensor>> made;
+  int threads = 8;
+
+  explicit SynthSource(const igc_synth_spec &s) : spec(s) {
+    int n = igc_synth_list(&spec, nullptr, 0);
+    std::vector<igc_synth_tensor> v((size_t)n);
+    igc_synth_list(&spec, v.data(), n);
+    for (auto &t : v) list[t.name] = t;
+    long cpus = sysconf(_SC_NPROCESSORS_ONLN);
+    threads = cpus > 0 ? (int)(cpus > 32 ? 32 : cpus) : 8;
+  }
+  const Tensor *find(const std::string &name) override {
+    auto m = made.find(name);
+    if (m != made.end()) return &m->second.second;
+    auto it = list.find(name);
+    if (it == list.end()) return nullptr;
+    const igc_synth_tensor &st = it->second;
+    auto &slot = made[name];
+    slot.first.resize(st.bytes);
+    igc_synth_tensor_fill(&spec, &st, slot.first.data(), threads);
+    Tensor &t = slot.second;
+    t.dtype = st.dtype;
+    t.rank = st.rank;
+    t.shape[0] = st.shape[0];
+    t.shape[1] = st.shape[1];
+    t.data = slot.first.data();
+    t.bytes = st.bytes;
+    return &t;
+  }
+  void release(const std::string &name) override { made.erase(name); }
+};
+
+// ---------------------------------------------------------------------------
+// the model
+
+struct RopeForm {
+  double theta = 10000.0, share = 1.0;
+  bool proportional = false;
+};
+
+struct DevPlane {
+  uint4 *tiles = nullptr;
+  uint2 *scales = nullptr;
+  int n_rb = 0, n_cc = 0, rows = 0, cols = 0;
+  int split = 1, grid = 1;
+  bool pair = false;
+  GemvPlane view() const { return GemvPlane{tiles, scales, n_rb, n_cc, rows, cols}; }
+};
+
+struct DevLayer {
+  int kind = 0, share = 0, source = -1, hd = 0, kv_heads = 1, inner = 0;
+  int q_rows = 0, kv_rows = 0, qkv_rows = 0;
+  float gain = 1.0f;
+  DevPlane qkv, o, gateup, down, ple_gate, ple_proj;
+  float *q_norm = nullptr, *k_norm = nullptr, *enter_norm = nullptr, *after_attn_norm = nullptr,
+        *before_feed_norm = nullptr, *after_feed_norm = nullptr, *after_ple_norm = nullptr;
+};
+
+struct igc_model {
+  int device = 0, sm_count = 148, smem_limit = 227 * 1024;
+  int vocab = 0, hidden = 0, layers = 0, heads = 0, kv_heads = 1, inner = 0, ple_dim = 0, ple_vocab = 0;
+  int slide_span = 512, window_limit = 0, share_count = 0, pad_id = 0;
+  float eps = 1e-6f, softcap = 0.0f;
+  int kind[128] = {0};
+  RopeForm rope[2];
+  int rope_hd[2] = {0, 0};
+  float *rope_cs[2] = {nullptr, nullptr}, *rope_sn[2] = {nullptr, nullptr};
+  uint16_t *embed = nullptr, *ple_embed = nullptr;
+  DevPlane ple_lift, head;
+  float *ple_norm = nullptr, *final_norm = nullptr;
+  std::vector<DevLayer> layer;
+  size_t decode_bytes = 0, device_bytes = 0;
+  int max_qkv = 0, max_inner = 0, max_q = 0, max_kvw = 0;
+  std::vector<void *> owned;
+
+  ~igc_model() {
+    cudaSetDevice(device);
+    for (void *p : owned) cudaFree(p);
+  }
+  template <typename T>
+  int alloc(T **p, size_t count) {
+    void *v = nullptr;
+    size_t bytes = count * sizeof(T);
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess) return fail_device(e, "cudaMalloc(model)");
+    owned.push_back(v);
+    device_bytes += bytes;
+    *p = (T *)v;
+    return IGC_OKAY;
+  }
+};
+
+static int layer_of_config(const Json &tc, int layers, int l) {
+  const Json *lt = tc.get("layer_types");
+  if (l == layers - 1) return 1; /* app_core.c:8395 */
+  if (lt && lt->kind == Json::ARR && (size_t)l < lt->arr.size() && lt->arr[l].kind == Json::STR)
+    return lt->arr[l].str == "sliding_attention" ? 0 : 1;
+  return ((l + 1) % 6) ? 0 : 1;
+}
+
+// app_core.c:8325 config_read, the text stack's part.
+static int read_config(igc_model *m, const std::string &text, const igc_setup *setup) {
+  Json root;
+  JsonReader rd(text.data(), text.size());
+  if (!rd.parse(root)) return IGC_FAIL_FORMAT;
+  const Json *tcp = root.get("text_config");
+  const Json &tc = tcp ? *tcp : root;
+  m->vocab = (int)tc.number("vocab_size", 262144);
+  m->hidden = (int)tc.number("hidden_size", 2304);
+  m->inner = (int)tc.number("intermediate_size", 9216);
+  m->layers = (int)tc.number("num_hidden_layers", 30);
+  m->heads = (int)tc.number("num_attention_heads", 8);
+  m->kv_heads = (int)tc.number("num_key_value_heads", 4);
+  m->slide_span = (int)tc.number("sliding_window", 512);
+  m->ple_vocab = (int)tc.number("vocab_size_per_layer_input", 262144);
+  m->ple_dim = (int)tc.number("hidden_size_per_layer_input", 256);
+  m->share_count = (int)tc.number("num_kv_shared_layers", 0);
+  m->eps = (float)tc.number("rms_norm_eps", 1e-6);
+  m->softcap = (float)tc.number("final_logit_softcapping", 0.0);
+  m->pad_id = (int)tc.number("pad_token_id", 0);
+  int max_pos = (int)tc.number("max_position_embeddings", 131072);
+  if (tc.flag("enable_moe_block", false) || tc.flag("attention_k_eq_v", false)) return IGC_FAIL_SUPPORT;
+  if (tc.flag("use_double_wide_mlp", false) && m->share_count > 0) {
+    // shared layers carry a doubled feed-forward; their planes say how wide
+  }
+  if (m->layers < 1 || m->layers > 128) return IGC_FAIL_SUPPORT;
+  for (int l = 0; l < m->layers; ++l) m->kind[l] = layer_of_config(tc, m->layers, l);
+  const Json *rp = tc.get("rope_parameters");
+  const char *names[2] = {"sliding_attention", "full_attention"};
+  for (int k = 0; k < 2; ++k) {
+    RopeForm &r = m->rope[k];
+    r.theta = k ? 1000000.0 : 10000.0;
+    r.share = 1.0;
+    r.proportional = (k == 1);
+    if (k == 1) r.share = 0.25;
+    const Json *kj = rp ? rp->get(names[k]) : nullptr;
+    if (kj) {
+      r.theta = kj->number("rope_theta", r.theta);
+      r.share = kj->number("partial_rotary_factor", 1.0);
+      r.proportional = kj->text("rope_type", "default") == "proportional";
+    } else if (rp && rp->get("rope_theta")) {
+      r.theta = rp->number("rope_theta", r.theta);
+      r.share = rp->number("partial_rotary_factor", 1.0);
+      r.proportional = rp->text("rope_type", "default") == "proportional";
+    }
+  }
+  int window = max_pos < 32768 ? max_pos : 32768;
+  if (setup && setup->window_limit > 0) window = setup->window_limit < max_pos ? setup->window_limit : max_pos;
+  if (window < 8) window = 8;
+  m->window_limit = window;
+  return IGC_OKAY;
+}
+
+static std::string pick_prefix(Source &src) {
+  const char *cands[] = {"model.language_model.", "language_model.model.", "model.", ""};
+  for (const char *c : cands) {
+    if (src.find(std::string(c) + "embed_tokens.weight")) return c;
+  }
+  return "#";
+}
+
+struct Binder {
+  igc_model *m;
+  Source &src;
+  std::string prefix;
+  cudaStream_t st;
+  Binder(igc_model *mm, Source &s, const std::string &p, cudaStream_t stream) : m(mm), src(s), prefix(p), st(stream) {}
+
+  // app_core.c:7941 vec_bind: any float type, materialised as f32 on the device.
+  int vec(const std::string &stem, int hint, float **out, bool required = true) {
+    const Tensor *t = src.find(stem + ".weight");
+    std::string name = stem + ".weight";
+    if (!t) { t = src.find(stem); name = stem; }
+    if (!t) return required ? IGC_FAIL_MISSING : IGC_OKAY;
+    size_t n = t->bytes / dtype_bytes(t->dtype);
+    if (hint > 0 && n != (size_t)hint) return IGC_FAIL_FORMAT;
+    std::vector<float> host(n);
+    for (size_t i = 0; i < n; ++i) host[i] = real_at(*t, i);
+    int c = m->alloc(out, n);
+    if (c != IGC_OKAY) return c;
+    CK(cudaMemcpy(*out, host.data(), n * sizeof(float), cudaMemcpyHostToDevice));
+    m->decode_bytes += n * sizeof(float);
+    src.release(name);
+    return IGC_OKAY;
+  }
+
+  // app_core.c:7886 plane_bind_gemma, 4-bit U8 codes with F16 group scales.
+  struct CodeView {
+    const Tensor *code = nullptr, *scale = nullptr;
+    int rows = 0, cols = 0, groups = 0;
+    std::string name;
+  };
+  int code_view(const std::string &stem, int col_hint, CodeView &v) {
+    v.name = stem;
+    v.code = src.find(stem + ".weight");
+    if (!v.code) return IGC_FAIL_MISSING;
+    v.scale = src.find(stem + ".weight_scale");
+    if (v.code->dtype != T_U8 || !v.scale) return IGC_FAIL_SUPPORT;
+    if (v.code->rank != 2) return IGC_FAIL_FORMAT;
+    int rows = (int)v.code->shape[0], bytes = (int)v.code->shape[1];
+    int cols = col_hint;
+    int bits = 0;
+    const int widths[] = {8, 4, 2, 1};
+    for (int w : widths)
+      if (((int64_t)cols * w + 7) / 8 == bytes) { bits = w; break; }
+    if (bits == 0) return IGC_FAIL_FORMAT;
+    if (bits != 4) return IGC_FAIL_SUPPORT;
+    int groups = v.scale->rank >= 2 ? (int)v.scale->shape[v.scale->rank - 1] : 1;
+    if (groups < 1 || cols % groups) return IGC_FAIL_FORMAT;
+    if (cols / groups != 32 || v.scale->dtype != T_F16) return IGC_FAIL_SUPPORT;
+    if ((int)v.scale->shape[0] != rows) return IGC_FAIL_FORMAT;
+    v.rows = rows;
+    v.cols = cols;
+    v.groups = groups;
+    return IGC_OKAY;
+  }
+
+  // Uploads one or more code planes of the same width into one tile array:
+  // `parts` are stacked by row block (q|k|v) or, for a pair, interleaved
+  // block by block (gate, up).
+  int upload(std::vector<CodeView> parts, bool pair, DevPlane &out) {
+    int cols = parts[0].cols;
+    int n_cc = (cols + 63) / 64;
+    int n_rb = 0;
+    for (auto &p : parts) {
+      if (p.cols != cols) return IGC_FAIL_FORMAT;
+      if (!pair && parts.size() > 1 && p.rows % 16) return IGC_FAIL_SUPPORT;
+      n_rb += (p.rows + 15) / 16;
+    }
+    if (pair && parts[0].rows != parts[1].rows) return IGC_FAIL_FORMAT;
+    out.n_rb = n_rb;
+    out.n_cc = n_cc;
+    out.cols = cols;
+    out.rows = pair ? parts[0].rows : n_rb * 16;
+    if (!pair && parts.size() == 1) out.rows = parts[0].rows;
+    out.pair = pair;
+    int c = m->alloc(&out.tiles, (size_t)n_rb * n_cc * 32);
+    if (c != IGC_OKAY) return c;
+    c = m->alloc(&out.scales, (size_t)n_rb * n_cc * 8);
+    if (c != IGC_OKAY) return c;
+    int rb_at = 0;
+    for (size_t k = 0; k < parts.size(); ++k) {
+      CodeView &p = parts[k];
+      uint8_t *dc = nullptr;
+      uint16_t *ds = nullptr;
+      size_t cb = p.code->bytes, sb = p.scale->bytes;
+      CK(cudaMalloc(&dc, cb));
+      CK(cudaMalloc(&ds, sb));
+      CK(cudaMemcpy(dc, p.code->data, cb, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(ds, p.scale->data, sb, cudaMemcpyHostToDevice));
+      int prb = (p.rows + 15) / 16;
+      int mul = pair ? 2 : 1, add = pair ? (int)k : rb_at;
+      cudaError_t e = igc_launch_repack(dc, (size_t)p.code->shape[1], ds, p.groups, p.rows, p.cols, prb, n_cc, mul,
+                                        add, out.tiles, out.scales, st);
+      cudaError_t e2 = cudaStreamSynchronize(st);
+      cudaFree(dc);
+      cudaFree(ds);
+      if (e != cudaSuccess) return fail_device(e, "repack");
+      if (e2 != cudaSuccess) return fail_device(e2, "repack sync");
+      rb_at += prb;
+      // app_core.c:1860 plane_bytes: codes and scales a product streams
+      m->decode_bytes += cb + sb;
+      src.release(p.name + ".weight");
+      src.release(p.name + ".weight_scale");
+    }
+    plan(out);
+    return IGC_OKAY;
+  }
+
+  void plan(DevPlane &p) {
+    int units = p.pair ? p.n_rb / 2 : p.n_rb;
+    int target = m->sm_count * GEMV_WARPS * 2;
+    int S = 1;
+    while (S < 8 && S * 2 <= p.n_cc && units * S < target) S *= 2;
+    p.split = S;
+    int per_iter = GEMV_WARPS / S;
+    int need = (units + per_iter - 1) / per_iter;
+    int cap = m->sm_count * 4;
+    p.grid = need < cap ? need : cap;
+    if (p.grid < 1) p.grid = 1;
+  }
+
+  int plane(const std::string &stem, int col_hint, DevPlane &out) {
+    CodeView v;
+    int c = code_view(stem, col_hint, v);
+    if (c != IGC_OKAY) return c;
+    return upload({v}, false, out);
+  }
+
+  int table(const std::string &stem, int cols, uint16_t **out, int *rows_out) {
+    const Tensor *t = src.find(stem + ".weight");
+    if (!t) return IGC_FAIL_MISSING;
+    if (t->dtype != T_BF16 || t->rank != 2) return IGC_FAIL_SUPPORT;
+    if (cols > 0 && t->shape[1] != cols) return IGC_FAIL_FORMAT;
+    int c = m->alloc(out, t->bytes / 2);
+    if (c != IGC_OKAY) return c;
+    CK(cudaMemcpy(*out, t->data, t->bytes, cudaMemcpyHostToDevice));
+    *rows_out = (int)t->shape[0];
+    m->decode_bytes += (size_t)t->shape[1] * 2; /* app_core.c:1880 plane_row_bytes */
+    src.release(stem + ".weight");
+    return IGC_OKAY;
+  }
+};
+
+// rope inverse frequencies (app_core.c:8121 rope_build) and the per-position
+// cos/sin tables the attention reads (app_core.c:8147 rope_wave)
+static int build_rope(igc_model *m, int kind, int hd, cudaStream_t st) {
+  const RopeForm &r = m->rope[kind];
+  int half = hd / 2, turn = half;
+  if (r.proportional) turn = (int)(r.share * hd / 2.0);
+  if (turn > half) turn = half;
+  if (turn < 0) turn = 0;
+  std::vector<float> steps((size_t)half, 0.0f);
+  for (int i = 0; i < half; ++i)
+    if (!r.proportional || i < turn) steps[i] = (float)(1.0 / pow(r.theta, (double)(2 * i) / (double)hd));
+  float *d_steps = nullptr;
+  CK(cudaMalloc(&d_steps, sizeof(float) * (size_t)half));
+  CK(cudaMemcpy(d_steps, steps.data(), sizeof(float) * (size_t)half, cudaMemcpyHostToDevice));
+  int c = m->alloc(&m->rope_cs[kind], (size_t)m->window_limit * half);
+  if (c == IGC_OKAY) c = m->alloc(&m->rope_sn[kind], (size_t)m->window_limit * half);
+  if (c != IGC_OKAY) { cudaFree(d_steps); return c; }
+  cudaError_t e = igc_launch_rope_table(d_steps, half, m->window_limit, m->rope_cs[kind], m->rope_sn[kind], st);
+  cudaError_t e2 = cudaStreamSynchronize(st);
+  cudaFree(d_steps);
+  if (e != cudaSuccess) return fail_device(e, "rope table");
+  if (e2 != cudaSuccess) return fail_device(e2, "rope table sync");
+  m->rope_hd[kind] = hd;
+  return IGC_OKAY;
+}
+
+// app_core.c:8497 model_bind, for the text stack: shapes come from the
+// tensors, the configuration is a hint.
+static int bind_model(igc_model *m, Source &src) {
+  std::string P = pick_prefix(src);
+  if (P == "#") return IGC_FAIL_MISSING;
+  cudaStream_t st;
+  CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+  struct StreamGuard {
+    cudaStream_t s;
+    ~StreamGuard() { cudaStreamDestroy(s); }
+  } guard{st};
+  Binder b(m, src, P, st);
+  int c, rows = 0;
+  c = b.table(P + "embed_tokens", 0, &m->embed, &rows);
+  if (c != IGC_OKAY) return c;
+  m->vocab = rows;
+  // the embedding table's width is the state size (app_core.c:8505)
+  {
+    int ple_rows = 0;
+    if (m->ple_dim > 0) {
+      c = b.table(P + "embed_tokens_per_layer", m->ple_dim * m->layers, &m->ple_embed, &ple_rows);
+      if (c != IGC_OKAY) return c;
+      m->ple_vocab = ple_rows;
+      c = b.plane(P + "per_layer_model_projection", m->hidden, m->ple_lift);
+      if (c != IGC_OKAY) return c;
+      c = b.vec(P + "per_layer_projection_norm", m->ple_dim, &m->ple_norm);
+      if (c != IGC_OKAY) return c;
+    }
+  }
+  c = b.vec(P + "norm", m->hidden, &m->final_norm);
+  if (c != IGC_OKAY) return c;
+  {
+    const char *heads[] = {"lm_head", "model.lm_head", "language_model.lm_head"};
+    c = IGC_FAIL_MISSING;
+    for (const char *h : heads) {
+      if (!src.find(std::string(h) + ".weight")) continue;
+      c = b.plane(h, m->hidden, m->head);
+      break;
+    }
+    if (c != IGC_OKAY) return c; /* a tied head over a bf16 table is not supported */
+  }
+  m->layer.resize((size_t)m->layers);
+  int first_share = m->layers - m->share_count;
+  for (int l = 0; l < m->layers; ++l) {
+    DevLayer &L = m->layer[l];
+    char stem[512];
+    L.kind = m->kind[l];
+    L.share = m->share_count > 0 && l >= first_share;
+    if (L.share) {
+      for (int pi = first_share - 1; pi >= 0; --pi)
+        if (m->kind[pi] == L.kind) { L.source = pi; break; }
+      if (L.source < 0) return IGC_FAIL_FORMAT;
+    }
+#define STEM(fmt) (snprintf(stem, sizeof(stem), "%slayers.%d." fmt, P.c_str(), l), std::string(stem))
+    Binder::CodeView q, k, v, o, gt, up, dn, pg, pp;
+    c = b.code_view(STEM("self_attn.q_proj"), m->hidden, q);
+    if (c != IGC_OKAY) return c;
+    L.q_rows = q.rows;
+    L.hd = q.rows / m->heads;
+    if (L.hd * m->heads != q.rows || L.hd % 16 || L.hd > 256) return IGC_FAIL_SUPPORT;
+    if (!L.share) {
+      c = b.code_view(STEM("self_attn.k_proj"), m->hidden, k);
+      if (c != IGC_OKAY) return c;
+      c = b.code_view(STEM("self_attn.v_proj"), m->hidden, v);
+      if (c != IGC_OKAY) return c; /* keys doubling as values is not supported */
+      L.kv_rows = k.rows;
+      L.kv_heads = k.rows / L.hd;
+      if (v.rows != k.rows || L.kv_heads < 1) return IGC_FAIL_FORMAT;
+      c = b.upload({q, k, v}, false, L.qkv);
+      if (c != IGC_OKAY) return c;
+      c = b.vec(STEM("self_attn.k_norm"), L.hd, &L.k_norm);
+      if (c != IGC_OKAY) return c;
+    } else {
+      const DevLayer &S = m->layer[L.source];
+      L.kv_rows = S.kv_rows;
+      L.kv_heads = S.kv_heads;
+      if (S.hd != L.hd) return IGC_FAIL_FORMAT;
+      c = b.upload({q}, false, L.qkv);
+      if (c != IGC_OKAY) return c;
+    }
+    L.qkv_rows = L.share ? L.q_rows : L.q_rows + 2 * L.kv_rows;
+    if (m->heads % L.kv_heads) return IGC_FAIL_FORMAT;
+    c = b.code_view(STEM("self_attn.o_proj"), L.q_rows, o);
+    if (c == IGC_OKAY) c = b.upload({o}, false, L.o);
+    if (c != IGC_OKAY) return c;
+    c = b.code_view(STEM("mlp.gate_proj"), m->hidden, gt);
+    if (c == IGC_OKAY) c = b.code_view(STEM("mlp.up_proj"), m->hidden, up);
+    if (c != IGC_OKAY) return c;
+    L.inner = gt.rows;
+    c = b.upload({gt, up}, true, L.gateup);
+    if (c != IGC_OKAY) return c;
+    c = b.code_view(STEM("mlp.down_proj"), L.inner, dn);
+    if (c == IGC_OKAY) c = b.upload({dn}, false, L.down);
+    if (c != IGC_OKAY) return c;
+    c = b.vec(STEM("self_attn.q_norm"), L.hd, &L.q_norm);
+    if (c == IGC_OKAY) c = b.vec(STEM("input_layernorm"), m->hidden, &L.enter_norm);
+    if (c == IGC_OKAY) c = b.vec(STEM("post_attention_layernorm"), m->hidden, &L.after_attn_norm);
+    if (c == IGC_OKAY) c = b.vec(STEM("pre_feedforward_layernorm"), m->hidden, &L.before_feed_norm);
+    if (c == IGC_OKAY) c = b.vec(STEM("post_feedforward_layernorm"), m->hidden, &L.after_feed_norm);
+    if (c != IGC_OKAY) return c;
+    if (m->ple_dim > 0) {
+      c = b.code_view(STEM("per_layer_input_gate"), m->hidden, pg);
+      if (c == IGC_OKAY) c = b.upload({pg}, false, L.ple_gate);
+      if (c == IGC_OKAY) c = b.code_view(STEM("per_layer_projection"), m->ple_dim, pp);
+      if (c == IGC_OKAY) c = b.upload({pp}, false, L.ple_proj);
+      if (c == IGC_OKAY) c = b.vec(STEM("post_per_layer_input_norm"), m->hidden, &L.after_ple_norm);
+      if (c != IGC_OKAY) return c;
+    }
+    {
+      const Tensor *g = src.find(STEM("layer_scalar"));
+      L.gain = g ? real_at(*g, 0) : 1.0f; /* app_core.c:8700-8708 */
+    }
+#undef STEM
+    if (L.qkv_rows > m->max_qkv) m->max_qkv = L.qkv_rows;
+    if (L.inner > m->max_inner) m->max_inner = L.inner;
+    if (L.q_rows > m->max_q) m->max_q = L.q_rows;
+    if (L.kv_rows > m->max_kvw) m->max_kvw = L.kv_rows;
+  }
+  for (int kind = 0; kind < 2; ++kind) {
+    int hd = 0;
+    for (auto &L : m->layer)
+      if (L.kind == kind) hd = L.hd;
+    if (hd) {
+      c = build_rope(m, kind, hd, st);
+      if (c != IGC_OKAY) return c;
+    }
+  }
+  return IGC_OKAY;
+}
+
+static int model_prepare(igc_model *m, const igc_setup *setup) {
+  m->device = setup ? setup->device : 0;
+  CK(cudaSetDevice(m->device));
+  CK(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, m->device));
+  CK(cudaDeviceGetAttribute(&m->smem_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
+  m->smem_limit -= 2048;  // the largest static part any kernel of igc_kernels.cu carries
+  CK(igc_kernels_configure(m->smem_limit + 2048));
+  return IGC_OKAY;
+}
+
+extern "C" int igc_model_load(const char *folder, const igc_setup *setup, igc_model **model_out) {
+  if (!folder || !model_out) return IGC_FAIL_ARGUMENT;
+  *model_out = nullptr;
+  if (setup && setup->cache_bits != 0) return IGC_FAIL_SUPPORT;
+  std::string text;
+  if (!slurp(std::string(folder) + "/config.json", text)) return IGC_FAIL_MISSING;
+  auto m = std::make_unique<igc_model>();
+  int c = model_prepare(m.get(), setup);
+  if (c != IGC_OKAY) return c;
+  c = read_config(m.get(), text, setup);
+  if (c != IGC_OKAY) return c;
+  SafeSource src;
+  c = src.open(folder);
+  if (c != IGC_OKAY) return c;
+  c = bind_model(m.get(), src);
+  if (c != IGC_OKAY) return c;
+  *model_out = m.release();
+  return IGC_OKAY;
+}
+
+extern "C" int igc_model_synth(const igc_synth_spec *spec, const igc_setup *setup, igc_model **model_out) {
+  if (!spec || !model_out) return IGC_FAIL_ARGUMENT;
+  *model_out = nullptr;
+  char *text = igc_synth_config_text(spec);
+  if (!text) return IGC_FAIL_MEMORY;
+  std::string t(text);
+  free(text);
+  auto m = std::make_unique<igc_model>();
+  int c = model_prepare(m.get(), setup);
+  if (c != IGC_OKAY) return c;
+  c = read_config(m.get(), t, setup);
+  if (c != IGC_OKAY) return c;
+  SynthSource src(*spec);
+  c = bind_model(m.get(), src);
+  if (c != IGC_OKAY) return c;
+  *model_out = m.release();
+  return IGC_OKAY;
+}
+
+extern "C" void igc_model_free(igc_model *model) { delete model; }
+extern "C" int igc_model_vocab_count(const igc_model *m) { return m ? m->vocab : 0; }
+extern "C" int igc_model_layer_count(const igc_model *m) { return m ? m->layers : 0; }
+extern "C" int igc_model_state_size(const igc_model *m) { return m ? m->hidden : 0; }
+extern "C" int igc_model_window_limit(const igc_model *m) { return m ? m->window_limit : 0; }
+extern "C" size_t igc_model_decode_bytes(const igc_model *m) { return m ? m->decode_bytes : 0; }
+extern "C" size_t igc_model_device_bytes(const igc_model *m) { return m ? m->device_bytes : 0; }
+
+// ---------------------------------------------------------------------------
+// sessions
+
+constexpr int ATT_CHUNKS = 128;  // attention span chunks a launch (grid.x)
+
+struct igc_session {
+  igc_model *m = nullptr;
+  cudaStream_t st = nullptr;
+  int fill = 0;
+  int guess_count = 0, guess_from = 0, guess_echo = 0;
+  std::vector<int32_t> echo;
+  uint64_t draw_state = 0x2545F4914F6CDD1DULL;
+  std::vector<float *> kc, vc;
+  int *d_io = nullptr;  // [0] position, [1..16] ids
+  int32_t *d_top = nullptr;
+  float *x0 = nullptr, *xa = nullptr, *xb = nullptr, *seed = nullptr, *ple_raw = nullptr, *ple = nullptr;
+  float *qkv = nullptr, *attn = nullptr, *obuf = nullptr, *act = nullptr, *dbuf = nullptr, *pa = nullptr,
+        *pp = nullptr, *logits = nullptr;
+  float *part_ml = nullptr, *part_acc = nullptr, *arg_val = nullptr;
+  int *arg_idx = nullptr;
+  float *cand_v = nullptr, *top_v = nullptr;
+  int *cand_i = nullptr, *top_i = nullptr;
+  int32_t *d_echo = nullptr;
+  int *d_echo_range = nullptr;
+  int32_t *h_io = nullptr, *h_top = nullptr;  // pinned
+  float *h_top_v = nullptr;
+  int *h_top_i = nullptr;
+  int logit_lanes = 0;  // rows the last pass left in `logits`
+  int use_graphs = 1;
+  cudaGraphExec_t graph[IGC_LANE_LIMIT + 1][2] = {};
+  double serve_seconds = 0.0;
+  size_t serve_tokens = 0;
+  long kernels_per_pass[IGC_LANE_LIMIT + 1][2] = {};
+  std::vector<void *> owned;
+  int arg_parts = 0;
+
+  ~igc_session() {
+    cudaSetDevice(m->device);
+    for (int k = 0; k <= IGC_LANE_LIMIT; ++k)
+      for (int w = 0; w < 2; ++w)
+        if (graph[k][w]) cudaGraphExecDestroy(graph[k][w]);
+    for (void *p : owned) cudaFree(p);
+    if (h_io) cudaFreeHost(h_io);
+    if (st) cudaStreamDestroy(st);
+  }
+  template <typename T>
+  int alloc(T **p, size_t count) {
+    void *v = nullptr;
+    cudaError_t e = cudaMalloc(&v, (count ? count : 1) * sizeof(T));
+    if (e != cudaSuccess) return fail_device(e, "cudaMalloc(session)");
+    owned.push_back(v);
+    *p = (T *)v;
+    return IGC_OKAY;
+  }
+};
+
+extern "C" int igc_session_open(igc_model *m, igc_session **out) {
+  if (!m || !out) return IGC_FAIL_ARGUMENT;
+  *out = nullptr;
+  CK(cudaSetDevice(m->device));
+  auto s = std::make_unique<igc_session>();
+  s->m = m;
+  CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+  const int K = IGC_LANE_LIMIT, H = m->hidden, PS = m->layers * m->ple_dim;
+  int c = IGC_OKAY;
+  s->kc.assign((size_t)m->layers, nullptr);
+  s->vc.assign((size_t)m->layers, nullptr);
+  for (int l = 0; l < m->layers && c == IGC_OKAY; ++l) {
+    const DevLayer &L = m->layer[l];
+    if (L.share) continue;
+    c = s->alloc(&s->kc[l], (size_t)m->window_limit * L.kv_rows);
+    if (c == IGC_OKAY) c = s->alloc(&s->vc[l], (size_t)m->window_limit * L.kv_rows);
+    if (c == IGC_OKAY) CK(cudaMemsetAsync(s->kc[l], 0, sizeof(float) * (size_t)m->window_limit * L.kv_rows, s->st));
+    if (c == IGC_OKAY) CK(cudaMemsetAsync(s->vc[l], 0, sizeof(float) * (size_t)m->window_limit * L.kv_rows, s->st));
+  }
+  s->arg_parts = m->sm_count * 4;
+  if (c == IGC_OKAY) c = s->alloc(&s->d_io, 1 + K);
+  if (c == IGC_OKAY) c = s->alloc(&s->d_top, K);
+  if (c == IGC_OKAY) c = s->alloc(&s->x0, (size_t)K * H);
+  if (c == IGC_OKAY) c = s->alloc(&s->xa, (size_t)K * H);
+  if (c == IGC_OKAY) c = s->alloc(&s->xb, (size_t)K * H);
+  if (c == IGC_OKAY) c = s->alloc(&s->seed, (size_t)K * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = s->alloc(&s->ple_raw, (size_t)K * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = s->alloc(&s->ple, (size_t)K * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = s->alloc(&s->qkv, (size_t)K * m->max_qkv);
+  if (c == IGC_OKAY) c = s->alloc(&s->attn, (size_t)K * m->max_q);
+  if (c == IGC_OKAY) c = s->alloc(&s->obuf, (size_t)K * H);
+  if (c == IGC_OKAY) c = s->alloc(&s->act, (size_t)K * m->max_inner);
+  if (c == IGC_OKAY) c = s->alloc(&s->dbuf, (size_t)K * H);
+  if (c == IGC_OKAY) c = s->alloc(&s->pa, (size_t)K * (m->ple_dim ? m->ple_dim : 1));
+  if (c == IGC_OKAY) c = s->alloc(&s->pp, (size_t)K * H);
+  if (c == IGC_OKAY) c = s->alloc(&s->logits, (size_t)K * m->vocab);
+  if (c == IGC_OKAY) c = s->alloc(&s->part_ml, (size_t)ATT_CHUNKS * K * m->heads * 2);
+  if (c == IGC_OKAY) c = s->alloc(&s->part_acc, (size_t)ATT_CHUNKS * K * m->max_q);
+  if (c == IGC_OKAY) c = s->alloc(&s->arg_val, (size_t)s->arg_parts * 16);
+  if (c == IGC_OKAY) c = s->alloc(&s->arg_idx, (size_t)s->arg_parts * 16);
+  int blocks = (m->vocab + 2047) / 2048;
+  if (c == IGC_OKAY) c = s->alloc(&s->cand_v, (size_t)K * blocks * 256);
+  if (c == IGC_OKAY) c = s->alloc(&s->cand_i, (size_t)K * blocks * 256);
+  if (c == IGC_OKAY) c = s->alloc(&s->top_v, (size_t)K * 256);
+  if (c == IGC_OKAY) c = s->alloc(&s->top_i, (size_t)K * 256);
+  if (c == IGC_OKAY) c = s->alloc(&s->d_echo, (size_t)m->window_limit);
+  if (c == IGC_OKAY) c = s->alloc(&s->d_echo_range, 2 * K);
+  if (c != IGC_OKAY) return c;
+  {
+    void *h = nullptr;
+    size_t bytes = sizeof(int32_t) * (size_t)(1 + K) + sizeof(int32_t) * K + (sizeof(float) + sizeof(int)) * K * 256;
+    CK(cudaMallocHost(&h, bytes));
+    s->h_io = (int32_t *)h;
+    s->h_top = s->h_io + 1 + K;
+    s->h_top_v = (float *)(s->h_top + K);
+    s->h_top_i = (int *)(s->h_top_v + K * 256);
+  }
+  CK(cudaStreamSynchronize(s->st));
+  s->echo.reserve((size_t)m->window_limit);
+  const char *g = getenv("IGC_NO_GRAPHS");
+  s->use_graphs = !(g && g[0] == '1');
+  *out = s.release();
+  return IGC_OKAY;
+}
+
+extern "C" void igc_session_close(igc_session *s) { delete s; }
+
+extern "C" void igc_session_reset(igc_session *s) { /* app_core.c:14375 */
+  if (!s) return;
+  s->guess_count = 0;
+  s->fill = 0;
+  s->echo.clear();
+  s->serve_seconds = 0.0;
+  s->serve_tokens = 0;
+}
+
+extern "C" int igc_session_fill(const igc_session *s) { return s ? s->fill : 0; }
+extern "C" int igc_session_guess_span(const igc_session *s) { return s ? s->guess_count : 0; }
+extern "C" int igc_session_guess_limit(const igc_session *s) { return s ? IGC_LANE_LIMIT : 0; }
+extern "C" double igc_session_serve_seconds(const igc_session *s) { return s ? s->serve_seconds : 0.0; }
+extern "C" size_t igc_session_serve_tokens(const igc_session *s) { return s ? s->serve_tokens : 0; }
+
+extern "C" int igc_session_hold(igc_session *s, int keep) { /* app_core.c:13935 */
+  if (!s || keep < 0) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  if (keep > s->fill) return IGC_FAIL_ARGUMENT;
+  s->fill = keep;
+  if ((int)s->echo.size() > keep) s->echo.resize((size_t)keep);
+  return IGC_OKAY;
+}
+
+static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, const float *x, int x_stride,
+                const float *p, const float *w_res, float gain, const float *w_in, float *x_out, float *out,
+                int out_stride, float out_scale = 1.0f, const float *aux = nullptr, int aux_stride = 0) {
+  GemvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.pl = pl.view();
+  a.lanes = K;
+  a.split = pl.split;
+  a.x = x;
+  a.x_stride = x_stride;
+  a.p = p;
+  a.p_stride = x_stride;
+  a.w_res = w_res;
+  a.gain = gain;
+  a.w_in = w_in;
+  a.eps = s->m->eps;
+  a.x_out = x_out;
+  a.out = out;
+  a.out_stride = out_stride;
+  a.out_scale = out_scale;
+  a.aux = aux;
+  a.aux_stride = aux_stride;
+  a.cap = s->m->softcap;
+  a.part_val = s->arg_val;
+  a.part_idx = s->arg_idx;
+  if (igc_gemv_smem(&a) <= (size_t)s->m->smem_limit) {
+    CKL(igc_launch_gemv(&a, pl.pair ? 1 : 0, pro, epi, pl.grid, s->st));
+    return IGC_OKAY;
+  }
+  // Too wide to stage sixteen lanes at once (the 6144-column down
+  // projection): two launches of eight lanes, each lane independent.
+  if (K <= 8 || epi == EPI_LOGITS) return IGC_FAIL_SUPPORT;
+  for (int j0 = 0; j0 < K; j0 += 8) {
+    GemvArgs b = a;
+    b.lanes = K - j0 < 8 ? K - j0 : 8;
+    b.x = x + (size_t)j0 * x_stride;
+    b.p = p ? p + (size_t)j0 * x_stride : nullptr;
+    b.x_out = x_out ? x_out + (size_t)j0 * x_stride : nullptr;
+    b.out = out + (size_t)j0 * out_stride;
+    b.aux = aux ? aux + (size_t)j0 * aux_stride : nullptr;
+    if (igc_gemv_smem(&b) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
+    CKL(igc_launch_gemv(&b, pl.pair ? 1 : 0, pro, epi, pl.grid, s->st));
+  }
+  return IGC_OKAY;
+}
+
+// One pass of K lanes at the position in d_io[0], ids in d_io[1..K]
+// (app_core.c:11843 session_pass).  want: 0 no head, 1 head and argmax.
+static int enqueue_pass(igc_session *s, int K, int want) {
+  igc_model *m = s->m;
+  const int H = m->hidden, PS = m->layers * m->ple_dim;
+  const int *d_p0 = s->d_io;
+  const int32_t *d_ids = s->d_io + 1;
+  CKL(igc_launch_embed(d_ids, K, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
+                       PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->st));
+  if (m->ple_dim > 0) {
+    int c = gemv(s, m->ple_lift, K, PRO_F32, EPI_STORE, s->x0, H, nullptr, nullptr, 1.0f, nullptr, nullptr,
+                 s->ple_raw, PS, (float)(1.0 / sqrt((double)H)));
+    if (c != IGC_OKAY) return c;
+    CKL(igc_launch_ple_finish(s->ple_raw, s->seed, K, m->layers, m->ple_dim, m->ple_norm, m->eps,
+                              (float)(1.0 / sqrt(2.0)), s->ple, s->st));
+  }
+  // the residual stream ping-pongs between xa and xb; `pend` is the last
+  // block's output still to be normed and added (with its gain) by the next
+  // consumer's prologue
+  float *cur = s->x0;
+  float *bufs[2] = {s->xa, s->xb};
+  int flip = 0;
+  const float *pend = nullptr, *pend_w = nullptr;
+  float pend_gain = 1.0f;
+  auto next_x = [&]() -> float * { float *o = bufs[flip]; flip ^= 1; return o; };
+  for (int l = 0; l < m->layers; ++l) {
+    const DevLayer &L = m->layer[l];
+    int c;
+    float *xo = nullptr;
+    if (pend) {
+      xo = next_x();
+      c = gemv(s, L.qkv, K, PRO_RESID_NORM, EPI_STORE, cur, H, pend, pend_w, pend_gain, L.enter_norm, xo, s->qkv,
+               L.qkv_rows);
+      cur = xo;
+    } else {
+      c = gemv(s, L.qkv, K, PRO_NORM, EPI_STORE, cur, H, nullptr, nullptr, 1.0f, L.enter_norm, nullptr, s->qkv,
+               L.qkv_rows);
+    }
+    if (c != IGC_OKAY) return c;
+    const int owner = L.share ? L.source : l;
+    const DevLayer &O = m->layer[owner];
+    CKL(igc_launch_attn_prep(s->qkv, L.qkv_rows, m->heads, L.kv_heads, L.hd, L.q_norm, L.k_norm,
+                             m->rope_cs[L.kind], m->rope_sn[L.kind], L.share ? 0 : 1, m->eps, d_p0, K,
+                             s->kc[l], s->vc[l], s->st));
+    CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, L.hd, s->kc[owner], s->vc[owner], O.kv_rows,
+                        m->heads / L.kv_heads, L.kind == 0 ? 1 : 0, m->slide_span, d_p0, K, ATT_CHUNKS, s->part_ml,
+                        s->part_acc, s->attn, L.q_rows, s->st));
+    ++g_launches;  // the combine kernel
+    c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H);
+    if (c != IGC_OKAY) return c;
+    xo = next_x();
+    c = gemv(s, L.gateup, K, PRO_RESID_NORM, EPI_GELU_PAIR, cur, H, s->obuf, L.after_attn_norm, 1.0f,
+             L.before_feed_norm, xo, s->act, L.inner);
+    if (c != IGC_OKAY) return c;
+    cur = xo;
+    c = gemv(s, L.down, K, PRO_F32, EPI_STORE, s->act, L.inner, nullptr, nullptr, 1.0f, nullptr, nullptr, s->dbuf, H);
+    if (c != IGC_OKAY) return c;
+    if (m->ple_dim > 0) {
+      xo = next_x();
+      c = gemv(s, L.ple_gate, K, PRO_RESID, EPI_GELU_MUL, cur, H, s->dbuf, L.after_feed_norm, 1.0f, nullptr, xo,
+               s->pa, m->ple_dim, 1.0f, s->ple + (size_t)l * m->ple_dim, PS);
+      if (c != IGC_OKAY) return c;
+      cur = xo;
+      c = gemv(s, L.ple_proj, K, PRO_F32, EPI_STORE, s->pa, m->ple_dim, nullptr, nullptr, 1.0f, nullptr, nullptr,
+               s->pp, H);
+      if (c != IGC_OKAY) return c;
+      pend = s->pp;
+      pend_w = L.after_ple_norm;
+    } else {
+      pend = s->dbuf;
+      pend_w = L.after_feed_norm;
+    }
+    pend_gain = L.gain;
+  }
+  if (want) {
+    float *xo = next_x();
+    int c = gemv(s, m->head, K, PRO_RESID_NORM, EPI_LOGITS, cur, H, pend, pend_w, pend_gain, m->final_norm, xo,
+                 s->logits, m->vocab);
+    if (c != IGC_OKAY) return c;
+    CKL(igc_launch_argmax(s->arg_val, s->arg_idx, m->head.grid, K, s->d_top, s->st));
+  }
+  return IGC_OKAY;
+}
+
+// Runs one pass: ids and position in, argmax ids out (when want), with a
+// captured graph per (K, want) after the first pass of that shape.
+static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
+  igc_model *m = s->m;
+  if (K < 1 || K > IGC_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
+  if (s->fill + K > m->window_limit) return IGC_FAIL_STATE;
+  for (int j = 0; j < K; ++j)
+    if (ids[j] < 0 || ids[j] >= m->vocab) return IGC_FAIL_ARGUMENT;
+  CK(cudaSetDevice(m->device));
+  s->h_io[0] = s->fill;
+  memcpy(s->h_io + 1, ids, sizeof(int32_t) * (size_t)K);
+  CK(cudaMemcpyAsync(s->d_io, s->h_io, sizeof(int32_t) * (size_t)(1 + K), cudaMemcpyHostToDevice, s->st));
+  int w = want ? 1 : 0;
+  if (s->use_graphs) {
+    if (!s->graph[K][w]) {
+      cudaGraph_t g;
+      long before = g_launches;
+      CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+      int c = enqueue_pass(s, K, want);
+      cudaError_t e = cudaStreamEndCapture(s->st, &g);
+      if (c != IGC_OKAY) return c;
+      if (e != cudaSuccess) return fail_device(e, "capture");
+      s->kernels_per_pass[K][w] = g_launches - before;
+      g_launches = before;
+      e = cudaGraphInstantiate(&s->graph[K][w], g, 0);
+      cudaGraphDestroy(g);
+      if (e != cudaSuccess) return fail_device(e, "graph instantiate");
+    }
+    CK(cudaGraphLaunch(s->graph[K][w], s->st));
+    g_launches += s->kernels_per_pass[K][w];
+  } else {
+    int c = enqueue_pass(s, K, want);
+    if (c != IGC_OKAY) return c;
+  }
+  if (want) CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * (size_t)K, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  s->fill += K;
+  for (int j = 0; j < K; ++j)
+    if ((int)s->echo.size() < m->window_limit) s->echo.push_back(ids[j]);
+  s->logit_lanes = want ? K : 0;
+  return IGC_OKAY;
+}
+
+extern "C" int igc_session_prime(igc_session *s, const int32_t *ids, int n) { /* app_core.c:14443 */
+  if (!s || !ids || n < 1) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  if (s->fill + n > s->m->window_limit) return IGC_FAIL_STATE;
+  for (int i = 0; i < n; ++i)
+    if (ids[i] < 0 || ids[i] >= s->m->vocab) return IGC_FAIL_ARGUMENT;
+  for (int i = 0; i + 1 < n;) {
+    int lanes = n - 1 - i;
+    if (lanes > IGC_LANE_LIMIT) lanes = IGC_LANE_LIMIT;
+    int c = run_pass(s, ids + i, lanes, 0);
+    if (c != IGC_OKAY) return c;
+    i += lanes;
+  }
+  return IGC_OKAY;
+}
+
+static double now_seconds() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+extern "C" int igc_session_step(igc_session *s, int32_t id, float *logits_out, int32_t *top_out) {
+  if (!s) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  double t0 = now_seconds();
+  int c = run_pass(s, &id, 1, 1);
+  if (c != IGC_OKAY) return c;
+  s->serve_seconds += now_seconds() - t0;
+  s->serve_tokens += 1;
+  if (top_out) *top_out = s->h_top[0];
+  if (logits_out) CK(cudaMemcpy(logits_out, s->logits, sizeof(float) * (size_t)s->m->vocab, cudaMemcpyDeviceToHost));
+  return IGC_OKAY;
+}
+
+extern "C" int igc_session_guess(igc_session *s, const int32_t *ids, int k, float *logits_out) {
+  if (!s || !ids) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  if (k < 1 || k > IGC_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
+  if (s->fill + k > s->m->window_limit) return IGC_FAIL_STATE;
+  s->guess_from = s->fill;
+  s->guess_echo = (int)s->echo.size();
+  double t0 = now_seconds();
+  int c = run_pass(s, ids, k, 1);
+  if (c != IGC_OKAY) return c;
+  s->serve_seconds += now_seconds() - t0;
+  s->guess_count = k;
+  if (logits_out)
+    CK(cudaMemcpy(logits_out, s->logits, sizeof(float) * (size_t)s->m->vocab * k, cudaMemcpyDeviceToHost));
+  return IGC_OKAY;
+}
+
+extern "C" int igc_session_guess_top(igc_session *s, int32_t *top_out) {
+  if (!s || !top_out) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count <= 0) return IGC_FAIL_STATE;
+  memcpy(top_out, s->h_top, sizeof(int32_t) * (size_t)s->guess_count);
+  return IGC_OKAY;
+}
+
+extern "C" int igc_session_guess_keep(igc_session *s, int keep) { /* app_core.c:12205 */
+  if (!s || s->guess_count <= 0) return IGC_FAIL_STATE;
+  if (keep < 0 || keep > s->guess_count) return IGC_FAIL_ARGUMENT;
+  s->serve_tokens += (size_t)keep;
+  s->fill = s->guess_from + keep;
+  s->echo.resize((size_t)(s->guess_echo + keep));
+  s->guess_count = 0;
+  return IGC_OKAY;
+}
+
+// ---------------------------------------------------------------------------
+// the sampler (app_core.c:14572 pick_shape, :14653 pick_draw, :14706
+// guess_draw_state, :14762 session_guess_taste).  The top candidates are
+// selected on the GPU; the shaping of at most top_count values, the draws and
+// the rejection rule are the reference's arithmetic on the host.
+
+struct Slot {
+  float w;
+  int32_t id;
+};
+
+static uint64_t draw_next(uint64_t *st) {
+  uint64_t v = *st;
+  v ^= v << 13;
+  v ^= v >> 7;
+  v ^= v << 17;
+  *st = v;
+  return v;
+}
+static float draw_unit(uint64_t *st) { return (float)((draw_next(st) >> 40) / 16777216.0); }
+
+static uint64_t guess_draw_state(uint64_t seed, uint64_t place, uint64_t part) {
+  uint64_t st = seed ^ (place * 0xD1342543DE82EF95ull) ^ part;
+  st ^= st >> 30;
+  st *= 0xBF58476D1CE4E5B9ull;
+  st ^= st >> 27;
+  st *= 0x94D049BB133111EBull;
+  st ^= st >> 31;
+  return st ? st : 0x2545F4914F6CDD1Dull;
+}
+
+// Top candidates of `lanes` rows of the logits, echo penalty applied per lane
+// over ids [from_j, upto_j) of the session's history.  Fills out[j] with the
+// kept candidates in descending order.
+static int device_top(igc_session *s, int lanes, int keep, const igc_taste *t, const int *echo_from,
+                      const int *echo_upto, std::vector<std::vector<Slot>> &out) {
+  igc_model *m = s->m;
+  const int32_t *d_echo = nullptr;
+  const int *d_from = nullptr, *d_upto = nullptr;
+  if (t->echo_penalty != 1.0f && t->echo_window > 0 && !s->echo.empty()) {
+    CK(cudaMemcpyAsync(s->d_echo, s->echo.data(), sizeof(int32_t) * s->echo.size(), cudaMemcpyHostToDevice, s->st));
+    std::vector<int> rng((size_t)2 * lanes);
+    for (int j = 0; j < lanes; ++j) {
+      rng[j] = echo_from[j];
+      rng[lanes + j] = echo_upto[j];
+    }
+    CK(cudaMemcpyAsync(s->d_echo_range, rng.data(), sizeof(int) * rng.size(), cudaMemcpyHostToDevice, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    d_echo = s->d_echo;
+    d_from = s->d_echo_range;
+    d_upto = s->d_echo_range + lanes;
+  }
+  CKL(igc_launch_topk(s->logits, m->vocab, lanes, keep, d_echo, d_from, d_upto, t->echo_penalty, s->cand_v,
+                      s->cand_i, s->top_v, s->top_i, s->st));
+  ++g_launches;
+  CK(cudaMemcpyAsync(s->h_top_v, s->top_v, sizeof(float) * (size_t)lanes * keep, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaMemcpyAsync(s->h_top_i, s->top_i, sizeof(int) * (size_t)lanes * keep, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  out.assign((size_t)lanes, {});
+  for (int j = 0; j < lanes; ++j) {
+    out[j].resize((size_t)keep);
+    for (int i = 0; i < keep; ++i) out[j][i] = Slot{s->h_top_v[j * keep + i], s->h_top_i[j * keep + i]};
+  }
+  return IGC_OKAY;
+}
+
+// pick_shape after the selection: softmax at the heat, top-p cut, renorm.
+static int shape_slots(std::vector<Slot> &sl, const igc_taste *t) {
+  int keep = (int)sl.size();
+  float total = 0.0f;
+  float peak = sl[0].w;
+  for (int i = 0; i < keep; ++i) {
+    sl[i].w = expf((sl[i].w - peak) / t->heat_value);
+    total += sl[i].w;
+  }
+  if (total <= 0.0f) {
+    sl[0].w = 1.0f;
+    return 1;
+  }
+  for (int i = 0; i < keep; ++i) sl[i].w /= total;
+  if (t->top_portion > 0.0f && t->top_portion < 1.0f) {
+    float run = 0.0f;
+    for (int i = 0; i < keep; ++i) {
+      run += sl[i].w;
+      if (run >= t->top_portion) {
+        keep = i + 1;
+        break;
+      }
+    }
+    total = 0.0f;
+    for (int i = 0; i < keep; ++i) total += sl[i].w;
+    for (int i = 0; i < keep; ++i) sl[i].w /= total;
+  }
+  return keep;
+}
+
+static int32_t pick_draw(const std::vector<Slot> &sl, int keep, float u) {
+  for (int i = 0; i < keep; ++i) {
+    u -= sl[i].w;
+    if (u <= 0.0f) return sl[i].id;
+  }
+  return sl[keep - 1].id;
+}
+
+static int taste_keep(const igc_model *m, const igc_taste *t) {
+  return t->top_count > 0 && t->top_count < m->vocab ? t->top_count : m->vocab;
+}
+
+// Candidate rows for the sampler: the device selection where top-k bounds the
+// set (at most 256), the whole row otherwise.
+static int shaped_rows(igc_session *s, int lanes, const igc_taste *t, const int *from, const int *upto,
+                       std::vector<std::vector<Slot>> &rows) {
+  int keep = taste_keep(s->m, t);
+  if (keep <= 256) return device_top(s, lanes, keep, t, from, upto, rows);
+  std::vector<float> all((size_t)lanes * s->m->vocab);
+  CK(cudaMemcpy(all.data(), s->logits, sizeof(float) * all.size(), cudaMemcpyDeviceToHost));
+  rows.assign((size_t)lanes, {});
+  for (int j = 0; j < lanes; ++j) {
+    std::vector<Slot> &sl = rows[j];
+    sl.resize((size_t)s->m->vocab);
+    for (int i = 0; i < s->m->vocab; ++i) sl[i] = Slot{all[(size_t)j * s->m->vocab + i], i};
+    if (t->echo_penalty != 1.0f && t->echo_window > 0)
+      for (int e = from[j]; e < upto[j]; ++e) {
+        int32_t id = s->echo[e];
+        if (id < 0 || id >= s->m->vocab) continue;
+        sl[id].w = sl[id].w > 0.0f ? sl[id].w / t->echo_penalty : sl[id].w * t->echo_penalty;
+      }
+    std::stable_sort(sl.begin(), sl.end(), [](const Slot &a, const Slot &b) { return a.w > b.w; });
+    sl.resize((size_t)keep);
+  }
+  return IGC_OKAY;
+}
+
+extern "C" int32_t igc_session_pick(igc_session *s, const igc_taste *t) { /* app_core.c:14810 */
+  if (!s || !t || s->logit_lanes < 1) return -1;
+  if (t->seed_value) s->draw_state = t->seed_value ^ (uint64_t)s->fill;
+  int last = s->logit_lanes - 1;
+  if (t->heat_value <= 0.0f) return s->h_top[last];
+  int n = (int)s->echo.size();
+  int from = n - t->echo_window > 0 ? n - t->echo_window : 0;
+  std::vector<std::vector<Slot>> rows;
+  // the step's row is the last lane of the last pass; shaping it alone
+  if (last != 0) return -1;
+  if (shaped_rows(s, 1, t, &from, &n, rows) != IGC_OKAY) return -1;
+  int keep = shape_slots(rows[0], t);
+  return pick_draw(rows[0], keep, draw_unit(&s->draw_state));
+}
+
+#define DRAW_TAKE 0x9E3779B97F4A7C15ull
+#define DRAW_MAKE 0xC2B2AE3D27D4EB4Full
+
+extern "C" int igc_session_guess_taste(igc_session *s, const int32_t *ids, int k, const igc_taste *t,
+                                       int32_t *made_out) {
+  if (!s || !ids || !made_out || !t) return -1;
+  if (k < 1 || s->guess_count != k) return -1;
+  if (t->heat_value <= 0.0f) return -1;
+  std::vector<int> from((size_t)k), upto((size_t)k);
+  for (int j = 0; j < k; ++j) {
+    int echo_count = s->guess_echo + j + 1;
+    if (echo_count > s->m->window_limit) echo_count = s->m->window_limit;
+    upto[j] = echo_count;
+    from[j] = echo_count - t->echo_window > 0 ? echo_count - t->echo_window : 0;
+  }
+  std::vector<std::vector<Slot>> rows;
+  if (shaped_rows(s, k, t, from.data(), upto.data(), rows) != IGC_OKAY) return -1;
+  int take = 0;
+  for (int j = 0; j < k; ++j) {
+    std::vector<Slot> &sl = rows[j];
+    uint64_t place = (uint64_t)(s->guess_from + j + 1);
+    int keep = shape_slots(sl, t);
+    if (j + 1 < k) {
+      int32_t want = ids[j + 1];
+      float share = 0.0f;
+      for (int i = 0; i < keep; ++i)
+        if (sl[i].id == want) { share = sl[i].w; break; }
+      uint64_t st = t->seed_value ? guess_draw_state(t->seed_value, place, DRAW_TAKE) : s->draw_state;
+      float u = draw_unit(&st);
+      if (!t->seed_value) s->draw_state = st;
+      if (u < share) {
+        take += 1;
+        continue;
+      }
+      int fill = 0;
+      float total = 0.0f;
+      for (int i = 0; i < keep; ++i) {
+        if (sl[i].id == want) continue;
+        sl[fill++] = sl[i];
+        total += sl[i].w;
+      }
+      if (fill < 1 || !(total > 0.0f)) {
+        *made_out = want;
+        return take;
+      }
+      for (int i = 0; i < fill; ++i) sl[i].w /= total;
+      keep = fill;
+    }
+    uint64_t st = t->seed_value ? guess_draw_state(t->seed_value, place, DRAW_MAKE) : s->draw_state;
+    float u = draw_unit(&st);
+    if (!t->seed_value) s->draw_state = st;
+    *made_out = pick_draw(sl, keep, u);
+    return take;
+  }
+  return take;
+}
+
+// app_main.c:520 main_answer_guess's round body: guess, verify, keep.
+extern "C" int igc_session_round(igc_session *s, const int32_t *ids, int k, const igc_taste *t, int32_t *take_out,
+                                 int32_t *made_out) {
+  if (!s || !ids || k < 1) return IGC_FAIL_ARGUMENT;
+  int c = igc_session_guess(s, ids, k, nullptr);
+  if (c != IGC_OKAY) return c;
+  int take = 0;
+  int32_t made = 0;
+  if (t && t->heat_value > 0.0f) {
+    take = igc_session_guess_taste(s, ids, k, t, &made);
+    if (take < 0) {
+      igc_session_guess_keep(s, 0);
+      return IGC_FAIL_STATE;
+    }
+  } else {
+    while (take + 1 < k && s->h_top[take] == ids[take + 1]) ++take;
+    made = s->h_top[take];
+  }
+  c = igc_session_guess_keep(s, take + 1);
+  if (c != IGC_OKAY) return c;
+  if (take_out) *take_out = take;
+  if (made_out) *made_out = made;
+  return take + 1;
+}
+
+

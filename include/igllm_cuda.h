@@ -1,0 +1,239 @@
+/* igllm_cuda.h - libigllm_cuda: the B200 backend for the speculative verify
+ * round of the Gemma-4-E2B text stack (iamhaymc/igllm, "INFERGEM").
+ *
+ * A plain C ABI: no C++ types, no device pointers cross it.  Every entry that
+ * has a counterpart in the reference engine names it (file:line in the
+ * reference's app_core.c / app_main.c) and keeps its argument meaning and its
+ * error behaviour: results are the reference's app_code values, zero for
+ * success and negative for failure, and a refused call leaves the session as
+ * it was.
+ *
+ * Two layers are exported.
+ *
+ *  1. The backend table (`igc_desk`), the device twin of the reference's
+ *     `back_desk` (app_core.c:5222-5245): the six entries the engine reaches
+ *     through `model->desk.X`, with host pointers in and out, synchronous.  A
+ *     reference build binds it where it calls `back_open` (app_core.c:5415).
+ *  2. The session layer, the device twin of the reference's public API
+ *     (app_core.c:158-425): model load, session open/prime/step, the guess
+ *     block, its keep and its tempered verify.  The whole pass runs on the
+ *     GPU with the weights resident in HBM; only ids go in and only ids (or,
+ *     on request, logit rows) come out.
+ *
+ * Threading: one caller at a time per session (the reference's rule,
+ * app_core.c:7789-7793).  Separate sessions, and separate models on separate
+ * devices, may be driven from separate threads.
+ */
+#ifndef IGLLM_CUDA_H
+#define IGLLM_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* app_core.c:40-49 app_code, plus one code the CPU engine never needed. */
+#define IGC_OKAY 0
+#define IGC_FAIL_ARGUMENT (-1)
+#define IGC_FAIL_MEMORY (-2)
+#define IGC_FAIL_FILE (-3)
+#define IGC_FAIL_FORMAT (-4)
+#define IGC_FAIL_MISSING (-5)
+#define IGC_FAIL_SUPPORT (-6)
+#define IGC_FAIL_STATE (-7)
+#define IGC_FAIL_DEVICE (-8) /* a CUDA call failed; igc_last_error() says which */
+
+#define IGC_LANE_LIMIT 16 /* app_core.c:1980 KERN_LANE_LIMIT */
+
+/* app_core.c:52-57 app_setup.  `thread_count` becomes the device ordinal:
+ * intra-op parallelism is the GPU's, and a process picks its GPU here.
+ * `window_limit` is the context length (0 keeps the checkpoint's
+ * max_position_embeddings, capped at 32768 so a default session stays a few
+ * hundred MB of HBM). */
+typedef struct igc_setup {
+  int device;
+  int window_limit;
+  int verbose_level;
+  int cache_bits; /* 0 only: caches are float, as app_setup.cache_bits = 0 */
+} igc_setup;
+
+/* app_core.c:60-67 app_taste, field for field. */
+typedef struct igc_taste {
+  float heat_value;
+  int top_count;
+  float top_portion;
+  float echo_penalty;
+  int echo_window;
+  uint64_t seed_value;
+} igc_taste;
+
+/* A weight matrix as the reference's `plane` describes it (app_core.c:1775-1797),
+ * restated with plain types so the reference can hand one across without
+ * this library seeing its struct.  `form` is 1 for a dense matrix (real_data
+ * of real_type) and 2 for a packed code plane.  Type codes are the
+ * reference's store_type values (app_core.c:1412): 1 F32, 2 F16, 3 BF16. */
+typedef struct igc_plane {
+  int form;
+  int row_count;
+  int col_count;
+  const void *real_data;
+  int real_type;
+  const uint8_t *code_data;
+  size_t row_stride;
+  const void *gain_data;
+  int gain_type;
+  const int8_t *bias_data;
+  int bit_count;
+  int code_bias;
+  int code_flip;
+  int group_size;
+  int group_count;
+  float enter_gain;
+  float leave_gain;
+} igc_plane;
+
+/* ---- 1. the backend table (app_core.c:5222-5245 back_desk) ------------- */
+
+typedef struct igc_desk igc_desk;
+struct igc_desk {
+  const char *name_text; /* "cuda/sm_100a" */
+  void *state;           /* the device, its stream, uploaded planes */
+  void (*mat_vec)(igc_desk *desk, const igc_plane *sheet, const float *act_data, float *out_data);
+  void (*mat_mat)(igc_desk *desk, const igc_plane *sheet, const float *act_data, int act_stride,
+                  int lane_count, float *out_data, int out_stride);
+  void (*norm_rms)(igc_desk *desk, const float *value_list, const float *gain_list,
+                   int value_count, float eps_value, float *value_out);
+  void (*soft_max)(igc_desk *desk, float *value_list, int value_count);
+  void (*gelu_gate)(igc_desk *desk, float *gate_list, const float *rise_list, int value_count);
+  void (*rope_turn)(igc_desk *desk, float *value_list, int head_size, const float *cos_list,
+                    const float *sin_list);
+};
+
+/* Replaces app_core.c:5415 back_open.  Each code plane is uploaded to HBM the
+ * first time a product names it (keyed by its code pointer) and stays there
+ * until igc_back_close.  Unsupported plane forms make the entry return
+ * without writing and set igc_desk_status to IGC_FAIL_SUPPORT. */
+int igc_back_open(igc_desk *desk, int device);
+/* Replaces app_core.c:5445 back_close. */
+void igc_back_close(igc_desk *desk);
+/* The first failure any entry of this desk met since the last call, then 0. */
+int igc_desk_status(igc_desk *desk);
+
+/* ---- 2. the session layer ----------------------------------------------- */
+
+typedef struct igc_model igc_model;
+typedef struct igc_session igc_session;
+
+/* app_core.c:12439 model_load: config.json + model.safetensors (or a sharded
+ * index) from `folder`, every bound plane uploaded once to HBM. */
+int igc_model_load(const char *folder, const igc_setup *setup, igc_model **model_out);
+/* app_core.c:12602 model_free */
+void igc_model_free(igc_model *model);
+int igc_model_vocab_count(const igc_model *model);  /* app_core.c:12664 */
+int igc_model_layer_count(const igc_model *model);  /* app_core.c:12663 */
+int igc_model_state_size(const igc_model *model);   /* app_core.c:12666 */
+int igc_model_window_limit(const igc_model *model); /* app_core.c:12665 */
+/* app_core.c:12747 model_decode_bytes: the bytes one decode step reads by the
+ * reference's rule, counted on this library's own bound planes. */
+size_t igc_model_decode_bytes(const igc_model *model);
+/* Device bytes the model holds (weights as uploaded, packed). */
+size_t igc_model_device_bytes(const igc_model *model);
+
+/* app_core.c:14219 session_open / :14368 session_close / :14375 session_reset */
+int igc_session_open(igc_model *model, igc_session **session_out);
+void igc_session_close(igc_session *session);
+void igc_session_reset(igc_session *session);
+/* app_core.c:13935 session_hold.  Caches are full length, so no ring turns
+ * over and the APP_FAIL_SUPPORT refusal never arises. */
+int igc_session_hold(igc_session *session, int keep_count);
+/* app_core.c:14443 session_prime: every id but the last, 16 lanes a pass. */
+int igc_session_prime(igc_session *session, const int32_t *id_list, int id_count);
+/* app_core.c:14473 session_step.  The reference returns a pointer to the
+ * logit row; here the row is copied to `logits_out` when it is not NULL and
+ * its argmax (app_main.c:482 main_guess_top) to `top_out` when that is not
+ * NULL.  IGC_FAIL_STATE while a block is in flight. */
+int igc_session_step(igc_session *session, int32_t id_value, float *logits_out, int32_t *top_out);
+/* app_core.c:12139 session_guess: `id_count` (1..16) lanes in one pass, one
+ * row of logits a lane kept on the device; copied to `logits_out`
+ * (id_count x vocab floats) when it is not NULL.  Refused (IGC_FAIL_STATE)
+ * while a block is already in flight. */
+int igc_session_guess(igc_session *session, const int32_t *id_list, int id_count,
+                      float *logits_out);
+/* The argmax of each row of the block in flight (app_main.c:482, first index
+ * on a tie), id_count ids into `top_out`. */
+int igc_session_guess_top(igc_session *session, int32_t *top_out);
+/* app_core.c:12205 session_guess_keep */
+int igc_session_guess_keep(igc_session *session, int keep_count);
+/* app_core.c:14762 session_guess_taste on the rows of the block in flight
+ * (the reference takes them as `row_list`; here they never leave the GPU).
+ * Returns the guesses kept and writes the following token to `made_out`;
+ * -1 when refused (greedy taste, no block, count mismatch). */
+int igc_session_guess_taste(igc_session *session, const int32_t *id_list, int id_count,
+                            const igc_taste *taste, int32_t *made_out);
+/* app_core.c:14844 session_pick on the row the last step produced. */
+int32_t igc_session_pick(igc_session *session, const igc_taste *taste);
+int igc_session_fill(const igc_session *session);        /* app_core.c:14513 */
+int igc_session_guess_span(const igc_session *session);  /* app_core.c:12364 */
+int igc_session_guess_limit(const igc_session *session); /* app_core.c:12368 */
+
+/* One whole verify round, the body of app_main.c:520 main_answer_guess's
+ * loop after the scout has drawn: guess the block, verify it (argmax
+ * comparison at heat 0, the rejection rule above it), keep the accepted
+ * lanes and the token after them.  Writes the kept guess count to
+ * `take_out` and the token after them to `made_out`, and returns
+ * take + 1, the tokens committed; negative on refusal. */
+int igc_session_round(igc_session *session, const int32_t *id_list, int id_count,
+                      const igc_taste *taste, int32_t *take_out, int32_t *made_out);
+
+/* Wall-clock seconds and committed tokens of the passes this session ran as
+ * steps and blocks (app_core.c:70-77 app_tally serve_seconds/serve_tokens). */
+double igc_session_serve_seconds(const igc_session *session);
+size_t igc_session_serve_tokens(const igc_session *session);
+
+/* ---- n-gram scout (app_core.c:12277-12361), host C --------------------- */
+
+typedef struct igc_scout igc_scout;
+int igc_scout_open(igc_scout **scout_out);
+void igc_scout_close(igc_scout *scout);
+void igc_scout_clear(igc_scout *scout);
+int igc_scout_note(igc_scout *scout, const int32_t *id_list, int id_count);
+int igc_scout_span(const igc_scout *scout);
+int igc_scout_draw(const igc_scout *scout, int32_t *id_out, int want_count);
+
+/* ---- synthetic checkpoints (no counterpart in the reference) ------------
+ *
+ * Seeded weights of a stated shape, generated by a counter-based hash so the
+ * same value lands at the same index whether it is written to a safetensors
+ * file for the CPU engine or generated straight into HBM. */
+typedef struct igc_synth_spec {
+  int vocab, hidden, layers, heads, kv_heads, head_dim, inner, ple_dim;
+  int slide_span, share_count, global_every; /* global layer when (l+1) % every == 0, last forced */
+  int window_limit;
+  float norm_offset;   /* 0: norms N(0,0.02); 1: norms 1+N(0,0.02) */
+  int with_layer_scalar; /* write layer_scalar = 1+N(0,0.02); 0 leaves it out (gain 1) */
+  uint64_t seed;
+} igc_synth_spec;
+
+/* Fill `out` with `count` values of stream `stream` of the spec's seed.
+ * kind 0: packed int4 bytes (two uniform codes a byte, low nibble first);
+ * kind 1: f16 |N(0,0.02)| bits; kind 2: bf16 N(0,0.02) bits;
+ * kind 3: bf16 offset + N(0,0.02) bits (offset = norm_offset). */
+int igc_synth_fill(uint64_t seed, uint64_t stream, int kind, float offset, size_t count, void *out,
+                   int threads);
+/* Write config.json, tokenizer.json and model.safetensors for the spec under
+ * `folder` (which must exist), readable by the reference's model_load. */
+int igc_synth_write(const igc_synth_spec *spec, const char *folder, int threads);
+/* Build a model of that spec directly in HBM, no file in between. */
+int igc_model_synth(const igc_synth_spec *spec, const igc_setup *setup, igc_model **model_out);
+
+/* The message of the last CUDA failure on this thread ("" when none). */
+const char *igc_last_error(void);
+/* Kernels this library launched on this thread since the last call, then 0. */
+long igc_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* IGLLM_CUDA_H */

@@ -1,0 +1,76 @@
+import os
+import sys
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
+
+
+def _built(path, builder):
+    if not os.path.exists(path):
+        builder()
+    return path
+
+
+@pytest.fixture(scope="session")
+def igc_lib():
+    import igllm_b200
+    from igllm_b200 import build
+    _built(igllm_b200.LIB_PATH, build.build)
+    return igllm_b200
+
+
+@pytest.fixture(scope="session")
+def igo_mod():
+    import igo
+    _built(igo.IGO_LIB, igo.build)
+    return igo
+
+
+TINY = dict(vocab=512, hidden=128, layers=7, heads=2, kv_heads=1, head_dim=64, inner=256, ple_dim=32,
+            slide_span=8, share_count=2, global_every=3, window_limit=256, norm_offset=1.0,
+            with_layer_scalar=1, seed=7)
+
+# Wider than one 64-column chunk in every direction, 8 query heads against 1
+# key/value head like the export, a window the block straddles, and ple_dim 32
+# (a half chunk, so the padded-column path of the projections runs).
+SMALL = dict(vocab=4096, hidden=256, layers=8, heads=8, kv_heads=1, head_dim=32, inner=512, ple_dim=32,
+             slide_span=16, share_count=3, global_every=4, window_limit=512, norm_offset=1.0,
+             with_layer_scalar=1, seed=11)
+
+# The export's literal norm distribution, N(0, 0.02) used as is.
+LITERAL = dict(TINY, norm_offset=0.0, with_layer_scalar=0, seed=3)
+
+
+def make_checkpoint(lib, folder, cfg):
+    spec = lib.SynthSpec(**cfg)
+    if not os.path.exists(os.path.join(folder, "model.safetensors")):
+        lib.synth_write(spec, folder, 4)
+    return spec
+
+
+@pytest.fixture(scope="session")
+def tiny_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("tiny"))
+    make_checkpoint(igc_lib, d, TINY)
+    return d
+
+
+@pytest.fixture(scope="session")
+def small_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("small"))
+    make_checkpoint(igc_lib, d, SMALL)
+    return d
+
+
+@pytest.fixture(scope="session")
+def literal_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("literal"))
+    make_checkpoint(igc_lib, d, LITERAL)
+    return d
