@@ -415,6 +415,48 @@ def synth_write(spec, folder, threads=8):
     _check(_lib().igc_synth_write(ctypes.byref(spec), str(folder).encode(), int(threads)), "synth_write")
 
 
+class SynthTensor(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 128), ("dtype", ctypes.c_int), ("rank", ctypes.c_int),
+                ("shape", ctypes.c_int64 * 2), ("kind", ctypes.c_int), ("offset", ctypes.c_float),
+                ("bytes", ctypes.c_size_t)]
+
+
+_DTYPE_NAME = {1: "F32", 2: "F16", 3: "BF16", 6: "U8"}
+
+
+def synth_tensors(spec, threads=8):
+    """Every tensor of a synthetic checkpoint, generated in memory:
+    name -> (dtype name, numpy array of the stored bits)."""
+    lib = _lib()
+    lib.igc_synth_list.restype = ctypes.c_int
+    lib.igc_synth_list.argtypes = [_P(SynthSpec), ctypes.c_void_p, ctypes.c_int]
+    lib.igc_synth_tensor_fill.restype = ctypes.c_int
+    lib.igc_synth_tensor_fill.argtypes = [_P(SynthSpec), _P(SynthTensor), ctypes.c_void_p, ctypes.c_int]
+    n = lib.igc_synth_list(ctypes.byref(spec), None, 0)
+    room = (SynthTensor * n)()
+    lib.igc_synth_list(ctypes.byref(spec), room, n)
+    out = {}
+    for t in room:
+        shape = [t.shape[0], t.shape[1]] if t.rank == 2 else [t.shape[0]]
+        arr = np.empty(shape, np.uint8 if t.dtype == 6 else np.uint16)
+        _check(lib.igc_synth_tensor_fill(ctypes.byref(spec), ctypes.byref(t), arr.ctypes.data_as(ctypes.c_void_p),
+                                         threads), "synth_tensor_fill")
+        out[t.name.decode()] = (_DTYPE_NAME[t.dtype], arr)
+    return out
+
+
+def synth_config(spec):
+    """The config.json a synthetic checkpoint carries, parsed."""
+    import json
+    lib = _lib()
+    lib.igc_synth_config_text.restype = ctypes.c_void_p
+    lib.igc_synth_config_text.argtypes = [_P(SynthSpec)]
+    p = lib.igc_synth_config_text(ctypes.byref(spec))
+    text = ctypes.string_at(p).decode()
+    ctypes.CDLL(None).free(ctypes.c_void_p(p))
+    return json.loads(text)
+
+
 def synth_fill(seed, name, kind, count, offset=0.0, threads=1):
     """The values of one synthetic tensor stream (kind 0 bytes, else u16 bits)."""
     lib = _lib()

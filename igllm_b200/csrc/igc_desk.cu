@@ -39,7 +39,10 @@ struct DeskState {
   int *arg_idx = nullptr;
 };
 
-DeskState *state_of(igc_desk *d) { return static_cast<DeskState *>(d->state); }
+DeskState *state_of(igc_desk *d) {
+  cudaGetLastError();  // an unchecked failure elsewhere must not be charged to this entry
+  return static_cast<DeskState *>(d->state);
+}
 
 bool note(DeskState *s, int code) {
   if (code != IGC_OKAY && s->status == IGC_OKAY) s->status = code;

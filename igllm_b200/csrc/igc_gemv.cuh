@@ -11,11 +11,19 @@
 // adds almost nothing until the sweep stops being memory bound.
 //
 // Precision: a weight code minus eight is an exact f16 integer, so the only
-// rounding before the f32 accumulator is the activation's.  Each activation
-// is staged as two f16 values, hi = f16(a) and lo = f16(a - hi), and both go
-// through the tensor core against the same dequantised weights: the product
-// carries about 22 significant bits of the activation, against the
-// reference's 24, at the cost of a second MMA per 16 columns.
+// rounding before the f32 accumulator is the activation's.  Each lane's
+// activations are first scaled by a power of two that puts the lane's largest
+// magnitude at 2^14 (exact, undone in the epilogue), then staged as two f16
+// values, hi = f16(a) and lo = f16(a - hi); both go through the tensor core
+// against the same dequantised weights, so the product carries about 22
+// significant bits of the activation at the cost of a second MMA per 16
+// columns, and no lane can overflow f16.
+//
+// Norms ride on linearity: W (norm(y) * w) = shrink(y) * W (y * w), so the
+// prologue stages y * w in one elementwise pass and the epilogue multiplies by
+// the shrink, whose sum of squares the same pass collects.  A residual
+// y = x + norm(p) * w_res needs p's shrink first; p's producer wrote the sum
+// of its squares as one partial per block (fixed order, so deterministic).
 //
 // Layout in HBM (written once by the upload repack, igc_repack_kernel):
 //   tiles  : [row_block][chunk][32 threads] uint4 - one 16-row x 64-column
@@ -25,6 +33,8 @@
 //            the f16 scales of rows g and g+8 for the chunk's two groups.
 // Row blocks are 16 rows; chunks are 64 columns (two groups of 32).
 #pragma once
+
+#include <cuda_bf16.h>
 
 #include "igc_device.cuh"
 
@@ -56,6 +66,9 @@ struct GemvArgs {
   const float *w_in;
   float eps;
   float *x_out;
+  const float *p_ssq;  // producer's partial sums of squares of p, [p_parts][16]
+  int p_parts;
+  float *out_ssq;      // this launch's partial sums of squares of out, [gridDim.x][16]
   // epilogue
   float *out;
   int out_stride;
@@ -87,156 +100,153 @@ __device__ __forceinline__ float rms_shrink(float ssq, int n, float eps) {
   return (float)(1.0 / sqrt((double)ssq / (double)n + (double)eps));
 }
 
-// Writes two consecutive columns (c even) of lane n as hi/lo f16 pairs.
+// First pass: two consecutive columns (c even) of lane n as raw f32 in the
+// two words their hi and lo f16 pairs will occupy.
 __device__ __forceinline__ void stage_pair(uint32_t *stage, int n, int c, float a0, float a1, int NT) {
+  int w = stage_word(n, c, NT);
+  stage[w] = __float_as_uint(a0);
+  stage[w + 8] = __float_as_uint(a1);
+}
+
+// Second pass, over the same words the same thread wrote: scaled, split into
+// hi/lo f16 pairs.
+__device__ __forceinline__ void stage_seal(uint32_t *stage, int n, int c, float scale, int NT) {
+  int w = stage_word(n, c, NT);
+  float a0 = __uint_as_float(stage[w]) * scale, a1 = __uint_as_float(stage[w + 8]) * scale;
   __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
   __half l0 = __float2half_rn(a0 - __half2float(h0)), l1 = __float2half_rn(a1 - __half2float(h1));
-  int w = stage_word(n, c, NT);
   __half2 hi = __halves2half2(h0, h1), lo = __halves2half2(l0, l1);
   stage[w] = *reinterpret_cast<uint32_t *>(&hi);
   stage[w + 8] = *reinterpret_cast<uint32_t *>(&lo);
 }
 
-// Per-lane block reduction of up to 16 partial sums; every thread gets all.
-__device__ __forceinline__ void block_sum16(float (&v)[16], int K, float *red /* [8][16] */) {
-  const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
-#pragma unroll
-  for (int j = 0; j < 16; ++j)
-    if (j < K) v[j] = warp_sum(v[j]);
-  if (l32 == 0)
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < K) red[warp * 16 + j] = v[j];
-  __syncthreads();
-#pragma unroll
-  for (int j = 0; j < 16; ++j)
-    if (j < K) {
-      float s = 0.0f;
-#pragma unroll
-      for (int w = 0; w < GEMV_WARPS; ++w) s += red[w * 16 + j];
-      v[j] = s;
-    }
-  __syncthreads();
+// The power of two that puts a lane's largest magnitude at or under 2^14.
+__device__ __forceinline__ float lane_scale(float amax) {
+  if (!(amax > 0.0f) || !isfinite(amax)) return 1.0f;
+  int e;
+  frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+  return ldexpf(1.0f, 14 - e);
 }
 
-// The prologue: every thread takes float4 columns for every lane, so the
-// loads of one phase are all in flight together.  Norms need a reduction over
-// the lane's whole vector: one phase per reduction.
+__device__ __forceinline__ float fmax4(float4 v) { return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))); }
+
+// Shared-memory scratch the prologue leaves for the epilogue and uses for its
+// own reductions (floats, after the staged activations):
+//   [0, 16)      per-lane factor the epilogue applies (norm shrink / 2^e)
+//   [16, 32)     per-lane power-of-two staging scale
+//   [32, 48)     per-lane shrink of the residual's norm
+//   [64, 192)    per-(lane, part) sums of squares
+//   [192, 320)   per-(lane, part) magnitudes
+//   [320, 576)   per-thread stripes of the residual's sums of squares
+constexpr int SCR_FACTOR = 0, SCR_SCALE = 16, SCR_SHRINK_P = 32, SCR_SSQ = 64, SCR_AMAX = 192, SCR_STRIPE = 320;
+constexpr int SCR_FLOATS = 576;
+
+// The prologue, one elementwise pass and one shared-memory pass.  Warps take
+// lanes: with K < 8 lanes, 8/K warps (a power of two) split one lane's
+// columns; with more, a warp takes lanes w and w + 8.  Each thread walks its
+// float4 columns with four loads in flight, and the per-lane reductions are
+// a fixed-order sum over the parts.
 template <int PRO>
-__device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *red, int NT) {
+__device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr, int NT) {
   const int cols = a.pl.cols, K = a.lanes, n4 = cols >> 2;
+  const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
   const int stage_words = (int)(gemv_stage_bytes(a.pl.n_cc, NT) / 4);
   for (int i = threadIdx.x; i < stage_words / 4; i += blockDim.x)
     reinterpret_cast<uint4 *>(stage)[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (PRO == PRO_RESID || PRO == PRO_RESID_NORM) {
+    // the residual's shrink from its producer's partials: thread (lane j,
+    // stripe q0) sums parts q0, q0 + 16, ...; stripes are then added in order
+    const int j = threadIdx.x & 15, q0 = threadIdx.x >> 4;
+    float t = 0.0f;
+    if (j < K)
+      for (int q = q0; q < a.p_parts; q += 16) t += a.p_ssq[q * 16 + j];
+    scr[SCR_STRIPE + threadIdx.x] = t;
+    __syncthreads();
+    if (threadIdx.x < 16 && (int)threadIdx.x < K) {
+      float u = 0.0f;
+      for (int q = 0; q < 16; ++q) u += scr[SCR_STRIPE + q * 16 + threadIdx.x];
+      scr[SCR_SHRINK_P + threadIdx.x] = rms_shrink(u, cols, a.eps);
+    }
+  }
   __syncthreads();
+  int wpl = 1;  // warps a lane
+  while (wpl * 2 * K <= GEMV_WARPS) wpl *= 2;
+  const int n_slots = (K + GEMV_WARPS - 1) / GEMV_WARPS;  // lanes a warp (1 or 2)
   const float4 *__restrict__ x4 = reinterpret_cast<const float4 *>(a.x);
-  const int xs4 = a.x_stride >> 2;
-  if (PRO == PRO_F32) {
-    for (int e = threadIdx.x; e < K * n4; e += blockDim.x) {
-      int j = e / n4, c4 = e - j * n4;
-      float4 v = x4[(size_t)j * xs4 + c4];
-      stage_pair(stage, j, c4 * 4, v.x, v.y, NT);
-      stage_pair(stage, j, c4 * 4 + 2, v.z, v.w, NT);
-    }
-    __syncthreads();
-    return;
-  }
-  const float4 *__restrict__ win4 = reinterpret_cast<const float4 *>(a.w_in);
-  float s[16];
-  if (PRO == PRO_NORM) {
-#pragma unroll
-    for (int j = 0; j < 16; ++j) s[j] = 0.0f;
-    for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x)
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < K) {
-          float4 v = x4[(size_t)j * xs4 + c4];
-          s[j] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        }
-    block_sum16(s, K, red);
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < K) s[j] = rms_shrink(s[j], cols, a.eps);
-    for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x) {
-      float4 w = win4[c4];
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < K) {
-          float4 v = x4[(size_t)j * xs4 + c4];
-          stage_pair(stage, j, c4 * 4, v.x * s[j] * w.x, v.y * s[j] * w.y, NT);
-          stage_pair(stage, j, c4 * 4 + 2, v.z * s[j] * w.z, v.w * s[j] * w.w, NT);
-        }
-    }
-    __syncthreads();
-    return;
-  }
-  // residual forms: y = (x + norm(p) * w_res) * gain
   const float4 *__restrict__ p4 = reinterpret_cast<const float4 *>(a.p);
   const float4 *__restrict__ wr4 = reinterpret_cast<const float4 *>(a.w_res);
-  const int ps4 = a.p_stride >> 2;
-  float sp[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) sp[j] = 0.0f;
-  for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x)
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < K) {
-        float4 v = p4[(size_t)j * ps4 + c4];
-        sp[j] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-      }
-  block_sum16(sp, K, red);
-#pragma unroll
-  for (int j = 0; j < 16; ++j)
-    if (j < K) sp[j] = rms_shrink(sp[j], cols, a.eps);
-  const bool writer = blockIdx.x == 0 && a.x_out;
-  float4 *xo4 = reinterpret_cast<float4 *>(a.x_out);
+  const float4 *__restrict__ win4 = reinterpret_cast<const float4 *>(a.w_in);
+  float4 *__restrict__ xo4 = (blockIdx.x == 0 && a.x_out) ? reinterpret_cast<float4 *>(a.x_out) : nullptr;
+  const int xs4 = a.x_stride >> 2, ps4 = a.p_stride >> 2;
   const float gain = a.gain;
-  auto resid = [&](int j, int c4, float4 wr) {
-    float4 xv = x4[(size_t)j * xs4 + c4], pv = p4[(size_t)j * ps4 + c4];
-    float4 y;
-    y.x = xv.x + pv.x * sp[j] * wr.x;
-    y.y = xv.y + pv.y * sp[j] * wr.y;
-    y.z = xv.z + pv.z * sp[j] * wr.z;
-    y.w = xv.w + pv.w * sp[j] * wr.w;
-    if (gain != 1.0f) {
-      y.x *= gain;
-      y.y *= gain;
-      y.z *= gain;
-      y.w *= gain;
-    }
-    return y;
-  };
-#pragma unroll
-  for (int j = 0; j < 16; ++j) s[j] = 0.0f;
-  for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x) {
-    float4 wr = wr4[c4];
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < K) {
-        float4 y = resid(j, c4, wr);
-        if (writer) xo4[(size_t)j * xs4 + c4] = y;
-        if (PRO == PRO_RESID) {
-          stage_pair(stage, j, c4 * 4, y.x, y.y, NT);
-          stage_pair(stage, j, c4 * 4 + 2, y.z, y.w, NT);
-        } else {
-          s[j] += y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
+  for (int slot = 0; slot < n_slots; ++slot) {
+    const int j = wpl > 1 ? warp / wpl : warp + slot * GEMV_WARPS;
+    const int part = wpl > 1 ? warp % wpl : 0;
+    float ssq = 0.0f, amax = 0.0f;
+    if (j < K) {
+      const int lo = (n4 * part) / wpl, hi = (n4 * (part + 1)) / wpl;
+      const float sp = (PRO == PRO_RESID || PRO == PRO_RESID_NORM) ? scr[SCR_SHRINK_P + j] : 0.0f;
+#pragma unroll 4
+      for (int c4 = lo + l32; c4 < hi; c4 += 32) {
+        float4 y = x4[(size_t)j * xs4 + c4];
+        if (PRO == PRO_RESID || PRO == PRO_RESID_NORM) {
+          // app_core.c:11690-11740: x += norm(p) * w, then the layer gain
+          float4 pv = p4[(size_t)j * ps4 + c4], wr = wr4[c4];
+          y.x = y.x + pv.x * sp * wr.x;
+          y.y = y.y + pv.y * sp * wr.y;
+          y.z = y.z + pv.z * sp * wr.z;
+          y.w = y.w + pv.w * sp * wr.w;
+          if (gain != 1.0f) {
+            y.x *= gain;
+            y.y *= gain;
+            y.z *= gain;
+            y.w *= gain;
+          }
+          if (xo4) xo4[(size_t)j * xs4 + c4] = y;
         }
+        if (PRO != PRO_F32) ssq += y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
+        if (PRO == PRO_NORM || PRO == PRO_RESID_NORM) {
+          float4 w = win4[c4];
+          y.x *= w.x;
+          y.y *= w.y;
+          y.z *= w.z;
+          y.w *= w.w;
+        }
+        amax = fmaxf(amax, fmax4(y));
+        stage_pair(stage, j, c4 * 4, y.x, y.y, NT);
+        stage_pair(stage, j, c4 * 4 + 2, y.z, y.w, NT);
       }
+    }
+    ssq = warp_sum(ssq);
+    amax = warp_max(amax);
+    if (l32 == 0 && j < K) {
+      scr[SCR_SSQ + j * 8 + part] = ssq;
+      scr[SCR_AMAX + j * 8 + part] = amax;
+    }
   }
-  if (PRO == PRO_RESID_NORM) {
-    block_sum16(s, K, red);
-#pragma unroll
-    for (int j = 0; j < 16; ++j)
-      if (j < K) s[j] = rms_shrink(s[j], cols, a.eps);
-    for (int c4 = threadIdx.x; c4 < n4; c4 += blockDim.x) {
-      float4 wr = wr4[c4], w = win4[c4];
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (j < K) {
-          float4 y = resid(j, c4, wr);
-          stage_pair(stage, j, c4 * 4, y.x * s[j] * w.x, y.y * s[j] * w.y, NT);
-          stage_pair(stage, j, c4 * 4 + 2, y.z * s[j] * w.z, y.w * s[j] * w.w, NT);
-        }
+  __syncthreads();
+  if (threadIdx.x < 16 && (int)threadIdx.x < K) {
+    const int j = threadIdx.x;
+    float ssq = 0.0f, amax = 0.0f;
+    for (int q = 0; q < wpl; ++q) {
+      ssq += scr[SCR_SSQ + j * 8 + q];
+      amax = fmaxf(amax, scr[SCR_AMAX + j * 8 + q]);
+    }
+    const float sc = lane_scale(amax);
+    const float shrink = (PRO == PRO_NORM || PRO == PRO_RESID_NORM) ? rms_shrink(ssq, cols, a.eps) : 1.0f;
+    scr[SCR_SCALE + j] = sc;
+    scr[SCR_FACTOR + j] = shrink * (1.0f / sc);
+  }
+  __syncthreads();
+  for (int slot = 0; slot < n_slots; ++slot) {
+    const int j = wpl > 1 ? warp / wpl : warp + slot * GEMV_WARPS;
+    const int part = wpl > 1 ? warp % wpl : 0;
+    if (j >= K) continue;
+    const int lo = (n4 * part) / wpl, hi = (n4 * (part + 1)) / wpl;
+    const float sc = scr[SCR_SCALE + j];
+    for (int c4 = lo + l32; c4 < hi; c4 += 32) {
+      stage_seal(stage, j, c4 * 4, sc, NT);
+      stage_seal(stage, j, c4 * 4 + 2, sc, NT);
     }
   }
   __syncthreads();

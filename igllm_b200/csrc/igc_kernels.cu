@@ -62,9 +62,10 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   uint32_t *stage = reinterpret_cast<uint32_t *>(smem_raw);
   const size_t stage_bytes = gemv_stage_bytes(a.pl.n_cc, NT);
-  float *red = reinterpret_cast<float *>(smem_raw + stage_bytes);  // [8 warps][32][8*NT]
+  float *scr = reinterpret_cast<float *>(smem_raw + stage_bytes);  // prologue scratch
+  float *red = scr + SCR_FLOATS;                                     // [8 warps][32][8*NT]
 
-  gemv_prologue<PRO>(a, stage, red, NT);
+  gemv_prologue<PRO>(a, stage, scr, NT);
 
   const int warp = threadIdx.x >> 5, lane32 = threadIdx.x & 31;
   const int g = lane32 >> 2, t = lane32 & 3;
@@ -74,13 +75,22 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   const int my_unit_off = warp / S, my_slice = warp % S;
   const int c_lo = (a.pl.n_cc * my_slice) / S, c_hi = (a.pl.n_cc * (my_slice + 1)) / S;
 
-  // EPI_LOGITS running argmax per (nt, lane parity)
+  // the epilogue factor of the two lanes each accumulator column holds
+  float sh[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int k = 0; k < 2; ++k) sh[nt][k] = scr[SCR_FACTOR + nt * 8 + 2 * t + k];
+
+  // EPI_LOGITS running argmax, EPI_STORE running sum of squares, per (nt, lane parity)
   float best_v[NT][2];
   int best_i[NT][2];
+  float ssq[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     best_v[nt][0] = best_v[nt][1] = -FLT_MAX;
     best_i[nt][0] = best_i[nt][1] = 0x7fffffff;
+    ssq[nt][0] = ssq[nt][1] = 0.0f;
   }
 
   for (int base = blockIdx.x * per_iter; base < n_units; base += gridDim.x * per_iter) {
@@ -166,26 +176,49 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int row = unit * 16 + g + (i >= 2 ? 8 : 0);
-          const int ln = nt * 8 + 2 * t + (i & 1);
+          const int k = i & 1;
+          const int ln = nt * 8 + 2 * t + k;
           if (row >= a.pl.rows || ln >= a.lanes) continue;
-          float v = tot[0][nt][i];
+          float v = tot[0][nt][i] * sh[nt][k];
           if (EPI == EPI_STORE) {
-            a.out[(size_t)ln * a.out_stride + row] = v * a.out_scale;
+            float o = v * a.out_scale;
+            a.out[(size_t)ln * a.out_stride + row] = o;
+            ssq[nt][k] += o * o;
           } else if (EPI == EPI_GELU_PAIR) {
-            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(v) * tot[PAIR][nt][i];
+            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(v) * (tot[PAIR][nt][i] * sh[nt][k]);
           } else if (EPI == EPI_GELU_MUL) {
             a.out[(size_t)ln * a.out_stride + row] =
                 gelu_tanh(v) * a.aux[(size_t)ln * a.aux_stride + row];
           } else {  // EPI_LOGITS
             float cv = a.cap > 0.0f ? logit_cap(v, a.cap) : v;
             a.out[(size_t)ln * a.out_stride + row] = cv;
-            const int k = i & 1;
             if (cv > best_v[nt][k] || (cv == best_v[nt][k] && row < best_i[nt][k])) {
               best_v[nt][k] = cv;
               best_i[nt][k] = row;
             }
           }
         }
+    }
+  }
+
+  if (EPI == EPI_STORE && a.out_ssq) {
+    // per-lane sums of squares of this block's outputs: across the 8 thread
+    // groups that hold the same lanes, then across warps in order
+    __syncthreads();
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float v = ssq[nt][k];
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (g == 0) red[warp * 16 + nt * 8 + 2 * t + k] = v;
+      }
+    __syncthreads();
+    if (threadIdx.x < NT * 8) {
+      float v = 0.0f;
+      for (int w = 0; w < GEMV_WARPS; ++w) v += red[w * 16 + threadIdx.x];
+      a.out_ssq[blockIdx.x * 16 + threadIdx.x] = v;
     }
   }
 
@@ -241,10 +274,12 @@ __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embe
   if (j >= lanes) return;
   int id = ids[j];
   const uint16_t *row = embed + (size_t)id * hidden;
+#pragma unroll 4
   for (int i = threadIdx.x; i < hidden; i += blockDim.x)
     x_out[(size_t)j * hidden + i] = __uint_as_float((uint32_t)row[i] << 16) * embed_gain;
   if (ple_embed) {
     const uint16_t *srow = ple_embed + (size_t)(id % ple_vocab) * ple_width;
+#pragma unroll 8
     for (int i = threadIdx.x; i < ple_width; i += blockDim.x)
       seed_out[(size_t)j * ple_width + i] = __uint_as_float((uint32_t)srow[i] << 16) * ple_gain;
   }
@@ -344,138 +379,220 @@ __global__ void attn_prep_kernel(float *qkv, int qkv_stride, int heads, int kv_h
   }
 }
 
-// attention, step 2: one block a span chunk and a group of up to 8 lanes; the
-// block's partial softmax (max, sum) and weighted value sum go to the
-// partials, combined by attn_combine_kernel.  Score scale is 1.0
-// (app_core.c:11314); sliding layers see [pos - span + 1, pos]
-// (app_core.c:11515-11518).
-constexpr int ATT_TILE = 16;
-constexpr int ATT_LANES = 8;
+// attention, step 2 (app_core.c:11415 session_attend_group, :11296
+// attend_score_band, :11333 attend_blend_band): scores with scale 1.0
+// (app_core.c:11314), softmax, weighted values, over each lane's own span
+// ([pos - window + 1, pos] on sliding layers, [0, pos] on global ones,
+// app_core.c:11515-11518).
+//
+// The span is cut into chunks whose boundaries sit at fixed multiples of
+// the session's chunk length, so a position's partial sums never depend on
+// how many lanes a pass carried; each block takes 32 (lane, head) pairs and
+// walks chunks in 32-position tiles with an online softmax.  Warp w scores
+// positions w, w+8, w+16, w+24 of a tile for all 32 pairs (each thread holds
+// a slice of the head dimension, and a transposing butterfly leaves thread p
+// with pair p's full dot product), then owns pairs 4w..4w+3 for the softmax
+// and the value blend, with their running max, sum and accumulator in its
+// registers.  Partials per chunk go to attn_combine_kernel.
+constexpr int ATT_T = 32;  // positions a tile
+constexpr int ATT_P = 32;  // (lane, head) pairs a block
 
-__host__ __device__ inline size_t attn_smem_floats(int heads, int hd, int kv_w) {
-  size_t pairs = (size_t)ATT_LANES * heads;
-  return pairs * hd                    /* qs   */
-         + (size_t)ATT_TILE * (kv_w + 1) /* ks   */
-         + (size_t)ATT_TILE * kv_w       /* vs   */
-         + pairs * ATT_TILE              /* sc   */
-         + pairs                         /* fac  */
-         + pairs * hd                    /* acc  */
-         + 2 * pairs;                    /* m, l */
+__host__ __device__ inline size_t attn_smem_floats(int hd, int kv_w) {
+  return (size_t)ATT_P * hd + 2 * (size_t)ATT_T * kv_w + (size_t)ATT_P * (ATT_T + 1) + ATT_P;
 }
 
+// DPL consecutive floats from shared memory, as float4 where they fit one.
+template <int DPL>
+__device__ __forceinline__ void load_slice(const float *src, float (&dst)[DPL]) {
+  if constexpr (DPL % 4 == 0) {
+#pragma unroll
+    for (int e = 0; e < DPL; e += 4) {
+      float4 v = *reinterpret_cast<const float4 *>(src + e);
+      dst[e] = v.x;
+      dst[e + 1] = v.y;
+      dst[e + 2] = v.z;
+      dst[e + 3] = v.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) dst[e] = src[e];
+  }
+}
+
+// 32 per-slot partial sums in every thread -> thread l holds slot l's total.
+__device__ __forceinline__ float transpose_sum32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < o; ++i) {
+      float send = up ? v[i] : v[i + o];
+      float keep = up ? v[i + o] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  return v[0];
+}
+
+template <int DPL, bool KV1>
 __global__ void __launch_bounds__(256) attn_chunk_kernel(const float *qkv, int qkv_stride, int heads,
-                                                         int hd, const float *kc, const float *vc,
-                                                         int kv_w, int group, int sliding, int span,
-                                                         const int *d_p0, int lanes,
-                                                         float *part_ml, float *part_acc) {
+                                                         const float *kc, const float *vc, int kv_w, int group,
+                                                         int sliding, int span, const int *d_p0, int lanes,
+                                                         int chunk_len, float *part_ml, float *part_acc) {
+  constexpr int HD = DPL * 32;
   extern __shared__ __align__(16) float sm[];
-  const int chunk = blockIdx.x, lg = blockIdx.y;
-  // The span every lane of the block reads, [lo_all, p0 + lanes), is cut into
-  // gridDim.x chunks of a whole number of tiles; the chunk length follows the
-  // position so one launch shape serves every position.
+  float *qs = sm;                          // [ATT_P][HD]
+  float *ks = qs + ATT_P * HD;             // [ATT_T][kv_w]
+  float *vs = ks + (size_t)ATT_T * kv_w;   // [ATT_T][kv_w]
+  float *sc = vs + (size_t)ATT_T * kv_w;   // [ATT_P][ATT_T + 1]
+  int *kvoff = reinterpret_cast<int *>(sc + ATT_P * (ATT_T + 1));  // [ATT_P]
+  const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
   const int p0 = *d_p0;
   const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
-  const int span_all = p0 + lanes - lo_all;
-  const int per = ATT_TILE * (int)gridDim.x;
-  const int chunk_len = ATT_TILE * ((span_all + per - 1) / per);
-  if (chunk * chunk_len >= span_all) return;  // past the span: the combine never reads it
-  const int j0 = lg * ATT_LANES;
-  const int nl = min(ATT_LANES, lanes - j0);
-  const int pairs = nl * heads;
-  const int pmax = ATT_LANES * heads;
-  float *qs = sm;                                  // [pmax][hd]
-  float *ks = qs + (size_t)pmax * hd;              // [TILE][kv_w + 1]
-  float *vs = ks + (size_t)ATT_TILE * (kv_w + 1);  // [TILE][kv_w]
-  float *sc = vs + (size_t)ATT_TILE * kv_w;        // [pmax][TILE]
-  float *fac = sc + (size_t)pmax * ATT_TILE;       // [pmax]
-  float *acc = fac + pmax;                         // [pmax][hd]
-  float *mrun = acc + (size_t)pmax * hd;           // [pmax]
-  float *lrun = mrun + pmax;                       // [pmax]
+  const int hi_all = p0 + lanes;
+  const int c_first = lo_all / chunk_len;
+  const int n_chunks = (hi_all - 1) / chunk_len - c_first + 1;
+  const int pair0 = blockIdx.y * ATT_P;
+  const int n_pairs = min(ATT_P, lanes * heads - pair0);
+  if ((int)blockIdx.x >= n_chunks) return;
 
-  const int c_from = lo_all + chunk * chunk_len;
-  const int c_upto = min(c_from + chunk_len, p0 + lanes);
-  for (int i = threadIdx.x; i < pairs * hd; i += blockDim.x) {
-    int pr = i / hd, d = i % hd;
-    int j = j0 + pr / heads, h = pr % heads;
-    qs[i] = qkv[(size_t)j * qkv_stride + (size_t)h * hd + d];
-    acc[i] = 0.0f;
+  for (int i = threadIdx.x; i < ATT_P * (HD / 4); i += blockDim.x) {
+    const int pr = i / (HD / 4), d4 = i % (HD / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (pr < n_pairs) {
+      const int p = pair0 + pr, j = p / heads, h = p - j * heads;
+      v = *reinterpret_cast<const float4 *>(qkv + (size_t)j * qkv_stride + (size_t)h * HD + d4 * 4);
+    }
+    reinterpret_cast<float4 *>(qs)[i] = v;
   }
-  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
-    mrun[i] = -FLT_MAX;
-    lrun[i] = 0.0f;
+  if (threadIdx.x < ATT_P) {
+    const int p = pair0 + threadIdx.x, h = p % heads;
+    kvoff[threadIdx.x] = (h / group) * HD;
   }
-  for (int tb = c_from; tb < c_upto; tb += ATT_TILE) {
-    const int tn = min(ATT_TILE, c_upto - tb);
-    __syncthreads();
-    for (int i = threadIdx.x; i < tn * kv_w; i += blockDim.x) {
-      int r = i / kv_w, d = i % kv_w;
-      ks[r * (kv_w + 1) + d] = kc[(size_t)(tb + r) * kv_w + d];
-      vs[r * kv_w + d] = vc[(size_t)(tb + r) * kv_w + d];
-    }
-    __syncthreads();
-    // scores: thread -> (pair, position)
-    for (int i = threadIdx.x; i < pairs * ATT_TILE; i += blockDim.x) {
-      int pr = i / ATT_TILE, r = i % ATT_TILE;
-      int j = j0 + pr / heads, h = pr % heads;
-      int pos = tb + r;
-      float s = -FLT_MAX;
-      int lo_j = sliding ? max(0, p0 + j - span + 1) : 0;
-      if (r < tn && pos <= p0 + j && pos >= lo_j) {
-        const float *kr = ks + r * (kv_w + 1) + (h / group) * hd;
-        const float *q = qs + (size_t)pr * hd;
-        float t = 0.0f;
-        for (int d = 0; d < hd; ++d) t += kr[d] * q[d];
-        s = t;
-      }
-      sc[pr * ATT_TILE + r] = s;
-    }
-    __syncthreads();
-    // online softmax update, one thread a pair
-    for (int pr = threadIdx.x; pr < pairs; pr += blockDim.x) {
-      float m_old = mrun[pr], m_new = m_old;
-      for (int r = 0; r < tn; ++r) m_new = fmaxf(m_new, sc[pr * ATT_TILE + r]);
-      float f = (m_new == -FLT_MAX) ? 1.0f : ((m_old == -FLT_MAX) ? 0.0f : expf(m_old - m_new));
-      float l = lrun[pr] * f;
-      for (int r = 0; r < ATT_TILE; ++r) {
-        float s = sc[pr * ATT_TILE + r];
-        float e = (r < tn && s != -FLT_MAX) ? expf(s - m_new) : 0.0f;
-        sc[pr * ATT_TILE + r] = e;
-        l += e;
-      }
-      lrun[pr] = l;
-      mrun[pr] = m_new;
-      fac[pr] = f;
-    }
-    __syncthreads();
-    // weighted values: thread -> (pair, dimension)
-    for (int i = threadIdx.x; i < pairs * hd; i += blockDim.x) {
-      int pr = i / hd, d = i % hd;
-      int h = pr % heads;
-      const float *vcol = vs + (h / group) * hd + d;
-      float a = acc[i] * fac[pr];
-      for (int r = 0; r < tn; ++r) a += sc[pr * ATT_TILE + r] * vcol[r * kv_w];
-      acc[i] = a;
-    }
+  // the pair this thread scores as lane l32 of the transposing sum
+  int lane_lo, lane_hi;
+  {
+    const int p = pair0 + l32, j = p / heads;
+    lane_lo = sliding ? max(0, p0 + j - span + 1) : 0;
+    lane_hi = l32 < n_pairs ? p0 + j : -1;
+  }
+  // the pairs this warp owns for the softmax and blend
+  int my_j[4], my_h[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int p = pair0 + warp * 4 + q;
+    my_j[q] = p / heads;
+    my_h[q] = p - my_j[q] * heads;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < pairs * hd; i += blockDim.x) {
-    int pr = i / hd, d = i % hd;
-    int j = j0 + pr / heads, h = pr % heads;
-    part_acc[(((size_t)chunk * 16 + j) * heads + h) * hd + d] = acc[i];
-  }
-  for (int pr = threadIdx.x; pr < pairs; pr += blockDim.x) {
-    int j = j0 + pr / heads, h = pr % heads;
-    part_ml[(((size_t)chunk * 16 + j) * heads + h) * 2 + 0] = mrun[pr];
-    part_ml[(((size_t)chunk * 16 + j) * heads + h) * 2 + 1] = lrun[pr];
+  int my_kv[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) my_kv[q] = kvoff[warp * 4 + q];
+
+  for (int cr = blockIdx.x; cr < n_chunks; cr += gridDim.x) {
+    const int c = c_first + cr;
+    const int c_lo = max(c * chunk_len, lo_all), c_hi = min((c + 1) * chunk_len, hi_all);
+    float m_run[4], l_run[4], acc[4][DPL];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      m_run[q] = -FLT_MAX;
+      l_run[q] = 0.0f;
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) acc[q][e] = 0.0f;
+    }
+    for (int tb = c * chunk_len; tb < c_hi; tb += ATT_T) {
+      if (tb + ATT_T <= c_lo) continue;
+      __syncthreads();
+      {
+        const int w4 = KV1 ? HD / 4 : kv_w / 4;
+        for (int i = threadIdx.x; i < ATT_T * w4; i += blockDim.x) {
+          const int r = i / w4, d4 = i - r * w4, pos = tb + r;
+          const bool in = pos >= c_lo && pos < c_hi;
+          float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+          if (in) {
+            kv = *reinterpret_cast<const float4 *>(kc + (size_t)pos * kv_w + d4 * 4);
+            vv = *reinterpret_cast<const float4 *>(vc + (size_t)pos * kv_w + d4 * 4);
+          }
+          reinterpret_cast<float4 *>(ks)[i] = kv;
+          reinterpret_cast<float4 *>(vs)[i] = vv;
+        }
+      }
+      __syncthreads();
+      // scores
+#pragma unroll 1
+      for (int r = warp; r < ATT_T; r += 8) {
+        const int pos = tb + r;
+        float kslice[DPL];
+        if (KV1) load_slice<DPL>(ks + r * HD + l32 * DPL, kslice);
+        float part[32];
+#pragma unroll
+        for (int pr = 0; pr < 32; ++pr) {
+          float qv[DPL], kv[DPL];
+          load_slice<DPL>(qs + pr * HD + l32 * DPL, qv);
+          if (KV1) {
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) kv[e] = kslice[e];
+          } else {
+            load_slice<DPL>(ks + r * kv_w + kvoff[pr] + l32 * DPL, kv);
+          }
+          float t = 0.0f;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) t += qv[e] * kv[e];
+          part[pr] = t;
+        }
+        const float s_ = transpose_sum32(part);
+        const bool valid = pos >= c_lo && pos < c_hi && pos >= lane_lo && pos <= lane_hi;
+        sc[l32 * (ATT_T + 1) + r] = valid ? s_ : -FLT_MAX;
+      }
+      __syncthreads();
+      // online softmax and blend for this warp's pairs
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int pr = warp * 4 + q;
+        const float s_ = sc[pr * (ATT_T + 1) + l32];
+        const float m_new = fmaxf(m_run[q], warp_max(s_));
+        const float f = (m_new == -FLT_MAX) ? 1.0f : (m_run[q] == -FLT_MAX ? 0.0f : expf(m_run[q] - m_new));
+        const float pe = (s_ == -FLT_MAX) ? 0.0f : expf(s_ - m_new);
+        l_run[q] = l_run[q] * f + warp_sum(pe);
+        m_run[q] = m_new;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[q][e] *= f;
+        sc[pr * (ATT_T + 1) + l32] = pe;
+      }
+      __syncwarp();
+#pragma unroll 2
+      for (int r = 0; r < ATT_T; ++r) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float pe = sc[(warp * 4 + q) * (ATT_T + 1) + r];
+          float vv[DPL];
+          load_slice<DPL>(vs + r * kv_w + (KV1 ? 0 : my_kv[q]) + l32 * DPL, vv);
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[q][e] += pe * vv[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (warp * 4 + q >= n_pairs) continue;
+      const size_t slot = ((size_t)cr * 16 + my_j[q]) * heads + my_h[q];
+      if (l32 == 0) {
+        part_ml[slot * 2 + 0] = m_run[q];
+        part_ml[slot * 2 + 1] = l_run[q];
+      }
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) part_acc[slot * HD + l32 * DPL + e] = acc[q][e];
+    }
   }
 }
 
 // attention, step 3: the chunks' partials merged into each head's output,
-// (sum_c acc_c e^{m_c - M}) / (sum_c l_c e^{m_c - M}).  One block a
-// (lane, head); the chunk weights are formed once, then one thread a
-// dimension sums the chunks with independent loads.
-__global__ void attn_combine_kernel(const float *part_ml, const float *part_acc, int n_grid, int lanes,
-                                    int heads, int hd, int sliding, int span, const int *d_p0, float *out,
+// (sum_c acc_c e^{m_c - M}) / (sum_c l_c e^{m_c - M}), chunks in ascending
+// order.  One block a (lane, head); the chunk weights are formed once, then
+// one thread a dimension sums the chunks.
+__global__ void attn_combine_kernel(const float *part_ml, const float *part_acc, int lanes, int heads, int hd,
+                                    int sliding, int span, int chunk_len, const int *d_p0, float *out,
                                     int out_stride) {
   __shared__ float wgt[1024];
   __shared__ float tot;
@@ -483,23 +600,23 @@ __global__ void attn_combine_kernel(const float *part_ml, const float *part_acc,
   if (j >= lanes) return;
   const int p0 = *d_p0;
   const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
-  const int span_all = p0 + lanes - lo_all;
-  const int per = ATT_TILE * n_grid;
-  const int chunk_len = ATT_TILE * ((span_all + per - 1) / per);
-  const int n_chunks = (span_all + chunk_len - 1) / chunk_len;
+  const int hi_all = p0 + lanes;
+  const int c_first = lo_all / chunk_len;
+  const int n_chunks = (hi_all - 1) / chunk_len - c_first + 1;
   if (threadIdx.x < 32) {
     float M = -FLT_MAX;
     for (int c = threadIdx.x; c < n_chunks; c += 32) M = fmaxf(M, part_ml[(((size_t)c * 16 + j) * heads + h) * 2]);
     M = warp_max(M);
-    float L = 0.0f;
     for (int c = threadIdx.x; c < n_chunks; c += 32) {
       float m = part_ml[(((size_t)c * 16 + j) * heads + h) * 2];
-      float w = (m == -FLT_MAX) ? 0.0f : expf(m - M);
-      wgt[c] = w;
-      L += part_ml[(((size_t)c * 16 + j) * heads + h) * 2 + 1] * w;
+      wgt[c] = (m == -FLT_MAX) ? 0.0f : expf(m - M);
     }
-    L = warp_sum(L);
-    if (threadIdx.x == 0) tot = L;
+    __syncwarp();
+    if (threadIdx.x == 0) {
+      float L = 0.0f;
+      for (int c = 0; c < n_chunks; ++c) L += part_ml[(((size_t)c * 16 + j) * heads + h) * 2 + 1] * wgt[c];
+      tot = L;
+    }
   }
   __syncthreads();
   const float inv = 1.0f / tot;
@@ -512,14 +629,16 @@ __global__ void attn_combine_kernel(const float *part_ml, const float *part_acc,
 }
 
 // argmax partials of the output head merged per lane (app_main.c:482: the
-// first index of the largest value)
+// first index of the largest value).  Thread (lane, stripe) scans parts
+// stripe, stripe + 32, ...; the stripes then meet in shared memory.
 __global__ void argmax_final_kernel(const float *part_val, const int *part_idx, int parts, int lanes,
                                     int32_t *top_out) {
-  int j = threadIdx.x;
-  if (j >= lanes) return;
+  __shared__ float sv[32][16];
+  __shared__ int si[32][16];
+  const int j = threadIdx.x & 15, stripe = threadIdx.x >> 4;
   float v = -FLT_MAX;
   int i = 0x7fffffff;
-  for (int p = 0; p < parts; ++p) {
+  for (int p = stripe; p < parts; p += 32) {
     float ov = part_val[p * 16 + j];
     int oi = part_idx[p * 16 + j];
     if (ov > v || (ov == v && oi < i)) {
@@ -527,7 +646,20 @@ __global__ void argmax_final_kernel(const float *part_val, const int *part_idx, 
       i = oi;
     }
   }
-  top_out[j] = i;
+  sv[stripe][j] = v;
+  si[stripe][j] = i;
+  __syncthreads();
+  if (threadIdx.x < 16 && (int)threadIdx.x < lanes) {
+    for (int s = 1; s < 32; ++s) {
+      float ov = sv[s][j];
+      int oi = si[s][j];
+      if (ov > v || (ov == v && oi < i)) {
+        v = ov;
+        i = oi;
+      }
+    }
+    top_out[j] = i;
+  }
 }
 
 // rope tables: cos/sin of pos * step in double (app_core.c:8147 rope_wave)
@@ -714,9 +846,8 @@ __global__ void desk_rope_kernel(float *x, int head, const float *cs, const floa
 // launchers
 
 static size_t gemv_smem_nt(const GemvArgs &a, int NT) {
-  size_t red = a.split > 1 ? (size_t)GEMV_WARPS * 32 * 8 * NT * 4 : 0;
-  if (red < (size_t)GEMV_WARPS * 16 * 4) red = (size_t)GEMV_WARPS * 16 * 4;
-  return gemv_stage_bytes(a.pl.n_cc, NT) + red;
+  size_t red = (size_t)GEMV_WARPS * 32 * 8 * NT * 4;  // the split reduction, and the ssq/argmax merges
+  return gemv_stage_bytes(a.pl.n_cc, NT) + SCR_FLOATS * 4 + red;
 }
 
 template <int NT, int PAIR, int PRO, int EPI>
@@ -799,7 +930,14 @@ cudaError_t igc_kernels_configure(int bytes) {
   if (bytes > optin) bytes = optin;
   e = allow_smem_nt<1>(bytes);
   if (e == cudaSuccess) e = allow_smem_nt<2>(bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<1, true>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<2, true>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<4, true>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<8, true>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<1, false>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<2, false>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<4, false>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<8, false>, bytes);
   if (e == cudaSuccess) e = allow_smem_fn(topk_stage2_kernel, bytes);
   return e;
 }
@@ -844,25 +982,39 @@ cudaError_t igc_launch_attn_prep(float *qkv, int qkv_stride, int heads, int kv_h
   return cudaGetLastError();
 }
 
-size_t igc_attn_smem(int heads, int hd, int kv_w) { return sizeof(float) * attn_smem_floats(heads, hd, kv_w); }
+size_t igc_attn_smem(int hd, int kv_w) { return sizeof(float) * attn_smem_floats(hd, kv_w); }
 
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int hd, const float *kc, const float *vc,
-                            int kv_w, int group, int sliding, int span, const int *d_p0, int lanes, int n_chunks,
-                            float *part_ml, float *part_acc, float *out, int out_stride, cudaStream_t st) {
-  size_t smem = igc_attn_smem(heads, hd, kv_w);
-  dim3 grid(n_chunks, (lanes + ATT_LANES - 1) / ATT_LANES);
-  attn_chunk_kernel<<<grid, 256, smem, st>>>(qkv, qkv_stride, heads, hd, kc, vc, kv_w, group, sliding, span, d_p0,
-                                             lanes, part_ml, part_acc);
+                            int kv_w, int group, int sliding, int span, const int *d_p0, int lanes, int chunk_len,
+                            int grid_x, float *part_ml, float *part_acc, float *out, int out_stride, cudaStream_t st) {
+  size_t smem = igc_attn_smem(hd, kv_w);
+  dim3 grid(grid_x, (lanes * heads + ATT_P - 1) / ATT_P);
+  const bool kv1 = kv_w == hd;
+#define IGC_ATT(D)                                                                                             \
+  if (kv1)                                                                                                     \
+    attn_chunk_kernel<D, true><<<grid, 256, smem, st>>>(qkv, qkv_stride, heads, kc, vc, kv_w, group, sliding, \
+                                                        span, d_p0, lanes, chunk_len, part_ml, part_acc);      \
+  else                                                                                                         \
+    attn_chunk_kernel<D, false><<<grid, 256, smem, st>>>(qkv, qkv_stride, heads, kc, vc, kv_w, group, sliding, \
+                                                         span, d_p0, lanes, chunk_len, part_ml, part_acc);
+  switch (hd) {
+    case 32: IGC_ATT(1) break;
+    case 64: IGC_ATT(2) break;
+    case 128: IGC_ATT(4) break;
+    case 256: IGC_ATT(8) break;
+    default: return cudaErrorInvalidValue;
+  }
+#undef IGC_ATT
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<lanes * heads, 256, 0, st>>>(part_ml, part_acc, n_chunks, lanes, heads, hd, sliding, span,
+  attn_combine_kernel<<<lanes * heads, 256, 0, st>>>(part_ml, part_acc, lanes, heads, hd, sliding, span, chunk_len,
                                                      d_p0, out, out_stride);
   return cudaGetLastError();
 }
 
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
                               cudaStream_t st) {
-  argmax_final_kernel<<<1, 32, 0, st>>>(part_val, part_idx, parts, lanes, top);
+  argmax_final_kernel<<<1, 512, 0, st>>>(part_val, part_idx, parts, lanes, top);
   return cudaGetLastError();
 }
 

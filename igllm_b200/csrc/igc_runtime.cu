@@ -58,6 +58,17 @@ static int fail_device(cudaError_t e, const char *where) {
     if (e_ != cudaSuccess) return fail_device(e_, #call); \
   } while (0)
 
+// An error a CUDA call left behind that its caller did not check would be
+// reported by the next launch check, against the wrong call.  Entry points
+// clear it first; IGC_DEBUG_ERRORS=1 names where a stale one was found.
+static void clear_stale(const char *where) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    const char *dbg = getenv("IGC_DEBUG_ERRORS");
+    if (dbg && dbg[0] == '1') fprintf(stderr, "igc: stale CUDA error before %s: %s\n", where, cudaGetErrorString(e));
+  }
+}
+
 extern "C" const char *igc_last_error(void) { return g_last_error.c_str(); }
 extern "C" long igc_launch_count(void) {
   long n = g_launches;
@@ -299,6 +310,7 @@ struct igc_model {
   ~igc_model() {
     cudaSetDevice(device);
     for (void *p : owned) cudaFree(p);
+    clear_stale("model free");
   }
   template <typename T>
   int alloc(T **p, size_t count) {
@@ -491,15 +503,23 @@ struct Binder {
     return IGC_OKAY;
   }
 
+  // Warps per row block and blocks per launch.  Each block stages the whole
+  // input once, so the grid stays near one or two blocks an SM (what the
+  // staging leaves room for at eight lanes) and each block walks many row
+  // blocks; a split shares one row block's chunks among warps where there
+  // are too few row blocks to keep every warp busy.
   void plan(DevPlane &p) {
     int units = p.pair ? p.n_rb / 2 : p.n_rb;
-    int target = m->sm_count * GEMV_WARPS * 2;
+    size_t stage = gemv_stage_bytes(p.n_cc, 1) + 8 * 1024;
+    int per_sm = (int)((size_t)m->smem_limit / stage);
+    if (per_sm > 2) per_sm = 2;
+    if (per_sm < 1) per_sm = 1;
+    int cap = m->sm_count * per_sm;
     int S = 1;
-    while (S < 8 && S * 2 <= p.n_cc && units * S < target) S *= 2;
+    while (S < 8 && S * 2 <= p.n_cc && units * S < cap * GEMV_WARPS) S *= 2;
     p.split = S;
     int per_iter = GEMV_WARPS / S;
     int need = (units + per_iter - 1) / per_iter;
-    int cap = m->sm_count * 4;
     p.grid = need < cap ? need : cap;
     if (p.grid < 1) p.grid = 1;
   }
@@ -665,6 +685,7 @@ static int bind_model(igc_model *m, Source &src) {
       L.gain = g ? real_at(*g, 0) : 1.0f; /* app_core.c:8700-8708 */
     }
 #undef STEM
+    if (igc_attn_smem(L.hd, L.kv_rows) > (size_t)m->smem_limit) return IGC_FAIL_SUPPORT;
     if (L.qkv_rows > m->max_qkv) m->max_qkv = L.qkv_rows;
     if (L.inner > m->max_inner) m->max_inner = L.inner;
     if (L.q_rows > m->max_q) m->max_q = L.q_rows;
@@ -683,6 +704,7 @@ static int bind_model(igc_model *m, Source &src) {
 }
 
 static int model_prepare(igc_model *m, const igc_setup *setup) {
+  clear_stale("model load");
   m->device = setup ? setup->device : 0;
   CK(cudaSetDevice(m->device));
   CK(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, m->device));
@@ -742,7 +764,6 @@ extern "C" size_t igc_model_device_bytes(const igc_model *m) { return m ? m->dev
 // ---------------------------------------------------------------------------
 // sessions
 
-constexpr int ATT_CHUNKS = 128;  // attention span chunks a launch (grid.x)
 
 struct igc_session {
   igc_model *m = nullptr;
@@ -758,6 +779,7 @@ struct igc_session {
   float *qkv = nullptr, *attn = nullptr, *obuf = nullptr, *act = nullptr, *dbuf = nullptr, *pa = nullptr,
         *pp = nullptr, *logits = nullptr;
   float *part_ml = nullptr, *part_acc = nullptr, *arg_val = nullptr;
+  float *ssq_o = nullptr, *ssq_d = nullptr, *ssq_pp = nullptr;
   int *arg_idx = nullptr;
   float *cand_v = nullptr, *top_v = nullptr;
   int *cand_i = nullptr, *top_i = nullptr;
@@ -767,6 +789,8 @@ struct igc_session {
   float *h_top_v = nullptr;
   int *h_top_i = nullptr;
   int logit_lanes = 0;  // rows the last pass left in `logits`
+  int chunk_len = 32;   // attention chunk length, fixed for the session
+  int max_chunks = 0;   // chunks the longest span can cover
   int use_graphs = 1;
   cudaGraphExec_t graph[IGC_LANE_LIMIT + 1][2] = {};
   double serve_seconds = 0.0;
@@ -783,6 +807,7 @@ struct igc_session {
     for (void *p : owned) cudaFree(p);
     if (h_io) cudaFreeHost(h_io);
     if (st) cudaStreamDestroy(st);
+    clear_stale("session close");
   }
   template <typename T>
   int alloc(T **p, size_t count) {
@@ -798,6 +823,7 @@ struct igc_session {
 extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (!m || !out) return IGC_FAIL_ARGUMENT;
   *out = nullptr;
+  clear_stale("session open");
   CK(cudaSetDevice(m->device));
   auto s = std::make_unique<igc_session>();
   s->m = m;
@@ -831,10 +857,17 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (c == IGC_OKAY) c = s->alloc(&s->pa, (size_t)K * (m->ple_dim ? m->ple_dim : 1));
   if (c == IGC_OKAY) c = s->alloc(&s->pp, (size_t)K * H);
   if (c == IGC_OKAY) c = s->alloc(&s->logits, (size_t)K * m->vocab);
-  if (c == IGC_OKAY) c = s->alloc(&s->part_ml, (size_t)ATT_CHUNKS * K * m->heads * 2);
-  if (c == IGC_OKAY) c = s->alloc(&s->part_acc, (size_t)ATT_CHUNKS * K * m->max_q);
+  // attention chunks: a power of two of at least 32 positions, at most 128
+  // of them over the window, so the partials stay a few tens of MB
+  while ((m->window_limit + s->chunk_len - 1) / s->chunk_len > 128) s->chunk_len *= 2;
+  s->max_chunks = (m->window_limit + s->chunk_len - 1) / s->chunk_len + 2;
+  if (c == IGC_OKAY) c = s->alloc(&s->part_ml, (size_t)s->max_chunks * K * m->heads * 2);
+  if (c == IGC_OKAY) c = s->alloc(&s->part_acc, (size_t)s->max_chunks * K * m->max_q);
   if (c == IGC_OKAY) c = s->alloc(&s->arg_val, (size_t)s->arg_parts * 16);
   if (c == IGC_OKAY) c = s->alloc(&s->arg_idx, (size_t)s->arg_parts * 16);
+  if (c == IGC_OKAY) c = s->alloc(&s->ssq_o, (size_t)s->arg_parts * 16);
+  if (c == IGC_OKAY) c = s->alloc(&s->ssq_d, (size_t)s->arg_parts * 16);
+  if (c == IGC_OKAY) c = s->alloc(&s->ssq_pp, (size_t)s->arg_parts * 16);
   int blocks = (m->vocab + 2047) / 2048;
   if (c == IGC_OKAY) c = s->alloc(&s->cand_v, (size_t)K * blocks * 256);
   if (c == IGC_OKAY) c = s->alloc(&s->cand_i, (size_t)K * blocks * 256);
@@ -886,11 +919,27 @@ extern "C" int igc_session_hold(igc_session *s, int keep) { /* app_core.c:13935 
   return IGC_OKAY;
 }
 
+// The sums of squares a projection's output leaves for its consumer's norm:
+// one row of 16 lanes per block of the launch that wrote them.
+struct Ssq {
+  float *buf = nullptr;
+  int parts = 0;
+};
+
 static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, const float *x, int x_stride,
                 const float *p, const float *w_res, float gain, const float *w_in, float *x_out, float *out,
-                int out_stride, float out_scale = 1.0f, const float *aux = nullptr, int aux_stride = 0) {
+                int out_stride, float out_scale = 1.0f, const float *aux = nullptr, int aux_stride = 0,
+                const Ssq *p_ssq = nullptr, Ssq *out_ssq = nullptr) {
   GemvArgs a;
   memset(&a, 0, sizeof(a));
+  if (p_ssq) {
+    a.p_ssq = p_ssq->buf;
+    a.p_parts = p_ssq->parts;
+  }
+  if (out_ssq) {
+    a.out_ssq = out_ssq->buf;
+    out_ssq->parts = pl.grid;
+  }
   a.pl = pl.view();
   a.lanes = K;
   a.split = pl.split;
@@ -926,6 +975,7 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
     b.x_out = x_out ? x_out + (size_t)j0 * x_stride : nullptr;
     b.out = out + (size_t)j0 * out_stride;
     b.aux = aux ? aux + (size_t)j0 * aux_stride : nullptr;
+    b.out_ssq = a.out_ssq ? a.out_ssq + j0 : nullptr;
     if (igc_gemv_smem(&b) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
     CKL(igc_launch_gemv(&b, pl.pair ? 1 : 0, pro, epi, pl.grid, s->st));
   }
@@ -950,12 +1000,14 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   }
   // the residual stream ping-pongs between xa and xb; `pend` is the last
   // block's output still to be normed and added (with its gain) by the next
-  // consumer's prologue
+  // consumer's prologue, `pend_ssq` the sums of squares its producer left
   float *cur = s->x0;
   float *bufs[2] = {s->xa, s->xb};
   int flip = 0;
   const float *pend = nullptr, *pend_w = nullptr;
   float pend_gain = 1.0f;
+  Ssq so{s->ssq_o, 0}, sd{s->ssq_d, 0}, spp{s->ssq_pp, 0};
+  const Ssq *pend_ssq = nullptr;
   auto next_x = [&]() -> float * { float *o = bufs[flip]; flip ^= 1; return o; };
   for (int l = 0; l < m->layers; ++l) {
     const DevLayer &L = m->layer[l];
@@ -964,7 +1016,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     if (pend) {
       xo = next_x();
       c = gemv(s, L.qkv, K, PRO_RESID_NORM, EPI_STORE, cur, H, pend, pend_w, pend_gain, L.enter_norm, xo, s->qkv,
-               L.qkv_rows);
+               L.qkv_rows, 1.0f, nullptr, 0, pend_ssq, nullptr);
       cur = xo;
     } else {
       c = gemv(s, L.qkv, K, PRO_NORM, EPI_STORE, cur, H, nullptr, nullptr, 1.0f, L.enter_norm, nullptr, s->qkv,
@@ -977,39 +1029,43 @@ static int enqueue_pass(igc_session *s, int K, int want) {
                              m->rope_cs[L.kind], m->rope_sn[L.kind], L.share ? 0 : 1, m->eps, d_p0, K,
                              s->kc[l], s->vc[l], s->st));
     CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, L.hd, s->kc[owner], s->vc[owner], O.kv_rows,
-                        m->heads / L.kv_heads, L.kind == 0 ? 1 : 0, m->slide_span, d_p0, K, ATT_CHUNKS, s->part_ml,
-                        s->part_acc, s->attn, L.q_rows, s->st));
+                        m->heads / L.kv_heads, L.kind == 0 ? 1 : 0, m->slide_span, d_p0, K, s->chunk_len,
+                        s->max_chunks, s->part_ml, s->part_acc, s->attn, L.q_rows, s->st));
     ++g_launches;  // the combine kernel
-    c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H);
+    c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
+             1.0f, nullptr, 0, nullptr, &so);
     if (c != IGC_OKAY) return c;
     xo = next_x();
     c = gemv(s, L.gateup, K, PRO_RESID_NORM, EPI_GELU_PAIR, cur, H, s->obuf, L.after_attn_norm, 1.0f,
-             L.before_feed_norm, xo, s->act, L.inner);
+             L.before_feed_norm, xo, s->act, L.inner, 1.0f, nullptr, 0, &so, nullptr);
     if (c != IGC_OKAY) return c;
     cur = xo;
-    c = gemv(s, L.down, K, PRO_F32, EPI_STORE, s->act, L.inner, nullptr, nullptr, 1.0f, nullptr, nullptr, s->dbuf, H);
+    c = gemv(s, L.down, K, PRO_F32, EPI_STORE, s->act, L.inner, nullptr, nullptr, 1.0f, nullptr, nullptr, s->dbuf, H,
+             1.0f, nullptr, 0, nullptr, &sd);
     if (c != IGC_OKAY) return c;
     if (m->ple_dim > 0) {
       xo = next_x();
       c = gemv(s, L.ple_gate, K, PRO_RESID, EPI_GELU_MUL, cur, H, s->dbuf, L.after_feed_norm, 1.0f, nullptr, xo,
-               s->pa, m->ple_dim, 1.0f, s->ple + (size_t)l * m->ple_dim, PS);
+               s->pa, m->ple_dim, 1.0f, s->ple + (size_t)l * m->ple_dim, PS, &sd, nullptr);
       if (c != IGC_OKAY) return c;
       cur = xo;
       c = gemv(s, L.ple_proj, K, PRO_F32, EPI_STORE, s->pa, m->ple_dim, nullptr, nullptr, 1.0f, nullptr, nullptr,
-               s->pp, H);
+               s->pp, H, 1.0f, nullptr, 0, nullptr, &spp);
       if (c != IGC_OKAY) return c;
       pend = s->pp;
       pend_w = L.after_ple_norm;
+      pend_ssq = &spp;
     } else {
       pend = s->dbuf;
       pend_w = L.after_feed_norm;
+      pend_ssq = &sd;
     }
     pend_gain = L.gain;
   }
   if (want) {
     float *xo = next_x();
     int c = gemv(s, m->head, K, PRO_RESID_NORM, EPI_LOGITS, cur, H, pend, pend_w, pend_gain, m->final_norm, xo,
-                 s->logits, m->vocab);
+                 s->logits, m->vocab, 1.0f, nullptr, 0, pend_ssq, nullptr);
     if (c != IGC_OKAY) return c;
     CKL(igc_launch_argmax(s->arg_val, s->arg_idx, m->head.grid, K, s->d_top, s->st));
   }
@@ -1024,6 +1080,7 @@ static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
   if (s->fill + K > m->window_limit) return IGC_FAIL_STATE;
   for (int j = 0; j < K; ++j)
     if (ids[j] < 0 || ids[j] >= m->vocab) return IGC_FAIL_ARGUMENT;
+  clear_stale("pass");
   CK(cudaSetDevice(m->device));
   s->h_io[0] = s->fill;
   memcpy(s->h_io + 1, ids, sizeof(int32_t) * (size_t)K);

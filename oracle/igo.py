@@ -175,13 +175,14 @@ def make_plane(code, scale_f32):
 
 class OracleModel:
     """The restatement's model over a checkpoint folder (configuration read
-    the way app_core.c:8325 config_read reads it)."""
+    the way app_core.c:8325 config_read reads it), or over tensors already in
+    memory (`tensors` name -> (dtype, array), `config` the parsed json)."""
 
-    def __init__(self, folder, window_limit=4096):
+    def __init__(self, folder=None, window_limit=4096, tensors=None, config=None):
         self.keep = []  # arrays the C struct points into
-        cfg = json.load(open(os.path.join(folder, "config.json")))
+        cfg = config if config is not None else json.load(open(os.path.join(folder, "config.json")))
         tc = cfg.get("text_config", cfg)
-        t = read_folder(folder)
+        t = tensors if tensors is not None else read_folder(folder)
         P = next(p for p in ("model.language_model.", "language_model.model.", "model.", "")
                  if p + "embed_tokens.weight" in t)
         L = int(tc["num_hidden_layers"])
