@@ -1,0 +1,404 @@
+#!/usr/bin/env python3
+"""bench.py - decode tok/s of the speculative verify round (greedy, --guess 4).
+
+Workload: the Gemma-4-E2B text stack with seeded random
+weights (35 layers, hidden 1536, FFN 6144, 8 query heads / 1 KV head, head
+256, vocab 262144, window 512, global every 5th, int4 g32 with f16 scales,
+bf16 N(0,0.02) norms and embeddings), a 1024-id prompt (a 256-id passage,
+uniform over the vocab, seed 0, repeated 4x with 10% substitutions), 256
+tokens generated greedily in verify rounds of 4 lanes.
+
+A step is one generation of those 256 tokens after the primed prompt: 64
+verify rounds whose blocks come from the always-right proposer of the
+reference's guess bracket (app_main.c:1235 main_guess_run), so every round
+commits 4 tokens and the rate measures the verify round itself.
+
+  value  device-resident: every block uploaded to HBM before the timed
+         region, rounds chained on the stream, CUDA events (igc_session_bench)
+  e2e    the same generation through the public round call
+         (igc_session_round) with host ids in and host ids out each round
+
+Also reported: the n-gram scout's own rate and acceptance, verify-round us
+for K = 1, 2, 4, 8, 16, the projection kernel against the HBM roofline
+(timed live with CUDA events), and the reference engine on the host cores.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TOKENS = 256
+GUESS = 4
+PROMPT_LEN = 1024
+VOCAB = 262144
+CKPT_DIR = os.environ.get("IGLLM_BENCH_CKPT", "/tmp/igllm_bench_e2b_s1")
+METRIC = "decode tok/s (greedy, --guess 4)"
+
+
+def make_prompt():
+    """A 256-id passage (uniform, seed 0) repeated 4x with 10% substitutions."""
+    rng = np.random.default_rng(0)
+    passage = rng.integers(0, VOCAB, 256)
+    prompt = np.tile(passage, 4)
+    swap = rng.random(PROMPT_LEN) < 0.10
+    prompt[swap] = rng.integers(0, VOCAB, int(swap.sum()))
+    return prompt.astype(np.int32)
+
+
+def oracle_blocks(last, cont, rounds, k):
+    """Round r's block: the last committed id, then the next k-1 true ids."""
+    seq = np.concatenate([[last], cont]).astype(np.int32)
+    return np.stack([seq[r * k: r * k + k] for r in range(rounds)])
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock and throttle-reason samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def profiler_range(on):
+    """cuProfilerStart/Stop around the timed rounds, so that a profiler run
+    with --profile-from-start off sees exactly those launches."""
+    import ctypes
+    try:
+        cu = ctypes.CDLL("libcuda.so.1")
+        (cu.cuProfilerStart if on else cu.cuProfilerStop)()
+    except OSError:
+        pass
+
+
+# ---------------------------------------------------------------------------
+# the reference engine on the host cores (oracle/_ref, built from app_core.c)
+
+def host_cores():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def ensure_checkpoint():
+    import igllm_b200 as ig
+    if not os.path.exists(os.path.join(CKPT_DIR, "model.safetensors")):
+        ig.synth_write(ig.spec_e2b(seed=1, window_limit=4096), CKPT_DIR, threads=min(32, host_cores()))
+    return CKPT_DIR
+
+
+def reference_rounds(rounds_per_step, steps, warmup, cores):
+    """The reference's own verify rounds on the host: prime the 1024-id
+    prompt, then steps of `rounds_per_step` session_guess(4) + keep(4)
+    rounds (every block kept, as the always-right proposer's would be; the
+    cost of a round does not depend on which ids it verifies)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import igo
+    folder = ensure_checkpoint()
+    rm = igo.RefModel(folder, threads=cores, window_limit=4096)
+    rs = igo.RefSession(rm)
+    prompt = make_prompt()
+    t0 = time.perf_counter()
+    rs.prime(prompt)
+    prime_s = time.perf_counter() - t0
+    rng = np.random.default_rng(7)
+    last = int(prompt[-1])
+    times = []
+    for it in range(warmup + steps):
+        t0 = time.perf_counter()
+        for _ in range(rounds_per_step):
+            blk = np.concatenate([[last], rng.integers(0, VOCAB, GUESS - 1)]).astype(np.int32)
+            rs.guess(blk, want=False)
+            top = rs.rows_argmax(GUESS)
+            rs.keep(GUESS)
+            last = int(top[-1])
+        if it >= warmup:
+            times.append(time.perf_counter() - t0)
+    rs.close()
+    rm.close()
+    return times, prime_s
+
+
+def cpu_baseline_line(cores, rounds=8):
+    times, prime_s = reference_rounds(rounds, 1, 0, cores)
+    tok = rounds * GUESS / times[0]
+    return {"value": round(tok, 3), "unit": "tok/s", "cores": cores, "kind": "reference",
+            "sample": f"{rounds} verify rounds of {GUESS} lanes after the 1024-id prime "
+                      f"(prime took {prime_s:.1f} s), reference engine app_core.c built with -O3 AVX-512, "
+                      f"{cores} threads, same synthetic E2B weights read from safetensors"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cores = host_cores()
+    rounds = 8
+    times, prime_s = reference_rounds(rounds, args.steps, args.warmup, cores)
+    total = sum(times)
+    tok = rounds * GUESS * len(times) / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(tok, 3), "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / len(times), 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "E2B int4 g32 verify rounds, greedy --guess 4, 1024-id prompt (config 0)",
+                   "sample": f"{rounds} rounds a step", "threads": cores},
+        "cpu_baseline": {"value": round(tok, 3), "unit": "tok/s", "cores": cores, "kind": "reference",
+                         "sample": f"{rounds} verify rounds of {GUESS} lanes a step after the 1024-id prime "
+                                   f"({prime_s:.1f} s)"},
+        "e2e": {"value": round(tok, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+
+def run_ours(args):
+    import igllm_b200 as ig
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if not dist:
+            return x
+        import torch
+        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    model = ig.Model(spec=ig.spec_e2b(seed=1, window_limit=4096), device=local, window_limit=4096)
+    sess = ig.Session(model)
+    prompt = make_prompt()
+    sess.prime(prompt)
+    base = sess.fill
+    # the true greedy continuation, by plain steps
+    cont = []
+    tok = int(prompt[-1])
+    for _ in range(TOKENS + GUESS):
+        tok, _ = sess.step(tok, want_logits=False)
+        cont.append(tok)
+    sess.hold(base)
+    rounds = TOKENS // GUESS
+    blocks = oracle_blocks(int(prompt[-1]), np.array(cont), rounds, GUESS)
+
+    # device-resident rounds
+    for _ in range(args.warmup):
+        sess.bench(blocks, GUESS)
+        sess.hold(base)
+    ig.launch_count()
+    barrier()
+    with ClockSampler(local) as clocks:
+        dev_ms = []
+        profiler_range(True)
+        for _ in range(args.steps):
+            ms, top = sess.bench(blocks, GUESS)
+            dev_ms.append(ms)
+            sess.hold(base)
+        profiler_range(False)
+    launches = ig.launch_count()
+    total_s = max_over_ranks(sum(dev_ms) / 1000.0)
+    value = world * TOKENS * args.steps / total_s
+    check_ok = int(top[-1]) == int(cont[rounds * GUESS - 1])
+
+    # end to end through the round call, host ids in and out each round
+    for _ in range(1):
+        for r in range(rounds):
+            sess.round(blocks[r])
+        sess.hold(base)
+    barrier()
+    e2e_s, takes = 0.0, 0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for r in range(rounds):
+            take, made = sess.round(blocks[r])
+            takes += take
+        e2e_s += time.perf_counter() - t0
+        sess.hold(base)
+    e2e_s = max_over_ranks(e2e_s)
+    e2e = world * TOKENS * args.steps / e2e_s
+    h2d = rounds * (1 + GUESS) * 4
+    d2h = rounds * GUESS * 4
+
+    # the shipped proposer: the n-gram scout, one generation
+    scout = ig.Scout()
+    scout.note(prompt)
+    last, made_n, rounds_n, drawn, kept = int(prompt[-1]), 0, 0, 0, 0
+    t0 = time.perf_counter()
+    while made_n < TOKENS:
+        d = scout.draw(min(GUESS - 1, TOKENS - made_n - 1)) if TOKENS - made_n > 1 else np.zeros(0, np.int32)
+        if len(d) == 0:
+            last, _ = sess.step(last, want_logits=False)
+            new = [last]
+        else:
+            blk = np.concatenate([[last], d]).astype(np.int32)
+            take, last = sess.round(blk)
+            new = list(blk[1:1 + take]) + [last]
+            drawn += len(d)
+            kept += take
+        rounds_n += 1
+        made_n += len(new)
+        scout.note(np.array(new, np.int32))
+    ngram_s = time.perf_counter() - t0
+    sess.hold(base)
+
+    # verify-round cost against K
+    per_k = {}
+    for k in (1, 2, 4, 8, 16):
+        r_k = 16
+        blk_k = oracle_blocks(int(prompt[-1]), np.array(cont), r_k, k) if r_k * k <= len(cont) else \
+            np.tile(blocks[:1, :1], (r_k, k))
+        sess.bench(blk_k, k)
+        sess.hold(base)
+        ms, _ = sess.bench(blk_k, k)
+        sess.hold(base)
+        per_k[str(k)] = round(1000.0 * ms / r_k, 1)
+
+    # the projection kernel against the HBM roofline, timed live
+    prof = sess.profile(blocks[0])
+    sess.hold(base)
+    gemv = [(b, ms) for c, b, ms in prof if c == 0]
+    head = [(b, ms) for c, b, ms in prof if c == 1]
+    attn_ms = sum(ms for c, b, ms in prof if c == 2)
+    other_ms = sum(ms for c, b, ms in prof if c == 3)
+    g_bytes, g_ms = sum(b for b, _ in gemv), sum(ms for _, ms in gemv)
+    h_bytes, h_ms = sum(b for b, _ in head), sum(ms for _, ms in head)
+    peak, peak_kind = peaks()
+    achieved = g_bytes / (g_ms / 1000.0) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemv_dram_traffic.json")) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    except Exception:
+        traffic = None
+    round_s = per_k[str(GUESS)] / 1e6
+    bytes_round = model.decode_bytes()
+
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(1000.0 * total_s / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, f16 hi/lo activations, f32 accumulate",
+        "data": "synthetic (seeded E2B-shaped weights, BASELINE config 0 prompt)",
+        "config": {"workload": "E2B int4 g32 greedy --guess 4 verify rounds, 1024-id prompt, 256 tokens (config 0)",
+                   "proposer": "always-right (reference guess bracket's oracle); n-gram scout reported beside",
+                   "l2": "weights 938 MB per round, larger than the 126 MB L2",
+                   "parallelism": f"replicas x{world}"},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "verify_round_us": per_k,
+        "ngram": {"tok_s": round(TOKENS / ngram_s, 1), "rounds": rounds_n, "guesses": drawn, "kept": kept},
+        "roofline": {"bound": "hbm", "kernel": "int4 skinny GEMM (layer projections)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "bytes_per_pass": g_bytes, "ms_per_pass": round(g_ms, 4),
+                     "head_gbs": round(h_bytes / (h_ms / 1000.0) / 1e9, 1) if h_ms else None,
+                     "attention_ms_per_pass": round(attn_ms, 4), "other_ms_per_pass": round(other_ms, 4),
+                     "round_frac": round(bytes_round / round_s / 1e9 / peak, 4)},
+        "clocks": clocks.summary(),
+        "check": {"last_round_argmax_matches_stepped_stream": check_ok, "e2e_kept": takes,
+                  "e2e_kept_max": rounds * (GUESS - 1) * args.steps},
+    }
+    if rank == 0 and world == 1 and not args.no_cpu:
+        try:
+            line["cpu_baseline"] = cpu_baseline_line(host_cores())
+        except Exception as exc:  # the reference build is missing: say so
+            line["cpu_baseline"] = {"value": None, "unit": "tok/s", "cores": host_cores(), "kind": "reference",
+                                    "sample": f"unavailable: {exc}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the host-core reference baseline")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -142,6 +142,8 @@ def _lib():
         "igc_session_round": (i, [vp, i32p, i, _P(Taste), i32p, i32p]),
         "igc_session_serve_seconds": (ctypes.c_double, [vp]),
         "igc_session_serve_tokens": (ctypes.c_size_t, [vp]),
+        "igc_session_bench": (i, [vp, i32p, i, i, fp, i32p]),
+        "igc_session_profile": (i, [vp, i32p, i, _P(ctypes.c_int), _P(ctypes.c_double), fp, i]),
         "igc_scout_open": (i, [_P(vp)]),
         "igc_scout_close": (None, [vp]),
         "igc_scout_clear": (None, [vp]),
@@ -175,7 +177,8 @@ def exported_symbols():
         "igc_session_prime", "igc_session_step", "igc_session_guess", "igc_session_guess_top",
         "igc_session_guess_keep", "igc_session_guess_taste", "igc_session_pick", "igc_session_fill",
         "igc_session_guess_span", "igc_session_guess_limit", "igc_session_round",
-        "igc_session_serve_seconds", "igc_session_serve_tokens", "igc_scout_open", "igc_scout_close",
+        "igc_session_serve_seconds", "igc_session_serve_tokens", "igc_session_bench", "igc_session_profile",
+        "igc_scout_open", "igc_scout_close",
         "igc_scout_clear", "igc_scout_note", "igc_scout_span", "igc_scout_draw", "igc_synth_fill",
         "igc_synth_write", "igc_model_synth", "igc_last_error", "igc_launch_count",
     ]
@@ -317,6 +320,29 @@ class Session:
         if n < 0:
             raise IgcError(n, "session_round")
         return take.value, made.value
+
+    def bench(self, blocks, k):
+        """Verify rounds with every block resident in HBM (see igc_session_bench);
+        returns (device ms, last round's argmax ids)."""
+        a, p = _ids(np.asarray(blocks, np.int32).reshape(-1))
+        ms = ctypes.c_float()
+        top = np.zeros(k, np.int32)
+        _check(_lib().igc_session_bench(self._h, p, len(a) // k, k, ctypes.byref(ms),
+                                        top.ctypes.data_as(_P(ctypes.c_int32))), "session_bench")
+        return ms.value, top
+
+    def profile(self, ids):
+        """One kept pass with per-launch device times: list of (class, bytes, ms)."""
+        a, p = _ids(ids)
+        cap = 4096
+        cls = np.zeros(cap, np.int32)
+        byt = np.zeros(cap, np.float64)
+        ms = np.zeros(cap, np.float32)
+        n = _lib().igc_session_profile(self._h, p, len(a), cls.ctypes.data_as(_P(ctypes.c_int)),
+                                       byt.ctypes.data_as(_P(ctypes.c_double)), ms.ctypes.data_as(_f), cap)
+        if n < 0:
+            raise IgcError(n, "session_profile")
+        return list(zip(cls[:n].tolist(), byt[:n].tolist(), ms[:n].tolist()))
 
     def serve_seconds(self):
         return _lib().igc_session_serve_seconds(self._h)

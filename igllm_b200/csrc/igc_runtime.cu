@@ -278,6 +278,7 @@ struct DevPlane {
   int n_rb = 0, n_cc = 0, rows = 0, cols = 0;
   int split = 1, grid = 1;
   bool pair = false;
+  double bytes = 0.0;  // codes and scales a product streams (app_core.c:1860 plane_bytes)
   GemvPlane view() const { return GemvPlane{tiles, scales, n_rb, n_cc, rows, cols}; }
 };
 
@@ -496,6 +497,7 @@ struct Binder {
       rb_at += prb;
       // app_core.c:1860 plane_bytes: codes and scales a product streams
       m->decode_bytes += cb + sb;
+      out.bytes += (double)(cb + sb);
       src.release(p.name + ".weight");
       src.release(p.name + ".weight_scale");
     }
@@ -798,9 +800,20 @@ struct igc_session {
   long kernels_per_pass[IGC_LANE_LIMIT + 1][2] = {};
   std::vector<void *> owned;
   int arg_parts = 0;
+  // per-launch timing for igc_session_profile: an event before every launch
+  struct Mark {
+    cudaEvent_t ev;
+    int cls;
+    double bytes;
+  };
+  bool prof_on = false;
+  std::vector<Mark> marks;
+  int32_t *d_rounds = nullptr;  // igc_session_bench's per-round [position, ids]
+  size_t d_rounds_cap = 0;
 
   ~igc_session() {
     cudaSetDevice(m->device);
+    for (auto &mk : marks) cudaEventDestroy(mk.ev);
     for (int k = 0; k <= IGC_LANE_LIMIT; ++k)
       for (int w = 0; w < 2; ++w)
         if (graph[k][w]) cudaGraphExecDestroy(graph[k][w]);
@@ -926,10 +939,24 @@ struct Ssq {
   int parts = 0;
 };
 
+// Launch classes igc_session_profile reports.
+enum { PROF_GEMV = 0, PROF_HEAD = 1, PROF_ATTN = 2, PROF_OTHER = 3, PROF_END = -1 };
+
+static void prof_mark(igc_session *s, int cls, double bytes) {
+  if (!s->prof_on) return;
+  igc_session::Mark mk;
+  mk.cls = cls;
+  mk.bytes = bytes;
+  cudaEventCreate(&mk.ev);
+  cudaEventRecord(mk.ev, s->st);
+  s->marks.push_back(mk);
+}
+
 static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, const float *x, int x_stride,
                 const float *p, const float *w_res, float gain, const float *w_in, float *x_out, float *out,
                 int out_stride, float out_scale = 1.0f, const float *aux = nullptr, int aux_stride = 0,
                 const Ssq *p_ssq = nullptr, Ssq *out_ssq = nullptr) {
+  prof_mark(s, &pl == &s->m->head ? PROF_HEAD : PROF_GEMV, pl.bytes);
   GemvArgs a;
   memset(&a, 0, sizeof(a));
   if (p_ssq) {
@@ -989,12 +1016,14 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   const int H = m->hidden, PS = m->layers * m->ple_dim;
   const int *d_p0 = s->d_io;
   const int32_t *d_ids = s->d_io + 1;
+  prof_mark(s, PROF_OTHER, 0.0);
   CKL(igc_launch_embed(d_ids, K, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
                        PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->st));
   if (m->ple_dim > 0) {
     int c = gemv(s, m->ple_lift, K, PRO_F32, EPI_STORE, s->x0, H, nullptr, nullptr, 1.0f, nullptr, nullptr,
                  s->ple_raw, PS, (float)(1.0 / sqrt((double)H)));
     if (c != IGC_OKAY) return c;
+    prof_mark(s, PROF_OTHER, 0.0);
     CKL(igc_launch_ple_finish(s->ple_raw, s->seed, K, m->layers, m->ple_dim, m->ple_norm, m->eps,
                               (float)(1.0 / sqrt(2.0)), s->ple, s->st));
   }
@@ -1025,6 +1054,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     if (c != IGC_OKAY) return c;
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
+    prof_mark(s, PROF_ATTN, 0.0);
     CKL(igc_launch_attn_prep(s->qkv, L.qkv_rows, m->heads, L.kv_heads, L.hd, L.q_norm, L.k_norm,
                              m->rope_cs[L.kind], m->rope_sn[L.kind], L.share ? 0 : 1, m->eps, d_p0, K,
                              s->kc[l], s->vc[l], s->st));
@@ -1067,8 +1097,10 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     int c = gemv(s, m->head, K, PRO_RESID_NORM, EPI_LOGITS, cur, H, pend, pend_w, pend_gain, m->final_norm, xo,
                  s->logits, m->vocab, 1.0f, nullptr, 0, pend_ssq, nullptr);
     if (c != IGC_OKAY) return c;
+    prof_mark(s, PROF_OTHER, 0.0);
     CKL(igc_launch_argmax(s->arg_val, s->arg_idx, m->head.grid, K, s->d_top, s->st));
   }
+  prof_mark(s, PROF_END, 0.0);
   return IGC_OKAY;
 }
 
@@ -1413,4 +1445,117 @@ extern "C" int igc_session_round(igc_session *s, const int32_t *ids, int k, cons
   return take + 1;
 }
 
+// ---------------------------------------------------------------------------
+// measurement entries (no counterpart in the reference)
 
+// `rounds` verify passes of `k` lanes with every block already in HBM: round
+// r runs blocks[r*k .. r*k+k) at the session's fill plus r*k, as a proposer
+// that is always right would, and the rounds follow one another on the
+// stream with no host round trip.  The span between the first and the last
+// pass is timed with CUDA events on the session's stream.  The session ends
+// with every round kept; `last_top` gets the last round's argmax ids.
+extern "C" int igc_session_bench(igc_session *s, const int32_t *blocks, int rounds, int k, float *device_ms,
+                                 int32_t *last_top) {
+  if (!s || !blocks || rounds < 1 || k < 1 || k > IGC_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  igc_model *m = s->m;
+  if (s->fill + rounds * k > m->window_limit) return IGC_FAIL_STATE;
+  for (int i = 0; i < rounds * k; ++i)
+    if (blocks[i] < 0 || blocks[i] >= m->vocab) return IGC_FAIL_ARGUMENT;
+  clear_stale("bench");
+  CK(cudaSetDevice(m->device));
+  const size_t rec = (size_t)(1 + k);
+  if (s->d_rounds_cap < rec * rounds) {
+    if (s->d_rounds) cudaFree(s->d_rounds);
+    s->d_rounds = nullptr;
+    CK(cudaMalloc(&s->d_rounds, sizeof(int32_t) * rec * rounds));
+    s->owned.push_back(s->d_rounds);
+    s->d_rounds_cap = rec * rounds;
+  }
+  std::vector<int32_t> host(rec * rounds);
+  for (int r = 0; r < rounds; ++r) {
+    host[r * rec] = s->fill + r * k;
+    memcpy(&host[r * rec + 1], blocks + (size_t)r * k, sizeof(int32_t) * k);
+  }
+  CK(cudaMemcpy(s->d_rounds, host.data(), sizeof(int32_t) * host.size(), cudaMemcpyHostToDevice));
+  // the pass of this shape, captured once
+  if (s->use_graphs && !s->graph[k][1]) {
+    CK(cudaMemcpyAsync(s->d_io, s->d_rounds, sizeof(int32_t) * rec, cudaMemcpyDeviceToDevice, s->st));
+    cudaGraph_t g;
+    long before = g_launches;
+    CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    int c = enqueue_pass(s, k, 1);
+    cudaError_t e = cudaStreamEndCapture(s->st, &g);
+    if (c != IGC_OKAY) return c;
+    if (e != cudaSuccess) return fail_device(e, "capture");
+    s->kernels_per_pass[k][1] = g_launches - before;
+    g_launches = before;
+    e = cudaGraphInstantiate(&s->graph[k][1], g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail_device(e, "graph instantiate");
+  }
+  cudaEvent_t a, b;
+  CK(cudaEventCreate(&a));
+  CK(cudaEventCreate(&b));
+  CK(cudaEventRecord(a, s->st));
+  for (int r = 0; r < rounds; ++r) {
+    CK(cudaMemcpyAsync(s->d_io, s->d_rounds + (size_t)r * rec, sizeof(int32_t) * rec, cudaMemcpyDeviceToDevice,
+                       s->st));
+    if (s->use_graphs) {
+      CK(cudaGraphLaunch(s->graph[k][1], s->st));
+      g_launches += s->kernels_per_pass[k][1];
+    } else {
+      int c = enqueue_pass(s, k, 1);
+      if (c != IGC_OKAY) return c;
+    }
+  }
+  CK(cudaEventRecord(b, s->st));
+  CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * k, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  float ms = 0.0f;
+  CK(cudaEventElapsedTime(&ms, a, b));
+  cudaEventDestroy(a);
+  cudaEventDestroy(b);
+  if (device_ms) *device_ms = ms;
+  if (last_top) memcpy(last_top, s->h_top, sizeof(int32_t) * k);
+  s->fill += rounds * k;
+  for (int i = 0; i < rounds * k && (int)s->echo.size() < m->window_limit; ++i) s->echo.push_back(blocks[i]);
+  s->logit_lanes = k;
+  return IGC_OKAY;
+}
+
+// One pass of `k` lanes (ids from `ids`, position the session's fill, kept)
+// with a CUDA event before every launch: for each launch its class (0 a
+// projection, 1 the output head, 2 attention, 3 the rest), the weight bytes
+// it streams and its device time in ms.  Returns the launches recorded.
+extern "C" int igc_session_profile(igc_session *s, const int32_t *ids, int k, int *cls_out, double *bytes_out,
+                                   float *ms_out, int capacity) {
+  if (!s || !ids || k < 1 || k > IGC_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  igc_model *m = s->m;
+  if (s->fill + k > m->window_limit) return IGC_FAIL_STATE;
+  clear_stale("profile");
+  CK(cudaSetDevice(m->device));
+  s->h_io[0] = s->fill;
+  memcpy(s->h_io + 1, ids, sizeof(int32_t) * (size_t)k);
+  CK(cudaMemcpyAsync(s->d_io, s->h_io, sizeof(int32_t) * (size_t)(1 + k), cudaMemcpyHostToDevice, s->st));
+  for (auto &mk : s->marks) cudaEventDestroy(mk.ev);
+  s->marks.clear();
+  s->prof_on = true;
+  int c = enqueue_pass(s, k, 1);
+  s->prof_on = false;
+  if (c != IGC_OKAY) return c;
+  CK(cudaStreamSynchronize(s->st));
+  int n = 0;
+  for (size_t i = 0; i + 1 < s->marks.size() && n < capacity; ++i, ++n) {
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, s->marks[i].ev, s->marks[i + 1].ev));
+    if (cls_out) cls_out[n] = s->marks[i].cls;
+    if (bytes_out) bytes_out[n] = s->marks[i].bytes;
+    if (ms_out) ms_out[n] = ms;
+  }
+  s->fill += k;
+  for (int j = 0; j < k && (int)s->echo.size() < m->window_limit; ++j) s->echo.push_back(ids[j]);
+  s->logit_lanes = k;
+  return n;
+}

@@ -192,6 +192,24 @@ int igc_session_round(igc_session *session, const int32_t *id_list, int id_count
 double igc_session_serve_seconds(const igc_session *session);
 size_t igc_session_serve_tokens(const igc_session *session);
 
+/* ---- measurement (no counterpart in the reference) ----------------------
+ *
+ * igc_session_bench: `rounds` verify passes of `k` lanes whose blocks are all
+ * uploaded to HBM first; round r runs blocks[r*k .. r*k+k) at the session's
+ * fill plus r*k - the always-right proposer of the reference's guess bracket
+ * (app_main.c:1235 main_guess_run, MAIN_GUESS_ORACLE) - with no host round
+ * trip between rounds.  `device_ms` gets the CUDA-event time of the rounds,
+ * `last_top` the last round's argmax ids (k of them); the rounds are kept.
+ *
+ * igc_session_profile: one kept pass of `k` lanes with a CUDA event before
+ * every launch; per launch its class (0 a layer projection, 1 the output
+ * head, 2 attention, 3 the rest), the weight bytes it streams and its device
+ * time.  Returns the number of launches written (at most `capacity`). */
+int igc_session_bench(igc_session *session, const int32_t *blocks, int rounds, int k, float *device_ms,
+                      int32_t *last_top);
+int igc_session_profile(igc_session *session, const int32_t *ids, int k, int *cls_out, double *bytes_out,
+                        float *ms_out, int capacity);
+
 /* ---- n-gram scout (app_core.c:12277-12361), host C --------------------- */
 
 typedef struct igc_scout igc_scout;
