@@ -340,11 +340,15 @@ def run_ours(args):
     h_bytes, h_ms = sum(b for b, _ in head), sum(ms for _, ms in head)
     peak, peak_kind = peaks()
     achieved = g_bytes / (g_ms / 1000.0) / 1e9
+    # DRAM bytes per projection launch: the algorithmic bytes times the
+    # DRAM/algorithmic ratio ncu measured on the same kernels (profiles/).
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "gemv_dram_traffic.json")) as f:
-            traffic = json.load(f).get("dram_bytes_per_launch")
-    except Exception:
+        with open(os.path.join(ROOT, "profiles", "gemv_e2b_layer0_k4_full.txt")) as f:
+            for ln in f:
+                if ln.startswith("dram_over_algorithmic:"):
+                    traffic = round(float(ln.split()[1]) * g_bytes / max(1, len(gemv)))
+    except OSError:
         traffic = None
     round_s = per_k[str(GUESS)] / 1e6
     bytes_round = model.decode_bytes()
@@ -365,6 +369,7 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "kernel": "int4 skinny GEMM (layer projections)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "launches_per_pass": len(gemv), "algorithmic_bytes_per_launch": round(g_bytes / max(1, len(gemv))),
                      "bytes_per_pass": g_bytes, "ms_per_pass": round(g_ms, 4),
                      "head_gbs": round(h_bytes / (h_ms / 1000.0) / 1e9, 1) if h_ms else None,
                      "attention_ms_per_pass": round(attn_ms, 4), "other_ms_per_pass": round(other_ms, 4),
