@@ -158,6 +158,7 @@ def _lib():
         "igc_desk_status": (i, [_P(_Desk)]),
         "igc_last_error": (ctypes.c_char_p, []),
         "igc_launch_count": (ctypes.c_long, []),
+        "igc_norm_rms_fixed": (i, [i, fp, fp, i, ctypes.c_float, fp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -180,7 +181,7 @@ def exported_symbols():
         "igc_session_serve_seconds", "igc_session_serve_tokens", "igc_session_bench", "igc_session_profile",
         "igc_scout_open", "igc_scout_close",
         "igc_scout_clear", "igc_scout_note", "igc_scout_span", "igc_scout_draw", "igc_synth_fill",
-        "igc_synth_write", "igc_model_synth", "igc_last_error", "igc_launch_count",
+        "igc_synth_write", "igc_model_synth", "igc_last_error", "igc_launch_count", "igc_norm_rms_fixed",
     ]
 
 
@@ -433,6 +434,25 @@ class Desk:
                           s.ctypes.data_as(_f))
         _check(self.status(), "desk.rope_turn")
         return x
+
+
+FIXED_NORM_LIMIT = 65536  # include/igllm_cuda.h IGC_FIXED_NORM_LIMIT
+
+
+def norm_rms_fixed(x, w, eps, device=0):
+    """igc_norm_rms_fixed: the desk's norm_rms through a fixed device array,
+    with no allocation on the device (vectors up to FIXED_NORM_LIMIT floats;
+    overlapping calls on one device race)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.zeros_like(x)
+    wa = np.ascontiguousarray(w, np.float32) if w is not None else None
+    wp = wa.ctypes.data_as(_f) if wa is not None else None
+    code = _lib().igc_norm_rms_fixed(int(device), x.ctypes.data_as(_f), wp, len(x), float(eps),
+                                     out.ctypes.data_as(_f))
+    if code == FAIL_ARGUMENT and len(x) > FIXED_NORM_LIMIT:
+        raise IgcError(code, f"norm_rms_fixed: {len(x)} floats exceed the fixed array's {FIXED_NORM_LIMIT}")
+    _check(code, "norm_rms_fixed")
+    return out
 
 
 def synth_write(spec, folder, threads=8):

@@ -23,6 +23,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -1558,4 +1559,65 @@ extern "C" int igc_session_profile(igc_session *s, const int32_t *ids, int k, in
   for (int j = 0; j < k && (int)s->echo.size() < m->window_limit; ++j) s->echo.push_back(ids[j]);
   s->logit_lanes = k;
   return n;
+}
+
+// ---------------------------------------------------------------------------
+// norm_rms with no allocation (no counterpart in the reference)
+//
+// The desk's norm_rms grows device buffers with cudaMalloc whenever a longer
+// vector arrives.  Two kinds of caller cannot allow that.  One is a host token
+// loop that promised to allocate nothing once it runs; the reference sizes
+// its backend's staging when the table opens for exactly this reason.  The
+// other is a caller that holds no desk and would otherwise open one, with
+// its buffers, to normalise a single vector.  This entry keeps its three
+// vectors (input, gain, output) in one array that is part of the library's
+// device image, and calls nothing that allocates.
+//
+// No word of the array has to start at zero: a call writes every word it
+// reads (the input, then the gain when one is given, then the kernel's
+// output) before reading it.  All calls on one device share the array, so
+// two calls that overlap in time on the same device, from two host threads
+// for instance, race: each may read the other's vectors.  Callers serialise
+// them.
+static __device__ __align__(256) float g_fixed_norm[3 * IGC_FIXED_NORM_LIMIT];  // 768 KiB a device
+static float *g_fixed_norm_at[IGC_FIXED_DEVICE_LIMIT];  // its address on each device, found on first use
+static std::mutex g_fixed_norm_lock;
+
+static int norm_rms_fixed_on(int device, const float *value_list, const float *gain_list, int value_count,
+                             float eps_value, float *value_out) {
+  CK(cudaSetDevice(device));
+  float *base = nullptr;
+  cudaError_t e = cudaSuccess;
+  {
+    // the address, looked up once per device with that device current
+    std::lock_guard<std::mutex> hold(g_fixed_norm_lock);
+    base = g_fixed_norm_at[device];
+    if (!base) {
+      e = cudaGetSymbolAddress((void **)&base, g_fixed_norm);
+      if (e == cudaSuccess) g_fixed_norm_at[device] = base;
+    }
+  }
+  if (e != cudaSuccess) return fail_device(e, "cudaGetSymbolAddress(g_fixed_norm)");
+  float *d_x = base, *d_w = base + IGC_FIXED_NORM_LIMIT, *d_out = base + 2 * IGC_FIXED_NORM_LIMIT;
+  const size_t bytes = sizeof(float) * (size_t)value_count;
+  cudaStream_t st = cudaStreamPerThread;
+  CK(cudaMemcpyAsync(d_x, value_list, bytes, cudaMemcpyHostToDevice, st));
+  if (gain_list) CK(cudaMemcpyAsync(d_w, gain_list, bytes, cudaMemcpyHostToDevice, st));
+  CKL(igc_launch_desk_norm(d_x, gain_list ? d_w : nullptr, value_count, eps_value, d_out, st));
+  CK(cudaMemcpyAsync(value_out, d_out, bytes, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  return IGC_OKAY;
+}
+
+extern "C" int igc_norm_rms_fixed(int device, const float *value_list, const float *gain_list, int value_count,
+                                  float eps_value, float *value_out) {
+  if (!value_list || !value_out || value_count < 1 || device < 0 || device >= IGC_FIXED_DEVICE_LIMIT)
+    return IGC_FAIL_ARGUMENT;
+  if (value_count > IGC_FIXED_NORM_LIMIT) return IGC_FAIL_ARGUMENT;  // longer than the fixed array holds
+  clear_stale("norm_rms_fixed");
+  int before = -1;
+  if (cudaGetDevice(&before) != cudaSuccess) before = -1;
+  int c = norm_rms_fixed_on(device, value_list, gain_list, value_count, eps_value, value_out);
+  if (before >= 0 && before != device) cudaSetDevice(before);  // the caller's device stays current
+  return c;
 }

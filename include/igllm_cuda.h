@@ -210,6 +210,27 @@ int igc_session_bench(igc_session *session, const int32_t *blocks, int rounds, i
 int igc_session_profile(igc_session *session, const int32_t *ids, int k, int *cls_out, double *bytes_out,
                         float *ms_out, int capacity);
 
+/* ---- normalisation with no allocation (no counterpart in the reference) --
+ *
+ * igc_norm_rms_fixed: the desk's norm_rms (app_core.c:4667 kern_norm_rms,
+ * host pointers in and out, synchronous) for callers that must not allocate:
+ * a token loop that promised to allocate nothing once running, or a caller
+ * holding no desk.  The input, gain and output live in one fixed array of the
+ * library's device image (3 x IGC_FIXED_NORM_LIMIT floats, 768 KiB a device);
+ * the call makes no allocating CUDA or library call.  The array's address is
+ * looked up on the first call on each device, with that device current; make
+ * that first call before any stream capture starts.  `device` is made current
+ * for the call and the caller's device restored after it.  `gain_list` may be
+ * NULL (no gain).  Vectors longer than IGC_FIXED_NORM_LIMIT, or a device at or
+ * beyond IGC_FIXED_DEVICE_LIMIT, are refused with IGC_FAIL_ARGUMENT and nothing
+ * is copied.  Nothing in the array needs to start at zero.  Calls on one
+ * device share the array: calls that overlap in time on the same device race,
+ * so callers serialise them. */
+#define IGC_FIXED_NORM_LIMIT 65536
+#define IGC_FIXED_DEVICE_LIMIT 64
+int igc_norm_rms_fixed(int device, const float *value_list, const float *gain_list, int value_count,
+                       float eps_value, float *value_out);
+
 /* ---- n-gram scout (app_core.c:12277-12361), host C --------------------- */
 
 typedef struct igc_scout igc_scout;
