@@ -37,6 +37,7 @@ struct DeskState {
   size_t buf_floats = 0;
   float *arg_val = nullptr;
   int *arg_idx = nullptr;
+  int *err = nullptr;  // set by a projection that gave up waiting for its weights
 };
 
 DeskState *state_of(igc_desk *d) {
@@ -127,7 +128,8 @@ void desk_mat_mat(igc_desk *d, const igc_plane *sheet, const float *act, int act
     a.out_scale = 1.0f;
     a.part_val = s->arg_val;
     a.part_idx = s->arg_idx;
-    if (igc_gemv_smem(&a) > (size_t)s->smem_limit) {
+    a.err = s->err;
+    if (igc_gemv_smem_min(&a, 0) > (size_t)s->smem_limit) {
       // wide planes stage at most eight lanes at a time
       int k8 = k < 8 ? k : 8;
       for (int j0 = 0; j0 < k; j0 += k8) {
@@ -135,10 +137,10 @@ void desk_mat_mat(igc_desk *d, const igc_plane *sheet, const float *act, int act
         b.lanes = k - j0 < k8 ? k - j0 : k8;
         b.x = s->buf_a + (size_t)j0 * p->cols;
         b.out = s->buf_b + (size_t)j0 * p->rows;
-        if (igc_gemv_smem(&b) > (size_t)s->smem_limit) return void(note(s, IGC_FAIL_SUPPORT));
-        if (!ok(s, igc_launch_gemv(&b, 0, PRO_F32, EPI_STORE, p->grid, s->st))) return;
+        if (igc_gemv_smem_min(&b, 0) > (size_t)s->smem_limit) return void(note(s, IGC_FAIL_SUPPORT));
+        if (!ok(s, igc_launch_gemv(&b, 0, PRO_F32, EPI_STORE, p->grid, (size_t)s->smem_limit, s->st))) return;
       }
-    } else if (!ok(s, igc_launch_gemv(&a, 0, PRO_F32, EPI_STORE, p->grid, s->st))) {
+    } else if (!ok(s, igc_launch_gemv(&a, 0, PRO_F32, EPI_STORE, p->grid, (size_t)s->smem_limit, s->st))) {
       return;
     }
     for (int j = 0; j < k; ++j)
@@ -146,6 +148,12 @@ void desk_mat_mat(igc_desk *d, const igc_plane *sheet, const float *act, int act
                                  sizeof(float) * p->rows, cudaMemcpyDeviceToHost, s->st)))
         return;
     if (!ok(s, cudaStreamSynchronize(s->st))) return;
+    int gave_up = 0;  // a projection that gave up waiting for its weight copies
+    if (!ok(s, cudaMemcpy(&gave_up, s->err, sizeof(int), cudaMemcpyDeviceToHost))) return;
+    if (gave_up) {
+      cudaMemset(s->err, 0, sizeof(int));
+      return void(note(s, IGC_FAIL_DEVICE));
+    }
     done += k;
   }
 }
@@ -208,7 +216,8 @@ extern "C" int igc_back_open(igc_desk *desk, int device) {
       cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess ||
       igc_kernels_configure(227 * 1024) != cudaSuccess ||
       cudaMalloc(&s->arg_val, (size_t)s->sm_count * 4 * 16 * 4) != cudaSuccess ||
-      cudaMalloc(&s->arg_idx, (size_t)s->sm_count * 4 * 16 * 4) != cudaSuccess) {
+      cudaMalloc(&s->arg_idx, (size_t)s->sm_count * 4 * 16 * 4) != cudaSuccess ||
+      cudaMalloc(&s->err, sizeof(int)) != cudaSuccess || cudaMemset(s->err, 0, sizeof(int)) != cudaSuccess) {
     delete s;
     return IGC_FAIL_DEVICE;
   }
@@ -237,6 +246,7 @@ extern "C" void igc_back_close(igc_desk *desk) {
   cudaFree(s->buf_c);
   cudaFree(s->arg_val);
   cudaFree(s->arg_idx);
+  cudaFree(s->err);
   if (s->st) cudaStreamDestroy(s->st);
   delete s;
   desk->state = nullptr;

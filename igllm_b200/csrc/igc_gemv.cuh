@@ -16,8 +16,10 @@
 // magnitude at 2^14 (exact, undone in the epilogue), then staged as two f16
 // values, hi = f16(a) and lo = f16(a - hi); both go through the tensor core
 // against the same dequantised weights, so the product carries about 22
-// significant bits of the activation at the cost of a second MMA per 16
-// columns, and no lane can overflow f16.
+// significant bits of the activation, and no lane can overflow f16.  The hi
+// and lo products are accumulated apart and added once per output, in the
+// same order whatever the lane count, so a lane's result does not depend on
+// how many lanes shared its pass.
 //
 // Norms ride on linearity: W (norm(y) * w) = shrink(y) * W (y * w), so the
 // prologue stages y * w in one elementwise pass and the epilogue multiplies by
@@ -31,7 +33,9 @@
 //            A fragments of the four 16-column products it takes part in.
 //   scales : [row_block][chunk][8] uint2 - for the thread group g = lane/4,
 //            the f16 scales of rows g and g+8 for the chunk's two groups.
-// Row blocks are 16 rows; chunks are 64 columns (two groups of 32).
+// Row blocks are 16 rows; chunks are 64 columns (two groups of 32).  One row
+// block's chunks are contiguous, so a warp fetches a run of them with one
+// bulk copy into shared memory.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -42,6 +46,13 @@ namespace igc {
 
 enum : int { PRO_F32 = 0, PRO_NORM = 1, PRO_RESID = 2, PRO_RESID_NORM = 3 };
 enum : int { EPI_STORE = 0, EPI_GELU_PAIR = 1, EPI_GELU_MUL = 2, EPI_LOGITS = 3 };
+
+// Lane modes.  PACK (up to 4 lanes): one 8-column B tile carries lanes 0-3 hi
+// in columns 0-3 and their lo halves in columns 4-7, so one product does both.
+// NT1 / NT2 (up to 8 / 16 lanes): hi and lo are separate B tiles, 8 lanes each.
+enum : int { MODE_PACK = 0, MODE_NT1 = 1, MODE_NT2 = 2 };
+
+__host__ __device__ inline int gemv_mode(int lanes) { return lanes <= 4 ? MODE_PACK : lanes <= 8 ? MODE_NT1 : MODE_NT2; }
 
 struct GemvPlane {
   const uint4 *tiles;
@@ -55,7 +66,12 @@ struct GemvPlane {
 struct GemvArgs {
   GemvPlane pl;
   int lanes;
-  int split;  // warps that share one row block's chunks (1, 2, 4 or 8)
+  int split;  // warps that share one row block's chunks (1, 2, 4 or 8), fixed per plane
+  // weight ring (set by the launcher): chunks a piece, pieces in flight a warp,
+  // and where the reduction space, barriers and ring sit in shared memory
+  int piece, depth;
+  int off_red, off_bars, off_ring;
+  int *err;  // set nonzero when a wait gave up
   // prologue
   const float *x;
   int x_stride;
@@ -82,17 +98,30 @@ struct GemvArgs {
 
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+constexpr int GEMV_PIECE_BYTES = 576;  // one chunk of one row block: 512 B of codes + 64 B of scales
+constexpr int GEMV_MAX_DEPTH = 8;
+constexpr int GEMV_PART_LIMIT = 320;  // producer partials the prologue reads (16 stripes x 20)
 
-// Staged activations: for chunk cc, lane tile nt and thread slot s, 16
-// consecutive u32 words - the hi B fragments of the chunk's four 16-column
-// products (b0, b1 each) and then the lo ones.  Word of (lane n, column c):
-__device__ __forceinline__ int stage_word(int n, int c, int NT) {
-  int cc = c >> 6, kb = (c >> 4) & 3, k = c & 15;
-  int nt = n >> 3, g = n & 7, t = (k & 7) >> 1;
-  return (((cc * NT + nt) * 32 + g * 4 + t) * 16) + kb * 2 + (k >> 3);
+// Staged activations, per chunk: PACK 32 thread slots x 8 words (the four
+// 16-column products' b0, b1), NT 32 slots x 16 words per 8-lane tile (hi
+// b0, b1 of the four products, then lo).  Word of (lane n, column c, half):
+__device__ __forceinline__ int stage_word(int n, int c, int lo, int MODE) {
+  const int cc = c >> 6, kb = (c >> 4) & 3, k = c & 15, t = (k & 7) >> 1;
+  if (MODE == MODE_PACK) {
+    const int g = n + (lo ? 4 : 0);
+    return ((cc * 32 + g * 4 + t) * 8) + kb * 2 + (k >> 3);
+  }
+  const int NT = MODE == MODE_NT2 ? 2 : 1;
+  const int nt = n >> 3, g = n & 7;
+  return (((cc * NT + nt) * 32 + g * 4 + t) * 16) + kb * 2 + (k >> 3) + (lo ? 8 : 0);
 }
 
-__host__ __device__ inline size_t gemv_stage_bytes(int n_cc, int NT) { return (size_t)n_cc * NT * 32 * 64; }
+__host__ __device__ inline int stage_chunk_words(int MODE) { return MODE == MODE_PACK ? 256 : MODE == MODE_NT1 ? 512 : 1024; }
+
+__host__ __device__ inline size_t gemv_stage_bytes(int n_cc, int MODE) { return (size_t)n_cc * stage_chunk_words(MODE) * 4; }
+
+// Accumulator floats a thread keeps per half (gate or up) of a unit.
+__host__ __device__ inline int gemv_acc_floats(int MODE) { return MODE == MODE_PACK ? 4 : MODE == MODE_NT1 ? 8 : 16; }
 
 // app_core.c:4667 kern_norm_rms's shrink: (mean of squares + eps)^-1/2 in
 // double, applied in float as x * shrink * w.
@@ -100,24 +129,16 @@ __device__ __forceinline__ float rms_shrink(float ssq, int n, float eps) {
   return (float)(1.0 / sqrt((double)ssq / (double)n + (double)eps));
 }
 
-// First pass: two consecutive columns (c even) of lane n as raw f32 in the
-// two words their hi and lo f16 pairs will occupy.
-__device__ __forceinline__ void stage_pair(uint32_t *stage, int n, int c, float a0, float a1, int NT) {
-  int w = stage_word(n, c, NT);
-  stage[w] = __float_as_uint(a0);
-  stage[w + 8] = __float_as_uint(a1);
-}
-
-// Second pass, over the same words the same thread wrote: scaled, split into
-// hi/lo f16 pairs.
-__device__ __forceinline__ void stage_seal(uint32_t *stage, int n, int c, float scale, int NT) {
-  int w = stage_word(n, c, NT);
-  float a0 = __uint_as_float(stage[w]) * scale, a1 = __uint_as_float(stage[w + 8]) * scale;
+// The pair of words that hold columns c, c + 1 (c even) of one lane: the
+// first pass leaves their raw f32 values there (c in the hi word, c + 1 in
+// the lo word); this turns them, scaled, into the hi and lo f16 pairs.
+__device__ __forceinline__ void seal_words(uint32_t *stage, int wh, int wl, float scale) {
+  float a0 = __uint_as_float(stage[wh]) * scale, a1 = __uint_as_float(stage[wl]) * scale;
   __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
   __half l0 = __float2half_rn(a0 - __half2float(h0)), l1 = __float2half_rn(a1 - __half2float(h1));
   __half2 hi = __halves2half2(h0, h1), lo = __halves2half2(l0, l1);
-  stage[w] = *reinterpret_cast<uint32_t *>(&hi);
-  stage[w + 8] = *reinterpret_cast<uint32_t *>(&lo);
+  stage[wh] = *reinterpret_cast<uint32_t *>(&hi);
+  stage[wl] = *reinterpret_cast<uint32_t *>(&lo);
 }
 
 // The power of two that puts a lane's largest magnitude at or under 2^14.
@@ -141,159 +162,248 @@ __device__ __forceinline__ float fmax4(float4 v) { return fmaxf(fmaxf(fabsf(v.x)
 constexpr int SCR_FACTOR = 0, SCR_SCALE = 16, SCR_SHRINK_P = 32, SCR_SSQ = 64, SCR_AMAX = 192, SCR_STRIPE = 320;
 constexpr int SCR_FLOATS = 576;
 
-// The prologue, one elementwise pass and one shared-memory pass.  Warps take
-// lanes: with K < 8 lanes, 8/K warps (a power of two) split one lane's
-// columns; with more, a warp takes lanes w and w + 8.  Each thread walks its
-// float4 columns with four loads in flight, and the per-lane reductions are
-// a fixed-order sum over the parts.
+// float4 columns a thread loads before computing on them: as many as keep
+// the register file in bounds for the arrays the prologue reads.
 template <int PRO>
-__device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr, int NT) {
+struct ProBatch {
+  static constexpr int value = PRO == PRO_F32 ? 8 : PRO == PRO_NORM ? 6 : 4;
+};
+
+// The prologue.  Warps take lanes: with K < 8 lanes, 8/K warps (a power of
+// two) split one lane's columns; with more, a warp takes lanes w and w + 8.
+// Thread l32 of a warp walks float4 columns c4 = lo + l32 + 32 i; the stage
+// words of column 4 c4 move by two chunks per step of i, so each thread
+// computes its four word offsets once and then only adds.  The producer
+// partials and the first batch of activations are loaded before anything
+// waits on either; the per-lane reductions are fixed-order sums.
+template <int PRO, int MODE>
+__device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
+  constexpr bool RES = PRO == PRO_RESID || PRO == PRO_RESID_NORM;
+  constexpr bool NRM = PRO == PRO_NORM || PRO == PRO_RESID_NORM;
+  constexpr int B = ProBatch<PRO>::value;
+  constexpr int PQ = GEMV_PART_LIMIT / 16;
   const int cols = a.pl.cols, K = a.lanes, n4 = cols >> 2;
   const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
-  const int stage_words = (int)(gemv_stage_bytes(a.pl.n_cc, NT) / 4);
-  for (int i = threadIdx.x; i < stage_words / 4; i += blockDim.x)
-    reinterpret_cast<uint4 *>(stage)[i] = make_uint4(0u, 0u, 0u, 0u);
-  if (PRO == PRO_RESID || PRO == PRO_RESID_NORM) {
-    // the residual's shrink from its producer's partials: thread (lane j,
-    // stripe q0) sums parts q0, q0 + 16, ...; stripes are then added in order
-    const int j = threadIdx.x & 15, q0 = threadIdx.x >> 4;
-    float t = 0.0f;
-    if (j < K)
-      for (int q = q0; q < a.p_parts; q += 16) t += a.p_ssq[q * 16 + j];
-    scr[SCR_STRIPE + threadIdx.x] = t;
+  const int step = 2 * stage_chunk_words(MODE);  // stage words between items i and i + 1
+  if (cols & 63) {
+    // columns past `cols` in the last chunk meet zero weights, and must be
+    // zero (not stale NaN patterns) for the products to stay exact
+    const int words = (int)(gemv_stage_bytes(a.pl.n_cc, MODE) / 16);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) reinterpret_cast<uint4 *>(stage)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
-    if (threadIdx.x < 16 && (int)threadIdx.x < K) {
-      float u = 0.0f;
-      for (int q = 0; q < 16; ++q) u += scr[SCR_STRIPE + q * 16 + threadIdx.x];
-      scr[SCR_SHRINK_P + threadIdx.x] = rms_shrink(u, cols, a.eps);
+  }
+  // the residual's partials: thread (lane j, stripe q0) holds parts q0, q0 + 16, ...
+  float part[RES ? PQ : 1];
+  if (RES) {
+    const int j = threadIdx.x & 15, q0 = threadIdx.x >> 4;
+#pragma unroll
+    for (int i = 0; i < PQ; ++i) {
+      const int q = q0 + 16 * i;
+      part[i] = (j < K && q < a.p_parts) ? a.p_ssq[q * 16 + j] : 0.0f;
     }
   }
-  __syncthreads();
   int wpl = 1;  // warps a lane
   while (wpl * 2 * K <= GEMV_WARPS) wpl *= 2;
   const int n_slots = (K + GEMV_WARPS - 1) / GEMV_WARPS;  // lanes a warp (1 or 2)
+  const int part_ = wpl > 1 ? warp % wpl : 0;
+  const int lo = (n4 * part_) / wpl, hi = (n4 * (part_ + 1)) / wpl;
+  const int c4_0 = lo + l32;
+  const int count = c4_0 < hi ? (hi - c4_0 + 31) >> 5 : 0;  // items of this thread per slot
   const float4 *__restrict__ x4 = reinterpret_cast<const float4 *>(a.x);
   const float4 *__restrict__ p4 = reinterpret_cast<const float4 *>(a.p);
   const float4 *__restrict__ wr4 = reinterpret_cast<const float4 *>(a.w_res);
   const float4 *__restrict__ win4 = reinterpret_cast<const float4 *>(a.w_in);
-  float4 *__restrict__ xo4 = (blockIdx.x == 0 && a.x_out) ? reinterpret_cast<float4 *>(a.x_out) : nullptr;
+  const bool write_x = blockIdx.x == 0 && a.x_out;
   const int xs4 = a.x_stride >> 2, ps4 = a.p_stride >> 2;
   const float gain = a.gain;
-  for (int slot = 0; slot < n_slots; ++slot) {
-    const int j = wpl > 1 ? warp / wpl : warp + slot * GEMV_WARPS;
-    const int part = wpl > 1 ? warp % wpl : 0;
-    float ssq = 0.0f, amax = 0.0f;
-    if (j < K) {
-      const int lo = (n4 * part) / wpl, hi = (n4 * (part + 1)) / wpl;
-      const float sp = (PRO == PRO_RESID || PRO == PRO_RESID_NORM) ? scr[SCR_SHRINK_P + j] : 0.0f;
-#pragma unroll 4
-      for (int c4 = lo + l32; c4 < hi; c4 += 32) {
-        float4 y = x4[(size_t)j * xs4 + c4];
-        if (PRO == PRO_RESID || PRO == PRO_RESID_NORM) {
+
+  int jj[2];
+  bool live[2];
+  int wh0[2], wl0[2], wh2[2], wl2[2];  // word offsets of item 0: columns c, c + 1 (hi, lo) and c + 2, c + 3
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    jj[slot] = wpl > 1 ? warp / wpl : warp + slot * GEMV_WARPS;
+    live[slot] = slot < n_slots && jj[slot] < K;
+    const int c = c4_0 * 4;
+    wh0[slot] = stage_word(jj[slot], c, 0, MODE);
+    wl0[slot] = stage_word(jj[slot], c, 1, MODE);
+    wh2[slot] = stage_word(jj[slot], c + 2, 0, MODE);
+    wl2[slot] = stage_word(jj[slot], c + 2, 1, MODE);
+  }
+
+  float4 X[B], Pv[B], WR[B], WI[B];
+  float ssq[2] = {0.0f, 0.0f}, amax[2] = {0.0f, 0.0f};
+  auto load = [&](int slot, int i0) {
+    const int j = jj[slot];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (i0 + b < count) {
+        const int c4 = c4_0 + 32 * (i0 + b);
+        X[b] = x4[(size_t)j * xs4 + c4];
+        if (RES) {
+          Pv[b] = p4[(size_t)j * ps4 + c4];
+          WR[b] = wr4[c4];
+        }
+        if (NRM) WI[b] = win4[c4];
+      }
+    }
+  };
+  auto compute = [&](int slot, int i0) {
+    const int j = jj[slot];
+    const float sp = RES ? scr[SCR_SHRINK_P + j] : 0.0f;
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (i0 + b < count) {
+        const int i = i0 + b;
+        float4 y = X[b];
+        if (RES) {
           // app_core.c:11690-11740: x += norm(p) * w, then the layer gain
-          float4 pv = p4[(size_t)j * ps4 + c4], wr = wr4[c4];
-          y.x = y.x + pv.x * sp * wr.x;
-          y.y = y.y + pv.y * sp * wr.y;
-          y.z = y.z + pv.z * sp * wr.z;
-          y.w = y.w + pv.w * sp * wr.w;
+          y.x = y.x + Pv[b].x * sp * WR[b].x;
+          y.y = y.y + Pv[b].y * sp * WR[b].y;
+          y.z = y.z + Pv[b].z * sp * WR[b].z;
+          y.w = y.w + Pv[b].w * sp * WR[b].w;
           if (gain != 1.0f) {
             y.x *= gain;
             y.y *= gain;
             y.z *= gain;
             y.w *= gain;
           }
-          if (xo4) xo4[(size_t)j * xs4 + c4] = y;
+          if (write_x) reinterpret_cast<float4 *>(a.x_out)[(size_t)j * xs4 + c4_0 + 32 * i] = y;
         }
-        if (PRO != PRO_F32) ssq += y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
-        if (PRO == PRO_NORM || PRO == PRO_RESID_NORM) {
-          float4 w = win4[c4];
-          y.x *= w.x;
-          y.y *= w.y;
-          y.z *= w.z;
-          y.w *= w.w;
+        if (PRO != PRO_F32) ssq[slot] += y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
+        if (NRM) {
+          y.x *= WI[b].x;
+          y.y *= WI[b].y;
+          y.z *= WI[b].z;
+          y.w *= WI[b].w;
         }
-        amax = fmaxf(amax, fmax4(y));
-        stage_pair(stage, j, c4 * 4, y.x, y.y, NT);
-        stage_pair(stage, j, c4 * 4 + 2, y.z, y.w, NT);
+        amax[slot] = fmaxf(amax[slot], fmax4(y));
+        const int o = step * i;
+        stage[wh0[slot] + o] = __float_as_uint(y.x);
+        stage[wl0[slot] + o] = __float_as_uint(y.y);
+        stage[wh2[slot] + o] = __float_as_uint(y.z);
+        stage[wl2[slot] + o] = __float_as_uint(y.w);
       }
     }
-    ssq = warp_sum(ssq);
-    amax = warp_max(amax);
-    if (l32 == 0 && j < K) {
-      scr[SCR_SSQ + j * 8 + part] = ssq;
-      scr[SCR_AMAX + j * 8 + part] = amax;
+  };
+
+  if (live[0]) load(0, 0);
+  if (RES) {
+    float tsum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < PQ; ++i) tsum += part[i];
+    scr[SCR_STRIPE + threadIdx.x] = tsum;
+    __syncthreads();
+    if (threadIdx.x < 16 && (int)threadIdx.x < K) {
+      float u = 0.0f;
+      for (int q = 0; q < 16; ++q) u += scr[SCR_STRIPE + q * 16 + threadIdx.x];
+      scr[SCR_SHRINK_P + threadIdx.x] = rms_shrink(u, cols, a.eps);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    if (!live[slot]) continue;
+    if (slot > 0) load(slot, 0);
+    compute(slot, 0);
+    for (int i0 = B; i0 < count; i0 += B) {
+      load(slot, i0);
+      compute(slot, i0);
+    }
+  }
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    if (slot >= n_slots) continue;
+    const float s_ = warp_sum(ssq[slot]);
+    const float m_ = warp_max(amax[slot]);
+    if (l32 == 0 && jj[slot] < K) {
+      scr[SCR_SSQ + jj[slot] * 8 + part_] = s_;
+      scr[SCR_AMAX + jj[slot] * 8 + part_] = m_;
     }
   }
   __syncthreads();
   if (threadIdx.x < 16 && (int)threadIdx.x < K) {
     const int j = threadIdx.x;
-    float ssq = 0.0f, amax = 0.0f;
+    float s_ = 0.0f, m_ = 0.0f;
     for (int q = 0; q < wpl; ++q) {
-      ssq += scr[SCR_SSQ + j * 8 + q];
-      amax = fmaxf(amax, scr[SCR_AMAX + j * 8 + q]);
+      s_ += scr[SCR_SSQ + j * 8 + q];
+      m_ = fmaxf(m_, scr[SCR_AMAX + j * 8 + q]);
     }
-    const float sc = lane_scale(amax);
-    const float shrink = (PRO == PRO_NORM || PRO == PRO_RESID_NORM) ? rms_shrink(ssq, cols, a.eps) : 1.0f;
+    const float sc = lane_scale(m_);
+    const float shrink = NRM ? rms_shrink(s_, cols, a.eps) : 1.0f;
     scr[SCR_SCALE + j] = sc;
     scr[SCR_FACTOR + j] = shrink * (1.0f / sc);
   }
   __syncthreads();
-  for (int slot = 0; slot < n_slots; ++slot) {
-    const int j = wpl > 1 ? warp / wpl : warp + slot * GEMV_WARPS;
-    const int part = wpl > 1 ? warp % wpl : 0;
-    if (j >= K) continue;
-    const int lo = (n4 * part) / wpl, hi = (n4 * (part + 1)) / wpl;
-    const float sc = scr[SCR_SCALE + j];
-    for (int c4 = lo + l32; c4 < hi; c4 += 32) {
-      stage_seal(stage, j, c4 * 4, sc, NT);
-      stage_seal(stage, j, c4 * 4 + 2, sc, NT);
+  // second pass over the same words: scaled, split into hi/lo f16 pairs
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    if (!live[slot]) continue;
+    const float sc = scr[SCR_SCALE + jj[slot]];
+#pragma unroll 4
+    for (int i = 0; i < count; ++i) {
+      const int o = step * i;
+      seal_words(stage, wh0[slot] + o, wl0[slot] + o, sc);
+      seal_words(stage, wh2[slot] + o, wl2[slot] + o, sc);
     }
   }
   __syncthreads();
 }
 
-// Accumulates one 64-column chunk of one row block into tot[NT][4].
-template <int NT>
-__device__ __forceinline__ void chunk_product(const uint4 &w, const uint2 &s, const uint4 (&b)[NT][4],
-                                              float (&tot)[NT][4]) {
-  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+// The four A fragments of one chunk (two 32-column groups, two 16-column
+// products each) and the group scales of rows g and g + 8.
+struct ChunkA {
+  uint32_t a0[4], a1[4], a2[4], a3[4];
+  float sg0, sg1, sg8_0, sg8_1;
+};
+
+__device__ __forceinline__ void chunk_a(const uint4 &w, const uint2 &s, ChunkA &A) {
   __half2 s01 = *reinterpret_cast<const __half2 *>(&s.x);
   __half2 s23 = *reinterpret_cast<const __half2 *>(&s.y);
-  float sg0 = __low2float(s01), sg8_0 = __high2float(s01);
-  float sg1 = __low2float(s23), sg8_1 = __high2float(s23);
-  uint32_t a0[4], a1[4], a2[4], a3[4];
-  dequant_i4(w.x, a0);
-  dequant_i4(w.y, a1);
-  dequant_i4(w.z, a2);
-  dequant_i4(w.w, a3);
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    // b[nt][0..1]: hi fragments of products 0..3, b[nt][2..3]: lo fragments
-    float g0[4], g1[4];
-    mma16816(g0, a0, b[nt][0].x, b[nt][0].y, zero);
-    mma16816(g0, a1, b[nt][0].z, b[nt][0].w, g0);
-    mma16816(g0, a0, b[nt][2].x, b[nt][2].y, g0);
-    mma16816(g0, a1, b[nt][2].z, b[nt][2].w, g0);
-    mma16816(g1, a2, b[nt][1].x, b[nt][1].y, zero);
-    mma16816(g1, a3, b[nt][1].z, b[nt][1].w, g1);
-    mma16816(g1, a2, b[nt][3].x, b[nt][3].y, g1);
-    mma16816(g1, a3, b[nt][3].z, b[nt][3].w, g1);
-    tot[nt][0] += sg0 * g0[0] + sg1 * g1[0];
-    tot[nt][1] += sg0 * g0[1] + sg1 * g1[1];
-    tot[nt][2] += sg8_0 * g0[2] + sg8_1 * g1[2];
-    tot[nt][3] += sg8_0 * g0[3] + sg8_1 * g1[3];
-  }
+  A.sg0 = __low2float(s01);
+  A.sg8_0 = __high2float(s01);
+  A.sg1 = __low2float(s23);
+  A.sg8_1 = __high2float(s23);
+  dequant_i4(w.x, A.a0);
+  dequant_i4(w.y, A.a1);
+  dequant_i4(w.z, A.a2);
+  dequant_i4(w.w, A.a3);
 }
 
-template <int NT>
-__device__ __forceinline__ void load_b(const uint32_t *stage, int cc, int lane32, uint4 (&b)[NT][4]) {
+// One chunk against one 8-column B tile (the four products' b0, b1 in two
+// uint4): acc[i] += sg(group 0) * g0[i] + sg(group 1) * g1[i], rows g (i < 2)
+// and g + 8, in one fixed order of fused multiply-adds.
+__device__ __forceinline__ void chunk_tile(const ChunkA &A, const uint4 &b01, const uint4 &b23, float *acc) {
+  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+  float g0[4], g1[4];
+  mma16816(g0, A.a0, b01.x, b01.y, zero);
+  mma16816(g0, A.a1, b01.z, b01.w, g0);
+  mma16816(g1, A.a2, b23.x, b23.y, zero);
+  mma16816(g1, A.a3, b23.z, b23.w, g1);
+  acc[0] = fmaf(A.sg1, g1[0], fmaf(A.sg0, g0[0], acc[0]));
+  acc[1] = fmaf(A.sg1, g1[1], fmaf(A.sg0, g0[1], acc[1]));
+  acc[2] = fmaf(A.sg8_1, g1[2], fmaf(A.sg8_0, g0[2], acc[2]));
+  acc[3] = fmaf(A.sg8_1, g1[3], fmaf(A.sg8_0, g0[3], acc[3]));
+}
+
+// One chunk of one row block into the thread's accumulators: PACK one tile
+// (hi and lo in its columns), NT per 8-lane tile a hi and a lo accumulator.
+template <int MODE>
+__device__ __forceinline__ void chunk_product(const uint4 &w, const uint2 &s, const uint32_t *stage_chunk, int lane32,
+                                              float *acc) {
+  ChunkA A;
+  chunk_a(w, s, A);
+  if (MODE == MODE_PACK) {
+    const uint4 *p = reinterpret_cast<const uint4 *>(stage_chunk + lane32 * 8);
+    chunk_tile(A, p[0], p[1], acc);
+  } else {
+    constexpr int NT = MODE == MODE_NT2 ? 2 : 1;
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    const uint4 *p = reinterpret_cast<const uint4 *>(stage + ((cc * NT + nt) * 32 + lane32) * 16);
-    b[nt][0] = p[0];
-    b[nt][1] = p[1];
-    b[nt][2] = p[2];
-    b[nt][3] = p[3];
+    for (int nt = 0; nt < NT; ++nt) {
+      const uint4 *p = reinterpret_cast<const uint4 *>(stage_chunk + (nt * 32 + lane32) * 16);
+      chunk_tile(A, p[0], p[1], acc + nt * 8);      // hi
+      chunk_tile(A, p[2], p[3], acc + nt * 8 + 4);  // lo
+    }
   }
 }
 

@@ -57,30 +57,77 @@ __global__ void repack_kernel(const uint8_t *code, size_t row_stride, const uint
 
 // ---------------------------------------------------------------------------
 // the skinny GEMM
-template <int NT, int PAIR, int PRO, int EPI>
+//
+// Work: a unit is one row block (a gate/up pair for PAIR planes).  The S
+// warps of a group share a unit, each taking a fixed slice of its chunks
+// (S is a property of the plane, so the summation order never depends on the
+// lane count); groups are spread over (block, group) slots round robin.
+// Each warp streams its own pieces (runs of chunks of one unit) through a
+// private ring of `depth` shared-memory slots filled by bulk copies that lane
+// 0 issues; the first pieces are in flight before the kernel waits for the
+// kernel ahead of it and before the activation prologue runs.
+template <int MODE, int PAIR, int PRO, int EPI>
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+  constexpr int NT = MODE == MODE_NT2 ? 2 : 1;
+  constexpr int H = PAIR + 1;
+  constexpr int ACC = MODE == MODE_PACK ? 4 : 8 * NT;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   uint32_t *stage = reinterpret_cast<uint32_t *>(smem_raw);
-  const size_t stage_bytes = gemv_stage_bytes(a.pl.n_cc, NT);
-  float *scr = reinterpret_cast<float *>(smem_raw + stage_bytes);  // prologue scratch
-  float *red = scr + SCR_FLOATS;                                     // [8 warps][32][8*NT]
-
-  gemv_prologue<PRO>(a, stage, scr, NT);
+  float *scr = reinterpret_cast<float *>(smem_raw + gemv_stage_bytes(a.pl.n_cc, MODE));
+  float *red = reinterpret_cast<float *>(smem_raw + a.off_red);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem_raw + a.off_bars);
+  unsigned char *ring = smem_raw + a.off_ring;
 
   const int warp = threadIdx.x >> 5, lane32 = threadIdx.x & 31;
   const int g = lane32 >> 2, t = lane32 & 3;
-  const int S = a.split;
-  const int per_iter = GEMV_WARPS / S;  // row-block units a CTA takes at once
+  const int S = a.split, G = GEMV_WARPS / S, grp = warp / S, slice = warp % S;
+  const int n_cc = a.pl.n_cc;
+  const int c_lo = (n_cc * slice) / S, c_hi = (n_cc * (slice + 1)) / S;
   const int n_units = PAIR ? a.pl.n_rb / 2 : a.pl.n_rb;
-  const int my_unit_off = warp / S, my_slice = warp % S;
-  const int c_lo = (a.pl.n_cc * my_slice) / S, c_hi = (a.pl.n_cc * (my_slice + 1)) / S;
+  const int Q = gridDim.x * G, q = blockIdx.x * G + grp;
+  const int my_units = q < n_units ? (n_units - q + Q - 1) / Q : 0;
+  const int P = a.piece, D = a.depth;
+  const int np = (c_hi - c_lo + P - 1) / P;  // pieces a unit
+  const int n_pieces = my_units * np;
+  const int slot_bytes = H * P * GEMV_PIECE_BYTES;
+  uint64_t *mb = bars + warp * D;
+  unsigned char *mr = ring + (size_t)warp * D * slot_bytes;
 
-  // the epilogue factor of the two lanes each accumulator column holds
+  pdl_release();
+  const uint64_t policy = l2_evict_first();
+  // piece n of this warp: unit q + (n / np) Q, chunks from c_lo + (n % np) P
+  auto issue = [&](int n) {
+    const int unit = q + (n / np) * Q, c0 = c_lo + (n % np) * P;
+    const int nc = min(P, c_hi - c0);
+    uint64_t *bar = &mb[n % D];
+    unsigned char *dst = mr + (size_t)(n % D) * slot_bytes;
+    mbar_expect(bar, (uint32_t)(H * nc * GEMV_PIECE_BYTES));
+#pragma unroll
+    for (int h = 0; h < H; ++h) {
+      const size_t tile = (size_t)(PAIR ? 2 * unit + h : unit) * n_cc + c0;
+      bulk_load(dst + h * P * 512, a.pl.tiles + tile * 32, (uint32_t)(nc * 512), bar, policy);
+      bulk_load(dst + H * P * 512 + h * P * 64, a.pl.scales + tile * 8, (uint32_t)(nc * 64), bar, policy);
+    }
+  };
+  if (lane32 == 0) {
+    for (int d = 0; d < D; ++d) mbar_init(&mb[d], 1);
+    mbar_init_fence();
+    for (int n = 0; n < D && n < n_pieces; ++n) issue(n);
+  }
+  __syncwarp();
+
+  pdl_wait();
+  gemv_prologue<PRO, MODE>(a, stage, scr);
+
+  // the epilogue factor of the lanes each accumulator column holds
   float sh[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int k = 0; k < 2; ++k) sh[nt][k] = scr[SCR_FACTOR + nt * 8 + 2 * t + k];
+    for (int k = 0; k < 2; ++k) {
+      const int ln = MODE == MODE_PACK ? (2 * t + k) & 3 : nt * 8 + 2 * t + k;
+      sh[nt][k] = scr[SCR_FACTOR + ln];
+    }
 
   // EPI_LOGITS running argmax, EPI_STORE running sum of squares, per (nt, lane parity)
   float best_v[NT][2];
@@ -93,104 +140,96 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
     ssq[nt][0] = ssq[nt][1] = 0.0f;
   }
 
-  for (int base = blockIdx.x * per_iter; base < n_units; base += gridDim.x * per_iter) {
-    const int unit = base + my_unit_off;
-    const bool active = unit < n_units;
-    float tot[PAIR + 1][NT][4];
+  bool failed = false;
+  int n = 0;
+  for (int u = 0; u < my_units; ++u) {
+    const int unit = q + u * Q;
+    float acc[H][ACC];
 #pragma unroll
-    for (int h = 0; h <= PAIR; ++h)
+    for (int h = 0; h < H; ++h)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) tot[h][nt][i] = 0.0f;
+      for (int i = 0; i < ACC; ++i) acc[h][i] = 0.0f;
 
-    if (active) {
-      constexpr int D = 4;  // chunks in flight per warp
-      uint4 wbuf[PAIR + 1][D];
-      uint2 sbuf[PAIR + 1][D];
-      const int rb0 = PAIR ? unit * 2 : unit;
+    for (int k = 0; k < np; ++k, ++n) {
+      const int c0 = c_lo + k * P, nc = min(P, c_hi - c0);
+      const int d = n % D;
+      if (!mbar_wait(&mb[d], (uint32_t)((n / D) & 1), failed ? 1 : (1 << 22))) {
+        if (!failed && lane32 == 0) atomicOr(a.err, 1);
+        failed = true;
+      }
+      const unsigned char *src = mr + (size_t)d * slot_bytes;
+      const uint4 *wt = reinterpret_cast<const uint4 *>(src);
+      const uint2 *ws = reinterpret_cast<const uint2 *>(src + H * P * 512);
+#pragma unroll 2
+      for (int c = 0; c < nc; ++c) {
+        const uint32_t *sc = stage + (size_t)(c0 + c) * stage_chunk_words(MODE);
 #pragma unroll
-      for (int d = 0; d < D; ++d)
-        if (c_lo + d < c_hi)
-#pragma unroll
-          for (int h = 0; h <= PAIR; ++h) {
-            long tile = (long)(rb0 + h) * a.pl.n_cc + c_lo + d;
-            wbuf[h][d] = ld_stream(a.pl.tiles + tile * 32 + lane32);
-            sbuf[h][d] = ld_stream2(a.pl.scales + tile * 8 + g);
-          }
-      for (int c = c_lo; c < c_hi; c += D) {
-#pragma unroll
-        for (int d = 0; d < D; ++d) {
-          if (c + d < c_hi) {
-            uint4 w[PAIR + 1];
-            uint2 s[PAIR + 1];
-#pragma unroll
-            for (int h = 0; h <= PAIR; ++h) {
-              w[h] = wbuf[h][d];
-              s[h] = sbuf[h][d];
-            }
-            const int cn = c + d + D;
-            if (cn < c_hi)
-#pragma unroll
-              for (int h = 0; h <= PAIR; ++h) {
-                long tile = (long)(rb0 + h) * a.pl.n_cc + cn;
-                wbuf[h][d] = ld_stream(a.pl.tiles + tile * 32 + lane32);
-                sbuf[h][d] = ld_stream2(a.pl.scales + tile * 8 + g);
-              }
-            uint4 b[NT][4];
-            load_b<NT>(stage, c + d, lane32, b);
-#pragma unroll
-            for (int h = 0; h <= PAIR; ++h) chunk_product<NT>(w[h], s[h], b, tot[h]);
-          }
-        }
+        for (int h = 0; h < H; ++h)
+          chunk_product<MODE>(wt[h * P * 32 + c * 32 + lane32], ws[h * P * 8 + c * 8 + g], sc, lane32, acc[h]);
+      }
+      __syncwarp();
+      if (lane32 == 0 && n + D < n_pieces && !failed) {
+        fence_async_smem();
+        issue(n + D);
       }
     }
 
-    // combine the S warps that shared this unit, in a fixed order
+    // the S warps of the group add their slices in a fixed order
     if (S > 1) {
-      float *mine = red + (warp * 32 + lane32) * (8 * NT);
+      float *mine = red + (size_t)threadIdx.x * (H * ACC);
 #pragma unroll
-      for (int h = 0; h <= PAIR; ++h)
+      for (int h = 0; h < H; ++h)
+#pragma unroll
+        for (int i = 0; i < ACC; ++i) mine[h * ACC + i] = acc[h][i];
+      named_sync(1 + grp, S * 32);
+      if (slice == 0) {
+        for (int o = 1; o < S; ++o) {
+          const float *other = red + (size_t)(threadIdx.x + o * 32) * (H * ACC);
+#pragma unroll
+          for (int h = 0; h < H; ++h)
+#pragma unroll
+            for (int i = 0; i < ACC; ++i) acc[h][i] += other[h * ACC + i];
+        }
+      }
+      named_sync(1 + grp, S * 32);
+    }
+
+    if (slice == 0) {
+      // hi + lo for each output: PACK adds the lo columns (threads t + 2)
+      float v[H][NT][4];
+#pragma unroll
+      for (int h = 0; h < H; ++h)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) mine[(h * NT + nt) * 4 + i] = tot[h][nt][i];
-      __syncthreads();
-      if (my_slice == 0) {
-        for (int o = 1; o < S; ++o) {
-          const float *other = red + ((warp + o) * 32 + lane32) * (8 * NT);
-#pragma unroll
-          for (int h = 0; h <= PAIR; ++h)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-              for (int i = 0; i < 4; ++i) tot[h][nt][i] += other[(h * NT + nt) * 4 + i];
-        }
-      }
-      __syncthreads();
-    }
-
-    if (active && my_slice == 0) {
+          for (int i = 0; i < 4; ++i) {
+            if (MODE == MODE_PACK) {
+              const float lo = __shfl_xor_sync(0xffffffffu, acc[h][i], 2);
+              v[h][nt][i] = acc[h][i] + lo;
+            } else {
+              v[h][nt][i] = acc[h][nt * 8 + i] + acc[h][nt * 8 + 4 + i];
+            }
+          }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int row = unit * 16 + g + (i >= 2 ? 8 : 0);
           const int k = i & 1;
-          const int ln = nt * 8 + 2 * t + k;
+          const int ln = MODE == MODE_PACK ? 2 * t + k : nt * 8 + 2 * t + k;
+          if (MODE == MODE_PACK && t >= 2) continue;
           if (row >= a.pl.rows || ln >= a.lanes) continue;
-          float v = tot[0][nt][i] * sh[nt][k];
+          const float x = v[0][nt][i] * sh[nt][k];
           if (EPI == EPI_STORE) {
-            float o = v * a.out_scale;
+            const float o = x * a.out_scale;
             a.out[(size_t)ln * a.out_stride + row] = o;
             ssq[nt][k] += o * o;
           } else if (EPI == EPI_GELU_PAIR) {
-            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(v) * (tot[PAIR][nt][i] * sh[nt][k]);
+            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(x) * (v[PAIR][nt][i] * sh[nt][k]);
           } else if (EPI == EPI_GELU_MUL) {
-            a.out[(size_t)ln * a.out_stride + row] =
-                gelu_tanh(v) * a.aux[(size_t)ln * a.aux_stride + row];
+            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(x) * a.aux[(size_t)ln * a.aux_stride + row];
           } else {  // EPI_LOGITS
-            float cv = a.cap > 0.0f ? logit_cap(v, a.cap) : v;
+            const float cv = a.cap > 0.0f ? logit_cap(x, a.cap) : x;
             a.out[(size_t)ln * a.out_stride + row] = cv;
             if (cv > best_v[nt][k] || (cv == best_v[nt][k] && row < best_i[nt][k])) {
               best_v[nt][k] = cv;
@@ -212,7 +251,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         float v = ssq[nt][k];
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (g == 0) red[warp * 16 + nt * 8 + 2 * t + k] = v;
+        const int ln = nt * 8 + 2 * t + k;
+        if (g == 0) red[warp * 16 + ln] = (MODE == MODE_PACK && t >= 2) ? 0.0f : v;
       }
     __syncthreads();
     if (threadIdx.x < NT * 8) {
@@ -264,7 +304,6 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
     }
   }
 }
-
 // ---------------------------------------------------------------------------
 // embedding rows (app_core.c:11863-11874, :11886-11891)
 __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embed, int hidden,
@@ -845,22 +884,86 @@ __global__ void desk_rope_kernel(float *x, int head, const float *cs, const floa
 // ---------------------------------------------------------------------------
 // launchers
 
-static size_t gemv_smem_nt(const GemvArgs &a, int NT) {
-  size_t red = (size_t)GEMV_WARPS * 32 * 8 * NT * 4;  // the split reduction, and the ssq/argmax merges
-  return gemv_stage_bytes(a.pl.n_cc, NT) + SCR_FLOATS * 4 + red;
+// Whether launches from this thread may overlap the kernel ahead of them
+// (programmatic dependent launch); the session turns it on while it records
+// a pass, whose kernels all wait for their predecessor before touching its
+// results.
+static thread_local int g_pdl = 0;
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-template <int NT, int PAIR, int PRO, int EPI>
-static cudaError_t launch_gemv_t(const GemvArgs &a, int grid, cudaStream_t st) {
-  size_t smem = gemv_smem_nt(a, NT);
-  gemv_kernel<NT, PAIR, PRO, EPI><<<grid, GEMV_THREADS, smem, st>>>(a);
-  return cudaGetLastError();
+static size_t align128(size_t x) { return (x + 127) & ~(size_t)127; }
+
+// Shared memory of one launch: staged activations | scratch | reduction
+// space | ring barriers | ring slots.
+struct GemvLayout {
+  size_t red, bars, ring, total;
+};
+
+static GemvLayout gemv_layout(const GemvArgs &a, int pair, int P, int D) {
+  const int MODE = gemv_mode(a.lanes), H = pair + 1;
+  GemvLayout L;
+  L.red = align128(gemv_stage_bytes(a.pl.n_cc, MODE) + SCR_FLOATS * 4);
+  size_t red_floats = a.split > 1 ? (size_t)GEMV_THREADS * H * gemv_acc_floats(MODE) : 0;
+  if (red_floats < (size_t)GEMV_WARPS * 16) red_floats = (size_t)GEMV_WARPS * 16;
+  L.bars = align128(L.red + red_floats * 4);
+  L.ring = align128(L.bars + (size_t)GEMV_WARPS * D * 8);
+  L.total = L.ring + (size_t)GEMV_WARPS * D * H * P * GEMV_PIECE_BYTES;
+  return L;
 }
 
-template <int NT, int PAIR>
-static cudaError_t launch_gemv_pe(const GemvArgs &a, int pro, int epi, int grid, cudaStream_t st) {
+// Pieces and depth for a launch of `grid` blocks within `smem_limit`: every
+// piece a warp will take in flight at once when they fit (one piece a unit),
+// else four pieces in flight of as many chunks as fit.  Fills the layout
+// fields of `a`; false when not even one chunk a warp fits.
+static bool gemv_fit(GemvArgs &a, int pair, int grid, size_t smem_limit, size_t *smem) {
+  const int H = pair + 1, S = a.split, G = GEMV_WARPS / S;
+  const int slen = (a.pl.n_cc + S - 1) / S;
+  const int n_units = pair ? a.pl.n_rb / 2 : a.pl.n_rb;
+  const int per_slot = (n_units + grid * G - 1) / (grid * G);
+  const GemvLayout base = gemv_layout(a, pair, 0, GEMV_MAX_DEPTH);
+  if (base.ring >= smem_limit) return false;
+  const long per_warp = (long)(smem_limit - base.ring) / (GEMV_WARPS * H * GEMV_PIECE_BYTES);
+  if (per_warp < 1) return false;
+  int P, D;
+  if ((long)per_slot * slen <= per_warp && per_slot <= GEMV_MAX_DEPTH) {
+    P = slen;
+    D = per_slot > 0 ? per_slot : 1;
+  } else {
+    D = per_warp < 4 ? (int)per_warp : 4;
+    P = (int)(per_warp / D);
+    if (P > slen) P = slen;
+    const int pieces = (slen + P - 1) / P;
+    P = (slen + pieces - 1) / pieces;
+  }
+  a.piece = P;
+  a.depth = D;
+  const GemvLayout L = gemv_layout(a, pair, P, D);
+  a.off_red = (int)L.red;
+  a.off_bars = (int)L.bars;
+  a.off_ring = (int)L.ring;
+  *smem = L.total;
+  return L.total <= smem_limit;
+}
+
+template <int MODE, int PAIR>
+static cudaError_t launch_gemv_pe(const GemvArgs &a, int pro, int epi, int grid, size_t smem, cudaStream_t st) {
 #define IGC_CASE(P, E) \
-  if (pro == P && epi == E) return launch_gemv_t<NT, PAIR, P, E>(a, grid, st);
+  if (pro == P && epi == E) return launch_k(gemv_kernel<MODE, PAIR, P, E>, dim3(grid), dim3(GEMV_THREADS), smem, st, a);
   if constexpr (PAIR) {
     IGC_CASE(PRO_RESID_NORM, EPI_GELU_PAIR)
     IGC_CASE(PRO_NORM, EPI_GELU_PAIR)
@@ -878,7 +981,6 @@ static cudaError_t launch_gemv_pe(const GemvArgs &a, int pro, int epi, int grid,
   return cudaErrorInvalidValue;
 }
 
-
 // The opt-in limit covers static and dynamic shared memory together, so each
 // kernel may ask for the limit less its own static part.
 template <typename F>
@@ -890,16 +992,11 @@ static cudaError_t allow_smem_fn(F *fn, int bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn > 0 ? dyn : 0);
 }
 
-template <int NT, int PAIR, int PRO, int EPI>
-static cudaError_t allow_smem_t(int bytes) {
-  return allow_smem_fn(gemv_kernel<NT, PAIR, PRO, EPI>, bytes);
-}
-
-template <int NT>
-static cudaError_t allow_smem_nt(int bytes) {
+template <int MODE>
+static cudaError_t allow_smem_mode(int bytes) {
   cudaError_t e = cudaSuccess;
 #define IGC_ALLOW(PAIR, P, E) \
-  if (e == cudaSuccess) e = allow_smem_t<NT, PAIR, P, E>(bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(gemv_kernel<MODE, PAIR, P, E>, bytes);
   IGC_ALLOW(1, PRO_RESID_NORM, EPI_GELU_PAIR)
   IGC_ALLOW(1, PRO_NORM, EPI_GELU_PAIR)
   IGC_ALLOW(1, PRO_F32, EPI_GELU_PAIR)
@@ -928,8 +1025,9 @@ cudaError_t igc_kernels_configure(int bytes) {
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return e;
   if (bytes > optin) bytes = optin;
-  e = allow_smem_nt<1>(bytes);
-  if (e == cudaSuccess) e = allow_smem_nt<2>(bytes);
+  e = allow_smem_mode<MODE_PACK>(bytes);
+  if (e == cudaSuccess) e = allow_smem_mode<MODE_NT1>(bytes);
+  if (e == cudaSuccess) e = allow_smem_mode<MODE_NT2>(bytes);
   if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<1, true>, bytes);
   if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<2, true>, bytes);
   if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<4, true>, bytes);
@@ -952,13 +1050,28 @@ cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint
   return cudaGetLastError();
 }
 
-cudaError_t igc_launch_gemv(const GemvArgs *a, int pair, int pro, int epi, int grid, cudaStream_t st) {
-  int NT = (a->lanes + 7) / 8;
-  if (NT == 1) return pair ? launch_gemv_pe<1, 1>(*a, pro, epi, grid, st) : launch_gemv_pe<1, 0>(*a, pro, epi, grid, st);
-  return pair ? launch_gemv_pe<2, 1>(*a, pro, epi, grid, st) : launch_gemv_pe<2, 0>(*a, pro, epi, grid, st);
+void igc_kernels_pdl(int on) { g_pdl = on; }
+
+cudaError_t igc_launch_gemv(GemvArgs *a, int pair, int pro, int epi, int grid, size_t smem_limit, cudaStream_t st) {
+  size_t smem = 0;
+  if (!gemv_fit(*a, pair, grid, smem_limit, &smem)) return cudaErrorInvalidValue;
+  switch (gemv_mode(a->lanes)) {
+    case MODE_PACK:
+      return pair ? launch_gemv_pe<MODE_PACK, 1>(*a, pro, epi, grid, smem, st)
+                  : launch_gemv_pe<MODE_PACK, 0>(*a, pro, epi, grid, smem, st);
+    case MODE_NT1:
+      return pair ? launch_gemv_pe<MODE_NT1, 1>(*a, pro, epi, grid, smem, st)
+                  : launch_gemv_pe<MODE_NT1, 0>(*a, pro, epi, grid, smem, st);
+    default:
+      return pair ? launch_gemv_pe<MODE_NT2, 1>(*a, pro, epi, grid, smem, st)
+                  : launch_gemv_pe<MODE_NT2, 0>(*a, pro, epi, grid, smem, st);
+  }
 }
 
-size_t igc_gemv_smem(const GemvArgs *a) { return gemv_smem_nt(*a, (a->lanes + 7) / 8); }
+// The smallest ring: one chunk a warp, with room for the deepest barriers.
+size_t igc_gemv_smem_min(const GemvArgs *a, int pair) {
+  return gemv_layout(*a, pair, 0, GEMV_MAX_DEPTH).ring + (size_t)GEMV_WARPS * (pair + 1) * GEMV_PIECE_BYTES;
+}
 
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,

@@ -14,8 +14,16 @@ cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint
                               int rows, int cols, int n_rb, int n_cc, int out_mul, int out_add, uint4 *tiles,
                               uint2 *scales, cudaStream_t st);
 
-cudaError_t igc_launch_gemv(const igc::GemvArgs *a, int pair, int pro, int epi, int grid, cudaStream_t st);
-size_t igc_gemv_smem(const igc::GemvArgs *a);
+// Launches from the calling thread may overlap the kernel ahead of them
+// (programmatic dependent launch) while `on` is set.
+void igc_kernels_pdl(int on);
+// Picks the weight ring for `grid` blocks within `smem_limit` bytes of shared
+// memory (filling a->piece, a->depth and the layout offsets) and launches;
+// cudaErrorInvalidValue when the lanes' staging leaves no room for it.
+cudaError_t igc_launch_gemv(igc::GemvArgs *a, int pair, int pro, int epi, int grid, size_t smem_limit,
+                            cudaStream_t st);
+// Shared memory the smallest ring needs.
+size_t igc_gemv_smem_min(const igc::GemvArgs *a, int pair);
 
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,

@@ -513,7 +513,7 @@ struct Binder {
   // are too few row blocks to keep every warp busy.
   void plan(DevPlane &p) {
     int units = p.pair ? p.n_rb / 2 : p.n_rb;
-    size_t stage = gemv_stage_bytes(p.n_cc, 1) + 8 * 1024;
+    size_t stage = gemv_stage_bytes(p.n_cc, MODE_NT1) + 8 * 1024;
     int per_sm = (int)((size_t)m->smem_limit / stage);
     if (per_sm > 2) per_sm = 2;
     if (per_sm < 1) per_sm = 1;
@@ -523,6 +523,9 @@ struct Binder {
     p.split = S;
     int per_iter = GEMV_WARPS / S;
     int need = (units + per_iter - 1) / per_iter;
+    // a plane with many units a warp (the output head) streams through a
+    // deep ring: one block an SM, with the shared memory to itself
+    if (S == 1 && units > 2 * cap * GEMV_WARPS) cap = m->sm_count;
     p.grid = need < cap ? need : cap;
     if (p.grid < 1) p.grid = 1;
   }
@@ -777,7 +780,8 @@ struct igc_session {
   uint64_t draw_state = 0x2545F4914F6CDD1DULL;
   std::vector<float *> kc, vc;
   int *d_io = nullptr;  // [0] position, [1..16] ids
-  int32_t *d_top = nullptr;
+  int32_t *d_top = nullptr;  // [0..16) argmax ids, [16] the kernels' error word (d_err)
+  int *d_err = nullptr;
   float *x0 = nullptr, *xa = nullptr, *xb = nullptr, *seed = nullptr, *ple_raw = nullptr, *ple = nullptr;
   float *qkv = nullptr, *attn = nullptr, *obuf = nullptr, *act = nullptr, *dbuf = nullptr, *pa = nullptr,
         *pp = nullptr, *logits = nullptr;
@@ -795,6 +799,7 @@ struct igc_session {
   int chunk_len = 32;   // attention chunk length, fixed for the session
   int max_chunks = 0;   // chunks the longest span can cover
   int use_graphs = 1;
+  int use_pdl = 1;
   cudaGraphExec_t graph[IGC_LANE_LIMIT + 1][2] = {};
   double serve_seconds = 0.0;
   size_t serve_tokens = 0;
@@ -856,7 +861,11 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   }
   s->arg_parts = m->sm_count * 4;
   if (c == IGC_OKAY) c = s->alloc(&s->d_io, 1 + K);
-  if (c == IGC_OKAY) c = s->alloc(&s->d_top, K);
+  if (c == IGC_OKAY) c = s->alloc(&s->d_top, K + 1);
+  if (c == IGC_OKAY) {
+    s->d_err = s->d_top + K;
+    CK(cudaMemsetAsync(s->d_top, 0, sizeof(int32_t) * (K + 1), s->st));
+  }
   if (c == IGC_OKAY) c = s->alloc(&s->x0, (size_t)K * H);
   if (c == IGC_OKAY) c = s->alloc(&s->xa, (size_t)K * H);
   if (c == IGC_OKAY) c = s->alloc(&s->xb, (size_t)K * H);
@@ -892,17 +901,19 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (c != IGC_OKAY) return c;
   {
     void *h = nullptr;
-    size_t bytes = sizeof(int32_t) * (size_t)(1 + K) + sizeof(int32_t) * K + (sizeof(float) + sizeof(int)) * K * 256;
+    size_t bytes = sizeof(int32_t) * (size_t)(1 + K) + sizeof(int32_t) * (K + 1) + (sizeof(float) + sizeof(int)) * K * 256;
     CK(cudaMallocHost(&h, bytes));
     s->h_io = (int32_t *)h;
     s->h_top = s->h_io + 1 + K;
-    s->h_top_v = (float *)(s->h_top + K);
+    s->h_top_v = (float *)(s->h_top + K + 1);
     s->h_top_i = (int *)(s->h_top_v + K * 256);
   }
   CK(cudaStreamSynchronize(s->st));
   s->echo.reserve((size_t)m->window_limit);
   const char *g = getenv("IGC_NO_GRAPHS");
   s->use_graphs = !(g && g[0] == '1');
+  const char *np = getenv("IGC_NO_PDL");
+  s->use_pdl = !(np && np[0] == '1');
   *out = s.release();
   return IGC_OKAY;
 }
@@ -963,6 +974,7 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   if (p_ssq) {
     a.p_ssq = p_ssq->buf;
     a.p_parts = p_ssq->parts;
+    if (a.p_parts > GEMV_PART_LIMIT) return IGC_FAIL_SUPPORT;  // more partials than the prologue reads
   }
   if (out_ssq) {
     a.out_ssq = out_ssq->buf;
@@ -988,8 +1000,10 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   a.cap = s->m->softcap;
   a.part_val = s->arg_val;
   a.part_idx = s->arg_idx;
-  if (igc_gemv_smem(&a) <= (size_t)s->m->smem_limit) {
-    CKL(igc_launch_gemv(&a, pl.pair ? 1 : 0, pro, epi, pl.grid, s->st));
+  a.err = s->d_err;
+  const int pair = pl.pair ? 1 : 0;
+  if (igc_gemv_smem_min(&a, pair) <= (size_t)s->m->smem_limit) {
+    CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st));
     return IGC_OKAY;
   }
   // Too wide to stage sixteen lanes at once (the 6144-column down
@@ -1004,16 +1018,33 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
     b.out = out + (size_t)j0 * out_stride;
     b.aux = aux ? aux + (size_t)j0 * aux_stride : nullptr;
     b.out_ssq = a.out_ssq ? a.out_ssq + j0 : nullptr;
-    if (igc_gemv_smem(&b) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
-    CKL(igc_launch_gemv(&b, pl.pair ? 1 : 0, pro, epi, pl.grid, s->st));
+    if (igc_gemv_smem_min(&b, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
+    CKL(igc_launch_gemv(&b, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st));
   }
   return IGC_OKAY;
 }
 
+// After a synchronised pass: a kernel that gave up waiting for its own bulk
+// copies left the error word set (its results are not to be trusted).
+static int check_err(igc_session *s) {
+  if (s->h_top[IGC_LANE_LIMIT] == 0) return IGC_OKAY;
+  s->h_top[IGC_LANE_LIMIT] = 0;
+  cudaMemsetAsync(s->d_err, 0, sizeof(int), s->st);
+  cudaStreamSynchronize(s->st);
+  g_last_error = "a kernel gave up waiting for its weight copies";
+  return IGC_FAIL_DEVICE;
+}
+
 // One pass of K lanes at the position in d_io[0], ids in d_io[1..K]
 // (app_core.c:11843 session_pass).  want: 0 no head, 1 head and argmax.
+struct PdlScope {  // kernels of a pass may start while the one ahead finishes
+  explicit PdlScope(bool on) { igc_kernels_pdl(on ? 1 : 0); }
+  ~PdlScope() { igc_kernels_pdl(0); }
+};
+
 static int enqueue_pass(igc_session *s, int K, int want) {
   igc_model *m = s->m;
+  PdlScope pdl(s->use_pdl != 0);
   const int H = m->hidden, PS = m->layers * m->ple_dim;
   const int *d_p0 = s->d_io;
   const int32_t *d_ids = s->d_io + 1;
@@ -1140,8 +1171,9 @@ static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
     int c = enqueue_pass(s, K, want);
     if (c != IGC_OKAY) return c;
   }
-  if (want) CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * (size_t)K, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * (IGC_LANE_LIMIT + 1), cudaMemcpyDeviceToHost, s->st));
   CK(cudaStreamSynchronize(s->st));
+  if (int ce = check_err(s)) return ce;
   s->fill += K;
   for (int j = 0; j < K; ++j)
     if ((int)s->echo.size() < m->window_limit) s->echo.push_back(ids[j]);
@@ -1511,8 +1543,9 @@ extern "C" int igc_session_bench(igc_session *s, const int32_t *blocks, int roun
     }
   }
   CK(cudaEventRecord(b, s->st));
-  CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * k, cudaMemcpyDeviceToHost, s->st));
+  CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * (IGC_LANE_LIMIT + 1), cudaMemcpyDeviceToHost, s->st));
   CK(cudaStreamSynchronize(s->st));
+  if (int ce = check_err(s)) return ce;
   float ms = 0.0f;
   CK(cudaEventElapsedTime(&ms, a, b));
   cudaEventDestroy(a);
@@ -1546,7 +1579,9 @@ extern "C" int igc_session_profile(igc_session *s, const int32_t *ids, int k, in
   int c = enqueue_pass(s, k, 1);
   s->prof_on = false;
   if (c != IGC_OKAY) return c;
+  CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * (IGC_LANE_LIMIT + 1), cudaMemcpyDeviceToHost, s->st));
   CK(cudaStreamSynchronize(s->st));
+  if (int ce = check_err(s)) return ce;
   int n = 0;
   for (size_t i = 0; i + 1 < s->marks.size() && n < capacity; ++i, ++n) {
     float ms = 0.0f;
