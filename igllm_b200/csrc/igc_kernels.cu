@@ -351,278 +351,227 @@ __global__ void ple_finish_kernel(const float *raw, const float *seed, int lanes
 }
 
 // ---------------------------------------------------------------------------
-// attention, step 1: q heads normed and turned, and for an owner layer the
-// new key and value rows normed, turned and written into the cache
-// (app_core.c:11481-11512).  One block a lane, one warp a head.
-__global__ void attn_prep_kernel(float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
-                                 const float *q_norm, const float *k_norm, const float *cs_tab,
-                                 const float *sn_tab, int owner, float eps, const int *d_p0, int lanes,
-                                 float *kc, float *vc) {
-  int j = blockIdx.x;
-  if (j >= lanes) return;
-  int pos = *d_p0 + j;
-  int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31, nw = blockDim.x >> 5;
-  int half = hd / 2;
-  const float *cs = cs_tab + (size_t)pos * half;
-  const float *sn = sn_tab + (size_t)pos * half;
-  float *row = qkv + (size_t)j * qkv_stride;
-  int n_q = heads, n_k = owner ? kv_heads : 0, n_v = owner ? kv_heads : 0;
-  int kv_w = kv_heads * hd;
-  for (int item = warp; item < n_q + n_k + n_v; item += nw) {
-    float *v;
-    const float *w;
-    bool turn;
-    float *cache = nullptr;
-    if (item < n_q) {
-      v = row + (size_t)item * hd;
-      w = q_norm;
-      turn = true;
-    } else if (item < n_q + n_k) {
-      int kh = item - n_q;
-      v = row + (size_t)heads * hd + (size_t)kh * hd;
-      w = k_norm;
-      turn = true;
-      cache = kc + (size_t)pos * kv_w + (size_t)kh * hd;
-    } else {
-      int vh = item - n_q - n_k;
-      v = row + (size_t)heads * hd + kv_w + (size_t)vh * hd;
-      w = nullptr;
-      turn = false;
-      cache = vc + (size_t)pos * kv_w + (size_t)vh * hd;
-    }
-    float s = 0.0f;
-    for (int d = l32; d < hd; d += 32) s += v[d] * v[d];
-    float sh = (float)(1.0 / sqrt((double)warp_sum(s) / (double)hd + (double)eps));
-    __syncwarp();
-    // normalise and turn, pairs (d, d + half) handled by one thread
-    for (int d = l32; d < half; d += 32) {
-      float lo = v[d] * sh, hi = v[d + half] * sh;
-      if (w) {
-        lo *= w[d];
-        hi *= w[d + half];
-      }
-      if (turn) {
-        float c = cs[d], si = sn[d];
-        float nlo = lo * c - hi * si;
-        float nhi = hi * c + lo * si;
-        lo = nlo;
-        hi = nhi;
-      }
-      v[d] = lo;
-      v[d + half] = hi;
-      if (cache) {
-        cache[d] = lo;
-        cache[d + half] = hi;
-      }
-    }
-  }
-}
-
-// attention, step 2 (app_core.c:11415 session_attend_group, :11296
-// attend_score_band, :11333 attend_blend_band): scores with scale 1.0
-// (app_core.c:11314), softmax, weighted values, over each lane's own span
-// ([pos - window + 1, pos] on sliding layers, [0, pos] on global ones,
-// app_core.c:11515-11518).
+// attention (app_core.c:11455 session_attend, :11415 session_attend_group,
+// :11296 attend_score_band, :11333 attend_blend_band): for each (lane, head)
+// pair, the query normed and turned (app_core.c:11492-11494), scores with
+// scale 1.0 (app_core.c:11314) over the lane's own span ([pos - window + 1,
+// pos] on sliding layers, [0, pos] on global ones, app_core.c:11515-11518),
+// softmax, weighted values.  On an owner layer the block's new key and value
+// rows are normed, turned and written into the cache here too
+// (app_core.c:11505-11512).
 //
-// The span is cut into chunks whose boundaries sit at fixed multiples of
-// the session's chunk length, so a position's partial sums never depend on
-// how many lanes a pass carried; each block takes 32 (lane, head) pairs and
-// walks chunks in 32-position tiles with an online softmax.  Warp w scores
-// positions w, w+8, w+16, w+24 of a tile for all 32 pairs (each thread holds
-// a slice of the head dimension, and a transposing butterfly leaves thread p
-// with pair p's full dot product), then owns pairs 4w..4w+3 for the softmax
-// and the value blend, with their running max, sum and accumulator in its
-// registers.  Partials per chunk go to attn_combine_kernel.
-constexpr int ATT_T = 32;  // positions a tile
-constexpr int ATT_P = 32;  // (lane, head) pairs a block
+// The span is cut into chunks whose boundaries sit at fixed multiples of the
+// session's chunk length, so a position's partial sums never depend on how
+// many lanes a pass carried.  A block takes one chunk and eight pairs, one
+// a warp.  Per 32-position tile, thread l of a warp scores position l (the
+// query read from shared memory by broadcast, the key row padded so the
+// warp's reads do not collide), the warp updates its online softmax, and
+// then thread l blends dimensions [l*DPL, (l+1)*DPL) of the values.
+// Partials per chunk go to attn_combine_kernel.
+constexpr int ATT_T = 32;        // positions a tile
+constexpr int ATT_PAIRS = 8;     // (lane, head) pairs a block, one a warp
+constexpr int ATT_BLOCK_ROWS = 16;  // block positions a chunk can hold
 
 __host__ __device__ inline size_t attn_smem_floats(int hd, int kv_w) {
-  return (size_t)ATT_P * hd + 2 * (size_t)ATT_T * kv_w + (size_t)ATT_P * (ATT_T + 1) + ATT_P;
+  const size_t ks = (size_t)kv_w + 4;
+  return (size_t)ATT_PAIRS * hd + 2 * (size_t)ATT_T * ks + 2 * (size_t)ATT_BLOCK_ROWS * ks;
 }
 
-// DPL consecutive floats from shared memory, as float4 where they fit one.
 template <int DPL>
-__device__ __forceinline__ void load_slice(const float *src, float (&dst)[DPL]) {
+__device__ __forceinline__ void load_dpl(const float *src, float (&v)[DPL]) {
   if constexpr (DPL % 4 == 0) {
 #pragma unroll
     for (int e = 0; e < DPL; e += 4) {
-      float4 v = *reinterpret_cast<const float4 *>(src + e);
-      dst[e] = v.x;
-      dst[e + 1] = v.y;
-      dst[e + 2] = v.z;
-      dst[e + 3] = v.w;
+      const float4 x = *reinterpret_cast<const float4 *>(src + e);
+      v[e] = x.x;
+      v[e + 1] = x.y;
+      v[e + 2] = x.z;
+      v[e + 3] = x.w;
     }
   } else {
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) dst[e] = src[e];
+    for (int e = 0; e < DPL; ++e) v[e] = src[e];
   }
 }
 
-// 32 per-slot partial sums in every thread -> thread l holds slot l's total.
-__device__ __forceinline__ float transpose_sum32(float (&v)[32]) {
-  const int lane = threadIdx.x & 31;
+template <int DPL>
+__device__ __forceinline__ void store_dpl(float *dst, const float (&v)[DPL]) {
+  if constexpr (DPL % 4 == 0) {
 #pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    const bool up = (lane & o) != 0;
+    for (int e = 0; e < DPL; e += 4) *reinterpret_cast<float4 *>(dst + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+  } else {
 #pragma unroll
-    for (int i = 0; i < o; ++i) {
-      float send = up ? v[i] : v[i + o];
-      float keep = up ? v[i + o] : v[i];
-      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    for (int e = 0; e < DPL; ++e) dst[e] = v[e];
+  }
+}
+
+// One head of 32 * DPL dimensions, DPL a thread: normed (app_core.c:4667,
+// double mean of squares) with an optional gain, then turned by the rope
+// tables of its position (pairs (d, d + hd/2), threads l and l + 16).
+template <int DPL>
+__device__ __forceinline__ void head_norm_turn(float (&v)[DPL], const float *gain, const float *cs, const float *sn,
+                                               float eps, bool turn, int l) {
+  constexpr int HD = 32 * DPL;
+  float s = 0.0f;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) s += v[e] * v[e];
+  s = warp_sum(s);
+  const float sh = (float)(1.0 / sqrt((double)s / (double)HD + (double)eps));
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) v[e] = gain ? v[e] * sh * gain[l * DPL + e] : v[e] * sh;
+  if (turn) {
+    float other[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) other[e] = __shfl_xor_sync(0xffffffffu, v[e], 16);
+    const int d0 = (l & 15) * DPL;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      const float c = cs[d0 + e], si = sn[d0 + e];
+      v[e] = l < 16 ? v[e] * c - other[e] * si : v[e] * c + other[e] * si;
     }
   }
-  return v[0];
 }
 
-template <int DPL, bool KV1>
-__global__ void __launch_bounds__(256) attn_chunk_kernel(const float *qkv, int qkv_stride, int heads,
-                                                         const float *kc, const float *vc, int kv_w, int group,
-                                                         int sliding, int span, const int *d_p0, int lanes,
-                                                         int chunk_len, float *part_ml, float *part_acc) {
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+template <int DPL>
+__global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_stride, int heads, int kv_heads,
+                                                   const float *q_norm, const float *k_norm, const float *cs_tab,
+                                                   const float *sn_tab, float eps, int owner, float *kc, float *vc,
+                                                   int sliding, int span, const int *d_p0, int lanes, int chunk_len,
+                                                   float *part_ml, float *part_acc) {
   constexpr int HD = DPL * 32;
+  const int kv_w = kv_heads * HD, KS = kv_w + 4, half = HD / 2;
   extern __shared__ __align__(16) float sm[];
-  float *qs = sm;                          // [ATT_P][HD]
-  float *ks = qs + ATT_P * HD;             // [ATT_T][kv_w]
-  float *vs = ks + (size_t)ATT_T * kv_w;   // [ATT_T][kv_w]
-  float *sc = vs + (size_t)ATT_T * kv_w;   // [ATT_P][ATT_T + 1]
-  int *kvoff = reinterpret_cast<int *>(sc + ATT_P * (ATT_T + 1));  // [ATT_P]
-  const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
+  float *qs = sm;                                // [8][HD]
+  float *ks = qs + ATT_PAIRS * HD;               // [32][KS]
+  float *vs = ks + (size_t)ATT_T * KS;           // [32][KS]
+  float *bk = vs + (size_t)ATT_T * KS;           // [16][KS] the block's new keys (owner layers)
+  float *bv = bk + (size_t)ATT_BLOCK_ROWS * KS;  // [16][KS] and values
+  const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int p0 = *d_p0;
   const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
   const int hi_all = p0 + lanes;
   const int c_first = lo_all / chunk_len;
   const int n_chunks = (hi_all - 1) / chunk_len - c_first + 1;
-  const int pair0 = blockIdx.y * ATT_P;
-  const int n_pairs = min(ATT_P, lanes * heads - pair0);
-  if ((int)blockIdx.x >= n_chunks) return;
+  const int cr = blockIdx.x;
+  if (cr >= n_chunks) return;
+  const int c = c_first + cr;
+  const int c_lo = max(c * chunk_len, lo_all), c_hi = min((c + 1) * chunk_len, hi_all);
 
-  for (int i = threadIdx.x; i < ATT_P * (HD / 4); i += blockDim.x) {
-    const int pr = i / (HD / 4), d4 = i % (HD / 4);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (pr < n_pairs) {
-      const int p = pair0 + pr, j = p / heads, h = p - j * heads;
-      v = *reinterpret_cast<const float4 *>(qkv + (size_t)j * qkv_stride + (size_t)h * HD + d4 * 4);
+  // this warp's query, normed and turned at its lane's position
+  const int pair = blockIdx.y * ATT_PAIRS + warp;
+  const bool has = pair < lanes * heads;
+  const int j = has ? pair / heads : 0, h = has ? pair - (pair / heads) * heads : 0;
+  const int kvoff = (h / (heads / kv_heads)) * HD;
+  if (has) {
+    float qv[DPL];
+    load_dpl<DPL>(qkv + (size_t)j * qkv_stride + (size_t)h * HD + l * DPL, qv);
+    const int pos = p0 + j;
+    head_norm_turn<DPL>(qv, q_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps, true, l);
+    store_dpl<DPL>(qs + warp * HD + l * DPL, qv);
+  }
+  // an owner layer's new keys and values that fall in this chunk: normed,
+  // turned (keys), kept in shared memory, and written to the cache once
+  int jb_lo = 0, jb_hi = 0;
+  if (owner) {
+    jb_lo = max(0, c * chunk_len - p0);
+    jb_hi = min(lanes, (c + 1) * chunk_len - p0);
+    const int per = 2 * kv_heads, items = max(0, jb_hi - jb_lo) * per;
+    for (int it = warp; it < items; it += ATT_PAIRS) {
+      const int jj = jb_lo + it / per, rest = it % per, kh = rest >> 1, is_v = rest & 1;
+      float v[DPL];
+      load_dpl<DPL>(qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + kh * HD + l * DPL, v);
+      const int pos = p0 + jj;
+      head_norm_turn<DPL>(v, is_v ? nullptr : k_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps,
+                          !is_v, l);
+      store_dpl<DPL>((is_v ? bv : bk) + (size_t)(jj - jb_lo) * KS + kh * HD + l * DPL, v);
+      if (blockIdx.y == 0) store_dpl<DPL>((is_v ? vc : kc) + (size_t)pos * kv_w + kh * HD + l * DPL, v);
     }
-    reinterpret_cast<float4 *>(qs)[i] = v;
   }
-  if (threadIdx.x < ATT_P) {
-    const int p = pair0 + threadIdx.x, h = p % heads;
-    kvoff[threadIdx.x] = (h / group) * HD;
-  }
-  // the pair this thread scores as lane l32 of the transposing sum
-  int lane_lo, lane_hi;
-  {
-    const int p = pair0 + l32, j = p / heads;
-    lane_lo = sliding ? max(0, p0 + j - span + 1) : 0;
-    lane_hi = l32 < n_pairs ? p0 + j : -1;
-  }
-  // the pairs this warp owns for the softmax and blend
-  int my_j[4], my_h[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int p = pair0 + warp * 4 + q;
-    my_j[q] = p / heads;
-    my_h[q] = p - my_j[q] * heads;
-  }
-  __syncthreads();
-  int my_kv[4];
-#pragma unroll
-  for (int q = 0; q < 4; ++q) my_kv[q] = kvoff[warp * 4 + q];
+  // the pair this thread's lane of the warp scores: its lane's span
+  const int lane_lo = sliding ? max(0, p0 + j - span + 1) : 0;
+  const int lane_hi = p0 + j;
 
-  for (int cr = blockIdx.x; cr < n_chunks; cr += gridDim.x) {
-    const int c = c_first + cr;
-    const int c_lo = max(c * chunk_len, lo_all), c_hi = min((c + 1) * chunk_len, hi_all);
-    float m_run[4], l_run[4], acc[4][DPL];
+  float m_run = -FLT_MAX, l_run = 0.0f, acc[DPL];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      m_run[q] = -FLT_MAX;
-      l_run[q] = 0.0f;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) acc[q][e] = 0.0f;
+  for (int e = 0; e < DPL; ++e) acc[e] = 0.0f;
+  const int w4 = kv_w / 4;
+  for (int tb = c * chunk_len; tb < c_hi; tb += ATT_T) {
+    if (tb + ATT_T <= c_lo) continue;
+    __syncthreads();  // the previous tile is consumed (and the query and block rows are written)
+    for (int i = threadIdx.x; i < ATT_T * w4; i += blockDim.x) {
+      const int r = i / w4, d4 = i - r * w4, pos = tb + r;
+      float *kd = ks + (size_t)r * KS + d4 * 4, *vd = vs + (size_t)r * KS + d4 * 4;
+      if (pos < c_lo || pos >= c_hi) {
+        *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+      } else if (owner && pos - p0 >= jb_lo && pos - p0 < jb_hi) {
+        const int rb = pos - p0 - jb_lo;
+        *reinterpret_cast<float4 *>(kd) = *reinterpret_cast<const float4 *>(bk + (size_t)rb * KS + d4 * 4);
+        *reinterpret_cast<float4 *>(vd) = *reinterpret_cast<const float4 *>(bv + (size_t)rb * KS + d4 * 4);
+      } else {
+        cp_async16(kd, kc + (size_t)pos * kv_w + d4 * 4);
+        cp_async16(vd, vc + (size_t)pos * kv_w + d4 * 4);
+      }
     }
-    for (int tb = c * chunk_len; tb < c_hi; tb += ATT_T) {
-      if (tb + ATT_T <= c_lo) continue;
-      __syncthreads();
-      {
-        const int w4 = KV1 ? HD / 4 : kv_w / 4;
-        for (int i = threadIdx.x; i < ATT_T * w4; i += blockDim.x) {
-          const int r = i / w4, d4 = i - r * w4, pos = tb + r;
-          const bool in = pos >= c_lo && pos < c_hi;
-          float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-          if (in) {
-            kv = *reinterpret_cast<const float4 *>(kc + (size_t)pos * kv_w + d4 * 4);
-            vv = *reinterpret_cast<const float4 *>(vc + (size_t)pos * kv_w + d4 * 4);
-          }
-          reinterpret_cast<float4 *>(ks)[i] = kv;
-          reinterpret_cast<float4 *>(vs)[i] = vv;
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+    if (has) {
+      // scores: thread l takes position tb + l
+      const int pos = tb + l;
+      const float4 *qr = reinterpret_cast<const float4 *>(qs + warp * HD);
+      const float4 *kr = reinterpret_cast<const float4 *>(ks + (size_t)l * KS + kvoff);
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 4
+      for (int d4 = 0; d4 < HD / 4; d4 += 4) {
+        float4 q0 = qr[d4], k0 = kr[d4];
+        a0 = fmaf(q0.x, k0.x, a0); a0 = fmaf(q0.y, k0.y, a0); a0 = fmaf(q0.z, k0.z, a0); a0 = fmaf(q0.w, k0.w, a0);
+        if (d4 + 1 < HD / 4) {
+          float4 q1 = qr[d4 + 1], k1 = kr[d4 + 1];
+          a1 = fmaf(q1.x, k1.x, a1); a1 = fmaf(q1.y, k1.y, a1); a1 = fmaf(q1.z, k1.z, a1); a1 = fmaf(q1.w, k1.w, a1);
+        }
+        if (d4 + 2 < HD / 4) {
+          float4 q2 = qr[d4 + 2], k2 = kr[d4 + 2];
+          a2 = fmaf(q2.x, k2.x, a2); a2 = fmaf(q2.y, k2.y, a2); a2 = fmaf(q2.z, k2.z, a2); a2 = fmaf(q2.w, k2.w, a2);
+        }
+        if (d4 + 3 < HD / 4) {
+          float4 q3 = qr[d4 + 3], k3 = kr[d4 + 3];
+          a3 = fmaf(q3.x, k3.x, a3); a3 = fmaf(q3.y, k3.y, a3); a3 = fmaf(q3.z, k3.z, a3); a3 = fmaf(q3.w, k3.w, a3);
         }
       }
-      __syncthreads();
-      // scores
-#pragma unroll 1
-      for (int r = warp; r < ATT_T; r += 8) {
-        const int pos = tb + r;
-        float kslice[DPL];
-        if (KV1) load_slice<DPL>(ks + r * HD + l32 * DPL, kslice);
-        float part[32];
+      const float s = (a0 + a1) + (a2 + a3);
+      const bool valid = pos >= c_lo && pos < c_hi && pos >= lane_lo && pos <= lane_hi;
+      const float sc = valid ? s : -FLT_MAX;
+      // online softmax over the warp's 32 positions
+      const float m_new = fmaxf(m_run, warp_max(sc));
+      const float f = (m_new == -FLT_MAX) ? 1.0f : (m_run == -FLT_MAX ? 0.0f : expf(m_run - m_new));
+      const float pe = valid ? expf(sc - m_new) : 0.0f;
+      l_run = l_run * f + warp_sum(pe);
+      m_run = m_new;
 #pragma unroll
-        for (int pr = 0; pr < 32; ++pr) {
-          float qv[DPL], kv[DPL];
-          load_slice<DPL>(qs + pr * HD + l32 * DPL, qv);
-          if (KV1) {
-#pragma unroll
-            for (int e = 0; e < DPL; ++e) kv[e] = kslice[e];
-          } else {
-            load_slice<DPL>(ks + r * kv_w + kvoff[pr] + l32 * DPL, kv);
-          }
-          float t = 0.0f;
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) t += qv[e] * kv[e];
-          part[pr] = t;
-        }
-        const float s_ = transpose_sum32(part);
-        const bool valid = pos >= c_lo && pos < c_hi && pos >= lane_lo && pos <= lane_hi;
-        sc[l32 * (ATT_T + 1) + r] = valid ? s_ : -FLT_MAX;
-      }
-      __syncthreads();
-      // online softmax and blend for this warp's pairs
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int pr = warp * 4 + q;
-        const float s_ = sc[pr * (ATT_T + 1) + l32];
-        const float m_new = fmaxf(m_run[q], warp_max(s_));
-        const float f = (m_new == -FLT_MAX) ? 1.0f : (m_run[q] == -FLT_MAX ? 0.0f : expf(m_run[q] - m_new));
-        const float pe = (s_ == -FLT_MAX) ? 0.0f : expf(s_ - m_new);
-        l_run[q] = l_run[q] * f + warp_sum(pe);
-        m_run[q] = m_new;
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[q][e] *= f;
-        sc[pr * (ATT_T + 1) + l32] = pe;
-      }
-      __syncwarp();
-#pragma unroll 2
+      for (int e = 0; e < DPL; ++e) acc[e] *= f;
+      // blend: thread l takes dimensions [l*DPL, (l+1)*DPL) of every position
+      const float *vcol = vs + kvoff + l * DPL;
+#pragma unroll 4
       for (int r = 0; r < ATT_T; ++r) {
+        const float pr = __shfl_sync(0xffffffffu, pe, r);
+        float vv[DPL];
+        load_dpl<DPL>(vcol + (size_t)r * KS, vv);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float pe = sc[(warp * 4 + q) * (ATT_T + 1) + r];
-          float vv[DPL];
-          load_slice<DPL>(vs + r * kv_w + (KV1 ? 0 : my_kv[q]) + l32 * DPL, vv);
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[q][e] += pe * vv[e];
-        }
+        for (int e = 0; e < DPL; ++e) acc[e] = fmaf(pr, vv[e], acc[e]);
       }
     }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      if (warp * 4 + q >= n_pairs) continue;
-      const size_t slot = ((size_t)cr * 16 + my_j[q]) * heads + my_h[q];
-      if (l32 == 0) {
-        part_ml[slot * 2 + 0] = m_run[q];
-        part_ml[slot * 2 + 1] = l_run[q];
-      }
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) part_acc[slot * HD + l32 * DPL + e] = acc[q][e];
+  }
+  if (has) {
+    const size_t slot = ((size_t)cr * 16 + j) * heads + h;
+    if (l == 0) {
+      part_ml[slot * 2 + 0] = m_run;
+      part_ml[slot * 2 + 1] = l_run;
     }
+    store_dpl<DPL>(part_acc + slot * HD + l * DPL, acc);
   }
 }
 
@@ -1028,14 +977,10 @@ cudaError_t igc_kernels_configure(int bytes) {
   e = allow_smem_mode<MODE_PACK>(bytes);
   if (e == cudaSuccess) e = allow_smem_mode<MODE_NT1>(bytes);
   if (e == cudaSuccess) e = allow_smem_mode<MODE_NT2>(bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<1, true>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<2, true>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<4, true>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<8, true>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<1, false>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<2, false>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<4, false>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_chunk_kernel<8, false>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<1>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<2>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<4>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<8>, bytes);
   if (e == cudaSuccess) e = allow_smem_fn(topk_stage2_kernel, bytes);
   return e;
 }
@@ -1087,29 +1032,17 @@ cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes
   return cudaGetLastError();
 }
 
-cudaError_t igc_launch_attn_prep(float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
-                                 const float *k_norm, const float *cs, const float *sn, int owner, float eps,
-                                 const int *d_p0, int lanes, float *kc, float *vc, cudaStream_t st) {
-  attn_prep_kernel<<<lanes, 256, 0, st>>>(qkv, qkv_stride, heads, kv_heads, hd, q_norm, k_norm, cs, sn, owner,
-                                          eps, d_p0, lanes, kc, vc);
-  return cudaGetLastError();
-}
-
 size_t igc_attn_smem(int hd, int kv_w) { return sizeof(float) * attn_smem_floats(hd, kv_w); }
 
-cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int hd, const float *kc, const float *vc,
-                            int kv_w, int group, int sliding, int span, const int *d_p0, int lanes, int chunk_len,
-                            int grid_x, float *part_ml, float *part_acc, float *out, int out_stride, cudaStream_t st) {
-  size_t smem = igc_attn_smem(hd, kv_w);
-  dim3 grid(grid_x, (lanes * heads + ATT_P - 1) / ATT_P);
-  const bool kv1 = kv_w == hd;
-#define IGC_ATT(D)                                                                                             \
-  if (kv1)                                                                                                     \
-    attn_chunk_kernel<D, true><<<grid, 256, smem, st>>>(qkv, qkv_stride, heads, kc, vc, kv_w, group, sliding, \
-                                                        span, d_p0, lanes, chunk_len, part_ml, part_acc);      \
-  else                                                                                                         \
-    attn_chunk_kernel<D, false><<<grid, 256, smem, st>>>(qkv, qkv_stride, heads, kc, vc, kv_w, group, sliding, \
-                                                         span, d_p0, lanes, chunk_len, part_ml, part_acc);
+cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
+                            const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
+                            float *vc, int sliding, int span, const int *d_p0, int lanes, int chunk_len, int grid_x,
+                            float *part_ml, float *part_acc, float *out, int out_stride, cudaStream_t st) {
+  const size_t smem = igc_attn_smem(hd, kv_heads * hd);
+  const dim3 grid(grid_x, (lanes * heads + ATT_PAIRS - 1) / ATT_PAIRS);
+#define IGC_ATT(D)                                                                                          \
+  attn_kernel<D><<<grid, 256, smem, st>>>(qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps, owner, \
+                                          kc, vc, sliding, span, d_p0, lanes, chunk_len, part_ml, part_acc);
   switch (hd) {
     case 32: IGC_ATT(1) break;
     case 64: IGC_ATT(2) break;

@@ -1087,12 +1087,15 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
     prof_mark(s, PROF_ATTN, 0.0);
-    CKL(igc_launch_attn_prep(s->qkv, L.qkv_rows, m->heads, L.kv_heads, L.hd, L.q_norm, L.k_norm,
-                             m->rope_cs[L.kind], m->rope_sn[L.kind], L.share ? 0 : 1, m->eps, d_p0, K,
-                             s->kc[l], s->vc[l], s->st));
-    CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, L.hd, s->kc[owner], s->vc[owner], O.kv_rows,
-                        m->heads / L.kv_heads, L.kind == 0 ? 1 : 0, m->slide_span, d_p0, K, s->chunk_len,
-                        s->max_chunks, s->part_ml, s->part_acc, s->attn, L.q_rows, s->st));
+    // chunks a span can touch: the window plus the block on sliding layers,
+    // the whole context on global ones (blocks past the live count exit)
+    const int sliding = L.kind == 0 ? 1 : 0;
+    int grid_x = s->max_chunks;
+    if (sliding) grid_x = std::min(grid_x, (m->slide_span + IGC_LANE_LIMIT) / s->chunk_len + 2);
+    CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
+                        m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
+                        m->slide_span, d_p0, K, s->chunk_len, grid_x, s->part_ml, s->part_acc, s->attn, L.q_rows,
+                        s->st));
     ++g_launches;  // the combine kernel
     c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
              1.0f, nullptr, 0, nullptr, &so);
