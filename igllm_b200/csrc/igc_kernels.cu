@@ -93,7 +93,6 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   uint64_t *mb = bars + warp * D;
   unsigned char *mr = ring + (size_t)warp * D * slot_bytes;
 
-  pdl_release();
   const uint64_t policy = l2_evict_first();
   // piece n of this warp: unit q + (n / np) Q, chunks from c_lo + (n % np) P
   auto issue = [&](int n) {
@@ -118,6 +117,10 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
 
   pdl_wait();
   gemv_prologue<PRO, MODE>(a, stage, scr);
+  // the next kernel may start (and fetch its weights) once this one is past
+  // its own wait: released any earlier, kernels still waiting would release
+  // the ones after them and pile up on the SMs
+  pdl_release();
 
   // the epilogue factor of the lanes each accumulator column holds
   float sh[NT][2];
@@ -306,21 +309,42 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
 }
 // ---------------------------------------------------------------------------
 // embedding rows (app_core.c:11863-11874, :11886-11891)
+// bf16 -> f32 of eight values, times `gain`.
+__device__ __forceinline__ void bf16x8_scaled(const uint4 &w, float gain, float4 &a, float4 &b) {
+  a = make_float4(__uint_as_float(w.x << 16) * gain, __uint_as_float(w.x & 0xffff0000u) * gain,
+                  __uint_as_float(w.y << 16) * gain, __uint_as_float(w.y & 0xffff0000u) * gain);
+  b = make_float4(__uint_as_float(w.z << 16) * gain, __uint_as_float(w.z & 0xffff0000u) * gain,
+                  __uint_as_float(w.w << 16) * gain, __uint_as_float(w.w & 0xffff0000u) * gain);
+}
+
+// Blocks (lane, slice): each takes every gridDim.y-th run of eight values of
+// the lane's embedding row and per-layer-embedding row, 16-byte loads
+// (widths are multiples of eight; rows start 16-byte aligned).
 __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embed, int hidden,
                              float embed_gain, const uint16_t *ple_embed, int ple_vocab,
                              int ple_width, float ple_gain, float *x_out, float *seed_out) {
-  int j = blockIdx.x;
+  pdl_release();
+  const int j = blockIdx.x;
   if (j >= lanes) return;
-  int id = ids[j];
-  const uint16_t *row = embed + (size_t)id * hidden;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < hidden; i += blockDim.x)
-    x_out[(size_t)j * hidden + i] = __uint_as_float((uint32_t)row[i] << 16) * embed_gain;
+  const int id = ids[j];
+  const int step = gridDim.y * blockDim.x, first = blockIdx.y * blockDim.x + threadIdx.x;
+  const uint4 *row = reinterpret_cast<const uint4 *>(embed + (size_t)id * hidden);
+  float4 *xo = reinterpret_cast<float4 *>(x_out + (size_t)j * hidden);
+  for (int i = first; i < hidden / 8; i += step) {
+    float4 a, b;
+    bf16x8_scaled(row[i], embed_gain, a, b);
+    xo[2 * i] = a;
+    xo[2 * i + 1] = b;
+  }
   if (ple_embed) {
-    const uint16_t *srow = ple_embed + (size_t)(id % ple_vocab) * ple_width;
-#pragma unroll 8
-    for (int i = threadIdx.x; i < ple_width; i += blockDim.x)
-      seed_out[(size_t)j * ple_width + i] = __uint_as_float((uint32_t)srow[i] << 16) * ple_gain;
+    const uint4 *srow = reinterpret_cast<const uint4 *>(ple_embed + (size_t)(id % ple_vocab) * ple_width);
+    float4 *so = reinterpret_cast<float4 *>(seed_out + (size_t)j * ple_width);
+    for (int i = first; i < ple_width / 8; i += step) {
+      float4 a, b;
+      bf16x8_scaled(srow[i], ple_gain, a, b);
+      so[2 * i] = a;
+      so[2 * i + 1] = b;
+    }
   }
 }
 
@@ -328,6 +352,8 @@ __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embe
 // then (chunk + seed) / sqrt(2).  One block a (lane, chunk).
 __global__ void ple_finish_kernel(const float *raw, const float *seed, int lanes, int layers,
                                   int ple_dim, const float *w, float eps, float blend, float *out) {
+  pdl_release();
+  pdl_wait();
   int j = blockIdx.x / layers, c = blockIdx.x % layers;
   if (j >= lanes) return;
   int width = layers * ple_dim;
@@ -412,6 +438,15 @@ template <int DPL>
 __device__ __forceinline__ void head_norm_turn(float (&v)[DPL], const float *gain, const float *cs, const float *sn,
                                                float eps, bool turn, int l) {
   constexpr int HD = 32 * DPL;
+  float c_[DPL], s_[DPL];
+  if (turn) {
+    const int d0 = (l & 15) * DPL;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      c_[e] = cs[d0 + e];
+      s_[e] = sn[d0 + e];
+    }
+  }
   float s = 0.0f;
 #pragma unroll
   for (int e = 0; e < DPL; ++e) s += v[e] * v[e];
@@ -423,12 +458,8 @@ __device__ __forceinline__ void head_norm_turn(float (&v)[DPL], const float *gai
     float other[DPL];
 #pragma unroll
     for (int e = 0; e < DPL; ++e) other[e] = __shfl_xor_sync(0xffffffffu, v[e], 16);
-    const int d0 = (l & 15) * DPL;
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) {
-      const float c = cs[d0 + e], si = sn[d0 + e];
-      v[e] = l < 16 ? v[e] * c - other[e] * si : v[e] * c + other[e] * si;
-    }
+    for (int e = 0; e < DPL; ++e) v[e] = l < 16 ? v[e] * c_[e] - other[e] * s_[e] : v[e] * c_[e] + other[e] * s_[e];
   }
 }
 
@@ -451,6 +482,8 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   float *bk = vs + (size_t)ATT_T * KS;           // [16][KS] the block's new keys (owner layers)
   float *bv = bk + (size_t)ATT_BLOCK_ROWS * KS;  // [16][KS] and values
   const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
+  pdl_release();
+  pdl_wait();
   const int p0 = *d_p0;
   const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
   const int hi_all = p0 + lanes;
@@ -575,43 +608,58 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   }
 }
 
-// attention, step 3: the chunks' partials merged into each head's output,
-// (sum_c acc_c e^{m_c - M}) / (sum_c l_c e^{m_c - M}), chunks in ascending
-// order.  One block a (lane, head); the chunk weights are formed once, then
-// one thread a dimension sums the chunks.
+// attention, second step: the chunks' partials merged into each head's
+// output, (sum_c acc_c e^{m_c - M}) / (sum_c l_c e^{m_c - M}).  One block a
+// (lane, head).  Warp 0 forms the chunk weights; its thread t sums the
+// weighted l_c of chunks t, t + 32, ... in order and the warp adds the 32
+// sums in a fixed tree; then one thread a dimension sums the chunks in
+// ascending order.
 __global__ void attn_combine_kernel(const float *part_ml, const float *part_acc, int lanes, int heads, int hd,
                                     int sliding, int span, int chunk_len, const int *d_p0, float *out,
                                     int out_stride) {
   __shared__ float wgt[1024];
   __shared__ float tot;
-  int j = blockIdx.x / heads, h = blockIdx.x % heads;
+  pdl_release();
+  pdl_wait();
+  const int j = blockIdx.x / heads, h = blockIdx.x % heads;
   if (j >= lanes) return;
   const int p0 = *d_p0;
   const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
   const int hi_all = p0 + lanes;
   const int c_first = lo_all / chunk_len;
   const int n_chunks = (hi_all - 1) / chunk_len - c_first + 1;
+  const size_t cstride = (size_t)16 * heads;  // slots between chunks
+  const size_t s0 = (size_t)j * heads + h;
   if (threadIdx.x < 32) {
+    constexpr int MAXC = 1024 / 32;
+    float m[MAXC], lv[MAXC];
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = threadIdx.x + 32 * i;
+      m[i] = c < n_chunks ? part_ml[(c * cstride + s0) * 2] : -FLT_MAX;
+      lv[i] = c < n_chunks ? part_ml[(c * cstride + s0) * 2 + 1] : 0.0f;
+    }
     float M = -FLT_MAX;
-    for (int c = threadIdx.x; c < n_chunks; c += 32) M = fmaxf(M, part_ml[(((size_t)c * 16 + j) * heads + h) * 2]);
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) M = fmaxf(M, m[i]);
     M = warp_max(M);
-    for (int c = threadIdx.x; c < n_chunks; c += 32) {
-      float m = part_ml[(((size_t)c * 16 + j) * heads + h) * 2];
-      wgt[c] = (m == -FLT_MAX) ? 0.0f : expf(m - M);
+    float L = 0.0f;
+#pragma unroll
+    for (int i = 0; i < MAXC; ++i) {
+      const int c = threadIdx.x + 32 * i;
+      const float w = (m[i] == -FLT_MAX) ? 0.0f : expf(m[i] - M);
+      if (c < n_chunks) wgt[c] = w;
+      L += lv[i] * w;
     }
-    __syncwarp();
-    if (threadIdx.x == 0) {
-      float L = 0.0f;
-      for (int c = 0; c < n_chunks; ++c) L += part_ml[(((size_t)c * 16 + j) * heads + h) * 2 + 1] * wgt[c];
-      tot = L;
-    }
+    L = warp_sum(L);
+    if (threadIdx.x == 0) tot = L;
   }
   __syncthreads();
   const float inv = 1.0f / tot;
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float o = 0.0f;
 #pragma unroll 8
-    for (int c = 0; c < n_chunks; ++c) o += part_acc[(((size_t)c * 16 + j) * heads + h) * hd + d] * wgt[c];
+    for (int c = 0; c < n_chunks; ++c) o += part_acc[(c * cstride + s0) * hd + d] * wgt[c];
     out[(size_t)j * out_stride + (size_t)h * hd + d] = o * inv;
   }
 }
@@ -623,6 +671,8 @@ __global__ void argmax_final_kernel(const float *part_val, const int *part_idx, 
                                     int32_t *top_out) {
   __shared__ float sv[32][16];
   __shared__ int si[32][16];
+  pdl_release();
+  pdl_wait();
   const int j = threadIdx.x & 15, stripe = threadIdx.x >> 4;
   float v = -FLT_MAX;
   int i = 0x7fffffff;
@@ -938,7 +988,11 @@ static cudaError_t allow_smem_fn(F *fn, int bytes) {
   cudaError_t e = cudaFuncGetAttributes(&at, fn);
   if (e != cudaSuccess) return e;
   int dyn = bytes - (int)at.sharedSizeBytes;
-  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn > 0 ? dyn : 0);
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn > 0 ? dyn : 0);
+  // one shared-memory split for every kernel of the pass, so an SM never
+  // waits to re-split L1 between consecutive kernels
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  return e;
 }
 
 template <int MODE>
@@ -1021,15 +1075,16 @@ size_t igc_gemv_smem_min(const GemvArgs *a, int pair) {
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
                              float *x_out, float *seed_out, cudaStream_t st) {
-  embed_kernel<<<lanes, 256, 0, st>>>(ids, lanes, embed, hidden, embed_gain, ple_embed, ple_vocab, ple_width,
+  if ((hidden & 7) || (ple_embed && (ple_width & 7))) return cudaErrorInvalidValue;
+  embed_kernel<<<dim3(lanes, 8), 256, 0, st>>>(ids, lanes, embed, hidden, embed_gain, ple_embed, ple_vocab, ple_width,
                                       ple_gain, x_out, seed_out);
   return cudaGetLastError();
 }
 
 cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes, int layers, int ple_dim,
                                   const float *w, float eps, float blend, float *out, cudaStream_t st) {
-  ple_finish_kernel<<<lanes * layers, 256, 0, st>>>(raw, seed, lanes, layers, ple_dim, w, eps, blend, out);
-  return cudaGetLastError();
+  return launch_k(ple_finish_kernel, dim3(lanes * layers), dim3(256), 0, st, raw, seed, lanes, layers, ple_dim, w, eps,
+                  blend, out);
 }
 
 size_t igc_attn_smem(int hd, int kv_w) { return sizeof(float) * attn_smem_floats(hd, kv_w); }
@@ -1040,9 +1095,10 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
                             float *part_ml, float *part_acc, float *out, int out_stride, cudaStream_t st) {
   const size_t smem = igc_attn_smem(hd, kv_heads * hd);
   const dim3 grid(grid_x, (lanes * heads + ATT_PAIRS - 1) / ATT_PAIRS);
-#define IGC_ATT(D)                                                                                          \
-  attn_kernel<D><<<grid, 256, smem, st>>>(qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps, owner, \
-                                          kc, vc, sliding, span, d_p0, lanes, chunk_len, part_ml, part_acc);
+  cudaError_t e;
+#define IGC_ATT(D)                                                                                              \
+  e = launch_k(attn_kernel<D>, grid, dim3(256), smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, \
+               eps, owner, kc, vc, sliding, span, d_p0, lanes, chunk_len, part_ml, part_acc);
   switch (hd) {
     case 32: IGC_ATT(1) break;
     case 64: IGC_ATT(2) break;
@@ -1051,17 +1107,14 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
     default: return cudaErrorInvalidValue;
   }
 #undef IGC_ATT
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  attn_combine_kernel<<<lanes * heads, 256, 0, st>>>(part_ml, part_acc, lanes, heads, hd, sliding, span, chunk_len,
-                                                     d_p0, out, out_stride);
-  return cudaGetLastError();
+  return launch_k(attn_combine_kernel, dim3(lanes * heads), dim3(256), 0, st, part_ml, part_acc, lanes, heads, hd,
+                  sliding, span, chunk_len, d_p0, out, out_stride);
 }
 
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
                               cudaStream_t st) {
-  argmax_final_kernel<<<1, 512, 0, st>>>(part_val, part_idx, parts, lanes, top);
-  return cudaGetLastError();
+  return launch_k(argmax_final_kernel, dim3(1), dim3(512), 0, st, part_val, part_idx, parts, lanes, top);
 }
 
 cudaError_t igc_launch_rope_table(const float *steps, int half, int window, float *cs, float *sn,
