@@ -116,6 +116,20 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
   __syncwarp();
 
   pdl_wait();
+  // the multiplier of the GELU product, loaded now so its latency hides
+  // behind the prologue (this thread's outputs: rows unit*16 + g (+8), lanes 2t+k)
+  float mul_pre[NT][4];
+  if (EPI == EPI_GELU_MUL && slice == 0 && my_units == 1) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int row = q * 16 + g + (i >= 2 ? 8 : 0);
+        const int ln = MODE == MODE_PACK ? 2 * t + (i & 1) : nt * 8 + 2 * t + (i & 1);
+        const bool ok = row < a.pl.rows && ln < a.lanes && !(MODE == MODE_PACK && t >= 2);
+        mul_pre[nt][i] = ok ? a.aux[(size_t)ln * a.aux_stride + row] : 0.0f;
+      }
+  }
   gemv_prologue<PRO, MODE>(a, stage, scr);
   // the next kernel may start (and fetch its weights) once this one is past
   // its own wait: released any earlier, kernels still waiting would release
@@ -230,7 +244,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
           } else if (EPI == EPI_GELU_PAIR) {
             a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(x) * (v[PAIR][nt][i] * sh[nt][k]);
           } else if (EPI == EPI_GELU_MUL) {
-            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(x) * a.aux[(size_t)ln * a.aux_stride + row];
+            const float mul = my_units == 1 ? mul_pre[nt][i] : a.aux[(size_t)ln * a.aux_stride + row];
+            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(x) * mul;
           } else {  // EPI_LOGITS
             const float cv = a.cap > 0.0f ? logit_cap(x, a.cap) : x;
             a.out[(size_t)ln * a.out_stride + row] = cv;

@@ -519,7 +519,9 @@ struct Binder {
     if (per_sm < 1) per_sm = 1;
     int cap = m->sm_count * per_sm;
     int S = 1;
-    while (S < 8 && S * 2 <= p.n_cc && units * S < cap * GEMV_WARPS) S *= 2;
+    // the widest split that still gives every unit's group one warp slot,
+    // so no group runs two units one after the other
+    while (S < 8 && S * 2 <= p.n_cc && units * S * 2 <= cap * GEMV_WARPS) S *= 2;
     p.split = S;
     int per_iter = GEMV_WARPS / S;
     int need = (units + per_iter - 1) / per_iter;
