@@ -138,9 +138,9 @@ void desk_mat_mat(igc_desk *d, const igc_plane *sheet, const float *act, int act
         b.x = s->buf_a + (size_t)j0 * p->cols;
         b.out = s->buf_b + (size_t)j0 * p->rows;
         if (igc_gemv_smem_min(&b, 0) > (size_t)s->smem_limit) return void(note(s, IGC_FAIL_SUPPORT));
-        if (!ok(s, igc_launch_gemv(&b, 0, PRO_F32, EPI_STORE, p->grid, (size_t)s->smem_limit, s->st))) return;
+        if (!ok(s, igc_launch_gemv(&b, 0, PRO_F32, EPI_STORE, p->grid, (size_t)s->smem_limit, s->st, nullptr))) return;
       }
-    } else if (!ok(s, igc_launch_gemv(&a, 0, PRO_F32, EPI_STORE, p->grid, (size_t)s->smem_limit, s->st))) {
+    } else if (!ok(s, igc_launch_gemv(&a, 0, PRO_F32, EPI_STORE, p->grid, (size_t)s->smem_limit, s->st, nullptr))) {
       return;
     }
     for (int j = 0; j < k; ++j)

@@ -71,6 +71,10 @@ struct GemvArgs {
   // and where the reduction space, barriers and ring sit in shared memory
   int piece, depth;
   int off_red, off_bars, off_ring;
+  // unit slots (block, group) the units are spread over, and groups a
+  // virtual 8-warp block holds: partial sums are written one per virtual
+  // block, so their grouping is the same whatever a launch's block width
+  int slots, vgroups;
   int *err;  // set nonzero when a wait gave up
   // prologue
   const float *x;
@@ -96,8 +100,13 @@ struct GemvArgs {
   int *part_idx;
 };
 
-constexpr int GEMV_THREADS = 256;
-constexpr int GEMV_WARPS = GEMV_THREADS / 32;
+// Warps a block: the planning unit of a plane (its split and block count
+// are chosen for 8-warp blocks).  Launches of up to 8 lanes run 16-warp
+// blocks where their shared memory fits, each holding two 8-warp blocks'
+// worth of groups, so a block's staging work is spread over twice the
+// threads; results are the same either way.
+constexpr int GEMV_WARPS = 8;
+constexpr int GEMV_MAX_WARPS = 16;
 constexpr int GEMV_PIECE_BYTES = 576;  // one chunk of one row block: 512 B of codes + 64 B of scales
 constexpr int GEMV_MAX_DEPTH = 8;
 constexpr int GEMV_PART_LIMIT = 320;  // producer partials the prologue reads (16 stripes x 20)
@@ -156,11 +165,11 @@ __device__ __forceinline__ float fmax4(float4 v) { return fmaxf(fmaxf(fabsf(v.x)
 //   [0, 16)      per-lane factor the epilogue applies (norm shrink / 2^e)
 //   [16, 32)     per-lane power-of-two staging scale
 //   [32, 48)     per-lane shrink of the residual's norm
-//   [64, 192)    per-(lane, part) sums of squares
-//   [192, 320)   per-(lane, part) magnitudes
-//   [320, 576)   per-thread stripes of the residual's sums of squares
-constexpr int SCR_FACTOR = 0, SCR_SCALE = 16, SCR_SHRINK_P = 32, SCR_SSQ = 64, SCR_AMAX = 192, SCR_STRIPE = 320;
-constexpr int SCR_FLOATS = 576;
+//   [64, 832)     per-(lane, 128-column part) sums of squares, 48 parts a lane
+//   [832, 1088)   per-(lane, warp) magnitudes, 16 warps a lane
+//   [1600, 2112)  per-thread stripes of the residual's sums of squares
+constexpr int SCR_FACTOR = 0, SCR_SCALE = 16, SCR_SHRINK_P = 32, SCR_SSQ = 64, SCR_AMAX = 832, SCR_STRIPE = 1600;
+constexpr int SCR_FLOATS = 2112;
 
 // float4 columns a thread loads before computing on them: as many as keep
 // the register file in bounds for the arrays the prologue reads.
@@ -169,22 +178,27 @@ struct ProBatch {
   static constexpr int value = PRO == PRO_F32 ? 8 : PRO == PRO_NORM ? 6 : 4;
 };
 
-// The prologue.  Warps take lanes: with K < 8 lanes, 8/K warps (a power of
-// two) split one lane's columns; with more, a warp takes lanes w and w + 8.
-// Thread l32 of a warp walks float4 columns c4 = lo + l32 + 32 i; the stage
-// words of column 4 c4 move by two chunks per step of i, so each thread
-// computes its four word offsets once and then only adds.  The producer
-// partials and the first batch of activations are loaded before anything
-// waits on either; the per-lane reductions are fixed-order sums.
-template <int PRO, int MODE>
+// The prologue.  A lane's columns are cut into fixed parts of 128 (32
+// float4, one a thread), and every per-lane sum is a fixed tree over those
+// parts, so a lane's staged values and sums do not depend on how many lanes
+// or warps a launch has.  Warps take lanes: with fewer lanes than warps,
+// `wpl` warps (a power of two) share one lane's parts round robin; with
+// more, a warp takes lanes w and w + WARPS.  A part's stage words sit two
+// chunks further on per part, so each thread computes its four word offsets
+// once and then only adds.  The producer partials and the first batch of
+// activations are loaded before anything waits on either.
+constexpr int GEMV_MAX_PARTS = 48;  // 6144 columns
+
+template <int PRO, int MODE, int WARPS>
 __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
   constexpr bool RES = PRO == PRO_RESID || PRO == PRO_RESID_NORM;
   constexpr bool NRM = PRO == PRO_NORM || PRO == PRO_RESID_NORM;
   constexpr int B = ProBatch<PRO>::value;
-  constexpr int PQ = GEMV_PART_LIMIT / 16;
+  constexpr int STRIPES = WARPS * 2;  // threads / 16
+  constexpr int PQ = (GEMV_PART_LIMIT + STRIPES - 1) / STRIPES;
   const int cols = a.pl.cols, K = a.lanes, n4 = cols >> 2;
+  const int nparts = (n4 + 31) >> 5;
   const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
-  const int step = 2 * stage_chunk_words(MODE);  // stage words between items i and i + 1
   if (cols & 63) {
     // columns past `cols` in the last chunk meet zero weights, and must be
     // zero (not stale NaN patterns) for the products to stay exact
@@ -192,23 +206,23 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     for (int i = threadIdx.x; i < words; i += blockDim.x) reinterpret_cast<uint4 *>(stage)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
   }
-  // the residual's partials: thread (lane j, stripe q0) holds parts q0, q0 + 16, ...
+  // the residual's partials: thread (lane j, stripe q0) holds parts q0, q0 + STRIPES, ...
   float part[RES ? PQ : 1];
   if (RES) {
     const int j = threadIdx.x & 15, q0 = threadIdx.x >> 4;
 #pragma unroll
     for (int i = 0; i < PQ; ++i) {
-      const int q = q0 + 16 * i;
+      const int q = q0 + STRIPES * i;
       part[i] = (j < K && q < a.p_parts) ? a.p_ssq[q * 16 + j] : 0.0f;
     }
   }
   int wpl = 1;  // warps a lane
-  while (wpl * 2 * K <= GEMV_WARPS) wpl *= 2;
-  const int n_slots = (K + GEMV_WARPS - 1) / GEMV_WARPS;  // lanes a warp (1 or 2)
-  const int part_ = wpl > 1 ? warp % wpl : 0;
-  const int lo = (n4 * part_) / wpl, hi = (n4 * (part_ + 1)) / wpl;
-  const int c4_0 = lo + l32;
-  const int count = c4_0 < hi ? (hi - c4_0 + 31) >> 5 : 0;  // items of this thread per slot
+  while (wpl * 2 * K <= WARPS) wpl *= 2;
+  const int n_slots = (K + WARPS - 1) / WARPS;  // lanes a warp (1 or 2)
+  const int w_local = wpl > 1 ? warp % wpl : 0;
+  const int count = w_local < nparts ? (nparts - w_local + wpl - 1) / wpl : 0;  // parts of this warp per slot
+  const int c4_0 = w_local * 32 + l32, c4_step = 32 * wpl;
+  const int step = 2 * wpl * stage_chunk_words(MODE);  // stage words between consecutive parts of this warp
   const float4 *__restrict__ x4 = reinterpret_cast<const float4 *>(a.x);
   const float4 *__restrict__ p4 = reinterpret_cast<const float4 *>(a.p);
   const float4 *__restrict__ wr4 = reinterpret_cast<const float4 *>(a.w_res);
@@ -219,10 +233,10 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
 
   int jj[2];
   bool live[2];
-  int wh0[2], wl0[2], wh2[2], wl2[2];  // word offsets of item 0: columns c, c + 1 (hi, lo) and c + 2, c + 3
+  int wh0[2], wl0[2], wh2[2], wl2[2];  // word offsets of part w_local: columns c, c + 1 (hi, lo) and c + 2, c + 3
 #pragma unroll
   for (int slot = 0; slot < 2; ++slot) {
-    jj[slot] = wpl > 1 ? warp / wpl : warp + slot * GEMV_WARPS;
+    jj[slot] = wpl > 1 ? warp / wpl : warp + slot * WARPS;
     live[slot] = slot < n_slots && jj[slot] < K;
     const int c = c4_0 * 4;
     wh0[slot] = stage_word(jj[slot], c, 0, MODE);
@@ -232,13 +246,13 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
   }
 
   float4 X[B], Pv[B], WR[B], WI[B];
-  float ssq[2] = {0.0f, 0.0f}, amax[2] = {0.0f, 0.0f};
+  float amax_acc[2] = {0.0f, 0.0f};  // magnitudes need no fixed order: one max per thread
   auto load = [&](int slot, int i0) {
     const int j = jj[slot];
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      if (i0 + b < count) {
-        const int c4 = c4_0 + 32 * (i0 + b);
+      const int c4 = c4_0 + c4_step * (i0 + b);
+      if (i0 + b < count && c4 < n4) {
         X[b] = x4[(size_t)j * xs4 + c4];
         if (RES) {
           Pv[b] = p4[(size_t)j * ps4 + c4];
@@ -253,36 +267,44 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     const float sp = RES ? scr[SCR_SHRINK_P + j] : 0.0f;
 #pragma unroll
     for (int b = 0; b < B; ++b) {
-      if (i0 + b < count) {
-        const int i = i0 + b;
-        float4 y = X[b];
-        if (RES) {
-          // app_core.c:11690-11740: x += norm(p) * w, then the layer gain
-          y.x = y.x + Pv[b].x * sp * WR[b].x;
-          y.y = y.y + Pv[b].y * sp * WR[b].y;
-          y.z = y.z + Pv[b].z * sp * WR[b].z;
-          y.w = y.w + Pv[b].w * sp * WR[b].w;
-          if (gain != 1.0f) {
-            y.x *= gain;
-            y.y *= gain;
-            y.z *= gain;
-            y.w *= gain;
+      const int i = i0 + b;
+      if (i < count) {  // warp-uniform: the part's sums are warp reductions
+        const int c4 = c4_0 + c4_step * i;
+        float ssq = 0.0f;
+        if (c4 < n4) {
+          float4 y = X[b];
+          if (RES) {
+            // app_core.c:11690-11740: x += norm(p) * w, then the layer gain
+            y.x = y.x + Pv[b].x * sp * WR[b].x;
+            y.y = y.y + Pv[b].y * sp * WR[b].y;
+            y.z = y.z + Pv[b].z * sp * WR[b].z;
+            y.w = y.w + Pv[b].w * sp * WR[b].w;
+            if (gain != 1.0f) {
+              y.x *= gain;
+              y.y *= gain;
+              y.z *= gain;
+              y.w *= gain;
+            }
+            if (write_x) reinterpret_cast<float4 *>(a.x_out)[(size_t)j * xs4 + c4] = y;
           }
-          if (write_x) reinterpret_cast<float4 *>(a.x_out)[(size_t)j * xs4 + c4_0 + 32 * i] = y;
+          if (NRM) {
+            ssq = y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
+            y.x *= WI[b].x;
+            y.y *= WI[b].y;
+            y.z *= WI[b].z;
+            y.w *= WI[b].w;
+          }
+          amax_acc[slot] = fmaxf(amax_acc[slot], fmax4(y));
+          const int o = step * i;
+          stage[wh0[slot] + o] = __float_as_uint(y.x);
+          stage[wl0[slot] + o] = __float_as_uint(y.y);
+          stage[wh2[slot] + o] = __float_as_uint(y.z);
+          stage[wl2[slot] + o] = __float_as_uint(y.w);
         }
-        if (PRO != PRO_F32) ssq[slot] += y.x * y.x + y.y * y.y + y.z * y.z + y.w * y.w;
-        if (NRM) {
-          y.x *= WI[b].x;
-          y.y *= WI[b].y;
-          y.z *= WI[b].z;
-          y.w *= WI[b].w;
+        if (NRM) {  // a norm's sum of squares: one fixed tree per part
+          ssq = warp_sum(ssq);
+          if (l32 == 0) scr[SCR_SSQ + j * GEMV_MAX_PARTS + w_local + wpl * i] = ssq;
         }
-        amax[slot] = fmaxf(amax[slot], fmax4(y));
-        const int o = step * i;
-        stage[wh0[slot] + o] = __float_as_uint(y.x);
-        stage[wl0[slot] + o] = __float_as_uint(y.y);
-        stage[wh2[slot] + o] = __float_as_uint(y.z);
-        stage[wl2[slot] + o] = __float_as_uint(y.w);
       }
     }
   };
@@ -296,7 +318,7 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     __syncthreads();
     if (threadIdx.x < 16 && (int)threadIdx.x < K) {
       float u = 0.0f;
-      for (int q = 0; q < 16; ++q) u += scr[SCR_STRIPE + q * 16 + threadIdx.x];
+      for (int q = 0; q < STRIPES; ++q) u += scr[SCR_STRIPE + q * 16 + threadIdx.x];
       scr[SCR_SHRINK_P + threadIdx.x] = rms_shrink(u, cols, a.eps);
     }
     __syncthreads();
@@ -313,26 +335,25 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
   }
 #pragma unroll
   for (int slot = 0; slot < 2; ++slot) {
-    if (slot >= n_slots) continue;
-    const float s_ = warp_sum(ssq[slot]);
-    const float m_ = warp_max(amax[slot]);
-    if (l32 == 0 && jj[slot] < K) {
-      scr[SCR_SSQ + jj[slot] * 8 + part_] = s_;
-      scr[SCR_AMAX + jj[slot] * 8 + part_] = m_;
-    }
+    if (!live[slot]) continue;
+    const float m_ = warp_max(amax_acc[slot]);
+    if (l32 == 0) scr[SCR_AMAX + jj[slot] * 16 + w_local] = m_;
   }
   __syncthreads();
-  if (threadIdx.x < 16 && (int)threadIdx.x < K) {
-    const int j = threadIdx.x;
-    float s_ = 0.0f, m_ = 0.0f;
-    for (int q = 0; q < wpl; ++q) {
-      s_ += scr[SCR_SSQ + j * 8 + q];
-      m_ = fmaxf(m_, scr[SCR_AMAX + j * 8 + q]);
+  // per lane, the parts' sums in a fixed tree: scale and norm factor
+  for (int j = warp; j < K; j += WARPS) {
+    float s_ = 0.0f;
+    if (NRM) {
+      const float *ps = scr + SCR_SSQ + j * GEMV_MAX_PARTS;
+      s_ = warp_sum((l32 < nparts ? ps[l32] : 0.0f) + (l32 + 32 < nparts ? ps[l32 + 32] : 0.0f));
     }
-    const float sc = lane_scale(m_);
-    const float shrink = NRM ? rms_shrink(s_, cols, a.eps) : 1.0f;
-    scr[SCR_SCALE + j] = sc;
-    scr[SCR_FACTOR + j] = shrink * (1.0f / sc);
+    const float m_ = warp_max(l32 < wpl ? scr[SCR_AMAX + j * 16 + l32] : 0.0f);
+    if (l32 == 0) {
+      const float sc = lane_scale(m_);
+      const float shrink = NRM ? rms_shrink(s_, cols, a.eps) : 1.0f;
+      scr[SCR_SCALE + j] = sc;
+      scr[SCR_FACTOR + j] = shrink * (1.0f / sc);
+    }
   }
   __syncthreads();
   // second pass over the same words: scaled, split into hi/lo f16 pairs
@@ -342,9 +363,11 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     const float sc = scr[SCR_SCALE + jj[slot]];
 #pragma unroll 4
     for (int i = 0; i < count; ++i) {
-      const int o = step * i;
-      seal_words(stage, wh0[slot] + o, wl0[slot] + o, sc);
-      seal_words(stage, wh2[slot] + o, wl2[slot] + o, sc);
+      if (c4_0 + c4_step * i < n4) {
+        const int o = step * i;
+        seal_words(stage, wh0[slot] + o, wl0[slot] + o, sc);
+        seal_words(stage, wh2[slot] + o, wl2[slot] + o, sc);
+      }
     }
   }
   __syncthreads();

@@ -66,8 +66,8 @@ __global__ void repack_kernel(const uint8_t *code, size_t row_stride, const uint
 // private ring of `depth` shared-memory slots filled by bulk copies that lane
 // 0 issues; the first pieces are in flight before the kernel waits for the
 // kernel ahead of it and before the activation prologue runs.
-template <int MODE, int PAIR, int PRO, int EPI>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
+template <int MODE, int WARPS, int PAIR, int PRO, int EPI>
+__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
   constexpr int NT = MODE == MODE_NT2 ? 2 : 1;
   constexpr int H = PAIR + 1;
   constexpr int ACC = MODE == MODE_PACK ? 4 : 8 * NT;
@@ -80,12 +80,12 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
 
   const int warp = threadIdx.x >> 5, lane32 = threadIdx.x & 31;
   const int g = lane32 >> 2, t = lane32 & 3;
-  const int S = a.split, G = GEMV_WARPS / S, grp = warp / S, slice = warp % S;
+  const int S = a.split, G = WARPS / S, grp = warp / S, slice = warp % S;
   const int n_cc = a.pl.n_cc;
   const int c_lo = (n_cc * slice) / S, c_hi = (n_cc * (slice + 1)) / S;
   const int n_units = PAIR ? a.pl.n_rb / 2 : a.pl.n_rb;
-  const int Q = gridDim.x * G, q = blockIdx.x * G + grp;
-  const int my_units = q < n_units ? (n_units - q + Q - 1) / Q : 0;
+  const int Q = a.slots, q = blockIdx.x * G + grp;
+  const int my_units = (q < n_units && q < Q) ? (n_units - q + Q - 1) / Q : 0;
   const int P = a.piece, D = a.depth;
   const int np = (c_hi - c_lo + P - 1) / P;  // pieces a unit
   const int n_pieces = my_units * np;
@@ -130,7 +130,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         mul_pre[nt][i] = ok ? a.aux[(size_t)ln * a.aux_stride + row] : 0.0f;
       }
   }
-  gemv_prologue<PRO, MODE>(a, stage, scr);
+  gemv_prologue<PRO, MODE, WARPS>(a, stage, scr);
   // the next kernel may start (and fetch its weights) once this one is past
   // its own wait: released any earlier, kernels still waiting would release
   // the ones after them and pile up on the SMs
@@ -273,18 +273,24 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         if (g == 0) red[warp * 16 + ln] = (MODE == MODE_PACK && t >= 2) ? 0.0f : v;
       }
     __syncthreads();
-    if (threadIdx.x < NT * 8) {
-      float v = 0.0f;
-      for (int w = 0; w < GEMV_WARPS; ++w) v += red[w * 16 + threadIdx.x];
-      a.out_ssq[blockIdx.x * 16 + threadIdx.x] = v;
+    // one partial per virtual 8-warp block: warps 8h .. 8h + 7
+    const int n_vb = (Q + a.vgroups - 1) / a.vgroups;
+    if (threadIdx.x < (WARPS / 8) * 16) {
+      const int h = threadIdx.x >> 4, ln = threadIdx.x & 15;
+      const int vb = blockIdx.x * (WARPS / 8) + h;
+      if (ln < NT * 8 && vb < n_vb) {
+        float v = 0.0f;
+        for (int w = 8 * h; w < 8 * h + 8; ++w) v += red[w * 16 + ln];
+        a.out_ssq[vb * 16 + ln] = v;
+      }
     }
   }
 
   if (EPI == EPI_LOGITS) {
     // reduce across the 8 thread groups that hold the same lanes, then across
     // the warps of the block; block partials go to part_val / part_idx
-    __shared__ float bv[GEMV_WARPS][16];
-    __shared__ int bi[GEMV_WARPS][16];
+    __shared__ float bv[GEMV_MAX_WARPS][16];
+    __shared__ int bi[GEMV_MAX_WARPS][16];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -306,19 +312,24 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_kernel(GemvArgs a) {
         }
       }
     __syncthreads();
-    if (threadIdx.x < NT * 8) {
-      float v = bv[0][threadIdx.x];
-      int i = bi[0][threadIdx.x];
-      for (int w = 1; w < GEMV_WARPS; ++w) {
-        float ov = bv[w][threadIdx.x];
-        int oi = bi[w][threadIdx.x];
-        if (ov > v || (ov == v && oi < i)) {
-          v = ov;
-          i = oi;
+    const int n_vb = (Q + a.vgroups - 1) / a.vgroups;
+    if (threadIdx.x < (WARPS / 8) * 16) {
+      const int h = threadIdx.x >> 4, ln = threadIdx.x & 15;
+      const int vb = blockIdx.x * (WARPS / 8) + h;
+      if (ln < NT * 8 && vb < n_vb) {
+        float v = bv[8 * h][ln];
+        int i = bi[8 * h][ln];
+        for (int w = 8 * h + 1; w < 8 * h + 8; ++w) {
+          float ov = bv[w][ln];
+          int oi = bi[w][ln];
+          if (ov > v || (ov == v && oi < i)) {
+            v = ov;
+            i = oi;
+          }
         }
+        a.part_val[vb * 16 + ln] = v;
+        a.part_idx[vb * 16 + ln] = i;
       }
-      a.part_val[blockIdx.x * 16 + threadIdx.x] = v;
-      a.part_idx[blockIdx.x * 16 + threadIdx.x] = i;
     }
   }
 }
@@ -928,15 +939,15 @@ struct GemvLayout {
   size_t red, bars, ring, total;
 };
 
-static GemvLayout gemv_layout(const GemvArgs &a, int pair, int P, int D) {
+static GemvLayout gemv_layout(const GemvArgs &a, int pair, int W, int P, int D) {
   const int MODE = gemv_mode(a.lanes), H = pair + 1;
   GemvLayout L;
   L.red = align128(gemv_stage_bytes(a.pl.n_cc, MODE) + SCR_FLOATS * 4);
-  size_t red_floats = a.split > 1 ? (size_t)GEMV_THREADS * H * gemv_acc_floats(MODE) : 0;
-  if (red_floats < (size_t)GEMV_WARPS * 16) red_floats = (size_t)GEMV_WARPS * 16;
+  size_t red_floats = a.split > 1 ? (size_t)W * 32 * H * gemv_acc_floats(MODE) : 0;
+  if (red_floats < (size_t)W * 16) red_floats = (size_t)W * 16;
   L.bars = align128(L.red + red_floats * 4);
-  L.ring = align128(L.bars + (size_t)GEMV_WARPS * D * 8);
-  L.total = L.ring + (size_t)GEMV_WARPS * D * H * P * GEMV_PIECE_BYTES;
+  L.ring = align128(L.bars + (size_t)W * D * 8);
+  L.total = L.ring + (size_t)W * D * H * P * GEMV_PIECE_BYTES;
   return L;
 }
 
@@ -944,14 +955,14 @@ static GemvLayout gemv_layout(const GemvArgs &a, int pair, int P, int D) {
 // piece a warp will take in flight at once when they fit (one piece a unit),
 // else four pieces in flight of as many chunks as fit.  Fills the layout
 // fields of `a`; false when not even one chunk a warp fits.
-static bool gemv_fit(GemvArgs &a, int pair, int grid, size_t smem_limit, size_t *smem) {
-  const int H = pair + 1, S = a.split, G = GEMV_WARPS / S;
+static bool gemv_fit(GemvArgs &a, int pair, int W, int grid, size_t smem_limit, size_t *smem) {
+  const int H = pair + 1, S = a.split, G = W / S;
   const int slen = (a.pl.n_cc + S - 1) / S;
   const int n_units = pair ? a.pl.n_rb / 2 : a.pl.n_rb;
   const int per_slot = (n_units + grid * G - 1) / (grid * G);
-  const GemvLayout base = gemv_layout(a, pair, 0, GEMV_MAX_DEPTH);
+  const GemvLayout base = gemv_layout(a, pair, W, 0, GEMV_MAX_DEPTH);
   if (base.ring >= smem_limit) return false;
-  const long per_warp = (long)(smem_limit - base.ring) / (GEMV_WARPS * H * GEMV_PIECE_BYTES);
+  const long per_warp = (long)(smem_limit - base.ring) / (W * H * GEMV_PIECE_BYTES);
   if (per_warp < 1) return false;
   int P, D;
   if ((long)per_slot * slen <= per_warp && per_slot <= GEMV_MAX_DEPTH) {
@@ -966,7 +977,7 @@ static bool gemv_fit(GemvArgs &a, int pair, int grid, size_t smem_limit, size_t 
   }
   a.piece = P;
   a.depth = D;
-  const GemvLayout L = gemv_layout(a, pair, P, D);
+  const GemvLayout L = gemv_layout(a, pair, W, P, D);
   a.off_red = (int)L.red;
   a.off_bars = (int)L.bars;
   a.off_ring = (int)L.ring;
@@ -974,10 +985,10 @@ static bool gemv_fit(GemvArgs &a, int pair, int grid, size_t smem_limit, size_t 
   return L.total <= smem_limit;
 }
 
-template <int MODE, int PAIR>
+template <int MODE, int WARPS, int PAIR>
 static cudaError_t launch_gemv_pe(const GemvArgs &a, int pro, int epi, int grid, size_t smem, cudaStream_t st) {
 #define IGC_CASE(P, E) \
-  if (pro == P && epi == E) return launch_k(gemv_kernel<MODE, PAIR, P, E>, dim3(grid), dim3(GEMV_THREADS), smem, st, a);
+  if (pro == P && epi == E) return launch_k(gemv_kernel<MODE, WARPS, PAIR, P, E>, dim3(grid), dim3(WARPS * 32), smem, st, a);
   if constexpr (PAIR) {
     IGC_CASE(PRO_RESID_NORM, EPI_GELU_PAIR)
     IGC_CASE(PRO_NORM, EPI_GELU_PAIR)
@@ -1010,11 +1021,11 @@ static cudaError_t allow_smem_fn(F *fn, int bytes) {
   return e;
 }
 
-template <int MODE>
+template <int MODE, int WARPS>
 static cudaError_t allow_smem_mode(int bytes) {
   cudaError_t e = cudaSuccess;
 #define IGC_ALLOW(PAIR, P, E) \
-  if (e == cudaSuccess) e = allow_smem_fn(gemv_kernel<MODE, PAIR, P, E>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(gemv_kernel<MODE, WARPS, PAIR, P, E>, bytes);
   IGC_ALLOW(1, PRO_RESID_NORM, EPI_GELU_PAIR)
   IGC_ALLOW(1, PRO_NORM, EPI_GELU_PAIR)
   IGC_ALLOW(1, PRO_F32, EPI_GELU_PAIR)
@@ -1043,9 +1054,11 @@ cudaError_t igc_kernels_configure(int bytes) {
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) return e;
   if (bytes > optin) bytes = optin;
-  e = allow_smem_mode<MODE_PACK>(bytes);
-  if (e == cudaSuccess) e = allow_smem_mode<MODE_NT1>(bytes);
-  if (e == cudaSuccess) e = allow_smem_mode<MODE_NT2>(bytes);
+  e = allow_smem_mode<MODE_PACK, 16>(bytes);
+  if (e == cudaSuccess) e = allow_smem_mode<MODE_PACK, 8>(bytes);
+  if (e == cudaSuccess) e = allow_smem_mode<MODE_NT1, 16>(bytes);
+  if (e == cudaSuccess) e = allow_smem_mode<MODE_NT1, 8>(bytes);
+  if (e == cudaSuccess) e = allow_smem_mode<MODE_NT2, 8>(bytes);
   if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<1>, bytes);
   if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<2>, bytes);
   if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<4>, bytes);
@@ -1066,25 +1079,50 @@ cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint
 
 void igc_kernels_pdl(int on) { g_pdl = on; }
 
-cudaError_t igc_launch_gemv(GemvArgs *a, int pair, int pro, int epi, int grid, size_t smem_limit, cudaStream_t st) {
-  size_t smem = 0;
-  if (!gemv_fit(*a, pair, grid, smem_limit, &smem)) return cudaErrorInvalidValue;
-  switch (gemv_mode(a->lanes)) {
-    case MODE_PACK:
-      return pair ? launch_gemv_pe<MODE_PACK, 1>(*a, pro, epi, grid, smem, st)
-                  : launch_gemv_pe<MODE_PACK, 0>(*a, pro, epi, grid, smem, st);
-    case MODE_NT1:
-      return pair ? launch_gemv_pe<MODE_NT1, 1>(*a, pro, epi, grid, smem, st)
-                  : launch_gemv_pe<MODE_NT1, 0>(*a, pro, epi, grid, smem, st);
-    default:
-      return pair ? launch_gemv_pe<MODE_NT2, 1>(*a, pro, epi, grid, smem, st)
-                  : launch_gemv_pe<MODE_NT2, 0>(*a, pro, epi, grid, smem, st);
+cudaError_t igc_launch_gemv(GemvArgs *a, int pair, int pro, int epi, int grid, size_t smem_limit, cudaStream_t st,
+                            int *grid_used) {
+  if (a->pl.cols > GEMV_MAX_PARTS * 128) return cudaErrorInvalidValue;  // wider than the prologue's parts
+  const int mode = gemv_mode(a->lanes);
+  const int units = pair ? a->pl.n_rb / 2 : a->pl.n_rb;
+  const int G8 = GEMV_WARPS / a->split;
+  // 16-warp blocks where the mode allows them and their shared memory fits
+  int W = GEMV_WARPS;
+  if (mode != MODE_NT2 && gemv_layout(*a, pair, 16, 0, GEMV_MAX_DEPTH).ring + (size_t)16 * (pair + 1) * GEMV_PIECE_BYTES <=
+                              smem_limit)
+    W = 16;
+  const int G = W / a->split;
+  if (a->out_ssq) {
+    // the planned 8-warp slots exactly, whatever the block width, so the
+    // sums-of-squares partials group the same rows in every lane mode
+    a->slots = grid * G8;
+    grid = (a->slots + G - 1) / G;
+  } else {
+    if (grid > (units + G - 1) / G) grid = (units + G - 1) / G;
+    if (grid < 1) grid = 1;
+    a->slots = grid * G;
   }
+  a->vgroups = G8;
+  if (grid_used) *grid_used = (a->slots + G8 - 1) / G8;  // partials written: one a virtual 8-warp block
+  size_t smem = 0;
+  if (!gemv_fit(*a, pair, W, grid, smem_limit, &smem)) return cudaErrorInvalidValue;
+  if (mode == MODE_PACK)
+    return W == 16 ? (pair ? launch_gemv_pe<MODE_PACK, 16, 1>(*a, pro, epi, grid, smem, st)
+                           : launch_gemv_pe<MODE_PACK, 16, 0>(*a, pro, epi, grid, smem, st))
+                   : (pair ? launch_gemv_pe<MODE_PACK, 8, 1>(*a, pro, epi, grid, smem, st)
+                           : launch_gemv_pe<MODE_PACK, 8, 0>(*a, pro, epi, grid, smem, st));
+  if (mode == MODE_NT1)
+    return W == 16 ? (pair ? launch_gemv_pe<MODE_NT1, 16, 1>(*a, pro, epi, grid, smem, st)
+                           : launch_gemv_pe<MODE_NT1, 16, 0>(*a, pro, epi, grid, smem, st))
+                   : (pair ? launch_gemv_pe<MODE_NT1, 8, 1>(*a, pro, epi, grid, smem, st)
+                           : launch_gemv_pe<MODE_NT1, 8, 0>(*a, pro, epi, grid, smem, st));
+  return pair ? launch_gemv_pe<MODE_NT2, 8, 1>(*a, pro, epi, grid, smem, st)
+              : launch_gemv_pe<MODE_NT2, 8, 0>(*a, pro, epi, grid, smem, st);
 }
 
-// The smallest ring: one chunk a warp, with room for the deepest barriers.
+// The smallest ring of the narrowest block: one chunk a warp, with room for
+// the deepest barriers.
 size_t igc_gemv_smem_min(const GemvArgs *a, int pair) {
-  return gemv_layout(*a, pair, 0, GEMV_MAX_DEPTH).ring + (size_t)GEMV_WARPS * (pair + 1) * GEMV_PIECE_BYTES;
+  return gemv_layout(*a, pair, GEMV_WARPS, 0, GEMV_MAX_DEPTH).ring + (size_t)GEMV_WARPS * (pair + 1) * GEMV_PIECE_BYTES;
 }
 
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,

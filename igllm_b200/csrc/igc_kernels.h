@@ -17,11 +17,13 @@ cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint
 // Launches from the calling thread may overlap the kernel ahead of them
 // (programmatic dependent launch) while `on` is set.
 void igc_kernels_pdl(int on);
-// Picks the weight ring for `grid` blocks within `smem_limit` bytes of shared
-// memory (filling a->piece, a->depth and the layout offsets) and launches;
-// cudaErrorInvalidValue when the lanes' staging leaves no room for it.
+// Launches at most `grid` blocks (fewer when the lane mode's wider blocks
+// need fewer; the count used goes to *grid_used), picking the weight ring
+// within `smem_limit` bytes of shared memory (filling a->piece, a->depth and
+// the layout offsets); cudaErrorInvalidValue when the lanes' staging leaves
+// no room for it.
 cudaError_t igc_launch_gemv(igc::GemvArgs *a, int pair, int pro, int epi, int grid, size_t smem_limit,
-                            cudaStream_t st);
+                            cudaStream_t st, int *grid_used);
 // Shared memory the smallest ring needs.
 size_t igc_gemv_smem_min(const igc::GemvArgs *a, int pair);
 

@@ -802,6 +802,7 @@ struct igc_session {
   int max_chunks = 0;   // chunks the longest span can cover
   int use_graphs = 1;
   int use_pdl = 1;
+  int head_parts = 0;  // argmax partials the output head's launch left
   cudaGraphExec_t graph[IGC_LANE_LIMIT + 1][2] = {};
   double serve_seconds = 0.0;
   size_t serve_tokens = 0;
@@ -1004,8 +1005,11 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   a.part_idx = s->arg_idx;
   a.err = s->d_err;
   const int pair = pl.pair ? 1 : 0;
+  int used = pl.grid;  // blocks the launch took: the partials it leaves
   if (igc_gemv_smem_min(&a, pair) <= (size_t)s->m->smem_limit) {
-    CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st));
+    CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
+    if (out_ssq) out_ssq->parts = used;
+    if (epi == EPI_LOGITS) s->head_parts = used;
     return IGC_OKAY;
   }
   // Too wide to stage sixteen lanes at once (the 6144-column down
@@ -1021,7 +1025,8 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
     b.aux = aux ? aux + (size_t)j0 * aux_stride : nullptr;
     b.out_ssq = a.out_ssq ? a.out_ssq + j0 : nullptr;
     if (igc_gemv_smem_min(&b, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
-    CKL(igc_launch_gemv(&b, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st));
+    CKL(igc_launch_gemv(&b, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
+    if (out_ssq) out_ssq->parts = used;
   }
   return IGC_OKAY;
 }
@@ -1135,7 +1140,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
                  s->logits, m->vocab, 1.0f, nullptr, 0, pend_ssq, nullptr);
     if (c != IGC_OKAY) return c;
     prof_mark(s, PROF_OTHER, 0.0);
-    CKL(igc_launch_argmax(s->arg_val, s->arg_idx, m->head.grid, K, s->d_top, s->st));
+    CKL(igc_launch_argmax(s->arg_val, s->arg_idx, s->head_parts, K, s->d_top, s->st));
   }
   prof_mark(s, PROF_END, 0.0);
   return IGC_OKAY;
