@@ -265,3 +265,28 @@ def test_e2b_shape_against_oracle(igc_lib, igo_mod):
     _check_rows(s.guess(blk), o.guess(blk))
     s.guess_keep(1)
     o.guess_keep(1)
+
+
+def test_lane_batching_is_bit_identical(igc_lib, small_dir):
+    """A position's logits do not depend on how many lanes shared its pass:
+    one lane at a time (the packed four-lane mode), one nine-lane block (two
+    8-lane tiles, 8-warp blocks) and blocks of four and five lanes (16-warp
+    blocks) give the same bits, which is what lets a greedy stream with
+    guessing equal the stream without it exactly."""
+    m = igc_lib.Model(folder=small_dir, window_limit=SMALL["window_limit"])
+    ids = np.array([3, 17, 29, 5, 8, 41, 77, 90, 12, 13, 14, 15, 16, 7, 9, 100, 200, 300, 11, 2, 4, 6, 8, 10,
+                    12, 14, 16, 18, 20], np.int32)
+    block = ids[19:28]
+    a = igc_lib.Session(m)
+    a.prime(ids[:20])
+    stepped = np.stack([a.step(t)[1] for t in block])
+    b = igc_lib.Session(m)
+    b.prime(ids[:20])
+    nine = b.guess(block)
+    c = igc_lib.Session(m)
+    c.prime(ids[:20])
+    four = c.guess(block[:4])
+    c.guess_keep(4)
+    five = c.guess(block[4:])
+    assert np.array_equal(stepped, nine)
+    assert np.array_equal(stepped, np.concatenate([four, five]))
