@@ -414,13 +414,14 @@ __global__ void ple_finish_kernel(const float *raw, const float *seed, int lanes
 //
 // The span is cut into chunks whose boundaries sit at fixed multiples of the
 // session's chunk length, so a position's partial sums never depend on how
-// many lanes a pass carried.  A block takes one chunk and eight pairs, one
-// a warp.  Per 32-position tile, thread l of a warp scores position l (the
-// query read from shared memory by broadcast, the key row padded so the
-// warp's reads do not collide), the warp updates its online softmax, and
-// then thread l blends dimensions [l*DPL, (l+1)*DPL) of the values.
-// Partials per chunk go to attn_combine_kernel.
-constexpr int ATT_T = 32;        // positions a tile
+// many lanes a pass carried.  A block takes eight pairs, one a warp, and
+// walks chunks blockIdx.x, + gridDim.x, ...  Per 16-position tile, threads
+// l and l + 16 of a warp score position l over the two halves of the head
+// (the query read from shared memory by broadcast, the key row padded so the
+// warp's reads do not collide) and add their halves; the warp updates its
+// online softmax, and then thread l blends dimensions [l*DPL, (l+1)*DPL) of
+// the values.  Partials per chunk go to attn_combine_kernel.
+constexpr int ATT_T = 16;        // positions a tile
 constexpr int ATT_PAIRS = 8;     // (lane, head) pairs a block, one a warp
 constexpr int ATT_BLOCK_ROWS = 16;  // block positions a chunk can hold
 
@@ -503,8 +504,8 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   const int kv_w = kv_heads * HD, KS = kv_w + 4, half = HD / 2;
   extern __shared__ __align__(16) float sm[];
   float *qs = sm;                                // [8][HD]
-  float *ks = qs + ATT_PAIRS * HD;               // [32][KS]
-  float *vs = ks + (size_t)ATT_T * KS;           // [32][KS]
+  float *ks = qs + ATT_PAIRS * HD;               // [ATT_T][KS]
+  float *vs = ks + (size_t)ATT_T * KS;           // [ATT_T][KS]
   float *bk = vs + (size_t)ATT_T * KS;           // [16][KS] the block's new keys (owner layers)
   float *bv = bk + (size_t)ATT_BLOCK_ROWS * KS;  // [16][KS] and values
   const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -515,10 +516,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   const int hi_all = p0 + lanes;
   const int c_first = lo_all / chunk_len;
   const int n_chunks = (hi_all - 1) / chunk_len - c_first + 1;
-  const int cr = blockIdx.x;
-  if (cr >= n_chunks) return;
-  const int c = c_first + cr;
-  const int c_lo = max(c * chunk_len, lo_all), c_hi = min((c + 1) * chunk_len, hi_all);
+  if ((int)blockIdx.x >= n_chunks) return;
 
   // this warp's query, normed and turned at its lane's position
   const int pair = blockIdx.y * ATT_PAIRS + warp;
@@ -532,105 +530,109 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     head_norm_turn<DPL>(qv, q_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps, true, l);
     store_dpl<DPL>(qs + warp * HD + l * DPL, qv);
   }
-  // an owner layer's new keys and values that fall in this chunk: normed,
-  // turned (keys), kept in shared memory, and written to the cache once
-  int jb_lo = 0, jb_hi = 0;
-  if (owner) {
-    jb_lo = max(0, c * chunk_len - p0);
-    jb_hi = min(lanes, (c + 1) * chunk_len - p0);
-    const int per = 2 * kv_heads, items = max(0, jb_hi - jb_lo) * per;
-    for (int it = warp; it < items; it += ATT_PAIRS) {
-      const int jj = jb_lo + it / per, rest = it % per, kh = rest >> 1, is_v = rest & 1;
-      float v[DPL];
-      load_dpl<DPL>(qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + kh * HD + l * DPL, v);
-      const int pos = p0 + jj;
-      head_norm_turn<DPL>(v, is_v ? nullptr : k_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps,
-                          !is_v, l);
-      store_dpl<DPL>((is_v ? bv : bk) + (size_t)(jj - jb_lo) * KS + kh * HD + l * DPL, v);
-      if (blockIdx.y == 0) store_dpl<DPL>((is_v ? vc : kc) + (size_t)pos * kv_w + kh * HD + l * DPL, v);
-    }
-  }
-  // the pair this thread's lane of the warp scores: its lane's span
+  // the pair this warp scores: its lane's span
   const int lane_lo = sliding ? max(0, p0 + j - span + 1) : 0;
   const int lane_hi = p0 + j;
-
-  float m_run = -FLT_MAX, l_run = 0.0f, acc[DPL];
-#pragma unroll
-  for (int e = 0; e < DPL; ++e) acc[e] = 0.0f;
+  const int r_pos = l & (ATT_T - 1), hhalf = l >> 4;  // position and head half this thread scores
   const int w4 = kv_w / 4;
-  for (int tb = c * chunk_len; tb < c_hi; tb += ATT_T) {
-    if (tb + ATT_T <= c_lo) continue;
-    __syncthreads();  // the previous tile is consumed (and the query and block rows are written)
-    for (int i = threadIdx.x; i < ATT_T * w4; i += blockDim.x) {
-      const int r = i / w4, d4 = i - r * w4, pos = tb + r;
-      float *kd = ks + (size_t)r * KS + d4 * 4, *vd = vs + (size_t)r * KS + d4 * 4;
-      if (pos < c_lo || pos >= c_hi) {
-        *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
-      } else if (owner && pos - p0 >= jb_lo && pos - p0 < jb_hi) {
-        const int rb = pos - p0 - jb_lo;
-        *reinterpret_cast<float4 *>(kd) = *reinterpret_cast<const float4 *>(bk + (size_t)rb * KS + d4 * 4);
-        *reinterpret_cast<float4 *>(vd) = *reinterpret_cast<const float4 *>(bv + (size_t)rb * KS + d4 * 4);
-      } else {
-        cp_async16(kd, kc + (size_t)pos * kv_w + d4 * 4);
-        cp_async16(vd, vc + (size_t)pos * kv_w + d4 * 4);
+
+  for (int cr = blockIdx.x; cr < n_chunks; cr += gridDim.x) {
+    const int c = c_first + cr;
+    const int c_lo = max(c * chunk_len, lo_all), c_hi = min((c + 1) * chunk_len, hi_all);
+    __syncthreads();  // the previous chunk's block rows and tiles are consumed
+    // an owner layer's new keys and values that fall in this chunk: normed,
+    // turned (keys), kept in shared memory, and written to the cache once
+    int jb_lo = 0, jb_hi = 0;
+    if (owner) {
+      jb_lo = max(0, c * chunk_len - p0);
+      jb_hi = min(lanes, (c + 1) * chunk_len - p0);
+      const int per = 2 * kv_heads, items = max(0, jb_hi - jb_lo) * per;
+      for (int it = warp; it < items; it += ATT_PAIRS) {
+        const int jj = jb_lo + it / per, rest = it % per, kh = rest >> 1, is_v = rest & 1;
+        float v[DPL];
+        load_dpl<DPL>(qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + kh * HD + l * DPL, v);
+        const int pos = p0 + jj;
+        head_norm_turn<DPL>(v, is_v ? nullptr : k_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps,
+                            !is_v, l);
+        store_dpl<DPL>((is_v ? bv : bk) + (size_t)(jj - jb_lo) * KS + kh * HD + l * DPL, v);
+        if (blockIdx.y == 0) store_dpl<DPL>((is_v ? vc : kc) + (size_t)pos * kv_w + kh * HD + l * DPL, v);
       }
     }
-    asm volatile("cp.async.wait_all;\n" ::: "memory");
-    __syncthreads();
+
+    float m_run = -FLT_MAX, l_run = 0.0f, acc[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) acc[e] = 0.0f;
+    for (int tb = c * chunk_len; tb < c_hi; tb += ATT_T) {
+      if (tb + ATT_T <= c_lo) continue;
+      __syncthreads();  // the previous tile is consumed (and the query and block rows are written)
+      for (int i = threadIdx.x; i < ATT_T * w4; i += blockDim.x) {
+        const int r = i / w4, d4 = i - r * w4, pos = tb + r;
+        float *kd = ks + (size_t)r * KS + d4 * 4, *vd = vs + (size_t)r * KS + d4 * 4;
+        if (pos < c_lo || pos >= c_hi) {
+          *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+          *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else if (owner && pos - p0 >= jb_lo && pos - p0 < jb_hi) {
+          const int rb = pos - p0 - jb_lo;
+          *reinterpret_cast<float4 *>(kd) = *reinterpret_cast<const float4 *>(bk + (size_t)rb * KS + d4 * 4);
+          *reinterpret_cast<float4 *>(vd) = *reinterpret_cast<const float4 *>(bv + (size_t)rb * KS + d4 * 4);
+        } else {
+          cp_async16(kd, kc + (size_t)pos * kv_w + d4 * 4);
+          cp_async16(vd, vc + (size_t)pos * kv_w + d4 * 4);
+        }
+      }
+      asm volatile("cp.async.wait_all;\n" ::: "memory");
+      __syncthreads();
+      if (has) {
+        // scores: threads r and r + 16 take the two halves of position tb + r
+        const int pos = tb + r_pos;
+        const float4 *qr = reinterpret_cast<const float4 *>(qs + warp * HD + hhalf * (HD / 2));
+        const float4 *kr = reinterpret_cast<const float4 *>(ks + (size_t)r_pos * KS + kvoff + hhalf * (HD / 2));
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+        for (int d4 = 0; d4 < HD / 8; d4 += 2) {
+          const float4 q0 = qr[d4], k0 = kr[d4];
+          a0 = fmaf(q0.x, k0.x, a0); a0 = fmaf(q0.y, k0.y, a0); a0 = fmaf(q0.z, k0.z, a0); a0 = fmaf(q0.w, k0.w, a0);
+          if (d4 + 1 < HD / 8) {
+            const float4 q1 = qr[d4 + 1], k1 = kr[d4 + 1];
+            a1 = fmaf(q1.x, k1.x, a1); a1 = fmaf(q1.y, k1.y, a1); a1 = fmaf(q1.z, k1.z, a1); a1 = fmaf(q1.w, k1.w, a1);
+          }
+        }
+        const float part = a0 + a1;
+        const float other = __shfl_xor_sync(0xffffffffu, part, 16);
+        const float s = hhalf == 0 ? part + other : other + part;  // the same sum in both threads
+        const bool valid = pos >= c_lo && pos < c_hi && pos >= lane_lo && pos <= lane_hi;
+        const float sc = valid ? s : -FLT_MAX;
+        // online softmax over the tile's 16 positions (each held twice)
+        const float m_new = fmaxf(m_run, warp_max(sc));
+        const float f = (m_new == -FLT_MAX) ? 1.0f : (m_run == -FLT_MAX ? 0.0f : expf(m_run - m_new));
+        const float pe = valid ? expf(sc - m_new) : 0.0f;
+        float psum = pe;
+#pragma unroll
+        for (int o = 1; o < ATT_T; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
+        l_run = l_run * f + psum;
+        m_run = m_new;
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) acc[e] *= f;
+        // blend: thread l takes dimensions [l*DPL, (l+1)*DPL) of every position
+        const float *vcol = vs + kvoff + l * DPL;
+#pragma unroll 4
+        for (int r = 0; r < ATT_T; ++r) {
+          const float pr = __shfl_sync(0xffffffffu, pe, r);
+          float vv[DPL];
+          load_dpl<DPL>(vcol + (size_t)r * KS, vv);
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) acc[e] = fmaf(pr, vv[e], acc[e]);
+        }
+      }
+    }
     if (has) {
-      // scores: thread l takes position tb + l
-      const int pos = tb + l;
-      const float4 *qr = reinterpret_cast<const float4 *>(qs + warp * HD);
-      const float4 *kr = reinterpret_cast<const float4 *>(ks + (size_t)l * KS + kvoff);
-      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 4
-      for (int d4 = 0; d4 < HD / 4; d4 += 4) {
-        float4 q0 = qr[d4], k0 = kr[d4];
-        a0 = fmaf(q0.x, k0.x, a0); a0 = fmaf(q0.y, k0.y, a0); a0 = fmaf(q0.z, k0.z, a0); a0 = fmaf(q0.w, k0.w, a0);
-        if (d4 + 1 < HD / 4) {
-          float4 q1 = qr[d4 + 1], k1 = kr[d4 + 1];
-          a1 = fmaf(q1.x, k1.x, a1); a1 = fmaf(q1.y, k1.y, a1); a1 = fmaf(q1.z, k1.z, a1); a1 = fmaf(q1.w, k1.w, a1);
-        }
-        if (d4 + 2 < HD / 4) {
-          float4 q2 = qr[d4 + 2], k2 = kr[d4 + 2];
-          a2 = fmaf(q2.x, k2.x, a2); a2 = fmaf(q2.y, k2.y, a2); a2 = fmaf(q2.z, k2.z, a2); a2 = fmaf(q2.w, k2.w, a2);
-        }
-        if (d4 + 3 < HD / 4) {
-          float4 q3 = qr[d4 + 3], k3 = kr[d4 + 3];
-          a3 = fmaf(q3.x, k3.x, a3); a3 = fmaf(q3.y, k3.y, a3); a3 = fmaf(q3.z, k3.z, a3); a3 = fmaf(q3.w, k3.w, a3);
-        }
+      const size_t slot = ((size_t)cr * 16 + j) * heads + h;
+      if (l == 0) {
+        part_ml[slot * 2 + 0] = m_run;
+        part_ml[slot * 2 + 1] = l_run;
       }
-      const float s = (a0 + a1) + (a2 + a3);
-      const bool valid = pos >= c_lo && pos < c_hi && pos >= lane_lo && pos <= lane_hi;
-      const float sc = valid ? s : -FLT_MAX;
-      // online softmax over the warp's 32 positions
-      const float m_new = fmaxf(m_run, warp_max(sc));
-      const float f = (m_new == -FLT_MAX) ? 1.0f : (m_run == -FLT_MAX ? 0.0f : expf(m_run - m_new));
-      const float pe = valid ? expf(sc - m_new) : 0.0f;
-      l_run = l_run * f + warp_sum(pe);
-      m_run = m_new;
-#pragma unroll
-      for (int e = 0; e < DPL; ++e) acc[e] *= f;
-      // blend: thread l takes dimensions [l*DPL, (l+1)*DPL) of every position
-      const float *vcol = vs + kvoff + l * DPL;
-#pragma unroll 4
-      for (int r = 0; r < ATT_T; ++r) {
-        const float pr = __shfl_sync(0xffffffffu, pe, r);
-        float vv[DPL];
-        load_dpl<DPL>(vcol + (size_t)r * KS, vv);
-#pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[e] = fmaf(pr, vv[e], acc[e]);
-      }
+      store_dpl<DPL>(part_acc + slot * HD + l * DPL, acc);
     }
-  }
-  if (has) {
-    const size_t slot = ((size_t)cr * 16 + j) * heads + h;
-    if (l == 0) {
-      part_ml[slot * 2 + 0] = m_run;
-      part_ml[slot * 2 + 1] = l_run;
-    }
-    store_dpl<DPL>(part_acc + slot * HD + l * DPL, acc);
   }
 }
 

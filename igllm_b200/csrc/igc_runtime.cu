@@ -798,7 +798,7 @@ struct igc_session {
   float *h_top_v = nullptr;
   int *h_top_i = nullptr;
   int logit_lanes = 0;  // rows the last pass left in `logits`
-  int chunk_len = 32;   // attention chunk length, fixed for the session
+  int chunk_len = 16;   // attention chunk length, fixed for the session
   int max_chunks = 0;   // chunks the longest span can cover
   int use_graphs = 1;
   int use_pdl = 1;
@@ -883,9 +883,9 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (c == IGC_OKAY) c = s->alloc(&s->pa, (size_t)K * (m->ple_dim ? m->ple_dim : 1));
   if (c == IGC_OKAY) c = s->alloc(&s->pp, (size_t)K * H);
   if (c == IGC_OKAY) c = s->alloc(&s->logits, (size_t)K * m->vocab);
-  // attention chunks: a power of two of at least 32 positions, at most 128
+  // attention chunks: a power of two of at least 16 positions, at most 256
   // of them over the window, so the partials stay a few tens of MB
-  while ((m->window_limit + s->chunk_len - 1) / s->chunk_len > 128) s->chunk_len *= 2;
+  while ((m->window_limit + s->chunk_len - 1) / s->chunk_len > 256) s->chunk_len *= 2;
   s->max_chunks = (m->window_limit + s->chunk_len - 1) / s->chunk_len + 2;
   if (c == IGC_OKAY) c = s->alloc(&s->part_ml, (size_t)s->max_chunks * K * m->heads * 2);
   if (c == IGC_OKAY) c = s->alloc(&s->part_acc, (size_t)s->max_chunks * K * m->max_q);
@@ -1096,9 +1096,13 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     prof_mark(s, PROF_ATTN, 0.0);
     // chunks a span can touch: the window plus the block on sliding layers,
     // the whole context on global ones (blocks past the live count exit)
+    // blocks walk the chunks with a stride of grid_x: about two blocks an
+    // SM over all pair groups, never more than the span can have chunks
     const int sliding = L.kind == 0 ? 1 : 0;
+    const int groups = (K * m->heads + 7) / 8;
     int grid_x = s->max_chunks;
     if (sliding) grid_x = std::min(grid_x, (m->slide_span + IGC_LANE_LIMIT) / s->chunk_len + 2);
+    grid_x = std::max(1, std::min(grid_x, (2 * m->sm_count + groups - 1) / groups));
     CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                         m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
                         m->slide_span, d_p0, K, s->chunk_len, grid_x, s->part_ml, s->part_acc, s->attn, L.q_rows,
