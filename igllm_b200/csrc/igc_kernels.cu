@@ -637,19 +637,28 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
 }
 
 // attention, second step: the chunks' partials merged into each head's
-// output, (sum_c acc_c e^{m_c - M}) / (sum_c l_c e^{m_c - M}).  One block a
-// (lane, head).  Warp 0 forms the chunk weights; its thread t sums the
-// weighted l_c of chunks t, t + 32, ... in order and the warp adds the 32
-// sums in a fixed tree; then one thread a dimension sums the chunks in
-// ascending order.
-__global__ void attn_combine_kernel(const float *part_ml, const float *part_acc, int lanes, int heads, int hd,
-                                    int sliding, int span, int chunk_len, const int *d_p0, float *out,
-                                    int out_stride) {
+// output, (sum_c acc_c e^{m_c - M}) / (sum_c l_c e^{m_c - M}).  Blocks
+// (lane, head, 64-dimension slice).  Every sum is keyed on the absolute
+// chunk index, so a chunk outside a lane's span (zero weight, zero partials)
+// changes nothing and the result does not depend on how many lanes shared
+// the pass: warp 0's thread t adds the weighted l_c of chunks c = t mod 32 in
+// ascending order and the warp adds the 32 sums in a fixed tree; thread
+// (g, d) adds acc_c of chunks c = g mod 4 in ascending order and the four
+// groups are added in order.
+constexpr int COMB_GROUPS = 4, COMB_DIMS = 64;
+
+__global__ void __launch_bounds__(COMB_GROUPS * COMB_DIMS) attn_combine_kernel(const float *part_ml, const float *part_acc,
+                                                                               int lanes, int heads, int hd, int sliding,
+                                                                               int span, int chunk_len, const int *d_p0,
+                                                                               float *out, int out_stride) {
   __shared__ float wgt[1024];
+  __shared__ float grp[COMB_GROUPS][COMB_DIMS];
   __shared__ float tot;
   pdl_release();
   pdl_wait();
-  const int j = blockIdx.x / heads, h = blockIdx.x % heads;
+  const int slices = (hd + COMB_DIMS - 1) / COMB_DIMS;
+  const int pair = blockIdx.x / slices, dslice = blockIdx.x - pair * slices;
+  const int j = pair / heads, h = pair % heads;
   if (j >= lanes) return;
   const int p0 = *d_p0;
   const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
@@ -660,10 +669,12 @@ __global__ void attn_combine_kernel(const float *part_ml, const float *part_acc,
   const size_t s0 = (size_t)j * heads + h;
   if (threadIdx.x < 32) {
     constexpr int MAXC = 1024 / 32;
+    // thread t holds the chunks whose absolute index is t mod 32
+    const int t0 = (threadIdx.x - c_first % 32 + 32) % 32;  // first relative chunk of this thread
     float m[MAXC], lv[MAXC];
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
-      const int c = threadIdx.x + 32 * i;
+      const int c = t0 + 32 * i;
       m[i] = c < n_chunks ? part_ml[(c * cstride + s0) * 2] : -FLT_MAX;
       lv[i] = c < n_chunks ? part_ml[(c * cstride + s0) * 2 + 1] : 0.0f;
     }
@@ -674,7 +685,7 @@ __global__ void attn_combine_kernel(const float *part_ml, const float *part_acc,
     float L = 0.0f;
 #pragma unroll
     for (int i = 0; i < MAXC; ++i) {
-      const int c = threadIdx.x + 32 * i;
+      const int c = t0 + 32 * i;
       const float w = (m[i] == -FLT_MAX) ? 0.0f : expf(m[i] - M);
       if (c < n_chunks) wgt[c] = w;
       L += lv[i] * w;
@@ -683,12 +694,20 @@ __global__ void attn_combine_kernel(const float *part_ml, const float *part_acc,
     if (threadIdx.x == 0) tot = L;
   }
   __syncthreads();
-  const float inv = 1.0f / tot;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    float o = 0.0f;
-#pragma unroll 8
-    for (int c = 0; c < n_chunks; ++c) o += part_acc[(c * cstride + s0) * hd + d] * wgt[c];
-    out[(size_t)j * out_stride + (size_t)h * hd + d] = o * inv;
+  const int g = threadIdx.x / COMB_DIMS, dl = threadIdx.x - g * COMB_DIMS, d = dslice * COMB_DIMS + dl;
+  float o = 0.0f;
+  if (d < hd) {
+    const int cg0 = (g - c_first % COMB_GROUPS + COMB_GROUPS) % COMB_GROUPS;  // first relative chunk of group g
+#pragma unroll 4
+    for (int c = cg0; c < n_chunks; c += COMB_GROUPS) o += part_acc[(c * cstride + s0) * hd + d] * wgt[c];
+  }
+  grp[g][dl] = o;
+  __syncthreads();
+  if (threadIdx.x < COMB_DIMS && d < hd) {
+    float v = grp[0][dl];
+#pragma unroll
+    for (int q = 1; q < COMB_GROUPS; ++q) v += grp[q][dl];
+    out[(size_t)j * out_stride + (size_t)h * hd + d] = v * (1.0f / tot);
   }
 }
 
@@ -1163,8 +1182,9 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
   }
 #undef IGC_ATT
   if (e != cudaSuccess) return e;
-  return launch_k(attn_combine_kernel, dim3(lanes * heads), dim3(256), 0, st, part_ml, part_acc, lanes, heads, hd,
-                  sliding, span, chunk_len, d_p0, out, out_stride);
+  const int slices = (hd + COMB_DIMS - 1) / COMB_DIMS;
+  return launch_k(attn_combine_kernel, dim3(lanes * heads * slices), dim3(COMB_GROUPS * COMB_DIMS), 0, st, part_ml,
+                  part_acc, lanes, heads, hd, sliding, span, chunk_len, d_p0, out, out_stride);
 }
 
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
