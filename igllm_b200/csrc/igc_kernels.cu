@@ -458,6 +458,36 @@ __device__ __forceinline__ void store_dpl(float *dst, const float (&v)[DPL]) {
   }
 }
 
+// The blend's dimensions of thread l: with four or more a thread, the
+// float4s l, l + 32, ... of the head (consecutive threads on consecutive
+// banks); with fewer, the DPL consecutive dimensions from l * DPL.
+template <int DPL>
+__device__ __forceinline__ void load_blend(const float *row, int l, float (&v)[DPL]) {
+  if constexpr (DPL % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < DPL / 4; ++k) {
+      const float4 x = reinterpret_cast<const float4 *>(row)[l + 32 * k];
+      v[4 * k] = x.x;
+      v[4 * k + 1] = x.y;
+      v[4 * k + 2] = x.z;
+      v[4 * k + 3] = x.w;
+    }
+  } else {
+    load_dpl<DPL>(row + l * DPL, v);
+  }
+}
+
+template <int DPL>
+__device__ __forceinline__ void store_blend(float *row, int l, const float (&v)[DPL]) {
+  if constexpr (DPL % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < DPL / 4; ++k)
+      reinterpret_cast<float4 *>(row)[l + 32 * k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
+  } else {
+    store_dpl<DPL>(row + l * DPL, v);
+  }
+}
+
 // One head of 32 * DPL dimensions, DPL a thread: normed (app_core.c:4667,
 // double mean of squares) with an optional gain, then turned by the rope
 // tables of its position (pairs (d, d + hd/2), threads l and l + 16).
@@ -583,17 +613,19 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
       asm volatile("cp.async.wait_all;\n" ::: "memory");
       __syncthreads();
       if (has) {
-        // scores: threads r and r + 16 take the two halves of position tb + r
+        // scores: threads r and r + 16 take the even and odd float4s of
+        // position tb + r (the two halves' query reads then fall in
+        // different banks)
         const int pos = tb + r_pos;
-        const float4 *qr = reinterpret_cast<const float4 *>(qs + warp * HD + hhalf * (HD / 2));
-        const float4 *kr = reinterpret_cast<const float4 *>(ks + (size_t)r_pos * KS + kvoff + hhalf * (HD / 2));
+        const float4 *qr = reinterpret_cast<const float4 *>(qs + warp * HD) + hhalf;
+        const float4 *kr = reinterpret_cast<const float4 *>(ks + (size_t)r_pos * KS + kvoff) + hhalf;
         float a0 = 0.f, a1 = 0.f;
 #pragma unroll 4
-        for (int d4 = 0; d4 < HD / 8; d4 += 2) {
-          const float4 q0 = qr[d4], k0 = kr[d4];
+        for (int m = 0; m < HD / 8; m += 2) {
+          const float4 q0 = qr[2 * m], k0 = kr[2 * m];
           a0 = fmaf(q0.x, k0.x, a0); a0 = fmaf(q0.y, k0.y, a0); a0 = fmaf(q0.z, k0.z, a0); a0 = fmaf(q0.w, k0.w, a0);
-          if (d4 + 1 < HD / 8) {
-            const float4 q1 = qr[d4 + 1], k1 = kr[d4 + 1];
+          if (m + 1 < HD / 8) {
+            const float4 q1 = qr[2 * m + 2], k1 = kr[2 * m + 2];
             a1 = fmaf(q1.x, k1.x, a1); a1 = fmaf(q1.y, k1.y, a1); a1 = fmaf(q1.z, k1.z, a1); a1 = fmaf(q1.w, k1.w, a1);
           }
         }
@@ -613,13 +645,13 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
         m_run = m_new;
 #pragma unroll
         for (int e = 0; e < DPL; ++e) acc[e] *= f;
-        // blend: thread l takes dimensions [l*DPL, (l+1)*DPL) of every position
-        const float *vcol = vs + kvoff + l * DPL;
+        // blend: thread l takes the dimensions of blend_dim(l, e) of every
+        // position (float4s l, l + 32, ... where the head has them)
 #pragma unroll 4
         for (int r = 0; r < ATT_T; ++r) {
           const float pr = __shfl_sync(0xffffffffu, pe, r);
           float vv[DPL];
-          load_dpl<DPL>(vcol + (size_t)r * KS, vv);
+          load_blend<DPL>(vs + (size_t)r * KS + kvoff, l, vv);
 #pragma unroll
           for (int e = 0; e < DPL; ++e) acc[e] = fmaf(pr, vv[e], acc[e]);
         }
@@ -631,7 +663,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
         part_ml[slot * 2 + 0] = m_run;
         part_ml[slot * 2 + 1] = l_run;
       }
-      store_dpl<DPL>(part_acc + slot * HD + l * DPL, acc);
+      store_blend<DPL>(part_acc + slot * HD, l, acc);
     }
   }
 }
