@@ -44,7 +44,8 @@
 
 namespace igc {
 
-enum : int { PRO_F32 = 0, PRO_NORM = 1, PRO_RESID = 2, PRO_RESID_NORM = 3 };
+// PRO_F32S: unnormed input whose producer left its magnitudes (one-pass staging).
+enum : int { PRO_F32 = 0, PRO_NORM = 1, PRO_RESID = 2, PRO_RESID_NORM = 3, PRO_F32S = 4 };
 enum : int { EPI_STORE = 0, EPI_GELU_PAIR = 1, EPI_GELU_MUL = 2, EPI_LOGITS = 3 };
 
 // Lane modes.  PACK (up to 4 lanes): one 8-column B tile carries lanes 0-3 hi
@@ -86,9 +87,16 @@ struct GemvArgs {
   const float *w_in;
   float eps;
   float *x_out;
-  const float *p_ssq;  // producer's partial sums of squares of p, [p_parts][16]
+  // partials are lane-major: [16 lanes][GEMV_PART_LIMIT parts]
+  const float *p_ssq;  // producer's partial sums of squares of p
   int p_parts;
-  float *out_ssq;      // this launch's partial sums of squares of out, [gridDim.x][16]
+  float *out_ssq;      // this launch's partial sums of squares of out, one a virtual block
+  // magnitudes: the producer's per-part largest |x|, which
+  // lets an unnormed prologue stage in one pass, and this launch's per virtual
+  // block largest |out| for its own consumer
+  const float *x_amax;
+  int x_amax_parts;
+  float *out_amax;
   // epilogue
   float *out;
   int out_stride;
@@ -189,13 +197,104 @@ struct ProBatch {
 // activations are loaded before anything waits on either.
 constexpr int GEMV_MAX_PARTS = 48;  // 6144 columns
 
+// The unnormed prologue when the producer left the magnitudes of x: the
+// lanes' staging scales are known before any activation arrives, so each
+// value is loaded, scaled and split into its final hi/lo words in one pass
+// (the same scale the general prologue would take: the power of two of the
+// same largest magnitude).
+template <int MODE, int WARPS>
+__device__ void gemv_prologue_scaled(const GemvArgs &a, uint32_t *stage, float *scr) {
+  constexpr int B = 8;
+  const int cols = a.pl.cols, K = a.lanes, n4 = cols >> 2;
+  const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
+  if (cols & 63) {
+    const int words = (int)(gemv_stage_bytes(a.pl.n_cc, MODE) / 16);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) reinterpret_cast<uint4 *>(stage)[i] = make_uint4(0u, 0u, 0u, 0u);
+    __syncthreads();
+  }
+  int wpl = 1;
+  while (wpl * 2 * K <= WARPS) wpl *= 2;
+  const int n_slots = (K + WARPS - 1) / WARPS;
+  const int w_local = wpl > 1 ? warp % wpl : 0;
+  const int span4 = (n4 + wpl - 1) / wpl, lo = w_local * span4, hi = min(n4, lo + span4);
+  const int c4_0 = lo + l32;
+  const int count = c4_0 < hi ? (hi - c4_0 + 31) >> 5 : 0;
+  const int step = 2 * stage_chunk_words(MODE);  // 128 columns further on: two chunks
+  const float4 *__restrict__ x4 = reinterpret_cast<const float4 *>(a.x);
+  const int xs4 = a.x_stride >> 2;
+  int jj[2];
+  bool live[2];
+  int wh0[2], wl0[2], wh2[2], wl2[2];
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    jj[slot] = wpl > 1 ? warp / wpl : warp + slot * WARPS;
+    live[slot] = slot < n_slots && jj[slot] < K;
+    const int c = c4_0 * 4;
+    wh0[slot] = stage_word(jj[slot], c, 0, MODE);
+    wl0[slot] = stage_word(jj[slot], c, 1, MODE);
+    wh2[slot] = stage_word(jj[slot], c + 2, 0, MODE);
+    wl2[slot] = stage_word(jj[slot], c + 2, 1, MODE);
+  }
+  float4 X[B];
+  auto load = [&](int slot, int i0) {
+#pragma unroll
+    for (int b = 0; b < B; ++b)
+      if (i0 + b < count) X[b] = x4[(size_t)jj[slot] * xs4 + c4_0 + 32 * (i0 + b)];
+  };
+  auto put = [&](int wh, int wl, float a0, float a1) {
+    __half h0 = __float2half_rn(a0), h1 = __float2half_rn(a1);
+    __half l0 = __float2half_rn(a0 - __half2float(h0)), l1 = __float2half_rn(a1 - __half2float(h1));
+    __half2 hv = __halves2half2(h0, h1), lv = __halves2half2(l0, l1);
+    stage[wh] = *reinterpret_cast<uint32_t *>(&hv);
+    stage[wl] = *reinterpret_cast<uint32_t *>(&lv);
+  };
+  auto seal = [&](int slot, int i0) {
+    const float sc = scr[SCR_SCALE + jj[slot]];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      if (i0 + b < count) {
+        const int o = step * (i0 + b);
+        const float4 y = X[b];
+        put(wh0[slot] + o, wl0[slot] + o, y.x * sc, y.y * sc);
+        put(wh2[slot] + o, wl2[slot] + o, y.z * sc, y.w * sc);
+      }
+    }
+  };
+  if (live[0]) load(0, 0);
+  // warp w reduces lane w's (and w + WARPS's) magnitude partials, 32 at a time
+  for (int j = warp; j < K; j += WARPS) {
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < GEMV_PART_LIMIT / 32; ++i) {
+      const int q = l32 + 32 * i;
+      if (q < a.x_amax_parts) m = fmaxf(m, a.x_amax[j * GEMV_PART_LIMIT + q]);
+    }
+    m = warp_max(m);
+    if (l32 == 0) {
+      const float sc = lane_scale(m);
+      scr[SCR_SCALE + j] = sc;
+      scr[SCR_FACTOR + j] = 1.0f / sc;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int slot = 0; slot < 2; ++slot) {
+    if (!live[slot]) continue;
+    if (slot > 0) load(slot, 0);
+    seal(slot, 0);
+    for (int i0 = B; i0 < count; i0 += B) {
+      load(slot, i0);
+      seal(slot, i0);
+    }
+  }
+  __syncthreads();
+}
+
 template <int PRO, int MODE, int WARPS>
 __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
   constexpr bool RES = PRO == PRO_RESID || PRO == PRO_RESID_NORM;
   constexpr bool NRM = PRO == PRO_NORM || PRO == PRO_RESID_NORM;
   constexpr int B = ProBatch<PRO>::value;
-  constexpr int STRIPES = WARPS * 2;  // threads / 16
-  constexpr int PQ = (GEMV_PART_LIMIT + STRIPES - 1) / STRIPES;
   const int cols = a.pl.cols, K = a.lanes, n4 = cols >> 2;
   const int nparts = (n4 + 31) >> 5;
   const int warp = threadIdx.x >> 5, l32 = threadIdx.x & 31;
@@ -206,14 +305,18 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     for (int i = threadIdx.x; i < words; i += blockDim.x) reinterpret_cast<uint4 *>(stage)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
   }
-  // the residual's partials: thread (lane j, stripe q0) holds parts q0, q0 + STRIPES, ...
-  float part[RES ? PQ : 1];
+  // the residual's partials: warp w holds lane w's (and w + WARPS's), thread
+  // l the parts l, l + 32, ... (a fixed tree whatever the lane count)
+  float part[RES ? 2 : 1][GEMV_PART_LIMIT / 32];
   if (RES) {
-    const int j = threadIdx.x & 15, q0 = threadIdx.x >> 4;
 #pragma unroll
-    for (int i = 0; i < PQ; ++i) {
-      const int q = q0 + STRIPES * i;
-      part[i] = (j < K && q < a.p_parts) ? a.p_ssq[q * 16 + j] : 0.0f;
+    for (int sl = 0; sl < 2; ++sl) {
+      const int j = warp + sl * WARPS;
+#pragma unroll
+      for (int i = 0; i < GEMV_PART_LIMIT / 32; ++i) {
+        const int q = l32 + 32 * i;
+        part[sl][i] = (j < K && q < a.p_parts) ? a.p_ssq[j * GEMV_PART_LIMIT + q] : 0.0f;
+      }
     }
   }
   int wpl = 1;  // warps a lane
@@ -311,15 +414,15 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
 
   if (live[0]) load(0, 0);
   if (RES) {
-    float tsum = 0.0f;
 #pragma unroll
-    for (int i = 0; i < PQ; ++i) tsum += part[i];
-    scr[SCR_STRIPE + threadIdx.x] = tsum;
-    __syncthreads();
-    if (threadIdx.x < 16 && (int)threadIdx.x < K) {
-      float u = 0.0f;
-      for (int q = 0; q < STRIPES; ++q) u += scr[SCR_STRIPE + q * 16 + threadIdx.x];
-      scr[SCR_SHRINK_P + threadIdx.x] = rms_shrink(u, cols, a.eps);
+    for (int sl = 0; sl < 2; ++sl) {
+      const int j = warp + sl * WARPS;
+      if (j >= K) continue;
+      float tsum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < GEMV_PART_LIMIT / 32; ++i) tsum += part[sl][i];
+      tsum = warp_sum(tsum);
+      if (l32 == 0) scr[SCR_SHRINK_P + j] = rms_shrink(tsum, cols, a.eps);
     }
     __syncthreads();
   }

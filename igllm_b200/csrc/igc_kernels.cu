@@ -130,7 +130,10 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
         mul_pre[nt][i] = ok ? a.aux[(size_t)ln * a.aux_stride + row] : 0.0f;
       }
   }
-  gemv_prologue<PRO, MODE, WARPS>(a, stage, scr);
+  if constexpr (PRO == PRO_F32S)
+    gemv_prologue_scaled<MODE, WARPS>(a, stage, scr);
+  else
+    gemv_prologue<PRO, MODE, WARPS>(a, stage, scr);
   // the next kernel may start (and fetch its weights) once this one is past
   // its own wait: released any earlier, kernels still waiting would release
   // the ones after them and pile up on the SMs
@@ -149,12 +152,13 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
   // EPI_LOGITS running argmax, EPI_STORE running sum of squares, per (nt, lane parity)
   float best_v[NT][2];
   int best_i[NT][2];
-  float ssq[NT][2];
+  float ssq[NT][2], mag[NT][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
     best_v[nt][0] = best_v[nt][1] = -FLT_MAX;
     best_i[nt][0] = best_i[nt][1] = 0x7fffffff;
     ssq[nt][0] = ssq[nt][1] = 0.0f;
+    mag[nt][0] = mag[nt][1] = 0.0f;
   }
 
   bool failed = false;
@@ -241,11 +245,16 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
             const float o = x * a.out_scale;
             a.out[(size_t)ln * a.out_stride + row] = o;
             ssq[nt][k] += o * o;
+            mag[nt][k] = fmaxf(mag[nt][k], fabsf(o));
           } else if (EPI == EPI_GELU_PAIR) {
-            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(x) * (v[PAIR][nt][i] * sh[nt][k]);
+            const float o = gelu_tanh(x) * (v[PAIR][nt][i] * sh[nt][k]);
+            a.out[(size_t)ln * a.out_stride + row] = o;
+            mag[nt][k] = fmaxf(mag[nt][k], fabsf(o));
           } else if (EPI == EPI_GELU_MUL) {
             const float mul = my_units == 1 ? mul_pre[nt][i] : a.aux[(size_t)ln * a.aux_stride + row];
-            a.out[(size_t)ln * a.out_stride + row] = gelu_tanh(x) * mul;
+            const float o = gelu_tanh(x) * mul;
+            a.out[(size_t)ln * a.out_stride + row] = o;
+            mag[nt][k] = fmaxf(mag[nt][k], fabsf(o));
           } else {  // EPI_LOGITS
             const float cv = a.cap > 0.0f ? logit_cap(x, a.cap) : x;
             a.out[(size_t)ln * a.out_stride + row] = cv;
@@ -281,7 +290,34 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
       if (ln < NT * 8 && vb < n_vb) {
         float v = 0.0f;
         for (int w = 8 * h; w < 8 * h + 8; ++w) v += red[w * 16 + ln];
-        a.out_ssq[vb * 16 + ln] = v;
+        a.out_ssq[ln * GEMV_PART_LIMIT + vb] = v;
+      }
+    }
+  }
+
+  if (EPI != EPI_LOGITS && a.out_amax) {
+    // per-lane largest |out| of each virtual 8-warp block, for the consumer's
+    // one-pass staging (a maximum: any order gives the same value)
+    __syncthreads();
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        float v = mag[nt][k];
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        const int ln = nt * 8 + 2 * t + k;
+        if (g == 0) red[warp * 16 + ln] = (MODE == MODE_PACK && t >= 2) ? 0.0f : v;
+      }
+    __syncthreads();
+    const int n_vb = (Q + a.vgroups - 1) / a.vgroups;
+    if (threadIdx.x < (WARPS / 8) * 16) {
+      const int h = threadIdx.x >> 4, ln = threadIdx.x & 15;
+      const int vb = blockIdx.x * (WARPS / 8) + h;
+      if (ln < NT * 8 && vb < n_vb) {
+        float v = 0.0f;
+        for (int w = 8 * h; w < 8 * h + 8; ++w) v = fmaxf(v, red[w * 16 + ln]);
+        a.out_amax[ln * GEMV_PART_LIMIT + vb] = v;
       }
     }
   }
@@ -682,7 +718,8 @@ constexpr int COMB_GROUPS = 4, COMB_DIMS = 64;
 __global__ void __launch_bounds__(COMB_GROUPS * COMB_DIMS) attn_combine_kernel(const float *part_ml, const float *part_acc,
                                                                                int lanes, int heads, int hd, int sliding,
                                                                                int span, int chunk_len, const int *d_p0,
-                                                                               float *out, int out_stride) {
+                                                                               float *out, int out_stride,
+                                                                               float *out_amax) {
   __shared__ float wgt[1024];
   __shared__ float grp[COMB_GROUPS][COMB_DIMS];
   __shared__ float tot;
@@ -735,11 +772,21 @@ __global__ void __launch_bounds__(COMB_GROUPS * COMB_DIMS) attn_combine_kernel(c
   }
   grp[g][dl] = o;
   __syncthreads();
+  float v = 0.0f;
   if (threadIdx.x < COMB_DIMS && d < hd) {
-    float v = grp[0][dl];
+    v = grp[0][dl];
 #pragma unroll
     for (int q = 1; q < COMB_GROUPS; ++q) v += grp[q][dl];
-    out[(size_t)j * out_stride + (size_t)h * hd + d] = v * (1.0f / tot);
+    v *= 1.0f / tot;
+    out[(size_t)j * out_stride + (size_t)h * hd + d] = v;
+  }
+  if (out_amax && threadIdx.x < COMB_DIMS) {
+    // this block's largest |out|: one partial a (head, slice) for lane j
+    __shared__ float amx[COMB_DIMS / 32];
+    const float m = warp_max(fabsf(v));
+    if ((threadIdx.x & 31) == 0) amx[threadIdx.x >> 5] = m;
+    named_sync(1, COMB_DIMS);
+    if (threadIdx.x == 0) out_amax[(size_t)j * GEMV_PART_LIMIT + h * slices + dslice] = fmaxf(amx[0], amx[1]);
   }
 }
 
@@ -1048,6 +1095,7 @@ static cudaError_t launch_gemv_pe(const GemvArgs &a, int pro, int epi, int grid,
     IGC_CASE(PRO_F32, EPI_GELU_PAIR)
   } else {
     IGC_CASE(PRO_F32, EPI_STORE)
+    IGC_CASE(PRO_F32S, EPI_STORE)
     IGC_CASE(PRO_NORM, EPI_STORE)
     IGC_CASE(PRO_RESID_NORM, EPI_STORE)
     IGC_CASE(PRO_RESID, EPI_GELU_MUL)
@@ -1083,6 +1131,7 @@ static cudaError_t allow_smem_mode(int bytes) {
   IGC_ALLOW(1, PRO_NORM, EPI_GELU_PAIR)
   IGC_ALLOW(1, PRO_F32, EPI_GELU_PAIR)
   IGC_ALLOW(0, PRO_F32, EPI_STORE)
+  IGC_ALLOW(0, PRO_F32S, EPI_STORE)
   IGC_ALLOW(0, PRO_NORM, EPI_STORE)
   IGC_ALLOW(0, PRO_RESID_NORM, EPI_STORE)
   IGC_ALLOW(0, PRO_RESID, EPI_GELU_MUL)
@@ -1158,6 +1207,7 @@ cudaError_t igc_launch_gemv(GemvArgs *a, int pair, int pro, int epi, int grid, s
   if (grid_used) *grid_used = (a->slots + G8 - 1) / G8;  // partials written: one a virtual 8-warp block
   size_t smem = 0;
   if (!gemv_fit(*a, pair, W, grid, smem_limit, &smem)) return cudaErrorInvalidValue;
+  if (pro == PRO_F32 && a->x_amax) pro = PRO_F32S;
   if (mode == MODE_PACK)
     return W == 16 ? (pair ? launch_gemv_pe<MODE_PACK, 16, 1>(*a, pro, epi, grid, smem, st)
                            : launch_gemv_pe<MODE_PACK, 16, 0>(*a, pro, epi, grid, smem, st))
@@ -1198,7 +1248,8 @@ size_t igc_attn_smem(int hd, int kv_w) { return sizeof(float) * attn_smem_floats
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int chunk_len, int grid_x,
-                            float *part_ml, float *part_acc, float *out, int out_stride, cudaStream_t st) {
+                            float *part_ml, float *part_acc, float *out, int out_stride, float *out_amax,
+                            cudaStream_t st) {
   const size_t smem = igc_attn_smem(hd, kv_heads * hd);
   const dim3 grid(grid_x, (lanes * heads + ATT_PAIRS - 1) / ATT_PAIRS);
   cudaError_t e;
@@ -1216,7 +1267,7 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
   if (e != cudaSuccess) return e;
   const int slices = (hd + COMB_DIMS - 1) / COMB_DIMS;
   return launch_k(attn_combine_kernel, dim3(lanes * heads * slices), dim3(COMB_GROUPS * COMB_DIMS), 0, st, part_ml,
-                  part_acc, lanes, heads, hd, sliding, span, chunk_len, d_p0, out, out_stride);
+                  part_acc, lanes, heads, hd, sliding, span, chunk_len, d_p0, out, out_stride, out_amax);
 }
 
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,

@@ -789,6 +789,7 @@ struct igc_session {
         *pp = nullptr, *logits = nullptr;
   float *part_ml = nullptr, *part_acc = nullptr, *arg_val = nullptr;
   float *ssq_o = nullptr, *ssq_d = nullptr, *ssq_pp = nullptr;
+  float *amax_attn = nullptr, *amax_act = nullptr, *amax_pa = nullptr;  // magnitude partials
   int *arg_idx = nullptr;
   float *cand_v = nullptr, *top_v = nullptr;
   int *cand_i = nullptr, *top_i = nullptr;
@@ -894,6 +895,9 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (c == IGC_OKAY) c = s->alloc(&s->ssq_o, (size_t)s->arg_parts * 16);
   if (c == IGC_OKAY) c = s->alloc(&s->ssq_d, (size_t)s->arg_parts * 16);
   if (c == IGC_OKAY) c = s->alloc(&s->ssq_pp, (size_t)s->arg_parts * 16);
+  if (c == IGC_OKAY) c = s->alloc(&s->amax_attn, (size_t)s->arg_parts * 16);
+  if (c == IGC_OKAY) c = s->alloc(&s->amax_act, (size_t)s->arg_parts * 16);
+  if (c == IGC_OKAY) c = s->alloc(&s->amax_pa, (size_t)s->arg_parts * 16);
   int blocks = (m->vocab + 2047) / 2048;
   if (c == IGC_OKAY) c = s->alloc(&s->cand_v, (size_t)K * blocks * 256);
   if (c == IGC_OKAY) c = s->alloc(&s->cand_i, (size_t)K * blocks * 256);
@@ -970,7 +974,8 @@ static void prof_mark(igc_session *s, int cls, double bytes) {
 static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, const float *x, int x_stride,
                 const float *p, const float *w_res, float gain, const float *w_in, float *x_out, float *out,
                 int out_stride, float out_scale = 1.0f, const float *aux = nullptr, int aux_stride = 0,
-                const Ssq *p_ssq = nullptr, Ssq *out_ssq = nullptr) {
+                const Ssq *p_ssq = nullptr, Ssq *out_ssq = nullptr, const Ssq *x_amax = nullptr,
+                Ssq *out_amax = nullptr) {
   prof_mark(s, &pl == &s->m->head ? PROF_HEAD : PROF_GEMV, pl.bytes);
   GemvArgs a;
   memset(&a, 0, sizeof(a));
@@ -983,6 +988,12 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
     a.out_ssq = out_ssq->buf;
     out_ssq->parts = pl.grid;
   }
+  if (x_amax) {  // the producer left x's magnitudes: one-pass staging
+    a.x_amax = x_amax->buf;
+    a.x_amax_parts = x_amax->parts;
+    if (a.x_amax_parts > GEMV_PART_LIMIT) return IGC_FAIL_SUPPORT;
+  }
+  if (out_amax) a.out_amax = out_amax->buf;
   a.pl = pl.view();
   a.lanes = K;
   a.split = pl.split;
@@ -1009,6 +1020,7 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   if (igc_gemv_smem_min(&a, pair) <= (size_t)s->m->smem_limit) {
     CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
     if (out_ssq) out_ssq->parts = used;
+    if (out_amax) out_amax->parts = used;
     if (epi == EPI_LOGITS) s->head_parts = used;
     return IGC_OKAY;
   }
@@ -1023,10 +1035,14 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
     b.x_out = x_out ? x_out + (size_t)j0 * x_stride : nullptr;
     b.out = out + (size_t)j0 * out_stride;
     b.aux = aux ? aux + (size_t)j0 * aux_stride : nullptr;
-    b.out_ssq = a.out_ssq ? a.out_ssq + j0 : nullptr;
+    b.p_ssq = a.p_ssq ? a.p_ssq + (size_t)j0 * GEMV_PART_LIMIT : nullptr;  // lane-major partials
+    b.out_ssq = a.out_ssq ? a.out_ssq + (size_t)j0 * GEMV_PART_LIMIT : nullptr;
+    b.x_amax = a.x_amax ? a.x_amax + (size_t)j0 * GEMV_PART_LIMIT : nullptr;
+    b.out_amax = a.out_amax ? a.out_amax + (size_t)j0 * GEMV_PART_LIMIT : nullptr;
     if (igc_gemv_smem_min(&b, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
     CKL(igc_launch_gemv(&b, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
     if (out_ssq) out_ssq->parts = used;
+    if (out_amax) out_amax->parts = used;
   }
   return IGC_OKAY;
 }
@@ -1075,6 +1091,13 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   const float *pend = nullptr, *pend_w = nullptr;
   float pend_gain = 1.0f;
   Ssq so{s->ssq_o, 0}, sd{s->ssq_d, 0}, spp{s->ssq_pp, 0};
+  Ssq ma{s->amax_attn, 0}, mact{s->amax_act, 0}, mpa{s->amax_pa, 0};
+  // producers leave magnitudes (for one-pass staging downstream) only where
+  // the staging is large enough to repay the extra epilogue step; the scale
+  // is the same either way, so results do not change
+  const bool mags = K > 4;
+  Ssq *mact_out = mags ? &mact : nullptr, *mpa_out = mags ? &mpa : nullptr;
+  const Ssq *ma_in = mags ? &ma : nullptr, *mact_in = mags ? &mact : nullptr, *mpa_in = mags ? &mpa : nullptr;
   const Ssq *pend_ssq = nullptr;
   auto next_x = [&]() -> float * { float *o = bufs[flip]; flip ^= 1; return o; };
   for (int l = 0; l < m->layers; ++l) {
@@ -1106,27 +1129,28 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                         m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
                         m->slide_span, d_p0, K, s->chunk_len, grid_x, s->part_ml, s->part_acc, s->attn, L.q_rows,
-                        s->st));
+                        mags ? ma.buf : nullptr, s->st));
     ++g_launches;  // the combine kernel
+    ma.parts = m->heads * ((L.hd + 63) / 64);
     c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
-             1.0f, nullptr, 0, nullptr, &so);
+             1.0f, nullptr, 0, nullptr, &so, ma_in);
     if (c != IGC_OKAY) return c;
     xo = next_x();
     c = gemv(s, L.gateup, K, PRO_RESID_NORM, EPI_GELU_PAIR, cur, H, s->obuf, L.after_attn_norm, 1.0f,
-             L.before_feed_norm, xo, s->act, L.inner, 1.0f, nullptr, 0, &so, nullptr);
+             L.before_feed_norm, xo, s->act, L.inner, 1.0f, nullptr, 0, &so, nullptr, nullptr, mact_out);
     if (c != IGC_OKAY) return c;
     cur = xo;
     c = gemv(s, L.down, K, PRO_F32, EPI_STORE, s->act, L.inner, nullptr, nullptr, 1.0f, nullptr, nullptr, s->dbuf, H,
-             1.0f, nullptr, 0, nullptr, &sd);
+             1.0f, nullptr, 0, nullptr, &sd, mact_in);
     if (c != IGC_OKAY) return c;
     if (m->ple_dim > 0) {
       xo = next_x();
       c = gemv(s, L.ple_gate, K, PRO_RESID, EPI_GELU_MUL, cur, H, s->dbuf, L.after_feed_norm, 1.0f, nullptr, xo,
-               s->pa, m->ple_dim, 1.0f, s->ple + (size_t)l * m->ple_dim, PS, &sd, nullptr);
+               s->pa, m->ple_dim, 1.0f, s->ple + (size_t)l * m->ple_dim, PS, &sd, nullptr, nullptr, mpa_out);
       if (c != IGC_OKAY) return c;
       cur = xo;
       c = gemv(s, L.ple_proj, K, PRO_F32, EPI_STORE, s->pa, m->ple_dim, nullptr, nullptr, 1.0f, nullptr, nullptr,
-               s->pp, H, 1.0f, nullptr, 0, nullptr, &spp);
+               s->pp, H, 1.0f, nullptr, 0, nullptr, &spp, mpa_in);
       if (c != IGC_OKAY) return c;
       pend = s->pp;
       pend_w = L.after_ple_norm;
