@@ -42,6 +42,7 @@ sys.path.insert(0, ROOT)
 TOKENS = 256
 GUESS = 4
 PROMPT_LEN = 1024
+PREFILL_LEN = 4096
 VOCAB = 262144
 CKPT_DIR = os.environ.get("IGLLM_BENCH_CKPT", "/tmp/igllm_bench_e2b_s1")
 METRIC = "decode tok/s (greedy, --guess 4)"
@@ -136,6 +137,47 @@ def profiler_range(on):
         pass
 
 
+class Ranks:
+    """One process a GPU under torchrun: its rank, the world size, and the
+    process group (None when alone).  Replicas share nothing but the barrier
+    around the timed region and the maximum of their times."""
+
+    def __init__(self, backend="nccl", device=None):
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dist = None
+        self.device = device
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist:
+            self.dist.barrier()
+
+    def max(self, x):
+        """The largest of every rank's x (each rank gets it)."""
+        if not self.dist:
+            return float(x)
+        import torch
+        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.dist:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+def aggregate(tokens_per_rank, slowest_seconds, world):
+    """Whole-job throughput: every rank's tokens over the slowest rank's time."""
+    return world * tokens_per_rank / slowest_seconds
+
+
 # ---------------------------------------------------------------------------
 # the reference engine on the host cores (oracle/_ref, built from app_core.c)
 
@@ -220,27 +262,13 @@ def run_reference(args):
 def run_ours(args):
     import igllm_b200 as ig
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         import torch
-        import torch.distributed as dist
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
-
-    def barrier():
-        if dist:
-            dist.barrier()
-
-    def max_over_ranks(x):
-        if not dist:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64, device=f"cuda:{local}")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    ranks = Ranks("nccl", device=f"cuda:{local}")
+    rank, world = ranks.rank, ranks.world
+    barrier, max_over_ranks = ranks.barrier, ranks.max
 
     model = ig.Model(spec=ig.spec_e2b(seed=1, window_limit=4096), device=local, window_limit=4096)
     sess = ig.Session(model)
@@ -273,7 +301,7 @@ def run_ours(args):
         profiler_range(False)
     launches = ig.launch_count()
     total_s = max_over_ranks(sum(dev_ms) / 1000.0)
-    value = world * TOKENS * args.steps / total_s
+    value = aggregate(TOKENS * args.steps, total_s, world)
     check_ok = int(top[-1]) == int(cont[rounds * GUESS - 1])
 
     # end to end through the round call, host ids in and out each round
@@ -291,7 +319,7 @@ def run_ours(args):
         e2e_s += time.perf_counter() - t0
         sess.hold(base)
     e2e_s = max_over_ranks(e2e_s)
-    e2e = world * TOKENS * args.steps / e2e_s
+    e2e = aggregate(TOKENS * args.steps, e2e_s, world)
     h2d = rounds * (1 + GUESS) * 4
     d2h = rounds * GUESS * 4
 
@@ -329,6 +357,21 @@ def run_ours(args):
         sess.hold(base)
         per_k[str(k)] = round(1000.0 * ms / r_k, 1)
 
+    # prefill: 4096 uniform ids (seed 1) through the
+    # prime call, then the first token; a warm-up prime captures the graphs
+    psess = ig.Session(model)
+    pids = np.random.default_rng(1).integers(0, VOCAB, PREFILL_LEN).astype(np.int32)
+    psess.prime(pids)
+    psess.reset()
+    t0 = time.perf_counter()
+    psess.prime(pids)
+    t1 = time.perf_counter()
+    psess.step(int(pids[-1]), want_logits=False)
+    t2 = time.perf_counter()
+    psess.close()
+    prefill = {"tok_s": round((PREFILL_LEN - 1) / (t1 - t0), 1), "ttft_ms": round(1000 * (t2 - t0), 2),
+               "prompt": f"{PREFILL_LEN} uniform ids, seed 1 (config 3), 16-lane passes"}
+
     # the projection kernel against the HBM roofline, timed live
     prof = sess.profile(blocks[0])
     sess.hold(base)
@@ -365,6 +408,7 @@ def run_ours(args):
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "verify_round_us": per_k,
+        "prefill": prefill,
         "ngram": {"tok_s": round(TOKENS / ngram_s, 1), "rounds": rounds_n, "guesses": drawn, "kept": kept},
         "roofline": {"bound": "hbm", "kernel": "int4 skinny GEMM (layer projections)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -386,9 +430,7 @@ def run_ours(args):
                                     "sample": f"unavailable: {exc}"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if dist:
-        dist.barrier()
-        dist.destroy_process_group()
+    ranks.close()
 
 
 def main():

@@ -290,3 +290,52 @@ def test_lane_batching_is_bit_identical(igc_lib, small_dir):
     five = c.guess(block[4:])
     assert np.array_equal(stepped, nine)
     assert np.array_equal(stepped, np.concatenate([four, five]))
+
+
+def _shaped(row, heat, top_count, top_portion):
+    """app_core.c:14572 pick_shape without echo penalty: top-k by logit,
+    softmax of (x - max) / heat, the top-p prefix whose running mass first
+    reaches the portion, renormalised.  Returns {id: probability}."""
+    order = np.argsort(-row, kind="stable")[:top_count]
+    w = np.exp((row[order].astype(np.float64) - row[order[0]]) / heat)
+    w /= w.sum()
+    keep = int(np.searchsorted(np.cumsum(w), top_portion) + 1)
+    w = w[:keep] / w[:keep].sum()
+    return dict(zip(order[:keep].tolist(), w.tolist()))
+
+
+def test_sampled_verify_matches_the_shaped_distribution(igc_lib, tiny_dir):
+    """The single-token rejection rule (app_core.c:14762 session_guess_taste:
+    accept the guess t with probability q(t), else draw from q without t)
+    emits tokens distributed as q itself.  Over 4000 seeds, the token a
+    two-lane sampled round emits after its first id matches q (heat 0.8,
+    top-k 64, top-p 0.95) by a chi-squared test."""
+    from scipy.stats import chi2
+    m = igc_lib.Model(folder=tiny_dir, window_limit=TINY["window_limit"])
+    s = igc_lib.Session(m)
+    ids = np.arange(3, 40, dtype=np.int32)
+    s.prime(ids)
+    last = int(ids[-1])
+    base = s.fill
+    row = s.guess(np.array([last], np.int32))[0]
+    s.guess_keep(0)
+    q = _shaped(row, 0.8, 64, 0.95)
+    guess = sorted(q, key=lambda t: -q[t])[1]  # the second likeliest: accepted now and then
+    counts = {}
+    n = 4000
+    for seed in range(1, n + 1):
+        take, made = s.round(np.array([last, guess], np.int32), igc_lib.Taste(0.8, 64, 0.95, 1.0, 64, seed))
+        token = guess if take >= 1 else made
+        counts[token] = counts.get(token, 0) + 1
+        s.hold(base)
+    assert set(counts) <= set(q), "a token outside the shaped support"
+    big = [t for t in q if q[t] * n >= 5]
+    obs = [counts.get(t, 0) for t in big] + [n - sum(counts.get(t, 0) for t in big)]
+    exp = [q[t] * n for t in big] + [n - sum(q[t] * n for t in big)]
+    if exp[-1] < 5:  # fold a thin remainder into the last big bin
+        obs[-2] += obs.pop()
+        exp[-2] += exp.pop()
+    stat = sum((o - e) ** 2 / e for o, e in zip(obs, exp))
+    p = chi2.sf(stat, len(obs) - 1)
+    assert p > 1e-3, (stat, len(obs), p)
+    assert 0.0 < counts.get(guess, 0) / n < 1.0
