@@ -108,6 +108,13 @@ __device__ __forceinline__ uint64_t l2_evict_first() {
   return pol;
 }
 
+// The opposite, for data read again soon (the key/value caches).
+__device__ __forceinline__ uint64_t l2_evict_last() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+
 // One bulk copy global -> shared (no multicast); `bytes` and both addresses
 // are multiples of 16.
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
@@ -134,6 +141,21 @@ __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.lau
 
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---- thread-block clusters -------------------------------------------------
+// All blocks of a cluster arrive, then wait; what each wrote to shared memory
+// before it arrived is visible to the others after the wait.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// Stores (x, y) at `p` in the shared memory of cluster block `rank` (8-byte
+// aligned); visible there after the next cluster barrier.
+__device__ __forceinline__ void st_cluster2(float *p, int rank, float x, float y) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(a) : "r"(smem_u32(p)), "r"(rank));
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};\n" ::"r"(a), "f"(x), "f"(y) : "memory");
 }
 
 __device__ __forceinline__ float warp_sum(float v) {

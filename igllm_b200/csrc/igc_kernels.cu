@@ -444,27 +444,50 @@ __global__ void ple_finish_kernel(const float *raw, const float *seed, int lanes
 // pair, the query normed and turned (app_core.c:11492-11494), scores with
 // scale 1.0 (app_core.c:11314) over the lane's own span ([pos - window + 1,
 // pos] on sliding layers, [0, pos] on global ones, app_core.c:11515-11518),
-// softmax, weighted values.  On an owner layer the block's new key and value
+// softmax, weighted values.  On an owner layer the pass's new key and value
 // rows are normed, turned and written into the cache here too
 // (app_core.c:11505-11512).
 //
-// The span is cut into chunks whose boundaries sit at fixed multiples of the
-// session's chunk length, so a position's partial sums never depend on how
-// many lanes a pass carried.  A block takes eight pairs, one a warp, and
-// walks chunks blockIdx.x, + gridDim.x, ...  Per 16-position tile, threads
-// l and l + 16 of a warp score position l over the two halves of the head
-// (the query read from shared memory by broadcast, the key row padded so the
-// warp's reads do not collide) and add their halves; the warp updates its
-// online softmax, and then thread l blends dimensions [l*DPL, (l+1)*DPL) of
-// the values.  Partials per chunk go to attn_combine_kernel.
-constexpr int ATT_T = 16;        // positions a tile
-constexpr int ATT_PAIRS = 8;     // (lane, head) pairs a block, one a warp
-constexpr int ATT_BLOCK_ROWS = 16;  // block positions a chunk can hold
+// One kernel: a cluster of CX blocks for each 16 query rows, the rows being
+// (lane, head) pairs of one key/value head, so that all of a block's rows
+// read the same keys and values.  Positions come in tiles of 16 at fixed
+// multiples of 16; block r of the cluster takes the tiles whose index is r
+// modulo CX, in ascending order, with an online softmax per row.  Scores
+// (16 rows x 16 positions) and weighted values are tensor-core products of
+// f16 hi/lo splits of both operands (hi*hi + hi*lo + lo*hi, f32 accumulate),
+// about 22 bits.  A tile's cached rows are bulk copies, the first ones
+// issued before the kernel waits on the projection ahead of it; the pass's
+// new rows are computed after the wait.  The cluster then merges its blocks'
+// partials through distributed shared memory: each block pushes its row
+// maxima, totals and values to the blocks that merge them, and block r
+// writes dimensions [r, r + 1) * hd / CX of every row.  Every sum is keyed on absolute
+// positions and runs in a fixed order, so a lane's output does not depend on
+// how many lanes share the pass.
+constexpr int AT_ROWS = 16;        // query rows a block
+constexpr int AT_POS = 16;         // positions a tile
+constexpr int AT_DEPTH = 3;        // tiles in flight a block
+constexpr int AT_SRED = 24;        // row stride of the score partials and weights
+constexpr int AT_MAX_CLUSTER = 16;
 
-__host__ __device__ inline size_t attn_smem_floats(int hd, int kv_w) {
-  const size_t ks = (size_t)kv_w + 4;
-  return (size_t)ATT_PAIRS * hd + 2 * (size_t)ATT_T * ks + 2 * (size_t)ATT_BLOCK_ROWS * ks;
-}
+template <int HD>
+struct AttnLayout {                  // offsets in floats
+  static constexpr int KS = HD + 8;  // key rows: a half-warp's float2 reads meet 32 banks
+  static constexpr int VS = HD + 4;  // value rows: a warp's scalar reads meet 32 banks
+  static constexpr int QS = HD + 4;
+  static constexpr int TILE = AT_POS * (KS + VS);  // a slot: 16 key rows, then 16 value rows
+  static constexpr int O_NEWK = AT_DEPTH * TILE;
+  static constexpr int O_NEWV = O_NEWK + AT_POS * KS;
+  static constexpr int O_Q = O_NEWV + AT_POS * VS;
+  static constexpr int O_ZERO = O_Q + AT_ROWS * QS;
+  static constexpr int O_SRED = O_ZERO + KS;                    // [8 warps][16][AT_SRED]
+  static constexpr int O_P = O_SRED + 8 * AT_ROWS * AT_SRED;    // hi, lo weights: 2 x [16][AT_SRED] halves
+  static constexpr int O_F = O_P + AT_ROWS * AT_SRED;
+  static constexpr int O_RO = O_F + AT_ROWS;              // pushed values: [sender][16][hd / CX]
+  static constexpr int O_RML = O_RO + AT_ROWS * HD;         // pushed maxima, totals: [sender][16][2]
+  static constexpr int O_AMX = O_RML + 2 * AT_ROWS * AT_MAX_CLUSTER;
+  static constexpr int O_BAR = (O_AMX + AT_ROWS + 1) & ~1;
+  static constexpr int FLOATS = O_BAR + 2 * AT_DEPTH;
+};
 
 template <int DPL>
 __device__ __forceinline__ void load_dpl(const float *src, float (&v)[DPL]) {
@@ -491,36 +514,6 @@ __device__ __forceinline__ void store_dpl(float *dst, const float (&v)[DPL]) {
   } else {
 #pragma unroll
     for (int e = 0; e < DPL; ++e) dst[e] = v[e];
-  }
-}
-
-// The blend's dimensions of thread l: with four or more a thread, the
-// float4s l, l + 32, ... of the head (consecutive threads on consecutive
-// banks); with fewer, the DPL consecutive dimensions from l * DPL.
-template <int DPL>
-__device__ __forceinline__ void load_blend(const float *row, int l, float (&v)[DPL]) {
-  if constexpr (DPL % 4 == 0) {
-#pragma unroll
-    for (int k = 0; k < DPL / 4; ++k) {
-      const float4 x = reinterpret_cast<const float4 *>(row)[l + 32 * k];
-      v[4 * k] = x.x;
-      v[4 * k + 1] = x.y;
-      v[4 * k + 2] = x.z;
-      v[4 * k + 3] = x.w;
-    }
-  } else {
-    load_dpl<DPL>(row + l * DPL, v);
-  }
-}
-
-template <int DPL>
-__device__ __forceinline__ void store_blend(float *row, int l, const float (&v)[DPL]) {
-  if constexpr (DPL % 4 == 0) {
-#pragma unroll
-    for (int k = 0; k < DPL / 4; ++k)
-      reinterpret_cast<float4 *>(row)[l + 32 * k] = make_float4(v[4 * k], v[4 * k + 1], v[4 * k + 2], v[4 * k + 3]);
-  } else {
-    store_dpl<DPL>(row + l * DPL, v);
   }
 }
 
@@ -556,237 +549,286 @@ __device__ __forceinline__ void head_norm_turn(float (&v)[DPL], const float *gai
   }
 }
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+__device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_t &lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const float2 b = __half22float2(h);
+  const __half2 r = __floats2half2_rn(x - b.x, y - b.y);
+  hi = *reinterpret_cast<const uint32_t *>(&h);
+  lo = *reinterpret_cast<const uint32_t *>(&r);
 }
 
-template <int DPL>
+template <int HD, int CX>
 __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_stride, int heads, int kv_heads,
                                                    const float *q_norm, const float *k_norm, const float *cs_tab,
                                                    const float *sn_tab, float eps, int owner, float *kc, float *vc,
-                                                   int sliding, int span, const int *d_p0, int lanes, int chunk_len,
-                                                   float *part_ml, float *part_acc) {
-  constexpr int HD = DPL * 32;
-  const int kv_w = kv_heads * HD, KS = kv_w + 4, half = HD / 2;
-  extern __shared__ __align__(16) float sm[];
-  float *qs = sm;                                // [8][HD]
-  float *ks = qs + ATT_PAIRS * HD;               // [ATT_T][KS]
-  float *vs = ks + (size_t)ATT_T * KS;           // [ATT_T][KS]
-  float *bk = vs + (size_t)ATT_T * KS;           // [16][KS] the block's new keys (owner layers)
-  float *bv = bk + (size_t)ATT_BLOCK_ROWS * KS;  // [16][KS] and values
-  const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
+                                                   int sliding, int span, const int *d_p0, int lanes, float *out,
+                                                   int out_stride, float *out_amax, int *err) {
+  using LY = AttnLayout<HD>;
+  constexpr int DPL = HD / 32, NKS = HD / 16, KPW = (NKS + 7) / 8, NNT = HD / 8, NPW = (NNT + 7) / 8;
+  constexpr int KS = LY::KS, VS = LY::VS, QS = LY::QS, DS = HD / CX;
+  static_assert(CX <= AT_MAX_CLUSTER && HD % CX == 0, "cluster size");
+  extern __shared__ __align__(128) float sm[];
+  float *ring = sm, *newk = sm + LY::O_NEWK, *newv = sm + LY::O_NEWV, *qs = sm + LY::O_Q, *zrow = sm + LY::O_ZERO;
+  float *sred = sm + LY::O_SRED, *fsc = sm + LY::O_F, *ro = sm + LY::O_RO, *rml = sm + LY::O_RML;
+  float *amx = sm + LY::O_AMX;
+  __half *ph = reinterpret_cast<__half *>(sm + LY::O_P), *pl = ph + AT_ROWS * AT_SRED;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + LY::O_BAR);
+  const int tid = threadIdx.x, warp = tid >> 5, l = tid & 31, g = l >> 2, t = l & 3;
+  const int r = blockIdx.x;  // rank in the cluster, which spans the grid's x
+  const int G = heads / kv_heads, row_blocks = (lanes * G + AT_ROWS - 1) / AT_ROWS;
+  const int kh = blockIdx.y / row_blocks, rb = blockIdx.y - kh * row_blocks;
+  const int kv_w = kv_heads * HD, half = HD / 2;
   pdl_release();
-  pdl_wait();
+
+  // this block's tiles: t0, t0 + CX, ... up to the pass's last position.  The
+  // position is written before the pass starts, so it is read before the wait.
   const int p0 = *d_p0;
-  const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
-  const int hi_all = p0 + lanes;
-  const int c_first = lo_all / chunk_len;
-  const int n_chunks = (hi_all - 1) / chunk_len - c_first + 1;
-  if ((int)blockIdx.x >= n_chunks) return;
-
-  // this warp's query, normed and turned at its lane's position
-  const int pair = blockIdx.y * ATT_PAIRS + warp;
-  const bool has = pair < lanes * heads;
-  const int j = has ? pair / heads : 0, h = has ? pair - (pair / heads) * heads : 0;
-  const int kvoff = (h / (heads / kv_heads)) * HD;
-  if (has) {
-    float qv[DPL];
-    load_dpl<DPL>(qkv + (size_t)j * qkv_stride + (size_t)h * HD + l * DPL, qv);
-    const int pos = p0 + j;
-    head_norm_turn<DPL>(qv, q_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps, true, l);
-    store_dpl<DPL>(qs + warp * HD + l * DPL, qv);
+  const int lo_all = sliding ? max(0, p0 - span + 1) : 0, hi_all = p0 + lanes;
+  const int t_first = lo_all / AT_POS, t_last = (hi_all - 1) / AT_POS;
+  const int t0 = t_first + (r - t_first % CX + CX) % CX;
+  const int n_tiles = t0 <= t_last ? (t_last - t0) / CX + 1 : 0;
+  const uint64_t policy = l2_evict_last();
+  // the cached rows of tile i (positions before the pass) into slot i %
+  // depth, by warp 0: lane 0 arms the barrier, then lane l copies key row l
+  // (l < 16) or value row l - 16
+  auto issue = [&](int i) {
+    const int tb = (t0 + i * CX) * AT_POS;
+    const int a = max(tb, lo_all), b = min(tb + AT_POS, p0);
+    float *slot = ring + (i % AT_DEPTH) * LY::TILE;
+    uint64_t *bar = &bars[i % AT_DEPTH];
+    if (l == 0) mbar_expect(bar, (uint32_t)(max(0, b - a) * HD * 8));
+    __syncwarp();
+    const int pos = tb + (l & 15);
+    if (pos >= a && pos < b) {
+      const size_t src = (size_t)pos * kv_w + (size_t)kh * HD;
+      if (l < 16)
+        bulk_load(slot + (pos - tb) * KS, kc + src, HD * 4, bar, policy);
+      else
+        bulk_load(slot + AT_POS * KS + (pos - tb) * VS, vc + src, HD * 4, bar, policy);
+    }
+  };
+  for (int i = tid; i < KS; i += blockDim.x) zrow[i] = 0.0f;
+  if (warp == 0) {
+    if (l == 0) {
+      for (int d = 0; d < AT_DEPTH; ++d) mbar_init(&bars[d], 1);
+      mbar_init_fence();
+    }
+    __syncwarp();
+    for (int i = 0; i < min(AT_DEPTH, n_tiles); ++i) issue(i);
   }
-  // the pair this warp scores: its lane's span
-  const int lane_lo = sliding ? max(0, p0 + j - span + 1) : 0;
-  const int lane_hi = p0 + j;
-  const int r_pos = l & (ATT_T - 1), hhalf = l >> 4;  // position and head half this thread scores
-  const int w4 = kv_w / 4;
 
-  for (int cr = blockIdx.x; cr < n_chunks; cr += gridDim.x) {
-    const int c = c_first + cr;
-    const int c_lo = max(c * chunk_len, lo_all), c_hi = min((c + 1) * chunk_len, hi_all);
-    __syncthreads();  // the previous chunk's block rows and tiles are consumed
-    // an owner layer's new keys and values that fall in this chunk: normed,
-    // turned (keys), kept in shared memory, and written to the cache once
-    int jb_lo = 0, jb_hi = 0;
+  pdl_wait();
+  // the queries, a warp a row, normed and turned at their lane's position
+  for (int row = warp; row < AT_ROWS; row += 8) {
+    const int f = rb * AT_ROWS + row, j = f / G, h = kh * G + (f - j * G);
+    float v[DPL];
+    if (j < lanes) {
+      load_dpl<DPL>(qkv + (size_t)j * qkv_stride + (size_t)h * HD + l * DPL, v);
+      const int pos = p0 + j;
+      head_norm_turn<DPL>(v, q_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps, true, l);
+    } else {
+#pragma unroll
+      for (int e = 0; e < DPL; ++e) v[e] = 0.0f;
+    }
+    store_dpl<DPL>(qs + row * QS + l * DPL, v);
+  }
+  // the pass's new key and value rows that fall in this block's tiles: on an
+  // owner layer normed, turned (keys) and written to the cache by the first
+  // row block; on a sharing layer read back from the owner's cache
+  for (int it = warp; it < 2 * lanes; it += 8) {
+    const int jj = it >> 1, is_v = it & 1, pos = p0 + jj, tile = pos / AT_POS;
+    if (tile < t0 || (tile - t0) % CX) continue;
+    const size_t at = (size_t)pos * kv_w + (size_t)kh * HD + l * DPL;
+    float v[DPL];
     if (owner) {
-      jb_lo = max(0, c * chunk_len - p0);
-      jb_hi = min(lanes, (c + 1) * chunk_len - p0);
-      const int per = 2 * kv_heads, items = max(0, jb_hi - jb_lo) * per;
-      for (int it = warp; it < items; it += ATT_PAIRS) {
-        const int jj = jb_lo + it / per, rest = it % per, kh = rest >> 1, is_v = rest & 1;
-        float v[DPL];
-        load_dpl<DPL>(qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + kh * HD + l * DPL, v);
-        const int pos = p0 + jj;
-        head_norm_turn<DPL>(v, is_v ? nullptr : k_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps,
-                            !is_v, l);
-        store_dpl<DPL>((is_v ? bv : bk) + (size_t)(jj - jb_lo) * KS + kh * HD + l * DPL, v);
-        if (blockIdx.y == 0) store_dpl<DPL>((is_v ? vc : kc) + (size_t)pos * kv_w + kh * HD + l * DPL, v);
-      }
+      load_dpl<DPL>(qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + kh * HD + l * DPL, v);
+      head_norm_turn<DPL>(v, is_v ? nullptr : k_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps,
+                          !is_v, l);
+      if (rb == 0) store_dpl<DPL>((is_v ? vc : kc) + at, v);
+    } else {
+      load_dpl<DPL>((is_v ? vc : kc) + at, v);
     }
+    store_dpl<DPL>((is_v ? newv + jj * VS : newk + jj * KS) + l * DPL, v);
+  }
+  __syncthreads();
 
-    float m_run = -FLT_MAX, l_run = 0.0f, acc[DPL];
+  // the query A fragments of this warp's k-steps (warp w: 16 columns from
+  // 16 (w + 8 i)); warps past the head's last k-step hold unused copies
+  uint32_t qh[KPW][4], ql[KPW][4];
 #pragma unroll
-    for (int e = 0; e < DPL; ++e) acc[e] = 0.0f;
-    for (int tb = c * chunk_len; tb < c_hi; tb += ATT_T) {
-      if (tb + ATT_T <= c_lo) continue;
-      __syncthreads();  // the previous tile is consumed (and the query and block rows are written)
-      for (int i = threadIdx.x; i < ATT_T * w4; i += blockDim.x) {
-        const int r = i / w4, d4 = i - r * w4, pos = tb + r;
-        float *kd = ks + (size_t)r * KS + d4 * 4, *vd = vs + (size_t)r * KS + d4 * 4;
-        if (pos < c_lo || pos >= c_hi) {
-          *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
-          *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
-        } else if (owner && pos - p0 >= jb_lo && pos - p0 < jb_hi) {
-          const int rb = pos - p0 - jb_lo;
-          *reinterpret_cast<float4 *>(kd) = *reinterpret_cast<const float4 *>(bk + (size_t)rb * KS + d4 * 4);
-          *reinterpret_cast<float4 *>(vd) = *reinterpret_cast<const float4 *>(bv + (size_t)rb * KS + d4 * 4);
-        } else {
-          cp_async16(kd, kc + (size_t)pos * kv_w + d4 * 4);
-          cp_async16(vd, vc + (size_t)pos * kv_w + d4 * 4);
-        }
-      }
-      asm volatile("cp.async.wait_all;\n" ::: "memory");
-      __syncthreads();
-      if (has) {
-        // scores: threads r and r + 16 take the even and odd float4s of
-        // position tb + r (the two halves' query reads then fall in
-        // different banks)
-        const int pos = tb + r_pos;
-        const float4 *qr = reinterpret_cast<const float4 *>(qs + warp * HD) + hhalf;
-        const float4 *kr = reinterpret_cast<const float4 *>(ks + (size_t)r_pos * KS + kvoff) + hhalf;
-        float a0 = 0.f, a1 = 0.f;
-#pragma unroll 4
-        for (int m = 0; m < HD / 8; m += 2) {
-          const float4 q0 = qr[2 * m], k0 = kr[2 * m];
-          a0 = fmaf(q0.x, k0.x, a0); a0 = fmaf(q0.y, k0.y, a0); a0 = fmaf(q0.z, k0.z, a0); a0 = fmaf(q0.w, k0.w, a0);
-          if (m + 1 < HD / 8) {
-            const float4 q1 = qr[2 * m + 2], k1 = kr[2 * m + 2];
-            a1 = fmaf(q1.x, k1.x, a1); a1 = fmaf(q1.y, k1.y, a1); a1 = fmaf(q1.z, k1.z, a1); a1 = fmaf(q1.w, k1.w, a1);
-          }
-        }
-        const float part = a0 + a1;
-        const float other = __shfl_xor_sync(0xffffffffu, part, 16);
-        const float s = hhalf == 0 ? part + other : other + part;  // the same sum in both threads
-        const bool valid = pos >= c_lo && pos < c_hi && pos >= lane_lo && pos <= lane_hi;
-        const float sc = valid ? s : -FLT_MAX;
-        // online softmax over the tile's 16 positions (each held twice)
-        const float m_new = fmaxf(m_run, warp_max(sc));
-        const float f = (m_new == -FLT_MAX) ? 1.0f : (m_run == -FLT_MAX ? 0.0f : expf(m_run - m_new));
-        const float pe = valid ? expf(sc - m_new) : 0.0f;
-        float psum = pe;
+  for (int i = 0; i < KPW; ++i) {
+    const float *q0 = qs + g * QS + 16 * min(warp + 8 * i, NKS - 1) + 2 * t, *q8 = q0 + 8 * QS;
+    split_h2(q0[0], q0[1], qh[i][0], ql[i][0]);
+    split_h2(q8[0], q8[1], qh[i][1], ql[i][1]);
+    split_h2(q0[8], q0[9], qh[i][2], ql[i][2]);
+    split_h2(q8[8], q8[9], qh[i][3], ql[i][3]);
+  }
+  // the softmax thread of (row sr, position sp of a tile) and its row's span
+  const int sr = tid >> 4, sp = tid & 15;
+  const int sj = (rb * AT_ROWS + sr) / G;
+  const bool row_ok = sj < lanes;
+  const int lo_r = sliding ? max(0, p0 + sj - span + 1) : 0, hi_r = p0 + sj;
+  float m_run = -FLT_MAX, l_run = 0.0f;
+  float oacc[NPW][4];
 #pragma unroll
-        for (int o = 1; o < ATT_T; o <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, o);
-        l_run = l_run * f + psum;
-        m_run = m_new;
+  for (int i = 0; i < NPW; ++i)
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) acc[e] *= f;
-        // blend: thread l takes the dimensions of blend_dim(l, e) of every
-        // position (float4s l, l + 32, ... where the head has them)
-#pragma unroll 4
-        for (int r = 0; r < ATT_T; ++r) {
-          const float pr = __shfl_sync(0xffffffffu, pe, r);
-          float vv[DPL];
-          load_blend<DPL>(vs + (size_t)r * KS + kvoff, l, vv);
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) acc[e] = fmaf(pr, vv[e], acc[e]);
-        }
-      }
+    for (int e = 0; e < 4; ++e) oacc[i][e] = 0.0f;
+  bool failed = false;
+
+  for (int i = 0; i < n_tiles; ++i) {
+    const int tb = (t0 + i * CX) * AT_POS;
+    const float *slot = ring + (i % AT_DEPTH) * LY::TILE;
+    if (!mbar_wait(&bars[i % AT_DEPTH], (uint32_t)((i / AT_DEPTH) & 1), failed ? 1 : (1 << 22))) {
+      if (!failed && tid == 0) atomicOr(err, 2);
+      failed = true;
     }
-    if (has) {
-      const size_t slot = ((size_t)cr * 16 + j) * heads + h;
-      if (l == 0) {
-        part_ml[slot * 2 + 0] = m_run;
-        part_ml[slot * 2 + 1] = l_run;
+    // a position's key and value rows: new, cached, or zeros outside the pass's span
+    auto krow = [&](int pos) -> const float * {
+      return (pos < lo_all || pos >= hi_all) ? zrow : pos >= p0 ? newk + (pos - p0) * KS : slot + (pos - tb) * KS;
+    };
+    auto vrow = [&](int pos) -> const float * {
+      return (pos < lo_all || pos >= hi_all) ? zrow
+             : pos >= p0                      ? newv + (pos - p0) * VS
+                                              : slot + AT_POS * KS + (pos - tb) * VS;
+    };
+    // scores: this warp's k-steps of the 16 x 16 tile, into the partials;
+    // the three split products in separate accumulators (short chains),
+    // added as hi*hi + (hi*lo + lo*hi)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      float shh[4] = {0.0f, 0.0f, 0.0f, 0.0f}, shl[4] = {0.0f, 0.0f, 0.0f, 0.0f}, slh[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const float *kr = krow(tb + 8 * nt + g) + 2 * t;
+#pragma unroll
+      for (int i2 = 0; i2 < KPW; ++i2) {
+        const int ks = warp + 8 * i2;
+        if (ks < NKS) {
+          const float2 k01 = *reinterpret_cast<const float2 *>(kr + 16 * ks);
+          const float2 k89 = *reinterpret_cast<const float2 *>(kr + 16 * ks + 8);
+          uint32_t bh0, bl0, bh1, bl1;
+          split_h2(k01.x, k01.y, bh0, bl0);
+          split_h2(k89.x, k89.y, bh1, bl1);
+          mma16816(shh, qh[i2], bh0, bh1, shh);
+          mma16816(shl, qh[i2], bl0, bl1, shl);
+          mma16816(slh, ql[i2], bh0, bh1, slh);
+        }
       }
-      store_blend<DPL>(part_acc + slot * HD, l, acc);
+      float sc[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] = shh[e] + (shl[e] + slh[e]);
+      float *sw = sred + (warp * AT_ROWS + g) * AT_SRED + 8 * nt + 2 * t;
+      *reinterpret_cast<float2 *>(sw) = make_float2(sc[0], sc[1]);
+      *reinterpret_cast<float2 *>(sw + 8 * AT_SRED) = make_float2(sc[2], sc[3]);
+    }
+    __syncthreads();  // the partials are written, and every warp is past tile i - 1
+    if (warp == 0 && i >= 1 && i - 1 + AT_DEPTH < n_tiles) {
+      fence_async_smem();
+      issue(i - 1 + AT_DEPTH);
+    }
+    // online softmax of row sr, one thread a position; the warps' partials
+    // added in warp order
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += sred[(w * AT_ROWS + sr) * AT_SRED + sp];
+    const int pos = tb + sp;
+    const bool valid = row_ok && pos >= lo_r && pos <= hi_r;
+    const float sv = valid ? s : -FLT_MAX;
+    float mt = sv;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+    const float m_new = fmaxf(m_run, mt);
+    const float fct = (m_new == -FLT_MAX) ? 1.0f : (m_run == -FLT_MAX ? 0.0f : expf(m_run - m_new));
+    const float e = valid ? expf(sv - m_new) : 0.0f;
+    float es = e;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) es += __shfl_xor_sync(0xffffffffu, es, o);
+    l_run = l_run * fct + es;
+    m_run = m_new;
+    const __half eh = __float2half_rn(e);
+    ph[sr * AT_SRED + sp] = eh;
+    pl[sr * AT_SRED + sp] = __float2half_rn(e - __half2float(eh));
+    if (sp == 0) fsc[sr] = fct;
+    __syncthreads();  // the weights and factors are written
+    // weighted values: this warp's 8-dimension tiles n = warp + 8 i
+    {
+      const uint32_t *h32 = reinterpret_cast<const uint32_t *>(ph), *l32 = reinterpret_cast<const uint32_t *>(pl);
+      constexpr int W = AT_SRED / 2;  // words a row
+      const uint32_t pah[4] = {h32[g * W + t], h32[(g + 8) * W + t], h32[g * W + t + 4], h32[(g + 8) * W + t + 4]};
+      const uint32_t pal[4] = {l32[g * W + t], l32[(g + 8) * W + t], l32[g * W + t + 4], l32[(g + 8) * W + t + 4]};
+      const float f0 = fsc[g], f8 = fsc[g + 8];
+      const float *v0 = vrow(tb + 2 * t), *v1 = vrow(tb + 2 * t + 1), *v8 = vrow(tb + 2 * t + 8),
+                  *v9 = vrow(tb + 2 * t + 9);
+#pragma unroll
+      for (int i2 = 0; i2 < NPW; ++i2) {
+        const int nt = warp + 8 * i2;
+        if (nt < NNT) {
+          const int n = 8 * nt + g;
+          uint32_t bh0, bl0, bh1, bl1;
+          split_h2(v0[n], v1[n], bh0, bl0);
+          split_h2(v8[n], v9[n], bh1, bl1);
+          const float z[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+          float thh[4], thl[4], tlh[4];
+          mma16816(thh, pah, bh0, bh1, z);
+          mma16816(thl, pah, bl0, bl1, z);
+          mma16816(tlh, pal, bh0, bh1, z);
+          oacc[i2][0] = fmaf(oacc[i2][0], f0, thh[0] + (thl[0] + tlh[0]));
+          oacc[i2][1] = fmaf(oacc[i2][1], f0, thh[1] + (thl[1] + tlh[1]));
+          oacc[i2][2] = fmaf(oacc[i2][2], f8, thh[2] + (thl[2] + tlh[2]));
+          oacc[i2][3] = fmaf(oacc[i2][3], f8, thh[3] + (thl[3] + tlh[3]));
+        }
+      }
     }
   }
-}
-
-// attention, second step: the chunks' partials merged into each head's
-// output, (sum_c acc_c e^{m_c - M}) / (sum_c l_c e^{m_c - M}).  Blocks
-// (lane, head, 64-dimension slice).  Every sum is keyed on the absolute
-// chunk index, so a chunk outside a lane's span (zero weight, zero partials)
-// changes nothing and the result does not depend on how many lanes shared
-// the pass: warp 0's thread t adds the weighted l_c of chunks c = t mod 32 in
-// ascending order and the warp adds the 32 sums in a fixed tree; thread
-// (g, d) adds acc_c of chunks c = g mod 4 in ascending order and the four
-// groups are added in order.
-constexpr int COMB_GROUPS = 4, COMB_DIMS = 64;
-
-__global__ void __launch_bounds__(COMB_GROUPS * COMB_DIMS) attn_combine_kernel(const float *part_ml, const float *part_acc,
-                                                                               int lanes, int heads, int hd, int sliding,
-                                                                               int span, int chunk_len, const int *d_p0,
-                                                                               float *out, int out_stride,
-                                                                               float *out_amax) {
-  __shared__ float wgt[1024];
-  __shared__ float grp[COMB_GROUPS][COMB_DIMS];
-  __shared__ float tot;
-  pdl_release();
-  pdl_wait();
-  const int slices = (hd + COMB_DIMS - 1) / COMB_DIMS;
-  const int pair = blockIdx.x / slices, dslice = blockIdx.x - pair * slices;
-  const int j = pair / heads, h = pair % heads;
-  if (j >= lanes) return;
-  const int p0 = *d_p0;
-  const int lo_all = sliding ? max(0, p0 - span + 1) : 0;
-  const int hi_all = p0 + lanes;
-  const int c_first = lo_all / chunk_len;
-  const int n_chunks = (hi_all - 1) / chunk_len - c_first + 1;
-  const size_t cstride = (size_t)16 * heads;  // slots between chunks
-  const size_t s0 = (size_t)j * heads + h;
-  if (threadIdx.x < 32) {
-    constexpr int MAXC = 1024 / 32;
-    // thread t holds the chunks whose absolute index is t mod 32
-    const int t0 = (threadIdx.x - c_first % 32 + 32) % 32;  // first relative chunk of this thread
-    float m[MAXC], lv[MAXC];
+  // push this block's partials to the blocks that merge them: the weighted
+  // values of dimensions [q DS, (q + 1) DS) to block q, and every row's
+  // maximum and total to every block (remote stores into buffers nothing
+  // else uses, made visible by the cluster barrier)
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-      const int c = t0 + 32 * i;
-      m[i] = c < n_chunks ? part_ml[(c * cstride + s0) * 2] : -FLT_MAX;
-      lv[i] = c < n_chunks ? part_ml[(c * cstride + s0) * 2 + 1] : 0.0f;
+  for (int i2 = 0; i2 < NPW; ++i2) {
+    const int nt = warp + 8 * i2;
+    if (nt < NNT) {
+      const int d = 8 * nt + 2 * t, q = d / DS;
+      float *at = ro + (r * AT_ROWS + g) * DS + (d - q * DS);
+      st_cluster2(at, q, oacc[i2][0], oacc[i2][1]);
+      st_cluster2(at + 8 * DS, q, oacc[i2][2], oacc[i2][3]);
     }
+  }
+  if (sp < CX) st_cluster2(rml + 2 * (r * AT_ROWS + sr), sp, m_run, l_run);
+  if (tid < AT_ROWS) amx[tid] = 0.0f;
+  cluster_sync();
+  // block r merges dimensions [r * DS, (r + 1) * DS) of every row, a thread a
+  // pair of them: block weights e^{m_q - M}, totals and values in rank order
+  constexpr int DP = DS / 2;
+  static_assert(AT_ROWS * DP <= 256, "one pass of the block");
+  if (tid < AT_ROWS * DP) {
+    const int row = tid / DP, dd = 2 * (tid - row * DP), d = r * DS + dd;
+    float2 mlq[CX];
+#pragma unroll
+    for (int q = 0; q < CX; ++q) mlq[q] = *reinterpret_cast<const float2 *>(rml + 2 * (q * AT_ROWS + row));
     float M = -FLT_MAX;
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) M = fmaxf(M, m[i]);
-    M = warp_max(M);
-    float L = 0.0f;
+    for (int q = 0; q < CX; ++q) M = fmaxf(M, mlq[q].x);
+    float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
 #pragma unroll
-    for (int i = 0; i < MAXC; ++i) {
-      const int c = t0 + 32 * i;
-      const float w = (m[i] == -FLT_MAX) ? 0.0f : expf(m[i] - M);
-      if (c < n_chunks) wgt[c] = w;
-      L += lv[i] * w;
+    for (int q = 0; q < CX; ++q) {
+      const float w = mlq[q].x == -FLT_MAX ? 0.0f : expf(mlq[q].x - M);
+      const float2 x = *reinterpret_cast<const float2 *>(ro + (q * AT_ROWS + row) * DS + dd);
+      L += mlq[q].y * w;
+      o0 = fmaf(x.x, w, o0);
+      o1 = fmaf(x.y, w, o1);
     }
-    L = warp_sum(L);
-    if (threadIdx.x == 0) tot = L;
+    const float inv = 1.0f / L, v0 = o0 * inv, v1 = o1 * inv;
+    const int f = rb * AT_ROWS + row, j = f / G, h = kh * G + (f - j * G);
+    if (j < lanes) {
+      *reinterpret_cast<float2 *>(out + (size_t)j * out_stride + (size_t)h * HD + d) = make_float2(v0, v1);
+      if (out_amax) atomicMax(reinterpret_cast<int *>(amx + row), __float_as_int(fmaxf(fabsf(v0), fabsf(v1))));
+    }
   }
   __syncthreads();
-  const int g = threadIdx.x / COMB_DIMS, dl = threadIdx.x - g * COMB_DIMS, d = dslice * COMB_DIMS + dl;
-  float o = 0.0f;
-  if (d < hd) {
-    const int cg0 = (g - c_first % COMB_GROUPS + COMB_GROUPS) % COMB_GROUPS;  // first relative chunk of group g
-#pragma unroll 4
-    for (int c = cg0; c < n_chunks; c += COMB_GROUPS) o += part_acc[(c * cstride + s0) * hd + d] * wgt[c];
-  }
-  grp[g][dl] = o;
-  __syncthreads();
-  float v = 0.0f;
-  if (threadIdx.x < COMB_DIMS && d < hd) {
-    v = grp[0][dl];
-#pragma unroll
-    for (int q = 1; q < COMB_GROUPS; ++q) v += grp[q][dl];
-    v *= 1.0f / tot;
-    out[(size_t)j * out_stride + (size_t)h * hd + d] = v;
-  }
-  if (out_amax && threadIdx.x < COMB_DIMS) {
-    // this block's largest |out|: one partial a (head, slice) for lane j
-    __shared__ float amx[COMB_DIMS / 32];
-    const float m = warp_max(fabsf(v));
-    if ((threadIdx.x & 31) == 0) amx[threadIdx.x >> 5] = m;
-    named_sync(1, COMB_DIMS);
-    if (threadIdx.x == 0) out_amax[(size_t)j * GEMV_PART_LIMIT + h * slices + dslice] = fmaxf(amx[0], amx[1]);
+  if (out_amax && tid < AT_ROWS) {
+    // one magnitude partial a (head, block) for lane j
+    const int f = rb * AT_ROWS + tid, j = f / G, h = kh * G + (f - j * G);
+    if (j < lanes) out_amax[(size_t)j * GEMV_PART_LIMIT + h * CX + r] = amx[tid];
   }
 }
 
@@ -1148,6 +1190,16 @@ using namespace igc;
 
 extern "C" {
 
+extern "C++" {
+template <int HD>
+static cudaError_t allow_attn(int bytes) {
+  cudaError_t e = allow_smem_fn(attn_kernel<HD, 8>, bytes);
+  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 16>, bytes);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<HD, 16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  return e;
+}
+}  // extern "C++"
+
 // Lets every kernel of this file use up to `bytes` of dynamic shared memory
 // on the current device; called once per device before the first launch.
 cudaError_t igc_kernels_configure(int bytes) {
@@ -1161,10 +1213,10 @@ cudaError_t igc_kernels_configure(int bytes) {
   if (e == cudaSuccess) e = allow_smem_mode<MODE_NT1, 16>(bytes);
   if (e == cudaSuccess) e = allow_smem_mode<MODE_NT1, 8>(bytes);
   if (e == cudaSuccess) e = allow_smem_mode<MODE_NT2, 8>(bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<1>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<2>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<4>, bytes);
-  if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<8>, bytes);
+  if (e == cudaSuccess) e = allow_attn<32>(bytes);
+  if (e == cudaSuccess) e = allow_attn<64>(bytes);
+  if (e == cudaSuccess) e = allow_attn<128>(bytes);
+  if (e == cudaSuccess) e = allow_attn<256>(bytes);
   if (e == cudaSuccess) e = allow_smem_fn(topk_stage2_kernel, bytes);
   return e;
 }
@@ -1243,31 +1295,65 @@ cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes
                   blend, out);
 }
 
-size_t igc_attn_smem(int hd, int kv_w) { return sizeof(float) * attn_smem_floats(hd, kv_w); }
+size_t igc_attn_smem(int hd) {
+  switch (hd) {
+    case 32: return sizeof(float) * AttnLayout<32>::FLOATS;
+    case 64: return sizeof(float) * AttnLayout<64>::FLOATS;
+    case 128: return sizeof(float) * AttnLayout<128>::FLOATS;
+    case 256: return sizeof(float) * AttnLayout<256>::FLOATS;
+    default: return 0;
+  }
+}
+
+extern "C++" {
+template <int HD, int CX>
+static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const float *qkv, int qkv_stride, int heads,
+                               int kv_heads, const float *q_norm, const float *k_norm, const float *cs,
+                               const float *sn, float eps, int owner, float *kc, float *vc, int sliding, int span,
+                               const int *d_p0, int lanes, float *out, int out_stride, float *out_amax, int *err) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = CX;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = g_pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, CX>, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
+                            owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, err);
+}
+}  // extern "C++"
 
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
-                            float *vc, int sliding, int span, const int *d_p0, int lanes, int chunk_len, int grid_x,
-                            float *part_ml, float *part_acc, float *out, int out_stride, float *out_amax,
-                            cudaStream_t st) {
-  const size_t smem = igc_attn_smem(hd, kv_heads * hd);
-  const dim3 grid(grid_x, (lanes * heads + ATT_PAIRS - 1) / ATT_PAIRS);
-  cudaError_t e;
-#define IGC_ATT(D)                                                                                              \
-  e = launch_k(attn_kernel<D>, grid, dim3(256), smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, \
-               eps, owner, kc, vc, sliding, span, d_p0, lanes, chunk_len, part_ml, part_acc);
+                            float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
+                            int out_stride, float *out_amax, int *err, cudaStream_t st) {
+  if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads || (cluster != 8 && cluster != 16))
+    return cudaErrorInvalidValue;
+  const size_t smem = igc_attn_smem(hd);
+  const int G = heads / kv_heads;
+  const dim3 grid(cluster, kv_heads * ((lanes * G + AT_ROWS - 1) / AT_ROWS));
+#define IGC_ATT(HD)                                                                                              \
+  return cluster == 8 ? launch_attn<HD, 8>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
+                                           sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,   \
+                                           out_amax, err)                                                         \
+                      : launch_attn<HD, 16>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
+                                            sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,  \
+                                            out_amax, err);
   switch (hd) {
-    case 32: IGC_ATT(1) break;
-    case 64: IGC_ATT(2) break;
-    case 128: IGC_ATT(4) break;
-    case 256: IGC_ATT(8) break;
+    case 32: IGC_ATT(32)
+    case 64: IGC_ATT(64)
+    case 128: IGC_ATT(128)
+    case 256: IGC_ATT(256)
     default: return cudaErrorInvalidValue;
   }
 #undef IGC_ATT
-  if (e != cudaSuccess) return e;
-  const int slices = (hd + COMB_DIMS - 1) / COMB_DIMS;
-  return launch_k(attn_combine_kernel, dim3(lanes * heads * slices), dim3(COMB_GROUPS * COMB_DIMS), 0, st, part_ml,
-                  part_acc, lanes, heads, hd, sliding, span, chunk_len, d_p0, out, out_stride, out_amax);
 }
 
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,

@@ -32,16 +32,17 @@ cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embe
                              float *x_out, float *seed_out, cudaStream_t st);
 cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes, int layers, int ple_dim,
                                   const float *w, float eps, float blend, float *out, cudaStream_t st);
-size_t igc_attn_smem(int hd, int kv_w);
-// Attention for one layer (query norm and rope, an owner layer's cache
-// writes, chunked scores and blend) and the merge of the chunks' partials;
-// `out_amax`, when given, gets each lane's largest |out| per (head, 64-dim
-// slice), [heads * ceil(hd / 64)][16].
+size_t igc_attn_smem(int hd);
+// Attention for one layer in one kernel (query norm and rope, an owner
+// layer's cache writes, scores, softmax and values over 16-position tiles,
+// and the merge of the cluster's partials); `cluster` (8 or 16) blocks a
+// cluster, a session constant.  `out_amax`, when given, gets each lane's
+// largest |out| per (head, cluster block), [heads * cluster][16]; `err` gets
+// bit 2 if a tile copy never arrived.
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
-                            float *vc, int sliding, int span, const int *d_p0, int lanes, int chunk_len, int grid_x,
-                            float *part_ml, float *part_acc, float *out, int out_stride, float *out_amax,
-                            cudaStream_t st);
+                            float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
+                            int out_stride, float *out_amax, int *err, cudaStream_t st);
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
                               cudaStream_t st);
 cudaError_t igc_launch_rope_table(const float *steps, int half, int window, float *cs, float *sn,

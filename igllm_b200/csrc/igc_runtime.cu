@@ -693,7 +693,7 @@ static int bind_model(igc_model *m, Source &src) {
       L.gain = g ? real_at(*g, 0) : 1.0f; /* app_core.c:8700-8708 */
     }
 #undef STEM
-    if (igc_attn_smem(L.hd, L.kv_rows) > (size_t)m->smem_limit) return IGC_FAIL_SUPPORT;
+    if (!igc_attn_smem(L.hd) || igc_attn_smem(L.hd) > (size_t)m->smem_limit) return IGC_FAIL_SUPPORT;
     if (L.qkv_rows > m->max_qkv) m->max_qkv = L.qkv_rows;
     if (L.inner > m->max_inner) m->max_inner = L.inner;
     if (L.q_rows > m->max_q) m->max_q = L.q_rows;
@@ -787,7 +787,7 @@ struct igc_session {
   float *x0 = nullptr, *xa = nullptr, *xb = nullptr, *seed = nullptr, *ple_raw = nullptr, *ple = nullptr;
   float *qkv = nullptr, *attn = nullptr, *obuf = nullptr, *act = nullptr, *dbuf = nullptr, *pa = nullptr,
         *pp = nullptr, *logits = nullptr;
-  float *part_ml = nullptr, *part_acc = nullptr, *arg_val = nullptr;
+  float *arg_val = nullptr;
   float *ssq_o = nullptr, *ssq_d = nullptr, *ssq_pp = nullptr;
   float *amax_attn = nullptr, *amax_act = nullptr, *amax_pa = nullptr;  // magnitude partials
   int *arg_idx = nullptr;
@@ -799,8 +799,7 @@ struct igc_session {
   float *h_top_v = nullptr;
   int *h_top_i = nullptr;
   int logit_lanes = 0;  // rows the last pass left in `logits`
-  int chunk_len = 16;   // attention chunk length, fixed for the session
-  int max_chunks = 0;   // chunks the longest span can cover
+  int attn_cluster = 16;  // attention blocks a cluster, fixed for the session
   int use_graphs = 1;
   int use_pdl = 1;
   int head_parts = 0;  // argmax partials the output head's launch left
@@ -884,12 +883,6 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (c == IGC_OKAY) c = s->alloc(&s->pa, (size_t)K * (m->ple_dim ? m->ple_dim : 1));
   if (c == IGC_OKAY) c = s->alloc(&s->pp, (size_t)K * H);
   if (c == IGC_OKAY) c = s->alloc(&s->logits, (size_t)K * m->vocab);
-  // attention chunks: a power of two of at least 16 positions, at most 256
-  // of them over the window, so the partials stay a few tens of MB
-  while ((m->window_limit + s->chunk_len - 1) / s->chunk_len > 256) s->chunk_len *= 2;
-  s->max_chunks = (m->window_limit + s->chunk_len - 1) / s->chunk_len + 2;
-  if (c == IGC_OKAY) c = s->alloc(&s->part_ml, (size_t)s->max_chunks * K * m->heads * 2);
-  if (c == IGC_OKAY) c = s->alloc(&s->part_acc, (size_t)s->max_chunks * K * m->max_q);
   if (c == IGC_OKAY) c = s->alloc(&s->arg_val, (size_t)s->arg_parts * 16);
   if (c == IGC_OKAY) c = s->alloc(&s->arg_idx, (size_t)s->arg_parts * 16);
   if (c == IGC_OKAY) c = s->alloc(&s->ssq_o, (size_t)s->arg_parts * 16);
@@ -921,6 +914,10 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   s->use_graphs = !(g && g[0] == '1');
   const char *np = getenv("IGC_NO_PDL");
   s->use_pdl = !(np && np[0] == '1');
+  // attention clusters of 16 blocks (half the tiles a block of 8 takes)
+  // unless IGC_ATTN_CLUSTER=8 or the heads' magnitude partials would not fit
+  const char *ac = getenv("IGC_ATTN_CLUSTER");
+  s->attn_cluster = (ac && atoi(ac) == 8) || m->heads * 16 > GEMV_PART_LIMIT ? 8 : 16;
   *out = s.release();
   return IGC_OKAY;
 }
@@ -1117,21 +1114,12 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
     prof_mark(s, PROF_ATTN, 0.0);
-    // chunks a span can touch: the window plus the block on sliding layers,
-    // the whole context on global ones (blocks past the live count exit)
-    // blocks walk the chunks with a stride of grid_x: about two blocks an
-    // SM over all pair groups, never more than the span can have chunks
     const int sliding = L.kind == 0 ? 1 : 0;
-    const int groups = (K * m->heads + 7) / 8;
-    int grid_x = s->max_chunks;
-    if (sliding) grid_x = std::min(grid_x, (m->slide_span + IGC_LANE_LIMIT) / s->chunk_len + 2);
-    grid_x = std::max(1, std::min(grid_x, (2 * m->sm_count + groups - 1) / groups));
     CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                         m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
-                        m->slide_span, d_p0, K, s->chunk_len, grid_x, s->part_ml, s->part_acc, s->attn, L.q_rows,
-                        mags ? ma.buf : nullptr, s->st));
-    ++g_launches;  // the combine kernel
-    ma.parts = m->heads * ((L.hd + 63) / 64);
+                        m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
+                        s->d_err, s->st));
+    ma.parts = m->heads * s->attn_cluster;
     c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
              1.0f, nullptr, 0, nullptr, &so, ma_in);
     if (c != IGC_OKAY) return c;
