@@ -455,9 +455,10 @@ __global__ void ple_finish_kernel(const float *raw, const float *seed, int lanes
 // modulo CX, in ascending order, with an online softmax per row.  Scores
 // (16 rows x 16 positions) and weighted values are tensor-core products of
 // f16 hi/lo splits of both operands (hi*hi + hi*lo + lo*hi, f32 accumulate),
-// about 22 bits.  A tile's cached rows are bulk copies, the first ones
-// issued before the kernel waits on the projection ahead of it; the pass's
-// new rows are computed after the wait.  The cluster then merges its blocks'
+// about 22 bits.  A tile's cached rows arrive by 16-byte asynchronous
+// copies spread over the block, the first tiles' issued before the kernel
+// waits on the projection ahead of it; the pass's new rows are computed
+// after the wait.  The cluster then merges its blocks'
 // partials through distributed shared memory: each block pushes its row
 // maxima, totals and values to the blocks that merge them, and block r
 // writes dimensions [r, r + 1) * hd / CX of every row.  Every sum is keyed on absolute
@@ -485,8 +486,7 @@ struct AttnLayout {                  // offsets in floats
   static constexpr int O_RO = O_F + AT_ROWS;              // pushed values: [sender][16][hd / CX]
   static constexpr int O_RML = O_RO + AT_ROWS * HD;         // pushed maxima, totals: [sender][16][2]
   static constexpr int O_AMX = O_RML + 2 * AT_ROWS * AT_MAX_CLUSTER;
-  static constexpr int O_BAR = (O_AMX + AT_ROWS + 1) & ~1;
-  static constexpr int FLOATS = O_BAR + 2 * AT_DEPTH;
+  static constexpr int FLOATS = O_AMX + AT_ROWS;
 };
 
 template <int DPL>
@@ -549,6 +549,17 @@ __device__ __forceinline__ void head_norm_turn(float (&v)[DPL], const float *gai
   }
 }
 
+__device__ __forceinline__ void cp_async16(float *dst, const float *src, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(smem_u32(dst)), "l"(src),
+               "l"(policy)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
 __device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_t &lo) {
   const __half2 h = __floats2half2_rn(x, y);
   const float2 b = __half22float2(h);
@@ -562,7 +573,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
                                                    const float *q_norm, const float *k_norm, const float *cs_tab,
                                                    const float *sn_tab, float eps, int owner, float *kc, float *vc,
                                                    int sliding, int span, const int *d_p0, int lanes, float *out,
-                                                   int out_stride, float *out_amax, int *err) {
+                                                   int out_stride, float *out_amax) {
   using LY = AttnLayout<HD>;
   constexpr int DPL = HD / 32, NKS = HD / 16, KPW = (NKS + 7) / 8, NNT = HD / 8, NPW = (NNT + 7) / 8;
   constexpr int KS = LY::KS, VS = LY::VS, QS = LY::QS, DS = HD / CX;
@@ -572,7 +583,6 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   float *sred = sm + LY::O_SRED, *fsc = sm + LY::O_F, *ro = sm + LY::O_RO, *rml = sm + LY::O_RML;
   float *amx = sm + LY::O_AMX;
   __half *ph = reinterpret_cast<__half *>(sm + LY::O_P), *pl = ph + AT_ROWS * AT_SRED;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + LY::O_BAR);
   const int tid = threadIdx.x, warp = tid >> 5, l = tid & 31, g = l >> 2, t = l & 3;
   const int r = blockIdx.x;  // rank in the cluster, which spans the grid's x
   const int G = heads / kv_heads, row_blocks = (lanes * G + AT_ROWS - 1) / AT_ROWS;
@@ -589,32 +599,29 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   const int n_tiles = t0 <= t_last ? (t_last - t0) / CX + 1 : 0;
   const uint64_t policy = l2_evict_last();
   // the cached rows of tile i (positions before the pass) into slot i %
-  // depth, by warp 0: lane 0 arms the barrier, then lane l copies key row l
-  // (l < 16) or value row l - 16
+  // depth: 16-byte asynchronous copies spread over the block (thread t the
+  // column 4 (t mod hd/4) of rows t / (hd/4), + 256 / (hd/4), ...), one
+  // commit group a tile
+  constexpr int CP_C4 = HD / 4, CP_RPP = 256 / CP_C4;
+  const int cp_col = 4 * (tid % CP_C4), cp_r0 = tid / CP_C4;
   auto issue = [&](int i) {
     const int tb = (t0 + i * CX) * AT_POS;
     const int a = max(tb, lo_all), b = min(tb + AT_POS, p0);
     float *slot = ring + (i % AT_DEPTH) * LY::TILE;
-    uint64_t *bar = &bars[i % AT_DEPTH];
-    if (l == 0) mbar_expect(bar, (uint32_t)(max(0, b - a) * HD * 8));
-    __syncwarp();
-    const int pos = tb + (l & 15);
-    if (pos >= a && pos < b) {
-      const size_t src = (size_t)pos * kv_w + (size_t)kh * HD;
-      if (l < 16)
-        bulk_load(slot + (pos - tb) * KS, kc + src, HD * 4, bar, policy);
-      else
-        bulk_load(slot + AT_POS * KS + (pos - tb) * VS, vc + src, HD * 4, bar, policy);
+#pragma unroll
+    for (int row = cp_r0; row < AT_POS; row += CP_RPP) {
+      const int pos = tb + row;
+      if (pos >= a && pos < b) {
+        const size_t src = (size_t)pos * kv_w + (size_t)kh * HD + cp_col;
+        cp_async16(slot + row * KS + cp_col, kc + src, policy);
+        cp_async16(slot + AT_POS * KS + row * VS + cp_col, vc + src, policy);
+      }
     }
   };
   for (int i = tid; i < KS; i += blockDim.x) zrow[i] = 0.0f;
-  if (warp == 0) {
-    if (l == 0) {
-      for (int d = 0; d < AT_DEPTH; ++d) mbar_init(&bars[d], 1);
-      mbar_init_fence();
-    }
-    __syncwarp();
-    for (int i = 0; i < min(AT_DEPTH, n_tiles); ++i) issue(i);
+  for (int i = 0; i < AT_DEPTH; ++i) {
+    if (i < n_tiles) issue(i);
+    cp_async_commit();
   }
 
   pdl_wait();
@@ -650,8 +657,9 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     }
     store_dpl<DPL>((is_v ? newv + jj * VS : newk + jj * KS) + l * DPL, v);
   }
-  __syncthreads();
 
+  cp_async_wait<AT_DEPTH - 1>();  // this thread's copies of tile 0
+  __syncthreads();
   // the query A fragments of this warp's k-steps (warp w: 16 columns from
   // 16 (w + 8 i)); warps past the head's last k-step hold unused copies
   uint32_t qh[KPW][4], ql[KPW][4];
@@ -674,15 +682,13 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   for (int i = 0; i < NPW; ++i)
 #pragma unroll
     for (int e = 0; e < 4; ++e) oacc[i][e] = 0.0f;
-  bool failed = false;
 
+  // tile i: scores, then (barrier) tile i - 1 + depth into the slot tile
+  // i - 1 left and the softmax, then (barrier, after which tile i + 1 is in
+  // place: one commit group a step keeps the count regular) the values
   for (int i = 0; i < n_tiles; ++i) {
     const int tb = (t0 + i * CX) * AT_POS;
     const float *slot = ring + (i % AT_DEPTH) * LY::TILE;
-    if (!mbar_wait(&bars[i % AT_DEPTH], (uint32_t)((i / AT_DEPTH) & 1), failed ? 1 : (1 << 22))) {
-      if (!failed && tid == 0) atomicOr(err, 2);
-      failed = true;
-    }
     // a position's key and value rows: new, cached, or zeros outside the pass's span
     auto krow = [&](int pos) -> const float * {
       return (pos < lo_all || pos >= hi_all) ? zrow : pos >= p0 ? newk + (pos - p0) * KS : slot + (pos - tb) * KS;
@@ -721,9 +727,9 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
       *reinterpret_cast<float2 *>(sw + 8 * AT_SRED) = make_float2(sc[2], sc[3]);
     }
     __syncthreads();  // the partials are written, and every warp is past tile i - 1
-    if (warp == 0 && i >= 1 && i - 1 + AT_DEPTH < n_tiles) {
-      fence_async_smem();
-      issue(i - 1 + AT_DEPTH);
+    if (i >= 1) {
+      if (i - 1 + AT_DEPTH < n_tiles) issue(i - 1 + AT_DEPTH);
+      cp_async_commit();
     }
     // online softmax of row sr, one thread a position; the warps' partials
     // added in warp order
@@ -748,7 +754,8 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     ph[sr * AT_SRED + sp] = eh;
     pl[sr * AT_SRED + sp] = __float2half_rn(e - __half2float(eh));
     if (sp == 0) fsc[sr] = fct;
-    __syncthreads();  // the weights and factors are written
+    cp_async_wait<1>();  // this thread's copies of tile i + 1
+    __syncthreads();     // the weights and factors are written; tile i + 1 is in place
     // weighted values: this warp's 8-dimension tiles n = warp + 8 i
     {
       const uint32_t *h32 = reinterpret_cast<const uint32_t *>(ph), *l32 = reinterpret_cast<const uint32_t *>(pl);
@@ -1310,7 +1317,7 @@ template <int HD, int CX>
 static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const float *qkv, int qkv_stride, int heads,
                                int kv_heads, const float *q_norm, const float *k_norm, const float *cs,
                                const float *sn, float eps, int owner, float *kc, float *vc, int sliding, int span,
-                               const int *d_p0, int lanes, float *out, int out_stride, float *out_amax, int *err) {
+                               const int *d_p0, int lanes, float *out, int out_stride, float *out_amax) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
@@ -1326,14 +1333,14 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const fl
   cfg.attrs = at;
   cfg.numAttrs = g_pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, attn_kernel<HD, CX>, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
-                            owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, err);
+                            owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax);
 }
 }  // extern "C++"
 
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
-                            int out_stride, float *out_amax, int *err, cudaStream_t st) {
+                            int out_stride, float *out_amax, cudaStream_t st) {
   if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads || (cluster != 8 && cluster != 16))
     return cudaErrorInvalidValue;
   const size_t smem = igc_attn_smem(hd);
@@ -1342,10 +1349,10 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
 #define IGC_ATT(HD)                                                                                              \
   return cluster == 8 ? launch_attn<HD, 8>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                            sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,   \
-                                           out_amax, err)                                                         \
+                                           out_amax)                                                              \
                       : launch_attn<HD, 16>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                             sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,  \
-                                            out_amax, err);
+                                            out_amax);
   switch (hd) {
     case 32: IGC_ATT(32)
     case 64: IGC_ATT(64)

@@ -37,12 +37,11 @@ size_t igc_attn_smem(int hd);
 // layer's cache writes, scores, softmax and values over 16-position tiles,
 // and the merge of the cluster's partials); `cluster` (8 or 16) blocks a
 // cluster, a session constant.  `out_amax`, when given, gets each lane's
-// largest |out| per (head, cluster block), [heads * cluster][16]; `err` gets
-// bit 2 if a tile copy never arrived.
+// largest |out| per (head, cluster block), [heads * cluster][16].
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
-                            int out_stride, float *out_amax, int *err, cudaStream_t st);
+                            int out_stride, float *out_amax, cudaStream_t st);
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
                               cudaStream_t st);
 cudaError_t igc_launch_rope_table(const float *steps, int half, int window, float *cs, float *sn,

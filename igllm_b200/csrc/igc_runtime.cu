@@ -1118,7 +1118,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                         m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
                         m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
-                        s->d_err, s->st));
+                        s->st));
     ma.parts = m->heads * s->attn_cluster;
     c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
              1.0f, nullptr, 0, nullptr, &so, ma_in);
