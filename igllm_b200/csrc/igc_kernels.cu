@@ -485,7 +485,9 @@ struct AttnLayout {                  // offsets in floats
   static constexpr int O_F = O_P + AT_ROWS * AT_SRED;
   static constexpr int O_RO = O_F + AT_ROWS;              // pushed values: [sender][16][hd / CX]
   static constexpr int O_RML = O_RO + AT_ROWS * HD;         // pushed maxima, totals: [sender][16][2]
-  static constexpr int O_AMX = O_RML + 2 * AT_ROWS * AT_MAX_CLUSTER;
+  static constexpr int O_W = O_RML + 2 * AT_ROWS * AT_MAX_CLUSTER;  // merge weights [16][16]
+  static constexpr int O_LINV = O_W + AT_ROWS * AT_MAX_CLUSTER;
+  static constexpr int O_AMX = O_LINV + AT_ROWS;
   static constexpr int FLOATS = O_AMX + AT_ROWS;
 };
 
@@ -560,6 +562,54 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
+// head_norm_turn in two halves, so that several rows' loads can be in
+// flight before any row's arithmetic: the row, its rope tables and gain
+template <int DPL>
+struct HeadRow {
+  float v[DPL], c[DPL], s[DPL], gn[DPL];
+};
+
+template <int DPL>
+__device__ __forceinline__ void head_row_load(HeadRow<DPL> &R, const float *src, const float *gain, const float *cs,
+                                              const float *sn, bool turn, int l) {
+  if (src) {
+    load_dpl<DPL>(src + l * DPL, R.v);
+  } else {
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) R.v[e] = 0.0f;
+  }
+  if (turn) {
+    const int d0 = (l & 15) * DPL;
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) {
+      R.c[e] = cs[d0 + e];
+      R.s[e] = sn[d0 + e];
+    }
+  }
+  if (gain) load_dpl<DPL>(gain + l * DPL, R.gn);
+}
+
+// the same arithmetic as head_norm_turn
+template <int DPL>
+__device__ __forceinline__ void head_row_finish(HeadRow<DPL> &R, bool gain, float eps, bool turn, int l) {
+  constexpr int HD = 32 * DPL;
+  float s = 0.0f;
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) s += R.v[e] * R.v[e];
+  s = warp_sum(s);
+  const float sh = (float)(1.0 / sqrt((double)s / (double)HD + (double)eps));
+#pragma unroll
+  for (int e = 0; e < DPL; ++e) R.v[e] = gain ? R.v[e] * sh * R.gn[e] : R.v[e] * sh;
+  if (turn) {
+    float other[DPL];
+#pragma unroll
+    for (int e = 0; e < DPL; ++e) other[e] = __shfl_xor_sync(0xffffffffu, R.v[e], 16);
+#pragma unroll
+    for (int e = 0; e < DPL; ++e)
+      R.v[e] = l < 16 ? R.v[e] * R.c[e] - other[e] * R.s[e] : R.v[e] * R.c[e] + other[e] * R.s[e];
+  }
+}
+
 __device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_t &lo) {
   const __half2 h = __floats2half2_rn(x, y);
   const float2 b = __half22float2(h);
@@ -581,7 +631,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   extern __shared__ __align__(128) float sm[];
   float *ring = sm, *newk = sm + LY::O_NEWK, *newv = sm + LY::O_NEWV, *qs = sm + LY::O_Q, *zrow = sm + LY::O_ZERO;
   float *sred = sm + LY::O_SRED, *fsc = sm + LY::O_F, *ro = sm + LY::O_RO, *rml = sm + LY::O_RML;
-  float *amx = sm + LY::O_AMX;
+  float *amx = sm + LY::O_AMX, *wts = sm + LY::O_W, *linv = sm + LY::O_LINV;
   __half *ph = reinterpret_cast<__half *>(sm + LY::O_P), *pl = ph + AT_ROWS * AT_SRED;
   const int tid = threadIdx.x, warp = tid >> 5, l = tid & 31, g = l >> 2, t = l & 3;
   const int r = blockIdx.x;  // rank in the cluster, which spans the grid's x
@@ -625,37 +675,66 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   }
 
   pdl_wait();
-  // the queries, a warp a row, normed and turned at their lane's position
-  for (int row = warp; row < AT_ROWS; row += 8) {
-    const int f = rb * AT_ROWS + row, j = f / G, h = kh * G + (f - j * G);
-    float v[DPL];
-    if (j < lanes) {
-      load_dpl<DPL>(qkv + (size_t)j * qkv_stride + (size_t)h * HD + l * DPL, v);
-      const int pos = p0 + j;
-      head_norm_turn<DPL>(v, q_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps, true, l);
-    } else {
+  // the rows a warp prepares: query rows warp and warp + 8 (normed and
+  // turned at their lane's position), then the pass's new key and value rows
+  // it = warp, warp + 8, ... that fall in this block's tiles (on an owner
+  // layer normed, turned (keys) and written to the cache by the first row
+  // block; on a sharing layer read back from the owner's cache).  Three at
+  // a time: all three rows' loads issue before any row's arithmetic.
+  {
+    const int n_items = 2 + (2 * lanes - warp + 7) / 8;
+    for (int k0 = 0; k0 < n_items; k0 += 3) {
+      HeadRow<DPL> R[3];
+      bool live[3], norm[3], turn[3];
+      const float *gain[3];
+      float *dst[3], *cache[3];
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) v[e] = 0.0f;
+      for (int b = 0; b < 3; ++b) {
+        const int k = k0 + b;
+        live[b] = false;
+        norm[b] = turn[b] = false;
+        gain[b] = nullptr;
+        dst[b] = cache[b] = nullptr;
+        const float *src = nullptr;
+        int pos = 0;
+        if (k < 2) {
+          const int row = warp + 8 * k, f = rb * AT_ROWS + row, j = f / G, h = kh * G + (f - j * G);
+          dst[b] = qs + row * QS;
+          live[b] = true;  // rows past the lanes are staged as zeros
+          if (j < lanes) {
+            src = qkv + (size_t)j * qkv_stride + (size_t)h * HD;
+            pos = p0 + j;
+            norm[b] = turn[b] = true;
+            gain[b] = q_norm;
+          }
+        } else if (k < n_items) {
+          const int it = warp + 8 * (k - 2), jj = it >> 1, is_v = it & 1, tile = (p0 + jj) / AT_POS;
+          if (it < 2 * lanes && tile >= t0 && (tile - t0) % CX == 0) {
+            pos = p0 + jj;
+            live[b] = true;
+            dst[b] = is_v ? newv + jj * VS : newk + jj * KS;
+            float *crow = (is_v ? vc : kc) + (size_t)pos * kv_w + (size_t)kh * HD;
+            if (owner) {
+              src = qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + (size_t)kh * HD;
+              norm[b] = true;
+              turn[b] = !is_v;
+              gain[b] = is_v ? nullptr : k_norm;
+              if (rb == 0) cache[b] = crow;
+            } else {
+              src = crow;
+            }
+          }
+        }
+        head_row_load<DPL>(R[b], src, gain[b], cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, turn[b], l);
+      }
+#pragma unroll
+      for (int b = 0; b < 3; ++b) {
+        if (!live[b]) continue;
+        if (norm[b]) head_row_finish<DPL>(R[b], gain[b] != nullptr, eps, turn[b], l);
+        store_dpl<DPL>(dst[b] + l * DPL, R[b].v);
+        if (cache[b]) store_dpl<DPL>(cache[b] + l * DPL, R[b].v);
+      }
     }
-    store_dpl<DPL>(qs + row * QS + l * DPL, v);
-  }
-  // the pass's new key and value rows that fall in this block's tiles: on an
-  // owner layer normed, turned (keys) and written to the cache by the first
-  // row block; on a sharing layer read back from the owner's cache
-  for (int it = warp; it < 2 * lanes; it += 8) {
-    const int jj = it >> 1, is_v = it & 1, pos = p0 + jj, tile = pos / AT_POS;
-    if (tile < t0 || (tile - t0) % CX) continue;
-    const size_t at = (size_t)pos * kv_w + (size_t)kh * HD + l * DPL;
-    float v[DPL];
-    if (owner) {
-      load_dpl<DPL>(qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + kh * HD + l * DPL, v);
-      head_norm_turn<DPL>(v, is_v ? nullptr : k_norm, cs_tab + (size_t)pos * half, sn_tab + (size_t)pos * half, eps,
-                          !is_v, l);
-      if (rb == 0) store_dpl<DPL>((is_v ? vc : kc) + at, v);
-    } else {
-      load_dpl<DPL>((is_v ? vc : kc) + at, v);
-    }
-    store_dpl<DPL>((is_v ? newv + jj * VS : newk + jj * KS) + l * DPL, v);
   }
 
   cp_async_wait<AT_DEPTH - 1>();  // this thread's copies of tile 0
@@ -803,28 +882,38 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   if (sp < CX) st_cluster2(rml + 2 * (r * AT_ROWS + sr), sp, m_run, l_run);
   if (tid < AT_ROWS) amx[tid] = 0.0f;
   cluster_sync();
+  // each row's block weights e^{m_q - M} and total: thread (row, q), the
+  // maximum and the total over the row's 16 threads in fixed trees
+  {
+    const int wr = tid >> 4, wq = tid & 15;
+    const float2 mq = wq < CX ? *reinterpret_cast<const float2 *>(rml + 2 * (wq * AT_ROWS + wr))
+                              : make_float2(-FLT_MAX, 0.0f);
+    float M = mq.x;
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    const float w = mq.x == -FLT_MAX ? 0.0f : expf(mq.x - M);
+    float L = mq.y * w;
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    wts[wr * AT_MAX_CLUSTER + wq] = w;
+    if (wq == 0) linv[wr] = 1.0f / L;
+  }
+  __syncthreads();
   // block r merges dimensions [r * DS, (r + 1) * DS) of every row, a thread a
-  // pair of them: block weights e^{m_q - M}, totals and values in rank order
+  // pair of them, blocks in rank order
   constexpr int DP = DS / 2;
   static_assert(AT_ROWS * DP <= 256, "one pass of the block");
   if (tid < AT_ROWS * DP) {
     const int row = tid / DP, dd = 2 * (tid - row * DP), d = r * DS + dd;
-    float2 mlq[CX];
-#pragma unroll
-    for (int q = 0; q < CX; ++q) mlq[q] = *reinterpret_cast<const float2 *>(rml + 2 * (q * AT_ROWS + row));
-    float M = -FLT_MAX;
-#pragma unroll
-    for (int q = 0; q < CX; ++q) M = fmaxf(M, mlq[q].x);
-    float L = 0.0f, o0 = 0.0f, o1 = 0.0f;
+    float o0 = 0.0f, o1 = 0.0f;
 #pragma unroll
     for (int q = 0; q < CX; ++q) {
-      const float w = mlq[q].x == -FLT_MAX ? 0.0f : expf(mlq[q].x - M);
+      const float w = wts[row * AT_MAX_CLUSTER + q];
       const float2 x = *reinterpret_cast<const float2 *>(ro + (q * AT_ROWS + row) * DS + dd);
-      L += mlq[q].y * w;
       o0 = fmaf(x.x, w, o0);
       o1 = fmaf(x.y, w, o1);
     }
-    const float inv = 1.0f / L, v0 = o0 * inv, v1 = o1 * inv;
+    const float inv = linv[row], v0 = o0 * inv, v1 = o1 * inv;
     const int f = rb * AT_ROWS + row, j = f / G, h = kh * G + (f - j * G);
     if (j < lanes) {
       *reinterpret_cast<float2 *>(out + (size_t)j * out_stride + (size_t)h * HD + d) = make_float2(v0, v1);
