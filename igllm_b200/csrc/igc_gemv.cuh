@@ -305,20 +305,7 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     for (int i = threadIdx.x; i < words; i += blockDim.x) reinterpret_cast<uint4 *>(stage)[i] = make_uint4(0u, 0u, 0u, 0u);
     __syncthreads();
   }
-  // the residual's partials: warp w holds lane w's (and w + WARPS's), thread
-  // l the parts l, l + 32, ... (a fixed tree whatever the lane count)
   float part[RES ? 2 : 1][GEMV_PART_LIMIT / 32];
-  if (RES) {
-#pragma unroll
-    for (int sl = 0; sl < 2; ++sl) {
-      const int j = warp + sl * WARPS;
-#pragma unroll
-      for (int i = 0; i < GEMV_PART_LIMIT / 32; ++i) {
-        const int q = l32 + 32 * i;
-        part[sl][i] = (j < K && q < a.p_parts) ? a.p_ssq[j * GEMV_PART_LIMIT + q] : 0.0f;
-      }
-    }
-  }
   int wpl = 1;  // warps a lane
   while (wpl * 2 * K <= WARPS) wpl *= 2;
   const int n_slots = (K + WARPS - 1) / WARPS;  // lanes a warp (1 or 2)
@@ -350,20 +337,31 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
 
   float4 X[B], Pv[B], WR[B], WI[B];
   float amax_acc[2] = {0.0f, 0.0f};  // magnitudes need no fixed order: one max per thread
-  auto load = [&](int slot, int i0) {
+  // x and the norm weights (`l2` reads x past L1: before the wait it was
+  // written by a kernel two or more launches back), then the producer's p
+  auto load_x = [&](int slot, int i0, bool l2) {
     const int j = jj[slot];
 #pragma unroll
     for (int b = 0; b < B; ++b) {
       const int c4 = c4_0 + c4_step * (i0 + b);
       if (i0 + b < count && c4 < n4) {
-        X[b] = x4[(size_t)j * xs4 + c4];
-        if (RES) {
-          Pv[b] = p4[(size_t)j * ps4 + c4];
-          WR[b] = wr4[c4];
-        }
+        X[b] = l2 ? __ldcg(x4 + (size_t)j * xs4 + c4) : x4[(size_t)j * xs4 + c4];
+        if (RES) WR[b] = wr4[c4];
         if (NRM) WI[b] = win4[c4];
       }
     }
+  };
+  auto load_p = [&](int slot, int i0) {
+    const int j = jj[slot];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int c4 = c4_0 + c4_step * (i0 + b);
+      if (RES && i0 + b < count && c4 < n4) Pv[b] = p4[(size_t)j * ps4 + c4];
+    }
+  };
+  auto load = [&](int slot, int i0) {
+    load_x(slot, i0, false);
+    load_p(slot, i0);
   };
   auto compute = [&](int slot, int i0) {
     const int j = jj[slot];
@@ -412,7 +410,26 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     }
   };
 
-  if (live[0]) load(0, 0);
+  if (RES) {
+    // a residual prologue runs ahead of the kernel's wait: the residual
+    // stream and the norm weights do not come from the kernel just before
+    if (live[0]) load_x(0, 0, true);
+    pdl_wait();
+    // the residual's partials: warp w holds lane w's (and w + WARPS's),
+    // thread l the parts l, l + 32, ... (a fixed tree whatever the lane count)
+#pragma unroll
+    for (int sl = 0; sl < 2; ++sl) {
+      const int j = warp + sl * WARPS;
+#pragma unroll
+      for (int i = 0; i < GEMV_PART_LIMIT / 32; ++i) {
+        const int q = l32 + 32 * i;
+        part[sl][i] = (j < K && q < a.p_parts) ? a.p_ssq[j * GEMV_PART_LIMIT + q] : 0.0f;
+      }
+    }
+    if (live[0]) load_p(0, 0);
+  } else if (live[0]) {
+    load(0, 0);
+  }
   if (RES) {
 #pragma unroll
     for (int sl = 0; sl < 2; ++sl) {

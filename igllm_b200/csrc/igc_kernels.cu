@@ -115,9 +115,12 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
   }
   __syncwarp();
 
-  pdl_wait();
-  // the multiplier of the GELU product, loaded now so its latency hides
-  // behind the prologue (this thread's outputs: rows unit*16 + g (+8), lanes 2t+k)
+  // a residual prologue waits inside, once its first loads are out
+  constexpr bool RES_PRO = PRO == PRO_RESID || PRO == PRO_RESID_NORM;
+  if constexpr (!RES_PRO) pdl_wait();
+  // the multiplier of the GELU product (rows written at the start of the
+  // pass), loaded now so its latency hides behind the prologue (this
+  // thread's outputs: rows unit*16 + g (+8), lanes 2t+k)
   float mul_pre[NT][4];
   if (EPI == EPI_GELU_MUL && slice == 0 && my_units == 1) {
 #pragma unroll
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
         const int row = q * 16 + g + (i >= 2 ? 8 : 0);
         const int ln = MODE == MODE_PACK ? 2 * t + (i & 1) : nt * 8 + 2 * t + (i & 1);
         const bool ok = row < a.pl.rows && ln < a.lanes && !(MODE == MODE_PACK && t >= 2);
-        mul_pre[nt][i] = ok ? a.aux[(size_t)ln * a.aux_stride + row] : 0.0f;
+        mul_pre[nt][i] = ok ? __ldcg(a.aux + (size_t)ln * a.aux_stride + row) : 0.0f;
       }
   }
   if constexpr (PRO == PRO_F32S)
@@ -580,14 +583,13 @@ __device__ __forceinline__ void head_row_load(HeadRow<DPL> &R, const float *src,
   }
   if (turn) {
     const int d0 = (l & 15) * DPL;
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) {
-      R.c[e] = cs[d0 + e];
-      R.s[e] = sn[d0 + e];
-    }
+    load_dpl<DPL>(cs + d0, R.c);
+    load_dpl<DPL>(sn + d0, R.s);
   }
   if (gain) load_dpl<DPL>(gain + l * DPL, R.gn);
 }
+
+__device__ __forceinline__ void prefetch_l1(const void *p) { asm volatile("prefetch.global.L1 [%0];\n" ::"l"(p)); }
 
 // the same arithmetic as head_norm_turn
 template <int DPL>
@@ -642,7 +644,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
 
   // this block's tiles: t0, t0 + CX, ... up to the pass's last position.  The
   // position is written before the pass starts, so it is read before the wait.
-  const int p0 = *d_p0;
+  const int p0 = __ldcg(d_p0);
   const int lo_all = sliding ? max(0, p0 - span + 1) : 0, hi_all = p0 + lanes;
   const int t_first = lo_all / AT_POS, t_last = (hi_all - 1) / AT_POS;
   const int t0 = t_first + (r - t_first % CX + CX) % CX;
@@ -672,6 +674,23 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   for (int i = 0; i < AT_DEPTH; ++i) {
     if (i < n_tiles) issue(i);
     cp_async_commit();
+  }
+  // the norm gains and the pass's rope rows into L1: they do not depend on
+  // the projection, so their latency passes while this kernel waits on it
+  {
+    constexpr int GL = HD / 32;                 // 128-byte lines a gain vector (hd floats)
+    constexpr int RL = HD >= 64 ? HD / 64 : 1;  // lines a rope row (hd / 2 floats)
+    const int n_pre = 2 * GL + lanes * 2 * RL;
+    for (int i = tid; i < n_pre; i += blockDim.x) {
+      if (i < 2 * GL) {
+        const float *gv = i < GL ? q_norm : k_norm;
+        if (gv) prefetch_l1(gv + (i % GL) * 32);
+      } else {
+        const int k = i - 2 * GL, jj = k / (2 * RL), part = k - jj * 2 * RL;  // cs lines, then sn lines
+        const float *tab = part < RL ? cs_tab : sn_tab;
+        prefetch_l1(tab + (size_t)(p0 + jj) * half + (part % RL) * 32);
+      }
+    }
   }
 
   pdl_wait();

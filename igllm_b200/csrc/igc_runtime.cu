@@ -1089,10 +1089,9 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   float pend_gain = 1.0f;
   Ssq so{s->ssq_o, 0}, sd{s->ssq_d, 0}, spp{s->ssq_pp, 0};
   Ssq ma{s->amax_attn, 0}, mact{s->amax_act, 0}, mpa{s->amax_pa, 0};
-  // producers leave magnitudes (for one-pass staging downstream) only where
-  // the staging is large enough to repay the extra epilogue step; the scale
-  // is the same either way, so results do not change
-  const bool mags = K > 4;
+  // producers leave magnitudes for one-pass staging downstream; the scale is
+  // the one a two-pass prologue would find, so results do not depend on it
+  const bool mags = true;
   Ssq *mact_out = mags ? &mact : nullptr, *mpa_out = mags ? &mpa : nullptr;
   const Ssq *ma_in = mags ? &ma : nullptr, *mact_in = mags ? &mact : nullptr, *mpa_in = mags ? &mpa : nullptr;
   const Ssq *pend_ssq = nullptr;
