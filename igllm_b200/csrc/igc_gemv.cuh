@@ -460,27 +460,26 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     if (l32 == 0) scr[SCR_AMAX + jj[slot] * 16 + w_local] = m_;
   }
   __syncthreads();
-  // per lane, the parts' sums in a fixed tree: scale and norm factor
-  for (int j = warp; j < K; j += WARPS) {
-    float s_ = 0.0f;
-    if (NRM) {
-      const float *ps = scr + SCR_SSQ + j * GEMV_MAX_PARTS;
-      s_ = warp_sum((l32 < nparts ? ps[l32] : 0.0f) + (l32 + 32 < nparts ? ps[l32 + 32] : 0.0f));
-    }
-    const float m_ = warp_max(l32 < wpl ? scr[SCR_AMAX + j * 16 + l32] : 0.0f);
-    if (l32 == 0) {
-      const float sc = lane_scale(m_);
-      const float shrink = NRM ? rms_shrink(s_, cols, a.eps) : 1.0f;
-      scr[SCR_SCALE + j] = sc;
-      scr[SCR_FACTOR + j] = shrink * (1.0f / sc);
-    }
-  }
-  __syncthreads();
-  // second pass over the same words: scaled, split into hi/lo f16 pairs
+  // each warp takes its lane's scale from the lane's warp magnitudes and
+  // seals its own words; the warp holding the lane's first part also sums
+  // the parts' squares in a fixed tree and leaves the epilogue factor
 #pragma unroll
   for (int slot = 0; slot < 2; ++slot) {
     if (!live[slot]) continue;
-    const float sc = scr[SCR_SCALE + jj[slot]];
+    const int j = jj[slot];
+    const float sc = lane_scale(warp_max(l32 < wpl ? scr[SCR_AMAX + j * 16 + l32] : 0.0f));
+    if (w_local == 0) {
+      float s_ = 0.0f;
+      if (NRM) {
+        const float *ps = scr + SCR_SSQ + j * GEMV_MAX_PARTS;
+        s_ = warp_sum((l32 < nparts ? ps[l32] : 0.0f) + (l32 + 32 < nparts ? ps[l32 + 32] : 0.0f));
+      }
+      if (l32 == 0) {
+        const float shrink = NRM ? rms_shrink(s_, cols, a.eps) : 1.0f;
+        scr[SCR_SCALE + j] = sc;
+        scr[SCR_FACTOR + j] = shrink * (1.0f / sc);
+      }
+    }
 #pragma unroll 4
     for (int i = 0; i < count; ++i) {
       if (c4_0 + c4_step * i < n4) {
