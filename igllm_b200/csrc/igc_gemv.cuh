@@ -122,15 +122,21 @@ constexpr int GEMV_PART_LIMIT = 320;  // producer partials the prologue reads (1
 // Staged activations, per chunk: PACK 32 thread slots x 8 words (the four
 // 16-column products' b0, b1), NT 32 slots x 16 words per 8-lane tile (hi
 // b0, b1 of the four products, then lo).  Word of (lane n, column c, half):
+// In the 8-lane-tile modes the 16-byte quarters of a slot are swizzled
+// (quarter j of slot L at j ^ ((L >> 1) & 3)), so that the four fragment
+// reads of a quarter-warp meet every bank once instead of four times.  The
+// packed mode's 32-byte slots are left as they are.
+__device__ __forceinline__ int stage_quad(int slot, int MODE) { return MODE == MODE_PACK ? 0 : (slot >> 1) & 3; }
+
 __device__ __forceinline__ int stage_word(int n, int c, int lo, int MODE) {
   const int cc = c >> 6, kb = (c >> 4) & 3, k = c & 15, t = (k & 7) >> 1;
   if (MODE == MODE_PACK) {
-    const int g = n + (lo ? 4 : 0);
-    return ((cc * 32 + g * 4 + t) * 8) + kb * 2 + (k >> 3);
+    const int L = (n + (lo ? 4 : 0)) * 4 + t, w = kb * 2 + (k >> 3);
+    return (cc * 32 + L) * 8 + ((((w >> 2) ^ stage_quad(L, MODE)) << 2) | (w & 3));
   }
   const int NT = MODE == MODE_NT2 ? 2 : 1;
-  const int nt = n >> 3, g = n & 7;
-  return (((cc * NT + nt) * 32 + g * 4 + t) * 16) + kb * 2 + (k >> 3) + (lo ? 8 : 0);
+  const int nt = n >> 3, L = (n & 7) * 4 + t, w = kb * 2 + (k >> 3) + (lo ? 8 : 0);
+  return (((cc * NT + nt) * 32 + L) * 16) + ((((w >> 2) ^ stage_quad(L, MODE)) << 2) | (w & 3));
 }
 
 __host__ __device__ inline int stage_chunk_words(int MODE) { return MODE == MODE_PACK ? 256 : MODE == MODE_NT1 ? 512 : 1024; }
@@ -535,16 +541,17 @@ __device__ __forceinline__ void chunk_product(const uint4 &w, const uint2 &s, co
                                               float *acc) {
   ChunkA A;
   chunk_a(w, s, A);
+  const int q = stage_quad(lane32, MODE);  // the swizzle of this thread's slot
   if (MODE == MODE_PACK) {
     const uint4 *p = reinterpret_cast<const uint4 *>(stage_chunk + lane32 * 8);
-    chunk_tile(A, p[0], p[1], acc);
+    chunk_tile(A, p[q], p[1 ^ q], acc);
   } else {
     constexpr int NT = MODE == MODE_NT2 ? 2 : 1;
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
       const uint4 *p = reinterpret_cast<const uint4 *>(stage_chunk + (nt * 32 + lane32) * 16);
-      chunk_tile(A, p[0], p[1], acc + nt * 8);      // hi
-      chunk_tile(A, p[2], p[3], acc + nt * 8 + 4);  // lo
+      chunk_tile(A, p[q], p[1 ^ q], acc + nt * 8);          // hi
+      chunk_tile(A, p[2 ^ q], p[3 ^ q], acc + nt * 8 + 4);  // lo
     }
   }
 }

@@ -67,7 +67,7 @@ __global__ void repack_kernel(const uint8_t *code, size_t row_stride, const uint
 // 0 issues; the first pieces are in flight before the kernel waits for the
 // kernel ahead of it and before the activation prologue runs.
 template <int MODE, int WARPS, int PAIR, int PRO, int EPI>
-__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs a) {
   constexpr int NT = MODE == MODE_NT2 ? 2 : 1;
   constexpr int H = PAIR + 1;
   constexpr int ACC = MODE == MODE_PACK ? 4 : 8 * NT;
