@@ -106,6 +106,11 @@ struct GemvArgs {
   float cap;
   float *part_val;  // EPI_LOGITS argmax partials [gridDim.x][16]
   int *part_idx;
+  // lane batches: with batches > 1 the launch's blockIdx.y takes lanes
+  // [y * lanes, (y + 1) * lanes) of lanes_total, every pointer above moved
+  // to its first lane (the lanes are independent, so the batches run side by
+  // side with the staging of `lanes` lanes each)
+  int batches, lanes_total;
 };
 
 // Warps a block: the planning unit of a plane (its split and block count

@@ -67,7 +67,21 @@ __global__ void repack_kernel(const uint8_t *code, size_t row_stride, const uint
 // 0 issues; the first pieces are in flight before the kernel waits for the
 // kernel ahead of it and before the activation prologue runs.
 template <int MODE, int WARPS, int PAIR, int PRO, int EPI>
-__global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs a) {
+__global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs args) {
+  GemvArgs a = args;
+  if (args.batches > 1) {
+    const int j0 = blockIdx.y * args.lanes;
+    a.lanes = min(args.lanes, args.lanes_total - j0);
+    a.x += (size_t)j0 * args.x_stride;
+    if (args.p) a.p += (size_t)j0 * args.p_stride;
+    if (args.x_out) a.x_out += (size_t)j0 * args.x_stride;
+    a.out += (size_t)j0 * args.out_stride;
+    if (args.aux) a.aux += (size_t)j0 * args.aux_stride;
+    if (args.p_ssq) a.p_ssq += (size_t)j0 * GEMV_PART_LIMIT;  // partials are lane-major
+    if (args.out_ssq) a.out_ssq += (size_t)j0 * GEMV_PART_LIMIT;
+    if (args.x_amax) a.x_amax += (size_t)j0 * GEMV_PART_LIMIT;
+    if (args.out_amax) a.out_amax += (size_t)j0 * GEMV_PART_LIMIT;
+  }
   constexpr int NT = MODE == MODE_NT2 ? 2 : 1;
   constexpr int H = PAIR + 1;
   constexpr int ACC = MODE == MODE_PACK ? 4 : 8 * NT;
@@ -290,7 +304,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs a) {
     if (threadIdx.x < (WARPS / 8) * 16) {
       const int h = threadIdx.x >> 4, ln = threadIdx.x & 15;
       const int vb = blockIdx.x * (WARPS / 8) + h;
-      if (ln < NT * 8 && vb < n_vb) {
+      if (ln < a.lanes && vb < n_vb) {
         float v = 0.0f;
         for (int w = 8 * h; w < 8 * h + 8; ++w) v += red[w * 16 + ln];
         a.out_ssq[ln * GEMV_PART_LIMIT + vb] = v;
@@ -317,7 +331,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs a) {
     if (threadIdx.x < (WARPS / 8) * 16) {
       const int h = threadIdx.x >> 4, ln = threadIdx.x & 15;
       const int vb = blockIdx.x * (WARPS / 8) + h;
-      if (ln < NT * 8 && vb < n_vb) {
+      if (ln < a.lanes && vb < n_vb) {
         float v = 0.0f;
         for (int w = 8 * h; w < 8 * h + 8; ++w) v = fmaxf(v, red[w * 16 + ln]);
         a.out_amax[ln * GEMV_PART_LIMIT + vb] = v;
@@ -355,7 +369,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs a) {
     if (threadIdx.x < (WARPS / 8) * 16) {
       const int h = threadIdx.x >> 4, ln = threadIdx.x & 15;
       const int vb = blockIdx.x * (WARPS / 8) + h;
-      if (ln < NT * 8 && vb < n_vb) {
+      if (ln < a.lanes && vb < n_vb) {
         float v = bv[8 * h][ln];
         int i = bi[8 * h][ln];
         for (int w = 8 * h + 1; w < 8 * h + 8; ++w) {
@@ -1245,7 +1259,9 @@ static bool gemv_fit(GemvArgs &a, int pair, int W, int grid, size_t smem_limit, 
 template <int MODE, int WARPS, int PAIR>
 static cudaError_t launch_gemv_pe(const GemvArgs &a, int pro, int epi, int grid, size_t smem, cudaStream_t st) {
 #define IGC_CASE(P, E) \
-  if (pro == P && epi == E) return launch_k(gemv_kernel<MODE, WARPS, PAIR, P, E>, dim3(grid), dim3(WARPS * 32), smem, st, a);
+  if (pro == P && epi == E)                                                                                   \
+    return launch_k(gemv_kernel<MODE, WARPS, PAIR, P, E>, dim3(grid, a.batches > 1 ? a.batches : 1), dim3(WARPS * 32), \
+                    smem, st, a);
   if constexpr (PAIR) {
     IGC_CASE(PRO_RESID_NORM, EPI_GELU_PAIR)
     IGC_CASE(PRO_NORM, EPI_GELU_PAIR)

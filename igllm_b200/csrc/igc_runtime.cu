@@ -1014,6 +1014,22 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   a.err = s->d_err;
   const int pair = pl.pair ? 1 : 0;
   int used = pl.grid;  // blocks the launch took: the partials it leaves
+  // IGC_NO_LANE_BATCH=1 keeps such planes on the wide modes (for comparison)
+  static const char *nb_env = getenv("IGC_NO_LANE_BATCH");
+  if (K > 4 && epi != EPI_LOGITS && pl.n_cc > 32 && !(nb_env && nb_env[0] == '1')) {
+    // A plane too wide to stage more than four lanes and still keep a deep
+    // weight ring (the 6144-column down projection): lanes in batches of
+    // four, side by side in one launch (blockIdx.y), each staged in the
+    // packed mode; the batches' weight reads meet in L2.
+    a.lanes = 4;
+    a.lanes_total = K;
+    a.batches = (K + 3) / 4;
+    if (igc_gemv_smem_min(&a, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
+    CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
+    if (out_ssq) out_ssq->parts = used;
+    if (out_amax) out_amax->parts = used;
+    return IGC_OKAY;
+  }
   if (igc_gemv_smem_min(&a, pair) <= (size_t)s->m->smem_limit) {
     CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
     if (out_ssq) out_ssq->parts = used;

@@ -47,6 +47,10 @@ SMALL = dict(vocab=4096, hidden=256, layers=8, heads=8, kv_heads=1, head_dim=32,
 # The export's literal norm distribution, N(0, 0.02) used as is.
 LITERAL = dict(TINY, norm_offset=0.0, with_layer_scalar=0, seed=3)
 
+# A feed-forward wider than 2048 columns: above four lanes its down
+# projection runs as side-by-side batches of four lanes in one launch.
+WIDE = dict(TINY, inner=4096, seed=13)
+
 
 def make_checkpoint(lib, folder, cfg):
     spec = lib.SynthSpec(**cfg)
@@ -73,4 +77,11 @@ def small_dir(tmp_path_factory, igc_lib):
 def literal_dir(tmp_path_factory, igc_lib):
     d = str(tmp_path_factory.mktemp("literal"))
     make_checkpoint(igc_lib, d, LITERAL)
+    return d
+
+
+@pytest.fixture(scope="session")
+def wide_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("wide"))
+    make_checkpoint(igc_lib, d, WIDE)
     return d

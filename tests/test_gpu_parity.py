@@ -10,7 +10,7 @@ agree wherever the oracle's top-2 gap is above the tolerance.
 import numpy as np
 import pytest
 
-from conftest import LITERAL, SMALL, TINY
+from conftest import LITERAL, SMALL, TINY, WIDE
 
 pytestmark = pytest.mark.gpu
 
@@ -35,10 +35,10 @@ def _pair(igc, igo, folder, cfg):
     return m, om
 
 
-@pytest.mark.parametrize("which", ["tiny", "small", "literal"])
-def test_pass_parity(igc_lib, igo_mod, which, tiny_dir, small_dir, literal_dir):
-    folder = {"tiny": tiny_dir, "small": small_dir, "literal": literal_dir}[which]
-    cfg = {"tiny": TINY, "small": SMALL, "literal": LITERAL}[which]
+@pytest.mark.parametrize("which", ["tiny", "small", "literal", "wide"])
+def test_pass_parity(igc_lib, igo_mod, which, tiny_dir, small_dir, literal_dir, wide_dir):
+    folder = {"tiny": tiny_dir, "small": small_dir, "literal": literal_dir, "wide": wide_dir}[which]
+    cfg = {"tiny": TINY, "small": SMALL, "literal": LITERAL, "wide": WIDE}[which]
     m, om = _pair(igc_lib, igo_mod, folder, cfg)
     s, o = igc_lib.Session(m), igo_mod.OracleSession(om, threads=8)
     rng = np.random.default_rng(2)
@@ -274,6 +274,29 @@ def test_lane_batching_is_bit_identical(igc_lib, small_dir):
     blocks) give the same bits, which is what lets a greedy stream with
     guessing equal the stream without it exactly."""
     m = igc_lib.Model(folder=small_dir, window_limit=SMALL["window_limit"])
+    ids = np.array([3, 17, 29, 5, 8, 41, 77, 90, 12, 13, 14, 15, 16, 7, 9, 100, 200, 300, 11, 2, 4, 6, 8, 10,
+                    12, 14, 16, 18, 20], np.int32)
+    block = ids[19:28]
+    a = igc_lib.Session(m)
+    a.prime(ids[:20])
+    stepped = np.stack([a.step(t)[1] for t in block])
+    b = igc_lib.Session(m)
+    b.prime(ids[:20])
+    nine = b.guess(block)
+    c = igc_lib.Session(m)
+    c.prime(ids[:20])
+    four = c.guess(block[:4])
+    c.guess_keep(4)
+    five = c.guess(block[4:])
+    assert np.array_equal(stepped, nine)
+    assert np.array_equal(stepped, np.concatenate([four, five]))
+
+
+def test_wide_lane_batches_are_bit_identical(igc_lib, wide_dir):
+    """The same for a down projection wide enough to run in side-by-side
+    batches of four lanes: a nine-lane block (three batches), blocks of four
+    and five, and single steps give the same bits."""
+    m = igc_lib.Model(folder=wide_dir, window_limit=WIDE["window_limit"])
     ids = np.array([3, 17, 29, 5, 8, 41, 77, 90, 12, 13, 14, 15, 16, 7, 9, 100, 200, 300, 11, 2, 4, 6, 8, 10,
                     12, 14, 16, 18, 20], np.int32)
     block = ids[19:28]
