@@ -1014,13 +1014,15 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   a.err = s->d_err;
   const int pair = pl.pair ? 1 : 0;
   int used = pl.grid;  // blocks the launch took: the partials it leaves
-  // IGC_NO_LANE_BATCH=1 keeps such planes on the wide modes (for comparison)
+  // IGC_NO_LANE_BATCH=1 keeps them on the wide modes (for comparison)
   static const char *nb_env = getenv("IGC_NO_LANE_BATCH");
-  if (K > 4 && epi != EPI_LOGITS && pl.n_cc > 32 && !(nb_env && nb_env[0] == '1')) {
-    // A plane too wide to stage more than four lanes and still keep a deep
-    // weight ring (the 6144-column down projection): lanes in batches of
-    // four, side by side in one launch (blockIdx.y), each staged in the
-    // packed mode; the batches' weight reads meet in L2.
+  if (K > 4 && epi != EPI_LOGITS && !(nb_env && nb_env[0] == '1')) {
+    // Above four lanes every projection but the head runs its lanes in
+    // batches of four, side by side in one launch (blockIdx.y), each staged
+    // in the packed mode: the staging stays small enough for a deep weight
+    // ring (the 6144-column down projection would leave none at eight lanes),
+    // the products spread over twice the blocks, and the batches' weight
+    // reads meet in L2.
     a.lanes = 4;
     a.lanes_total = K;
     a.batches = (K + 3) / 4;
