@@ -1016,16 +1016,19 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   int used = pl.grid;  // blocks the launch took: the partials it leaves
   // IGC_NO_LANE_BATCH=1 keeps them on the wide modes (for comparison)
   static const char *nb_env = getenv("IGC_NO_LANE_BATCH");
-  if (K > 4 && epi != EPI_LOGITS && !(nb_env && nb_env[0] == '1')) {
-    // Above four lanes every projection but the head runs its lanes in
-    // batches of four, side by side in one launch (blockIdx.y), each staged
-    // in the packed mode: the staging stays small enough for a deep weight
-    // ring (the 6144-column down projection would leave none at eight lanes),
-    // the products spread over twice the blocks, and the batches' weight
-    // reads meet in L2.
+  const int batches = (K + 3) / 4;
+  const bool wide = pl.n_cc > 32;                                 // 8-lane staging leaves no weight ring
+  const bool one_wave = (pl.grid + 1) / 2 * batches <= s->m->sm_count;  // 16-warp blocks, one an SM
+  if (K > 4 && epi != EPI_LOGITS && (wide || one_wave) && !(nb_env && nb_env[0] == '1')) {
+    // Above four lanes a projection runs its lanes in batches of four, side
+    // by side in one launch (blockIdx.y), each staged in the packed mode,
+    // where that keeps every block in one wave of the SMs (the products
+    // spread over more blocks, and the batches' weight reads meet in L2), and
+    // always for a plane too wide to stage eight lanes with a weight ring
+    // (the 6144-column down projection would leave none).
     a.lanes = 4;
     a.lanes_total = K;
-    a.batches = (K + 3) / 4;
+    a.batches = batches;
     if (igc_gemv_smem_min(&a, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
     CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
     if (out_ssq) out_ssq->parts = used;
