@@ -1016,19 +1016,26 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   int used = pl.grid;  // blocks the launch took: the partials it leaves
   // IGC_NO_LANE_BATCH=1 keeps them on the wide modes (for comparison)
   static const char *nb_env = getenv("IGC_NO_LANE_BATCH");
-  const int batches = (K + 3) / 4;
-  const bool wide = pl.n_cc > 32;                                 // 8-lane staging leaves no weight ring
-  const bool one_wave = (pl.grid + 1) / 2 * batches <= s->m->sm_count;  // 16-warp blocks, one an SM
-  if (K > 4 && epi != EPI_LOGITS && (wide || one_wave) && !(nb_env && nb_env[0] == '1')) {
-    // Above four lanes a projection runs its lanes in batches of four, side
-    // by side in one launch (blockIdx.y), each staged in the packed mode,
-    // where that keeps every block in one wave of the SMs (the products
-    // spread over more blocks, and the batches' weight reads meet in L2), and
-    // always for a plane too wide to stage eight lanes with a weight ring
-    // (the 6144-column down projection would leave none).
-    a.lanes = 4;
+  const bool wide = pl.n_cc > 32;                                         // 8-lane staging leaves no weight ring
+  const bool one_wave = (pl.grid + 1) / 2 * ((K + 3) / 4) <= s->m->sm_count;  // 16-warp blocks, one an SM
+  int lb = 0;                                                             // lanes a batch
+  if (K > 4 && epi != EPI_LOGITS && !(nb_env && nb_env[0] == '1')) {
+    if (wide || one_wave)
+      lb = 4;
+    else if (K > 8)
+      lb = 8;
+  }
+  if (lb) {
+    // A projection runs its lanes in batches, side by side in one launch
+    // (blockIdx.y): of four (the packed mode) where that keeps every block in
+    // one wave of the SMs, and always for a plane too wide to stage eight
+    // lanes with a weight ring (the 6144-column down projection would leave
+    // none); above eight lanes otherwise of eight, which takes as many blocks
+    // as one sixteen-lane launch but stages a quarter of the words a warp.
+    // The batches' weight reads meet in L2.
+    a.lanes = lb;
     a.lanes_total = K;
-    a.batches = batches;
+    a.batches = (K + lb - 1) / lb;
     if (igc_gemv_smem_min(&a, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
     CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
     if (out_ssq) out_ssq->parts = used;

@@ -267,6 +267,27 @@ def test_e2b_shape_against_oracle(igc_lib, igo_mod):
     o.guess_keep(1)
 
 
+def test_e2b_lane_batches_are_bit_identical(igc_lib):
+    """At the benchmark's size the wider lane counts run their projections
+    in side-by-side batches of four or eight lanes (whichever keeps the
+    blocks to one wave of the SMs): single steps, a nine-lane block and a
+    sixteen-lane block give the same bits."""
+    spec = igc_lib.spec_e2b(norm_offset=1.0, seed=6, window_limit=1024)
+    m = igc_lib.Model(spec=spec, window_limit=1024)
+    rng = np.random.default_rng(8)
+    ids = rng.integers(0, 262144, 40).astype(np.int32)
+    block = rng.integers(0, 262144, 16).astype(np.int32)
+    a = igc_lib.Session(m)
+    a.prime(ids)
+    stepped = np.stack([a.step(t)[1] for t in block[:9]])
+    b = igc_lib.Session(m)
+    b.prime(ids)
+    assert np.array_equal(stepped, b.guess(block[:9]))
+    c = igc_lib.Session(m)
+    c.prime(ids)
+    assert np.array_equal(stepped, c.guess(block)[:9])
+
+
 def test_lane_batching_is_bit_identical(igc_lib, small_dir):
     """A position's logits do not depend on how many lanes shared its pass:
     one lane at a time (the packed four-lane mode), one nine-lane block (two
