@@ -1370,10 +1370,16 @@ cudaError_t igc_launch_gemv(GemvArgs *a, int pair, int pro, int epi, int grid, s
   const int mode = gemv_mode(a->lanes);
   const int units = pair ? a->pl.n_rb / 2 : a->pl.n_rb;
   const int G8 = GEMV_WARPS / a->split;
-  // 16-warp blocks where the mode allows them and their shared memory fits
+  // 16-warp blocks where the mode allows them and their shared memory fits,
+  // except for one or two lanes when the 8-warp blocks fit one wave of the
+  // SMs (the products then spread over twice the SMs, and with so few lanes
+  // the per-warp staging stays short)
   int W = GEMV_WARPS;
-  if (mode != MODE_NT2 && gemv_layout(*a, pair, 16, 0, GEMV_MAX_DEPTH).ring + (size_t)16 * (pair + 1) * GEMV_PIECE_BYTES <=
-                              smem_limit)
+  int sms = 0, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const bool spread = a->lanes <= 2 && sms > 0 && grid * (a->batches > 1 ? a->batches : 1) <= sms;
+  if (mode != MODE_NT2 && !spread &&
+      gemv_layout(*a, pair, 16, 0, GEMV_MAX_DEPTH).ring + (size_t)16 * (pair + 1) * GEMV_PIECE_BYTES <= smem_limit)
     W = 16;
   const int G = W / a->split;
   if (a->out_ssq) {
