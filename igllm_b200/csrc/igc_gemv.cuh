@@ -151,10 +151,12 @@ __host__ __device__ inline size_t gemv_stage_bytes(int n_cc, int MODE) { return 
 // Accumulator floats a thread keeps per half (gate or up) of a unit.
 __host__ __device__ inline int gemv_acc_floats(int MODE) { return MODE == MODE_PACK ? 4 : MODE == MODE_NT1 ? 8 : 16; }
 
-// app_core.c:4667 kern_norm_rms's shrink: (mean of squares + eps)^-1/2 in
-// double, applied in float as x * shrink * w.
+// app_core.c:4667 kern_norm_rms's shrink: (mean of squares + eps)^-1/2,
+// applied in float as x * shrink * w.  The reference forms it in double; in
+// float it differs by about an ulp and stays off the double units' latency,
+// which sits on every residual prologue's critical path.
 __device__ __forceinline__ float rms_shrink(float ssq, int n, float eps) {
-  return (float)(1.0 / sqrt((double)ssq / (double)n + (double)eps));
+  return 1.0f / sqrtf(ssq / (float)n + eps);
 }
 
 // The pair of words that hold columns c, c + 1 (c even) of one lane: the

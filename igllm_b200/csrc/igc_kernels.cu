@@ -537,7 +537,7 @@ __device__ __forceinline__ void store_dpl(float *dst, const float (&v)[DPL]) {
 }
 
 // One head of 32 * DPL dimensions, DPL a thread: normed (app_core.c:4667,
-// double mean of squares) with an optional gain, then turned by the rope
+// the shrink in float, see rms_shrink) with an optional gain, then turned by the rope
 // tables of its position (pairs (d, d + hd/2), threads l and l + 16).
 template <int DPL>
 __device__ __forceinline__ void head_norm_turn(float (&v)[DPL], const float *gain, const float *cs, const float *sn,
@@ -556,7 +556,7 @@ __device__ __forceinline__ void head_norm_turn(float (&v)[DPL], const float *gai
 #pragma unroll
   for (int e = 0; e < DPL; ++e) s += v[e] * v[e];
   s = warp_sum(s);
-  const float sh = (float)(1.0 / sqrt((double)s / (double)HD + (double)eps));
+  const float sh = 1.0f / sqrtf(s / (float)HD + eps);
 #pragma unroll
   for (int e = 0; e < DPL; ++e) v[e] = gain ? v[e] * sh * gain[l * DPL + e] : v[e] * sh;
   if (turn) {
@@ -613,7 +613,7 @@ __device__ __forceinline__ void head_row_finish(HeadRow<DPL> &R, bool gain, floa
 #pragma unroll
   for (int e = 0; e < DPL; ++e) s += R.v[e] * R.v[e];
   s = warp_sum(s);
-  const float sh = (float)(1.0 / sqrt((double)s / (double)HD + (double)eps));
+  const float sh = 1.0f / sqrtf(s / (float)HD + eps);
 #pragma unroll
   for (int e = 0; e < DPL; ++e) R.v[e] = gain ? R.v[e] * sh * R.gn[e] : R.v[e] * sh;
   if (turn) {
