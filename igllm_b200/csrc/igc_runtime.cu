@@ -1019,25 +1019,40 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
   const bool wide = pl.n_cc > 32;                                         // 8-lane staging leaves no weight ring
   const bool one_wave = (pl.grid + 1) / 2 * ((K + 3) / 4) <= s->m->sm_count;  // 16-warp blocks, one an SM
   int lb = 0;                                                             // lanes a batch
+  bool wave_cap = false;                                                  // batches of four held to one wave
   if (K > 4 && epi != EPI_LOGITS && !(nb_env && nb_env[0] == '1')) {
-    if (wide || one_wave)
+    if (wide || one_wave) {
       lb = 4;
-    else if (K > 8)
+    } else if (!out_ssq) {
+      lb = 4;
+      wave_cap = true;
+    } else if (K > 8) {
       lb = 8;
+    }
   }
   if (lb) {
     // A projection runs its lanes in batches, side by side in one launch
     // (blockIdx.y): of four (the packed mode) where that keeps every block in
     // one wave of the SMs, and always for a plane too wide to stage eight
     // lanes with a weight ring (the 6144-column down projection would leave
-    // none); above eight lanes otherwise of eight, which takes as many blocks
-    // as one sixteen-lane launch but stages a quarter of the words a warp.
-    // The batches' weight reads meet in L2.
+    // none).  A projection that leaves no sums-of-squares partials (q|k|v,
+    // gate|up) also takes batches of four where they would need a second
+    // wave: its grid is held to the SMs' count over the batches, and some
+    // warp groups take a second row block (each output is still summed in
+    // the same order, so results do not change).  Above eight lanes
+    // otherwise of eight, which takes as many blocks as one sixteen-lane
+    // launch but stages a quarter of the words a warp.  The batches' weight
+    // reads meet in L2.
     a.lanes = lb;
     a.lanes_total = K;
     a.batches = (K + lb - 1) / lb;
     if (igc_gemv_smem_min(&a, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
-    CKL(igc_launch_gemv(&a, pair, pro, epi, pl.grid, (size_t)s->m->smem_limit, s->st, &used));
+    int g = pl.grid;
+    if (wave_cap) {
+      const int per = s->m->sm_count / a.batches;
+      if (g > per) g = per > 0 ? per : 1;
+    }
+    CKL(igc_launch_gemv(&a, pair, pro, epi, g, (size_t)s->m->smem_limit, s->st, &used));
     if (out_ssq) out_ssq->parts = used;
     if (out_amax) out_amax->parts = used;
     return IGC_OKAY;
