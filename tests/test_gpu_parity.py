@@ -269,8 +269,9 @@ def test_e2b_shape_against_oracle(igc_lib, igo_mod):
 
 def test_e2b_lane_batches_are_bit_identical(igc_lib):
     """At the benchmark's size the wider lane counts run their projections
-    in side-by-side batches of four or eight lanes (whichever keeps the
-    blocks to one wave of the SMs): single steps, a nine-lane block and a
+    in side-by-side batches of four or eight lanes (q|k|v and gate|up in
+    batches of four held to one wave of the SMs, some warp groups taking two
+    row blocks): single steps, an eight-lane block, a nine-lane block and a
     sixteen-lane block give the same bits."""
     spec = igc_lib.spec_e2b(norm_offset=1.0, seed=6, window_limit=1024)
     m = igc_lib.Model(spec=spec, window_limit=1024)
@@ -286,6 +287,9 @@ def test_e2b_lane_batches_are_bit_identical(igc_lib):
     c = igc_lib.Session(m)
     c.prime(ids)
     assert np.array_equal(stepped, c.guess(block)[:9])
+    d = igc_lib.Session(m)
+    d.prime(ids)
+    assert np.array_equal(stepped[:8], d.guess(block[:8]))
 
 
 def test_lane_batching_is_bit_identical(igc_lib, small_dir):
