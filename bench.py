@@ -19,8 +19,9 @@ commits 4 tokens and the rate measures the verify round itself.
          (igc_session_round) with host ids in and host ids out each round
 
 Also reported: the n-gram scout's own rate and acceptance, verify-round us
-for K = 1, 2, 4, 8, 16, the projection kernel against the HBM roofline
-(timed live with CUDA events), and the reference engine on the host cores.
+for K = 1, 2, 4, 8, 16, the projection kernels against the HBM roofline
+(timed inside the timed graphed passes by launch stamps), and the reference
+engine on the host cores.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 """
@@ -48,9 +49,10 @@ CKPT_DIR = os.environ.get("IGLLM_BENCH_CKPT", "/tmp/igllm_bench_e2b_s1")
 METRIC = "decode tok/s (greedy, --guess 4)"
 
 
-def make_prompt():
-    """A 256-id passage (uniform, seed 0) repeated 4x with 10% substitutions."""
-    rng = np.random.default_rng(0)
+def make_prompt(seed=0):
+    """A 256-id passage (uniform, seed 0 for config 0; a replica takes its
+    rank as the seed) repeated 4x with 10% substitutions."""
+    rng = np.random.default_rng(seed)
     passage = rng.integers(0, VOCAB, 256)
     prompt = np.tile(passage, 4)
     swap = rng.random(PROMPT_LEN) < 0.10
@@ -138,20 +140,21 @@ def profiler_range(on):
 
 
 class Ranks:
-    """One process a GPU under torchrun: its rank, the world size, and the
-    process group (None when alone).  Replicas share nothing but the barrier
-    around the timed region and the maximum of their times."""
+    """One process a GPU under torchrun: its rank, the world size, and a host
+    process group (None when alone).  Replicas share nothing on the device:
+    the group is gloo over host sockets, used only for the barrier around the
+    timed region and the maximum of the ranks' device times, so no NCCL
+    communicator exists."""
 
-    def __init__(self, backend="nccl", device=None):
+    def __init__(self, backend="gloo"):
         self.rank = int(os.environ.get("RANK", "0"))
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
         self.dist = None
-        self.device = device
         if self.world > 1:
             import datetime
             import torch.distributed as dist
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=600))
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
             self.dist = dist
 
     def barrier(self):
@@ -163,7 +166,7 @@ class Ranks:
         if not self.dist:
             return float(x)
         import torch
-        t = torch.tensor([float(x)], dtype=torch.float64, device=self.device)
+        t = torch.tensor([float(x)], dtype=torch.float64)
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
 
@@ -186,30 +189,46 @@ def host_cores():
 
 
 def ensure_checkpoint():
-    import igllm_b200 as ig
+    """The synthetic E2B checkpoint on disk for the reference engine.  It is
+    written by a child process that exits before the reference runs, so the
+    process that times the reference never maps this repository's CUDA
+    library (the generator lives there, beside the in-HBM one)."""
     if not os.path.exists(os.path.join(CKPT_DIR, "model.safetensors")):
-        ig.synth_write(ig.spec_e2b(seed=1, window_limit=4096), CKPT_DIR, threads=min(32, host_cores()))
+        code = ("import sys; sys.path.insert(0, %r); import igllm_b200 as ig; "
+                "ig.synth_write(ig.spec_e2b(seed=1, window_limit=4096), %r, threads=%d)"
+                % (ROOT, CKPT_DIR, min(32, host_cores())))
+        subprocess.run([sys.executable, "-c", code], check=True)
     return CKPT_DIR
 
 
 def reference_rounds(rounds_per_step, steps, warmup, cores):
-    """The reference's own verify rounds on the host: prime the 1024-id
-    prompt, then steps of `rounds_per_step` session_guess(4) + keep(4)
-    rounds (every block kept, as the always-right proposer's would be; the
-    cost of a round does not depend on which ids it verifies)."""
+    """The reference's own verify rounds on the host, over the positions the
+    GPU arm covers: prime the 1024-id prompt, then session_guess(4) +
+    keep(4) rounds from position 1024 to 1280 (64 rounds, every block kept,
+    as the always-right proposer's would be; the cost of a round does not
+    depend on which ids it verifies), `rounds_per_step` of them a step.
+    When a step would run past position 1280 the session is primed again,
+    untimed: the reference's session_hold refuses once its sliding ring has
+    turned over (app_core.c:13935-13945), so it cannot wind back."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import igo
     folder = ensure_checkpoint()
     rm = igo.RefModel(folder, threads=cores, window_limit=4096)
     rs = igo.RefSession(rm)
     prompt = make_prompt()
+    rounds_total = TOKENS // GUESS
     t0 = time.perf_counter()
     rs.prime(prompt)
     prime_s = time.perf_counter() - t0
     rng = np.random.default_rng(7)
     last = int(prompt[-1])
+    done = 0
     times = []
     for it in range(warmup + steps):
+        if done + rounds_per_step > rounds_total:
+            rs.reset()
+            rs.prime(prompt)
+            last, done = int(prompt[-1]), 0
         t0 = time.perf_counter()
         for _ in range(rounds_per_step):
             blk = np.concatenate([[last], rng.integers(0, VOCAB, GUESS - 1)]).astype(np.int32)
@@ -217,6 +236,7 @@ def reference_rounds(rounds_per_step, steps, warmup, cores):
             top = rs.rows_argmax(GUESS)
             rs.keep(GUESS)
             last = int(top[-1])
+        done += rounds_per_step
         if it >= warmup:
             times.append(time.perf_counter() - t0)
     rs.close()
@@ -246,8 +266,10 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(tok, 3), "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * total / len(times), 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "E2B int4 g32 verify rounds, greedy --guess 4, 1024-id prompt (config 0)",
-                   "sample": f"{rounds} rounds a step", "threads": cores},
+        "config": {"workload": "E2B int4 g32 greedy --guess 4 verify rounds, 1024-id prompt, 256 tokens (config 0)",
+                   "sample": f"{rounds} rounds of 4 lanes a step, positions 1024-1280 as the GPU arm "
+                             f"(re-primed untimed after every 64 rounds)",
+                   "threads": cores},
         "cpu_baseline": {"value": round(tok, 3), "unit": "tok/s", "cores": cores, "kind": "reference",
                          "sample": f"{rounds} verify rounds of {GUESS} lanes a step after the 1024-id prime "
                                    f"({prime_s:.1f} s)"},
@@ -266,13 +288,13 @@ def run_ours(args):
     if int(os.environ.get("WORLD_SIZE", "1")) > 1:
         import torch
         torch.cuda.set_device(local)
-    ranks = Ranks("nccl", device=f"cuda:{local}")
+    ranks = Ranks("gloo")
     rank, world = ranks.rank, ranks.world
     barrier, max_over_ranks = ranks.barrier, ranks.max
 
     model = ig.Model(spec=ig.spec_e2b(seed=1, window_limit=4096), device=local, window_limit=4096)
     sess = ig.Session(model)
-    prompt = make_prompt()
+    prompt = make_prompt(rank)  # config 0's prompt on rank 0; each replica its own stream
     sess.prime(prompt)
     base = sess.fill
     # the true greedy continuation, by plain steps
@@ -290,6 +312,7 @@ def run_ours(args):
         sess.bench(blocks, GUESS)
         sess.hold(base)
     ig.launch_count()
+    sess.stamps(GUESS, reset=True)
     barrier()
     with ClockSampler(local) as clocks:
         dev_ms = []
@@ -300,6 +323,7 @@ def run_ours(args):
             sess.hold(base)
         profiler_range(False)
     launches = ig.launch_count()
+    stamps = sess.stamps(GUESS, reset=True)  # the timed passes' own launch spans
     total_s = max_over_ranks(sum(dev_ms) / 1000.0)
     value = aggregate(TOKENS * args.steps, total_s, world)
     check_ok = int(top[-1]) == int(cont[rounds * GUESS - 1])
@@ -372,17 +396,22 @@ def run_ours(args):
     prefill = {"tok_s": round((PREFILL_LEN - 1) / (t1 - t0), 1), "ttft_ms": round(1000 * (t2 - t0), 2),
                "prompt": f"{PREFILL_LEN} uniform ids, seed 1 (config 3), 16-lane passes"}
 
-    # the projection kernel against the HBM roofline, timed live
-    prof = sess.profile(blocks[0])
-    sess.hold(base)
-    gemv = [(b, ms) for c, b, ms in prof if c == 0]
-    head = [(b, ms) for c, b, ms in prof if c == 1]
-    attn_ms = sum(ms for c, b, ms in prof if c == 2)
-    other_ms = sum(ms for c, b, ms in prof if c == 3)
-    g_bytes, g_ms = sum(b for b, _ in gemv), sum(ms for _, ms in gemv)
-    h_bytes, h_ms = sum(b for b, _ in head), sum(ms for _, ms in head)
+    # the projection kernels against the HBM roofline, from the timed
+    # region's own graphed passes: every projection and attention launch
+    # stamped its span (first block past its wait on the kernel ahead to the
+    # last block's end) and the pass's last kernel summed them on the device
+    passes = args.steps * rounds
+    gemv = [(b, ns) for c, b, ns in stamps if c == 0]
+    head = [(b, ns) for c, b, ns in stamps if c == 1]
+    attn_ns = sum(ns for c, b, ns in stamps if c == 2)
+    g_bytes = sum(b for b, _ in gemv)                      # per pass
+    g_ms = sum(ns for _, ns in gemv) / 1e6 / passes       # per pass
+    h_bytes = sum(b for b, _ in head)
+    h_ms = sum(ns for _, ns in head) / 1e6 / passes
+    attn_ms = attn_ns / 1e6 / passes
+    pass_ms = sum(dev_ms) / passes  # this rank's device time a pass
     peak, peak_kind = peaks()
-    achieved = g_bytes / (g_ms / 1000.0) / 1e9
+    achieved = g_bytes / (g_ms / 1000.0) / 1e9 if g_ms > 0 else None
     # DRAM bytes per projection launch: the algorithmic bytes times the
     # DRAM/algorithmic ratio ncu measured on the same kernels (profiles/).
     traffic = None
@@ -411,12 +440,18 @@ def run_ours(args):
         "prefill": prefill,
         "ngram": {"tok_s": round(TOKENS / ngram_s, 1), "rounds": rounds_n, "guesses": drawn, "kept": kept},
         "roofline": {"bound": "hbm", "kernel": "int4 skinny GEMM (layer projections)",
-                     "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                     "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic,
+                     "peak_kind": peak_kind,
+                     "timing": "launch stamps of the timed graphed passes (%globaltimer: first block past its "
+                               "wait to last block's end), summed on the device over every timed pass",
                      "launches_per_pass": len(gemv), "algorithmic_bytes_per_launch": round(g_bytes / max(1, len(gemv))),
                      "bytes_per_pass": g_bytes, "ms_per_pass": round(g_ms, 4),
+                     "head_ms_per_pass": round(h_ms, 4),
                      "head_gbs": round(h_bytes / (h_ms / 1000.0) / 1e9, 1) if h_ms else None,
-                     "attention_ms_per_pass": round(attn_ms, 4), "other_ms_per_pass": round(other_ms, 4),
+                     "attention_ms_per_pass": round(attn_ms, 4),
+                     "pass_ms": round(pass_ms, 4),
+                     "stamped_share_of_pass": round((g_ms + h_ms + attn_ms) / pass_ms, 4) if pass_ms else None,
                      "round_frac": round(bytes_round / round_s / 1e9 / peak, 4)},
         "clocks": clocks.summary(),
         "check": {"last_round_argmax_matches_stepped_stream": check_ok, "e2e_kept": takes,
@@ -433,6 +468,32 @@ def run_ours(args):
     ranks.close()
 
 
+def run_profile_case(args):
+    """A small verify-round case for kernel profilers (no JSON line): the E2B
+    layer stack at full width with a vocabulary of `--case-vocab` ids, so the
+    per-layer kernels are the benchmark's own while the device holds about
+    1.3 GB (at 32768 ids).  The session is primed to `--case-context` ids,
+    then `--case-rounds` verify rounds of `--case-k` lanes run between
+    cuProfilerStart and cuProfilerStop: a profiler started with
+    --profile-from-start off sees those launches only."""
+    import igllm_b200 as ig
+    spec = ig.spec_e2b(seed=1, window_limit=4096)
+    spec.vocab = args.case_vocab
+    model = ig.Model(spec=spec, device=0, window_limit=4096)
+    sess = ig.Session(model)
+    rng = np.random.default_rng(0)
+    sess.prime(rng.integers(0, args.case_vocab, args.case_context).astype(np.int32))
+    blocks = rng.integers(0, args.case_vocab, (args.case_rounds, args.case_k)).astype(np.int32)
+    sess.bench(blocks[:1], args.case_k)  # captures the pass of this shape
+    profiler_range(True)
+    ms, _ = sess.bench(blocks, args.case_k)
+    profiler_range(False)
+    print(f"profile case: {args.case_rounds} rounds of {args.case_k} lanes at context {args.case_context}, "
+          f"vocab {args.case_vocab}: {1000 * ms / args.case_rounds:.1f} us/round", flush=True)
+    sess.close()
+    model.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -440,8 +501,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the host-core reference baseline")
+    ap.add_argument("--profile-case", action="store_true",
+                    help="run the small profiler case instead of the benchmark (no JSON line)")
+    ap.add_argument("--case-vocab", type=int, default=32768)
+    ap.add_argument("--case-k", type=int, default=4)
+    ap.add_argument("--case-rounds", type=int, default=3)
+    ap.add_argument("--case-context", type=int, default=1024)
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile_case:
+        run_profile_case(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -144,6 +144,7 @@ def _lib():
         "igc_session_serve_tokens": (ctypes.c_size_t, [vp]),
         "igc_session_bench": (i, [vp, i32p, i, i, fp, i32p]),
         "igc_session_profile": (i, [vp, i32p, i, _P(ctypes.c_int), _P(ctypes.c_double), fp, i]),
+        "igc_session_stamps": (i, [vp, i, _P(ctypes.c_int), _P(ctypes.c_double), _P(ctypes.c_double), i, i]),
         "igc_scout_open": (i, [_P(vp)]),
         "igc_scout_close": (None, [vp]),
         "igc_scout_clear": (None, [vp]),
@@ -179,6 +180,7 @@ def exported_symbols():
         "igc_session_guess_keep", "igc_session_guess_taste", "igc_session_pick", "igc_session_fill",
         "igc_session_guess_span", "igc_session_guess_limit", "igc_session_round",
         "igc_session_serve_seconds", "igc_session_serve_tokens", "igc_session_bench", "igc_session_profile",
+        "igc_session_stamps",
         "igc_scout_open", "igc_scout_close",
         "igc_scout_clear", "igc_scout_note", "igc_scout_span", "igc_scout_draw", "igc_synth_fill",
         "igc_synth_write", "igc_model_synth", "igc_last_error", "igc_launch_count", "igc_norm_rms_fixed",
@@ -345,6 +347,20 @@ class Session:
             raise IgcError(n, "session_profile")
         return list(zip(cls[:n].tolist(), byt[:n].tolist(), ms[:n].tolist()))
 
+    def stamps(self, k, reset=False):
+        """Launch stamps of the graphed k-lane passes with a head since the last
+        reset: list of (class, weight bytes, total ns)."""
+        cap = 4096
+        cls = np.zeros(cap, np.int32)
+        byt = np.zeros(cap, np.float64)
+        ns = np.zeros(cap, np.float64)
+        n = _lib().igc_session_stamps(self._h, int(k), cls.ctypes.data_as(_P(ctypes.c_int)),
+                                      byt.ctypes.data_as(_P(ctypes.c_double)),
+                                      ns.ctypes.data_as(_P(ctypes.c_double)), cap, 1 if reset else 0)
+        if n < 0:
+            raise IgcError(n, "session_stamps")
+        return list(zip(cls[:n].tolist(), byt[:n].tolist(), ns[:n].tolist()))
+
     def serve_seconds(self):
         return _lib().igc_session_serve_seconds(self._h)
 
@@ -408,7 +424,10 @@ class Desk:
     def norm_rms(self, x, w, eps):
         x = np.ascontiguousarray(x, np.float32)
         out = np.zeros_like(x)
-        wp = np.ascontiguousarray(w, np.float32).ctypes.data_as(_f) if w is not None else None
+        wa = np.ascontiguousarray(w, np.float32) if w is not None else None
+        if wa is not None and wa.size != x.size:
+            raise ValueError(f"norm_rms: gain has {wa.size} values for {x.size}")
+        wp = wa.ctypes.data_as(_f) if wa is not None else None
         self._d.norm_rms(ctypes.byref(self._d), x.ctypes.data_as(_f), wp, len(x), eps, out.ctypes.data_as(_f))
         _check(self.status(), "desk.norm_rms")
         return out
@@ -446,6 +465,8 @@ def norm_rms_fixed(x, w, eps, device=0):
     x = np.ascontiguousarray(x, np.float32)
     out = np.zeros_like(x)
     wa = np.ascontiguousarray(w, np.float32) if w is not None else None
+    if wa is not None and wa.size != x.size:
+        raise ValueError(f"norm_rms_fixed: gain has {wa.size} values for {x.size}")
     wp = wa.ctypes.data_as(_f) if wa is not None else None
     code = _lib().igc_norm_rms_fixed(int(device), x.ctypes.data_as(_f), wp, len(x), float(eps),
                                      out.ctypes.data_as(_f))

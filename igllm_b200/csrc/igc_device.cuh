@@ -139,6 +139,27 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 
+// ---- launch stamps ---------------------------------------------------------
+// A stamped launch keeps two words: the earliest time any of its blocks got
+// past its wait on the kernel ahead (when it could start its real work) and
+// the latest time a block finished.  Their difference is the launch's span
+// on the critical path of the pass, measured inside the graphed pass itself.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void stamp_begin(unsigned long long *st) {
+  if (st && threadIdx.x == 0) atomicMin(st, global_ns());
+}
+// Every thread of the block calls it (it holds a block barrier).
+__device__ __forceinline__ void stamp_end(unsigned long long *st) {
+  if (st) {
+    __syncthreads();
+    if (threadIdx.x == 0) atomicMax(st + 1, global_ns());
+  }
+}
+
 __device__ __forceinline__ void named_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(threads) : "memory");
 }

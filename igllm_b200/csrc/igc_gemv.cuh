@@ -111,6 +111,8 @@ struct GemvArgs {
   // to its first lane (the lanes are independent, so the batches run side by
   // side with the staging of `lanes` lanes each)
   int batches, lanes_total;
+  // launch stamp (igc_device.cuh stamp_begin / stamp_end), or null
+  unsigned long long *stamp;
 };
 
 // Warps a block: the planning unit of a plane (its split and block count
@@ -428,6 +430,7 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     // stream and the norm weights do not come from the kernel just before
     if (live[0]) load_x(0, 0, true);
     pdl_wait();
+    stamp_begin(a.stamp);
     // the residual's partials: warp w holds lane w's (and w + WARPS's),
     // thread l the parts l, l + 32, ... (a fixed tree whatever the lane count)
 #pragma unroll

@@ -131,7 +131,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs args) {
 
   // a residual prologue waits inside, once its first loads are out
   constexpr bool RES_PRO = PRO == PRO_RESID || PRO == PRO_RESID_NORM;
-  if constexpr (!RES_PRO) pdl_wait();
+  if constexpr (!RES_PRO) {
+    pdl_wait();
+    stamp_begin(a.stamp);
+  }
   // the multiplier of the GELU product (rows written at the start of the
   // pass), loaded now so its latency hides behind the prologue (this
   // thread's outputs: rows unit*16 + g (+8), lanes 2t+k)
@@ -191,10 +194,13 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs args) {
     for (int k = 0; k < np; ++k, ++n) {
       const int c0 = c_lo + k * P, nc = min(P, c_hi - c0);
       const int d = n % D;
-      if (!mbar_wait(&mb[d], (uint32_t)((n / D) & 1), failed ? 1 : (1 << 22))) {
-        if (!failed && lane32 == 0) atomicOr(a.err, 1);
-        failed = true;
-      }
+      // the warp agrees on the outcome: a lane whose poll gave up marks the
+      // whole warp failed, so no lane computes on bytes that never arrived
+      // unnoticed and every lane sees the same `failed` from here on
+      const bool ok = mbar_wait(&mb[d], (uint32_t)((n / D) & 1), failed ? 1 : (1 << 22));
+      const bool now_failed = __any_sync(0xffffffffu, !ok);
+      if (now_failed && !failed && lane32 == 0) atomicOr(a.err, 1);
+      failed = failed || now_failed;
       const unsigned char *src = mr + (size_t)d * slot_bytes;
       const uint4 *wt = reinterpret_cast<const uint4 *>(src);
       const uint2 *ws = reinterpret_cast<const uint2 *>(src + H * P * 512);
@@ -385,6 +391,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1) gemv_kernel(GemvArgs args) {
       }
     }
   }
+  stamp_end(a.stamp);
 }
 // ---------------------------------------------------------------------------
 // embedding rows (app_core.c:11863-11874, :11886-11891)
@@ -401,8 +408,16 @@ __device__ __forceinline__ void bf16x8_scaled(const uint4 &w, float gain, float4
 // (widths are multiples of eight; rows start 16-byte aligned).
 __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embed, int hidden,
                              float embed_gain, const uint16_t *ple_embed, int ple_vocab,
-                             int ple_width, float ple_gain, float *x_out, float *seed_out) {
+                             int ple_width, float ple_gain, float *x_out, float *seed_out,
+                             unsigned long long *stamp, int stamp_n) {
   pdl_release();
+  // the pass's launch stamps start over (every later kernel of the pass
+  // stamps only after its wait, so after this kernel has finished)
+  if (stamp && blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < stamp_n; i += blockDim.x) {
+      stamp[2 * i] = ~0ull;
+      stamp[2 * i + 1] = 0ull;
+    }
   const int j = blockIdx.x;
   if (j >= lanes) return;
   const int id = ids[j];
@@ -639,7 +654,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
                                                    const float *q_norm, const float *k_norm, const float *cs_tab,
                                                    const float *sn_tab, float eps, int owner, float *kc, float *vc,
                                                    int sliding, int span, const int *d_p0, int lanes, float *out,
-                                                   int out_stride, float *out_amax) {
+                                                   int out_stride, float *out_amax, unsigned long long *stamp) {
   using LY = AttnLayout<HD>;
   constexpr int DPL = HD / 32, NKS = HD / 16, KPW = (NKS + 7) / 8, NNT = HD / 8, NPW = (NNT + 7) / 8;
   constexpr int KS = LY::KS, VS = LY::VS, QS = LY::QS, DS = HD / CX;
@@ -708,6 +723,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   }
 
   pdl_wait();
+  stamp_begin(stamp);
   // the rows a warp prepares: query rows warp and warp + 8 (normed and
   // turned at their lane's position), then the pass's new key and value rows
   // it = warp, warp + 8, ... that fall in this block's tiles (on an owner
@@ -959,17 +975,25 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     const int f = rb * AT_ROWS + tid, j = f / G, h = kh * G + (f - j * G);
     if (j < lanes) out_amax[(size_t)j * GEMV_PART_LIMIT + h * CX + r] = amx[tid];
   }
+  stamp_end(stamp);
 }
 
 // argmax partials of the output head merged per lane (app_main.c:482: the
 // first index of the largest value).  Thread (lane, stripe) scans parts
 // stripe, stripe + 32, ...; the stripes then meet in shared memory.
 __global__ void argmax_final_kernel(const float *part_val, const int *part_idx, int parts, int lanes,
-                                    int32_t *top_out) {
+                                    int32_t *top_out, const unsigned long long *stamp,
+                                    unsigned long long *stamp_sum, int stamp_n) {
   __shared__ float sv[32][16];
   __shared__ int si[32][16];
   pdl_release();
   pdl_wait();
+  // the last kernel of a pass adds each stamped launch's span to its total
+  if (stamp_sum)
+    for (int k = threadIdx.x; k < stamp_n; k += blockDim.x) {
+      const unsigned long long b = stamp[2 * k], e = stamp[2 * k + 1];
+      if (b != ~0ull && e > b) stamp_sum[k] += e - b;
+    }
   const int j = threadIdx.x & 15, stripe = threadIdx.x >> 4;
   float v = -FLT_MAX;
   int i = 0x7fffffff;
@@ -1451,10 +1475,11 @@ size_t igc_gemv_smem_min(const GemvArgs *a, int pair) {
 
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
-                             float *x_out, float *seed_out, cudaStream_t st) {
+                             float *x_out, float *seed_out, unsigned long long *stamp, int stamp_n,
+                             cudaStream_t st) {
   if ((hidden & 7) || (ple_embed && (ple_width & 7))) return cudaErrorInvalidValue;
   embed_kernel<<<dim3(lanes, 8), 256, 0, st>>>(ids, lanes, embed, hidden, embed_gain, ple_embed, ple_vocab, ple_width,
-                                      ple_gain, x_out, seed_out);
+                                      ple_gain, x_out, seed_out, stamp, stamp_n);
   return cudaGetLastError();
 }
 
@@ -1479,7 +1504,8 @@ template <int HD, int CX>
 static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const float *qkv, int qkv_stride, int heads,
                                int kv_heads, const float *q_norm, const float *k_norm, const float *cs,
                                const float *sn, float eps, int owner, float *kc, float *vc, int sliding, int span,
-                               const int *d_p0, int lanes, float *out, int out_stride, float *out_amax) {
+                               const int *d_p0, int lanes, float *out, int out_stride, float *out_amax,
+                               unsigned long long *stamp) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
@@ -1495,14 +1521,14 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const fl
   cfg.attrs = at;
   cfg.numAttrs = g_pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, attn_kernel<HD, CX>, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
-                            owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax);
+                            owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp);
 }
 }  // extern "C++"
 
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
-                            int out_stride, float *out_amax, cudaStream_t st) {
+                            int out_stride, float *out_amax, unsigned long long *stamp, cudaStream_t st) {
   if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads || (cluster != 8 && cluster != 16))
     return cudaErrorInvalidValue;
   const size_t smem = igc_attn_smem(hd);
@@ -1511,10 +1537,10 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
 #define IGC_ATT(HD)                                                                                              \
   return cluster == 8 ? launch_attn<HD, 8>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                            sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,   \
-                                           out_amax)                                                              \
+                                           out_amax, stamp)                                                       \
                       : launch_attn<HD, 16>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                             sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,  \
-                                            out_amax);
+                                            out_amax, stamp);
   switch (hd) {
     case 32: IGC_ATT(32)
     case 64: IGC_ATT(64)
@@ -1526,8 +1552,10 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
 }
 
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
+                              const unsigned long long *stamp, unsigned long long *stamp_sum, int stamp_n,
                               cudaStream_t st) {
-  return launch_k(argmax_final_kernel, dim3(1), dim3(512), 0, st, part_val, part_idx, parts, lanes, top);
+  return launch_k(argmax_final_kernel, dim3(1), dim3(512), 0, st, part_val, part_idx, parts, lanes, top, stamp,
+                  stamp_sum, stamp_n);
 }
 
 cudaError_t igc_launch_rope_table(const float *steps, int half, int window, float *cs, float *sn,

@@ -29,7 +29,8 @@ size_t igc_gemv_smem_min(const igc::GemvArgs *a, int pair);
 
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
-                             float *x_out, float *seed_out, cudaStream_t st);
+                             float *x_out, float *seed_out, unsigned long long *stamp, int stamp_n,
+                             cudaStream_t st);
 cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes, int layers, int ple_dim,
                                   const float *w, float eps, float blend, float *out, cudaStream_t st);
 size_t igc_attn_smem(int hd);
@@ -41,8 +42,11 @@ size_t igc_attn_smem(int hd);
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
-                            int out_stride, float *out_amax, cudaStream_t st);
+                            int out_stride, float *out_amax, unsigned long long *stamp, cudaStream_t st);
+// `stamp_sum`, when given, gets each of the pass's `stamp_n` stamped launches'
+// spans added (igc_device.cuh stamp_begin / stamp_end).
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,
+                              const unsigned long long *stamp, unsigned long long *stamp_sum, int stamp_n,
                               cudaStream_t st);
 cudaError_t igc_launch_rope_table(const float *steps, int half, int window, float *cs, float *sn,
                                   cudaStream_t st);

@@ -819,6 +819,17 @@ struct igc_session {
   std::vector<Mark> marks;
   int32_t *d_rounds = nullptr;  // igc_session_bench's per-round [position, ids]
   size_t d_rounds_cap = 0;
+  // launch stamps of the graphed pass (igc_session_stamps): [IGC_STAMP_LIMIT]
+  // (begin, end) pairs the pass's kernels write, and per stamped launch the
+  // total of its spans over every pass with a head since the last reset
+  unsigned long long *d_stamp = nullptr, *d_stamp_sum = nullptr;
+  struct StampMeta {
+    int cls;
+    double bytes;
+  };
+  int stamp_n = 0;                     // launches stamped in the pass being enqueued
+  std::vector<StampMeta> stamp_build;  // their classes and weight bytes
+  std::vector<StampMeta> stamp_meta[IGC_LANE_LIMIT + 1];  // of the pass with a head, per lane count
 
   ~igc_session() {
     cudaSetDevice(m->device);
@@ -898,6 +909,9 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (c == IGC_OKAY) c = s->alloc(&s->top_i, (size_t)K * 256);
   if (c == IGC_OKAY) c = s->alloc(&s->d_echo, (size_t)m->window_limit);
   if (c == IGC_OKAY) c = s->alloc(&s->d_echo_range, 2 * K);
+  if (c == IGC_OKAY) c = s->alloc(&s->d_stamp, 2 * IGC_STAMP_LIMIT);
+  if (c == IGC_OKAY) c = s->alloc(&s->d_stamp_sum, IGC_STAMP_LIMIT);
+  if (c == IGC_OKAY) CK(cudaMemsetAsync(s->d_stamp_sum, 0, sizeof(unsigned long long) * IGC_STAMP_LIMIT, s->st));
   if (c != IGC_OKAY) return c;
   {
     void *h = nullptr;
@@ -968,14 +982,24 @@ static void prof_mark(igc_session *s, int cls, double bytes) {
   s->marks.push_back(mk);
 }
 
+// The next launch stamp of the pass being enqueued, with its class and the
+// weight bytes its launch streams (null once the stamps run out).
+static unsigned long long *next_stamp(igc_session *s, int cls, double bytes) {
+  if (s->stamp_n >= IGC_STAMP_LIMIT) return nullptr;
+  s->stamp_build.push_back({cls, bytes});
+  return s->d_stamp + 2 * (size_t)s->stamp_n++;
+}
+
 static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, const float *x, int x_stride,
                 const float *p, const float *w_res, float gain, const float *w_in, float *x_out, float *out,
                 int out_stride, float out_scale = 1.0f, const float *aux = nullptr, int aux_stride = 0,
                 const Ssq *p_ssq = nullptr, Ssq *out_ssq = nullptr, const Ssq *x_amax = nullptr,
                 Ssq *out_amax = nullptr) {
-  prof_mark(s, &pl == &s->m->head ? PROF_HEAD : PROF_GEMV, pl.bytes);
+  const int cls = &pl == &s->m->head ? PROF_HEAD : PROF_GEMV;
+  prof_mark(s, cls, pl.bytes);
   GemvArgs a;
   memset(&a, 0, sizeof(a));
+  a.stamp = next_stamp(s, cls, pl.bytes);
   if (p_ssq) {
     a.p_ssq = p_ssq->buf;
     a.p_parts = p_ssq->parts;
@@ -1111,9 +1135,11 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   const int H = m->hidden, PS = m->layers * m->ple_dim;
   const int *d_p0 = s->d_io;
   const int32_t *d_ids = s->d_io + 1;
+  s->stamp_n = 0;
+  s->stamp_build.clear();
   prof_mark(s, PROF_OTHER, 0.0);
   CKL(igc_launch_embed(d_ids, K, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
-                       PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->st));
+                       PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->d_stamp, IGC_STAMP_LIMIT, s->st));
   if (m->ple_dim > 0) {
     int c = gemv(s, m->ple_lift, K, PRO_F32, EPI_STORE, s->x0, H, nullptr, nullptr, 1.0f, nullptr, nullptr,
                  s->ple_raw, PS, (float)(1.0 / sqrt((double)H)));
@@ -1160,7 +1186,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                         m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
                         m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
-                        s->st));
+                        next_stamp(s, PROF_ATTN, 0.0), s->st));
     ma.parts = m->heads * s->attn_cluster;
     c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
              1.0f, nullptr, 0, nullptr, &so, ma_in);
@@ -1198,7 +1224,9 @@ static int enqueue_pass(igc_session *s, int K, int want) {
                  s->logits, m->vocab, 1.0f, nullptr, 0, pend_ssq, nullptr);
     if (c != IGC_OKAY) return c;
     prof_mark(s, PROF_OTHER, 0.0);
-    CKL(igc_launch_argmax(s->arg_val, s->arg_idx, s->head_parts, K, s->d_top, s->st));
+    CKL(igc_launch_argmax(s->arg_val, s->arg_idx, s->head_parts, K, s->d_top, s->d_stamp, s->d_stamp_sum,
+                          s->stamp_n, s->st));
+    s->stamp_meta[K] = s->stamp_build;
   }
   prof_mark(s, PROF_END, 0.0);
   return IGC_OKAY;
@@ -1661,6 +1689,34 @@ extern "C" int igc_session_profile(igc_session *s, const int32_t *ids, int k, in
   s->fill += k;
   for (int j = 0; j < k && (int)s->echo.size() < m->window_limit; ++j) s->echo.push_back(ids[j]);
   s->logit_lanes = k;
+  return n;
+}
+
+// The launch stamps of the graphed passes with a head: for each stamped
+// launch of the `k`-lane pass, its class (as igc_session_profile), the
+// weight bytes it streams and the total of its spans, in ns, over every such
+// pass since the last reset (each span runs from the first block past its
+// wait on the kernel ahead to the last block's end).  With `reset` the totals
+// start over after the read.  Returns the launches written.
+extern "C" int igc_session_stamps(igc_session *s, int k, int *cls_out, double *bytes_out, double *ns_out,
+                                  int capacity, int reset) {
+  if (!s || k < 1 || k > IGC_LANE_LIMIT || capacity < 0) return IGC_FAIL_ARGUMENT;
+  clear_stale("stamps");
+  CK(cudaSetDevice(s->m->device));
+  std::vector<unsigned long long> sum(IGC_STAMP_LIMIT);
+  CK(cudaStreamSynchronize(s->st));
+  CK(cudaMemcpy(sum.data(), s->d_stamp_sum, sizeof(unsigned long long) * IGC_STAMP_LIMIT, cudaMemcpyDeviceToHost));
+  const auto &meta = s->stamp_meta[k];
+  int n = 0;
+  for (size_t i = 0; i < meta.size() && n < capacity; ++i, ++n) {
+    if (cls_out) cls_out[n] = meta[i].cls;
+    if (bytes_out) bytes_out[n] = meta[i].bytes;
+    if (ns_out) ns_out[n] = (double)sum[i];
+  }
+  if (reset) {
+    CK(cudaMemsetAsync(s->d_stamp_sum, 0, sizeof(unsigned long long) * IGC_STAMP_LIMIT, s->st));
+    CK(cudaStreamSynchronize(s->st));
+  }
   return n;
 }
 

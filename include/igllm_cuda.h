@@ -204,11 +204,24 @@ size_t igc_session_serve_tokens(const igc_session *session);
  * igc_session_profile: one kept pass of `k` lanes with a CUDA event before
  * every launch; per launch its class (0 a layer projection, 1 the output
  * head, 2 attention, 3 the rest), the weight bytes it streams and its device
- * time.  Returns the number of launches written (at most `capacity`). */
+ * time.  Returns the number of launches written (at most `capacity`).
+ *
+ * igc_session_stamps: the launch stamps every pass with a head leaves, read
+ * from the graphed passes themselves (no events between launches).  Each
+ * projection and attention launch records when its first block got past its
+ * wait on the kernel ahead and when its last block finished; the pass's last
+ * kernel adds that span to the launch's total.  For each stamped launch of
+ * the `k`-lane pass: its class (as above), its weight bytes and its total in
+ * ns over every pass with a head since the last reset.  Read them after
+ * passes of one lane count only.  With `reset` the totals start over after
+ * the read.  Returns the number of launches written. */
+#define IGC_STAMP_LIMIT 512
 int igc_session_bench(igc_session *session, const int32_t *blocks, int rounds, int k, float *device_ms,
                       int32_t *last_top);
 int igc_session_profile(igc_session *session, const int32_t *ids, int k, int *cls_out, double *bytes_out,
                         float *ms_out, int capacity);
+int igc_session_stamps(igc_session *session, int k, int *cls_out, double *bytes_out, double *ns_out, int capacity,
+                       int reset);
 
 /* ---- normalisation with no allocation (no counterpart in the reference) --
  *
@@ -219,7 +232,13 @@ int igc_session_profile(igc_session *session, const int32_t *ids, int k, int *cl
  * library's device image (3 x IGC_FIXED_NORM_LIMIT floats, 768 KiB a device);
  * the call makes no allocating CUDA or library call.  The array's address is
  * looked up on the first call on each device, with that device current; make
- * that first call before any stream capture starts.  `device` is made current
+ * that first call before any stream capture starts.  That first call may also
+ * be the one that creates the device's context or loads the library's device
+ * image (CUDA loads modules lazily), which the driver allocates for; the
+ * no-allocation guarantee holds from the second call on a device.  The looked
+ * up address is kept for the life of the process: a caller that resets the
+ * device (cudaDeviceReset) or tears its primary context down must not call
+ * this entry on that device again.  `device` is made current
  * for the call and the caller's device restored after it.  `gain_list` may be
  * NULL (no gain).  Vectors longer than IGC_FIXED_NORM_LIMIT, or a device at or
  * beyond IGC_FIXED_DEVICE_LIMIT, are refused with IGC_FAIL_ARGUMENT and nothing

@@ -430,6 +430,9 @@ class RefSession:
     def fill(self):
         return self.lib.ref_session_fill(self.h)
 
+    def reset(self):
+        self.lib.ref_session_reset(self.h)
+
     def prime(self, ids):
         a = np.ascontiguousarray(ids, np.int32)
         assert self.lib.ref_session_prime(self.h, iptr(a), len(a)) == 0

@@ -23,7 +23,7 @@ def _rank_main(rank, world, port, out):
                       MASTER_PORT=str(port))
     sys.path.insert(0, ROOT)
     import bench
-    ranks = bench.Ranks("gloo", device="cpu")
+    ranks = bench.Ranks()  # gloo over host sockets: no NCCL communicator
     ranks.barrier()
     seconds = 1.0 + 0.5 * rank  # the slower rank sets the job's time
     slowest = ranks.max(seconds)
