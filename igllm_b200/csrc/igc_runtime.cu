@@ -802,6 +802,7 @@ struct igc_session {
   int attn_cluster = 16;  // attention blocks a cluster, fixed for the session
   int use_graphs = 1;
   int use_pdl = 1;
+  int use_stamps = 1;  // IGC_NO_STAMPS=1 launches without launch stamps (for comparison)
   int head_parts = 0;  // argmax partials the output head's launch left
   cudaGraphExec_t graph[IGC_LANE_LIMIT + 1][2] = {};
   double serve_seconds = 0.0;
@@ -928,6 +929,8 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   s->use_graphs = !(g && g[0] == '1');
   const char *np = getenv("IGC_NO_PDL");
   s->use_pdl = !(np && np[0] == '1');
+  const char *ns = getenv("IGC_NO_STAMPS");
+  s->use_stamps = !(ns && ns[0] == '1');
   // attention clusters of 16 blocks (half the tiles a block of 8 takes)
   // unless IGC_ATTN_CLUSTER=8 or the heads' magnitude partials would not fit
   const char *ac = getenv("IGC_ATTN_CLUSTER");
@@ -985,7 +988,7 @@ static void prof_mark(igc_session *s, int cls, double bytes) {
 // The next launch stamp of the pass being enqueued, with its class and the
 // weight bytes its launch streams (null once the stamps run out).
 static unsigned long long *next_stamp(igc_session *s, int cls, double bytes) {
-  if (s->stamp_n >= IGC_STAMP_LIMIT) return nullptr;
+  if (!s->use_stamps || s->stamp_n >= IGC_STAMP_LIMIT) return nullptr;
   s->stamp_build.push_back({cls, bytes});
   return s->d_stamp + 2 * (size_t)s->stamp_n++;
 }
@@ -1139,7 +1142,8 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   s->stamp_build.clear();
   prof_mark(s, PROF_OTHER, 0.0);
   CKL(igc_launch_embed(d_ids, K, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
-                       PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->d_stamp, IGC_STAMP_LIMIT, s->st));
+                       PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->use_stamps ? s->d_stamp : nullptr,
+                       IGC_STAMP_LIMIT, s->st));
   if (m->ple_dim > 0) {
     int c = gemv(s, m->ple_lift, K, PRO_F32, EPI_STORE, s->x0, H, nullptr, nullptr, 1.0f, nullptr, nullptr,
                  s->ple_raw, PS, (float)(1.0 / sqrt((double)H)));
@@ -1224,8 +1228,8 @@ static int enqueue_pass(igc_session *s, int K, int want) {
                  s->logits, m->vocab, 1.0f, nullptr, 0, pend_ssq, nullptr);
     if (c != IGC_OKAY) return c;
     prof_mark(s, PROF_OTHER, 0.0);
-    CKL(igc_launch_argmax(s->arg_val, s->arg_idx, s->head_parts, K, s->d_top, s->d_stamp, s->d_stamp_sum,
-                          s->stamp_n, s->st));
+    CKL(igc_launch_argmax(s->arg_val, s->arg_idx, s->head_parts, K, s->d_top, s->d_stamp,
+                          s->use_stamps ? s->d_stamp_sum : nullptr, s->stamp_n, s->st));
     s->stamp_meta[K] = s->stamp_build;
   }
   prof_mark(s, PROF_END, 0.0);

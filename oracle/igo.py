@@ -357,6 +357,30 @@ def ref_lib_path():
 
 
 _REF = None
+_REF_CUDA = None
+REF_CUDA_PATH = os.path.join(REF_DIR, "libref_cuda.so")
+
+
+def ref_cuda_lib():
+    """The reference engine with its backend table served by libigllm_cuda
+    (oracle/app_cuda.c), built by oracle/Makefile where the reference source
+    and the CUDA library were both present."""
+    global _REF_CUDA
+    if _REF_CUDA is None:
+        if not os.path.exists(REF_CUDA_PATH):
+            raise RuntimeError(f"{REF_CUDA_PATH} is missing: run `make -C oracle all` after building the library")
+        lib = _bind_ref(ctypes.CDLL(REF_CUDA_PATH))
+        vp, i = ctypes.c_void_p, ctypes.c_int
+        lib.ref_model_load_cuda.restype = i
+        lib.ref_model_load_cuda.argtypes = [ctypes.c_char_p, i, i, i, ctypes.POINTER(vp)]
+        lib.ref_desk_name.restype = ctypes.c_char_p
+        lib.ref_desk_name.argtypes = [vp]
+        lib.ref_cuda_status.restype = i
+        lib.ref_cuda_status.argtypes = []
+        lib.ref_cuda_close.restype = None
+        lib.ref_cuda_close.argtypes = []
+        _REF_CUDA = lib
+    return _REF_CUDA
 
 
 def ref_lib():
@@ -365,42 +389,54 @@ def ref_lib():
         path = ref_lib_path()
         if not os.path.exists(path):
             build()
-        lib = ctypes.CDLL(path)
-        vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)
-        i32p = ctypes.POINTER(ctypes.c_int32)
-        for name, res, args in [
-            ("ref_model_load", i, [ctypes.c_char_p, i, i, ctypes.POINTER(vp)]),
-            ("ref_model_free", None, [vp]),
-            ("ref_model_vocab", i, [vp]),
-            ("ref_model_decode_bytes", ctypes.c_size_t, [vp]),
-            ("ref_model_window", i, [vp]),
-            ("ref_session_open", i, [vp, ctypes.POINTER(vp)]),
-            ("ref_session_close", None, [vp]),
-            ("ref_session_reset", None, [vp]),
-            ("ref_session_fill", i, [vp]),
-            ("ref_session_hold", i, [vp, i]),
-            ("ref_session_prime", i, [vp, i32p, i]),
-            ("ref_session_step", i, [vp, ctypes.c_int32, f]),
-            ("ref_session_guess", i, [vp, i32p, i, f]),
-            ("ref_session_rows", vp, [vp]),
-            ("ref_session_keep", i, [vp, i]),
-            ("ref_session_taste", i, [vp, f, i32p, i, ctypes.POINTER(Taste), i32p]),
-            ("ref_session_pick", ctypes.c_int32, [vp, f, ctypes.POINTER(Taste)]),
-            ("ref_session_serve_seconds", ctypes.c_double, [vp]),
-            ("ref_session_serve_tokens", ctypes.c_size_t, [vp]),
-        ]:
-            fn = getattr(lib, name)
-            fn.restype = res
-            fn.argtypes = args
-        _REF = lib
+        _REF = _bind_ref(ctypes.CDLL(path))
     return _REF
 
 
+def _bind_ref(lib):
+    """Argument and result types of the ref_* wrappers (oracle/ref_harness.c)."""
+    vp, i, f = ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)
+    i32p = ctypes.POINTER(ctypes.c_int32)
+    for name, res, args in [
+        ("ref_model_load", i, [ctypes.c_char_p, i, i, ctypes.POINTER(vp)]),
+        ("ref_model_free", None, [vp]),
+        ("ref_model_vocab", i, [vp]),
+        ("ref_model_decode_bytes", ctypes.c_size_t, [vp]),
+        ("ref_model_window", i, [vp]),
+        ("ref_session_open", i, [vp, ctypes.POINTER(vp)]),
+        ("ref_session_close", None, [vp]),
+        ("ref_session_reset", None, [vp]),
+        ("ref_session_fill", i, [vp]),
+        ("ref_session_hold", i, [vp, i]),
+        ("ref_session_prime", i, [vp, i32p, i]),
+        ("ref_session_step", i, [vp, ctypes.c_int32, f]),
+        ("ref_session_guess", i, [vp, i32p, i, f]),
+        ("ref_session_rows", vp, [vp]),
+        ("ref_session_keep", i, [vp, i]),
+        ("ref_session_taste", i, [vp, f, i32p, i, ctypes.POINTER(Taste), i32p]),
+        ("ref_session_pick", ctypes.c_int32, [vp, f, ctypes.POINTER(Taste)]),
+        ("ref_session_serve_seconds", ctypes.c_double, [vp]),
+        ("ref_session_serve_tokens", ctypes.c_size_t, [vp]),
+    ]:
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
 class RefModel:
-    def __init__(self, folder, threads=8, window_limit=0):
-        self.lib = ref_lib()
+    """The reference's model_load; with `cuda_device` set, the build whose
+    backend table is libigllm_cuda's (its products on that GPU)."""
+
+    def __init__(self, folder, threads=8, window_limit=0, cuda_device=None):
         self.h = ctypes.c_void_p()
-        code = self.lib.ref_model_load(str(folder).encode(), threads, window_limit, ctypes.byref(self.h))
+        if cuda_device is None:
+            self.lib = ref_lib()
+            code = self.lib.ref_model_load(str(folder).encode(), threads, window_limit, ctypes.byref(self.h))
+        else:
+            self.lib = ref_cuda_lib()
+            code = self.lib.ref_model_load_cuda(str(folder).encode(), threads, window_limit, int(cuda_device),
+                                                ctypes.byref(self.h))
         if code != 0:
             raise RuntimeError(f"reference model_load failed: {code}")
         self.vocab = self.lib.ref_model_vocab(self.h)

@@ -341,3 +341,17 @@ def test_rejection_rule_edges(igo_mod, tiny_dir):
     greedy = igo.Taste(0.0, 64, 0.95, 1.0, 64, 0)
     assert s.guess_taste(rows, blk, greedy)[0] < 0
     s.guess_keep(0)
+
+
+def test_dropin_build_exports_the_shim():
+    """oracle/_ref/libref_cuda.so, the reference with its backend table on
+    libigllm_cuda (oracle/app_cuda.c), loads here and exports the reference's
+    wrappers plus the CUDA load entry (nothing is called without a GPU)."""
+    import os
+    import igo
+    if not os.path.exists(igo.REF_CUDA_PATH):
+        pytest.skip("built only where the reference source and the CUDA library are both present")
+    lib = ctypes.CDLL(igo.REF_CUDA_PATH)
+    for name in ("ref_model_load_cuda", "ref_cuda_status", "ref_cuda_close", "ref_desk_name", "ref_model_load",
+                 "ref_session_guess", "ref_session_keep"):
+        assert hasattr(lib, name), name
