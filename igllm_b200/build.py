@@ -18,9 +18,9 @@ BUILD = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "lib")
 TARGET = os.path.join(LIB, "libigllm_cuda.so")
 
-CUDA_SOURCES = ["igc_kernels.cu", "igc_runtime.cu", "igc_desk.cu"]
+CUDA_SOURCES = ["igc_kernels.cu", "igc_lanes.cu", "igc_runtime.cu", "igc_desk.cu"]
 C_SOURCES = ["igc_synth.c", "igc_scout.c"]
-HEADERS = ["igc_device.cuh", "igc_gemv.cuh", "igc_kernels.h", "igc_json.h", "igc_synth.h"]
+HEADERS = ["igc_device.cuh", "igc_gemv.cuh", "igc_kernels.h", "igc_lanes.h", "igc_json.h", "igc_synth.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -15,6 +15,7 @@
 
 #include "../../include/igllm_cuda.h"
 #include "igc_kernels.h"
+#include "igc_lanes.h"
 
 using namespace igc;
 
@@ -38,6 +39,11 @@ struct DeskState {
   float *arg_val = nullptr;
   int *arg_idx = nullptr;
   int *err = nullptr;  // set by a projection that gave up waiting for its weights
+  // the batched-lane path (igc_lanes.cu): activations, staged operand
+  // blocks, per-lane factors, K-slice partials and the summed product
+  float *lane_act = nullptr, *lane_factor = nullptr, *lane_part = nullptr, *lane_out = nullptr;
+  void *lane_tiles = nullptr;
+  size_t lane_act_n = 0, lane_factor_n = 0, lane_part_n = 0, lane_out_n = 0, lane_tiles_n = 0;
 };
 
 DeskState *state_of(igc_desk *d) {
@@ -103,12 +109,84 @@ const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
   return &(s->planes[p->code_data] = dp);
 }
 
+// A device buffer of at least `bytes`, grown (never shrunk) on demand.
+template <typename T>
+bool room(DeskState *s, T **p, size_t *have, size_t bytes) {
+  if (bytes <= *have) return true;
+  cudaFree(*p);
+  *p = nullptr;
+  *have = 0;
+  if (!ok(s, cudaMalloc((void **)p, bytes))) return false;
+  *have = bytes;
+  return true;
+}
+
+// Lanes at which a product runs as the tcgen05 GEMM of igc_lanes.cu (the
+// reference never passes more than 16; a caller batching many lanes - a
+// prefill chunk, or many streams' blocks - does).
+constexpr int DESK_LANE_GEMM = 64;
+
+void desk_mat_mat_lanes(DeskState *s, const DeskPlane *p, const float *act, int act_stride, int lanes, float *out,
+                        int out_stride) {
+  const int m_tiles = (lanes + LG_M - 1) / LG_M, rows_pad = p->n_rb * 16;
+  const int split = igc_lane_gemm_split(lanes, p->n_rb, p->n_cc, s->sm_count);
+  if (!room(s, &s->lane_act, &s->lane_act_n, sizeof(float) * (size_t)lanes * p->cols) ||
+      !room(s, &s->lane_factor, &s->lane_factor_n, sizeof(float) * (size_t)lanes) ||
+      !room(s, &s->lane_tiles, &s->lane_tiles_n, (size_t)m_tiles * p->n_cc * LG_M * 64 * 2) ||
+      !room(s, &s->lane_part, &s->lane_part_n, sizeof(float) * (size_t)split * lanes * rows_pad) ||
+      !room(s, &s->lane_out, &s->lane_out_n, sizeof(float) * (size_t)lanes * p->rows))
+    return;
+  if (!ok(s, cudaMemcpy2DAsync(s->lane_act, sizeof(float) * p->cols, act, sizeof(float) * act_stride,
+                               sizeof(float) * p->cols, lanes, cudaMemcpyHostToDevice, s->st)))
+    return;
+  LaneStageArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.mode = LS_PLAIN;
+  sa.lanes = lanes;
+  sa.cols = p->cols;
+  sa.x = s->lane_act;
+  sa.x_stride = p->cols;
+  sa.gain = 1.0f;
+  sa.out_scale = 1.0f;
+  sa.a_tiles = s->lane_tiles;
+  sa.n_cc = p->n_cc;
+  sa.factor = s->lane_factor;
+  if (!ok(s, igc_launch_lane_stage(&sa, s->st))) return;
+  LaneGemmArgs ga;
+  memset(&ga, 0, sizeof(ga));
+  ga.tiles = p->tiles;
+  ga.scales = p->scales;
+  ga.n_rb = p->n_rb;
+  ga.n_cc = p->n_cc;
+  ga.a_tiles = reinterpret_cast<const uint4 *>(s->lane_tiles);
+  ga.factor = s->lane_factor;
+  ga.out = s->lane_part;
+  ga.lanes = lanes;
+  ga.out_stride = rows_pad;
+  ga.split = split;
+  ga.err = s->err;
+  if (!ok(s, igc_launch_lane_gemm(&ga, s->st))) return;
+  if (!ok(s, igc_launch_lane_sum(s->lane_part, split, lanes, p->rows, rows_pad, s->lane_out, p->rows, s->st)))
+    return;
+  if (!ok(s, cudaMemcpy2DAsync(out, sizeof(float) * out_stride, s->lane_out, sizeof(float) * p->rows,
+                               sizeof(float) * p->rows, lanes, cudaMemcpyDeviceToHost, s->st)))
+    return;
+  if (!ok(s, cudaStreamSynchronize(s->st))) return;
+  int gave_up = 0;
+  if (!ok(s, cudaMemcpy(&gave_up, s->err, sizeof(int), cudaMemcpyDeviceToHost))) return;
+  if (gave_up) {
+    cudaMemset(s->err, 0, sizeof(int));
+    note(s, IGC_FAIL_DEVICE);
+  }
+}
+
 void desk_mat_mat(igc_desk *d, const igc_plane *sheet, const float *act, int act_stride, int lanes, float *out,
                   int out_stride) {
   DeskState *s = state_of(d);
   if (cudaSetDevice(s->device) != cudaSuccess) return void(note(s, IGC_FAIL_DEVICE));
   const DeskPlane *p = plane_of(s, sheet);
   if (!p) return;
+  if (lanes >= DESK_LANE_GEMM) return desk_mat_mat_lanes(s, p, act, act_stride, lanes, out, out_stride);
   for (int done = 0; done < lanes;) {  // app_core.c:5250: chunks of 16 lanes
     int k = lanes - done < IGC_LANE_LIMIT ? lanes - done : IGC_LANE_LIMIT;
     if (!grow(s, (size_t)IGC_LANE_LIMIT * (size_t)(p->cols > p->rows ? p->cols : p->rows))) return;
@@ -247,6 +325,11 @@ extern "C" void igc_back_close(igc_desk *desk) {
   cudaFree(s->arg_val);
   cudaFree(s->arg_idx);
   cudaFree(s->err);
+  cudaFree(s->lane_act);
+  cudaFree(s->lane_factor);
+  cudaFree(s->lane_part);
+  cudaFree(s->lane_out);
+  cudaFree(s->lane_tiles);
   if (s->st) cudaStreamDestroy(s->st);
   delete s;
   desk->state = nullptr;

@@ -1,0 +1,459 @@
+// igc_lanes.cu - the batched-lane path: many lanes through one weight sweep
+// on the tcgen05 tensor cores.
+//
+// The K-lane skinny GEMM of igc_gemv.cuh streams each weight once for at most
+// sixteen lanes.  A prefill chunk (app_core.c:14443-14467 session_prime runs
+// its prompt 16 lanes a pass; here a chunk is up to 256) carries enough lanes
+// that the product is a real dense contraction: out[m][n] = sum_k A[m][k] *
+// W[n][k] with M lanes, N weight rows and K input columns.  That runs here as
+// a tcgen05 GEMM:
+//
+//   lane_stage_kernel   one block a lane: the row-wise work between two
+//                       products (residual add, RMS norms, the GELU pair and
+//                       GELU x input of app_core.c:11637-11743) in f32, then
+//                       the lane scaled by a power of two and stored as f16
+//                       in the operand layout the tensor core reads (below),
+//                       with the factor that undoes the scale.
+//   lane_gemm_kernel    one block a (128-lane, 256-row) tile and K slice:
+//                       a producer warp bulk-copies the staged activations
+//                       and the packed int4 weights (with their f16 group
+//                       scales) of each 64-column step from this GPU's HBM
+//                       into a three-deep shared-memory ring; four warps turn
+//                       the codes into f16 weights, (code - 8) * scale, in
+//                       the operand layout; one thread issues the step's four
+//                       tcgen05.mma (M 128, N 256, K 16, f32 accumulate in
+//                       TMEM) and commits them to the ring slot's barrier; at
+//                       the end the four warps read the accumulators back
+//                       with tcgen05.ld and store them, times each lane's
+//                       factor, as the slice's partial sums.
+//   lane_sum_kernel     adds the K slices' partials in a fixed order.
+//
+// Operand layout (both operands K-major, 128-byte swizzle, the canonical
+// form a tcgen05 shared-memory descriptor names): a 64-column step of 128
+// rows is 16 KB, rows in groups of eight 128-byte rows (1 KB apart), and the
+// 16-byte piece j of row r sits at piece j ^ (r mod 8).  The staged
+// activations are stored in global memory already in this layout, one 16 KB
+// block per (128-lane tile, 64-column step), so one bulk copy moves a block.
+//
+// Precision: the weights are (code - 8) * scale rounded once to f16 (the
+// scale's own f16 bits times a small integer), the activations f16 after the
+// power-of-two scaling, the sums f32 - within about 1e-3 of the fp32 product
+// relative to the row's magnitude, well inside the 2e-2 the verify round is
+// held to.  The decode path keeps the exact-weight mma.sync GEMM.
+//
+// Every wait on a barrier gives up after a bounded number of polls and sets
+// the error word; the block then runs to its end and frees its tensor memory.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <float.h>
+#include <stdint.h>
+
+#include "igc_device.cuh"
+#include "igc_gemv.cuh"
+#include "igc_lanes.h"
+
+namespace igc {
+
+// ---------------------------------------------------------------------------
+// tcgen05 helpers (PTX ISA 8.6+, sm_100a)
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (stride byte offset), leading byte offset unused (1),
+// descriptor version 1, base offset 0 (every operand block is 1 KB aligned).
+__device__ __forceinline__ uint64_t lg_desc(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: f32 accumulator, f16 A and B, both
+// K-major, N = LG_N, M = LG_M.
+constexpr uint32_t LG_IDESC = (1u << 4) | ((uint32_t)(LG_N >> 3) << 17) | ((uint32_t)(LG_M >> 4) << 24);
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(LG_IDESC), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives on `bar` once every earlier tcgen05.mma of this thread has completed.
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 32 lanes x 32 columns of f32 accumulators: thread i gets row (lane base +
+// i), columns col .. col + 31.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Byte offset of the 16-byte piece j of row r inside one operand block.
+__host__ __device__ __forceinline__ uint32_t lg_swz(int r, int j) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
+}
+
+// ---------------------------------------------------------------------------
+// the GEMM
+
+constexpr int LG_STAGES = 3;
+constexpr int LG_A_BYTES = LG_M * 64 * 2;       // 16 KB
+constexpr int LG_B_BYTES = LG_N * 64 * 2;       // 32 KB
+constexpr int LG_RB = LG_N / 16;                // row blocks a tile
+constexpr int LG_CODE_BYTES = LG_RB * 512;      // 8 KB
+constexpr int LG_SCALE_BYTES = LG_RB * 64;      // 1 KB
+constexpr int LG_STAGE_BYTES = LG_A_BYTES + LG_B_BYTES + LG_CODE_BYTES + LG_SCALE_BYTES;  // 57 KB, 1 KB multiple
+constexpr int LG_BAR_BYTES = 256;
+constexpr int LG_SMEM = 1024 + LG_STAGES * LG_STAGE_BYTES + LG_BAR_BYTES;  // + alignment slack
+constexpr int LG_THREADS = 192;
+constexpr int LG_TRIES = 1 << 22;  // polls a wait makes before it gives up
+
+__global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a) {
+  extern __shared__ __align__(1024) uint8_t lg_raw[];
+  uint8_t *base = lg_raw + ((1024 - (smem_u32(lg_raw) & 1023)) & 1023);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + LG_STAGES * LG_STAGE_BYTES);
+  uint64_t *full = bars, *bfull = bars + LG_STAGES, *empty = bars + 2 * LG_STAGES, *accf = bars + 3 * LG_STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * LG_STAGES + 1);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nt = blockIdx.x, mt = blockIdx.y, z = blockIdx.z;
+  const int c_lo = (a.n_cc * z) / a.split, c_hi = (a.n_cc * (z + 1)) / a.split, nk = c_hi - c_lo;
+  const int rb0 = nt * LG_RB, rbv = min(LG_RB, a.n_rb - rb0);  // row blocks this tile holds
+
+  if (tid == 0) {
+    for (int s = 0; s < LG_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&bfull[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accf, 1);
+    mbar_init_fence();
+  }
+  if (warp == 1) {  // 256 columns of tensor memory: one f32 accumulator a tile column
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(LG_N)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool failed = false;
+
+  if (warp == 0) {
+    // producer: the staged activations (one 16 KB block) and each row
+    // block's codes (512 B) and scales (64 B) of the step
+    const uint64_t policy = l2_evict_last();  // both are read again by the other tiles
+    for (int k = 0; k < nk; ++k) {
+      const int s = k % LG_STAGES, c = c_lo + k;
+      if (k >= LG_STAGES) {
+        const bool ok = mbar_wait(&empty[s], (uint32_t)(((k / LG_STAGES) - 1) & 1), failed ? 1 : LG_TRIES);
+        if (__any_sync(0xffffffffu, !ok)) failed = true;
+      }
+      uint8_t *st = base + s * LG_STAGE_BYTES;
+      if (lane == 0)
+        mbar_expect(&full[s], (uint32_t)(LG_A_BYTES + rbv * (512 + 64)));
+      __syncwarp();
+      if (lane == 0)
+        bulk_load(st, a.a_tiles + ((size_t)mt * a.n_cc + c) * (LG_A_BYTES / 16), LG_A_BYTES, &full[s],
+                  policy);
+      if (lane < rbv) {
+        const size_t tile = (size_t)(rb0 + lane) * a.n_cc + c;
+        bulk_load(st + LG_A_BYTES + LG_B_BYTES + lane * 512, a.tiles + tile * 32, 512, &full[s], policy);
+        bulk_load(st + LG_A_BYTES + LG_B_BYTES + LG_CODE_BYTES + lane * 64, a.scales + tile * 8, 64, &full[s],
+                  policy);
+      }
+    }
+  } else if (warp == 1) {
+    // the MMA issuer: four K=16 products a 64-column step
+    for (int k = 0; k < nk; ++k) {
+      const int s = k % LG_STAGES;
+      const uint32_t ph = (uint32_t)((k / LG_STAGES) & 1);
+      bool ok = mbar_wait(&full[s], ph, failed ? 1 : LG_TRIES);
+      ok = mbar_wait(&bfull[s], ph, (failed || !ok) ? 1 : LG_TRIES) && ok;
+      if (__any_sync(0xffffffffu, !ok)) failed = true;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t sa = smem_u32(base + s * LG_STAGE_BYTES), sb = sa + LG_A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma(tmem, lg_desc(sa + kk * 32), lg_desc(sb + kk * 32), (k > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) tc_commit(accf);
+    __syncwarp();
+  } else {
+    // warps 2-5: codes to f16 weights in the operand layout, then the epilogue
+    const int dt = tid - 64;  // 0..127
+    for (int k = 0; k < nk; ++k) {
+      const int s = k % LG_STAGES;
+      const uint32_t ph = (uint32_t)((k / LG_STAGES) & 1);
+      const bool ok = mbar_wait(&full[s], ph, failed ? 1 : LG_TRIES);
+      if (__any_sync(0xffffffffu, !ok)) failed = true;
+      uint8_t *st = base + s * LG_STAGE_BYTES;
+      uint8_t *bt = st + LG_A_BYTES;
+      const uint4 *codes = reinterpret_cast<const uint4 *>(st + LG_A_BYTES + LG_B_BYTES);
+      const uint2 *scs = reinterpret_cast<const uint2 *>(st + LG_A_BYTES + LG_B_BYTES + LG_CODE_BYTES);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int slot = dt + 128 * j, rbl = slot >> 5, ts = slot & 31, g = ts >> 2, tq = ts & 3;
+        const int n0 = rbl * 16 + g, n8 = n0 + 8;
+        uint32_t v[4][4];  // [kb][register]: rows g, g+8 x columns (c, c+1), (c+8, c+9)
+        if (rbl < rbv) {
+          const uint4 w = codes[rbl * 32 + ts];
+          const uint2 sc = scs[rbl * 8 + g];
+          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) {
+            uint32_t q[4];
+            dequant_i4(words[kb], q);
+            const uint32_t sg = kb < 2 ? sc.x : sc.y;  // f16 scales of rows g (low half) and g+8 (high half)
+            const __half2 s2 = *reinterpret_cast<const __half2 *>(&sg);
+            const __half2 s0 = __low2half2(s2), s8 = __high2half2(s2);
+            __half2 h;
+            h = __hmul2(*reinterpret_cast<__half2 *>(&q[0]), s0);
+            v[kb][0] = *reinterpret_cast<uint32_t *>(&h);
+            h = __hmul2(*reinterpret_cast<__half2 *>(&q[1]), s8);
+            v[kb][1] = *reinterpret_cast<uint32_t *>(&h);
+            h = __hmul2(*reinterpret_cast<__half2 *>(&q[2]), s0);
+            v[kb][2] = *reinterpret_cast<uint32_t *>(&h);
+            h = __hmul2(*reinterpret_cast<__half2 *>(&q[3]), s8);
+            v[kb][3] = *reinterpret_cast<uint32_t *>(&h);
+          }
+        } else {
+#pragma unroll
+          for (int kb = 0; kb < 4; ++kb) v[kb][0] = v[kb][1] = v[kb][2] = v[kb][3] = 0u;
+        }
+        // the slot's first k-iteration must not overwrite weights the MMA of
+        // the step three back still reads: the producer only refilled the
+        // slot after that MMA committed, and this warp waited on the refill
+#pragma unroll
+        for (int kb = 0; kb < 4; ++kb) {
+          const int p0 = 2 * kb, p1 = 2 * kb + 1;  // 16-byte pieces of columns c and c + 8
+          *reinterpret_cast<uint32_t *>(bt + lg_swz(n0, p0) + 4 * tq) = v[kb][0];
+          *reinterpret_cast<uint32_t *>(bt + lg_swz(n8, p0) + 4 * tq) = v[kb][1];
+          *reinterpret_cast<uint32_t *>(bt + lg_swz(n0, p1) + 4 * tq) = v[kb][2];
+          *reinterpret_cast<uint32_t *>(bt + lg_swz(n8, p1) + 4 * tq) = v[kb][3];
+        }
+      }
+      fence_async_smem();  // the weights written here are read by the tensor core (async proxy)
+      mbar_arrive(&bfull[s]);
+    }
+    // epilogue: this warp's quarter of the tile's lanes
+    {
+      const bool ok = mbar_wait(accf, 0u, failed ? 1 : LG_TRIES);
+      if (__any_sync(0xffffffffu, !ok)) failed = true;
+    }
+    tc_fence_after();
+    const int q = warp & 3;  // the tensor-memory lanes this warp may read
+    const int m_local = q * 32 + lane, m = mt * LG_M + m_local;
+    const bool live = m < a.lanes;
+    const float f = live ? a.factor[m] : 0.0f;
+    const int n_rows = a.n_rb * 16;
+    float *orow = a.out + ((size_t)z * a.lanes + (live ? m : 0)) * a.out_stride;
+    for (int c0 = 0; c0 < LG_N; c0 += 32) {
+      const int n0 = nt * LG_N + c0;
+      if (n0 >= n_rows) break;  // warp-uniform
+      float v[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
+      if (live) {
+        if (n0 + 32 <= n_rows) {
+          float4 *o4 = reinterpret_cast<float4 *>(orow + n0);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o4[i] = make_float4(v[4 * i] * f, v[4 * i + 1] * f, v[4 * i + 2] * f, v[4 * i + 3] * f);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (n0 + i < n_rows) orow[n0 + i] = v[i] * f;
+        }
+      }
+    }
+    tc_fence_before();
+  }
+  if (failed && lane == 0) atomicOr(a.err, 1);
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(LG_N) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// the row-wise stage between two products
+
+__device__ __forceinline__ float block_sum(float v, float *red) {
+  // fixed order: warps in order, lanes by the xor tree
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+  for (int w = 0; w < nw; ++w) t += red[w];
+  return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+  v = warp_max(v);
+  const int warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+  for (int w = 0; w < nw; ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+
+// The producer's output row of lane j: its K-slice partials added in order.
+__device__ __forceinline__ float slice_sum(const LaneStageArgs &a, int j, int i) {
+  float s = 0.0f;
+  for (int z = 0; z < a.p_splits; ++z) s += a.p[((size_t)z * a.lanes + j) * a.p_stride + i];
+  return s;
+}
+
+__global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
+  extern __shared__ float ls_row[];  // the lane's staged values (cols floats), then the residual's
+  __shared__ float red[32];
+  const int j = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+  float *y = ls_row;
+  const int n = a.cols;
+  if (a.mode == LS_PLAIN || a.mode == LS_NORM) {
+    for (int i = tid; i < n; i += nt) y[i] = a.x[(size_t)j * a.x_stride + i];
+  } else if (a.mode == LS_GELU_PAIR) {
+    // app_core.c:11673 gelu(gate) * up: the pair plane interleaves 16-row
+    // blocks of gate and up rows
+    for (int i = tid; i < n; i += nt) {
+      const int gi = (i >> 4) * 32 + (i & 15);
+      y[i] = gelu_tanh(slice_sum(a, j, gi)) * slice_sum(a, j, gi + 16);
+    }
+  } else if (a.mode == LS_GELU_MUL) {
+    // app_core.c:11723: gelu(gate) times the layer's per-layer input
+    for (int i = tid; i < n; i += nt) y[i] = gelu_tanh(slice_sum(a, j, i)) * a.aux[(size_t)j * a.aux_stride + i];
+  } else {
+    // LS_RESID, LS_RESID_NORM (app_core.c:11690-11740): x += norm(p) * w_res,
+    // then the layer gain; the new stream is written back
+    float *pr = ls_row + n;
+    float ss = 0.0f;
+    for (int i = tid; i < n; i += nt) {
+      const float v = slice_sum(a, j, i);
+      pr[i] = v;
+      ss += v * v;
+    }
+    const float sp = rms_shrink(block_sum(ss, red), n, a.eps);
+    for (int i = tid; i < n; i += nt) {
+      float v = a.x[(size_t)j * a.x_stride + i] + pr[i] * sp * a.w_res[i];
+      if (a.gain != 1.0f) v *= a.gain;
+      y[i] = v;
+      a.x_out[(size_t)j * a.x_stride + i] = v;
+    }
+  }
+  if (a.mode == LS_NORM || a.mode == LS_RESID_NORM) {
+    __syncthreads();
+    float ss = 0.0f;
+    for (int i = tid; i < n; i += nt) ss += y[i] * y[i];
+    const float sh = rms_shrink(block_sum(ss, red), n, a.eps);
+    for (int i = tid; i < n; i += nt) y[i] = y[i] * sh * a.w_in[i];
+  }
+  __syncthreads();
+  float mx = 0.0f;
+  for (int i = tid; i < n; i += nt) mx = fmaxf(mx, fabsf(y[i]));
+  const float sc = lane_scale(block_max(mx, red));
+  if (tid == 0) a.factor[j] = a.out_scale / sc;
+  // f16 pieces of eight columns into the operand block of (lane tile, step)
+  const int mt = j / LG_M, r = j % LG_M, pieces = a.n_cc * 8;
+  uint8_t *dst = reinterpret_cast<uint8_t *>(a.a_tiles);
+  for (int p = tid; p < pieces; p += nt) {
+    const int c0 = p * 8, cc = p >> 3, pj = p & 7;
+    uint32_t w[4];
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float v0 = c0 + 2 * h < n ? y[c0 + 2 * h] * sc : 0.0f;
+      const float v1 = c0 + 2 * h + 1 < n ? y[c0 + 2 * h + 1] * sc : 0.0f;
+      __half2 hv = __floats2half2_rn(v0, v1);
+      w[h] = *reinterpret_cast<uint32_t *>(&hv);
+    }
+    *reinterpret_cast<uint4 *>(dst + ((size_t)mt * a.n_cc + cc) * LG_A_BYTES + lg_swz(r, pj)) =
+        make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+// K-slice partials added in order: out[j][i] = sum_z p[z][j][i].
+__global__ void lane_sum_kernel(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
+                                int out_stride) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)lanes * cols) return;
+  const int j = (int)(idx / cols), i = (int)(idx - (long)j * cols);
+  float s = 0.0f;
+  for (int z = 0; z < splits; ++z) s += p[((size_t)z * lanes + j) * p_stride + i];
+  out[(size_t)j * out_stride + i] = s;
+}
+
+}  // namespace igc
+
+using namespace igc;
+
+extern "C" {
+
+size_t igc_lane_stage_smem(int mode, int cols) {
+  return sizeof(float) * (size_t)cols * ((mode == LS_RESID || mode == LS_RESID_NORM) ? 2 : 1);
+}
+
+cudaError_t igc_launch_lane_stage(const LaneStageArgs *a, cudaStream_t st) {
+  if (a->lanes < 1 || a->cols < 1 || a->cols > a->n_cc * 64) return cudaErrorInvalidValue;
+  const size_t smem = igc_lane_stage_smem(a->mode, a->cols);
+  if (smem > 200 * 1024) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(lane_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  lane_stage_kernel<<<a->lanes, 256, smem, st>>>(*a);
+  return cudaGetLastError();
+}
+
+int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count) {
+  const int tiles = ((n_rb + LG_RB - 1) / LG_RB) * ((lanes + LG_M - 1) / LG_M);
+  int split = 1;
+  while (split < 16 && tiles * split * 2 <= sm_count && n_cc / (split * 2) >= 2) split *= 2;
+  return split;
+}
+
+cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
+  if (a->lanes < 1 || a->split < 1 || a->split > a->n_cc || a->n_rb < 1) return cudaErrorInvalidValue;
+  cudaError_t e = cudaFuncSetAttribute(lane_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LG_SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
+  lane_gemm_kernel<<<grid, LG_THREADS, LG_SMEM, st>>>(*a);
+  return cudaGetLastError();
+}
+
+cudaError_t igc_launch_lane_sum(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
+                                int out_stride, cudaStream_t st) {
+  const long n = (long)lanes * cols;
+  lane_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, splits, lanes, cols, p_stride, out, out_stride);
+  return cudaGetLastError();
+}
+
+}  // extern "C"

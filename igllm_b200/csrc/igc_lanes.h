@@ -1,0 +1,64 @@
+// igc_lanes.h - the batched-lane path (igc_lanes.cu): row-wise stages and the
+// tcgen05 int4 GEMM for chunks of many lanes.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace igc {
+
+constexpr int LG_M = 128;  // lanes a tile (tensor-memory lanes)
+constexpr int LG_N = 256;  // weight rows a tile (tensor-memory columns)
+
+// What a stage computes for its lane before staging it (app_core.c:11637-11743).
+enum : int {
+  LS_PLAIN = 0,       // y = x
+  LS_NORM = 1,        // y = norm(x) * w_in
+  LS_RESID = 2,       // x_out = (x + norm(p) * w_res) * gain; y = x_out
+  LS_RESID_NORM = 3,  // the same, then y = norm(x_out) * w_in
+  LS_GELU_PAIR = 4,   // y = gelu(gate) * up, p the pair plane's rows (16-row blocks of gate, then up)
+  LS_GELU_MUL = 5     // y = gelu(p) * aux
+};
+
+struct LaneStageArgs {
+  int mode, lanes, cols;  // cols: the staged row's length (the next product's input columns)
+  const float *x;         // [lanes][x_stride]: the input (PLAIN, NORM) or residual stream (RESID*)
+  int x_stride;
+  const float *p;         // [p_splits][lanes][p_stride]: the producer's K-slice partials
+  int p_stride, p_splits;
+  const float *w_res;
+  float gain;
+  const float *w_in;
+  float eps;
+  float *x_out;           // RESID*: the new residual stream, same layout as x
+  const float *aux;       // GELU_MUL: [lanes][aux_stride]
+  int aux_stride;
+  float out_scale;        // folded into the lane's factor
+  void *a_tiles;          // out: [lane tile][n_cc][16 KB] f16 operand blocks
+  int n_cc;               // 64-column steps of the next product
+  float *factor;          // out: [lanes] the factor undoing the staging scale (times out_scale)
+};
+
+struct LaneGemmArgs {
+  const uint4 *tiles;     // the plane, as the upload repack lays it out
+  const uint2 *scales;
+  int n_rb, n_cc;
+  const uint4 *a_tiles;   // staged activations (LaneStageArgs::a_tiles)
+  const float *factor;    // [lanes]
+  float *out;             // [split][lanes][out_stride] partial sums, plane row order
+  int lanes, out_stride, split;
+  int *err;               // set nonzero when a wait gave up
+};
+
+}  // namespace igc
+
+extern "C" {
+size_t igc_lane_stage_smem(int mode, int cols);
+cudaError_t igc_launch_lane_stage(const igc::LaneStageArgs *a, cudaStream_t st);
+// K slices that keep about one wave of the SMs busy for this product.
+int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count);
+cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, cudaStream_t st);
+cudaError_t igc_launch_lane_sum(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
+                                int out_stride, cudaStream_t st);
+}

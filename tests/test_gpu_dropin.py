@@ -44,7 +44,9 @@ def test_reference_pass_through_the_cuda_desk(igo_mod, igc_lib, which, tiny_dir,
     a.prime(ids)
     b.prime(ids)
     worst = _check(b.step(ids[-1]), a.step(ids[-1]))
-    for k in (1, 4, 9):
+    # blocks up to the reference's own limit (session_guess_limit: the
+    # narrowest sliding window, 8 on the tiny shape)
+    for k in ((1, 4, 7) if which == "tiny" else (1, 4, 9)):
         blk = rng.integers(0, cfg["vocab"], k).astype(np.int32)
         worst = max(worst, _check(b.guess(blk), a.guess(blk)))
         assert a.keep(min(k, 3)) == b.keep(min(k, 3)) == 0

@@ -1,0 +1,58 @@
+"""The batched-lane path (igc_lanes.cu) on the GPU: the tcgen05 int4 GEMM.
+
+A product of 64 or more lanes through the backend table's mat_mat runs as the
+tcgen05 GEMM: staged f16 activations and (code - 8) * scale f16 weights in
+shared memory, tcgen05.mma with f32 accumulators in tensor memory, K slices
+added in a fixed order.  Checked against the CPU checker's igo_mat_mat (the
+restatement of app_core.c:3688 kern_row_code, fp32).  Tolerance: the f16
+rounding of weights and activations keeps the result within 4e-3 of the
+largest output magnitude (measured about 1e-3); the logits the verify round
+is held to allow 2e-2 absolute.
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REL = 4e-3
+
+
+def _plane(igc_lib, rng, rows, cols):
+    code = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+    sc16 = np.abs(rng.normal(0, 0.02, (rows, cols // 32))).astype(np.float16)
+    plane = igc_lib.IgcPlane(form=2, row_count=rows, col_count=cols, code_data=code.ctypes.data,
+                             row_stride=cols // 2, gain_data=sc16.ctypes.data, gain_type=2, bit_count=4,
+                             code_bias=8, code_flip=0, group_size=32, group_count=cols // 32)
+    return plane, code, sc16
+
+
+@pytest.mark.parametrize("rows,cols,lanes", [
+    (37, 96, 200),      # one partial row tile, a partial last column step, a partial second lane tile
+    (300, 1536, 64),    # the fewest lanes the path takes
+    (2560, 1536, 256),  # q|k|v of the E2B shape, two full lane tiles
+    (1536, 6144, 130),  # the down projection: eight K slices
+    (256, 1536, 512),   # the per-layer-embedding gate: one row tile, four lane tiles
+])
+def test_lane_gemm_matches_the_checker(igc_lib, igo_mod, rows, cols, lanes):
+    rng = np.random.default_rng(rows + cols + lanes)
+    plane, code, sc16 = _plane(igc_lib, rng, rows, cols)
+    act = rng.normal(0, 1, (lanes, cols)).astype(np.float32)
+    act[3] *= 1000.0  # lanes of very different magnitude each take their own staging scale
+    act[5] *= 1e-3
+    desk = igc_lib.Desk(0)
+    try:
+        got = desk.mat_mat(plane, act, lanes, rows)
+        again = desk.mat_mat(plane, act, lanes, rows)
+    finally:
+        desk.close()
+    lib = igo_mod.igo_lib()
+    op = igo_mod.make_plane(code, sc16.astype(np.float32))
+    want = np.zeros((lanes, rows), np.float32)
+    lib.igo_mat_mat(ctypes.byref(op), igo_mod.fptr(act), cols, lanes, igo_mod.fptr(want), rows, 8)
+    assert np.array_equal(got, again)  # fixed-order sums: the same bits every call
+    for j in range(lanes):  # each lane against its own magnitude
+        err = float(np.abs(got[j] - want[j]).max())
+        assert err <= REL * max(1e-30, float(np.abs(want[j]).max())), (j, err)
