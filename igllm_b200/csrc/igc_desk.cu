@@ -292,7 +292,7 @@ extern "C" int igc_back_open(igc_desk *desk, int device) {
   if (cudaDeviceGetAttribute(&s->sm_count, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
       cudaDeviceGetAttribute(&s->smem_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) != cudaSuccess ||
       cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess ||
-      igc_kernels_configure(227 * 1024) != cudaSuccess ||
+      igc_kernels_configure(227 * 1024) != cudaSuccess || igc_lanes_configure() != cudaSuccess ||
       cudaMalloc(&s->arg_val, (size_t)s->sm_count * 4 * 16 * 4) != cudaSuccess ||
       cudaMalloc(&s->arg_idx, (size_t)s->sm_count * 4 * 16 * 4) != cudaSuccess ||
       cudaMalloc(&s->err, sizeof(int)) != cudaSuccess || cudaMemset(s->err, 0, sizeof(int)) != cudaSuccess) {

@@ -423,13 +423,31 @@ size_t igc_lane_stage_smem(int mode, int cols) {
   return sizeof(float) * (size_t)cols * ((mode == LS_RESID || mode == LS_RESID_NORM) ? 2 : 1);
 }
 
+constexpr int LS_SMEM_LIMIT = 160 * 1024;  // a stage row (and a residual's partner row) in shared memory
+
+cudaError_t igc_lanes_configure(void) {
+  cudaError_t e = cudaFuncSetAttribute(lane_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LS_SMEM_LIMIT);
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(lane_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LG_SMEM);
+  return e;
+}
+
 cudaError_t igc_launch_lane_stage(const LaneStageArgs *a, cudaStream_t st) {
   if (a->lanes < 1 || a->cols < 1 || a->cols > a->n_cc * 64) return cudaErrorInvalidValue;
   const size_t smem = igc_lane_stage_smem(a->mode, a->cols);
-  if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(lane_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
+  if (smem > LS_SMEM_LIMIT) return cudaErrorInvalidValue;
   lane_stage_kernel<<<a->lanes, 256, smem, st>>>(*a);
+  return cudaGetLastError();
+}
+
+// Positions of a prefill chunk's 16-lane attention groups: out[i] = p0 + 16 i.
+__global__ void lane_positions_kernel(const int *p0, int groups, int *out) {
+  const int i = threadIdx.x;
+  if (i < groups) out[i] = *p0 + 16 * i;
+}
+
+cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st) {
+  if (groups < 1 || groups > 1024) return cudaErrorInvalidValue;
+  lane_positions_kernel<<<1, 1024, 0, st>>>(p0, groups, out);
   return cudaGetLastError();
 }
 
@@ -442,8 +460,6 @@ int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count) {
 
 cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
   if (a->lanes < 1 || a->split < 1 || a->split > a->n_cc || a->n_rb < 1) return cudaErrorInvalidValue;
-  cudaError_t e = cudaFuncSetAttribute(lane_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LG_SMEM);
-  if (e != cudaSuccess) return e;
   dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
   lane_gemm_kernel<<<grid, LG_THREADS, LG_SMEM, st>>>(*a);
   return cudaGetLastError();

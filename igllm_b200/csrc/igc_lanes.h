@@ -54,11 +54,15 @@ struct LaneGemmArgs {
 }  // namespace igc
 
 extern "C" {
+// Lets the stage and GEMM kernels take their shared memory (once per device).
+cudaError_t igc_lanes_configure(void);
 size_t igc_lane_stage_smem(int mode, int cols);
 cudaError_t igc_launch_lane_stage(const igc::LaneStageArgs *a, cudaStream_t st);
 // K slices that keep about one wave of the SMs busy for this product.
 int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count);
 cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, cudaStream_t st);
+// out[i] = *p0 + 16 i for i < groups (a prefill chunk's attention groups).
+cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st);
 cudaError_t igc_launch_lane_sum(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride, cudaStream_t st);
 }

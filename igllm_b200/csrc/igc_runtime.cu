@@ -31,6 +31,7 @@
 #include "../../include/igllm_cuda.h"
 #include "igc_json.h"
 #include "igc_kernels.h"
+#include "igc_lanes.h"
 #include "igc_synth.h"
 
 using namespace igc;
@@ -719,6 +720,7 @@ static int model_prepare(igc_model *m, const igc_setup *setup) {
   CK(cudaDeviceGetAttribute(&m->smem_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
   m->smem_limit -= 2048;  // the largest static part any kernel of igc_kernels.cu carries
   CK(igc_kernels_configure(m->smem_limit + 2048));
+  CK(igc_lanes_configure());
   return IGC_OKAY;
 }
 
@@ -803,6 +805,8 @@ struct igc_session {
   int use_graphs = 1;
   int use_pdl = 1;
   int use_stamps = 1;  // IGC_NO_STAMPS=1 launches without launch stamps (for comparison)
+  int use_chunks = 1;  // IGC_NO_CHUNKS=1 primes in 16-lane passes only
+  std::map<int, long> kernels_per_chunk;
   int head_parts = 0;  // argmax partials the output head's launch left
   cudaGraphExec_t graph[IGC_LANE_LIMIT + 1][2] = {};
   double serve_seconds = 0.0;
@@ -828,12 +832,27 @@ struct igc_session {
     int cls;
     double bytes;
   };
+  // the batched-lane prime (igc_lanes.cu): buffers for chunks of up to
+  // `cap` lanes, allocated on the first prime that uses them, and a captured
+  // graph per chunk length
+  struct Chunks {
+    int cap = 0;
+    int32_t *d_ids = nullptr;  // [0] position, [1..cap] ids
+    int *d_pos = nullptr;      // the 16-lane attention groups' positions
+    float *x0 = nullptr, *xa = nullptr, *xb = nullptr, *seed = nullptr, *ple_raw = nullptr, *ple = nullptr;
+    float *qkv = nullptr, *attn = nullptr, *part = nullptr, *factor = nullptr;
+    void *a_tiles = nullptr;
+    int32_t *h_ids = nullptr;  // pinned
+    std::map<int, cudaGraphExec_t> graph;
+  } ch;
   int stamp_n = 0;                     // launches stamped in the pass being enqueued
   std::vector<StampMeta> stamp_build;  // their classes and weight bytes
   std::vector<StampMeta> stamp_meta[IGC_LANE_LIMIT + 1];  // of the pass with a head, per lane count
 
   ~igc_session() {
     cudaSetDevice(m->device);
+    for (auto &kv : ch.graph) cudaGraphExecDestroy(kv.second);
+    if (ch.h_ids) cudaFreeHost(ch.h_ids);
     for (auto &mk : marks) cudaEventDestroy(mk.ev);
     for (int k = 0; k <= IGC_LANE_LIMIT; ++k)
       for (int w = 0; w < 2; ++w)
@@ -931,6 +950,8 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   s->use_pdl = !(np && np[0] == '1');
   const char *ns = getenv("IGC_NO_STAMPS");
   s->use_stamps = !(ns && ns[0] == '1');
+  const char *nc = getenv("IGC_NO_CHUNKS");
+  s->use_chunks = !(nc && nc[0] == '1');
   // attention clusters of 16 blocks (half the tiles a block of 8 takes)
   // unless IGC_ATTN_CLUSTER=8 or the heads' magnitude partials would not fit
   const char *ac = getenv("IGC_ATTN_CLUSTER");
@@ -1281,18 +1302,288 @@ static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
   return IGC_OKAY;
 }
 
+// ---------------------------------------------------------------------------
+// the batched-lane prime: chunks of up to IGC_CHUNK_LANES lanes, every
+// projection a tcgen05 GEMM (igc_lanes.cu), attention in 16-lane groups in
+// position order (each group writes its keys and values to the cache before
+// the next group reads them)
+
+constexpr int IGC_CHUNK_LANES = 256;  // lanes a chunk
+constexpr int IGC_CHUNK_MIN = 64;     // fewer lanes than this run as 16-lane passes
+
+static int chunks_ready(igc_session *s) {
+  auto &C = s->ch;
+  if (C.cap) return IGC_OKAY;
+  igc_model *m = s->m;
+  const int M = IGC_CHUNK_LANES, H = m->hidden, PS = m->layers * m->ple_dim;
+  // the largest K-slice partials any product of any chunk length leaves
+  size_t part = 0;
+  int max_cc = 1;
+  auto see = [&](const DevPlane &pl) {
+    if (!pl.tiles) return;
+    for (int lanes = IGC_CHUNK_MIN; lanes <= M; ++lanes)
+      part = std::max(part, (size_t)igc_lane_gemm_split(lanes, pl.n_rb, pl.n_cc, m->sm_count) * lanes * pl.n_rb * 16);
+    max_cc = std::max(max_cc, pl.n_cc);
+  };
+  see(m->ple_lift);
+  for (auto &L : m->layer) {
+    see(L.qkv);
+    see(L.o);
+    see(L.gateup);
+    see(L.down);
+    see(L.ple_gate);
+    see(L.ple_proj);
+  }
+  int c = IGC_OKAY;
+  if (c == IGC_OKAY) c = s->alloc(&C.d_ids, 1 + M);
+  if (c == IGC_OKAY) c = s->alloc(&C.d_pos, M / 16 + 1);
+  if (c == IGC_OKAY) c = s->alloc(&C.x0, (size_t)M * H);
+  if (c == IGC_OKAY) c = s->alloc(&C.xa, (size_t)M * H);
+  if (c == IGC_OKAY) c = s->alloc(&C.xb, (size_t)M * H);
+  if (c == IGC_OKAY) c = s->alloc(&C.seed, (size_t)M * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = s->alloc(&C.ple_raw, (size_t)M * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = s->alloc(&C.ple, (size_t)M * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = s->alloc(&C.qkv, (size_t)M * m->max_qkv);
+  if (c == IGC_OKAY) c = s->alloc(&C.attn, (size_t)M * m->max_q);
+  if (c == IGC_OKAY) c = s->alloc(&C.part, part);
+  if (c == IGC_OKAY) c = s->alloc(&C.factor, (size_t)M);
+  if (c == IGC_OKAY) c = s->alloc((uint8_t **)&C.a_tiles, (size_t)((M + LG_M - 1) / LG_M) * max_cc * LG_M * 64 * 2);
+  if (c != IGC_OKAY) return c;
+  CK(cudaMallocHost(&C.h_ids, sizeof(int32_t) * (1 + M)));
+  C.cap = M;
+  return IGC_OKAY;
+}
+
+// One stage into the chunk's operand blocks for the product `pl` (its
+// columns and steps), then the product's K-slice partials into `part`.
+static int chunk_product(igc_session *s, const DevPlane &pl, int M, LaneStageArgs sa, int *split_out) {
+  auto &C = s->ch;
+  sa.lanes = M;
+  sa.cols = pl.cols;
+  sa.n_cc = pl.n_cc;
+  sa.a_tiles = C.a_tiles;
+  sa.factor = C.factor;
+  sa.eps = s->m->eps;
+  CKL(igc_launch_lane_stage(&sa, s->st));
+  LaneGemmArgs ga;
+  memset(&ga, 0, sizeof(ga));
+  ga.tiles = pl.tiles;
+  ga.scales = pl.scales;
+  ga.n_rb = pl.n_rb;
+  ga.n_cc = pl.n_cc;
+  ga.a_tiles = reinterpret_cast<const uint4 *>(C.a_tiles);
+  ga.factor = C.factor;
+  ga.out = C.part;
+  ga.lanes = M;
+  ga.out_stride = pl.n_rb * 16;
+  ga.split = igc_lane_gemm_split(M, pl.n_rb, pl.n_cc, s->m->sm_count);
+  ga.err = s->d_err;
+  CKL(igc_launch_lane_gemm(&ga, s->st));
+  *split_out = ga.split;
+  return IGC_OKAY;
+}
+
+static LaneStageArgs stage_of(int mode, const float *x, int x_stride) {
+  LaneStageArgs a;
+  memset(&a, 0, sizeof(a));
+  a.mode = mode;
+  a.x = x;
+  a.x_stride = x_stride;
+  a.gain = 1.0f;
+  a.out_scale = 1.0f;
+  return a;
+}
+
+// One chunk of M lanes at the position in ch.d_ids[0], ids in ch.d_ids[1..M]
+// (app_core.c:11843 session_pass without the head: a prime keeps no logits).
+static int enqueue_chunk(igc_session *s, int M) {
+  igc_model *m = s->m;
+  auto &C = s->ch;
+  PdlScope pdl(false);
+  const int H = m->hidden, PS = m->layers * m->ple_dim, groups = (M + 15) / 16;
+  const int *d_p0 = C.d_ids;
+  int c, split = 1;
+  CKL(igc_launch_lane_positions(d_p0, groups, C.d_pos, s->st));
+  CKL(igc_launch_embed(C.d_ids + 1, M, m->embed, H, (float)sqrt((double)H), m->ple_embed,
+                       m->ple_vocab ? m->ple_vocab : 1, PS, (float)sqrt((double)m->ple_dim), C.x0, C.seed, nullptr, 0,
+                       s->st));
+  if (m->ple_dim > 0) {
+    LaneStageArgs sa = stage_of(LS_PLAIN, C.x0, H);
+    sa.out_scale = (float)(1.0 / sqrt((double)H));
+    c = chunk_product(s, m->ple_lift, M, sa, &split);
+    if (c != IGC_OKAY) return c;
+    CKL(igc_launch_lane_sum(C.part, split, M, PS, m->ple_lift.n_rb * 16, C.ple_raw, PS, s->st));
+    CKL(igc_launch_ple_finish(C.ple_raw, C.seed, M, m->layers, m->ple_dim, m->ple_norm, m->eps,
+                              (float)(1.0 / sqrt(2.0)), C.ple, s->st));
+  }
+  // the residual stream ping-pongs between xa and xb; `pend` (in C.part,
+  // `pend_split` slices of `pend_stride`) is the last block's output still
+  // to be normed and added (with its gain) by the next stage
+  float *cur = C.x0;
+  float *bufs[2] = {C.xa, C.xb};
+  int flip = 0;
+  auto next_x = [&]() -> float * { float *o = bufs[flip]; flip ^= 1; return o; };
+  bool pend = false;
+  int pend_split = 1, pend_stride = 0;
+  const float *pend_w = nullptr;
+  float pend_gain = 1.0f;
+  for (int l = 0; l < m->layers; ++l) {
+    const DevLayer &L = m->layer[l];
+    // q|k|v
+    {
+      LaneStageArgs sa = stage_of(pend ? LS_RESID_NORM : LS_NORM, cur, H);
+      sa.w_in = L.enter_norm;
+      if (pend) {
+        float *xo = next_x();
+        sa.p = C.part;
+        sa.p_splits = pend_split;
+        sa.p_stride = pend_stride;
+        sa.w_res = pend_w;
+        sa.gain = pend_gain;
+        sa.x_out = xo;
+        cur = xo;
+      }
+      c = chunk_product(s, L.qkv, M, sa, &split);
+      if (c != IGC_OKAY) return c;
+      CKL(igc_launch_lane_sum(C.part, split, M, L.qkv_rows, L.qkv.n_rb * 16, C.qkv, L.qkv_rows, s->st));
+    }
+    // attention, 16 lanes at a time in position order
+    const int owner = L.share ? L.source : l;
+    const DevLayer &O = m->layer[owner];
+    for (int gi = 0; gi < groups; ++gi) {
+      const int j0 = gi * 16, n = M - j0 < 16 ? M - j0 : 16;
+      CKL(igc_launch_attn(C.qkv + (size_t)j0 * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
+                          m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner],
+                          L.kind == 0 ? 1 : 0, m->slide_span, C.d_pos + gi, n, s->attn_cluster,
+                          C.attn + (size_t)j0 * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
+    }
+    // o
+    c = chunk_product(s, L.o, M, stage_of(LS_PLAIN, C.attn, L.q_rows), &split);
+    if (c != IGC_OKAY) return c;
+    // gate|up: x += norm(o) * w, then norm(x) * w
+    {
+      LaneStageArgs sa = stage_of(LS_RESID_NORM, cur, H);
+      float *xo = next_x();
+      sa.p = C.part;
+      sa.p_splits = split;
+      sa.p_stride = L.o.n_rb * 16;
+      sa.w_res = L.after_attn_norm;
+      sa.w_in = L.before_feed_norm;
+      sa.x_out = xo;
+      cur = xo;
+      c = chunk_product(s, L.gateup, M, sa, &split);
+      if (c != IGC_OKAY) return c;
+    }
+    // down: gelu(gate) * up
+    {
+      LaneStageArgs sa = stage_of(LS_GELU_PAIR, nullptr, 0);
+      sa.p = C.part;
+      sa.p_splits = split;
+      sa.p_stride = L.gateup.n_rb * 16;
+      c = chunk_product(s, L.down, M, sa, &split);
+      if (c != IGC_OKAY) return c;
+    }
+    if (m->ple_dim > 0) {
+      // per-layer-embedding gate: x += norm(down) * w
+      LaneStageArgs sa = stage_of(LS_RESID, cur, H);
+      float *xo = next_x();
+      sa.p = C.part;
+      sa.p_splits = split;
+      sa.p_stride = L.down.n_rb * 16;
+      sa.w_res = L.after_feed_norm;
+      sa.x_out = xo;
+      cur = xo;
+      c = chunk_product(s, L.ple_gate, M, sa, &split);
+      if (c != IGC_OKAY) return c;
+      // its projection: gelu(gate) * the layer's per-layer input
+      LaneStageArgs sb = stage_of(LS_GELU_MUL, nullptr, 0);
+      sb.p = C.part;
+      sb.p_splits = split;
+      sb.p_stride = L.ple_gate.n_rb * 16;
+      sb.aux = C.ple + (size_t)l * m->ple_dim;
+      sb.aux_stride = PS;
+      c = chunk_product(s, L.ple_proj, M, sb, &split);
+      if (c != IGC_OKAY) return c;
+      pend_stride = L.ple_proj.n_rb * 16;
+      pend_w = L.after_ple_norm;
+    } else {
+      pend_stride = L.down.n_rb * 16;
+      pend_w = L.after_feed_norm;
+    }
+    pend = true;
+    pend_split = split;
+    pend_gain = L.gain;
+  }
+  return IGC_OKAY;
+}
+
+// One chunk of M lanes (64 <= M <= IGC_CHUNK_LANES), kept, with a captured
+// graph per chunk length.
+static int run_chunk(igc_session *s, const int32_t *ids, int M) {
+  igc_model *m = s->m;
+  auto &C = s->ch;
+  int c = chunks_ready(s);
+  if (c != IGC_OKAY) return c;
+  clear_stale("prime chunk");
+  CK(cudaSetDevice(m->device));
+  C.h_ids[0] = s->fill;
+  memcpy(C.h_ids + 1, ids, sizeof(int32_t) * (size_t)M);
+  CK(cudaMemcpyAsync(C.d_ids, C.h_ids, sizeof(int32_t) * (size_t)(1 + M), cudaMemcpyHostToDevice, s->st));
+  if (s->use_graphs) {
+    auto it = C.graph.find(M);
+    if (it == C.graph.end()) {
+      cudaGraph_t g;
+      long before = g_launches;
+      CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+      c = enqueue_chunk(s, M);
+      cudaError_t e = cudaStreamEndCapture(s->st, &g);
+      if (c != IGC_OKAY) return c;
+      if (e != cudaSuccess) return fail_device(e, "capture");
+      cudaGraphExec_t ex;
+      e = cudaGraphInstantiate(&ex, g, 0);
+      cudaGraphDestroy(g);
+      if (e != cudaSuccess) return fail_device(e, "graph instantiate");
+      it = C.graph.emplace(M, ex).first;
+      s->kernels_per_chunk[M] = g_launches - before;
+      g_launches = before;
+    }
+    CK(cudaGraphLaunch(it->second, s->st));
+    g_launches += s->kernels_per_chunk[M];
+  } else {
+    c = enqueue_chunk(s, M);
+    if (c != IGC_OKAY) return c;
+  }
+  CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * (IGC_LANE_LIMIT + 1), cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  if (int ce = check_err(s)) return ce;
+  s->fill += M;
+  for (int j = 0; j < M; ++j)
+    if ((int)s->echo.size() < m->window_limit) s->echo.push_back(ids[j]);
+  s->logit_lanes = 0;
+  return IGC_OKAY;
+}
+
 extern "C" int igc_session_prime(igc_session *s, const int32_t *ids, int n) { /* app_core.c:14443 */
   if (!s || !ids || n < 1) return IGC_FAIL_ARGUMENT;
   if (s->guess_count > 0) return IGC_FAIL_STATE;
   if (s->fill + n > s->m->window_limit) return IGC_FAIL_STATE;
   for (int i = 0; i < n; ++i)
     if (ids[i] < 0 || ids[i] >= s->m->vocab) return IGC_FAIL_ARGUMENT;
+  // every id but the last (which the caller steps): chunks of many lanes
+  // through the tcgen05 path while at least IGC_CHUNK_MIN remain, then
+  // passes of at most 16 lanes (the reference's chunking, app_core.c:14443)
   for (int i = 0; i + 1 < n;) {
-    int lanes = n - 1 - i;
-    if (lanes > IGC_LANE_LIMIT) lanes = IGC_LANE_LIMIT;
-    int c = run_pass(s, ids + i, lanes, 0);
+    int left = n - 1 - i, c;
+    if (s->use_chunks && left >= IGC_CHUNK_MIN) {
+      const int lanes = left < IGC_CHUNK_LANES ? left : IGC_CHUNK_LANES;
+      c = run_chunk(s, ids + i, lanes);
+      i += lanes;
+    } else {
+      const int lanes = left > IGC_LANE_LIMIT ? IGC_LANE_LIMIT : left;
+      c = run_pass(s, ids + i, lanes, 0);
+      i += lanes;
+    }
     if (c != IGC_OKAY) return c;
-    i += lanes;
   }
   return IGC_OKAY;
 }

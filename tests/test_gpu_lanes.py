@@ -49,10 +49,43 @@ def test_lane_gemm_matches_the_checker(igc_lib, igo_mod, rows, cols, lanes):
     finally:
         desk.close()
     lib = igo_mod.igo_lib()
-    op = igo_mod.make_plane(code, sc16.astype(np.float32))
+    sc32 = sc16.astype(np.float32)  # kept alive: the plane holds its pointer
+    op = igo_mod.make_plane(code, sc32)
     want = np.zeros((lanes, rows), np.float32)
     lib.igo_mat_mat(ctypes.byref(op), igo_mod.fptr(act), cols, lanes, igo_mod.fptr(want), rows, 8)
     assert np.array_equal(got, again)  # fixed-order sums: the same bits every call
     for j in range(lanes):  # each lane against its own magnitude
         err = float(np.abs(got[j] - want[j]).max())
         assert err <= REL * max(1e-30, float(np.abs(want[j]).max())), (j, err)
+
+
+@pytest.mark.parametrize("which", ["tiny", "small", "wide"])
+def test_chunked_prime_matches_the_checker(igc_lib, igo_mod, which, tiny_dir, small_dir, wide_dir):
+    """A prompt of 64 or more ids primes in chunks of up to 256 lanes through
+    the tcgen05 path (every projection a lane GEMM, attention in 16-lane
+    groups in position order); what it leaves in the caches must give the
+    checker's logits on the step, the block and the step after a keep that
+    follow it, within 2e-2 (and 2e-3 of the row's magnitude)."""
+    from conftest import SMALL, TINY, WIDE
+    folder, cfg = {"tiny": (tiny_dir, TINY), "small": (small_dir, SMALL), "wide": (wide_dir, WIDE)}[which]
+    m = igc_lib.Model(folder=folder, window_limit=cfg["window_limit"])
+    om = igo_mod.OracleModel(folder, window_limit=cfg["window_limit"])
+    s, o = igc_lib.Session(m), igo_mod.OracleSession(om, threads=8)
+    rng = np.random.default_rng(31)
+    n = min(cfg["window_limit"] - 40, 300)  # a 256-lane chunk and the rest (tiny: one chunk of 215)
+    ids = rng.integers(0, cfg["vocab"], n).astype(np.int32)
+    s.prime(ids)
+    o.prime(ids)
+
+    def close(got, want):
+        err = float(np.abs(got - want).max())
+        assert err <= 2e-2 and err <= 2e-3 * max(1.0, float(np.abs(want).max())), err
+
+    top, row = s.step(ids[-1])
+    close(row, o.step(ids[-1]))
+    blk = np.array([top] + rng.integers(0, cfg["vocab"], 3).tolist(), np.int32)
+    close(s.guess(blk), o.guess(blk))
+    s.guess_keep(2)
+    o.guess_keep(2)
+    _, row = s.step(9)
+    close(row, o.step(9))
