@@ -396,6 +396,8 @@ def run_ours(args):
     prefill = {"tok_s": round((PREFILL_LEN - 1) / (t1 - t0), 1), "ttft_ms": round(1000 * (t2 - t0), 2),
                "prompt": f"{PREFILL_LEN} uniform ids, seed 1 (config 3), 16-lane passes"}
 
+    crowd = crowd_bench(ig, model) if not args.no_crowd else None
+
     # the projection kernels against the HBM roofline, from the timed
     # region's own graphed passes: every projection and attention launch
     # stamped its span (first block past its wait on the kernel ahead to the
@@ -439,6 +441,7 @@ def run_ours(args):
         "verify_round_us": per_k,
         "prefill": prefill,
         "ngram": {"tok_s": round(TOKENS / ngram_s, 1), "rounds": rounds_n, "guesses": drawn, "kept": kept},
+        "crowd": crowd,
         "roofline": {"bound": "hbm", "kernel": "int4 skinny GEMM (layer projections)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic,
@@ -466,6 +469,72 @@ def run_ours(args):
     if rank == 0:
         print(json.dumps(line), flush=True)
     ranks.close()
+
+
+CROWD_STREAMS = 64
+CROWD_TOKENS = 128
+
+
+def crowd_bench(ig, model):
+    """BASELINE config 4 on one GPU: 64 independent streams, each primed with
+    its own 1024-id prompt (built as config 0's, seeds 100..163), greedy
+    --guess 4 verify rounds of all 64 streams at once through igc_crowd_round
+    (256 lanes a weight sweep, the tcgen05 lane GEMM).  Blocks come from each
+    stream's own greedy continuation (the always-right proposer, found first
+    by one-lane crowd rounds), CROWD_TOKENS tokens a stream; the timed rounds
+    take host ids in and host ids out each round."""
+    sessions = [ig.Session(model) for _ in range(CROWD_STREAMS)]
+    prompts = [make_prompt(100 + i) for i in range(CROWD_STREAMS)]
+    t0 = time.perf_counter()
+    for s_, p_ in zip(sessions, prompts):
+        s_.prime(p_)
+    prime_s = time.perf_counter() - t0
+    base = [s_.fill for s_ in sessions]
+    last = np.array([p_[-1] for p_ in prompts], np.int32)
+    # each stream's greedy continuation, one lane a stream a round
+    one = ig.Crowd(model, CROWD_STREAMS, 1)
+    cont = np.zeros((CROWD_STREAMS, CROWD_TOKENS + GUESS), np.int32)
+    cur = last.copy()
+    for t in range(CROWD_TOKENS + GUESS):
+        _, made, _ = one.round(sessions, cur.reshape(-1, 1))
+        cont[:, t] = made
+        cur = made
+    one.close()
+    for s_, b_ in zip(sessions, base):
+        s_.hold(b_)
+    crowd = ig.Crowd(model, CROWD_STREAMS, GUESS)
+    seqs = np.concatenate([last[:, None], cont], axis=1)  # seqs[:, i] is the id at base + i
+
+    def generation():
+        done = np.zeros(CROWD_STREAMS, np.int64)
+        rounds = 0
+        while done.min() < CROWD_TOKENS:
+            blocks = np.stack([seqs[j, done[j]: done[j] + GUESS] for j in range(CROWD_STREAMS)])
+            take, made, _ = crowd.round(sessions, blocks)
+            done += take + 1
+            rounds += 1
+        return int(done.sum()), rounds
+
+    generation()  # captures the round's graph
+    for s_, b_ in zip(sessions, base):
+        s_.hold(b_)
+    t0 = time.perf_counter()
+    tokens, rounds = generation()
+    wall = time.perf_counter() - t0
+    crowd.close()
+    for s_ in sessions:
+        s_.close()
+    flops = 2.0 * CROWD_STREAMS * GUESS * model.linear_params() * rounds
+    tflops = flops / wall / 1e12
+    return {"streams": CROWD_STREAMS, "k": GUESS, "tokens_per_stream": CROWD_TOKENS,
+            "tok_s": round(tokens / wall, 1), "round_ms": round(1000 * wall / rounds, 3), "rounds": rounds,
+            "tokens": tokens, "prime_s_all": round(prime_s, 2),
+            "tensor": {"tflops": round(tflops, 1), "peak": 1388.0, "frac": round(tflops / 1388.0, 4),
+                       "peak_kind": "measured sustained bf16 (MEASURED_PEAKS.json bf16_tflops_sustained); "
+                                    "three f16 products a step (hi/lo split) counted once"},
+            "workload": "config 4 on one GPU: 64 streams x 1024-id prompts (seeds 100-163), greedy --guess 4, "
+                        f"{CROWD_TOKENS} tokens a stream, all streams in one crowd round; host ids in and out "
+                        "every round (wall clock)"}
 
 
 def run_profile_case(args):
@@ -501,6 +570,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the host-core reference baseline")
+    ap.add_argument("--no-crowd", action="store_true", help="skip the 64-stream crowd measurement")
     ap.add_argument("--profile-case", action="store_true",
                     help="run the small profiler case instead of the benchmark (no JSON line)")
     ap.add_argument("--case-vocab", type=int, default=32768)

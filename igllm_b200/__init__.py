@@ -125,6 +125,7 @@ def _lib():
         "igc_model_window_limit": (i, [vp]),
         "igc_model_decode_bytes": (ctypes.c_size_t, [vp]),
         "igc_model_device_bytes": (ctypes.c_size_t, [vp]),
+        "igc_model_weight_count": (ctypes.c_size_t, [vp]),
         "igc_session_open": (i, [vp, _P(vp)]),
         "igc_session_close": (None, [vp]),
         "igc_session_reset": (None, [vp]),
@@ -160,6 +161,9 @@ def _lib():
         "igc_last_error": (ctypes.c_char_p, []),
         "igc_launch_count": (ctypes.c_long, []),
         "igc_norm_rms_fixed": (i, [i, fp, fp, i, ctypes.c_float, fp]),
+        "igc_crowd_open": (i, [vp, i, i, _P(vp)]),
+        "igc_crowd_close": (None, [vp]),
+        "igc_crowd_round": (i, [vp, _P(vp), i, i32p, i32p, i32p, fp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -174,7 +178,7 @@ def exported_symbols():
     return [
         "igc_back_open", "igc_back_close", "igc_desk_status", "igc_model_load", "igc_model_free",
         "igc_model_vocab_count", "igc_model_layer_count", "igc_model_state_size",
-        "igc_model_window_limit", "igc_model_decode_bytes", "igc_model_device_bytes",
+        "igc_model_window_limit", "igc_model_decode_bytes", "igc_model_device_bytes", "igc_model_weight_count",
         "igc_session_open", "igc_session_close", "igc_session_reset", "igc_session_hold",
         "igc_session_prime", "igc_session_step", "igc_session_guess", "igc_session_guess_top",
         "igc_session_guess_keep", "igc_session_guess_taste", "igc_session_pick", "igc_session_fill",
@@ -184,6 +188,7 @@ def exported_symbols():
         "igc_scout_open", "igc_scout_close",
         "igc_scout_clear", "igc_scout_note", "igc_scout_span", "igc_scout_draw", "igc_synth_fill",
         "igc_synth_write", "igc_model_synth", "igc_last_error", "igc_launch_count", "igc_norm_rms_fixed",
+        "igc_crowd_open", "igc_crowd_close", "igc_crowd_round",
     ]
 
 
@@ -233,6 +238,10 @@ class Model:
 
     def device_bytes(self):
         return _lib().igc_model_device_bytes(self._h)
+
+    def linear_params(self):
+        """Weights of the int4 projections one lane multiplies (head included)."""
+        return _lib().igc_model_weight_count(self._h)
 
     def close(self):
         if self._h:
@@ -366,6 +375,49 @@ class Session:
 
     def serve_tokens(self):
         return _lib().igc_session_serve_tokens(self._h)
+
+
+CROWD_LANE_LIMIT = 512  # include/igllm_cuda.h IGC_CROWD_LANE_LIMIT
+
+
+class Crowd:
+    """igc_crowd: one greedy verify round for many sessions of one model in
+    one pass (the lanes of every session's block share each weight sweep)."""
+
+    def __init__(self, model, session_limit, lanes_per_session):
+        self.model = model
+        self.k = int(lanes_per_session)
+        self.limit = int(session_limit)
+        self._h = ctypes.c_void_p()
+        _check(_lib().igc_crowd_open(model._h, self.limit, self.k, ctypes.byref(self._h)), "crowd_open")
+
+    def close(self):
+        if self._h:
+            _lib().igc_crowd_close(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def round(self, sessions, blocks, want_logits=False):
+        """blocks: (len(sessions), k) ids.  Returns (takes, mades, logits or None)."""
+        n = len(sessions)
+        a, p = _ids(np.asarray(blocks, np.int32).reshape(-1))
+        if len(a) != n * self.k:
+            raise ValueError(f"crowd round: {len(a)} ids for {n} sessions of {self.k}")
+        hs = (ctypes.c_void_p * n)(*[s._h.value for s in sessions])
+        take = np.zeros(n, np.int32)
+        made = np.zeros(n, np.int32)
+        rows = np.empty((n * self.k, self.model.vocab), np.float32) if want_logits else None
+        rp = rows.ctypes.data_as(_f) if want_logits else None
+        c = _lib().igc_crowd_round(self._h, hs, n, p, take.ctypes.data_as(_P(ctypes.c_int32)),
+                                   made.ctypes.data_as(_P(ctypes.c_int32)), rp)
+        if c < 0:
+            raise IgcError(c, "crowd_round")
+        return take, made, rows
 
 
 class Scout:

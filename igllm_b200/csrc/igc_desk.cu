@@ -132,7 +132,7 @@ void desk_mat_mat_lanes(DeskState *s, const DeskPlane *p, const float *act, int 
   const int split = igc_lane_gemm_split(lanes, p->n_rb, p->n_cc, s->sm_count);
   if (!room(s, &s->lane_act, &s->lane_act_n, sizeof(float) * (size_t)lanes * p->cols) ||
       !room(s, &s->lane_factor, &s->lane_factor_n, sizeof(float) * (size_t)lanes) ||
-      !room(s, &s->lane_tiles, &s->lane_tiles_n, (size_t)m_tiles * p->n_cc * LG_M * 64 * 2) ||
+      !room(s, &s->lane_tiles, &s->lane_tiles_n, (size_t)m_tiles * p->n_cc * LG_A_STEP_BYTES) ||
       !room(s, &s->lane_part, &s->lane_part_n, sizeof(float) * (size_t)split * lanes * rows_pad) ||
       !room(s, &s->lane_out, &s->lane_out_n, sizeof(float) * (size_t)lanes * p->rows))
     return;

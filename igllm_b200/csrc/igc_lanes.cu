@@ -14,15 +14,16 @@
 //                       the lane scaled by a power of two and stored as f16
 //                       in the operand layout the tensor core reads (below),
 //                       with the factor that undoes the scale.
-//   lane_gemm_kernel    one block a (128-lane, 256-row) tile and K slice:
+//   lane_gemm_kernel    one block a (128-lane, 128-row) tile and K slice:
 //                       a producer warp bulk-copies the staged activations
 //                       and the packed int4 weights (with their f16 group
 //                       scales) of each 64-column step from this GPU's HBM
 //                       into a three-deep shared-memory ring; four warps turn
-//                       the codes into f16 weights, (code - 8) * scale, in
-//                       the operand layout; one thread issues the step's four
-//                       tcgen05.mma (M 128, N 256, K 16, f32 accumulate in
-//                       TMEM) and commits them to the ring slot's barrier; at
+//                       the codes into f16 hi/lo weights, (code - 8) * scale,
+//                       in the operand layout; one thread issues the step's
+//                       twelve tcgen05.mma (M 128, N 128, K 16, f32
+//                       accumulate in TMEM) and commits them to the ring
+//                       slot's barrier; at
 //                       the end the four warps read the accumulators back
 //                       with tcgen05.ld and store them, times each lane's
 //                       factor, as the slice's partial sums.
@@ -32,14 +33,18 @@
 // form a tcgen05 shared-memory descriptor names): a 64-column step of 128
 // rows is 16 KB, rows in groups of eight 128-byte rows (1 KB apart), and the
 // 16-byte piece j of row r sits at piece j ^ (r mod 8).  The staged
-// activations are stored in global memory already in this layout, one 16 KB
-// block per (128-lane tile, 64-column step), so one bulk copy moves a block.
+// activations are stored in global memory already in this layout, a hi and
+// a lo block per (128-lane tile, 64-column step), so bulk copies move them
+// as they are.
 //
-// Precision: the weights are (code - 8) * scale rounded once to f16 (the
-// scale's own f16 bits times a small integer), the activations f16 after the
-// power-of-two scaling, the sums f32 - within about 1e-3 of the fp32 product
-// relative to the row's magnitude, well inside the 2e-2 the verify round is
-// held to.  The decode path keeps the exact-weight mma.sync GEMM.
+// Precision: both operands are split into f16 hi and lo parts.  A weight
+// (code - 8) * scale is a 4-bit integer times an f16 scale, so hi + lo holds
+// it exactly; an activation (after the lane's power-of-two scaling) keeps
+// about 22 bits in hi + lo.  Each 16-column step is three products into the
+// same f32 accumulators, A_hi W_hi + A_lo W_hi + A_hi W_lo (the lo x lo term
+// is below f32's own rounding), so the result matches the fp32 product to
+// the accumulator's precision, as the decode path's hi/lo staging does.
+// Results of a lane depend only on that lane's row and the K slices.
 //
 // Every wait on a barrier gives up after a bounded number of polls and sets
 // the error word; the block then runs to its end and frees its tensor memory.
@@ -119,12 +124,16 @@ __host__ __device__ __forceinline__ uint32_t lg_swz(int r, int j) {
 // the GEMM
 
 constexpr int LG_STAGES = 3;
-constexpr int LG_A_BYTES = LG_M * 64 * 2;       // 16 KB
-constexpr int LG_B_BYTES = LG_N * 64 * 2;       // 32 KB
+constexpr int LG_OP_BYTES = 128 * 64 * 2;       // one operand block: 128 rows x 64 columns of f16, 16 KB
+constexpr int LG_A_BYTES = LG_OP_BYTES;         // activations, hi (then lo)
+constexpr int LG_B_BYTES = LG_OP_BYTES;         // weights, hi (then lo)
 constexpr int LG_RB = LG_N / 16;                // row blocks a tile
-constexpr int LG_CODE_BYTES = LG_RB * 512;      // 8 KB
-constexpr int LG_SCALE_BYTES = LG_RB * 64;      // 1 KB
-constexpr int LG_STAGE_BYTES = LG_A_BYTES + LG_B_BYTES + LG_CODE_BYTES + LG_SCALE_BYTES;  // 57 KB, 1 KB multiple
+constexpr int LG_CODE_BYTES = LG_RB * 512;      // 4 KB
+constexpr int LG_SCALE_BYTES = LG_RB * 64;      // 512 B
+// a ring slot: A hi, A lo, B hi, B lo, codes, scales; a 1 KB multiple
+constexpr int LG_OFF_B = 2 * LG_A_BYTES, LG_OFF_CODES = LG_OFF_B + 2 * LG_B_BYTES,
+              LG_OFF_SCALES = LG_OFF_CODES + LG_CODE_BYTES;
+constexpr int LG_STAGE_BYTES = (LG_OFF_SCALES + LG_SCALE_BYTES + 1023) / 1024 * 1024;  // 69 KB
 constexpr int LG_BAR_BYTES = 256;
 constexpr int LG_SMEM = 1024 + LG_STAGES * LG_STAGE_BYTES + LG_BAR_BYTES;  // + alignment slack
 constexpr int LG_THREADS = 192;
@@ -175,16 +184,16 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
       }
       uint8_t *st = base + s * LG_STAGE_BYTES;
       if (lane == 0)
-        mbar_expect(&full[s], (uint32_t)(LG_A_BYTES + rbv * (512 + 64)));
+        mbar_expect(&full[s], (uint32_t)(2 * LG_A_BYTES + rbv * (512 + 64)));
       __syncwarp();
-      if (lane == 0)
-        bulk_load(st, a.a_tiles + ((size_t)mt * a.n_cc + c) * (LG_A_BYTES / 16), LG_A_BYTES, &full[s],
-                  policy);
+      if (lane < 2) {  // the activations' hi and lo blocks of this step
+        const uint4 *src = a.a_tiles + (((size_t)mt * a.n_cc + c) * 2 + lane) * (LG_A_BYTES / 16);
+        bulk_load(st + lane * LG_A_BYTES, src, LG_A_BYTES, &full[s], policy);
+      }
       if (lane < rbv) {
         const size_t tile = (size_t)(rb0 + lane) * a.n_cc + c;
-        bulk_load(st + LG_A_BYTES + LG_B_BYTES + lane * 512, a.tiles + tile * 32, 512, &full[s], policy);
-        bulk_load(st + LG_A_BYTES + LG_B_BYTES + LG_CODE_BYTES + lane * 64, a.scales + tile * 8, 64, &full[s],
-                  policy);
+        bulk_load(st + LG_OFF_CODES + lane * 512, a.tiles + tile * 32, 512, &full[s], policy);
+        bulk_load(st + LG_OFF_SCALES + lane * 64, a.scales + tile * 8, 64, &full[s], policy);
       }
     }
   } else if (warp == 1) {
@@ -197,10 +206,15 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
       if (__any_sync(0xffffffffu, !ok)) failed = true;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t sa = smem_u32(base + s * LG_STAGE_BYTES), sb = sa + LG_A_BYTES;
+        const uint32_t ah = smem_u32(base + s * LG_STAGE_BYTES), al = ah + LG_A_BYTES;
+        const uint32_t bh = ah + LG_OFF_B, bl = bh + LG_B_BYTES;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          tc_mma(tmem, lg_desc(sa + kk * 32), lg_desc(sb + kk * 32), (k > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t o = kk * 32;  // 16 columns further along K inside the swizzled rows
+          tc_mma(tmem, lg_desc(ah + o), lg_desc(bh + o), (k > 0 || kk > 0) ? 1u : 0u);
+          tc_mma(tmem, lg_desc(al + o), lg_desc(bh + o), 1u);
+          tc_mma(tmem, lg_desc(ah + o), lg_desc(bl + o), 1u);
+        }
         tc_commit(&empty[s]);
       }
       __syncwarp();
@@ -216,49 +230,38 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
       const bool ok = mbar_wait(&full[s], ph, failed ? 1 : LG_TRIES);
       if (__any_sync(0xffffffffu, !ok)) failed = true;
       uint8_t *st = base + s * LG_STAGE_BYTES;
-      uint8_t *bt = st + LG_A_BYTES;
-      const uint4 *codes = reinterpret_cast<const uint4 *>(st + LG_A_BYTES + LG_B_BYTES);
-      const uint2 *scs = reinterpret_cast<const uint2 *>(st + LG_A_BYTES + LG_B_BYTES + LG_CODE_BYTES);
+      uint8_t *bh = st + LG_OFF_B, *bl = bh + LG_B_BYTES;
+      const uint4 *codes = reinterpret_cast<const uint4 *>(st + LG_OFF_CODES);
+      const uint2 *scs = reinterpret_cast<const uint2 *>(st + LG_OFF_SCALES);
+      // the slot was refilled only after the MMA of the step three back (which
+      // read these weight blocks) committed, and this warp waited on the refill
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 2; ++j) {
         const int slot = dt + 128 * j, rbl = slot >> 5, ts = slot & 31, g = ts >> 2, tq = ts & 3;
         const int n0 = rbl * 16 + g, n8 = n0 + 8;
-        uint32_t v[4][4];  // [kb][register]: rows g, g+8 x columns (c, c+1), (c+8, c+9)
-        if (rbl < rbv) {
-          const uint4 w = codes[rbl * 32 + ts];
-          const uint2 sc = scs[rbl * 8 + g];
-          const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int kb = 0; kb < 4; ++kb) {
-            uint32_t q[4];
-            dequant_i4(words[kb], q);
-            const uint32_t sg = kb < 2 ? sc.x : sc.y;  // f16 scales of rows g (low half) and g+8 (high half)
-            const __half2 s2 = *reinterpret_cast<const __half2 *>(&sg);
-            const __half2 s0 = __low2half2(s2), s8 = __high2half2(s2);
-            __half2 h;
-            h = __hmul2(*reinterpret_cast<__half2 *>(&q[0]), s0);
-            v[kb][0] = *reinterpret_cast<uint32_t *>(&h);
-            h = __hmul2(*reinterpret_cast<__half2 *>(&q[1]), s8);
-            v[kb][1] = *reinterpret_cast<uint32_t *>(&h);
-            h = __hmul2(*reinterpret_cast<__half2 *>(&q[2]), s0);
-            v[kb][2] = *reinterpret_cast<uint32_t *>(&h);
-            h = __hmul2(*reinterpret_cast<__half2 *>(&q[3]), s8);
-            v[kb][3] = *reinterpret_cast<uint32_t *>(&h);
-          }
-        } else {
-#pragma unroll
-          for (int kb = 0; kb < 4; ++kb) v[kb][0] = v[kb][1] = v[kb][2] = v[kb][3] = 0u;
-        }
-        // the slot's first k-iteration must not overwrite weights the MMA of
-        // the step three back still reads: the producer only refilled the
-        // slot after that MMA committed, and this warp waited on the refill
+        const bool have = rbl < rbv;
+        const uint4 w = have ? codes[rbl * 32 + ts] : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
+        const uint2 sc = have ? scs[rbl * 8 + g] : make_uint2(0u, 0u);
+        const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int kb = 0; kb < 4; ++kb) {
-          const int p0 = 2 * kb, p1 = 2 * kb + 1;  // 16-byte pieces of columns c and c + 8
-          *reinterpret_cast<uint32_t *>(bt + lg_swz(n0, p0) + 4 * tq) = v[kb][0];
-          *reinterpret_cast<uint32_t *>(bt + lg_swz(n8, p0) + 4 * tq) = v[kb][1];
-          *reinterpret_cast<uint32_t *>(bt + lg_swz(n0, p1) + 4 * tq) = v[kb][2];
-          *reinterpret_cast<uint32_t *>(bt + lg_swz(n8, p1) + 4 * tq) = v[kb][3];
+          // register r of the product: rows g (r even) or g+8 (r odd), columns
+          // (c, c+1) for r < 2 and (c+8, c+9) above, c = 16 kb + 2 tq
+          uint32_t q[4];
+          dequant_i4(words[kb], q);
+          const uint32_t sg = kb < 2 ? sc.x : sc.y;  // f16 scales of rows g (low half) and g+8 (high half)
+          const __half2 s2 = *reinterpret_cast<const __half2 *>(&sg);
+          const float sr[2] = {__low2float(s2), __high2float(s2)};
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const __half2 c2 = *reinterpret_cast<const __half2 *>(&q[r]);
+            const float p0 = __low2float(c2) * sr[r & 1], p1 = __high2float(c2) * sr[r & 1];  // exact in f32
+            const __half2 hi = __floats2half2_rn(p0, p1);
+            const __half2 lo = __floats2half2_rn(p0 - __low2float(hi), p1 - __high2float(hi));
+            const uint32_t off = lg_swz((r & 1) ? n8 : n0, 2 * kb + (r >> 1)) + 4 * tq;
+            *reinterpret_cast<__half2 *>(bh + off) = hi;
+            *reinterpret_cast<__half2 *>(bl + off) = lo;
+          }
         }
       }
       fence_async_smem();  // the weights written here are read by the tensor core (async proxy)
@@ -275,14 +278,35 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
     const bool live = m < a.lanes;
     const float f = live ? a.factor[m] : 0.0f;
     const int n_rows = a.n_rb * 16;
-    float *orow = a.out + ((size_t)z * a.lanes + (live ? m : 0)) * a.out_stride;
+    const bool argm = a.arg_val != nullptr;
+    float best = -FLT_MAX;
+    int best_i = 0x7fffffff;
+    float *orow = a.out ? a.out + ((size_t)z * a.lanes + (live ? m : 0)) * a.out_stride : nullptr;
     for (int c0 = 0; c0 < LG_N; c0 += 32) {
       const int n0 = nt * LG_N + c0;
       if (n0 >= n_rows) break;  // warp-uniform
       float v[32];
       tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)c0, v);
-      if (live) {
-        if (n0 + 32 <= n_rows) {
+      if (argm) {
+        // app_core.c:11755 kern_logit_cap, then app_main.c:482's argmax
+        // (rows in increasing order: a strict > keeps the first index)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = v[i] * f;
+          if (a.cap > 0.0f) x = logit_cap(x, a.cap);
+          v[i] = x;
+          if (n0 + i < a.rows && x > best) {
+            best = x;
+            best_i = n0 + i;
+          }
+        }
+      }
+      if (live && orow) {
+        if (argm) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (n0 + i < a.rows) orow[n0 + i] = v[i];
+        } else if (n0 + 32 <= n_rows) {
           float4 *o4 = reinterpret_cast<float4 *>(orow + n0);
 #pragma unroll
           for (int i = 0; i < 8; ++i) o4[i] = make_float4(v[4 * i] * f, v[4 * i + 1] * f, v[4 * i + 2] * f, v[4 * i + 3] * f);
@@ -292,6 +316,10 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
             if (n0 + i < n_rows) orow[n0 + i] = v[i] * f;
         }
       }
+    }
+    if (argm && live) {
+      a.arg_val[(size_t)nt * a.lanes + m] = best;
+      a.arg_idx[(size_t)nt * a.lanes + m] = best_i;
     }
     tc_fence_before();
   }
@@ -384,22 +412,58 @@ __global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
   for (int i = tid; i < n; i += nt) mx = fmaxf(mx, fabsf(y[i]));
   const float sc = lane_scale(block_max(mx, red));
   if (tid == 0) a.factor[j] = a.out_scale / sc;
-  // f16 pieces of eight columns into the operand block of (lane tile, step)
+  // f16 hi and lo pieces of eight columns into the operand blocks of (lane
+  // tile, step); columns past the row are zero
   const int mt = j / LG_M, r = j % LG_M, pieces = a.n_cc * 8;
   uint8_t *dst = reinterpret_cast<uint8_t *>(a.a_tiles);
   for (int p = tid; p < pieces; p += nt) {
     const int c0 = p * 8, cc = p >> 3, pj = p & 7;
-    uint32_t w[4];
+    uint32_t wh[4], wl[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
       const float v0 = c0 + 2 * h < n ? y[c0 + 2 * h] * sc : 0.0f;
       const float v1 = c0 + 2 * h + 1 < n ? y[c0 + 2 * h + 1] * sc : 0.0f;
-      __half2 hv = __floats2half2_rn(v0, v1);
-      w[h] = *reinterpret_cast<uint32_t *>(&hv);
+      const __half2 hv = __floats2half2_rn(v0, v1);
+      const __half2 lv = __floats2half2_rn(v0 - __low2float(hv), v1 - __high2float(hv));
+      wh[h] = *reinterpret_cast<const uint32_t *>(&hv);
+      wl[h] = *reinterpret_cast<const uint32_t *>(&lv);
     }
-    *reinterpret_cast<uint4 *>(dst + ((size_t)mt * a.n_cc + cc) * LG_A_BYTES + lg_swz(r, pj)) =
-        make_uint4(w[0], w[1], w[2], w[3]);
+    uint8_t *blk = dst + ((size_t)mt * a.n_cc + cc) * 2 * LG_OP_BYTES + lg_swz(r, pj);
+    *reinterpret_cast<uint4 *>(blk) = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+    *reinterpret_cast<uint4 *>(blk + LG_OP_BYTES) = make_uint4(wl[0], wl[1], wl[2], wl[3]);
   }
+}
+
+// The output head's argmax partials merged per lane (first index on a tie).
+__global__ void lane_argmax_kernel(const float *val, const int *idx, int parts, int lanes, int32_t *top) {
+  const int j = blockIdx.x, tid = threadIdx.x;
+  __shared__ float sv[256];
+  __shared__ int si[256];
+  float v = -FLT_MAX;
+  int i = 0x7fffffff;
+  for (int p = tid; p < parts; p += blockDim.x) {
+    const float ov = val[(size_t)p * lanes + j];
+    const int oi = idx[(size_t)p * lanes + j];
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+  sv[tid] = v;
+  si[tid] = i;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (tid < w) {
+      const float ov = sv[tid + w];
+      const int oi = si[tid + w];
+      if (ov > sv[tid] || (ov == sv[tid] && oi < si[tid])) {
+        sv[tid] = ov;
+        si[tid] = oi;
+      }
+    }
+    __syncthreads();
+  }
+  if (tid == 0) top[j] = si[0];
 }
 
 // K-slice partials added in order: out[j][i] = sum_z p[z][j][i].
@@ -460,8 +524,16 @@ int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count) {
 
 cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
   if (a->lanes < 1 || a->split < 1 || a->split > a->n_cc || a->n_rb < 1) return cudaErrorInvalidValue;
+  if (a->arg_val && (a->split != 1 || !a->arg_idx)) return cudaErrorInvalidValue;
   dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
   lane_gemm_kernel<<<grid, LG_THREADS, LG_SMEM, st>>>(*a);
+  return cudaGetLastError();
+}
+
+cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,
+                                   cudaStream_t st) {
+  if (lanes < 1 || parts < 1) return cudaErrorInvalidValue;
+  lane_argmax_kernel<<<lanes, 256, 0, st>>>(val, idx, parts, lanes, top);
   return cudaGetLastError();
 }
 

@@ -9,7 +9,8 @@
 namespace igc {
 
 constexpr int LG_M = 128;  // lanes a tile (tensor-memory lanes)
-constexpr int LG_N = 256;  // weight rows a tile (tensor-memory columns)
+constexpr int LG_N = 128;  // weight rows a tile (tensor-memory columns)
+constexpr int LG_A_STEP_BYTES = 2 * 128 * 64 * 2;  // staged activations a (lane tile, 64-column step): hi and lo blocks
 
 // What a stage computes for its lane before staging it (app_core.c:11637-11743).
 enum : int {
@@ -35,7 +36,7 @@ struct LaneStageArgs {
   const float *aux;       // GELU_MUL: [lanes][aux_stride]
   int aux_stride;
   float out_scale;        // folded into the lane's factor
-  void *a_tiles;          // out: [lane tile][n_cc][16 KB] f16 operand blocks
+  void *a_tiles;          // out: [lane tile][n_cc][hi, lo][16 KB] f16 operand blocks
   int n_cc;               // 64-column steps of the next product
   float *factor;          // out: [lanes] the factor undoing the staging scale (times out_scale)
 };
@@ -49,6 +50,14 @@ struct LaneGemmArgs {
   float *out;             // [split][lanes][out_stride] partial sums, plane row order
   int lanes, out_stride, split;
   int *err;               // set nonzero when a wait gave up
+  // the output head's epilogue (split 1): each value times the lane's factor
+  // and soft-capped (`cap` > 0), the largest of the tile's first `rows` rows
+  // per lane (first index on a tie) to arg_val / arg_idx [tile][lanes], and
+  // the capped values to `out` only when it is not null
+  float *arg_val;
+  int *arg_idx;
+  int rows;
+  float cap;
 };
 
 }  // namespace igc
@@ -63,6 +72,10 @@ int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count);
 cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, cudaStream_t st);
 // out[i] = *p0 + 16 i for i < groups (a prefill chunk's attention groups).
 cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st);
+// Per lane the largest of `parts` argmax partials [part][lanes] (first index
+// on a tie), into top[lanes].
+cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,
+                                   cudaStream_t st);
 cudaError_t igc_launch_lane_sum(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride, cudaStream_t st);
 }

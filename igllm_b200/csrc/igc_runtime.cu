@@ -25,6 +25,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <unordered_map>
 #include <vector>
 
@@ -770,10 +771,32 @@ extern "C" int igc_model_state_size(const igc_model *m) { return m ? m->hidden :
 extern "C" int igc_model_window_limit(const igc_model *m) { return m ? m->window_limit : 0; }
 extern "C" size_t igc_model_decode_bytes(const igc_model *m) { return m ? m->decode_bytes : 0; }
 extern "C" size_t igc_model_device_bytes(const igc_model *m) { return m ? m->device_bytes : 0; }
+// Weights of the int4 projections one lane multiplies (each product's rows x
+// columns, both halves of a gate|up pair): half the FLOPs of a lane.
+extern "C" size_t igc_model_weight_count(const igc_model *m) {
+  if (!m) return 0;
+  auto n = [](const DevPlane &p) -> size_t { return p.tiles ? (size_t)p.rows * p.cols * (p.pair ? 2 : 1) : 0; };
+  size_t t = n(m->ple_lift) + n(m->head);
+  for (auto &L : m->layer) t += n(L.qkv) + n(L.o) + n(L.gateup) + n(L.down) + n(L.ple_gate) + n(L.ple_proj);
+  return t;
+}
 
 // ---------------------------------------------------------------------------
 // sessions
 
+
+// Device buffers of the batched-lane passes (igc_lanes.cu) for up to `cap`
+// lanes: the residual stream, the per-layer inputs, q|k|v, attention, the
+// K-slice partials, the staged operand blocks and their factors, and the
+// output head's argmax partials.
+struct LaneBuf {
+  int cap = 0, split_lanes = 0;
+  float *x0 = nullptr, *xa = nullptr, *xb = nullptr, *seed = nullptr, *ple_raw = nullptr, *ple = nullptr;
+  float *qkv = nullptr, *attn = nullptr, *part = nullptr, *factor = nullptr;
+  float *arg_val = nullptr;
+  int *arg_idx = nullptr;
+  void *a_tiles = nullptr;
+};
 
 struct igc_session {
   igc_model *m = nullptr;
@@ -836,12 +859,9 @@ struct igc_session {
   // `cap` lanes, allocated on the first prime that uses them, and a captured
   // graph per chunk length
   struct Chunks {
-    int cap = 0;
+    LaneBuf B;
     int32_t *d_ids = nullptr;  // [0] position, [1..cap] ids
     int *d_pos = nullptr;      // the 16-lane attention groups' positions
-    float *x0 = nullptr, *xa = nullptr, *xb = nullptr, *seed = nullptr, *ple_raw = nullptr, *ple = nullptr;
-    float *qkv = nullptr, *attn = nullptr, *part = nullptr, *factor = nullptr;
-    void *a_tiles = nullptr;
     int32_t *h_ids = nullptr;  // pinned
     std::map<int, cudaGraphExec_t> graph;
   } ch;
@@ -1303,26 +1323,30 @@ static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
 }
 
 // ---------------------------------------------------------------------------
-// the batched-lane prime: chunks of up to IGC_CHUNK_LANES lanes, every
-// projection a tcgen05 GEMM (igc_lanes.cu), attention in 16-lane groups in
-// position order (each group writes its keys and values to the cache before
-// the next group reads them)
+// the batched-lane passes: every projection a tcgen05 GEMM (igc_lanes.cu)
+// with a row-wise stage before it.  Two callers: the prime, in chunks of up
+// to 256 lanes of one session (attention in 16-lane groups in position
+// order: each group writes its keys and values to the cache before the next
+// group reads them), and the crowd (igc_crowd_round), one block of k lanes
+// from each of many sessions (attention for all of them in one launch).
 
-constexpr int IGC_CHUNK_LANES = 256;  // lanes a chunk
+constexpr int IGC_CHUNK_LANES = 256;  // lanes a prime chunk
 constexpr int IGC_CHUNK_MIN = 64;     // fewer lanes than this run as 16-lane passes
 
-static int chunks_ready(igc_session *s) {
-  auto &C = s->ch;
-  if (C.cap) return IGC_OKAY;
-  igc_model *m = s->m;
-  const int M = IGC_CHUNK_LANES, H = m->hidden, PS = m->layers * m->ple_dim;
-  // the largest K-slice partials any product of any chunk length leaves
+// Sizes `B` for passes of up to `cap` lanes.  `split_lanes` > 0 fixes every
+// product's K slices to those of a pass of that many lanes (results then do
+// not depend on how many lanes a pass carries); 0 lets each pass choose.
+static int lane_buf_alloc(igc_model *m, LaneBuf &B, int cap, int split_lanes, std::vector<void *> &owned) {
+  const int H = m->hidden, PS = m->layers * m->ple_dim;
   size_t part = 0;
   int max_cc = 1;
   auto see = [&](const DevPlane &pl) {
     if (!pl.tiles) return;
-    for (int lanes = IGC_CHUNK_MIN; lanes <= M; ++lanes)
-      part = std::max(part, (size_t)igc_lane_gemm_split(lanes, pl.n_rb, pl.n_cc, m->sm_count) * lanes * pl.n_rb * 16);
+    if (split_lanes > 0)
+      part = std::max(part, (size_t)igc_lane_gemm_split(split_lanes, pl.n_rb, pl.n_cc, m->sm_count) * cap * pl.n_rb * 16);
+    else
+      for (int lanes = 1; lanes <= cap; ++lanes)
+        part = std::max(part, (size_t)igc_lane_gemm_split(lanes, pl.n_rb, pl.n_cc, m->sm_count) * lanes * pl.n_rb * 16);
     max_cc = std::max(max_cc, pl.n_cc);
   };
   see(m->ple_lift);
@@ -1334,54 +1358,44 @@ static int chunks_ready(igc_session *s) {
     see(L.ple_gate);
     see(L.ple_proj);
   }
+  max_cc = std::max(max_cc, m->head.n_cc);
+  auto grab = [&](auto **p, size_t count) -> int {
+    void *v = nullptr;
+    cudaError_t e = cudaMalloc(&v, (count ? count : 1) * sizeof(**p));
+    if (e != cudaSuccess) return fail_device(e, "cudaMalloc(lanes)");
+    owned.push_back(v);
+    *p = (std::remove_reference_t<decltype(*p)>)v;
+    return IGC_OKAY;
+  };
   int c = IGC_OKAY;
-  if (c == IGC_OKAY) c = s->alloc(&C.d_ids, 1 + M);
-  if (c == IGC_OKAY) c = s->alloc(&C.d_pos, M / 16 + 1);
-  if (c == IGC_OKAY) c = s->alloc(&C.x0, (size_t)M * H);
-  if (c == IGC_OKAY) c = s->alloc(&C.xa, (size_t)M * H);
-  if (c == IGC_OKAY) c = s->alloc(&C.xb, (size_t)M * H);
-  if (c == IGC_OKAY) c = s->alloc(&C.seed, (size_t)M * (PS ? PS : 1));
-  if (c == IGC_OKAY) c = s->alloc(&C.ple_raw, (size_t)M * (PS ? PS : 1));
-  if (c == IGC_OKAY) c = s->alloc(&C.ple, (size_t)M * (PS ? PS : 1));
-  if (c == IGC_OKAY) c = s->alloc(&C.qkv, (size_t)M * m->max_qkv);
-  if (c == IGC_OKAY) c = s->alloc(&C.attn, (size_t)M * m->max_q);
-  if (c == IGC_OKAY) c = s->alloc(&C.part, part);
-  if (c == IGC_OKAY) c = s->alloc(&C.factor, (size_t)M);
-  if (c == IGC_OKAY) c = s->alloc((uint8_t **)&C.a_tiles, (size_t)((M + LG_M - 1) / LG_M) * max_cc * LG_M * 64 * 2);
+  if (c == IGC_OKAY) c = grab(&B.x0, (size_t)cap * H);
+  if (c == IGC_OKAY) c = grab(&B.xa, (size_t)cap * H);
+  if (c == IGC_OKAY) c = grab(&B.xb, (size_t)cap * H);
+  if (c == IGC_OKAY) c = grab(&B.seed, (size_t)cap * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = grab(&B.ple_raw, (size_t)cap * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = grab(&B.ple, (size_t)cap * (PS ? PS : 1));
+  if (c == IGC_OKAY) c = grab(&B.qkv, (size_t)cap * m->max_qkv);
+  if (c == IGC_OKAY) c = grab(&B.attn, (size_t)cap * m->max_q);
+  if (c == IGC_OKAY) c = grab(&B.part, part);
+  if (c == IGC_OKAY) c = grab(&B.factor, (size_t)cap);
+  if (c == IGC_OKAY) c = grab((uint8_t **)&B.a_tiles, (size_t)((cap + LG_M - 1) / LG_M) * max_cc * LG_A_STEP_BYTES);
+  const size_t head_tiles = (size_t)(m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16);
+  if (c == IGC_OKAY) c = grab(&B.arg_val, head_tiles * cap);
+  if (c == IGC_OKAY) c = grab(&B.arg_idx, head_tiles * cap);
   if (c != IGC_OKAY) return c;
-  CK(cudaMallocHost(&C.h_ids, sizeof(int32_t) * (1 + M)));
-  C.cap = M;
+  B.cap = cap;
+  B.split_lanes = split_lanes;
   return IGC_OKAY;
 }
 
-// One stage into the chunk's operand blocks for the product `pl` (its
-// columns and steps), then the product's K-slice partials into `part`.
-static int chunk_product(igc_session *s, const DevPlane &pl, int M, LaneStageArgs sa, int *split_out) {
-  auto &C = s->ch;
-  sa.lanes = M;
-  sa.cols = pl.cols;
-  sa.n_cc = pl.n_cc;
-  sa.a_tiles = C.a_tiles;
-  sa.factor = C.factor;
-  sa.eps = s->m->eps;
-  CKL(igc_launch_lane_stage(&sa, s->st));
-  LaneGemmArgs ga;
-  memset(&ga, 0, sizeof(ga));
-  ga.tiles = pl.tiles;
-  ga.scales = pl.scales;
-  ga.n_rb = pl.n_rb;
-  ga.n_cc = pl.n_cc;
-  ga.a_tiles = reinterpret_cast<const uint4 *>(C.a_tiles);
-  ga.factor = C.factor;
-  ga.out = C.part;
-  ga.lanes = M;
-  ga.out_stride = pl.n_rb * 16;
-  ga.split = igc_lane_gemm_split(M, pl.n_rb, pl.n_cc, s->m->sm_count);
-  ga.err = s->d_err;
-  CKL(igc_launch_lane_gemm(&ga, s->st));
-  *split_out = ga.split;
-  return IGC_OKAY;
-}
+// One pass of the batched-lane path over the stack's layers.
+struct LaneRun {
+  igc_model *m;
+  cudaStream_t st;
+  LaneBuf *B;
+  int *d_err;
+  int M;  // lanes
+};
 
 static LaneStageArgs stage_of(int mode, const float *x, int x_stride) {
   LaneStageArgs a;
@@ -1394,127 +1408,193 @@ static LaneStageArgs stage_of(int mode, const float *x, int x_stride) {
   return a;
 }
 
-// One chunk of M lanes at the position in ch.d_ids[0], ids in ch.d_ids[1..M]
-// (app_core.c:11843 session_pass without the head: a prime keeps no logits).
-static int enqueue_chunk(igc_session *s, int M) {
-  igc_model *m = s->m;
-  auto &C = s->ch;
-  PdlScope pdl(false);
-  const int H = m->hidden, PS = m->layers * m->ple_dim, groups = (M + 15) / 16;
-  const int *d_p0 = C.d_ids;
-  int c, split = 1;
-  CKL(igc_launch_lane_positions(d_p0, groups, C.d_pos, s->st));
-  CKL(igc_launch_embed(C.d_ids + 1, M, m->embed, H, (float)sqrt((double)H), m->ple_embed,
-                       m->ple_vocab ? m->ple_vocab : 1, PS, (float)sqrt((double)m->ple_dim), C.x0, C.seed, nullptr, 0,
-                       s->st));
-  if (m->ple_dim > 0) {
-    LaneStageArgs sa = stage_of(LS_PLAIN, C.x0, H);
-    sa.out_scale = (float)(1.0 / sqrt((double)H));
-    c = chunk_product(s, m->ple_lift, M, sa, &split);
-    if (c != IGC_OKAY) return c;
-    CKL(igc_launch_lane_sum(C.part, split, M, PS, m->ple_lift.n_rb * 16, C.ple_raw, PS, s->st));
-    CKL(igc_launch_ple_finish(C.ple_raw, C.seed, M, m->layers, m->ple_dim, m->ple_norm, m->eps,
-                              (float)(1.0 / sqrt(2.0)), C.ple, s->st));
+// A stage into the pass's operand blocks for the product `pl` (its columns
+// and steps), then the product: K-slice partials into B.part, or with `head`
+// set the output head's argmax partials (and logits into `logits` when given).
+static int lane_product(LaneRun &r, const DevPlane &pl, LaneStageArgs sa, int *split_out, bool head = false,
+                        float *logits = nullptr) {
+  LaneBuf &B = *r.B;
+  sa.lanes = r.M;
+  sa.cols = pl.cols;
+  sa.n_cc = pl.n_cc;
+  sa.a_tiles = B.a_tiles;
+  sa.factor = B.factor;
+  sa.eps = r.m->eps;
+  CKL(igc_launch_lane_stage(&sa, r.st));
+  LaneGemmArgs ga;
+  memset(&ga, 0, sizeof(ga));
+  ga.tiles = pl.tiles;
+  ga.scales = pl.scales;
+  ga.n_rb = pl.n_rb;
+  ga.n_cc = pl.n_cc;
+  ga.a_tiles = reinterpret_cast<const uint4 *>(B.a_tiles);
+  ga.factor = B.factor;
+  ga.lanes = r.M;
+  ga.err = r.d_err;
+  if (head) {
+    ga.split = 1;
+    ga.out = logits;
+    ga.out_stride = pl.rows;
+    ga.arg_val = B.arg_val;
+    ga.arg_idx = B.arg_idx;
+    ga.rows = pl.rows;
+    ga.cap = r.m->softcap;
+  } else {
+    ga.out = B.part;
+    ga.out_stride = pl.n_rb * 16;
+    ga.split = igc_lane_gemm_split(B.split_lanes > 0 ? B.split_lanes : r.M, pl.n_rb, pl.n_cc, r.m->sm_count);
   }
-  // the residual stream ping-pongs between xa and xb; `pend` (in C.part,
+  CKL(igc_launch_lane_gemm(&ga, r.st));
+  *split_out = ga.split;
+  return IGC_OKAY;
+}
+
+// embed, the per-layer-embedding lift, the layers (attention by `attend`),
+// and with `top` the final norm, the head and each lane's argmax.
+template <typename Attend>
+static int lane_stack(LaneRun &r, const int32_t *d_ids, Attend attend, int32_t *top = nullptr,
+                      float *logits = nullptr) {
+  igc_model *m = r.m;
+  LaneBuf &B = *r.B;
+  const int H = m->hidden, PS = m->layers * m->ple_dim, M = r.M;
+  int c, split = 1;
+  CKL(igc_launch_embed(d_ids, M, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
+                       PS, (float)sqrt((double)m->ple_dim), B.x0, B.seed, nullptr, 0, r.st));
+  if (m->ple_dim > 0) {
+    LaneStageArgs sa = stage_of(LS_PLAIN, B.x0, H);
+    sa.out_scale = (float)(1.0 / sqrt((double)H));
+    c = lane_product(r, m->ple_lift, sa, &split);
+    if (c != IGC_OKAY) return c;
+    CKL(igc_launch_lane_sum(B.part, split, M, PS, m->ple_lift.n_rb * 16, B.ple_raw, PS, r.st));
+    CKL(igc_launch_ple_finish(B.ple_raw, B.seed, M, m->layers, m->ple_dim, m->ple_norm, m->eps,
+                              (float)(1.0 / sqrt(2.0)), B.ple, r.st));
+  }
+  // the residual stream ping-pongs between xa and xb; `pend` (in B.part,
   // `pend_split` slices of `pend_stride`) is the last block's output still
   // to be normed and added (with its gain) by the next stage
-  float *cur = C.x0;
-  float *bufs[2] = {C.xa, C.xb};
+  float *cur = B.x0;
+  float *bufs[2] = {B.xa, B.xb};
   int flip = 0;
   auto next_x = [&]() -> float * { float *o = bufs[flip]; flip ^= 1; return o; };
   bool pend = false;
   int pend_split = 1, pend_stride = 0;
   const float *pend_w = nullptr;
   float pend_gain = 1.0f;
+  auto resid = [&](LaneStageArgs &sa) {  // the next stage adds the pending block
+    float *xo = next_x();
+    sa.p = B.part;
+    sa.p_splits = pend_split;
+    sa.p_stride = pend_stride;
+    sa.w_res = pend_w;
+    sa.gain = pend_gain;
+    sa.x_out = xo;
+    cur = xo;
+  };
   for (int l = 0; l < m->layers; ++l) {
     const DevLayer &L = m->layer[l];
-    // q|k|v
-    {
+    {  // q|k|v
       LaneStageArgs sa = stage_of(pend ? LS_RESID_NORM : LS_NORM, cur, H);
       sa.w_in = L.enter_norm;
-      if (pend) {
-        float *xo = next_x();
-        sa.p = C.part;
-        sa.p_splits = pend_split;
-        sa.p_stride = pend_stride;
-        sa.w_res = pend_w;
-        sa.gain = pend_gain;
-        sa.x_out = xo;
-        cur = xo;
-      }
-      c = chunk_product(s, L.qkv, M, sa, &split);
+      if (pend) resid(sa);
+      c = lane_product(r, L.qkv, sa, &split);
       if (c != IGC_OKAY) return c;
-      CKL(igc_launch_lane_sum(C.part, split, M, L.qkv_rows, L.qkv.n_rb * 16, C.qkv, L.qkv_rows, s->st));
+      CKL(igc_launch_lane_sum(B.part, split, M, L.qkv_rows, L.qkv.n_rb * 16, B.qkv, L.qkv_rows, r.st));
     }
-    // attention, 16 lanes at a time in position order
+    c = attend(l, L);
+    if (c != IGC_OKAY) return c;
+    c = lane_product(r, L.o, stage_of(LS_PLAIN, B.attn, L.q_rows), &split);
+    if (c != IGC_OKAY) return c;
+    {  // gate|up: x += norm(o) * w, then norm(x) * w
+      pend_split = split;
+      pend_stride = L.o.n_rb * 16;
+      pend_w = L.after_attn_norm;
+      pend_gain = 1.0f;
+      LaneStageArgs sa = stage_of(LS_RESID_NORM, cur, H);
+      resid(sa);
+      sa.w_in = L.before_feed_norm;
+      c = lane_product(r, L.gateup, sa, &split);
+      if (c != IGC_OKAY) return c;
+    }
+    {  // down: gelu(gate) * up
+      LaneStageArgs sa = stage_of(LS_GELU_PAIR, nullptr, 0);
+      sa.p = B.part;
+      sa.p_splits = split;
+      sa.p_stride = L.gateup.n_rb * 16;
+      c = lane_product(r, L.down, sa, &split);
+      if (c != IGC_OKAY) return c;
+    }
+    pend_split = split;
+    pend_stride = L.down.n_rb * 16;
+    pend_w = L.after_feed_norm;
+    pend_gain = 1.0f;
+    if (m->ple_dim > 0) {
+      // per-layer-embedding gate: x += norm(down) * w
+      LaneStageArgs sa = stage_of(LS_RESID, cur, H);
+      resid(sa);
+      c = lane_product(r, L.ple_gate, sa, &split);
+      if (c != IGC_OKAY) return c;
+      // its projection: gelu(gate) * the layer's per-layer input
+      LaneStageArgs sb = stage_of(LS_GELU_MUL, nullptr, 0);
+      sb.p = B.part;
+      sb.p_splits = split;
+      sb.p_stride = L.ple_gate.n_rb * 16;
+      sb.aux = B.ple + (size_t)l * m->ple_dim;
+      sb.aux_stride = PS;
+      c = lane_product(r, L.ple_proj, sb, &split);
+      if (c != IGC_OKAY) return c;
+      pend_split = split;
+      pend_stride = L.ple_proj.n_rb * 16;
+      pend_w = L.after_ple_norm;
+    }
+    pend = true;
+    pend_gain = L.gain;
+  }
+  if (top) {
+    // app_core.c:11897-11976: final norm, head, soft cap, argmax
+    LaneStageArgs sa = stage_of(pend ? LS_RESID_NORM : LS_NORM, cur, H);
+    sa.w_in = m->final_norm;
+    if (pend) resid(sa);
+    c = lane_product(r, m->head, sa, &split, true, logits);
+    if (c != IGC_OKAY) return c;
+    CKL(igc_launch_lane_argmax(B.arg_val, B.arg_idx, (m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16), M, top, r.st));
+  }
+  return IGC_OKAY;
+}
+
+static int chunks_ready(igc_session *s) {
+  auto &C = s->ch;
+  if (C.B.cap) return IGC_OKAY;
+  const int M = IGC_CHUNK_LANES;
+  int c = lane_buf_alloc(s->m, C.B, M, 0, s->owned);
+  if (c == IGC_OKAY) c = s->alloc(&C.d_ids, 1 + M);
+  if (c == IGC_OKAY) c = s->alloc(&C.d_pos, M / 16 + 1);
+  if (c != IGC_OKAY) return c;
+  CK(cudaMallocHost(&C.h_ids, sizeof(int32_t) * (1 + M)));
+  return IGC_OKAY;
+}
+
+// One chunk of M lanes at the position in ch.d_ids[0], ids in ch.d_ids[1..M]
+// (app_core.c:11843 session_pass without the head: a prime keeps no logits).
+static int enqueue_chunk(igc_session *s, int M) {
+  igc_model *m = s->m;
+  auto &C = s->ch;
+  PdlScope pdl(false);
+  const int groups = (M + 15) / 16;
+  CKL(igc_launch_lane_positions(C.d_ids, groups, C.d_pos, s->st));
+  LaneRun r{m, s->st, &C.B, s->d_err, M};
+  auto attend = [&](int l, const DevLayer &L) -> int {
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
     for (int gi = 0; gi < groups; ++gi) {
       const int j0 = gi * 16, n = M - j0 < 16 ? M - j0 : 16;
-      CKL(igc_launch_attn(C.qkv + (size_t)j0 * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
-                          m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner],
-                          L.kind == 0 ? 1 : 0, m->slide_span, C.d_pos + gi, n, s->attn_cluster,
-                          C.attn + (size_t)j0 * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
+      CKL(igc_launch_attn(C.B.qkv + (size_t)j0 * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
+                          L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner],
+                          s->vc[owner], L.kind == 0 ? 1 : 0, m->slide_span, C.d_pos + gi, n, s->attn_cluster,
+                          C.B.attn + (size_t)j0 * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
     }
-    // o
-    c = chunk_product(s, L.o, M, stage_of(LS_PLAIN, C.attn, L.q_rows), &split);
-    if (c != IGC_OKAY) return c;
-    // gate|up: x += norm(o) * w, then norm(x) * w
-    {
-      LaneStageArgs sa = stage_of(LS_RESID_NORM, cur, H);
-      float *xo = next_x();
-      sa.p = C.part;
-      sa.p_splits = split;
-      sa.p_stride = L.o.n_rb * 16;
-      sa.w_res = L.after_attn_norm;
-      sa.w_in = L.before_feed_norm;
-      sa.x_out = xo;
-      cur = xo;
-      c = chunk_product(s, L.gateup, M, sa, &split);
-      if (c != IGC_OKAY) return c;
-    }
-    // down: gelu(gate) * up
-    {
-      LaneStageArgs sa = stage_of(LS_GELU_PAIR, nullptr, 0);
-      sa.p = C.part;
-      sa.p_splits = split;
-      sa.p_stride = L.gateup.n_rb * 16;
-      c = chunk_product(s, L.down, M, sa, &split);
-      if (c != IGC_OKAY) return c;
-    }
-    if (m->ple_dim > 0) {
-      // per-layer-embedding gate: x += norm(down) * w
-      LaneStageArgs sa = stage_of(LS_RESID, cur, H);
-      float *xo = next_x();
-      sa.p = C.part;
-      sa.p_splits = split;
-      sa.p_stride = L.down.n_rb * 16;
-      sa.w_res = L.after_feed_norm;
-      sa.x_out = xo;
-      cur = xo;
-      c = chunk_product(s, L.ple_gate, M, sa, &split);
-      if (c != IGC_OKAY) return c;
-      // its projection: gelu(gate) * the layer's per-layer input
-      LaneStageArgs sb = stage_of(LS_GELU_MUL, nullptr, 0);
-      sb.p = C.part;
-      sb.p_splits = split;
-      sb.p_stride = L.ple_gate.n_rb * 16;
-      sb.aux = C.ple + (size_t)l * m->ple_dim;
-      sb.aux_stride = PS;
-      c = chunk_product(s, L.ple_proj, M, sb, &split);
-      if (c != IGC_OKAY) return c;
-      pend_stride = L.ple_proj.n_rb * 16;
-      pend_w = L.after_ple_norm;
-    } else {
-      pend_stride = L.down.n_rb * 16;
-      pend_w = L.after_feed_norm;
-    }
-    pend = true;
-    pend_split = split;
-    pend_gain = L.gain;
-  }
-  return IGC_OKAY;
+    return IGC_OKAY;
+  };
+  return lane_stack(r, C.d_ids + 1, attend);
 }
 
 // One chunk of M lanes (64 <= M <= IGC_CHUNK_LANES), kept, with a captured
@@ -1637,6 +1717,192 @@ extern "C" int igc_session_guess_keep(igc_session *s, int keep) { /* app_core.c:
   s->echo.resize((size_t)(s->guess_echo + keep));
   s->guess_count = 0;
   return IGC_OKAY;
+}
+
+// ---------------------------------------------------------------------------
+// the crowd: one verify round for many sessions in one pass (no counterpart
+// in the reference, which runs one session at a time, app_core.c:7789-7793)
+//
+// Every session of a crowd round shares the model; each brings a block of k
+// ids at its own position and its own caches.  The block's lanes of all
+// sessions go through one weight sweep per projection (the tcgen05 lane
+// GEMM), attention runs once per layer for all sessions (blockIdx.z the
+// session, its caches and position from device tables), and the head ends
+// in each lane's argmax.  Each session then keeps its leading matches, as
+// igc_session_round does for one.  The K slices of every product are fixed
+// by the crowd's capacity, so a session's results do not depend on how many
+// sessions share its round.
+
+struct igc_crowd {
+  igc_model *m = nullptr;
+  cudaStream_t st = nullptr;
+  int cap = 0, k = 0, lanes = 0;
+  LaneBuf B;
+  // device: [ids: lanes][pos: cap][kc: layers * cap][vc: layers * cap], mirrored in pinned host memory
+  uint8_t *d_tab = nullptr, *h_tab = nullptr;
+  size_t tab_bytes = 0;
+  int32_t *d_top = nullptr;  // [lanes] argmax, then the kernels' error word
+  int32_t *h_top = nullptr;
+  float *logits = nullptr;   // [lanes][vocab], allocated on the first round that asks for rows
+  std::map<std::pair<int, int>, cudaGraphExec_t> graph;  // (sessions, rows wanted)
+  std::map<std::pair<int, int>, long> launches;
+  std::vector<void *> owned;
+
+  int32_t *ids() { return reinterpret_cast<int32_t *>(d_tab); }
+  int *pos() { return reinterpret_cast<int *>(d_tab + sizeof(int32_t) * lanes); }
+  float **kc() { return reinterpret_cast<float **>(d_tab + sizeof(int32_t) * lanes + sizeof(int) * cap); }
+  float **vc() { return kc() + (size_t)m->layers * cap; }
+
+  ~igc_crowd() {
+    cudaSetDevice(m->device);
+    for (auto &kv : graph) cudaGraphExecDestroy(kv.second);
+    for (void *p : owned) cudaFree(p);
+    if (h_tab) cudaFreeHost(h_tab);
+    if (h_top) cudaFreeHost(h_top);
+    if (st) cudaStreamDestroy(st);
+    clear_stale("crowd close");
+  }
+};
+
+extern "C" int igc_crowd_open(igc_model *m, int session_limit, int lanes_per_session, igc_crowd **out) {
+  if (!m || !out || session_limit < 1 || lanes_per_session < 1 || lanes_per_session > IGC_LANE_LIMIT)
+    return IGC_FAIL_ARGUMENT;
+  if (session_limit * lanes_per_session > IGC_CROWD_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
+  *out = nullptr;
+  clear_stale("crowd open");
+  CK(cudaSetDevice(m->device));
+  auto cr = std::make_unique<igc_crowd>();
+  cr->m = m;
+  cr->cap = session_limit;
+  cr->k = lanes_per_session;
+  cr->lanes = session_limit * lanes_per_session;
+  CK(cudaStreamCreateWithFlags(&cr->st, cudaStreamNonBlocking));
+  int c = lane_buf_alloc(m, cr->B, cr->lanes, cr->lanes, cr->owned);
+  if (c != IGC_OKAY) return c;
+  cr->tab_bytes = sizeof(int32_t) * cr->lanes + sizeof(int) * cr->cap + 2 * sizeof(float *) * m->layers * cr->cap;
+  void *v = nullptr;
+  CK(cudaMalloc(&v, cr->tab_bytes));
+  cr->owned.push_back(v);
+  cr->d_tab = (uint8_t *)v;
+  CK(cudaMalloc(&v, sizeof(int32_t) * (cr->lanes + 1)));
+  cr->owned.push_back(v);
+  cr->d_top = (int32_t *)v;
+  CK(cudaMemset(cr->d_top, 0, sizeof(int32_t) * (cr->lanes + 1)));
+  CK(cudaMallocHost(&v, cr->tab_bytes));
+  cr->h_tab = (uint8_t *)v;
+  CK(cudaMallocHost(&v, sizeof(int32_t) * (cr->lanes + 1)));
+  cr->h_top = (int32_t *)v;
+  *out = cr.release();
+  return IGC_OKAY;
+}
+
+extern "C" void igc_crowd_close(igc_crowd *cr) { delete cr; }
+
+static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
+  igc_model *m = cr->m;
+  PdlScope pdl(false);
+  const int k = cr->k;
+  LaneRun r{m, cr->st, &cr->B, cr->d_top + cr->lanes, S * k};
+  auto attend = [&](int l, const DevLayer &L) -> int {
+    const int owner = L.share ? L.source : l;
+    const DevLayer &O = m->layer[owner];
+    CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
+                             m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr, L.kind == 0 ? 1 : 0,
+                             m->slide_span, cr->pos(), k, 16, cr->B.attn, L.q_rows, nullptr, nullptr,
+                             cr->kc() + (size_t)l * cr->cap, cr->vc() + (size_t)l * cr->cap, cr->pos(), S, cr->st));
+    return IGC_OKAY;
+  };
+  return lane_stack(r, cr->ids(), attend, cr->d_top, rows ? cr->logits : nullptr);
+}
+
+extern "C" int igc_crowd_round(igc_crowd *cr, igc_session **sessions, int count, const int32_t *ids,
+                               int32_t *take_out, int32_t *made_out, float *logits_out) {
+  if (!cr || !sessions || !ids || count < 1 || count > cr->cap) return IGC_FAIL_ARGUMENT;
+  igc_model *m = cr->m;
+  const int k = cr->k;
+  for (int j = 0; j < count; ++j) {
+    igc_session *s = sessions[j];
+    if (!s || s->m != m) return IGC_FAIL_ARGUMENT;
+    if (s->guess_count > 0) return IGC_FAIL_STATE;
+    if (s->fill + k > m->window_limit) return IGC_FAIL_STATE;
+    for (int q = 0; q < j; ++q)
+      if (sessions[q] == s) return IGC_FAIL_ARGUMENT;  // a session once a round
+  }
+  for (int i = 0; i < count * k; ++i)
+    if (ids[i] < 0 || ids[i] >= m->vocab) return IGC_FAIL_ARGUMENT;
+  clear_stale("crowd round");
+  CK(cudaSetDevice(m->device));
+  if (logits_out && !cr->logits) {
+    void *v = nullptr;
+    CK(cudaMalloc(&v, sizeof(float) * (size_t)cr->lanes * m->vocab));
+    cr->owned.push_back(v);
+    cr->logits = (float *)v;
+  }
+  // the tables: ids, positions and every layer's (owner's) caches per session
+  int32_t *h_ids = reinterpret_cast<int32_t *>(cr->h_tab);
+  int *h_pos = reinterpret_cast<int *>(cr->h_tab + sizeof(int32_t) * cr->lanes);
+  float **h_kc = reinterpret_cast<float **>(cr->h_tab + sizeof(int32_t) * cr->lanes + sizeof(int) * cr->cap);
+  float **h_vc = h_kc + (size_t)m->layers * cr->cap;
+  memcpy(h_ids, ids, sizeof(int32_t) * (size_t)count * k);
+  for (int j = 0; j < count; ++j) {
+    h_pos[j] = sessions[j]->fill;
+    for (int l = 0; l < m->layers; ++l) {
+      const DevLayer &L = m->layer[l];
+      const int owner = L.share ? L.source : l;
+      h_kc[(size_t)l * cr->cap + j] = sessions[j]->kc[owner];
+      h_vc[(size_t)l * cr->cap + j] = sessions[j]->vc[owner];
+    }
+  }
+  CK(cudaMemcpyAsync(cr->d_tab, cr->h_tab, cr->tab_bytes, cudaMemcpyHostToDevice, cr->st));
+  const bool rows = logits_out != nullptr;
+  const auto key = std::make_pair(count, rows ? 1 : 0);
+  auto it = cr->graph.find(key);
+  if (it == cr->graph.end()) {
+    cudaGraph_t g;
+    long before = g_launches;
+    CK(cudaStreamBeginCapture(cr->st, cudaStreamCaptureModeThreadLocal));
+    int c = enqueue_crowd(cr, count, rows);
+    cudaError_t e = cudaStreamEndCapture(cr->st, &g);
+    if (c != IGC_OKAY) return c;
+    if (e != cudaSuccess) return fail_device(e, "capture");
+    cudaGraphExec_t ex;
+    e = cudaGraphInstantiate(&ex, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return fail_device(e, "graph instantiate");
+    it = cr->graph.emplace(key, ex).first;
+    cr->launches[key] = g_launches - before;
+    g_launches = before;
+  }
+  CK(cudaGraphLaunch(it->second, cr->st));
+  g_launches += cr->launches[key];
+  CK(cudaMemcpyAsync(cr->h_top, cr->d_top, sizeof(int32_t) * (cr->lanes + 1), cudaMemcpyDeviceToHost, cr->st));
+  if (rows)
+    CK(cudaMemcpyAsync(logits_out, cr->logits, sizeof(float) * (size_t)count * k * m->vocab, cudaMemcpyDeviceToHost,
+                       cr->st));
+  CK(cudaStreamSynchronize(cr->st));
+  if (cr->h_top[cr->lanes]) {
+    cr->h_top[cr->lanes] = 0;
+    cudaMemsetAsync(cr->d_top + cr->lanes, 0, sizeof(int32_t), cr->st);
+    cudaStreamSynchronize(cr->st);
+    g_last_error = "a kernel gave up waiting for its copies";
+    return IGC_FAIL_DEVICE;
+  }
+  // greedy verify and keep, per session (igc_session_round's rule)
+  int total = 0;
+  for (int j = 0; j < count; ++j) {
+    igc_session *s = sessions[j];
+    const int32_t *blk = ids + (size_t)j * k, *top = cr->h_top + (size_t)j * k;
+    int take = 0;
+    while (take + 1 < k && top[take] == blk[take + 1]) ++take;
+    if (take_out) take_out[j] = take;
+    if (made_out) made_out[j] = top[take];
+    s->fill += take + 1;
+    s->serve_tokens += (size_t)(take + 1);
+    for (int i = 0; i <= take && (int)s->echo.size() < m->window_limit; ++i) s->echo.push_back(blk[i]);
+    s->logit_lanes = 0;
+    total += take + 1;
+  }
+  return total;
 }
 
 // ---------------------------------------------------------------------------

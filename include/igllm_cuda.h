@@ -140,6 +140,9 @@ int igc_model_window_limit(const igc_model *model); /* app_core.c:12665 */
 size_t igc_model_decode_bytes(const igc_model *model);
 /* Device bytes the model holds (weights as uploaded, packed). */
 size_t igc_model_device_bytes(const igc_model *model);
+/* Weights of the int4 projections one lane multiplies, head included (no
+ * counterpart in the reference): a lane's FLOPs are twice this. */
+size_t igc_model_weight_count(const igc_model *model);
 
 /* app_core.c:14219 session_open / :14368 session_close / :14375 session_reset */
 int igc_session_open(igc_model *model, igc_session **session_out);
@@ -191,6 +194,33 @@ int igc_session_round(igc_session *session, const int32_t *id_list, int id_count
  * steps and blocks (app_core.c:70-77 app_tally serve_seconds/serve_tokens). */
 double igc_session_serve_seconds(const igc_session *session);
 size_t igc_session_serve_tokens(const igc_session *session);
+
+/* ---- the crowd: many sessions' blocks in one pass (no counterpart in the
+ * reference, which serialises sessions, app_core.c:7789-7793 and
+ * TODO.md:126-132) --------------------------------------------------------
+ *
+ * igc_crowd_open: room for rounds of up to `session_limit` sessions of one
+ * model, each verifying a block of `lanes_per_session` ids (1..16); at most
+ * IGC_CROWD_LANE_LIMIT lanes in all.
+ *
+ * igc_crowd_round: one greedy verify round for `count` sessions at once:
+ * session j's block is ids[j*k .. j*k+k) at its own position.  The lanes of
+ * all blocks share one weight sweep per projection (the tcgen05 lane GEMM),
+ * attention runs for every session in one launch per layer, and each
+ * session keeps its leading matches exactly as igc_session_round does:
+ * take_out[j] the guesses kept, made_out[j] the id after them, fill advanced
+ * by take + 1.  `logits_out`, when not NULL, gets every lane's soft-capped
+ * logits (count*k x vocab floats).  Returns the ids committed in all, or a
+ * negative app_code (a session with a block in flight, a full window, a
+ * session named twice or another model's session are refused before
+ * anything runs).  A session's results do not depend on how many sessions
+ * share its round. */
+#define IGC_CROWD_LANE_LIMIT 512
+typedef struct igc_crowd igc_crowd;
+int igc_crowd_open(igc_model *model, int session_limit, int lanes_per_session, igc_crowd **crowd_out);
+void igc_crowd_close(igc_crowd *crowd);
+int igc_crowd_round(igc_crowd *crowd, igc_session **sessions, int count, const int32_t *id_list, int32_t *take_out,
+                    int32_t *made_out, float *logits_out);
 
 /* ---- measurement (no counterpart in the reference) ----------------------
  *

@@ -1,13 +1,15 @@
 """The batched-lane path (igc_lanes.cu) on the GPU: the tcgen05 int4 GEMM.
 
 A product of 64 or more lanes through the backend table's mat_mat runs as the
-tcgen05 GEMM: staged f16 activations and (code - 8) * scale f16 weights in
-shared memory, tcgen05.mma with f32 accumulators in tensor memory, K slices
-added in a fixed order.  Checked against the CPU checker's igo_mat_mat (the
-restatement of app_core.c:3688 kern_row_code, fp32).  Tolerance: the f16
-rounding of weights and activations keeps the result within 4e-3 of the
-largest output magnitude (measured about 1e-3); the logits the verify round
-is held to allow 2e-2 absolute.
+tcgen05 GEMM: staged activations and (code - 8) * scale weights, each split
+into f16 hi and lo parts, in shared memory, three tcgen05.mma products a
+16-column step into f32 accumulators in tensor memory, K slices added in a
+fixed order.  Checked against the CPU checker's igo_mat_mat (the restatement
+of app_core.c:3688 kern_row_code, fp32).  Tolerance: 2e-4 of each lane's
+largest output magnitude (the hi/lo split keeps about 22 bits of every
+activation and every weight exactly; the rest is f32 summation order), the
+same relative bar the decode path's tests hold; the verify round's logits
+are held to 2e-2 absolute.
 """
 
 import ctypes
@@ -17,7 +19,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-REL = 4e-3
+REL = 2e-4
 
 
 def _plane(igc_lib, rng, rows, cols):
@@ -65,7 +67,7 @@ def test_chunked_prime_matches_the_checker(igc_lib, igo_mod, which, tiny_dir, sm
     the tcgen05 path (every projection a lane GEMM, attention in 16-lane
     groups in position order); what it leaves in the caches must give the
     checker's logits on the step, the block and the step after a keep that
-    follow it, within 2e-2 (and 2e-3 of the row's magnitude)."""
+    follow it, within 2e-2 (and 2e-4 of the row's magnitude)."""
     from conftest import SMALL, TINY, WIDE
     folder, cfg = {"tiny": (tiny_dir, TINY), "small": (small_dir, SMALL), "wide": (wide_dir, WIDE)}[which]
     m = igc_lib.Model(folder=folder, window_limit=cfg["window_limit"])
@@ -79,7 +81,7 @@ def test_chunked_prime_matches_the_checker(igc_lib, igo_mod, which, tiny_dir, sm
 
     def close(got, want):
         err = float(np.abs(got - want).max())
-        assert err <= 2e-2 and err <= 2e-3 * max(1.0, float(np.abs(want).max())), err
+        assert err <= 2e-2 and err <= 2e-4 * max(1.0, float(np.abs(want).max())), err
 
     top, row = s.step(ids[-1])
     close(row, o.step(ids[-1]))
@@ -89,3 +91,50 @@ def test_chunked_prime_matches_the_checker(igc_lib, igo_mod, which, tiny_dir, sm
     o.guess_keep(2)
     _, row = s.step(9)
     close(row, o.step(9))
+
+
+def test_crowd_round_matches_each_session_alone(igc_lib, small_dir):
+    """Five sessions at different positions verify a block of four in one
+    crowd round: every lane's logits agree with the session's own guess (the
+    16-lane path) within 2e-2 and 2e-4 of the row's magnitude, the argmax ids
+    agree wherever the top-2 gap is above 2e-2, each session keeps its
+    leading matches as igc_session_round would, and a session's results do
+    not depend on how many sessions share the round."""
+    from conftest import SMALL
+    m = igc_lib.Model(folder=small_dir, window_limit=SMALL["window_limit"])
+    rng = np.random.default_rng(41)
+    prompts = [rng.integers(0, SMALL["vocab"], n).astype(np.int32) for n in (20, 33, 70, 90, 131)]
+    crowd_s = [igc_lib.Session(m) for _ in prompts]
+    alone_s = [igc_lib.Session(m) for _ in prompts]
+    for s, t, p in zip(crowd_s, alone_s, prompts):
+        s.prime(p)
+        t.prime(p)
+    blocks = []
+    for t, p in zip(alone_s, prompts):
+        top, _ = t.step(p[-1], want_logits=False)
+        blocks.append([p[-1], top] + rng.integers(0, SMALL["vocab"], 2).tolist())  # the first guess is right
+        t.hold(t.fill - 1)
+    blocks = np.array(blocks, np.int32)
+    crowd = igc_lib.Crowd(m, 8, 4)
+    takes, mades, rows = crowd.round(crowd_s, blocks, want_logits=True)
+    for j, (t, blk) in enumerate(zip(alone_s, blocks)):
+        want = t.guess(blk)
+        got = rows[4 * j: 4 * j + 4]
+        err = float(np.abs(got - want).max())
+        assert err <= 2e-2 and err <= 2e-4 * max(1.0, float(np.abs(want).max())), (j, err)
+        top = want.argmax(1)
+        take = 0
+        while take + 1 < 4 and top[take] == blk[take + 1]:
+            take += 1
+        gaps = np.sort(want, 1)[:, -2:]
+        if (gaps[:, 1] - gaps[:, 0] > 2e-2).all():
+            assert takes[j] == take and mades[j] == top[take], (j, takes[j], take)
+        t.guess_keep(int(takes[j]) + 1)
+        assert crowd_s[j].fill == t.fill
+    assert (takes >= 1).all()
+    # the same sessions one at a time through the crowd: the same bits
+    for s, t in zip(crowd_s, alone_s):
+        s.hold(t.fill - int(takes[crowd_s.index(s)]) - 1)
+    solo = np.concatenate([crowd.round([s], blocks[j:j + 1], want_logits=True)[2] for j, s in enumerate(crowd_s)])
+    assert np.array_equal(solo, rows)
+    crowd.close()
