@@ -396,7 +396,31 @@ def run_ours(args):
     prefill = {"tok_s": round((PREFILL_LEN - 1) / (t1 - t0), 1), "ttft_ms": round(1000 * (t2 - t0), 2),
                "prompt": f"{PREFILL_LEN} uniform ids, seed 1 (config 3), 16-lane passes"}
 
+    # config 1: sampled verify rounds (heat 0.8, top-k 64, top-p 0.95,
+    # --guess 8) through the round call; each block guesses the greedy
+    # continuation from the session's current position
+    sampled_rounds, sampled_tokens = 64, 0
+    seq = np.concatenate([[int(prompt[-1])], cont]).astype(np.int32)
+    sess.round(seq[:8], ig.Taste(0.8, 64, 0.95, 1.0, 64, 1))  # captures the 8-lane pass
+    sess.hold(base)
+    t0 = time.perf_counter()
+    done = 0
+    for r in range(sampled_rounds):
+        at = min(done, len(seq) - 8)
+        take, made = sess.round(seq[at: at + 8], ig.Taste(0.8, 64, 0.95, 1.0, 64, 1000 + r))
+        sampled_tokens += take + 1
+        done += take + 1 if take == 7 else 0  # a rejected guess leaves the session off the greedy path
+        if take < 7:
+            sess.hold(base + done)
+    sampled_s = time.perf_counter() - t0
+    sess.hold(base)
+    sampled = {"round_ms": round(1000 * sampled_s / sampled_rounds, 3),
+               "tok_s": round(sampled_tokens / sampled_s, 1), "tokens": sampled_tokens, "rounds": sampled_rounds,
+               "workload": "config 1: heat 0.8, top-k 64, top-p 0.95, --guess 8, guesses from the greedy "
+                           "continuation, through igc_session_round (host ids in and out)"}
+
     crowd = crowd_bench(ig, model) if not args.no_crowd else None
+    long_ctx = long_context_bench(ig) if not args.no_crowd else None
 
     # the projection kernels against the HBM roofline, from the timed
     # region's own graphed passes: every projection and attention launch
@@ -441,7 +465,9 @@ def run_ours(args):
         "verify_round_us": per_k,
         "prefill": prefill,
         "ngram": {"tok_s": round(TOKENS / ngram_s, 1), "rounds": rounds_n, "guesses": drawn, "kept": kept},
+        "sampled": sampled,
         "crowd": crowd,
+        "long_context": long_ctx,
         "roofline": {"bound": "hbm", "kernel": "int4 skinny GEMM (layer projections)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic,
@@ -537,6 +563,50 @@ def crowd_bench(ig, model):
                         "every round (wall clock)"}
 
 
+def long_context_bench(ig):
+    """an 8192-id prompt (a random 2048-id document x4 with
+    5% edits, seed 2), greedy --guess 8 verify rounds at that depth, then a
+    second prompt sharing the first 7680 ids by the --keep path (wind back to
+    7680, prime the other 512; the reference re-primes all 8192 because its
+    session_hold refuses once a sliding ring has turned over,
+    app_core.c:13935-13945), beside a full re-prime for comparison."""
+    rng = np.random.default_rng(2)
+    doc = rng.integers(0, VOCAB, 2048)
+    first = np.tile(doc, 4)
+    edit = rng.random(8192) < 0.05
+    first[edit] = rng.integers(0, VOCAB, int(edit.sum()))
+    second = first.copy()
+    second[7680:] = rng.integers(0, VOCAB, 512)
+    first, second = first.astype(np.int32), second.astype(np.int32)
+    model = ig.Model(spec=ig.spec_e2b(seed=1, window_limit=9216), device=0, window_limit=9216)
+    s = ig.Session(model)
+    s.prime(second)  # captures the chunk graphs
+    s.reset()
+    t0 = time.perf_counter()
+    s.prime(first)
+    prime_s = time.perf_counter() - t0
+    base = s.fill
+    blocks = np.random.default_rng(3).integers(0, VOCAB, (16, 8)).astype(np.int32)
+    s.bench(blocks[:1], 8)
+    s.hold(base)
+    ms, _ = s.bench(blocks, 8)
+    s.hold(7680)
+    t0 = time.perf_counter()
+    s.prime(second[7680:])
+    keep_s = time.perf_counter() - t0
+    s.reset()
+    t0 = time.perf_counter()
+    s.prime(second)
+    full_s = time.perf_counter() - t0
+    s.close()
+    model.close()
+    return {"prime_8192_ms": round(1000 * prime_s, 1), "prime_tok_s": round(8191 / prime_s, 1),
+            "verify_round_us_k8_at_8192": round(1000 * ms / len(blocks), 1),
+            "keep_prefix_7680_then_512_ms": round(1000 * keep_s, 1), "full_reprime_ms": round(1000 * full_s, 1),
+            "workload": "config 2: 8192-id prompt (2048-id document x4, 5% edits, seed 2), greedy --guess 8 "
+                        "rounds at depth 8192, second prompt sharing 7680 ids by the keep path"}
+
+
 def run_profile_case(args):
     """A small verify-round case for kernel profilers (no JSON line): the E2B
     layer stack at full width with a vocabulary of `--case-vocab` ids, so the
@@ -549,8 +619,27 @@ def run_profile_case(args):
     spec = ig.spec_e2b(seed=1, window_limit=4096)
     spec.vocab = args.case_vocab
     model = ig.Model(spec=spec, device=0, window_limit=4096)
-    sess = ig.Session(model)
     rng = np.random.default_rng(0)
+    if args.case_streams > 0:
+        # crowd rounds: `--case-streams` sessions primed to `--case-context`
+        # ids each, `--case-rounds` greedy rounds of `--case-k` lanes for all
+        sessions = [ig.Session(model) for _ in range(args.case_streams)]
+        for s_ in sessions:
+            s_.prime(rng.integers(0, args.case_vocab, args.case_context).astype(np.int32))
+        crowd = ig.Crowd(model, args.case_streams, args.case_k)
+        blocks = rng.integers(0, args.case_vocab, (args.case_streams, args.case_k)).astype(np.int32)
+        crowd.round(sessions, blocks)  # captures the round's graph
+        profiler_range(True)
+        t0 = time.perf_counter()
+        for _ in range(args.case_rounds):
+            crowd.round(sessions, blocks)
+        wall = time.perf_counter() - t0
+        profiler_range(False)
+        print(f"profile case: {args.case_rounds} crowd rounds of {args.case_streams} x {args.case_k} lanes at "
+              f"context {args.case_context}, vocab {args.case_vocab}: {1000 * wall / args.case_rounds:.2f} ms/round",
+              flush=True)
+        return
+    sess = ig.Session(model)
     sess.prime(rng.integers(0, args.case_vocab, args.case_context).astype(np.int32))
     blocks = rng.integers(0, args.case_vocab, (args.case_rounds, args.case_k)).astype(np.int32)
     sess.bench(blocks[:1], args.case_k)  # captures the pass of this shape
@@ -570,13 +659,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the host-core reference baseline")
-    ap.add_argument("--no-crowd", action="store_true", help="skip the 64-stream crowd measurement")
+    ap.add_argument("--no-crowd", action="store_true",
+                    help="skip the 64-stream crowd and long-context measurements")
     ap.add_argument("--profile-case", action="store_true",
                     help="run the small profiler case instead of the benchmark (no JSON line)")
     ap.add_argument("--case-vocab", type=int, default=32768)
     ap.add_argument("--case-k", type=int, default=4)
     ap.add_argument("--case-rounds", type=int, default=3)
     ap.add_argument("--case-context", type=int, default=1024)
+    ap.add_argument("--case-streams", type=int, default=0, help="profile crowd rounds of this many sessions")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)

@@ -21,6 +21,9 @@ and this library through igc_model_load.
             token a sampled round emits at its first lane is distributed as
             the reference's shaped distribution of that lane's row
             (chi-squared; app_test.c:4410-4520 tests the rule the same way).
+  config 2  the 8192-id prompt and a second sharing its first 7680 ids: the
+            --keep path (wind back, prime the rest) leaves exactly the caches
+            a full prime leaves (this library only; the reference re-primes).
 
 Tolerance: logits agree within 2e-2 absolute (the task's bar, fp32
 accumulate).  Under these literal weights most steps have a top-2 gap below
@@ -227,3 +230,44 @@ def test_config1_sampled_verify_matches_the_reference_distribution(igc_lib, e2b)
     # the acceptance rate of the guess is its probability under q
     sd = np.sqrt(q[g1] * (1 - q[g1]) / n)
     assert abs(accepted / n - q[g1]) < 5 * sd
+
+
+def _config2_prompts():
+    """a random 2048-id document repeated 4x with 5% edits
+    (8192 ids), and a second prompt sharing its first 7680 ids."""
+    rng = np.random.default_rng(2)
+    doc = rng.integers(0, VOCAB, 2048)
+    first = np.tile(doc, 4)
+    edit = rng.random(8192) < 0.05
+    first[edit] = rng.integers(0, VOCAB, int(edit.sum()))
+    second = first.copy()
+    second[7680:] = rng.integers(0, VOCAB, 512)
+    return first.astype(np.int32), second.astype(np.int32)
+
+
+def test_config2_keep_prefix_matches_a_full_prime(igc_lib):
+    """The --keep path at depth: after the 8192-id prompt, winding back to the
+    7680 ids the second prompt shares and priming only its last 512 leaves
+    the caches a full prime of the second prompt leaves, to the bit (the
+    reference re-primes in full here, because its session_hold refuses once
+    a sliding ring has turned over, app_core.c:13935-13945); then greedy
+    --guess 8 blocks verify at depth 8192 on every layer kind."""
+    spec = igc_lib.spec_e2b(seed=1, window_limit=9216)
+    m = igc_lib.Model(spec=spec, window_limit=9216)
+    first, second = _config2_prompts()
+    a, b = igc_lib.Session(m), igc_lib.Session(m)
+    a.prime(first)
+    a.step(first[-1], want_logits=False)
+    a.hold(7680)
+    a.prime(second[7680:])
+    b.prime(second)
+    assert a.fill == b.fill == 8191
+    top_a, row_a = a.step(second[-1])
+    top_b, row_b = b.step(second[-1])
+    assert np.array_equal(row_a, row_b) and top_a == top_b
+    rng = np.random.default_rng(9)
+    blk = np.array([top_a] + rng.integers(0, VOCAB, 7).tolist(), np.int32)
+    assert np.array_equal(a.guess(blk), b.guess(blk))
+    a.guess_keep(8)
+    b.guess_keep(8)
+    assert a.fill == b.fill == 8200
