@@ -1430,6 +1430,7 @@ cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint
 }
 
 void igc_kernels_pdl(int on) { g_pdl = on; }
+int igc_kernels_pdl_get(void) { return g_pdl; }
 
 cudaError_t igc_launch_gemv(GemvArgs *a, int pair, int pro, int epi, int grid, size_t smem_limit, cudaStream_t st,
                             int *grid_used) {

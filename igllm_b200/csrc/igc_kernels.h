@@ -17,6 +17,7 @@ cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint
 // Launches from the calling thread may overlap the kernel ahead of them
 // (programmatic dependent launch) while `on` is set.
 void igc_kernels_pdl(int on);
+int igc_kernels_pdl_get(void);
 // Launches at most `grid` blocks (fewer when the lane mode's wider blocks
 // need fewer; the count used goes to *grid_used), picking the weight ring
 // within `smem_limit` bytes of shared memory (filling a->piece, a->depth and

@@ -55,6 +55,7 @@
 
 #include "igc_device.cuh"
 #include "igc_gemv.cuh"
+#include "igc_kernels.h"
 #include "igc_lanes.h"
 
 namespace igc {
@@ -171,30 +172,45 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
+  // the next kernel may start its own set-up; it waits for this one to end
+  // before it reads anything this one writes
+  pdl_release();
 
   if (warp == 0) {
-    // producer: the staged activations (one 16 KB block) and each row
-    // block's codes (512 B) and scales (64 B) of the step
+    // producer: the staged activations (a hi and a lo 16 KB block) and each
+    // row block's codes (512 B) and scales (64 B) of the step.  The weights
+    // of the first steps are requested before the wait on the kernel ahead
+    // (the stage that writes the activations); nothing else is.
     const uint64_t policy = l2_evict_last();  // both are read again by the other tiles
-    for (int k = 0; k < nk; ++k) {
+    auto weights = [&](int k) {
       const int s = k % LG_STAGES, c = c_lo + k;
-      if (k >= LG_STAGES) {
-        const bool ok = mbar_wait(&empty[s], (uint32_t)(((k / LG_STAGES) - 1) & 1), failed ? 1 : LG_TRIES);
-        if (__any_sync(0xffffffffu, !ok)) failed = true;
-      }
       uint8_t *st = base + s * LG_STAGE_BYTES;
-      if (lane == 0)
-        mbar_expect(&full[s], (uint32_t)(2 * LG_A_BYTES + rbv * (512 + 64)));
+      if (lane == 0) mbar_expect(&full[s], (uint32_t)(2 * LG_A_BYTES + rbv * (512 + 64)));
       __syncwarp();
-      if (lane < 2) {  // the activations' hi and lo blocks of this step
-        const uint4 *src = a.a_tiles + (((size_t)mt * a.n_cc + c) * 2 + lane) * (LG_A_BYTES / 16);
-        bulk_load(st + lane * LG_A_BYTES, src, LG_A_BYTES, &full[s], policy);
-      }
       if (lane < rbv) {
         const size_t tile = (size_t)(rb0 + lane) * a.n_cc + c;
         bulk_load(st + LG_OFF_CODES + lane * 512, a.tiles + tile * 32, 512, &full[s], policy);
         bulk_load(st + LG_OFF_SCALES + lane * 64, a.scales + tile * 8, 64, &full[s], policy);
       }
+    };
+    auto acts = [&](int k) {
+      const int s = k % LG_STAGES, c = c_lo + k;
+      uint8_t *st = base + s * LG_STAGE_BYTES;
+      if (lane < 2) {  // the activations' hi and lo blocks of this step
+        const uint4 *src = a.a_tiles + (((size_t)mt * a.n_cc + c) * 2 + lane) * (LG_A_BYTES / 16);
+        bulk_load(st + lane * LG_A_BYTES, src, LG_A_BYTES, &full[s], policy);
+      }
+    };
+    const int first = nk < LG_STAGES ? nk : LG_STAGES;
+    for (int k = 0; k < first; ++k) weights(k);
+    pdl_wait();
+    for (int k = 0; k < first; ++k) acts(k);
+    for (int k = first; k < nk; ++k) {
+      const int s = k % LG_STAGES;
+      const bool ok = mbar_wait(&empty[s], (uint32_t)(((k / LG_STAGES) - 1) & 1), failed ? 1 : LG_TRIES);
+      if (__any_sync(0xffffffffu, !ok)) failed = true;
+      weights(k);
+      acts(k);
     }
   } else if (warp == 1) {
     // the MMA issuer: four K=16 products a 64-column step
@@ -267,11 +283,13 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
       fence_async_smem();  // the weights written here are read by the tensor core (async proxy)
       mbar_arrive(&bfull[s]);
     }
-    // epilogue: this warp's quarter of the tile's lanes
+    // epilogue: this warp's quarter of the tile's lanes (the wait returns at
+    // once: the accumulators needed the activations the kernel ahead wrote)
     {
       const bool ok = mbar_wait(accf, 0u, failed ? 1 : LG_TRIES);
       if (__any_sync(0xffffffffu, !ok)) failed = true;
     }
+    pdl_wait();
     tc_fence_after();
     const int q = warp & 3;  // the tensor-memory lanes this warp may read
     const int m_local = q * 32 + lane, m = mt * LG_M + m_local;
@@ -367,6 +385,8 @@ __device__ __forceinline__ float slice_sum(const LaneStageArgs &a, int j, int i)
 __global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
   extern __shared__ float ls_row[];  // the lane's staged values (cols floats), then the residual's
   __shared__ float red[32];
+  pdl_release();
+  pdl_wait();  // every input comes from kernels ahead; the operand blocks are still read by the one just ahead
   const int j = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   float *y = ls_row;
   const int n = a.cols;
@@ -436,6 +456,8 @@ __global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
 
 // The output head's argmax partials merged per lane (first index on a tie).
 __global__ void lane_argmax_kernel(const float *val, const int *idx, int parts, int lanes, int32_t *top) {
+  pdl_release();
+  pdl_wait();
   const int j = blockIdx.x, tid = threadIdx.x;
   __shared__ float sv[256];
   __shared__ int si[256];
@@ -469,6 +491,8 @@ __global__ void lane_argmax_kernel(const float *val, const int *idx, int parts, 
 // K-slice partials added in order: out[j][i] = sum_z p[z][j][i].
 __global__ void lane_sum_kernel(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride) {
+  pdl_release();
+  pdl_wait();
   const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long)lanes * cols) return;
   const int j = (int)(idx / cols), i = (int)(idx - (long)j * cols);
@@ -480,6 +504,25 @@ __global__ void lane_sum_kernel(const float *p, int splits, int lanes, int cols,
 }  // namespace igc
 
 using namespace igc;
+
+// A launch that may overlap the kernel ahead of it (programmatic dependent
+// launch) while the calling thread has that turned on (igc_kernels_pdl);
+// every kernel here waits for the one ahead before it reads its results.
+template <typename... KArgs, typename... Args>
+static cudaError_t lane_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = igc_kernels_pdl_get() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 extern "C" {
 
@@ -499,20 +542,20 @@ cudaError_t igc_launch_lane_stage(const LaneStageArgs *a, cudaStream_t st) {
   if (a->lanes < 1 || a->cols < 1 || a->cols > a->n_cc * 64) return cudaErrorInvalidValue;
   const size_t smem = igc_lane_stage_smem(a->mode, a->cols);
   if (smem > LS_SMEM_LIMIT) return cudaErrorInvalidValue;
-  lane_stage_kernel<<<a->lanes, 256, smem, st>>>(*a);
-  return cudaGetLastError();
+  return lane_launch(lane_stage_kernel, dim3(a->lanes), dim3(256), smem, st, *a);
 }
 
 // Positions of a prefill chunk's 16-lane attention groups: out[i] = p0 + 16 i.
 __global__ void lane_positions_kernel(const int *p0, int groups, int *out) {
+  pdl_release();
+  pdl_wait();
   const int i = threadIdx.x;
   if (i < groups) out[i] = *p0 + 16 * i;
 }
 
 cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st) {
   if (groups < 1 || groups > 1024) return cudaErrorInvalidValue;
-  lane_positions_kernel<<<1, 1024, 0, st>>>(p0, groups, out);
-  return cudaGetLastError();
+  return lane_launch(lane_positions_kernel, dim3(1), dim3(1024), 0, st, p0, groups, out);
 }
 
 int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count) {
@@ -526,22 +569,20 @@ cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
   if (a->lanes < 1 || a->split < 1 || a->split > a->n_cc || a->n_rb < 1) return cudaErrorInvalidValue;
   if (a->arg_val && (a->split != 1 || !a->arg_idx)) return cudaErrorInvalidValue;
   dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
-  lane_gemm_kernel<<<grid, LG_THREADS, LG_SMEM, st>>>(*a);
-  return cudaGetLastError();
+  return lane_launch(lane_gemm_kernel, grid, dim3(LG_THREADS), (size_t)LG_SMEM, st, *a);
 }
 
 cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,
                                    cudaStream_t st) {
   if (lanes < 1 || parts < 1) return cudaErrorInvalidValue;
-  lane_argmax_kernel<<<lanes, 256, 0, st>>>(val, idx, parts, lanes, top);
-  return cudaGetLastError();
+  return lane_launch(lane_argmax_kernel, dim3(lanes), dim3(256), 0, st, val, idx, parts, lanes, top);
 }
 
 cudaError_t igc_launch_lane_sum(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride, cudaStream_t st) {
   const long n = (long)lanes * cols;
-  lane_sum_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(p, splits, lanes, cols, p_stride, out, out_stride);
-  return cudaGetLastError();
+  return lane_launch(lane_sum_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, p, splits, lanes, cols,
+                     p_stride, out, out_stride);
 }
 
 }  // extern "C"

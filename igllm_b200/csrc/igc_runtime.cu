@@ -1578,13 +1578,17 @@ static int chunks_ready(igc_session *s) {
 static int enqueue_chunk(igc_session *s, int M) {
   igc_model *m = s->m;
   auto &C = s->ch;
-  PdlScope pdl(false);
+  // kernels overlap the one ahead (each waits before reading its results),
+  // except the attention groups: a group copies cached rows before its wait,
+  // and those rows are the previous group's own writes
+  PdlScope pdl(s->use_pdl != 0);
   const int groups = (M + 15) / 16;
   CKL(igc_launch_lane_positions(C.d_ids, groups, C.d_pos, s->st));
   LaneRun r{m, s->st, &C.B, s->d_err, M};
   auto attend = [&](int l, const DevLayer &L) -> int {
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
+    igc_kernels_pdl(0);
     for (int gi = 0; gi < groups; ++gi) {
       const int j0 = gi * 16, n = M - j0 < 16 ? M - j0 : 16;
       CKL(igc_launch_attn(C.B.qkv + (size_t)j0 * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
@@ -1592,6 +1596,7 @@ static int enqueue_chunk(igc_session *s, int M) {
                           s->vc[owner], L.kind == 0 ? 1 : 0, m->slide_span, C.d_pos + gi, n, s->attn_cluster,
                           C.B.attn + (size_t)j0 * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
     }
+    igc_kernels_pdl(s->use_pdl != 0);
     return IGC_OKAY;
   };
   return lane_stack(r, C.d_ids + 1, attend);
@@ -1733,6 +1738,10 @@ extern "C" int igc_session_guess_keep(igc_session *s, int keep) { /* app_core.c:
 // by the crowd's capacity, so a session's results do not depend on how many
 // sessions share its round.
 
+// Attention blocks a cluster in a crowd round: with many sessions in one
+// launch, clusters of 8 take half the blocks (and waves) clusters of 16 do.
+constexpr int IGC_CROWD_CLUSTER = 8;
+
 struct igc_crowd {
   igc_model *m = nullptr;
   cudaStream_t st = nullptr;
@@ -1800,7 +1809,9 @@ extern "C" void igc_crowd_close(igc_crowd *cr) { delete cr; }
 
 static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
   igc_model *m = cr->m;
-  PdlScope pdl(false);
+  // kernels overlap the one ahead (each waits before reading its results;
+  // attention copies only rows written by earlier rounds before its wait)
+  PdlScope pdl(true);
   const int k = cr->k;
   LaneRun r{m, cr->st, &cr->B, cr->d_top + cr->lanes, S * k};
   auto attend = [&](int l, const DevLayer &L) -> int {
@@ -1808,7 +1819,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
     const DevLayer &O = m->layer[owner];
     CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                              m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr, L.kind == 0 ? 1 : 0,
-                             m->slide_span, cr->pos(), k, 16, cr->B.attn, L.q_rows, nullptr, nullptr,
+                             m->slide_span, cr->pos(), k, IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr, nullptr,
                              cr->kc() + (size_t)l * cr->cap, cr->vc() + (size_t)l * cr->cap, cr->pos(), S, cr->st));
     return IGC_OKAY;
   };
