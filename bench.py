@@ -456,6 +456,9 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(1000.0 * total_s / args.steps, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int4 weights, f16 hi/lo activations, f32 accumulate",
         "data": "synthetic (seeded E2B-shaped weights, BASELINE config 0 prompt)",
+        "weights": "BASELINE's distributions (int4 codes uniform in [-8,7], f16 scales |N(0,0.02)|, bf16 norms and "
+                   "embeddings N(0,0.02)) drawn by a counter-based splitmix64 generator over a normal quantile "
+                   "table, not numpy PCG64 (the same bits in HBM and in the reference's safetensors file)",
         "config": {"workload": "E2B int4 g32 greedy --guess 4 verify rounds, 1024-id prompt, 256 tokens (config 0)",
                    "proposer": "always-right (reference guess bracket's oracle); n-gram scout reported beside",
                    "l2": "weights 938 MB per round, larger than the 126 MB L2",
@@ -616,9 +619,9 @@ def run_profile_case(args):
     cuProfilerStart and cuProfilerStop: a profiler started with
     --profile-from-start off sees those launches only."""
     import igllm_b200 as ig
-    spec = ig.spec_e2b(seed=1, window_limit=4096)
+    spec = ig.spec_e2b(seed=1, window_limit=args.case_window)
     spec.vocab = args.case_vocab
-    model = ig.Model(spec=spec, device=0, window_limit=4096)
+    model = ig.Model(spec=spec, device=0, window_limit=args.case_window)
     rng = np.random.default_rng(0)
     if args.case_streams > 0:
         # crowd rounds: `--case-streams` sessions primed to `--case-context`
@@ -668,6 +671,7 @@ def main():
     ap.add_argument("--case-rounds", type=int, default=3)
     ap.add_argument("--case-context", type=int, default=1024)
     ap.add_argument("--case-streams", type=int, default=0, help="profile crowd rounds of this many sessions")
+    ap.add_argument("--case-window", type=int, default=4096, help="positions each session's caches hold")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)
