@@ -20,7 +20,8 @@
 //                       scales) of each 64-column step from this GPU's HBM
 //                       into a three-deep shared-memory ring; four warps turn
 //                       the codes into f16 hi/lo weights, (code - 8) * scale,
-//                       in the operand layout; one thread issues the step's
+//                       in the operand layout (eight warps, one 16-byte tile
+//                       slot each); one thread issues the step's
 //                       twelve tcgen05.mma (M 128, N 128, K 16, f32
 //                       accumulate in TMEM) and commits them to the ring
 //                       slot's barrier; at
@@ -137,7 +138,8 @@ constexpr int LG_OFF_B = 2 * LG_A_BYTES, LG_OFF_CODES = LG_OFF_B + 2 * LG_B_BYTE
 constexpr int LG_STAGE_BYTES = (LG_OFF_SCALES + LG_SCALE_BYTES + 1023) / 1024 * 1024;  // 69 KB
 constexpr int LG_BAR_BYTES = 256;
 constexpr int LG_SMEM = 1024 + LG_STAGES * LG_STAGE_BYTES + LG_BAR_BYTES;  // + alignment slack
-constexpr int LG_THREADS = 192;
+constexpr int LG_DQ_WARPS = 8;  // warps that turn codes into weights (then run the epilogue)
+constexpr int LG_THREADS = 64 + 32 * LG_DQ_WARPS;
 constexpr int LG_TRIES = 1 << 22;  // polls a wait makes before it gives up
 
 __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a) {
@@ -155,7 +157,7 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
   if (tid == 0) {
     for (int s = 0; s < LG_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&bfull[s], 128);
+      mbar_init(&bfull[s], 32 * LG_DQ_WARPS);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accf, 1);
@@ -238,8 +240,9 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
     if (lane == 0) tc_commit(accf);
     __syncwarp();
   } else {
-    // warps 2-5: codes to f16 weights in the operand layout, then the epilogue
-    const int dt = tid - 64;  // 0..127
+    // warps 2-9: codes to f16 hi/lo weights in the operand layout (one
+    // 16-byte thread slot of one row block's tile each), then the epilogue
+    const int dt = tid - 64;  // 0..255: row block dt / 32, thread slot dt % 32
     for (int k = 0; k < nk; ++k) {
       const int s = k % LG_STAGES;
       const uint32_t ph = (uint32_t)((k / LG_STAGES) & 1);
@@ -251,9 +254,8 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
       const uint2 *scs = reinterpret_cast<const uint2 *>(st + LG_OFF_SCALES);
       // the slot was refilled only after the MMA of the step three back (which
       // read these weight blocks) committed, and this warp waited on the refill
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int slot = dt + 128 * j, rbl = slot >> 5, ts = slot & 31, g = ts >> 2, tq = ts & 3;
+      {
+        const int rbl = dt >> 5, ts = dt & 31, g = ts >> 2, tq = ts & 3;
         const int n0 = rbl * 16 + g, n8 = n0 + 8;
         const bool have = rbl < rbv;
         const uint4 w = have ? codes[rbl * 32 + ts] : make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);
@@ -267,13 +269,15 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
           dequant_i4(words[kb], q);
           const uint32_t sg = kb < 2 ? sc.x : sc.y;  // f16 scales of rows g (low half) and g+8 (high half)
           const __half2 s2 = *reinterpret_cast<const __half2 *>(&sg);
-          const float sr[2] = {__low2float(s2), __high2float(s2)};
+          const __half2 sr[2] = {__low2half2(s2), __high2half2(s2)};
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
+            // hi = the product rounded to f16; lo = the exact remainder (a
+            // 4-bit integer times an f16 needs at most 15 significant bits,
+            // so the fused multiply-add's one rounding leaves it as it is)
             const __half2 c2 = *reinterpret_cast<const __half2 *>(&q[r]);
-            const float p0 = __low2float(c2) * sr[r & 1], p1 = __high2float(c2) * sr[r & 1];  // exact in f32
-            const __half2 hi = __floats2half2_rn(p0, p1);
-            const __half2 lo = __floats2half2_rn(p0 - __low2float(hi), p1 - __high2float(hi));
+            const __half2 hi = __hmul2(c2, sr[r & 1]);
+            const __half2 lo = __hfma2(c2, sr[r & 1], __hneg2(hi));
             const uint32_t off = lg_swz((r & 1) ? n8 : n0, 2 * kb + (r >> 1)) + 4 * tq;
             *reinterpret_cast<__half2 *>(bh + off) = hi;
             *reinterpret_cast<__half2 *>(bl + off) = lo;
@@ -291,7 +295,9 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
     }
     pdl_wait();
     tc_fence_after();
-    const int q = warp & 3;  // the tensor-memory lanes this warp may read
+    // a warp may read the tensor-memory lanes of its quarter (warp mod 4):
+    // warps 2-5 take columns 0-63 of their lanes, warps 6-9 columns 64-127
+    const int q = warp & 3, c_first = warp < 6 ? 0 : LG_N / 2;
     const int m_local = q * 32 + lane, m = mt * LG_M + m_local;
     const bool live = m < a.lanes;
     const float f = live ? a.factor[m] : 0.0f;
@@ -300,7 +306,7 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
     float best = -FLT_MAX;
     int best_i = 0x7fffffff;
     float *orow = a.out ? a.out + ((size_t)z * a.lanes + (live ? m : 0)) * a.out_stride : nullptr;
-    for (int c0 = 0; c0 < LG_N; c0 += 32) {
+    for (int c0 = c_first; c0 < c_first + LG_N / 2; c0 += 32) {
       const int n0 = nt * LG_N + c0;
       if (n0 >= n_rows) break;  // warp-uniform
       float v[32];
@@ -335,9 +341,27 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
         }
       }
     }
-    if (argm && live) {
-      a.arg_val[(size_t)nt * a.lanes + m] = best;
-      a.arg_idx[(size_t)nt * a.lanes + m] = best_i;
+    if (argm) {
+      // the two warps of a lane quarter meet in shared memory (the ring is
+      // idle now: every product has completed); the column half 0 warp keeps
+      // the first index on a tie
+      float *bv = reinterpret_cast<float *>(base);
+      int *bi = reinterpret_cast<int *>(base + LG_M * sizeof(float));
+      if (c_first != 0) {
+        bv[m_local] = best;
+        bi[m_local] = best_i;
+      }
+      named_sync(1, 32 * LG_DQ_WARPS);
+      if (c_first == 0 && live) {
+        const float ov = bv[m_local];
+        const int oi = bi[m_local];
+        if (ov > best || (ov == best && oi < best_i)) {
+          best = ov;
+          best_i = oi;
+        }
+        a.arg_val[(size_t)nt * a.lanes + m] = best;
+        a.arg_idx[(size_t)nt * a.lanes + m] = best_i;
+      }
     }
     tc_fence_before();
   }
