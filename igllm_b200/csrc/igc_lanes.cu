@@ -512,6 +512,229 @@ __global__ void lane_argmax_kernel(const float *val, const int *idx, int parts, 
   if (tid == 0) top[j] = si[0];
 }
 
+// ---------------------------------------------------------------------------
+// attention of the batched-lane passes (app_core.c:11415-11578
+// session_attend / session_attend_group), in f32 on the CUDA cores: at a
+// handful of query rows per cached row the work is the cache's bytes.
+
+constexpr int LA_ROWS = 32;  // query rows a split block: a group's lanes x the heads of one key/value head
+constexpr int LA_TPR = 8;    // threads a row (each holds hd / 8 dimensions: d = s + 8 k)
+constexpr int LA_TILE = 16;  // cached positions a tile
+
+__device__ __forceinline__ int la_pos(const LaneAttnArgs &a, int g) {
+  return a.pos_tab[(size_t)g * a.pos_stride] + g * a.pos_step;
+}
+
+__device__ __forceinline__ void la_cp16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void la_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void la_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// One block a lane: its queries normed (q_norm) and turned at its position,
+// and on an owner layer its keys normed (k_norm) and turned and its values
+// normed (no weight), written to the cache (app_core.c:11480-11512).  A warp
+// a head row; a lane holds dimensions d and d + hd/2 for d = lane + 32 e.
+__global__ void __launch_bounds__(256) lane_qk_kernel(LaneAttnArgs a) {
+  pdl_release();
+  pdl_wait();
+  const int j = blockIdx.x, g = j / a.group_lanes, i = j - g * a.group_lanes;
+  const int p = la_pos(a, g) + i;
+  float *kc = a.kc_tab ? a.kc_tab[g] : a.kc, *vc = a.vc_tab ? a.vc_tab[g] : a.vc;
+  const int hd = a.hd, half = hd / 2, kv_w = a.kv_heads * hd;
+  const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const float *row = a.qkv + (size_t)j * a.qkv_stride;
+  const float *cs = a.cs + (size_t)p * half, *sn = a.sn + (size_t)p * half;
+  const int n_items = a.heads + (a.owner ? 2 * a.kv_heads : 0);
+  for (int it = warp; it < n_items; it += 8) {
+    const float *src, *w;
+    float *dst;
+    bool turn = true;
+    if (it < a.heads) {
+      src = row + (size_t)it * hd;
+      dst = a.qbuf + (size_t)j * a.heads * hd + (size_t)it * hd;
+      w = a.q_norm;
+    } else if (it < a.heads + a.kv_heads) {
+      const int kh = it - a.heads;
+      src = row + (size_t)a.heads * hd + (size_t)kh * hd;
+      dst = kc + (size_t)p * kv_w + (size_t)kh * hd;
+      w = a.k_norm;
+    } else {
+      const int kh = it - a.heads - a.kv_heads;
+      src = row + (size_t)a.heads * hd + kv_w + (size_t)kh * hd;
+      dst = vc + (size_t)p * kv_w + (size_t)kh * hd;
+      w = nullptr;
+      turn = false;
+    }
+    float lo[4], hi[4], ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = l + 32 * e;
+      lo[e] = d < half ? src[d] : 0.0f;
+      hi[e] = d < half ? src[d + half] : 0.0f;
+      ss += lo[e] * lo[e] + hi[e] * hi[e];
+    }
+    const float sh = rms_shrink(warp_sum(ss), hd, a.eps);  // app_core.c:4667 kern_norm_rms
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = l + 32 * e;
+      if (d >= half) continue;
+      float x = lo[e] * sh, y = hi[e] * sh;
+      if (w) {
+        x *= w[d];
+        y *= w[d + half];
+      }
+      if (turn) {  // app_core.c:5196 kern_rope_turn: pairs (d, d + hd/2)
+        const float c = cs[d], sv = sn[d];
+        const float x2 = x * c - y * sv, y2 = y * c + x * sv;
+        x = x2;
+        y = y2;
+      }
+      dst[d] = x;
+      dst[d + half] = y;
+    }
+  }
+}
+
+// One block a (group, key/value head, split of positions): the group's query
+// rows against the split's cached rows, scores scaled by 1 (app_core.c:11314),
+// each lane masked to its own window, an online softmax, and the split's
+// weighted values, row maximum and total left for the merge.
+__global__ void __launch_bounds__(256) lane_attn_kernel(LaneAttnArgs a) {
+  extern __shared__ __align__(16) float la_sm[];  // two tiles: keys [16][hd], values [16][hd]
+  pdl_release();
+  pdl_wait();
+  const int gk = blockIdx.x, g = gk / a.kv_heads, kh = gk - g * a.kv_heads, z = blockIdx.y;
+  const int G = a.heads / a.kv_heads, hd = a.hd, kv_w = a.kv_heads * hd;
+  const int n_l = min(a.group_lanes, a.lanes - g * a.group_lanes);
+  const int p0 = la_pos(a, g), p_last = p0 + n_l - 1;
+  const int lo_all = a.sliding ? max(0, p0 - a.span + 1) : 0;
+  const int n_split = (p_last + 1 - lo_all + a.split_pos - 1) / a.split_pos;
+  if (z >= n_split) return;  // the whole block: this split lies past the group's positions
+  const int a0 = lo_all + z * a.split_pos, a1 = min(p_last + 1, a0 + a.split_pos);
+  const float *kc = (a.kc_tab ? a.kc_tab[g] : a.kc) + (size_t)kh * hd;
+  const float *vc = (a.vc_tab ? a.vc_tab[g] : a.vc) + (size_t)kh * hd;
+  const int tid = threadIdx.x, r = tid / LA_TPR, sl = tid % LA_TPR, DPT = hd / LA_TPR;
+  const int rows = n_l * G;
+  const bool live = r < rows;
+  const int li = live ? r / G : 0, h = kh * G + (live ? r % G : 0);
+  const int p_me = p0 + li, lo_me = a.sliding ? max(0, p_me - a.span + 1) : 0;
+  float q[32], acc[32];
+  const float *qr = a.qbuf + ((size_t)(g * a.group_lanes + li) * a.heads + h) * hd;
+#pragma unroll
+  for (int k = 0; k < 32; ++k) {
+    q[k] = (live && k < DPT) ? qr[sl + LA_TPR * k] : 0.0f;
+    acc[k] = 0.0f;
+  }
+  float m_run = -FLT_MAX, l_run = 0.0f;
+  const int tile_f = LA_TILE * hd;  // floats of one tile's keys (or values)
+  const int n_tiles = (a1 - a0 + LA_TILE - 1) / LA_TILE, c4 = hd / 4;
+  auto issue = [&](int ti) {
+    float *kt = la_sm + (ti & 1) * 2 * tile_f, *vt = kt + tile_f;
+    const int tb = a0 + ti * LA_TILE;
+    for (int e = tid; e < LA_TILE * c4; e += blockDim.x) {
+      const int u = e / c4, c = (e - u * c4) * 4, t = tb + u;
+      if (t < a1) {
+        la_cp16(kt + u * hd + c, kc + (size_t)t * kv_w + c);
+        la_cp16(vt + u * hd + c, vc + (size_t)t * kv_w + c);
+      }
+    }
+    la_commit();
+  };
+  issue(0);
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    if (ti + 1 < n_tiles) {
+      issue(ti + 1);
+      la_wait<1>();
+    } else {
+      la_wait<0>();
+    }
+    __syncthreads();
+    const float *kt = la_sm + (ti & 1) * 2 * tile_f, *vt = kt + tile_f;
+    const int tb = a0 + ti * LA_TILE;
+    float sc[LA_TILE];
+    float mt = -FLT_MAX;
+#pragma unroll
+    for (int u = 0; u < LA_TILE; ++u) {
+      const float *kr = kt + u * hd + sl;
+      float part = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 32; ++k)
+        if (k < DPT) part = fmaf(q[k], kr[LA_TPR * k], part);
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      part += __shfl_xor_sync(0xffffffffu, part, 4);
+      const int t = tb + u;
+      const bool ok = live && t < a1 && t >= lo_me && t <= p_me;
+      sc[u] = ok ? part : -FLT_MAX;
+      mt = fmaxf(mt, sc[u]);
+    }
+    const float m_new = fmaxf(m_run, mt);
+    if (m_new > -FLT_MAX) {
+      const float f = m_run > -FLT_MAX ? expf(m_run - m_new) : 0.0f;
+      float tot = 0.0f;
+#pragma unroll
+      for (int u = 0; u < LA_TILE; ++u) {
+        sc[u] = sc[u] > -FLT_MAX ? expf(sc[u] - m_new) : 0.0f;
+        tot += sc[u];
+      }
+      l_run = l_run * f + tot;
+      m_run = m_new;
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        if (k >= DPT) continue;
+        float v = acc[k] * f;
+#pragma unroll
+        for (int u = 0; u < LA_TILE; ++u) v = fmaf(sc[u], vt[u * hd + sl + LA_TPR * k], v);
+        acc[k] = v;
+      }
+    }
+    __syncthreads();  // the buffer is refilled two tiles on
+  }
+  if (live) {
+    float *pr = a.part + (((size_t)gk * a.max_splits + z) * LA_ROWS + r) * (hd + 2);
+#pragma unroll
+    for (int k = 0; k < 32; ++k)
+      if (k < DPT) pr[sl + LA_TPR * k] = acc[k];
+    if (sl == 0) {
+      pr[hd] = m_run;
+      pr[hd + 1] = l_run;
+    }
+  }
+}
+
+// One block a (group, key/value head): the splits of every row merged in
+// split order into the lanes' attention output.
+__global__ void __launch_bounds__(256) lane_attn_merge_kernel(LaneAttnArgs a) {
+  pdl_release();
+  pdl_wait();
+  const int gk = blockIdx.x, g = gk / a.kv_heads, kh = gk - g * a.kv_heads;
+  const int G = a.heads / a.kv_heads, hd = a.hd;
+  const int n_l = min(a.group_lanes, a.lanes - g * a.group_lanes);
+  const int p0 = la_pos(a, g), p_last = p0 + n_l - 1;
+  const int lo_all = a.sliding ? max(0, p0 - a.span + 1) : 0;
+  const int n_split = (p_last + 1 - lo_all + a.split_pos - 1) / a.split_pos;
+  const int rows = n_l * G;
+  for (int e = threadIdx.x; e < rows * hd; e += blockDim.x) {
+    const int r = e / hd, d = e - r * hd, li = r / G, h = kh * G + r % G;
+    const float *pr = a.part + ((size_t)gk * a.max_splits * LA_ROWS + r) * (hd + 2);
+    const size_t zs = (size_t)LA_ROWS * (hd + 2);
+    float M = -FLT_MAX;
+    for (int z = 0; z < n_split; ++z) M = fmaxf(M, pr[z * zs + hd]);
+    float L = 0.0f, o = 0.0f;
+    for (int z = 0; z < n_split; ++z) {
+      const float mz = pr[z * zs + hd];
+      const float w = mz > -FLT_MAX ? expf(mz - M) : 0.0f;
+      L = fmaf(pr[z * zs + hd + 1], w, L);
+      o = fmaf(pr[z * zs + d], w, o);
+    }
+    a.out[(size_t)(g * a.group_lanes + li) * a.out_stride + (size_t)h * hd + d] = o / L;
+  }
+}
+
 // K-slice partials added in order: out[j][i] = sum_z p[z][j][i].
 __global__ void lane_sum_kernel(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride) {
@@ -559,6 +782,9 @@ constexpr int LS_SMEM_LIMIT = 160 * 1024;  // a stage row (and a residual's part
 cudaError_t igc_lanes_configure(void) {
   cudaError_t e = cudaFuncSetAttribute(lane_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LS_SMEM_LIMIT);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(lane_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LG_SMEM);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(lane_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(sizeof(float) * 4 * LA_TILE * 256));
   return e;
 }
 
@@ -569,18 +795,7 @@ cudaError_t igc_launch_lane_stage(const LaneStageArgs *a, cudaStream_t st) {
   return lane_launch(lane_stage_kernel, dim3(a->lanes), dim3(256), smem, st, *a);
 }
 
-// Positions of a prefill chunk's 16-lane attention groups: out[i] = p0 + 16 i.
-__global__ void lane_positions_kernel(const int *p0, int groups, int *out) {
-  pdl_release();
-  pdl_wait();
-  const int i = threadIdx.x;
-  if (i < groups) out[i] = *p0 + 16 * i;
-}
 
-cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st) {
-  if (groups < 1 || groups > 1024) return cudaErrorInvalidValue;
-  return lane_launch(lane_positions_kernel, dim3(1), dim3(1024), 0, st, p0, groups, out);
-}
 
 int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count) {
   const int tiles = ((n_rb + LG_RB - 1) / LG_RB) * ((lanes + LG_M - 1) / LG_M);
@@ -594,6 +809,23 @@ cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
   if (a->arg_val && (a->split != 1 || !a->arg_idx)) return cudaErrorInvalidValue;
   dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
   return lane_launch(lane_gemm_kernel, grid, dim3(LG_THREADS), (size_t)LG_SMEM, st, *a);
+}
+
+size_t igc_lane_attn_smem(int hd) { return sizeof(float) * 4 * LA_TILE * (size_t)hd; }
+
+cudaError_t igc_launch_lane_attn(const LaneAttnArgs *a, cudaStream_t st) {
+  const int G = a->kv_heads > 0 ? a->heads / a->kv_heads : 0;
+  if (a->hd % 32 || a->hd > 256 || G < 1 || a->heads % a->kv_heads || a->group_lanes * G > LA_ROWS ||
+      a->groups < 1 || a->lanes < 1 || a->lanes > a->groups * a->group_lanes || a->split_pos < LA_TILE ||
+      a->max_splits < 1)
+    return cudaErrorInvalidValue;
+  cudaError_t e = lane_launch(lane_qk_kernel, dim3(a->lanes), dim3(256), 0, st, *a);
+  if (e == cudaSuccess)
+    e = lane_launch(lane_attn_kernel, dim3(a->groups * a->kv_heads, a->max_splits), dim3(256),
+                    igc_lane_attn_smem(a->hd), st, *a);
+  if (e == cudaSuccess)
+    e = lane_launch(lane_attn_merge_kernel, dim3(a->groups * a->kv_heads), dim3(256), 0, st, *a);
+  return e;
 }
 
 cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,
