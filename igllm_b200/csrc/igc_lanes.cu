@@ -655,6 +655,7 @@ __global__ void __launch_bounds__(256) lane_attn_kernel(LaneAttnArgs a) {
     __syncthreads();
     const float *kt = la_sm + (ti & 1) * 2 * tile_f, *vt = kt + tile_f;
     const int tb = a0 + ti * LA_TILE;
+    const int nv = min(LA_TILE, a1 - tb);  // rows the tile holds: the rest of the buffer is stale
     float sc[LA_TILE];
     float mt = -FLT_MAX;
 #pragma unroll
@@ -668,7 +669,7 @@ __global__ void __launch_bounds__(256) lane_attn_kernel(LaneAttnArgs a) {
       part += __shfl_xor_sync(0xffffffffu, part, 2);
       part += __shfl_xor_sync(0xffffffffu, part, 4);
       const int t = tb + u;
-      const bool ok = live && t < a1 && t >= lo_me && t <= p_me;
+      const bool ok = live && u < nv && t >= lo_me && t <= p_me;
       sc[u] = ok ? part : -FLT_MAX;
       mt = fmaxf(mt, sc[u]);
     }
@@ -688,7 +689,8 @@ __global__ void __launch_bounds__(256) lane_attn_kernel(LaneAttnArgs a) {
         if (k >= DPT) continue;
         float v = acc[k] * f;
 #pragma unroll
-        for (int u = 0; u < LA_TILE; ++u) v = fmaf(sc[u], vt[u * hd + sl + LA_TPR * k], v);
+        for (int u = 0; u < LA_TILE; ++u)
+          if (u < nv) v = fmaf(sc[u], vt[u * hd + sl + LA_TPR * k], v);
         acc[k] = v;
       }
     }
