@@ -654,8 +654,19 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
                                                    const float *q_norm, const float *k_norm, const float *cs_tab,
                                                    const float *sn_tab, float eps, int owner, float *kc, float *vc,
                                                    int sliding, int span, const int *d_p0, int lanes, float *out,
-                                                   int out_stride, float *out_amax, unsigned long long *stamp) {
+                                                   int out_stride, float *out_amax, unsigned long long *stamp,
+                                                   float *const *kc_tab, float *const *vc_tab, const int *pos_tab) {
   using LY = AttnLayout<HD>;
+  if (kc_tab) {
+    // one of many sessions' blocks (blockIdx.z): its caches and position
+    // from the tables, its `lanes` rows of the batch's q|k|v and output
+    const int zb = blockIdx.z;
+    kc = kc_tab[zb];
+    vc = vc_tab[zb];
+    d_p0 = pos_tab + zb;
+    qkv += (size_t)zb * lanes * qkv_stride;
+    out += (size_t)zb * lanes * out_stride;
+  }
   constexpr int DPL = HD / 32, NKS = HD / 16, KPW = (NKS + 7) / 8, NNT = HD / 8, NPW = (NNT + 7) / 8;
   constexpr int KS = LY::KS, VS = LY::VS, QS = LY::QS, DS = HD / CX;
   static_assert(CX <= AT_MAX_CLUSTER && HD % CX == 0, "cluster size");
@@ -1506,7 +1517,8 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const fl
                                int kv_heads, const float *q_norm, const float *k_norm, const float *cs,
                                const float *sn, float eps, int owner, float *kc, float *vc, int sliding, int span,
                                const int *d_p0, int lanes, float *out, int out_stride, float *out_amax,
-                               unsigned long long *stamp) {
+                               unsigned long long *stamp, float *const *kc_tab, float *const *vc_tab,
+                               const int *pos_tab) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
@@ -1522,7 +1534,8 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const fl
   cfg.attrs = at;
   cfg.numAttrs = g_pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, attn_kernel<HD, CX>, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
-                            owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp);
+                            owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp, kc_tab,
+                            vc_tab, pos_tab);
 }
 }  // extern "C++"
 
@@ -1530,18 +1543,30 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
                             int out_stride, float *out_amax, unsigned long long *stamp, cudaStream_t st) {
-  if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads || (cluster != 8 && cluster != 16))
+  return igc_launch_attn_many(qkv, qkv_stride, heads, kv_heads, hd, q_norm, k_norm, cs, sn, eps, owner, kc, vc, sliding,
+                              span, d_p0, lanes, cluster, out, out_stride, out_amax, stamp, nullptr, nullptr, nullptr, 1,
+                              st);
+}
+
+cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
+                                 const float *q_norm, const float *k_norm, const float *cs, const float *sn, float eps,
+                                 int owner, float *kc, float *vc, int sliding, int span, const int *d_p0, int lanes,
+                                 int cluster, float *out, int out_stride, float *out_amax, unsigned long long *stamp,
+                                 float *const *kc_tab, float *const *vc_tab, const int *pos_tab, int batch,
+                                 cudaStream_t st) {
+  if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads || (cluster != 8 && cluster != 16) ||
+      batch < 1 || (batch > 1 && !kc_tab))
     return cudaErrorInvalidValue;
   const size_t smem = igc_attn_smem(hd);
   const int G = heads / kv_heads;
-  const dim3 grid(cluster, kv_heads * ((lanes * G + AT_ROWS - 1) / AT_ROWS));
+  const dim3 grid(cluster, kv_heads * ((lanes * G + AT_ROWS - 1) / AT_ROWS), batch);
 #define IGC_ATT(HD)                                                                                              \
   return cluster == 8 ? launch_attn<HD, 8>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                            sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,   \
-                                           out_amax, stamp)                                                       \
+                                           out_amax, stamp, kc_tab, vc_tab, pos_tab)                              \
                       : launch_attn<HD, 16>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                             sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,  \
-                                            out_amax, stamp);
+                                            out_amax, stamp, kc_tab, vc_tab, pos_tab);
   switch (hd) {
     case 32: IGC_ATT(32)
     case 64: IGC_ATT(64)

@@ -44,6 +44,16 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
                             int out_stride, float *out_amax, unsigned long long *stamp, cudaStream_t st);
+// The same for `batch` sessions' blocks of `lanes` lanes each in one launch
+// (blockIdx.z the session): session z's caches are kc_tab[z] / vc_tab[z],
+// its first position pos_tab[z], its rows of q|k|v and of the output follow
+// the sessions before it.
+cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
+                                 const float *q_norm, const float *k_norm, const float *cs, const float *sn, float eps,
+                                 int owner, float *kc, float *vc, int sliding, int span, const int *d_p0, int lanes,
+                                 int cluster, float *out, int out_stride, float *out_amax, unsigned long long *stamp,
+                                 float *const *kc_tab, float *const *vc_tab, const int *pos_tab, int batch,
+                                 cudaStream_t st);
 // `stamp_sum`, when given, gets each of the pass's `stamp_n` stamped launches'
 // spans added (igc_device.cuh stamp_begin / stamp_end).
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,

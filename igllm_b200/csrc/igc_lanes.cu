@@ -18,7 +18,7 @@
 //                       a producer warp bulk-copies the staged activations
 //                       and the packed int4 weights (with their f16 group
 //                       scales) of each 64-column step from this GPU's HBM
-//                       into a three-deep shared-memory ring; four warps turn
+//                       into a four-deep shared-memory ring; eight warps turn
 //                       the codes into f16 hi/lo weights, (code - 8) * scale,
 //                       in the operand layout (eight warps, one 16-byte tile
 //                       slot each); one thread issues the step's
@@ -125,19 +125,27 @@ __host__ __device__ __forceinline__ uint32_t lg_swz(int r, int j) {
 // ---------------------------------------------------------------------------
 // the GEMM
 
-constexpr int LG_STAGES = 3;
+// Two rings.  The copy ring holds what the producer brings from global
+// memory a step (the activations' hi and lo blocks, the row blocks' codes and
+// scales); a slot is refilled once the products that read its activations
+// have committed.  The weight ring holds the dequantised hi and lo weight
+// blocks; the dequant warps refill a slot once the products of the step two
+// back have committed.  Four copy slots let the copies run ahead of the
+// dequant and the products by four steps.
+constexpr int LG_RSTAGES = 4, LG_BSTAGES = 2;
 constexpr int LG_OP_BYTES = 128 * 64 * 2;       // one operand block: 128 rows x 64 columns of f16, 16 KB
 constexpr int LG_A_BYTES = LG_OP_BYTES;         // activations, hi (then lo)
 constexpr int LG_B_BYTES = LG_OP_BYTES;         // weights, hi (then lo)
 constexpr int LG_RB = LG_N / 16;                // row blocks a tile
 constexpr int LG_CODE_BYTES = LG_RB * 512;      // 4 KB
 constexpr int LG_SCALE_BYTES = LG_RB * 64;      // 512 B
-// a ring slot: A hi, A lo, B hi, B lo, codes, scales; a 1 KB multiple
-constexpr int LG_OFF_B = 2 * LG_A_BYTES, LG_OFF_CODES = LG_OFF_B + 2 * LG_B_BYTES,
-              LG_OFF_SCALES = LG_OFF_CODES + LG_CODE_BYTES;
-constexpr int LG_STAGE_BYTES = (LG_OFF_SCALES + LG_SCALE_BYTES + 1023) / 1024 * 1024;  // 69 KB
+// a copy slot: A hi, A lo, codes, scales, rounded to 1 KB; a weight slot: B hi, B lo
+constexpr int LG_OFF_CODES = 2 * LG_A_BYTES, LG_OFF_SCALES = LG_OFF_CODES + LG_CODE_BYTES;
+constexpr int LG_RSLOT = (LG_OFF_SCALES + LG_SCALE_BYTES + 1023) / 1024 * 1024;  // 37 KB
+constexpr int LG_BSLOT = 2 * LG_B_BYTES;                                          // 32 KB
+constexpr int LG_RING_BYTES = LG_RSTAGES * LG_RSLOT + LG_BSTAGES * LG_BSLOT;
 constexpr int LG_BAR_BYTES = 256;
-constexpr int LG_SMEM = 1024 + LG_STAGES * LG_STAGE_BYTES + LG_BAR_BYTES;  // + alignment slack
+constexpr int LG_SMEM = 1024 + LG_RING_BYTES + LG_BAR_BYTES;  // + alignment slack
 constexpr int LG_DQ_WARPS = 8;  // warps that turn codes into weights (then run the epilogue)
 constexpr int LG_THREADS = 64 + 32 * LG_DQ_WARPS;
 constexpr int LG_TRIES = 1 << 22;  // polls a wait makes before it gives up
@@ -145,9 +153,11 @@ constexpr int LG_TRIES = 1 << 22;  // polls a wait makes before it gives up
 __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a) {
   extern __shared__ __align__(1024) uint8_t lg_raw[];
   uint8_t *base = lg_raw + ((1024 - (smem_u32(lg_raw) & 1023)) & 1023);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(base + LG_STAGES * LG_STAGE_BYTES);
-  uint64_t *full = bars, *bfull = bars + LG_STAGES, *empty = bars + 2 * LG_STAGES, *accf = bars + 3 * LG_STAGES;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * LG_STAGES + 1);
+  uint8_t *bring = base + LG_RSTAGES * LG_RSLOT;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(base + LG_RING_BYTES);
+  uint64_t *full = bars, *rempty = full + LG_RSTAGES, *bfull = rempty + LG_RSTAGES, *bempty = bfull + LG_BSTAGES,
+           *accf = bempty + LG_BSTAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(accf + 1);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nt = blockIdx.x, mt = blockIdx.y, z = blockIdx.z;
@@ -155,15 +165,18 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
   const int rb0 = nt * LG_RB, rbv = min(LG_RB, a.n_rb - rb0);  // row blocks this tile holds
 
   if (tid == 0) {
-    for (int s = 0; s < LG_STAGES; ++s) {
+    for (int s = 0; s < LG_RSTAGES; ++s) {
       mbar_init(&full[s], 1);
+      mbar_init(&rempty[s], 1);
+    }
+    for (int s = 0; s < LG_BSTAGES; ++s) {
       mbar_init(&bfull[s], 32 * LG_DQ_WARPS);
-      mbar_init(&empty[s], 1);
+      mbar_init(&bempty[s], 1);
     }
     mbar_init(accf, 1);
     mbar_init_fence();
   }
-  if (warp == 1) {  // 256 columns of tensor memory: one f32 accumulator a tile column
+  if (warp == 1) {  // LG_N columns of tensor memory: one f32 accumulator a tile column
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
                  "r"(LG_N)
                  : "memory");
@@ -185,8 +198,8 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
     // (the stage that writes the activations); nothing else is.
     const uint64_t policy = l2_evict_last();  // both are read again by the other tiles
     auto weights = [&](int k) {
-      const int s = k % LG_STAGES, c = c_lo + k;
-      uint8_t *st = base + s * LG_STAGE_BYTES;
+      const int s = k % LG_RSTAGES, c = c_lo + k;
+      uint8_t *st = base + s * LG_RSLOT;
       if (lane == 0) mbar_expect(&full[s], (uint32_t)(2 * LG_A_BYTES + rbv * (512 + 64)));
       __syncwarp();
       if (lane < rbv) {
@@ -196,36 +209,35 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
       }
     };
     auto acts = [&](int k) {
-      const int s = k % LG_STAGES, c = c_lo + k;
-      uint8_t *st = base + s * LG_STAGE_BYTES;
+      const int s = k % LG_RSTAGES, c = c_lo + k;
+      uint8_t *st = base + s * LG_RSLOT;
       if (lane < 2) {  // the activations' hi and lo blocks of this step
         const uint4 *src = a.a_tiles + (((size_t)mt * a.n_cc + c) * 2 + lane) * (LG_A_BYTES / 16);
         bulk_load(st + lane * LG_A_BYTES, src, LG_A_BYTES, &full[s], policy);
       }
     };
-    const int first = nk < LG_STAGES ? nk : LG_STAGES;
+    const int first = nk < LG_RSTAGES ? nk : LG_RSTAGES;
     for (int k = 0; k < first; ++k) weights(k);
     pdl_wait();
     for (int k = 0; k < first; ++k) acts(k);
     for (int k = first; k < nk; ++k) {
-      const int s = k % LG_STAGES;
-      const bool ok = mbar_wait(&empty[s], (uint32_t)(((k / LG_STAGES) - 1) & 1), failed ? 1 : LG_TRIES);
+      const int s = k % LG_RSTAGES;
+      const bool ok = mbar_wait(&rempty[s], (uint32_t)(((k / LG_RSTAGES) - 1) & 1), failed ? 1 : LG_TRIES);
       if (__any_sync(0xffffffffu, !ok)) failed = true;
       weights(k);
       acts(k);
     }
   } else if (warp == 1) {
-    // the MMA issuer: four K=16 products a 64-column step
+    // the MMA issuer: twelve K=16 products a 64-column step
     for (int k = 0; k < nk; ++k) {
-      const int s = k % LG_STAGES;
-      const uint32_t ph = (uint32_t)((k / LG_STAGES) & 1);
-      bool ok = mbar_wait(&full[s], ph, failed ? 1 : LG_TRIES);
-      ok = mbar_wait(&bfull[s], ph, (failed || !ok) ? 1 : LG_TRIES) && ok;
+      const int r = k % LG_RSTAGES, b = k % LG_BSTAGES;
+      bool ok = mbar_wait(&full[r], (uint32_t)((k / LG_RSTAGES) & 1), failed ? 1 : LG_TRIES);
+      ok = mbar_wait(&bfull[b], (uint32_t)((k / LG_BSTAGES) & 1), (failed || !ok) ? 1 : LG_TRIES) && ok;
       if (__any_sync(0xffffffffu, !ok)) failed = true;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t ah = smem_u32(base + s * LG_STAGE_BYTES), al = ah + LG_A_BYTES;
-        const uint32_t bh = ah + LG_OFF_B, bl = bh + LG_B_BYTES;
+        const uint32_t ah = smem_u32(base + r * LG_RSLOT), al = ah + LG_A_BYTES;
+        const uint32_t bh = smem_u32(bring + b * LG_BSLOT), bl = bh + LG_B_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint32_t o = kk * 32;  // 16 columns further along K inside the swizzled rows
@@ -233,7 +245,8 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
           tc_mma(tmem, lg_desc(al + o), lg_desc(bh + o), 1u);
           tc_mma(tmem, lg_desc(ah + o), lg_desc(bl + o), 1u);
         }
-        tc_commit(&empty[s]);
+        tc_commit(&rempty[r]);  // both slots are free once these products complete
+        tc_commit(&bempty[b]);
       }
       __syncwarp();
     }
@@ -244,16 +257,15 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
     // 16-byte thread slot of one row block's tile each), then the epilogue
     const int dt = tid - 64;  // 0..255: row block dt / 32, thread slot dt % 32
     for (int k = 0; k < nk; ++k) {
-      const int s = k % LG_STAGES;
-      const uint32_t ph = (uint32_t)((k / LG_STAGES) & 1);
-      const bool ok = mbar_wait(&full[s], ph, failed ? 1 : LG_TRIES);
+      const int rs = k % LG_RSTAGES, b = k % LG_BSTAGES;
+      bool ok = mbar_wait(&full[rs], (uint32_t)((k / LG_RSTAGES) & 1), failed ? 1 : LG_TRIES);
+      if (k >= LG_BSTAGES)  // the products of the step two back have read this weight slot
+        ok = mbar_wait(&bempty[b], (uint32_t)(((k / LG_BSTAGES) - 1) & 1), (failed || !ok) ? 1 : LG_TRIES) && ok;
       if (__any_sync(0xffffffffu, !ok)) failed = true;
-      uint8_t *st = base + s * LG_STAGE_BYTES;
-      uint8_t *bh = st + LG_OFF_B, *bl = bh + LG_B_BYTES;
+      uint8_t *st = base + rs * LG_RSLOT;
+      uint8_t *bh = bring + b * LG_BSLOT, *bl = bh + LG_B_BYTES;
       const uint4 *codes = reinterpret_cast<const uint4 *>(st + LG_OFF_CODES);
       const uint2 *scs = reinterpret_cast<const uint2 *>(st + LG_OFF_SCALES);
-      // the slot was refilled only after the MMA of the step three back (which
-      // read these weight blocks) committed, and this warp waited on the refill
       {
         const int rbl = dt >> 5, ts = dt & 31, g = ts >> 2, tq = ts & 3;
         const int n0 = rbl * 16 + g, n8 = n0 + 8;
@@ -285,7 +297,7 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
         }
       }
       fence_async_smem();  // the weights written here are read by the tensor core (async proxy)
-      mbar_arrive(&bfull[s]);
+      mbar_arrive(&bfull[b]);
     }
     // epilogue: this warp's quarter of the tile's lanes (the wait returns at
     // once: the accumulators needed the activations the kernel ahead wrote)
@@ -512,231 +524,6 @@ __global__ void lane_argmax_kernel(const float *val, const int *idx, int parts, 
   if (tid == 0) top[j] = si[0];
 }
 
-// ---------------------------------------------------------------------------
-// attention of the batched-lane passes (app_core.c:11415-11578
-// session_attend / session_attend_group), in f32 on the CUDA cores: at a
-// handful of query rows per cached row the work is the cache's bytes.
-
-constexpr int LA_ROWS = 32;  // query rows a split block: a group's lanes x the heads of one key/value head
-constexpr int LA_TPR = 8;    // threads a row (each holds hd / 8 dimensions: d = s + 8 k)
-constexpr int LA_TILE = 16;  // cached positions a tile
-
-__device__ __forceinline__ int la_pos(const LaneAttnArgs &a, int g) {
-  return a.pos_tab[(size_t)g * a.pos_stride] + g * a.pos_step;
-}
-
-__device__ __forceinline__ void la_cp16(void *dst, const void *src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void la_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void la_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
-// One block a lane: its queries normed (q_norm) and turned at its position,
-// and on an owner layer its keys normed (k_norm) and turned and its values
-// normed (no weight), written to the cache (app_core.c:11480-11512).  A warp
-// a head row; a lane holds dimensions d and d + hd/2 for d = lane + 32 e.
-__global__ void __launch_bounds__(256) lane_qk_kernel(LaneAttnArgs a) {
-  pdl_release();
-  pdl_wait();
-  const int j = blockIdx.x, g = j / a.group_lanes, i = j - g * a.group_lanes;
-  const int p = la_pos(a, g) + i;
-  float *kc = a.kc_tab ? a.kc_tab[g] : a.kc, *vc = a.vc_tab ? a.vc_tab[g] : a.vc;
-  const int hd = a.hd, half = hd / 2, kv_w = a.kv_heads * hd;
-  const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
-  const float *row = a.qkv + (size_t)j * a.qkv_stride;
-  const float *cs = a.cs + (size_t)p * half, *sn = a.sn + (size_t)p * half;
-  const int n_items = a.heads + (a.owner ? 2 * a.kv_heads : 0);
-  for (int it = warp; it < n_items; it += 8) {
-    const float *src, *w;
-    float *dst;
-    bool turn = true;
-    if (it < a.heads) {
-      src = row + (size_t)it * hd;
-      dst = a.qbuf + (size_t)j * a.heads * hd + (size_t)it * hd;
-      w = a.q_norm;
-    } else if (it < a.heads + a.kv_heads) {
-      const int kh = it - a.heads;
-      src = row + (size_t)a.heads * hd + (size_t)kh * hd;
-      dst = kc + (size_t)p * kv_w + (size_t)kh * hd;
-      w = a.k_norm;
-    } else {
-      const int kh = it - a.heads - a.kv_heads;
-      src = row + (size_t)a.heads * hd + kv_w + (size_t)kh * hd;
-      dst = vc + (size_t)p * kv_w + (size_t)kh * hd;
-      w = nullptr;
-      turn = false;
-    }
-    float lo[4], hi[4], ss = 0.0f;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = l + 32 * e;
-      lo[e] = d < half ? src[d] : 0.0f;
-      hi[e] = d < half ? src[d + half] : 0.0f;
-      ss += lo[e] * lo[e] + hi[e] * hi[e];
-    }
-    const float sh = rms_shrink(warp_sum(ss), hd, a.eps);  // app_core.c:4667 kern_norm_rms
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = l + 32 * e;
-      if (d >= half) continue;
-      float x = lo[e] * sh, y = hi[e] * sh;
-      if (w) {
-        x *= w[d];
-        y *= w[d + half];
-      }
-      if (turn) {  // app_core.c:5196 kern_rope_turn: pairs (d, d + hd/2)
-        const float c = cs[d], sv = sn[d];
-        const float x2 = x * c - y * sv, y2 = y * c + x * sv;
-        x = x2;
-        y = y2;
-      }
-      dst[d] = x;
-      dst[d + half] = y;
-    }
-  }
-}
-
-// One block a (group, key/value head, split of positions): the group's query
-// rows against the split's cached rows, scores scaled by 1 (app_core.c:11314),
-// each lane masked to its own window, an online softmax, and the split's
-// weighted values, row maximum and total left for the merge.
-__global__ void __launch_bounds__(256) lane_attn_kernel(LaneAttnArgs a) {
-  extern __shared__ __align__(16) float la_sm[];  // two tiles: keys [16][hd], values [16][hd]
-  pdl_release();
-  pdl_wait();
-  const int gk = blockIdx.x, g = gk / a.kv_heads, kh = gk - g * a.kv_heads, z = blockIdx.y;
-  const int G = a.heads / a.kv_heads, hd = a.hd, kv_w = a.kv_heads * hd;
-  const int n_l = min(a.group_lanes, a.lanes - g * a.group_lanes);
-  const int p0 = la_pos(a, g), p_last = p0 + n_l - 1;
-  const int lo_all = a.sliding ? max(0, p0 - a.span + 1) : 0;
-  const int n_split = (p_last + 1 - lo_all + a.split_pos - 1) / a.split_pos;
-  if (z >= n_split) return;  // the whole block: this split lies past the group's positions
-  const int a0 = lo_all + z * a.split_pos, a1 = min(p_last + 1, a0 + a.split_pos);
-  const float *kc = (a.kc_tab ? a.kc_tab[g] : a.kc) + (size_t)kh * hd;
-  const float *vc = (a.vc_tab ? a.vc_tab[g] : a.vc) + (size_t)kh * hd;
-  const int tid = threadIdx.x, r = tid / LA_TPR, sl = tid % LA_TPR, DPT = hd / LA_TPR;
-  const int rows = n_l * G;
-  const bool live = r < rows;
-  const int li = live ? r / G : 0, h = kh * G + (live ? r % G : 0);
-  const int p_me = p0 + li, lo_me = a.sliding ? max(0, p_me - a.span + 1) : 0;
-  float q[32], acc[32];
-  const float *qr = a.qbuf + ((size_t)(g * a.group_lanes + li) * a.heads + h) * hd;
-#pragma unroll
-  for (int k = 0; k < 32; ++k) {
-    q[k] = (live && k < DPT) ? qr[sl + LA_TPR * k] : 0.0f;
-    acc[k] = 0.0f;
-  }
-  float m_run = -FLT_MAX, l_run = 0.0f;
-  const int tile_f = LA_TILE * hd;  // floats of one tile's keys (or values)
-  const int n_tiles = (a1 - a0 + LA_TILE - 1) / LA_TILE, c4 = hd / 4;
-  auto issue = [&](int ti) {
-    float *kt = la_sm + (ti & 1) * 2 * tile_f, *vt = kt + tile_f;
-    const int tb = a0 + ti * LA_TILE;
-    for (int e = tid; e < LA_TILE * c4; e += blockDim.x) {
-      const int u = e / c4, c = (e - u * c4) * 4, t = tb + u;
-      if (t < a1) {
-        la_cp16(kt + u * hd + c, kc + (size_t)t * kv_w + c);
-        la_cp16(vt + u * hd + c, vc + (size_t)t * kv_w + c);
-      }
-    }
-    la_commit();
-  };
-  issue(0);
-  for (int ti = 0; ti < n_tiles; ++ti) {
-    if (ti + 1 < n_tiles) {
-      issue(ti + 1);
-      la_wait<1>();
-    } else {
-      la_wait<0>();
-    }
-    __syncthreads();
-    const float *kt = la_sm + (ti & 1) * 2 * tile_f, *vt = kt + tile_f;
-    const int tb = a0 + ti * LA_TILE;
-    const int nv = min(LA_TILE, a1 - tb);  // rows the tile holds: the rest of the buffer is stale
-    float sc[LA_TILE];
-    float mt = -FLT_MAX;
-#pragma unroll
-    for (int u = 0; u < LA_TILE; ++u) {
-      const float *kr = kt + u * hd + sl;
-      float part = 0.0f;
-#pragma unroll
-      for (int k = 0; k < 32; ++k)
-        if (k < DPT) part = fmaf(q[k], kr[LA_TPR * k], part);
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      part += __shfl_xor_sync(0xffffffffu, part, 4);
-      const int t = tb + u;
-      const bool ok = live && u < nv && t >= lo_me && t <= p_me;
-      sc[u] = ok ? part : -FLT_MAX;
-      mt = fmaxf(mt, sc[u]);
-    }
-    const float m_new = fmaxf(m_run, mt);
-    if (m_new > -FLT_MAX) {
-      const float f = m_run > -FLT_MAX ? expf(m_run - m_new) : 0.0f;
-      float tot = 0.0f;
-#pragma unroll
-      for (int u = 0; u < LA_TILE; ++u) {
-        sc[u] = sc[u] > -FLT_MAX ? expf(sc[u] - m_new) : 0.0f;
-        tot += sc[u];
-      }
-      l_run = l_run * f + tot;
-      m_run = m_new;
-#pragma unroll
-      for (int k = 0; k < 32; ++k) {
-        if (k >= DPT) continue;
-        float v = acc[k] * f;
-#pragma unroll
-        for (int u = 0; u < LA_TILE; ++u)
-          if (u < nv) v = fmaf(sc[u], vt[u * hd + sl + LA_TPR * k], v);
-        acc[k] = v;
-      }
-    }
-    __syncthreads();  // the buffer is refilled two tiles on
-  }
-  if (live) {
-    float *pr = a.part + (((size_t)gk * a.max_splits + z) * LA_ROWS + r) * (hd + 2);
-#pragma unroll
-    for (int k = 0; k < 32; ++k)
-      if (k < DPT) pr[sl + LA_TPR * k] = acc[k];
-    if (sl == 0) {
-      pr[hd] = m_run;
-      pr[hd + 1] = l_run;
-    }
-  }
-}
-
-// One block a (group, key/value head): the splits of every row merged in
-// split order into the lanes' attention output.
-__global__ void __launch_bounds__(256) lane_attn_merge_kernel(LaneAttnArgs a) {
-  pdl_release();
-  pdl_wait();
-  const int gk = blockIdx.x, g = gk / a.kv_heads, kh = gk - g * a.kv_heads;
-  const int G = a.heads / a.kv_heads, hd = a.hd;
-  const int n_l = min(a.group_lanes, a.lanes - g * a.group_lanes);
-  const int p0 = la_pos(a, g), p_last = p0 + n_l - 1;
-  const int lo_all = a.sliding ? max(0, p0 - a.span + 1) : 0;
-  const int n_split = (p_last + 1 - lo_all + a.split_pos - 1) / a.split_pos;
-  const int rows = n_l * G;
-  for (int e = threadIdx.x; e < rows * hd; e += blockDim.x) {
-    const int r = e / hd, d = e - r * hd, li = r / G, h = kh * G + r % G;
-    const float *pr = a.part + ((size_t)gk * a.max_splits * LA_ROWS + r) * (hd + 2);
-    const size_t zs = (size_t)LA_ROWS * (hd + 2);
-    float M = -FLT_MAX;
-    for (int z = 0; z < n_split; ++z) M = fmaxf(M, pr[z * zs + hd]);
-    float L = 0.0f, o = 0.0f;
-    for (int z = 0; z < n_split; ++z) {
-      const float mz = pr[z * zs + hd];
-      const float w = mz > -FLT_MAX ? expf(mz - M) : 0.0f;
-      L = fmaf(pr[z * zs + hd + 1], w, L);
-      o = fmaf(pr[z * zs + d], w, o);
-    }
-    a.out[(size_t)(g * a.group_lanes + li) * a.out_stride + (size_t)h * hd + d] = o / L;
-  }
-}
-
 // K-slice partials added in order: out[j][i] = sum_z p[z][j][i].
 __global__ void lane_sum_kernel(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride) {
@@ -784,9 +571,6 @@ constexpr int LS_SMEM_LIMIT = 160 * 1024;  // a stage row (and a residual's part
 cudaError_t igc_lanes_configure(void) {
   cudaError_t e = cudaFuncSetAttribute(lane_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LS_SMEM_LIMIT);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(lane_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, LG_SMEM);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(lane_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(sizeof(float) * 4 * LA_TILE * 256));
   return e;
 }
 
@@ -795,6 +579,19 @@ cudaError_t igc_launch_lane_stage(const LaneStageArgs *a, cudaStream_t st) {
   const size_t smem = igc_lane_stage_smem(a->mode, a->cols);
   if (smem > LS_SMEM_LIMIT) return cudaErrorInvalidValue;
   return lane_launch(lane_stage_kernel, dim3(a->lanes), dim3(256), smem, st, *a);
+}
+
+// Positions of a prefill chunk's 16-lane attention groups: out[i] = p0 + 16 i.
+__global__ void lane_positions_kernel(const int *p0, int groups, int *out) {
+  pdl_release();
+  pdl_wait();
+  const int i = threadIdx.x;
+  if (i < groups) out[i] = *p0 + 16 * i;
+}
+
+cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st) {
+  if (groups < 1 || groups > 1024) return cudaErrorInvalidValue;
+  return lane_launch(lane_positions_kernel, dim3(1), dim3(1024), 0, st, p0, groups, out);
 }
 
 
@@ -811,23 +608,6 @@ cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
   if (a->arg_val && (a->split != 1 || !a->arg_idx)) return cudaErrorInvalidValue;
   dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
   return lane_launch(lane_gemm_kernel, grid, dim3(LG_THREADS), (size_t)LG_SMEM, st, *a);
-}
-
-size_t igc_lane_attn_smem(int hd) { return sizeof(float) * 4 * LA_TILE * (size_t)hd; }
-
-cudaError_t igc_launch_lane_attn(const LaneAttnArgs *a, cudaStream_t st) {
-  const int G = a->kv_heads > 0 ? a->heads / a->kv_heads : 0;
-  if (a->hd % 32 || a->hd > 256 || G < 1 || a->heads % a->kv_heads || a->group_lanes * G > LA_ROWS ||
-      a->groups < 1 || a->lanes < 1 || a->lanes > a->groups * a->group_lanes || a->split_pos < LA_TILE ||
-      a->max_splits < 1)
-    return cudaErrorInvalidValue;
-  cudaError_t e = lane_launch(lane_qk_kernel, dim3(a->lanes), dim3(256), 0, st, *a);
-  if (e == cudaSuccess)
-    e = lane_launch(lane_attn_kernel, dim3(a->groups * a->kv_heads, a->max_splits), dim3(256),
-                    igc_lane_attn_smem(a->hd), st, *a);
-  if (e == cudaSuccess)
-    e = lane_launch(lane_attn_merge_kernel, dim3(a->groups * a->kv_heads), dim3(256), 0, st, *a);
-  return e;
 }
 
 cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,

@@ -60,31 +60,6 @@ struct LaneGemmArgs {
   float cap;
 };
 
-// Attention for the batched-lane passes (igc_lanes.cu lane_qk / lane_attn /
-// lane_attn_merge).  Lanes come in groups of `group_lanes` consecutive lanes
-// at consecutive positions that share one cache: a prime chunk's lanes (all
-// groups in the session's cache) or one block of a crowd's session.  Group g
-// starts at position pos_tab[g * pos_stride] + g * pos_step; its caches are
-// kc_tab[g] / vc_tab[g], or kc / vc when the tables are null.
-struct LaneAttnArgs {
-  const float *qkv;  // [lanes][qkv_stride]: q (heads x hd), then k, then v (kv_heads x hd each)
-  int qkv_stride, heads, kv_heads, hd;
-  const float *q_norm, *k_norm, *cs, *sn;  // rope tables [position][hd / 2]
-  float eps;
-  int owner;  // this layer writes its lanes' keys and values
-  float *kc, *vc;
-  float *const *kc_tab, *const *vc_tab;
-  const int *pos_tab;
-  int pos_stride, pos_step;
-  int groups, group_lanes, lanes;
-  int sliding, span;  // a sliding layer's lane at p sees [p - span + 1, p]
-  int split_pos, max_splits;  // positions a split block covers; splits the grid holds
-  float *qbuf;  // [lanes][heads x hd] the normed, turned queries
-  float *part;  // [groups x kv_heads][max_splits][32 rows][hd + 2] a split's values, maximum, total
-  float *out;   // [lanes][out_stride]
-  int out_stride;
-};
-
 }  // namespace igc
 
 extern "C" {
@@ -95,11 +70,8 @@ cudaError_t igc_launch_lane_stage(const igc::LaneStageArgs *a, cudaStream_t st);
 // K slices that keep about one wave of the SMs busy for this product.
 int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count);
 cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, cudaStream_t st);
-// Attention of a batched-lane pass, three launches: queries (and an owner
-// layer's new keys and values, written to the cache), the split blocks, the
-// merge.  Shared memory of a split block, and its grid for `positions`.
-size_t igc_lane_attn_smem(int hd);
-cudaError_t igc_launch_lane_attn(const igc::LaneAttnArgs *a, cudaStream_t st);
+// out[i] = *p0 + 16 i for i < groups (a prefill chunk's attention groups).
+cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st);
 // Per lane the largest of `parts` argmax partials [part][lanes] (first index
 // on a tie), into top[lanes].
 cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,

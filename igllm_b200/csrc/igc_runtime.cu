@@ -796,13 +796,7 @@ struct LaneBuf {
   float *arg_val = nullptr;
   int *arg_idx = nullptr;
   void *a_tiles = nullptr;
-  // attention (igc_lanes.cu lane_attn): normed queries, split partials, and
-  // the positions a split block covers / the splits a launch holds
-  float *qbuf = nullptr, *apart = nullptr;
-  int att_groups = 0, split_pos = 0, max_splits = 0;
 };
-
-constexpr int IGC_ATT_GROUP = 4;  // lanes a group of the batched-lane attention (4 lanes x 8 heads = 32 rows)
 
 struct igc_session {
   igc_model *m = nullptr;
@@ -867,6 +861,7 @@ struct igc_session {
   struct Chunks {
     LaneBuf B;
     int32_t *d_ids = nullptr;  // [0] position, [1..cap] ids
+    int *d_pos = nullptr;      // the 16-lane attention groups' positions
     int32_t *h_ids = nullptr;  // pinned
     std::map<int, cudaGraphExec_t> graph;
   } ch;
@@ -1341,8 +1336,7 @@ constexpr int IGC_CHUNK_MIN = 64;     // fewer lanes than this run as 16-lane pa
 // Sizes `B` for passes of up to `cap` lanes.  `split_lanes` > 0 fixes every
 // product's K slices to those of a pass of that many lanes (results then do
 // not depend on how many lanes a pass carries); 0 lets each pass choose.
-static int lane_buf_alloc(igc_model *m, LaneBuf &B, int cap, int split_lanes, std::vector<void *> &owned,
-                          int att_lanes = IGC_ATT_GROUP) {
+static int lane_buf_alloc(igc_model *m, LaneBuf &B, int cap, int split_lanes, std::vector<void *> &owned) {
   const int H = m->hidden, PS = m->layers * m->ple_dim;
   size_t part = 0;
   int max_cc = 1;
@@ -1388,18 +1382,6 @@ static int lane_buf_alloc(igc_model *m, LaneBuf &B, int cap, int split_lanes, st
   const size_t head_tiles = (size_t)(m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16);
   if (c == IGC_OKAY) c = grab(&B.arg_val, head_tiles * cap);
   if (c == IGC_OKAY) c = grab(&B.arg_idx, head_tiles * cap);
-  // attention splits: at most 33 a group whatever the window (128 positions
-  // a split up to a 4096-position window, longer splits beyond)
-  int hd_max = 0, kvh_max = 1;
-  for (auto &L : m->layer) {
-    hd_max = std::max(hd_max, L.hd);
-    kvh_max = std::max(kvh_max, L.kv_heads);
-  }
-  B.split_pos = std::max(128, ((m->window_limit + 31) / 32 + 15) / 16 * 16);
-  B.max_splits = (m->window_limit + IGC_ATT_GROUP + B.split_pos - 1) / B.split_pos + 1;
-  B.att_groups = (cap + att_lanes - 1) / att_lanes;
-  if (c == IGC_OKAY) c = grab(&B.qbuf, (size_t)cap * m->max_q);
-  if (c == IGC_OKAY) c = grab(&B.apart, (size_t)B.att_groups * kvh_max * B.max_splits * 32 * (hd_max + 2));
   if (c != IGC_OKAY) return c;
   B.cap = cap;
   B.split_lanes = split_lanes;
@@ -1465,39 +1447,6 @@ static int lane_product(LaneRun &r, const DevPlane &pl, LaneStageArgs sa, int *s
   CKL(igc_launch_lane_gemm(&ga, r.st));
   *split_out = ga.split;
   return IGC_OKAY;
-}
-
-// The batched-lane attention of layer `l` over the pass's q|k|v (B.qkv) into
-// B.attn: groups of `group_lanes` lanes, positions and caches as LaneAttnArgs
-// describes them (the caller fills pos_* and the cache fields).
-static LaneAttnArgs lane_attn_args(igc_model *m, LaneBuf &B, int l, int lanes, int group_lanes) {
-  const DevLayer &L = m->layer[l];
-  const DevLayer &O = m->layer[L.share ? L.source : l];
-  LaneAttnArgs a;
-  memset(&a, 0, sizeof(a));
-  a.qkv = B.qkv;
-  a.qkv_stride = L.qkv_rows;
-  a.heads = m->heads;
-  a.kv_heads = O.kv_heads;
-  a.hd = L.hd;
-  a.q_norm = L.q_norm;
-  a.k_norm = L.k_norm;
-  a.cs = m->rope_cs[L.kind];
-  a.sn = m->rope_sn[L.kind];
-  a.eps = m->eps;
-  a.owner = L.share ? 0 : 1;
-  a.group_lanes = group_lanes;
-  a.groups = (lanes + group_lanes - 1) / group_lanes;
-  a.lanes = lanes;
-  a.sliding = L.kind == 0 ? 1 : 0;
-  a.span = m->slide_span;
-  a.split_pos = B.split_pos;
-  a.max_splits = B.max_splits;
-  a.qbuf = B.qbuf;
-  a.part = B.apart;
-  a.out = B.attn;
-  a.out_stride = L.q_rows;
-  return a;
 }
 
 // embed, the per-layer-embedding lift, the layers (attention by `attend`),
@@ -1618,6 +1567,7 @@ static int chunks_ready(igc_session *s) {
   const int M = IGC_CHUNK_LANES;
   int c = lane_buf_alloc(s->m, C.B, M, 0, s->owned);
   if (c == IGC_OKAY) c = s->alloc(&C.d_ids, 1 + M);
+  if (c == IGC_OKAY) c = s->alloc(&C.d_pos, M / 16 + 1);
   if (c != IGC_OKAY) return c;
   CK(cudaMallocHost(&C.h_ids, sizeof(int32_t) * (1 + M)));
   return IGC_OKAY;
@@ -1628,18 +1578,25 @@ static int chunks_ready(igc_session *s) {
 static int enqueue_chunk(igc_session *s, int M) {
   igc_model *m = s->m;
   auto &C = s->ch;
-  // kernels overlap the one ahead (each waits before reading its results)
+  // kernels overlap the one ahead (each waits before reading its results),
+  // except the attention groups: a group copies cached rows before its wait,
+  // and those rows are the previous group's own writes
   PdlScope pdl(s->use_pdl != 0);
+  const int groups = (M + 15) / 16;
+  CKL(igc_launch_lane_positions(C.d_ids, groups, C.d_pos, s->st));
   LaneRun r{m, s->st, &C.B, s->d_err, M};
   auto attend = [&](int l, const DevLayer &L) -> int {
     const int owner = L.share ? L.source : l;
-    LaneAttnArgs a = lane_attn_args(m, C.B, l, M, IGC_ATT_GROUP);
-    a.kc = s->kc[owner];
-    a.vc = s->vc[owner];
-    a.pos_tab = C.d_ids;  // the chunk's first position; group g starts 4 g further on
-    a.pos_stride = 0;
-    a.pos_step = IGC_ATT_GROUP;
-    CKL(igc_launch_lane_attn(&a, s->st));
+    const DevLayer &O = m->layer[owner];
+    igc_kernels_pdl(0);
+    for (int gi = 0; gi < groups; ++gi) {
+      const int j0 = gi * 16, n = M - j0 < 16 ? M - j0 : 16;
+      CKL(igc_launch_attn(C.B.qkv + (size_t)j0 * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
+                          L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner],
+                          s->vc[owner], L.kind == 0 ? 1 : 0, m->slide_span, C.d_pos + gi, n, s->attn_cluster,
+                          C.B.attn + (size_t)j0 * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
+    }
+    igc_kernels_pdl(s->use_pdl != 0);
     return IGC_OKAY;
   };
   return lane_stack(r, C.d_ids + 1, attend);
@@ -1781,13 +1738,16 @@ extern "C" int igc_session_guess_keep(igc_session *s, int keep) { /* app_core.c:
 // by the crowd's capacity, so a session's results do not depend on how many
 // sessions share its round.
 
+// Attention blocks a cluster in a crowd round: with many sessions in one
+// launch, clusters of 8 take half the blocks (and waves) clusters of 16 do.
+constexpr int IGC_CROWD_CLUSTER = 8;
+
 struct igc_crowd {
   igc_model *m = nullptr;
   cudaStream_t st = nullptr;
   int cap = 0, k = 0, lanes = 0;
-  int gl = 1, gps = 1, groups = 0;  // attention groups: lanes a group, groups a session, groups in all
   LaneBuf B;
-  // device: [ids: lanes][pos: groups][kc: layers * groups][vc: layers * groups], mirrored in pinned host memory
+  // device: [ids: lanes][pos: cap][kc: layers * cap][vc: layers * cap], mirrored in pinned host memory
   uint8_t *d_tab = nullptr, *h_tab = nullptr;
   size_t tab_bytes = 0;
   int32_t *d_top = nullptr;  // [lanes] argmax, then the kernels' error word
@@ -1799,8 +1759,8 @@ struct igc_crowd {
 
   int32_t *ids() { return reinterpret_cast<int32_t *>(d_tab); }
   int *pos() { return reinterpret_cast<int *>(d_tab + sizeof(int32_t) * lanes); }
-  float **kc() { return reinterpret_cast<float **>(d_tab + sizeof(int32_t) * lanes + sizeof(int) * groups); }
-  float **vc() { return kc() + (size_t)m->layers * groups; }
+  float **kc() { return reinterpret_cast<float **>(d_tab + sizeof(int32_t) * lanes + sizeof(int) * cap); }
+  float **vc() { return kc() + (size_t)m->layers * cap; }
 
   ~igc_crowd() {
     cudaSetDevice(m->device);
@@ -1817,9 +1777,6 @@ extern "C" int igc_crowd_open(igc_model *m, int session_limit, int lanes_per_ses
   if (!m || !out || session_limit < 1 || lanes_per_session < 1 || lanes_per_session > IGC_LANE_LIMIT)
     return IGC_FAIL_ARGUMENT;
   if (session_limit * lanes_per_session > IGC_CROWD_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
-  // a session's block is one or more attention groups of up to four lanes
-  const int gl = lanes_per_session < IGC_ATT_GROUP ? lanes_per_session : IGC_ATT_GROUP;
-  if (lanes_per_session % gl) return IGC_FAIL_SUPPORT;
   *out = nullptr;
   clear_stale("crowd open");
   CK(cudaSetDevice(m->device));
@@ -1828,13 +1785,10 @@ extern "C" int igc_crowd_open(igc_model *m, int session_limit, int lanes_per_ses
   cr->cap = session_limit;
   cr->k = lanes_per_session;
   cr->lanes = session_limit * lanes_per_session;
-  cr->gl = gl;
-  cr->gps = lanes_per_session / gl;
-  cr->groups = session_limit * cr->gps;
   CK(cudaStreamCreateWithFlags(&cr->st, cudaStreamNonBlocking));
-  int c = lane_buf_alloc(m, cr->B, cr->lanes, cr->lanes, cr->owned, gl);
+  int c = lane_buf_alloc(m, cr->B, cr->lanes, cr->lanes, cr->owned);
   if (c != IGC_OKAY) return c;
-  cr->tab_bytes = sizeof(int32_t) * cr->lanes + sizeof(int) * cr->groups + 2 * sizeof(float *) * m->layers * cr->groups;
+  cr->tab_bytes = sizeof(int32_t) * cr->lanes + sizeof(int) * cr->cap + 2 * sizeof(float *) * m->layers * cr->cap;
   void *v = nullptr;
   CK(cudaMalloc(&v, cr->tab_bytes));
   cr->owned.push_back(v);
@@ -1861,14 +1815,12 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
   const int k = cr->k;
   LaneRun r{m, cr->st, &cr->B, cr->d_top + cr->lanes, S * k};
   auto attend = [&](int l, const DevLayer &L) -> int {
-    (void)L;
-    LaneAttnArgs a = lane_attn_args(m, cr->B, l, S * k, cr->gl);
-    a.kc_tab = cr->kc() + (size_t)l * cr->groups;
-    a.vc_tab = cr->vc() + (size_t)l * cr->groups;
-    a.pos_tab = cr->pos();
-    a.pos_stride = 1;
-    a.pos_step = 0;
-    CKL(igc_launch_lane_attn(&a, cr->st));
+    const int owner = L.share ? L.source : l;
+    const DevLayer &O = m->layer[owner];
+    CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
+                             m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr, L.kind == 0 ? 1 : 0,
+                             m->slide_span, cr->pos(), k, IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr, nullptr,
+                             cr->kc() + (size_t)l * cr->cap, cr->vc() + (size_t)l * cr->cap, cr->pos(), S, cr->st));
     return IGC_OKAY;
   };
   return lane_stack(r, cr->ids(), attend, cr->d_top, rows ? cr->logits : nullptr);
@@ -1898,23 +1850,18 @@ extern "C" int igc_crowd_round(igc_crowd *cr, igc_session **sessions, int count,
     cr->logits = (float *)v;
   }
   // the tables: ids, positions and every layer's (owner's) caches per session
-  // the tables: ids, and per attention group its first position and every
-  // layer's (owner's) caches (group g is lanes [g gl, (g + 1) gl) of session g / gps)
   int32_t *h_ids = reinterpret_cast<int32_t *>(cr->h_tab);
   int *h_pos = reinterpret_cast<int *>(cr->h_tab + sizeof(int32_t) * cr->lanes);
-  float **h_kc = reinterpret_cast<float **>(cr->h_tab + sizeof(int32_t) * cr->lanes + sizeof(int) * cr->groups);
-  float **h_vc = h_kc + (size_t)m->layers * cr->groups;
+  float **h_kc = reinterpret_cast<float **>(cr->h_tab + sizeof(int32_t) * cr->lanes + sizeof(int) * cr->cap);
+  float **h_vc = h_kc + (size_t)m->layers * cr->cap;
   memcpy(h_ids, ids, sizeof(int32_t) * (size_t)count * k);
   for (int j = 0; j < count; ++j) {
-    for (int q = 0; q < cr->gps; ++q) {
-      const int g = j * cr->gps + q;
-      h_pos[g] = sessions[j]->fill + q * cr->gl;
-      for (int l = 0; l < m->layers; ++l) {
-        const DevLayer &L = m->layer[l];
-        const int owner = L.share ? L.source : l;
-        h_kc[(size_t)l * cr->groups + g] = sessions[j]->kc[owner];
-        h_vc[(size_t)l * cr->groups + g] = sessions[j]->vc[owner];
-      }
+    h_pos[j] = sessions[j]->fill;
+    for (int l = 0; l < m->layers; ++l) {
+      const DevLayer &L = m->layer[l];
+      const int owner = L.share ? L.source : l;
+      h_kc[(size_t)l * cr->cap + j] = sessions[j]->kc[owner];
+      h_vc[(size_t)l * cr->cap + j] = sessions[j]->vc[owner];
     }
   }
   CK(cudaMemcpyAsync(cr->d_tab, cr->h_tab, cr->tab_bytes, cudaMemcpyHostToDevice, cr->st));
