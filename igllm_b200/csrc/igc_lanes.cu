@@ -597,10 +597,21 @@ cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaS
 
 
 int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count) {
+  // the split that minimises waves x (steps a block + a block's fixed cost,
+  // about six steps' worth: set-up, pipeline fill, epilogue), at least two
+  // steps a slice; ties keep the fewer slices
   const int tiles = ((n_rb + LG_RB - 1) / LG_RB) * ((lanes + LG_M - 1) / LG_M);
-  int split = 1;
-  while (split < 16 && tiles * split * 2 <= sm_count && n_cc / (split * 2) >= 2) split *= 2;
-  return split;
+  int best = 1;
+  long best_cost = -1;
+  for (int split = 1; split <= 16 && split * 2 <= n_cc; ++split) {
+    const long waves = ((long)tiles * split + sm_count - 1) / sm_count;
+    const long cost = waves * ((n_cc + split - 1) / split + 6);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = split;
+    }
+  }
+  return best;
 }
 
 cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {

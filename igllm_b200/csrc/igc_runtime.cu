@@ -1330,7 +1330,16 @@ static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
 // group reads them), and the crowd (igc_crowd_round), one block of k lanes
 // from each of many sessions (attention for all of them in one launch).
 
-constexpr int IGC_CHUNK_LANES = 256;  // lanes a prime chunk
+constexpr int IGC_CHUNK_LANES = 256;  // lanes a prime chunk (IGC_CHUNK_LANES=512 in the environment for comparison)
+
+static int chunk_lanes() {
+  static const int n = [] {
+    const char *e = getenv("IGC_CHUNK_LANES");
+    const int v = e ? atoi(e) : 0;
+    return v == 512 || v == 128 ? v : IGC_CHUNK_LANES;
+  }();
+  return n;
+}
 constexpr int IGC_CHUNK_MIN = 64;     // fewer lanes than this run as 16-lane passes
 
 // Sizes `B` for passes of up to `cap` lanes.  `split_lanes` > 0 fixes every
@@ -1564,7 +1573,7 @@ static int lane_stack(LaneRun &r, const int32_t *d_ids, Attend attend, int32_t *
 static int chunks_ready(igc_session *s) {
   auto &C = s->ch;
   if (C.B.cap) return IGC_OKAY;
-  const int M = IGC_CHUNK_LANES;
+  const int M = chunk_lanes();
   int c = lane_buf_alloc(s->m, C.B, M, 0, s->owned);
   if (c == IGC_OKAY) c = s->alloc(&C.d_ids, 1 + M);
   if (c == IGC_OKAY) c = s->alloc(&C.d_pos, M / 16 + 1);
@@ -1602,7 +1611,7 @@ static int enqueue_chunk(igc_session *s, int M) {
   return lane_stack(r, C.d_ids + 1, attend);
 }
 
-// One chunk of M lanes (64 <= M <= IGC_CHUNK_LANES), kept, with a captured
+// One chunk of M lanes (64 <= M <= chunk_lanes()), kept, with a captured
 // graph per chunk length.
 static int run_chunk(igc_session *s, const int32_t *ids, int M) {
   igc_model *m = s->m;
@@ -1660,7 +1669,7 @@ extern "C" int igc_session_prime(igc_session *s, const int32_t *ids, int n) { /*
   for (int i = 0; i + 1 < n;) {
     int left = n - 1 - i, c;
     if (s->use_chunks && left >= IGC_CHUNK_MIN) {
-      const int lanes = left < IGC_CHUNK_LANES ? left : IGC_CHUNK_LANES;
+      const int lanes = left < chunk_lanes() ? left : chunk_lanes();
       c = run_chunk(s, ids + i, lanes);
       i += lanes;
     } else {

@@ -62,3 +62,15 @@ def test_synth_tensors_match_the_written_file(igc_lib, tiny_dir):
     for name, (dt, arr) in mem.items():
         assert disk[name][0] == dt
         assert np.array_equal(np.asarray(disk[name][1]).view(arr.dtype).reshape(arr.shape), arr), name
+
+
+def test_crowd_and_stamps_refuse_bad_arguments_before_any_device_call(igc_lib):
+    """The crowd entries and the stamp reader check their arguments first, as
+    every session entry does (a refused call changes nothing)."""
+    lib = igc_lib._lib()
+    out = ctypes.c_void_p()
+    assert lib.igc_crowd_open(None, 4, 4, ctypes.byref(out)) == igc_lib.FAIL_ARGUMENT
+    assert not out.value
+    assert lib.igc_crowd_round(None, None, 1, None, None, None, None) == igc_lib.FAIL_ARGUMENT
+    assert lib.igc_session_stamps(None, 4, None, None, None, 0, 0) == igc_lib.FAIL_ARGUMENT
+    assert lib.igc_model_weight_count(None) == 0
