@@ -623,6 +623,21 @@ def run_profile_case(args):
     spec.vocab = args.case_vocab
     model = ig.Model(spec=spec, device=0, window_limit=args.case_window)
     rng = np.random.default_rng(0)
+    if args.case_prime > 0:
+        # one prime of `--case-prime` ids (the chunked tcgen05 path), captured
+        # first by an identical prime outside the profiler range
+        sess = ig.Session(model)
+        ids = rng.integers(0, args.case_vocab, args.case_prime).astype(np.int32)
+        sess.prime(ids)
+        sess.reset()
+        profiler_range(True)
+        t0 = time.perf_counter()
+        sess.prime(ids)
+        wall = time.perf_counter() - t0
+        profiler_range(False)
+        print(f"profile case: prime of {args.case_prime} ids, vocab {args.case_vocab}: {1000 * wall:.1f} ms",
+              flush=True)
+        return
     if args.case_streams > 0:
         # crowd rounds: `--case-streams` sessions primed to `--case-context`
         # ids each, `--case-rounds` greedy rounds of `--case-k` lanes for all
@@ -672,6 +687,7 @@ def main():
     ap.add_argument("--case-context", type=int, default=1024)
     ap.add_argument("--case-streams", type=int, default=0, help="profile crowd rounds of this many sessions")
     ap.add_argument("--case-window", type=int, default=4096, help="positions each session's caches hold")
+    ap.add_argument("--case-prime", type=int, default=0, help="profile one prime of this many ids")
     args = ap.parse_args()
     if args.profile_case:
         run_profile_case(args)
