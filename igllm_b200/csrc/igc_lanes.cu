@@ -3,7 +3,7 @@
 //
 // The K-lane skinny GEMM of igc_gemv.cuh streams each weight once for at most
 // sixteen lanes.  A prefill chunk (app_core.c:14443-14467 session_prime runs
-// its prompt 16 lanes a pass; here a chunk is up to 256) carries enough lanes
+// its prompt 16 lanes a pass; here a chunk is up to 512) carries enough lanes
 // that the product is a real dense contraction: out[m][n] = sum_k A[m][k] *
 // W[n][k] with M lanes, N weight rows and K input columns.  That runs here as
 // a tcgen05 GEMM:
@@ -524,6 +524,56 @@ __global__ void lane_argmax_kernel(const float *val, const int *idx, int parts, 
   if (tid == 0) top[j] = si[0];
 }
 
+// A prime chunk's new key and value rows, written to an owner layer's cache
+// before its attention runs (app_core.c:11500-11512): one block a lane at
+// position *p0 + lane; keys normed (k_norm) and turned, values normed with no
+// weight.  A warp a head row; a lane holds dimensions d and d + hd/2 for
+// d = lane + 32 e.  With every row of the chunk in the cache, the attention
+// of all the chunk's 16-lane groups runs as one launch.
+__global__ void __launch_bounds__(256) lane_kv_kernel(const float *qkv, int qkv_stride, int heads, int kv_heads,
+                                                      int hd, const float *k_norm, const float *cs_tab,
+                                                      const float *sn_tab, float eps, const int *p0, float *kc,
+                                                      float *vc) {
+  pdl_release();
+  pdl_wait();
+  const int j = blockIdx.x, p = *p0 + j;
+  const int half = hd / 2, kv_w = kv_heads * hd;
+  const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const float *row = qkv + (size_t)j * qkv_stride + (size_t)heads * hd;
+  const float *cs = cs_tab + (size_t)p * half, *sn = sn_tab + (size_t)p * half;
+  for (int it = warp; it < 2 * kv_heads; it += blockDim.x >> 5) {
+    const bool is_v = it >= kv_heads;
+    const int kh = is_v ? it - kv_heads : it;
+    const float *src = row + (is_v ? kv_w : 0) + (size_t)kh * hd;
+    float *dst = (is_v ? vc : kc) + (size_t)p * kv_w + (size_t)kh * hd;
+    float lo[4], hi[4], ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = l + 32 * e;
+      lo[e] = d < half ? src[d] : 0.0f;
+      hi[e] = d < half ? src[d + half] : 0.0f;
+      ss += lo[e] * lo[e] + hi[e] * hi[e];
+    }
+    const float sh = rms_shrink(warp_sum(ss), hd, eps);  // app_core.c:4667 kern_norm_rms
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = l + 32 * e;
+      if (d >= half) continue;
+      float x = lo[e] * sh, y = hi[e] * sh;
+      if (!is_v) {
+        x *= k_norm[d];
+        y *= k_norm[d + half];
+        const float c = cs[d], sv = sn[d];  // app_core.c:5196 kern_rope_turn: pairs (d, d + hd/2)
+        const float x2 = x * c - y * sv, y2 = y * c + x * sv;
+        x = x2;
+        y = y2;
+      }
+      dst[d] = x;
+      dst[d + half] = y;
+    }
+  }
+}
+
 // K-slice partials added in order: out[j][i] = sum_z p[z][j][i].
 __global__ void lane_sum_kernel(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride) {
@@ -619,6 +669,14 @@ cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
   if (a->arg_val && (a->split != 1 || !a->arg_idx)) return cudaErrorInvalidValue;
   dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
   return lane_launch(lane_gemm_kernel, grid, dim3(LG_THREADS), (size_t)LG_SMEM, st, *a);
+}
+
+cudaError_t igc_launch_lane_kv(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *k_norm,
+                               const float *cs, const float *sn, float eps, const int *p0, int lanes, float *kc,
+                               float *vc, cudaStream_t st) {
+  if (lanes < 1 || hd % 32 || hd > 256 || kv_heads < 1) return cudaErrorInvalidValue;
+  return lane_launch(lane_kv_kernel, dim3(lanes), dim3(256), 0, st, qkv, qkv_stride, heads, kv_heads, hd, k_norm, cs,
+                     sn, eps, p0, kc, vc);
 }
 
 cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,

@@ -70,6 +70,11 @@ cudaError_t igc_launch_lane_stage(const igc::LaneStageArgs *a, cudaStream_t st);
 // K slices that keep about one wave of the SMs busy for this product.
 int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count);
 cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, cudaStream_t st);
+// A prime chunk's `lanes` new key and value rows (normed; keys turned) into
+// an owner layer's caches at positions *p0 + lane.
+cudaError_t igc_launch_lane_kv(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *k_norm,
+                               const float *cs, const float *sn, float eps, const int *p0, int lanes, float *kc,
+                               float *vc, cudaStream_t st);
 // out[i] = *p0 + 16 i for i < groups (a prefill chunk's attention groups).
 cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st);
 // Per lane the largest of `parts` argmax partials [part][lanes] (first index

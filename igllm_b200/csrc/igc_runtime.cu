@@ -862,6 +862,10 @@ struct igc_session {
     LaneBuf B;
     int32_t *d_ids = nullptr;  // [0] position, [1..cap] ids
     int *d_pos = nullptr;      // the 16-lane attention groups' positions
+    // per layer, every group's caches (the layer's owner's, the same for all
+    // groups): [layers][groups_cap], for the batched attention launch
+    float **kc_tab = nullptr, **vc_tab = nullptr;
+    int groups_cap = 0;
     int32_t *h_ids = nullptr;  // pinned
     std::map<int, cudaGraphExec_t> graph;
   } ch;
@@ -1325,10 +1329,10 @@ static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
 // ---------------------------------------------------------------------------
 // the batched-lane passes: every projection a tcgen05 GEMM (igc_lanes.cu)
 // with a row-wise stage before it.  Two callers: the prime, in chunks of up
-// to 256 lanes of one session (attention in 16-lane groups in position
-// order: each group writes its keys and values to the cache before the next
-// group reads them), and the crowd (igc_crowd_round), one block of k lanes
-// from each of many sessions (attention for all of them in one launch).
+// to 512 lanes of one session (the keys and values of all its lanes written
+// to the cache first, then the attention of all its 16-lane groups in one
+// launch), and the crowd (igc_crowd_round), one block of k lanes from each of
+// many sessions (attention for all of them in one launch).
 
 // Lanes a prime chunk.  512 measured 11% faster than 256 at 4096 and 8192
 // ids (fewer weight sweeps; IGC_CHUNK_LANES=256 or 128 in the environment
@@ -1577,10 +1581,24 @@ static int chunks_ready(igc_session *s) {
   auto &C = s->ch;
   if (C.B.cap) return IGC_OKAY;
   const int M = chunk_lanes();
-  int c = lane_buf_alloc(s->m, C.B, M, 0, s->owned);
+  igc_model *m = s->m;
+  int c = lane_buf_alloc(m, C.B, M, 0, s->owned);
+  C.groups_cap = M / 16 + 1;
   if (c == IGC_OKAY) c = s->alloc(&C.d_ids, 1 + M);
-  if (c == IGC_OKAY) c = s->alloc(&C.d_pos, M / 16 + 1);
+  if (c == IGC_OKAY) c = s->alloc(&C.d_pos, C.groups_cap);
+  if (c == IGC_OKAY) c = s->alloc(&C.kc_tab, (size_t)m->layers * C.groups_cap);
+  if (c == IGC_OKAY) c = s->alloc(&C.vc_tab, (size_t)m->layers * C.groups_cap);
   if (c != IGC_OKAY) return c;
+  std::vector<float *> hk((size_t)m->layers * C.groups_cap), hv(hk.size());
+  for (int l = 0; l < m->layers; ++l) {
+    const int owner = m->layer[l].share ? m->layer[l].source : l;
+    for (int z = 0; z < C.groups_cap; ++z) {
+      hk[(size_t)l * C.groups_cap + z] = s->kc[owner];
+      hv[(size_t)l * C.groups_cap + z] = s->vc[owner];
+    }
+  }
+  CK(cudaMemcpy(C.kc_tab, hk.data(), sizeof(float *) * hk.size(), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(C.vc_tab, hv.data(), sizeof(float *) * hv.size(), cudaMemcpyHostToDevice));
   CK(cudaMallocHost(&C.h_ids, sizeof(int32_t) * (1 + M)));
   return IGC_OKAY;
 }
@@ -1597,17 +1615,31 @@ static int enqueue_chunk(igc_session *s, int M) {
   const int groups = (M + 15) / 16;
   CKL(igc_launch_lane_positions(C.d_ids, groups, C.d_pos, s->st));
   LaneRun r{m, s->st, &C.B, s->d_err, M};
+  // Attention: an owner layer first writes every lane's new key and value
+  // rows to its cache; then every 16-lane group reads all its rows from the
+  // cache (as a sharing layer does), all full groups in one launch
+  // (blockIdx.z the group) and a ragged last group in another.  These launch
+  // without overlap: a group copies cached rows before its own wait, and
+  // those rows are the prep launch's writes.
   auto attend = [&](int l, const DevLayer &L) -> int {
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
+    const int full = M / 16, tail = M - 16 * full, sliding = L.kind == 0 ? 1 : 0;
     igc_kernels_pdl(0);
-    for (int gi = 0; gi < groups; ++gi) {
-      const int j0 = gi * 16, n = M - j0 < 16 ? M - j0 : 16;
-      CKL(igc_launch_attn(C.B.qkv + (size_t)j0 * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
-                          L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner],
-                          s->vc[owner], L.kind == 0 ? 1 : 0, m->slide_span, C.d_pos + gi, n, s->attn_cluster,
-                          C.B.attn + (size_t)j0 * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
-    }
+    if (!L.share)
+      CKL(igc_launch_lane_kv(C.B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.k_norm, m->rope_cs[L.kind],
+                             m->rope_sn[L.kind], m->eps, C.d_ids, M, s->kc[owner], s->vc[owner], s->st));
+    if (full > 0)
+      CKL(igc_launch_attn_many(C.B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
+                               m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding,
+                               m->slide_span, C.d_pos, 16, s->attn_cluster, C.B.attn, L.q_rows, nullptr, nullptr,
+                               C.kc_tab + (size_t)l * C.groups_cap, C.vc_tab + (size_t)l * C.groups_cap, C.d_pos,
+                               full, s->st));
+    if (tail > 0)
+      CKL(igc_launch_attn(C.B.qkv + (size_t)16 * full * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
+                          L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, s->kc[owner], s->vc[owner],
+                          sliding, m->slide_span, C.d_pos + full, tail, s->attn_cluster,
+                          C.B.attn + (size_t)16 * full * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
     igc_kernels_pdl(s->use_pdl != 0);
     return IGC_OKAY;
   };

@@ -63,7 +63,7 @@ def test_lane_gemm_matches_the_checker(igc_lib, igo_mod, rows, cols, lanes):
 
 @pytest.mark.parametrize("which", ["tiny", "small", "wide"])
 def test_chunked_prime_matches_the_checker(igc_lib, igo_mod, which, tiny_dir, small_dir, wide_dir):
-    """A prompt of 64 or more ids primes in chunks of up to 256 lanes through
+    """A prompt of 64 or more ids primes in chunks of up to 512 lanes through
     the tcgen05 path (every projection a lane GEMM, attention in 16-lane
     groups in position order); what it leaves in the caches must give the
     checker's logits on the step, the block and the step after a keep that
@@ -74,10 +74,14 @@ def test_chunked_prime_matches_the_checker(igc_lib, igo_mod, which, tiny_dir, sm
     om = igo_mod.OracleModel(folder, window_limit=cfg["window_limit"])
     s, o = igc_lib.Session(m), igo_mod.OracleSession(om, threads=8)
     rng = np.random.default_rng(31)
-    n = min(cfg["window_limit"] - 40, 300)  # a 256-lane chunk and the rest (tiny: one chunk of 215)
+    n = min(cfg["window_limit"] - 40, 300)
     ids = rng.integers(0, cfg["vocab"], n).astype(np.int32)
-    s.prime(ids)
-    o.prime(ids)
+    # a chunk of n - 41 lanes, then 40 lanes by 16-lane passes (a second
+    # prime continuing from the first one's last id)
+    for part in (ids[:n - 40], ids[n - 41:]):
+        s.prime(part)
+        o.prime(part)
+    assert s.fill == o.fill == n - 1
 
     def close(got, want):
         err = float(np.abs(got - want).max())
