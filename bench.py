@@ -394,7 +394,8 @@ def run_ours(args):
     t2 = time.perf_counter()
     psess.close()
     prefill = {"tok_s": round((PREFILL_LEN - 1) / (t1 - t0), 1), "ttft_ms": round(1000 * (t2 - t0), 2),
-               "prompt": f"{PREFILL_LEN} uniform ids, seed 1 (config 3), 16-lane passes"}
+               "prompt": f"{PREFILL_LEN} uniform ids, seed 1 (config 3), chunks of 512 lanes through the tcgen05 lane "
+                         "GEMM; TTFT = the prime plus the first step"}
 
     # config 1: sampled verify rounds (heat 0.8, top-k 64, top-p 0.95,
     # --guess 8) through the round call; each block guesses the greedy
