@@ -22,6 +22,8 @@ using namespace igc;
 namespace {
 
 struct DeskPlane {
+  CUtensorMap tm_codes, tm_scales;  // the lane GEMM's tensor maps (igc_lane_tmaps)
+  bool tm_ok = false;
   uint4 *tiles = nullptr;
   uint2 *scales = nullptr;
   int n_rb = 0, n_cc = 0, rows = 0, cols = 0, split = 1, grid = 1;
@@ -106,6 +108,7 @@ const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
   int per_iter = GEMV_WARPS / dp.split;
   dp.grid = (dp.n_rb + per_iter - 1) / per_iter;
   if (dp.grid > s->sm_count * 4) dp.grid = s->sm_count * 4;
+  dp.tm_ok = igc_lane_tmaps(dp.tiles, dp.scales, dp.n_rb, dp.n_cc, &dp.tm_codes, &dp.tm_scales) == 0;
   return &(s->planes[p->code_data] = dp);
 }
 
@@ -165,7 +168,8 @@ void desk_mat_mat_lanes(DeskState *s, const DeskPlane *p, const float *act, int 
   ga.out_stride = rows_pad;
   ga.split = split;
   ga.err = s->err;
-  if (!ok(s, igc_launch_lane_gemm(&ga, s->st))) return;
+  if (!p->tm_ok) return void(note(s, IGC_FAIL_SUPPORT));
+  if (!ok(s, igc_launch_lane_gemm(&ga, &p->tm_codes, &p->tm_scales, s->st))) return;
   if (!ok(s, igc_launch_lane_sum(s->lane_part, split, lanes, p->rows, rows_pad, s->lane_out, p->rows, s->st)))
     return;
   if (!ok(s, cudaMemcpy2DAsync(out, sizeof(float) * out_stride, s->lane_out, sizeof(float) * p->rows,

@@ -49,6 +49,8 @@
 //
 // Every wait on a barrier gives up after a bounded number of polls and sets
 // the error word; the block then runs to its end and frees its tensor memory.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <float.h>
@@ -117,6 +119,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// One 3-D tensor load into shared memory, completed on an mbarrier (no
+// multicast; the map covers this GPU's own memory only).  x, the innermost
+// coordinate, is always 0 here.
+__device__ __forceinline__ void tma_load3(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Byte offset of the 16-byte piece j of row r inside one operand block.
 __host__ __device__ __forceinline__ uint32_t lg_swz(int r, int j) {
   return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((j ^ (r & 7)) << 4));
@@ -150,7 +163,9 @@ constexpr int LG_DQ_WARPS = 8;  // warps that turn codes into weights (then run 
 constexpr int LG_THREADS = 64 + 32 * LG_DQ_WARPS;
 constexpr int LG_TRIES = 1 << 22;  // polls a wait makes before it gives up
 
-__global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a) {
+__global__ void __launch_bounds__(LG_THREADS, 1)
+    lane_gemm_kernel(LaneGemmArgs a, const __grid_constant__ CUtensorMap tm_codes,
+                     const __grid_constant__ CUtensorMap tm_scales) {
   extern __shared__ __align__(1024) uint8_t lg_raw[];
   uint8_t *base = lg_raw + ((1024 - (smem_u32(lg_raw) & 1023)) & 1023);
   uint8_t *bring = base + LG_RSTAGES * LG_RSLOT;
@@ -192,21 +207,22 @@ __global__ void __launch_bounds__(LG_THREADS, 1) lane_gemm_kernel(LaneGemmArgs a
   pdl_release();
 
   if (warp == 0) {
-    // producer: the staged activations (a hi and a lo 16 KB block) and each
-    // row block's codes (512 B) and scales (64 B) of the step.  The weights
-    // of the first steps are requested before the wait on the kernel ahead
-    // (the stage that writes the activations); nothing else is.
-    const uint64_t policy = l2_evict_last();  // both are read again by the other tiles
+    // producer: the staged activations (a hi and a lo 16 KB block) and the 8
+    // row blocks' codes (8 x 512 B) and scales (8 x 64 B) of the step, the
+    // weights by one tensor load each (row blocks past the plane arrive as
+    // zeros).  The weights of the first steps are requested before the wait
+    // on the kernel ahead (the stage that writes the activations); nothing
+    // else is.
+    const uint64_t policy = l2_evict_last();  // the activations are read again by the other tiles
     auto weights = [&](int k) {
       const int s = k % LG_RSTAGES, c = c_lo + k;
       uint8_t *st = base + s * LG_RSLOT;
-      if (lane == 0) mbar_expect(&full[s], (uint32_t)(2 * LG_A_BYTES + rbv * (512 + 64)));
-      __syncwarp();
-      if (lane < rbv) {
-        const size_t tile = (size_t)(rb0 + lane) * a.n_cc + c;
-        bulk_load(st + LG_OFF_CODES + lane * 512, a.tiles + tile * 32, 512, &full[s], policy);
-        bulk_load(st + LG_OFF_SCALES + lane * 64, a.scales + tile * 8, 64, &full[s], policy);
+      if (lane == 0) {
+        mbar_expect(&full[s], (uint32_t)(2 * LG_A_BYTES + LG_CODE_BYTES + LG_SCALE_BYTES));
+        tma_load3(st + LG_OFF_CODES, &tm_codes, 0, c, rb0, &full[s]);
+        tma_load3(st + LG_OFF_SCALES, &tm_scales, 0, c, rb0, &full[s]);
       }
+      __syncwarp();
     };
     auto acts = [&](int k) {
       const int s = k % LG_RSTAGES, c = c_lo + k;
@@ -664,11 +680,43 @@ int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count) {
   return best;
 }
 
-cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, cudaStream_t st) {
-  if (a->lanes < 1 || a->split < 1 || a->split > a->n_cc || a->n_rb < 1) return cudaErrorInvalidValue;
+int igc_lane_tmaps(const void *tiles, const void *scales, int n_rb, int n_cc, CUtensorMap *codes_map,
+                   CUtensorMap *scales_map) {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = [] {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }();
+  if (!encode || !tiles || !scales || n_rb < 1 || n_cc < 1) return -1;
+  const cuuint32_t ones[3] = {1, 1, 1};
+  // codes: 128 words a tile, tiles `n_cc` apart in a row block
+  const cuuint64_t cdim[3] = {128, (cuuint64_t)n_cc, (cuuint64_t)n_rb};
+  const cuuint64_t cstride[2] = {512, (cuuint64_t)n_cc * 512};
+  const cuuint32_t cbox[3] = {128, 1, (cuuint32_t)LG_RB};
+  // scales: 16 words a (row block, step) record
+  const cuuint64_t sdim[3] = {16, (cuuint64_t)n_cc, (cuuint64_t)n_rb};
+  const cuuint64_t sstride[2] = {64, (cuuint64_t)n_cc * 64};
+  const cuuint32_t sbox[3] = {16, 1, (cuuint32_t)LG_RB};
+  CUresult r = encode(codes_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(tiles), cdim, cstride, cbox,
+                      ones, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r == CUDA_SUCCESS)
+    r = encode(scales_map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 3, const_cast<void *>(scales), sdim, sstride, sbox, ones,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -1;
+}
+
+cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, const CUtensorMap *codes_map, const CUtensorMap *scales_map,
+                                 cudaStream_t st) {
+  if (a->lanes < 1 || a->split < 1 || a->split > a->n_cc || a->n_rb < 1 || !codes_map || !scales_map)
+    return cudaErrorInvalidValue;
   if (a->arg_val && (a->split != 1 || !a->arg_idx)) return cudaErrorInvalidValue;
   dim3 grid((a->n_rb + LG_RB - 1) / LG_RB, (a->lanes + LG_M - 1) / LG_M, a->split);
-  return lane_launch(lane_gemm_kernel, grid, dim3(LG_THREADS), (size_t)LG_SMEM, st, *a);
+  return lane_launch(lane_gemm_kernel, grid, dim3(LG_THREADS), (size_t)LG_SMEM, st, *a, *codes_map, *scales_map);
 }
 
 cudaError_t igc_launch_lane_kv(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *k_norm,

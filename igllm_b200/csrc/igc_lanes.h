@@ -2,6 +2,7 @@
 // tcgen05 int4 GEMM for chunks of many lanes.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -69,7 +70,14 @@ size_t igc_lane_stage_smem(int mode, int cols);
 cudaError_t igc_launch_lane_stage(const igc::LaneStageArgs *a, cudaStream_t st);
 // K slices that keep about one wave of the SMs busy for this product.
 int igc_lane_gemm_split(int lanes, int n_rb, int n_cc, int sm_count);
-cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, cudaStream_t st);
+// The two tensor maps a plane's lane GEMMs load its weights through (3-D,
+// 32-bit elements): the code tiles [row block][step][128 words] and the scale
+// records [row block][step][16 words], each read 8 row blocks of one step at
+// a time.  Host only (the driver's encoder); 0 on success.
+int igc_lane_tmaps(const void *tiles, const void *scales, int n_rb, int n_cc, CUtensorMap *codes_map,
+                   CUtensorMap *scales_map);
+cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, const CUtensorMap *codes_map,
+                                 const CUtensorMap *scales_map, cudaStream_t st);
 // A prime chunk's `lanes` new key and value rows (normed; keys turned) into
 // an owner layer's caches at positions *p0 + lane.
 cudaError_t igc_launch_lane_kv(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *k_norm,

@@ -276,6 +276,9 @@ struct RopeForm {
 };
 
 struct DevPlane {
+  // the lane GEMM's tensor maps of this plane's weights (igc_lane_tmaps)
+  CUtensorMap tm_codes, tm_scales;
+  bool tm_ok = false;
   uint4 *tiles = nullptr;
   uint2 *scales = nullptr;
   int n_rb = 0, n_cc = 0, rows = 0, cols = 0;
@@ -505,6 +508,7 @@ struct Binder {
       src.release(p.name + ".weight_scale");
     }
     plan(out);
+    out.tm_ok = igc_lane_tmaps(out.tiles, out.scales, out.n_rb, out.n_cc, &out.tm_codes, &out.tm_scales) == 0;
     return IGC_OKAY;
   }
 
@@ -1460,7 +1464,8 @@ static int lane_product(LaneRun &r, const DevPlane &pl, LaneStageArgs sa, int *s
     ga.out_stride = pl.n_rb * 16;
     ga.split = igc_lane_gemm_split(B.split_lanes > 0 ? B.split_lanes : r.M, pl.n_rb, pl.n_cc, r.m->sm_count);
   }
-  CKL(igc_launch_lane_gemm(&ga, r.st));
+  if (!pl.tm_ok) return IGC_FAIL_SUPPORT;  // the driver offered no tensor-map encoder
+  CKL(igc_launch_lane_gemm(&ga, &pl.tm_codes, &pl.tm_scales, r.st));
   *split_out = ga.split;
   return IGC_OKAY;
 }
