@@ -143,11 +143,9 @@ __host__ __device__ __forceinline__ uint32_t lg_swz(int r, int j) {
 // scales); a slot is refilled once the products that read its activations
 // have committed.  The weight ring holds the dequantised hi and lo weight
 // blocks; the dequant warps refill a slot once the products of the step two
-// back have committed.  The rings are sized so that two blocks share an SM
-// (two copy slots and one weight slot each, 107 KB): one block's chain of
-// copy, dequant and products overlaps the other's.
-constexpr int LG_RSTAGES = 2, LG_BSTAGES = 1;
-constexpr int LG_BLOCKS_PER_SM = 2;
+// back have committed.  Four copy slots let the copies run ahead of the
+// dequant and the products by four steps.
+constexpr int LG_RSTAGES = 4, LG_BSTAGES = 2;
 constexpr int LG_OP_BYTES = 128 * 64 * 2;       // one operand block: 128 rows x 64 columns of f16, 16 KB
 constexpr int LG_A_BYTES = LG_OP_BYTES;         // activations, hi (then lo)
 constexpr int LG_B_BYTES = LG_OP_BYTES;         // weights, hi (then lo)
@@ -165,7 +163,7 @@ constexpr int LG_DQ_WARPS = 8;  // warps that turn codes into weights (then run 
 constexpr int LG_THREADS = 64 + 32 * LG_DQ_WARPS;
 constexpr int LG_TRIES = 1 << 22;  // polls a wait makes before it gives up
 
-__global__ void __launch_bounds__(LG_THREADS, LG_BLOCKS_PER_SM)
+__global__ void __launch_bounds__(LG_THREADS, 1)
     lane_gemm_kernel(LaneGemmArgs a, const __grid_constant__ CUtensorMap tm_codes,
                      const __grid_constant__ CUtensorMap tm_scales) {
   extern __shared__ __align__(1024) uint8_t lg_raw[];
@@ -277,7 +275,7 @@ __global__ void __launch_bounds__(LG_THREADS, LG_BLOCKS_PER_SM)
     for (int k = 0; k < nk; ++k) {
       const int rs = k % LG_RSTAGES, b = k % LG_BSTAGES;
       bool ok = mbar_wait(&full[rs], (uint32_t)((k / LG_RSTAGES) & 1), failed ? 1 : LG_TRIES);
-      if (k >= LG_BSTAGES)  // the products that last read this weight slot have completed
+      if (k >= LG_BSTAGES)  // the products of the step two back have read this weight slot
         ok = mbar_wait(&bempty[b], (uint32_t)(((k / LG_BSTAGES) - 1) & 1), (failed || !ok) ? 1 : LG_TRIES) && ok;
       if (__any_sync(0xffffffffu, !ok)) failed = true;
       uint8_t *st = base + rs * LG_RSLOT;
