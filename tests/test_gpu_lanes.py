@@ -142,3 +142,41 @@ def test_crowd_round_matches_each_session_alone(igc_lib, small_dir):
     solo = np.concatenate([crowd.round([s], blocks[j:j + 1], want_logits=True)[2] for j, s in enumerate(crowd_s)])
     assert np.array_equal(solo, rows)
     crowd.close()
+
+
+def test_crowd_refuses_what_it_cannot_run(igc_lib, small_dir, tiny_dir):
+    """A crowd round refuses, before anything runs and leaving every session
+    as it was: a session named twice, a session with a block in flight, a
+    session of another model, a full window, more sessions than the crowd
+    holds, and lanes a session that do not split into attention groups."""
+    from conftest import SMALL, TINY
+    m = igc_lib.Model(folder=small_dir, window_limit=SMALL["window_limit"])
+    other = igc_lib.Model(folder=tiny_dir, window_limit=TINY["window_limit"])
+    a, b = igc_lib.Session(m), igc_lib.Session(m)
+    for s in (a, b):
+        s.prime(np.arange(3, 30, dtype=np.int32))
+    crowd = igc_lib.Crowd(m, 2, 4)
+    blk = np.array([[29, 1, 2, 3], [29, 4, 5, 6]], np.int32)
+
+    def refused(sessions, blocks, code):
+        fills = [s.fill for s in sessions]
+        with pytest.raises(igc_lib.IgcError) as e:
+            crowd.round(sessions, blocks)
+        assert e.value.code == code
+        assert [s.fill for s in sessions] == fills
+
+    refused([a, a], blk, igc_lib.FAIL_ARGUMENT)
+    refused([a, igc_lib.Session(other)], blk, igc_lib.FAIL_ARGUMENT)
+    refused([a, b, igc_lib.Session(m)], np.tile(blk[:1], (3, 1)), igc_lib.FAIL_ARGUMENT)
+    b.guess(np.array([29, 7], np.int32), want_logits=False)
+    refused([a, b], blk, igc_lib.FAIL_STATE)
+    b.guess_keep(0)
+    full = igc_lib.Session(m)
+    full.prime(np.arange(SMALL["window_limit"] - 2, dtype=np.int32) % SMALL["vocab"])
+    refused([a, full], blk, igc_lib.FAIL_STATE)
+    take, made, _ = crowd.round([a, b], blk)  # the same sessions, unrefused, still run
+    assert a.fill == 26 + take[0] + 1 and b.fill == 26 + take[1] + 1  # primed to 26, then take + 1 kept
+    crowd.close()
+    with pytest.raises(igc_lib.IgcError) as e:
+        igc_lib.Crowd(m, 4, 6)
+    assert e.value.code == igc_lib.FAIL_SUPPORT
