@@ -65,7 +65,8 @@ class SynthSpec(ctypes.Structure):
                 ("inner", ctypes.c_int), ("ple_dim", ctypes.c_int), ("slide_span", ctypes.c_int),
                 ("share_count", ctypes.c_int), ("global_every", ctypes.c_int),
                 ("window_limit", ctypes.c_int), ("norm_offset", ctypes.c_float),
-                ("with_layer_scalar", ctypes.c_int), ("seed", ctypes.c_uint64)]
+                ("with_layer_scalar", ctypes.c_int), ("seed", ctypes.c_uint64),
+                ("cache_scale_k", ctypes.c_float), ("cache_scale_v", ctypes.c_float)]
 
 
 def spec_e2b(norm_offset=0.0, seed=1, window_limit=32768):
@@ -86,6 +87,16 @@ class IgcPlane(ctypes.Structure):  # app_core.c:1775 plane
                 ("code_bias", ctypes.c_int), ("code_flip", ctypes.c_int),
                 ("group_size", ctypes.c_int), ("group_count", ctypes.c_int),
                 ("enter_gain", ctypes.c_float), ("leave_gain", ctypes.c_float)]
+
+
+KEEP_PROMPT = 0  # app_core.c:367
+KEEP_TALK = 1    # app_core.c:368
+KEEP_RUNS = 16   # app_core.c:385
+
+
+class KeepNote(ctypes.Structure):  # app_core.c:387-392 app_keep_note
+    _fields_ = [("run_count", ctypes.c_int), ("from_list", ctypes.c_int32 * KEEP_RUNS),
+                ("till_list", ctypes.c_int32 * KEEP_RUNS), ("mark_list", ctypes.c_uint64 * KEEP_RUNS)]
 
 
 class _Desk(ctypes.Structure):
@@ -164,6 +175,15 @@ def _lib():
         "igc_crowd_open": (i, [vp, i, i, _P(vp)]),
         "igc_crowd_close": (None, [vp]),
         "igc_crowd_round": (i, [vp, _P(vp), i, i32p, i32p, i32p, fp]),
+        "igc_session_save": (i, [vp, ctypes.c_char_p, ctypes.c_uint64, _P(KeepNote), i]),
+        "igc_session_load": (i, [vp, ctypes.c_char_p, _P(ctypes.c_uint64), _P(KeepNote), _P(ctypes.c_int)]),
+        "igc_session_ids": (i, [vp, i32p, i]),
+        "igc_keep_note_share": (i, [_P(KeepNote), _P(KeepNote), i]),
+        "igc_model_cache_scale": (ctypes.c_float, [vp, i, i]),
+        "igc_session_cache_peak": (ctypes.c_float, [vp, i, i]),
+        "igc_session_cache_room": (ctypes.c_size_t, [vp]),
+        "igc_session_cache_room_at": (ctypes.c_size_t, [vp, i]),
+        "igc_model_memory_bytes": (ctypes.c_size_t, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -189,6 +209,9 @@ def exported_symbols():
         "igc_scout_clear", "igc_scout_note", "igc_scout_span", "igc_scout_draw", "igc_synth_fill",
         "igc_synth_write", "igc_model_synth", "igc_last_error", "igc_launch_count", "igc_norm_rms_fixed",
         "igc_crowd_open", "igc_crowd_close", "igc_crowd_round",
+        "igc_session_save", "igc_session_load", "igc_session_ids", "igc_keep_note_share",
+        "igc_model_cache_scale", "igc_session_cache_peak", "igc_session_cache_room", "igc_session_cache_room_at",
+        "igc_model_memory_bytes",
     ]
 
 
@@ -210,10 +233,10 @@ def launch_count():
 class Model:
     """app_core.c:12439 model_load (or a synthetic spec built straight in HBM)."""
 
-    def __init__(self, folder=None, spec=None, device=0, window_limit=0):
+    def __init__(self, folder=None, spec=None, device=0, window_limit=0, cache_bits=0):
         lib = _lib()
         self._h = ctypes.c_void_p()
-        setup = Setup(device, window_limit, 0, 0)
+        setup = Setup(device, window_limit, 0, int(cache_bits))
         if spec is not None:
             _check(lib.igc_model_synth(ctypes.byref(spec), ctypes.byref(setup), ctypes.byref(self._h)),
                    "model_synth")
@@ -242,6 +265,14 @@ class Model:
     def linear_params(self):
         """Weights of the int4 projections one lane multiplies (head included)."""
         return _lib().igc_model_weight_count(self._h)
+
+    def memory_bytes(self):
+        """app_core.c:12667 model_memory_bytes."""
+        return _lib().igc_model_memory_bytes(self._h)
+
+    def cache_scale(self, layer, value_side):
+        """app_core.c:14515 model_cache_scale."""
+        return _lib().igc_model_cache_scale(self._h, int(layer), int(value_side))
 
     def close(self):
         if self._h:
@@ -283,6 +314,36 @@ class Session:
 
     def hold(self, keep):
         _check(_lib().igc_session_hold(self._h, int(keep)), "session_hold")
+
+    def save(self, path, stamp=0, note=None, kind=KEEP_PROMPT):
+        """app_core.c:14010 session_save."""
+        _check(_lib().igc_session_save(self._h, str(path).encode(), int(stamp),
+                                       ctypes.byref(note) if note is not None else None, int(kind)),
+               "session_save")
+
+    def load(self, path):
+        """app_core.c:14076 session_load; returns (stamp, note, kind)."""
+        stamp, note, kind = ctypes.c_uint64(), KeepNote(), ctypes.c_int()
+        _check(_lib().igc_session_load(self._h, str(path).encode(), ctypes.byref(stamp), ctypes.byref(note),
+                                       ctypes.byref(kind)), "session_load")
+        return stamp.value, note, kind.value
+
+    def ids(self):
+        """app_core.c:14183 session_ids."""
+        n = _lib().igc_session_ids(self._h, None, 0)
+        a = np.zeros(max(n, 1), np.int32)
+        _lib().igc_session_ids(self._h, a.ctypes.data_as(_P(ctypes.c_int32)), len(a))
+        return a[:n]
+
+    def cache_peak(self, layer, value_side):
+        """app_core.c:14540 session_cache_peak."""
+        return _lib().igc_session_cache_peak(self._h, int(layer), int(value_side))
+
+    def cache_room(self, cache_bits=None):
+        """Bytes the caches occupy (at `cache_bits` storage when given)."""
+        if cache_bits is None:
+            return _lib().igc_session_cache_room(self._h)
+        return _lib().igc_session_cache_room_at(self._h, int(cache_bits))
 
     def prime(self, ids):
         a, p = _ids(ids)
@@ -557,7 +618,7 @@ def synth_tensors(spec, threads=8):
     out = {}
     for t in room:
         shape = [t.shape[0], t.shape[1]] if t.rank == 2 else [t.shape[0]]
-        arr = np.empty(shape, np.uint8 if t.dtype == 6 else np.uint16)
+        arr = np.empty(shape, {6: np.uint8, 1: np.float32}.get(t.dtype, np.uint16))
         _check(lib.igc_synth_tensor_fill(ctypes.byref(spec), ctypes.byref(t), arr.ctypes.data_as(ctypes.c_void_p),
                                          threads), "synth_tensor_fill")
         out[t.name.decode()] = (_DTYPE_NAME[t.dtype], arr)
@@ -584,3 +645,8 @@ def synth_fill(seed, name, kind, count, offset=0.0, threads=1):
     _check(lib.igc_synth_fill(seed, stream, kind, offset, count, out.ctypes.data_as(ctypes.c_void_p), threads),
            "synth_fill")
     return out
+
+
+def keep_note_share(held, now, same_count):
+    """app_core.c:13991 keep_note_share."""
+    return _lib().igc_keep_note_share(ctypes.byref(held), ctypes.byref(now), int(same_count))

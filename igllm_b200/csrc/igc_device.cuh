@@ -210,4 +210,55 @@ __device__ __forceinline__ float logit_cap(float x, float cap) {
   return cap * (1.0f - 2.0f / (expf(t + t) + 1.0f));
 }
 
+// The byte cache's 8-bit float, e4m3 (app_core.c:10975-11035 cache_pack8,
+// cache_code8, cache_real8): one sign bit, four exponent bits biased by 7,
+// three significand bits.  Exponent field 0 counts steps of 2^-9 outright;
+// any other field e holds (8 + significand) * 2^(e - 10).  Encoding rounds to
+// nearest with ties to even, saturates at +-448 (code 0x7E, so the NaN code
+// 0x7F never appears), stores a NaN as +448 and anything that rounds to zero
+// as +0.  Worked from the format's
+// definition on the float's exponent bits: a in [2^e, 2^(e+1)) has steps of
+// 2^(e-3), and the rounded step count q in [8, 16] gives the code
+// ((e + 7) << 3) + q - 8, a carry into the next exponent when q is 16.
+__device__ __forceinline__ uint32_t cache_code8(float x) {
+  const uint32_t sign = x < 0.0f ? 0x80u : 0u;
+  const float a = fabsf(x);
+  if (!(a < 448.0f)) return sign | 0x7Eu;
+  if (a < 0.015625f) {
+    const uint32_t q = (uint32_t)rintf(a * 512.0f);
+    return q ? sign | q : 0u;  // a value that rounds to zero stores +0
+  }
+  const int e = (int)((__float_as_uint(a) >> 23) & 0xFFu) - 127;
+  const float q = rintf(a * __uint_as_float((uint32_t)(127 + 3 - e) << 23));
+  return sign | (uint32_t)(((e + 7) << 3) + (int)q - 8);
+}
+
+__device__ __forceinline__ float cache_real8(uint32_t code) {
+  const uint32_t f = (code >> 3) & 15u, m = code & 7u;
+  const float a = f == 0 ? (float)m * 0.001953125f : (float)(8u + m) * __uint_as_float((f + 127u - 10u) << 23);
+  return (code & 0x80u) ? -a : a;
+}
+
+// How a layer's key and value caches are stored, and where the largest
+// magnitudes written go.  A side whose scale is 0 holds float rows; a
+// positive scale makes it e4m3 bytes of value / scale (written by
+// lane_kv_kernel, read back as float rows by lane_widen_kernel; the
+// attention kernel itself reads float rows only).  `peak` ([key, value]) or,
+// for a batched launch, peak_tab[block z] takes the running maximum of
+// |value| over every row written (app_core.c:11208 cache_lay).
+struct CacheStore {
+  float kq, vq;
+  float *peak;
+  float *const *peak_tab;
+};
+
+// A stored value of a byte side: the decoded grid value times the side's
+// scale, one rounding, as the reference's dequantizing table holds it
+// (app_core.c:11050 cache_grid_fill).
+__device__ __forceinline__ float cache_load8(uint32_t code, float scale) { return __fmul_rn(cache_real8(code), scale); }
+
+// A value's code on a byte side: value / scale onto the grid (app_core.c:11205
+// cache_lay divides by the scale, then cache_code8).
+__device__ __forceinline__ uint32_t cache_store8(float x, float scale) { return cache_code8(__fdiv_rn(x, scale)); }
+
 }  // namespace igc

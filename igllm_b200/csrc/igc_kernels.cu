@@ -409,7 +409,8 @@ __device__ __forceinline__ void bf16x8_scaled(const uint4 &w, float gain, float4
 __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embed, int hidden,
                              float embed_gain, const uint16_t *ple_embed, int ple_vocab,
                              int ple_width, float ple_gain, float *x_out, float *seed_out,
-                             unsigned long long *stamp, int stamp_n) {
+                             unsigned long long *stamp, int stamp_n, const float *peak, float *peak_saved,
+                             int peak_n) {
   pdl_release();
   // the pass's launch stamps start over (every later kernel of the pass
   // stamps only after its wait, so after this kernel has finished)
@@ -418,6 +419,10 @@ __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embe
       stamp[2 * i] = ~0ull;
       stamp[2 * i + 1] = 0ull;
     }
+  // the cache peaks as they stand before this pass writes any row, for a
+  // block that is then kept with no lane (app_core.c:12153-12156)
+  if (peak_saved && blockIdx.x == 1 % gridDim.x && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < peak_n; i += blockDim.x) peak_saved[i] = peak[i];
   const int j = blockIdx.x;
   if (j >= lanes) return;
   const int id = ids[j];
@@ -655,14 +660,18 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
                                                    const float *sn_tab, float eps, int owner, float *kc, float *vc,
                                                    int sliding, int span, const int *d_p0, int lanes, float *out,
                                                    int out_stride, float *out_amax, unsigned long long *stamp,
-                                                   float *const *kc_tab, float *const *vc_tab, const int *pos_tab) {
+                                                   float *const *kc_tab, float *const *vc_tab, const int *pos_tab,
+                                                   CacheStore cq) {
   using LY = AttnLayout<HD>;
+  float *peak = cq.peak;
   if (kc_tab) {
-    // one of many sessions' blocks (blockIdx.z): its caches and position
-    // from the tables, its `lanes` rows of the batch's q|k|v and output
+    // one of many sessions' blocks (blockIdx.z): its caches, peaks and
+    // position from the tables, its `lanes` rows of the batch's q|k|v and
+    // output
     const int zb = blockIdx.z;
     kc = kc_tab[zb];
     vc = vc_tab[zb];
+    if (cq.peak_tab) peak = cq.peak_tab[zb];
     d_p0 = pos_tab + zb;
     qkv += (size_t)zb * lanes * qkv_stride;
     out += (size_t)zb * lanes * out_stride;
@@ -748,6 +757,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
       bool live[3], norm[3], turn[3];
       const float *gain[3];
       float *dst[3], *cache[3];
+      int side[3];  // 0 key, 1 value
 #pragma unroll
       for (int b = 0; b < 3; ++b) {
         const int k = k0 + b;
@@ -755,6 +765,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
         norm[b] = turn[b] = false;
         gain[b] = nullptr;
         dst[b] = cache[b] = nullptr;
+        side[b] = 0;
         const float *src = nullptr;
         int pos = 0;
         if (k < 2) {
@@ -773,6 +784,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
             pos = p0 + jj;
             live[b] = true;
             dst[b] = is_v ? newv + jj * VS : newk + jj * KS;
+            side[b] = is_v;
             float *crow = (is_v ? vc : kc) + (size_t)pos * kv_w + (size_t)kh * HD;
             if (owner) {
               src = qkv + (size_t)jj * qkv_stride + (size_t)heads * HD + (is_v ? kv_w : 0) + (size_t)kh * HD;
@@ -791,6 +803,14 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
       for (int b = 0; b < 3; ++b) {
         if (!live[b]) continue;
         if (norm[b]) head_row_finish<DPL>(R[b], gain[b] != nullptr, eps, turn[b], l);
+        if (cache[b] && peak) {
+          // the row's largest magnitude (app_core.c:11208 cache_lay; a NaN is passed over)
+          float mx = 0.0f;
+#pragma unroll
+          for (int e = 0; e < DPL; ++e) mx = fmaxf(mx, fabsf(R[b].v[e]));
+          mx = warp_max(mx);
+          if (l == 0) atomicMax(reinterpret_cast<int *>(peak) + side[b], __float_as_int(mx));
+        }
         store_dpl<DPL>(dst[b] + l * DPL, R[b].v);
         if (cache[b]) store_dpl<DPL>(cache[b] + l * DPL, R[b].v);
       }
@@ -1488,10 +1508,11 @@ size_t igc_gemv_smem_min(const GemvArgs *a, int pair) {
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
                              float *x_out, float *seed_out, unsigned long long *stamp, int stamp_n,
-                             cudaStream_t st) {
-  if ((hidden & 7) || (ple_embed && (ple_width & 7))) return cudaErrorInvalidValue;
+                             const float *peak, float *peak_saved, int peak_n, cudaStream_t st) {
+  if ((hidden & 7) || (ple_embed && (ple_width & 7)) || (peak_saved && (!peak || peak_n < 0)))
+    return cudaErrorInvalidValue;
   embed_kernel<<<dim3(lanes, 8), 256, 0, st>>>(ids, lanes, embed, hidden, embed_gain, ple_embed, ple_vocab, ple_width,
-                                      ple_gain, x_out, seed_out, stamp, stamp_n);
+                                      ple_gain, x_out, seed_out, stamp, stamp_n, peak, peak_saved, peak_n);
   return cudaGetLastError();
 }
 
@@ -1518,7 +1539,7 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const fl
                                const float *sn, float eps, int owner, float *kc, float *vc, int sliding, int span,
                                const int *d_p0, int lanes, float *out, int out_stride, float *out_amax,
                                unsigned long long *stamp, float *const *kc_tab, float *const *vc_tab,
-                               const int *pos_tab) {
+                               const int *pos_tab, CacheStore cq) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(256);
@@ -1535,17 +1556,18 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const fl
   cfg.numAttrs = g_pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, attn_kernel<HD, CX>, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
                             owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp, kc_tab,
-                            vc_tab, pos_tab);
+                            vc_tab, pos_tab, cq);
 }
 }  // extern "C++"
 
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
-                            int out_stride, float *out_amax, unsigned long long *stamp, cudaStream_t st) {
+                            int out_stride, float *out_amax, unsigned long long *stamp, const igc::CacheStore *store,
+                            cudaStream_t st) {
   return igc_launch_attn_many(qkv, qkv_stride, heads, kv_heads, hd, q_norm, k_norm, cs, sn, eps, owner, kc, vc, sliding,
                               span, d_p0, lanes, cluster, out, out_stride, out_amax, stamp, nullptr, nullptr, nullptr, 1,
-                              st);
+                              store, st);
 }
 
 cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
@@ -1553,20 +1575,24 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
                                  int owner, float *kc, float *vc, int sliding, int span, const int *d_p0, int lanes,
                                  int cluster, float *out, int out_stride, float *out_amax, unsigned long long *stamp,
                                  float *const *kc_tab, float *const *vc_tab, const int *pos_tab, int batch,
-                                 cudaStream_t st) {
+                                 const igc::CacheStore *store, cudaStream_t st) {
   if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads || (cluster != 8 && cluster != 16) ||
       batch < 1 || (batch > 1 && !kc_tab))
     return cudaErrorInvalidValue;
+  igc::CacheStore cq = {};
+  if (store) cq = *store;
+  // float caches only: a byte side is decoded into float rows first (igc_launch_lane_widen)
+  if (cq.kq != 0.0f || cq.vq != 0.0f || (cq.peak_tab && !kc_tab)) return cudaErrorInvalidValue;
   const size_t smem = igc_attn_smem(hd);
   const int G = heads / kv_heads;
   const dim3 grid(cluster, kv_heads * ((lanes * G + AT_ROWS - 1) / AT_ROWS), batch);
 #define IGC_ATT(HD)                                                                                              \
   return cluster == 8 ? launch_attn<HD, 8>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                            sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,   \
-                                           out_amax, stamp, kc_tab, vc_tab, pos_tab)                              \
+                                           out_amax, stamp, kc_tab, vc_tab, pos_tab, cq)                          \
                       : launch_attn<HD, 16>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                             sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,  \
-                                            out_amax, stamp, kc_tab, vc_tab, pos_tab);
+                                            out_amax, stamp, kc_tab, vc_tab, pos_tab, cq);
   switch (hd) {
     case 32: IGC_ATT(32)
     case 64: IGC_ATT(64)

@@ -31,7 +31,7 @@ size_t igc_gemv_smem_min(const igc::GemvArgs *a, int pair);
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
                              float *x_out, float *seed_out, unsigned long long *stamp, int stamp_n,
-                             cudaStream_t st);
+                             const float *peak, float *peak_saved, int peak_n, cudaStream_t st);
 cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes, int layers, int ple_dim,
                                   const float *w, float eps, float blend, float *out, cudaStream_t st);
 size_t igc_attn_smem(int hd);
@@ -39,11 +39,14 @@ size_t igc_attn_smem(int hd);
 // layer's cache writes, scores, softmax and values over 16-position tiles,
 // and the merge of the cluster's partials); `cluster` (8 or 16) blocks a
 // cluster, a session constant.  `out_amax`, when given, gets each lane's
-// largest |out| per (head, cluster block), [heads * cluster][16].
+// largest |out| per (head, cluster block), [heads * cluster][16].  `store`
+// (nullable: float sides, no peaks) says which sides of the cache are e4m3
+// bytes and where the rows' largest magnitudes go.
 cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *q_norm,
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
-                            int out_stride, float *out_amax, unsigned long long *stamp, cudaStream_t st);
+                            int out_stride, float *out_amax, unsigned long long *stamp, const igc::CacheStore *store,
+                            cudaStream_t st);
 // The same for `batch` sessions' blocks of `lanes` lanes each in one launch
 // (blockIdx.z the session): session z's caches are kc_tab[z] / vc_tab[z],
 // its first position pos_tab[z], its rows of q|k|v and of the output follow
@@ -53,7 +56,7 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
                                  int owner, float *kc, float *vc, int sliding, int span, const int *d_p0, int lanes,
                                  int cluster, float *out, int out_stride, float *out_amax, unsigned long long *stamp,
                                  float *const *kc_tab, float *const *vc_tab, const int *pos_tab, int batch,
-                                 cudaStream_t st);
+                                 const igc::CacheStore *store, cudaStream_t st);
 // `stamp_sum`, when given, gets each of the pass's `stamp_n` stamped launches'
 // spans added (igc_device.cuh stamp_begin / stamp_end).
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,

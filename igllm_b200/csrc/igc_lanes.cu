@@ -540,19 +540,38 @@ __global__ void lane_argmax_kernel(const float *val, const int *idx, int parts, 
   if (tid == 0) top[j] = si[0];
 }
 
-// A prime chunk's new key and value rows, written to an owner layer's cache
-// before its attention runs (app_core.c:11500-11512): one block a lane at
-// position *p0 + lane; keys normed (k_norm) and turned, values normed with no
-// weight.  A warp a head row; a lane holds dimensions d and d + hd/2 for
-// d = lane + 32 e.  With every row of the chunk in the cache, the attention
-// of all the chunk's 16-lane groups runs as one launch.
+// A pass's new key and value rows, written to an owner layer's cache before
+// its attention runs (app_core.c:11500-11512): one block a lane at position
+// *p0 + lane; keys normed (k_norm) and turned, values normed with no weight,
+// each side stored as floats or, where its scale is positive, as e4m3 codes
+// of value / scale.  A warp a head row; a lane holds dimensions d and d +
+// hd/2 for d = lane + 32 e.  With every row of the pass in the cache, the
+// attention of all its 16-lane groups runs as one launch.  With `tab` set,
+// lane j belongs to session j / per at position tab->pos[j / per] + j % per,
+// with that session's caches and peaks.
+struct KvTables {
+  const int *pos;
+  float *const *kc, *const *vc, *const *peak;
+  int per;
+};
+
 __global__ void __launch_bounds__(256) lane_kv_kernel(const float *qkv, int qkv_stride, int heads, int kv_heads,
                                                       int hd, const float *k_norm, const float *cs_tab,
                                                       const float *sn_tab, float eps, const int *p0, float *kc,
-                                                      float *vc) {
+                                                      float *vc, CacheStore cq, KvTables tab) {
   pdl_release();
   pdl_wait();
-  const int j = blockIdx.x, p = *p0 + j;
+  const int j = blockIdx.x;
+  int p;
+  if (tab.pos) {
+    const int z = j / tab.per;
+    p = tab.pos[z] + (j - z * tab.per);
+    kc = tab.kc[z];
+    vc = tab.vc[z];
+    cq.peak = tab.peak ? tab.peak[z] : nullptr;
+  } else {
+    p = *p0 + j;
+  }
   const int half = hd / 2, kv_w = kv_heads * hd;
   const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
   const float *row = qkv + (size_t)j * qkv_stride + (size_t)heads * hd;
@@ -561,8 +580,11 @@ __global__ void __launch_bounds__(256) lane_kv_kernel(const float *qkv, int qkv_
     const bool is_v = it >= kv_heads;
     const int kh = is_v ? it - kv_heads : it;
     const float *src = row + (is_v ? kv_w : 0) + (size_t)kh * hd;
-    float *dst = (is_v ? vc : kc) + (size_t)p * kv_w + (size_t)kh * hd;
-    float lo[4], hi[4], ss = 0.0f;
+    const size_t at = (size_t)p * kv_w + (size_t)kh * hd;
+    const float q = is_v ? cq.vq : cq.kq;  // a byte side's scale, else 0
+    float *dst = (is_v ? vc : kc) + at;
+    uint8_t *dstb = reinterpret_cast<uint8_t *>(is_v ? vc : kc) + at;
+    float lo[4], hi[4], ss = 0.0f, mx = 0.0f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const int d = l + 32 * e;
@@ -584,8 +606,49 @@ __global__ void __launch_bounds__(256) lane_kv_kernel(const float *qkv, int qkv_
         x = x2;
         y = y2;
       }
-      dst[d] = x;
-      dst[d + half] = y;
+      mx = fmaxf(mx, fmaxf(fabsf(x), fabsf(y)));
+      if (q > 0.0f) {
+        dstb[d] = (uint8_t)cache_store8(x, q);
+        dstb[d + half] = (uint8_t)cache_store8(y, q);
+      } else {
+        dst[d] = x;
+        dst[d + half] = y;
+      }
+    }
+    // the row's largest magnitude (app_core.c:11208 cache_lay's peak)
+    mx = warp_max(mx);
+    if (cq.peak && l == 0) atomicMax(reinterpret_cast<int *>(cq.peak) + (is_v ? 1 : 0), __float_as_int(mx));
+  }
+}
+
+// Rows of a layer's byte cache sides decoded into float rows the attention
+// kernel reads (app_core.c:11050 cache_grid_fill's table: each code's grid
+// value times the side's scale): block row z covers one session, rows [lo,
+// p0 + lanes) with lo = p0 - span + 1 on a sliding layer (not below 0) and
+// 0 on a global one, 16 codes a thread and step.  A float side is skipped.
+__global__ void __launch_bounds__(256) lane_widen_kernel(WidenArgs w) {
+  pdl_release();
+  pdl_wait();
+  const int z = blockIdx.y;
+  const uint8_t *kc = w.kc_tab ? reinterpret_cast<const uint8_t *>(w.kc_tab[z]) : w.kc;
+  const uint8_t *vc = w.vc_tab ? reinterpret_cast<const uint8_t *>(w.vc_tab[z]) : w.vc;
+  float *kf = w.kf_tab ? w.kf_tab[z] : w.kf, *vf = w.vf_tab ? w.vf_tab[z] : w.vf;
+  const int p0 = w.pos_tab ? w.pos_tab[z] : *w.p0;
+  const int lo = w.sliding ? max(0, p0 - w.span + 1) : 0;
+  const size_t first = (size_t)lo * w.kv_w, n16 = (size_t)(p0 + w.lanes - lo) * w.kv_w / 16;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t at = first + 16 * i;
+#pragma unroll
+    for (int side = 0; side < 2; ++side) {
+      const float q = side ? w.vq : w.kq;
+      if (!(q > 0.0f)) continue;
+      const uint4 c = *reinterpret_cast<const uint4 *>((side ? vc : kc) + at);
+      float4 *o = reinterpret_cast<float4 *>((side ? vf : kf) + at);
+      const uint32_t ws[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        o[k] = make_float4(cache_load8(ws[k] & 0xFFu, q), cache_load8((ws[k] >> 8) & 0xFFu, q),
+                           cache_load8((ws[k] >> 16) & 0xFFu, q), cache_load8(ws[k] >> 24, q));
     }
   }
 }
@@ -721,10 +784,38 @@ cudaError_t igc_launch_lane_gemm(const LaneGemmArgs *a, const CUtensorMap *codes
 
 cudaError_t igc_launch_lane_kv(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *k_norm,
                                const float *cs, const float *sn, float eps, const int *p0, int lanes, float *kc,
-                               float *vc, cudaStream_t st) {
+                               float *vc, const CacheStore *store, cudaStream_t st) {
+  return igc_launch_lane_kv_many(qkv, qkv_stride, heads, kv_heads, hd, k_norm, cs, sn, eps, p0, lanes, kc, vc, store,
+                                 nullptr, nullptr, nullptr, nullptr, 0, st);
+}
+
+cudaError_t igc_launch_lane_kv_many(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
+                                    const float *k_norm, const float *cs, const float *sn, float eps, const int *p0,
+                                    int lanes, float *kc, float *vc, const CacheStore *store, const int *pos_tab,
+                                    float *const *kc_tab, float *const *vc_tab, float *const *peak_tab, int per,
+                                    cudaStream_t st) {
   if (lanes < 1 || hd % 32 || hd > 256 || kv_heads < 1) return cudaErrorInvalidValue;
+  if (pos_tab ? (!kc_tab || !vc_tab || per < 1 || lanes % per) : (!p0 || !kc || !vc)) return cudaErrorInvalidValue;
+  CacheStore cq = {};
+  if (store) cq = *store;
+  if (!(cq.kq >= 0.0f) || !(cq.vq >= 0.0f)) return cudaErrorInvalidValue;
+  KvTables tab = {pos_tab, kc_tab, vc_tab, peak_tab, per};
   return lane_launch(lane_kv_kernel, dim3(lanes), dim3(256), 0, st, qkv, qkv_stride, heads, kv_heads, hd, k_norm, cs,
-                     sn, eps, p0, kc, vc);
+                     sn, eps, p0, kc, vc, cq, tab);
+}
+
+cudaError_t igc_launch_lane_widen(const WidenArgs *w, int batch, int rows_most, int sm_count, cudaStream_t st) {
+  if (!w || batch < 1 || rows_most < 1 || w->kv_w < 16 || w->kv_w % 16 || w->lanes < 1) return cudaErrorInvalidValue;
+  if (!(w->kq >= 0.0f) || !(w->vq >= 0.0f)) return cudaErrorInvalidValue;
+  if (batch > 1 && (!w->pos_tab || !w->kc_tab || !w->vc_tab || !w->kf_tab || !w->vf_tab)) return cudaErrorInvalidValue;
+  if (!w->pos_tab && !w->p0) return cudaErrorInvalidValue;
+  // enough blocks for the most rows a launch can see, at most about two
+  // waves of the GPU in all (each thread then strides)
+  const long steps = ((long)rows_most * w->kv_w / 16 + 255) / 256;
+  long x = steps < 1 ? 1 : steps;
+  const long cap = (2L * sm_count * 4 + batch - 1) / batch;
+  if (x > cap) x = cap < 1 ? 1 : cap;
+  return lane_launch(lane_widen_kernel, dim3((unsigned)x, batch), dim3(256), 0, st, *w);
 }
 
 cudaError_t igc_launch_lane_argmax(const float *val, const int *idx, int parts, int lanes, int32_t *top,

@@ -61,6 +61,18 @@ struct LaneGemmArgs {
   float cap;
 };
 
+// A byte cache's rows decoded into float rows (igc_launch_lane_widen): one
+// session by pointers, or block row z's session by the tables.
+struct WidenArgs {
+  const uint8_t *kc, *vc;  // the byte caches (a side whose scale is 0 is not read)
+  float *kf, *vf;          // the float rows, the same layout
+  const int *p0;           // the pass's first position
+  float *const *kc_tab, *const *vc_tab, *const *kf_tab, *const *vf_tab;
+  const int *pos_tab;
+  float kq, vq;            // the sides' scales, 0 for a float side
+  int kv_w, lanes, sliding, span;
+};
+
 }  // namespace igc
 
 extern "C" {
@@ -78,11 +90,26 @@ int igc_lane_tmaps(const void *tiles, const void *scales, int n_rb, int n_cc, CU
                    CUtensorMap *scales_map);
 cudaError_t igc_launch_lane_gemm(const igc::LaneGemmArgs *a, const CUtensorMap *codes_map,
                                  const CUtensorMap *scales_map, cudaStream_t st);
-// A prime chunk's `lanes` new key and value rows (normed; keys turned) into
-// an owner layer's caches at positions *p0 + lane.
+// A pass's `lanes` new key and value rows (normed; keys turned) into an
+// owner layer's caches at positions *p0 + lane; `store` (nullable) says which
+// sides are e4m3 bytes and where the rows' peaks go.
 cudaError_t igc_launch_lane_kv(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd, const float *k_norm,
                                const float *cs, const float *sn, float eps, const int *p0, int lanes, float *kc,
-                               float *vc, cudaStream_t st);
+                               float *vc, const igc::CacheStore *store, cudaStream_t st);
+// The same for many sessions' blocks of `per` lanes: lane j is session
+// j / per's lane j % per, at pos_tab[j / per] + j % per, into that session's
+// caches kc_tab / vc_tab and peaks peak_tab (nullable).
+cudaError_t igc_launch_lane_kv_many(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
+                                    const float *k_norm, const float *cs, const float *sn, float eps, const int *p0,
+                                    int lanes, float *kc, float *vc, const igc::CacheStore *store, const int *pos_tab,
+                                    float *const *kc_tab, float *const *vc_tab, float *const *peak_tab, int per,
+                                    cudaStream_t st);
+// Byte cache rows decoded into float rows for the attention kernel: for each
+// of `batch` sessions (tables) or one (pointers), rows [lo, p0 + lanes) of
+// each byte side (lo = p0 - span + 1 on a sliding layer, clipped at 0; 0 on
+// a global one).  `rows_most` bounds the rows any launch of this shape sees
+// (it sizes the grid); kv_w, a row's values, is a multiple of 16.
+cudaError_t igc_launch_lane_widen(const igc::WidenArgs *w, int batch, int rows_most, int sm_count, cudaStream_t st);
 // out[i] = *p0 + 16 i for i < groups (a prefill chunk's attention groups).
 cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st);
 // Per lane the largest of `parts` argmax partials [part][lanes] (first index

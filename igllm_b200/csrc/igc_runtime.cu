@@ -292,6 +292,13 @@ struct DevLayer {
   int kind = 0, share = 0, source = -1, hd = 0, kv_heads = 1, inner = 0;
   int q_rows = 0, kv_rows = 0, qkv_rows = 0;
   float gain = 1.0f;
+  // the export's static ranges of an owner's key and value caches
+  // (self_attn.k_cache_scale / v_cache_scale, 0 where it ships none), and the
+  // rows the reference's ring of this layer holds (app_core.c:8723-8731
+  // cache_span: 0 on a sharing layer; the window on a global layer or the
+  // last owner of a kind that sharers read; else the sliding span)
+  float k_scale = 0.0f, v_scale = 0.0f;
+  int span = 0;
   DevPlane qkv, o, gateup, down, ple_gate, ple_proj;
   float *q_norm = nullptr, *k_norm = nullptr, *enter_norm = nullptr, *after_attn_norm = nullptr,
         *before_feed_norm = nullptr, *after_feed_norm = nullptr, *after_ple_norm = nullptr;
@@ -311,6 +318,12 @@ struct igc_model {
   float *ple_norm = nullptr, *final_norm = nullptr;
   std::vector<DevLayer> layer;
   size_t decode_bytes = 0, device_bytes = 0;
+  // bytes of every checkpoint tensor the text stack binds (app_core.c:12667
+  // model_memory_bytes, the reference's model->weight_bytes)
+  size_t weight_bytes = 0;
+  // app_setup.cache_bits: 8 stores a cache side as e4m3 bytes wherever the
+  // export ships that side's scale (app_core.c:14270-14284)
+  int cache_bits = 0;
   int max_qkv = 0, max_inner = 0, max_q = 0, max_kvw = 0;
   std::vector<void *> owned;
 
@@ -423,8 +436,23 @@ struct Binder {
     if (c != IGC_OKAY) return c;
     CK(cudaMemcpy(*out, host.data(), n * sizeof(float), cudaMemcpyHostToDevice));
     m->decode_bytes += n * sizeof(float);
+    m->weight_bytes += t->bytes;
     src.release(name);
     return IGC_OKAY;
+  }
+
+  // app_core.c:8104 scale_bind: a calibration scalar (one value of any float
+  // type), 0 where the tensor is absent or holds more than one value.
+  float scalar(const std::string &name) {
+    const Tensor *t = src.find(name);
+    if (!t) return 0.0f;
+    size_t n = 1;
+    for (int i = 0; i < t->rank; ++i) n *= (size_t)t->shape[i];
+    if (n != 1 || dtype_bytes(t->dtype) == 0 || t->bytes < dtype_bytes(t->dtype)) return 0.0f;
+    m->weight_bytes += t->bytes;
+    const float v = real_at(*t, 0);
+    src.release(name);
+    return v;
   }
 
   // app_core.c:7886 plane_bind_gemma, 4-bit U8 codes with F16 group scales.
@@ -503,6 +531,7 @@ struct Binder {
       rb_at += prb;
       // app_core.c:1860 plane_bytes: codes and scales a product streams
       m->decode_bytes += cb + sb;
+      m->weight_bytes += cb + sb;
       out.bytes += (double)(cb + sb);
       src.release(p.name + ".weight");
       src.release(p.name + ".weight_scale");
@@ -555,6 +584,7 @@ struct Binder {
     CK(cudaMemcpy(*out, t->data, t->bytes, cudaMemcpyHostToDevice));
     *rows_out = (int)t->shape[0];
     m->decode_bytes += (size_t)t->shape[1] * 2; /* app_core.c:1880 plane_row_bytes */
+    m->weight_bytes += t->bytes;
     src.release(stem + ".weight");
     return IGC_OKAY;
   }
@@ -658,6 +688,10 @@ static int bind_model(igc_model *m, Source &src) {
       if (c != IGC_OKAY) return c;
       c = b.vec(STEM("self_attn.k_norm"), L.hd, &L.k_norm);
       if (c != IGC_OKAY) return c;
+      L.k_scale = b.scalar(STEM("self_attn.k_cache_scale"));
+      L.v_scale = b.scalar(STEM("self_attn.v_cache_scale"));
+      if (!(L.k_scale > 0.0f)) L.k_scale = 0.0f;  // no grid to round onto (app_core.c:11199)
+      if (!(L.v_scale > 0.0f)) L.v_scale = 0.0f;
     } else {
       const DevLayer &S = m->layer[L.source];
       L.kv_rows = S.kv_rows;
@@ -696,7 +730,7 @@ static int bind_model(igc_model *m, Source &src) {
     }
     {
       const Tensor *g = src.find(STEM("layer_scalar"));
-      L.gain = g ? real_at(*g, 0) : 1.0f; /* app_core.c:8700-8708 */
+      L.gain = g ? real_at(*g, 0) : 1.0f; /* app_core.c:8700-8708, read and not counted in weight_bytes */
     }
 #undef STEM
     if (!igc_attn_smem(L.hd) || igc_attn_smem(L.hd) > (size_t)m->smem_limit) return IGC_FAIL_SUPPORT;
@@ -704,6 +738,20 @@ static int bind_model(igc_model *m, Source &src) {
     if (L.inner > m->max_inner) m->max_inner = L.inner;
     if (L.q_rows > m->max_q) m->max_q = L.q_rows;
     if (L.kv_rows > m->max_kvw) m->max_kvw = L.kv_rows;
+  }
+  // the reference's ring depth per layer (app_core.c:8553-8562 keep_flag,
+  // :8723-8731 cache_span); this library keeps every owner full length, and
+  // the spans describe its save files
+  for (int l = 0; l < m->layers; ++l) {
+    DevLayer &L = m->layer[l];
+    if (L.share) { L.span = 0; continue; }
+    int last = -1;
+    for (int q = 0; q < first_share; ++q)
+      if (m->kind[q] == L.kind) last = q;
+    const bool keep_full = m->share_count > 0 && last == l;
+    L.span = (L.kind == 1 || keep_full) ? m->window_limit
+                                        : (m->slide_span < m->window_limit ? m->slide_span : m->window_limit);
+    if (L.span < 1) L.span = 1;
   }
   for (int kind = 0; kind < 2; ++kind) {
     int hd = 0;
@@ -720,6 +768,7 @@ static int bind_model(igc_model *m, Source &src) {
 static int model_prepare(igc_model *m, const igc_setup *setup) {
   clear_stale("model load");
   m->device = setup ? setup->device : 0;
+  m->cache_bits = setup ? setup->cache_bits : 0;
   CK(cudaSetDevice(m->device));
   CK(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, m->device));
   CK(cudaDeviceGetAttribute(&m->smem_limit, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device));
@@ -732,7 +781,6 @@ static int model_prepare(igc_model *m, const igc_setup *setup) {
 extern "C" int igc_model_load(const char *folder, const igc_setup *setup, igc_model **model_out) {
   if (!folder || !model_out) return IGC_FAIL_ARGUMENT;
   *model_out = nullptr;
-  if (setup && setup->cache_bits != 0) return IGC_FAIL_SUPPORT;
   std::string text;
   if (!slurp(std::string(folder) + "/config.json", text)) return IGC_FAIL_MISSING;
   auto m = std::make_unique<igc_model>();
@@ -809,7 +857,19 @@ struct igc_session {
   int guess_count = 0, guess_from = 0, guess_echo = 0;
   std::vector<int32_t> echo;
   uint64_t draw_state = 0x2545F4914F6CDD1DULL;
+  // every owner layer's caches, full length: float rows, or e4m3 bytes on a
+  // side the model stores as bytes (layer_store); sharing layers hold none
   std::vector<float *> kc, vc;
+  // the largest magnitude written to each owner's caches, [layer][key, value]
+  // (app_core.c:11208 cache_lay's key_peak / value_peak), and the copy the
+  // pass in flight started from (app_core.c:12153-12156)
+  float *d_peak = nullptr, *d_peak_saved = nullptr;
+  // where a layer with a byte side has its rows decoded to floats for the
+  // attention kernel (window x widest row floats a side; one layer at a time)
+  float *kf = nullptr, *vf = nullptr;
+  // the first position whose rows every sliding layer holds: 0, except after
+  // loading a file written from rings that had turned over
+  int floor = 0;
   int *d_io = nullptr;  // [0] position, [1..16] ids
   int32_t *d_top = nullptr;  // [0..16) argmax ids, [16] the kernels' error word (d_err)
   int *d_err = nullptr;
@@ -901,6 +961,61 @@ struct igc_session {
   }
 };
 
+// How owner layer `owner`'s caches are stored: a side is e4m3 bytes where the
+// setup asks for 8-bit caches and the export ships that side's scale
+// (app_core.c:14270-14284), else float; `peak` (or per batched block
+// peak_tab) takes the magnitudes of the rows written.
+static CacheStore layer_store(const igc_model *m, int owner, float *peak, float *const *peak_tab = nullptr) {
+  const DevLayer &O = m->layer[owner];
+  const bool bytes = m->cache_bits == 8;
+  CacheStore cq;
+  cq.kq = bytes ? O.k_scale : 0.0f;
+  cq.vq = bytes ? O.v_scale : 0.0f;
+  cq.peak = peak;
+  cq.peak_tab = peak_tab;
+  return cq;
+}
+
+static size_t side_bytes(float q) { return q > 0.0f ? 1u : sizeof(float); }
+
+static bool layer_bytes(const igc_model *m, int owner) {
+  const CacheStore cq = layer_store(m, owner, nullptr);
+  return cq.kq > 0.0f || cq.vq > 0.0f;
+}
+
+// The float rows a layer's attention reads from: its owner's cache on a float
+// side, the session's decoded rows on a byte side.
+static float *attn_rows(const igc_session *s, int owner, int value_side) {
+  const CacheStore cq = layer_store(s->m, owner, nullptr);
+  if (value_side) return cq.vq > 0.0f ? s->vf : s->vc[owner];
+  return cq.kq > 0.0f ? s->kf : s->kc[owner];
+}
+
+// The decode of owner `owner`'s byte rows that a pass of `lanes` lanes reads
+// (a sliding layer's window behind its first lane, a global layer's prefix),
+// and the most rows it can cover.
+static WidenArgs widen_of(const igc_session *s, int owner, int sliding, int lanes) {
+  const igc_model *m = s->m;
+  const CacheStore cq = layer_store(m, owner, nullptr);
+  WidenArgs w;
+  memset(&w, 0, sizeof(w));
+  w.kc = reinterpret_cast<const uint8_t *>(s->kc[owner]);
+  w.vc = reinterpret_cast<const uint8_t *>(s->vc[owner]);
+  w.kf = s->kf;
+  w.vf = s->vf;
+  w.kq = cq.kq;
+  w.vq = cq.vq;
+  w.kv_w = m->layer[owner].kv_rows;
+  w.lanes = lanes;
+  w.sliding = sliding;
+  w.span = m->slide_span;
+  return w;
+}
+static int widen_rows_most(const igc_model *m, int sliding, int lanes) {
+  const int r = sliding ? m->slide_span + lanes - 1 : m->window_limit;
+  return r < m->window_limit ? r : m->window_limit;
+}
+
 extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   if (!m || !out) return IGC_FAIL_ARGUMENT;
   *out = nullptr;
@@ -916,11 +1031,29 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   for (int l = 0; l < m->layers && c == IGC_OKAY; ++l) {
     const DevLayer &L = m->layer[l];
     if (L.share) continue;
-    c = s->alloc(&s->kc[l], (size_t)m->window_limit * L.kv_rows);
-    if (c == IGC_OKAY) c = s->alloc(&s->vc[l], (size_t)m->window_limit * L.kv_rows);
-    if (c == IGC_OKAY) CK(cudaMemsetAsync(s->kc[l], 0, sizeof(float) * (size_t)m->window_limit * L.kv_rows, s->st));
-    if (c == IGC_OKAY) CK(cudaMemsetAsync(s->vc[l], 0, sizeof(float) * (size_t)m->window_limit * L.kv_rows, s->st));
+    const CacheStore cq = layer_store(m, l, nullptr);
+    const size_t kb = side_bytes(cq.kq) * (size_t)m->window_limit * L.kv_rows;
+    const size_t vb = side_bytes(cq.vq) * (size_t)m->window_limit * L.kv_rows;
+    uint8_t *kp = nullptr, *vp = nullptr;
+    c = s->alloc(&kp, kb);
+    if (c == IGC_OKAY) c = s->alloc(&vp, vb);
+    if (c != IGC_OKAY) break;
+    s->kc[l] = reinterpret_cast<float *>(kp);
+    s->vc[l] = reinterpret_cast<float *>(vp);
+    CK(cudaMemsetAsync(kp, 0, kb, s->st));  // a zero code decodes to zero: a cleared cache either way
+    CK(cudaMemsetAsync(vp, 0, vb, s->st));
   }
+  {
+    int widest = 0;  // the widest row a byte side decodes into
+    for (int l = 0; l < m->layers; ++l)
+      if (!m->layer[l].share && layer_bytes(m, l)) widest = std::max(widest, m->layer[l].kv_rows);
+    if (c == IGC_OKAY && widest > 0) c = s->alloc(&s->kf, (size_t)m->window_limit * widest);
+    if (c == IGC_OKAY && widest > 0) c = s->alloc(&s->vf, (size_t)m->window_limit * widest);
+  }
+  if (c == IGC_OKAY) c = s->alloc(&s->d_peak, 2 * (size_t)m->layers);
+  if (c == IGC_OKAY) c = s->alloc(&s->d_peak_saved, 2 * (size_t)m->layers);
+  if (c == IGC_OKAY) CK(cudaMemsetAsync(s->d_peak, 0, sizeof(float) * 2 * (size_t)m->layers, s->st));
+  if (c == IGC_OKAY) CK(cudaMemsetAsync(s->d_peak_saved, 0, sizeof(float) * 2 * (size_t)m->layers, s->st));
   s->arg_parts = m->sm_count * 4;
   if (c == IGC_OKAY) c = s->alloc(&s->d_io, 1 + K);
   if (c == IGC_OKAY) c = s->alloc(&s->d_top, K + 1);
@@ -994,9 +1127,13 @@ extern "C" void igc_session_reset(igc_session *s) { /* app_core.c:14375 */
   if (!s) return;
   s->guess_count = 0;
   s->fill = 0;
+  s->floor = 0;
   s->echo.clear();
   s->serve_seconds = 0.0;
   s->serve_tokens = 0;
+  cudaSetDevice(s->m->device);
+  cudaMemsetAsync(s->d_peak, 0, sizeof(float) * 2 * (size_t)s->m->layers, s->st);
+  cudaStreamSynchronize(s->st);
 }
 
 extern "C" int igc_session_fill(const igc_session *s) { return s ? s->fill : 0; }
@@ -1009,6 +1146,10 @@ extern "C" int igc_session_hold(igc_session *s, int keep) { /* app_core.c:13935 
   if (!s || keep < 0) return IGC_FAIL_ARGUMENT;
   if (s->guess_count > 0) return IGC_FAIL_STATE;
   if (keep > s->fill) return IGC_FAIL_ARGUMENT;
+  // full-length caches wind back anywhere, except below rows a loaded file
+  // did not carry: the next id at `keep` reads the sliding window behind it
+  if (s->floor > 0 && keep > 0 && keep - s->m->slide_span + 1 < s->floor) return IGC_FAIL_SUPPORT;
+  if (keep == 0) s->floor = 0;
   s->fill = keep;
   if ((int)s->echo.size() > keep) s->echo.resize((size_t)keep);
   return IGC_OKAY;
@@ -1192,7 +1333,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   prof_mark(s, PROF_OTHER, 0.0);
   CKL(igc_launch_embed(d_ids, K, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
                        PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->use_stamps ? s->d_stamp : nullptr,
-                       IGC_STAMP_LIMIT, s->st));
+                       IGC_STAMP_LIMIT, s->d_peak, s->d_peak_saved, 2 * m->layers, s->st));
   if (m->ple_dim > 0) {
     int c = gemv(s, m->ple_lift, K, PRO_F32, EPI_STORE, s->x0, H, nullptr, nullptr, 1.0f, nullptr, nullptr,
                  s->ple_raw, PS, (float)(1.0 / sqrt((double)H)));
@@ -1236,10 +1377,31 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     const DevLayer &O = m->layer[owner];
     prof_mark(s, PROF_ATTN, 0.0);
     const int sliding = L.kind == 0 ? 1 : 0;
-    CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
-                        m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
-                        m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
-                        next_stamp(s, PROF_ATTN, 0.0), s->st));
+    if (!layer_bytes(m, owner)) {
+      // queries, an owner's new rows and the attention in one kernel
+      const CacheStore cq = layer_store(m, owner, L.share ? nullptr : s->d_peak + 2 * l);
+      CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
+                          m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, s->kc[owner], s->vc[owner], sliding,
+                          m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
+                          next_stamp(s, PROF_ATTN, 0.0), &cq, s->st));
+    } else {
+      // a byte cache: an owner's new rows onto the grid, the rows the pass
+      // reads decoded to floats, then the attention over those (as a sharing
+      // layer reads).  No overlap: attention copies rows before its wait.
+      const CacheStore cq = layer_store(m, owner, s->d_peak + 2 * l);
+      igc_kernels_pdl(0);
+      if (!L.share)
+        CKL(igc_launch_lane_kv(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.k_norm, m->rope_cs[L.kind],
+                               m->rope_sn[L.kind], m->eps, d_p0, K, s->kc[owner], s->vc[owner], &cq, s->st));
+      WidenArgs w = widen_of(s, owner, sliding, K);
+      w.p0 = d_p0;
+      CKL(igc_launch_lane_widen(&w, 1, widen_rows_most(m, sliding, K), m->sm_count, s->st));
+      CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
+                          m->rope_sn[L.kind], m->eps, 0, attn_rows(s, owner, 0), attn_rows(s, owner, 1), sliding,
+                          m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
+                          next_stamp(s, PROF_ATTN, 0.0), nullptr, s->st));
+      igc_kernels_pdl(s->use_pdl != 0);
+    }
     ma.parts = m->heads * s->attn_cluster;
     c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
              1.0f, nullptr, 0, nullptr, &so, ma_in);
@@ -1480,7 +1642,7 @@ static int lane_stack(LaneRun &r, const int32_t *d_ids, Attend attend, int32_t *
   const int H = m->hidden, PS = m->layers * m->ple_dim, M = r.M;
   int c, split = 1;
   CKL(igc_launch_embed(d_ids, M, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
-                       PS, (float)sqrt((double)m->ple_dim), B.x0, B.seed, nullptr, 0, r.st));
+                       PS, (float)sqrt((double)m->ple_dim), B.x0, B.seed, nullptr, 0, nullptr, nullptr, 0, r.st));
   if (m->ple_dim > 0) {
     LaneStageArgs sa = stage_of(LS_PLAIN, B.x0, H);
     sa.out_scale = (float)(1.0 / sqrt((double)H));
@@ -1598,8 +1760,8 @@ static int chunks_ready(igc_session *s) {
   for (int l = 0; l < m->layers; ++l) {
     const int owner = m->layer[l].share ? m->layer[l].source : l;
     for (int z = 0; z < C.groups_cap; ++z) {
-      hk[(size_t)l * C.groups_cap + z] = s->kc[owner];
-      hv[(size_t)l * C.groups_cap + z] = s->vc[owner];
+      hk[(size_t)l * C.groups_cap + z] = attn_rows(s, owner, 0);
+      hv[(size_t)l * C.groups_cap + z] = attn_rows(s, owner, 1);
     }
   }
   CK(cudaMemcpy(C.kc_tab, hk.data(), sizeof(float *) * hk.size(), cudaMemcpyHostToDevice));
@@ -1631,20 +1793,27 @@ static int enqueue_chunk(igc_session *s, int M) {
     const DevLayer &O = m->layer[owner];
     const int full = M / 16, tail = M - 16 * full, sliding = L.kind == 0 ? 1 : 0;
     igc_kernels_pdl(0);
+    const CacheStore kv = layer_store(m, owner, s->d_peak + 2 * owner);
     if (!L.share)
       CKL(igc_launch_lane_kv(C.B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.k_norm, m->rope_cs[L.kind],
-                             m->rope_sn[L.kind], m->eps, C.d_ids, M, s->kc[owner], s->vc[owner], s->st));
+                             m->rope_sn[L.kind], m->eps, C.d_ids, M, s->kc[owner], s->vc[owner], &kv, s->st));
+    if (layer_bytes(m, owner)) {
+      // a byte cache's rows the chunk reads, decoded to floats (all groups at once)
+      WidenArgs w = widen_of(s, owner, sliding, M);
+      w.p0 = C.d_ids;
+      CKL(igc_launch_lane_widen(&w, 1, widen_rows_most(m, sliding, M), m->sm_count, s->st));
+    }
     if (full > 0)
       CKL(igc_launch_attn_many(C.B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding,
                                m->slide_span, C.d_pos, 16, s->attn_cluster, C.B.attn, L.q_rows, nullptr, nullptr,
                                C.kc_tab + (size_t)l * C.groups_cap, C.vc_tab + (size_t)l * C.groups_cap, C.d_pos,
-                               full, s->st));
+                               full, nullptr, s->st));
     if (tail > 0)
       CKL(igc_launch_attn(C.B.qkv + (size_t)16 * full * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
-                          L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, s->kc[owner], s->vc[owner],
-                          sliding, m->slide_span, C.d_pos + full, tail, s->attn_cluster,
-                          C.B.attn + (size_t)16 * full * L.q_rows, L.q_rows, nullptr, nullptr, s->st));
+                          L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, attn_rows(s, owner, 0),
+                          attn_rows(s, owner, 1), sliding, m->slide_span, C.d_pos + full, tail, s->attn_cluster,
+                          C.B.attn + (size_t)16 * full * L.q_rows, L.q_rows, nullptr, nullptr, nullptr, s->st));
     igc_kernels_pdl(s->use_pdl != 0);
     return IGC_OKAY;
   };
@@ -1768,8 +1937,327 @@ extern "C" int igc_session_guess_keep(igc_session *s, int keep) { /* app_core.c:
   if (keep < 0 || keep > s->guess_count) return IGC_FAIL_ARGUMENT;
   s->serve_tokens += (size_t)keep;
   s->fill = s->guess_from + keep;
-  s->echo.resize((size_t)(s->guess_echo + keep));
+  s->echo.resize((size_t)std::min(s->guess_echo + keep, s->m->window_limit));
   s->guess_count = 0;
+  if (keep == 0) {
+    // a block undone whole leaves the peaks where they stood (app_core.c:12208-12213)
+    CK(cudaMemcpyAsync(s->d_peak, s->d_peak_saved, sizeof(float) * 2 * (size_t)s->m->layers,
+                       cudaMemcpyDeviceToDevice, s->st));
+    CK(cudaStreamSynchronize(s->st));
+  }
+  return IGC_OKAY;
+}
+
+// ---------------------------------------------------------------------------
+// cache files (app_core.c:13864-14182 session_save / session_load): the
+// reference's layout, so a file either engine writes is one the other reads.
+//
+//   16 bytes   "igllm cache 4\n\0\0"
+//   7 x u64    keep mark, caller's stamp, fill, ids held, layers, cache_bits,
+//              kind (IGC_KEEP_PROMPT / IGC_KEEP_TALK)
+//   u64        runs, then 3 x u64 a run (first id, one past the last, mark)
+//   i32 x ids  the ids held
+//   per owner layer with rows: its key rows, then its value rows, as the
+//              reference's ring holds them (slot = position mod span), each
+//              value a float or an e4m3 byte as the side stores it
+//   f32 x layers  key peaks, then f32 x layers value peaks
+//
+// This library's caches are full length, so a save gathers the ring's order
+// (a turned-over ring is the last `span` positions, rotated) and a load puts
+// rows back at their positions; a load from a turned-over ring leaves the
+// rows before it absent, which `floor` records for igc_session_hold.
+
+static const char k_keep_text[16] = {'i', 'g', 'l', 'l', 'm', ' ', 'c', 'a', 'c', 'h', 'e', ' ', '4', '\n', 0, 0};
+
+// the file's 64-bit fold (app_core.c:12888 keep_mix; the boost hash_combine step)
+static uint64_t keep_mix(uint64_t mark, uint64_t value) {
+  mark ^= value + 0x9E3779B97F4A7C15ull + (mark << 6) + (mark >> 2);
+  return mark;
+}
+
+// What decides a cache's layout, folded (app_core.c:13869 keep_mark): the
+// shapes, the storage, the checkpoint's size, and per layer its ring, heads
+// and bytes a value.
+static uint64_t keep_mark(const igc_session *s) {
+  const igc_model *m = s->m;
+  uint64_t mark = 0x243F6A8885A308D3ull;
+  mark = keep_mix(mark, (uint64_t)m->layers);
+  mark = keep_mix(mark, (uint64_t)m->heads);
+  mark = keep_mix(mark, (uint64_t)m->hidden);
+  mark = keep_mix(mark, (uint64_t)m->window_limit);
+  mark = keep_mix(mark, (uint64_t)m->slide_span);
+  mark = keep_mix(mark, (uint64_t)(int64_t)m->cache_bits);
+  mark = keep_mix(mark, (uint64_t)m->vocab);
+  mark = keep_mix(mark, (uint64_t)m->weight_bytes);
+  for (int l = 0; l < m->layers; ++l) {
+    const DevLayer &L = m->layer[l];
+    const CacheStore cq = layer_store(m, L.share ? L.source : l, nullptr);
+    mark = keep_mix(mark, (uint64_t)L.span);
+    mark = keep_mix(mark, (uint64_t)L.kv_heads);
+    mark = keep_mix(mark, (uint64_t)L.hd);
+    mark = keep_mix(mark, (uint64_t)L.share);
+    mark = keep_mix(mark, (uint64_t)(L.share ? sizeof(float) : side_bytes(cq.kq)));
+    mark = keep_mix(mark, (uint64_t)(L.share ? sizeof(float) : side_bytes(cq.vq)));
+  }
+  return mark;
+}
+
+// app_core.c:13957 keep_note_sane: runs in order, each non-empty, none past
+// the context.
+static bool note_sane(const igc_keep_note *n, int window) {
+  if (n->run_count < 0 || n->run_count > IGC_KEEP_RUNS) return false;
+  for (int i = 0; i < n->run_count; ++i) {
+    if (n->from_list[i] < 0 || n->till_list[i] <= n->from_list[i]) return false;
+    if (n->till_list[i] > window) return false;
+    if (i > 0 && n->from_list[i] < n->till_list[i - 1]) return false;
+  }
+  return true;
+}
+
+// app_core.c:13991 keep_note_share: the shared prefix ends at the first run,
+// inside it, that either side lacks, that the two place or fold differently,
+// or that reaches past it.
+extern "C" int igc_keep_note_share(const igc_keep_note *held, const igc_keep_note *now, int same_count) {
+  if (!held || !now || same_count < 0) return 0;
+  const int most = std::max(held->run_count, now->run_count);
+  for (int i = 0; i < most; ++i) {
+    const bool in_h = i < held->run_count, in_n = i < now->run_count;
+    const int hf = in_h ? held->from_list[i] : same_count, nf = in_n ? now->from_list[i] : same_count;
+    const int from = std::min(hf, nf);
+    if (from >= same_count) break;
+    if (!in_h || !in_n || hf != nf || held->till_list[i] != now->till_list[i] ||
+        held->mark_list[i] != now->mark_list[i] || held->till_list[i] > same_count)
+      return from;
+  }
+  return same_count;
+}
+
+// The ring order of an owner's `rows` kept rows at fill `fill`: the file's
+// slots [0, rows) come from positions [first[0], first[0] + count[0]) then
+// [first[1], first[1] + count[1]).
+struct RingRuns {
+  int first[2], count[2];
+};
+static RingRuns ring_runs(int fill, int span) {
+  RingRuns r{{0, 0}, {0, 0}};
+  if (fill <= span) {
+    r.count[0] = fill;
+    return r;
+  }
+  const int turn = fill % span;  // slots [0, turn) hold the newest positions
+  r.first[0] = fill - turn;
+  r.count[0] = turn;
+  r.first[1] = fill - span;
+  r.count[1] = span - turn;
+  return r;
+}
+
+extern "C" size_t igc_model_memory_bytes(const igc_model *m) { return m ? m->weight_bytes : 0; }
+
+extern "C" float igc_model_cache_scale(const igc_model *m, int layer, int value_side) { /* app_core.c:14515 */
+  if (!m || layer < 0 || layer >= m->layers) return 0.0f;
+  return value_side ? m->layer[layer].v_scale : m->layer[layer].k_scale;
+}
+
+extern "C" float igc_session_cache_peak(const igc_session *s, int layer, int value_side) { /* app_core.c:14540 */
+  if (!s || layer < 0 || layer >= s->m->layers) return 0.0f;
+  float v = 0.0f;
+  cudaSetDevice(s->m->device);
+  if (cudaMemcpyAsync(&v, s->d_peak + 2 * layer + (value_side ? 1 : 0), sizeof(float), cudaMemcpyDeviceToHost,
+                      s->st) != cudaSuccess ||
+      cudaStreamSynchronize(s->st) != cudaSuccess)
+    return 0.0f;
+  return v;
+}
+
+// Bytes the caches occupy at `cache_bits` storage: this library keeps every
+// owner full length (window_limit rows), so this is more than the
+// reference's rings for the same model (app_core.c:14522 counts rings).
+extern "C" size_t igc_session_cache_room_at(const igc_session *s, int cache_bits) {
+  if (!s) return 0;
+  const igc_model *m = s->m;
+  size_t total = 0;
+  for (int l = 0; l < m->layers; ++l) {
+    const DevLayer &L = m->layer[l];
+    if (L.share) continue;
+    const size_t slots = (size_t)m->window_limit * L.kv_rows;
+    total += slots * (cache_bits == 8 && L.k_scale > 0.0f ? 1u : sizeof(float));
+    total += slots * (cache_bits == 8 && L.v_scale > 0.0f ? 1u : sizeof(float));
+  }
+  return total;
+}
+extern "C" size_t igc_session_cache_room(const igc_session *s) {
+  return s ? igc_session_cache_room_at(s, s->m->cache_bits) : 0;
+}
+
+extern "C" int igc_session_ids(const igc_session *s, int32_t *ids, int limit) { /* app_core.c:14183 */
+  if (!s) return -1;
+  const int n = (int)s->echo.size();
+  if (!ids || limit < n) return n;
+  if (n > 0) memcpy(ids, s->echo.data(), sizeof(int32_t) * (size_t)n);
+  return n;
+}
+
+namespace {
+struct FileCloser {
+  FILE *f;
+  ~FileCloser() {
+    if (f) fclose(f);
+  }
+};
+}  // namespace
+
+extern "C" int igc_session_save(const igc_session *s, const char *path, uint64_t stamp, const igc_keep_note *note,
+                                int kind) { /* app_core.c:14010 */
+  if (!s || !path) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  if (kind != IGC_KEEP_PROMPT && kind != IGC_KEEP_TALK) return IGC_FAIL_ARGUMENT;
+  const igc_model *m = s->m;
+  if (note && !note_sane(note, m->window_limit)) return IGC_FAIL_ARGUMENT;
+  clear_stale("session save");
+  CK(cudaSetDevice(m->device));
+  // everything off the device first, so a failed copy writes no file
+  std::vector<std::vector<uint8_t>> rows((size_t)m->layers);
+  for (int l = 0; l < m->layers; ++l) {
+    const DevLayer &L = m->layer[l];
+    if (L.share) continue;
+    const int n = std::min(s->fill, L.span);
+    if (n < 1) continue;
+    const CacheStore cq = layer_store(m, l, nullptr);
+    const RingRuns rr = ring_runs(s->fill, L.span);
+    const size_t kw = side_bytes(cq.kq) * L.kv_rows, vw = side_bytes(cq.vq) * L.kv_rows;
+    auto &buf = rows[l];
+    buf.resize((size_t)n * (kw + vw));
+    uint8_t *kdst = buf.data(), *vdst = buf.data() + (size_t)n * kw;
+    for (int part = 0; part < 2; ++part) {
+      if (rr.count[part] == 0) continue;
+      const uint8_t *ks = reinterpret_cast<const uint8_t *>(s->kc[l]) + (size_t)rr.first[part] * kw;
+      const uint8_t *vs = reinterpret_cast<const uint8_t *>(s->vc[l]) + (size_t)rr.first[part] * vw;
+      CK(cudaMemcpyAsync(kdst, ks, (size_t)rr.count[part] * kw, cudaMemcpyDeviceToHost, s->st));
+      CK(cudaMemcpyAsync(vdst, vs, (size_t)rr.count[part] * vw, cudaMemcpyDeviceToHost, s->st));
+      kdst += (size_t)rr.count[part] * kw;
+      vdst += (size_t)rr.count[part] * vw;
+    }
+  }
+  std::vector<float> peak(2 * (size_t)m->layers);
+  CK(cudaMemcpyAsync(peak.data(), s->d_peak, sizeof(float) * peak.size(), cudaMemcpyDeviceToHost, s->st));
+  CK(cudaStreamSynchronize(s->st));
+
+  FileCloser fc{fopen(path, "wb")};
+  if (!fc.f) return IGC_FAIL_MISSING;
+  uint64_t head[7] = {keep_mark(s), stamp, (uint64_t)s->fill, (uint64_t)s->echo.size(), (uint64_t)m->layers,
+                      (uint64_t)(int64_t)m->cache_bits, (uint64_t)kind};
+  const uint64_t runs = note ? (uint64_t)note->run_count : 0;
+  bool ok = fwrite(k_keep_text, 1, 16, fc.f) == 16 && fwrite(head, 8, 7, fc.f) == 7 && fwrite(&runs, 8, 1, fc.f) == 1;
+  for (int i = 0; ok && i < (int)runs; ++i) {
+    const uint64_t run[3] = {(uint64_t)(uint32_t)note->from_list[i], (uint64_t)(uint32_t)note->till_list[i],
+                             note->mark_list[i]};
+    ok = fwrite(run, 8, 3, fc.f) == 3;
+  }
+  if (ok && !s->echo.empty()) ok = fwrite(s->echo.data(), 4, s->echo.size(), fc.f) == s->echo.size();
+  for (int l = 0; ok && l < m->layers; ++l)
+    if (!rows[l].empty()) ok = fwrite(rows[l].data(), 1, rows[l].size(), fc.f) == rows[l].size();
+  std::vector<float> side((size_t)m->layers);
+  for (int v = 0; ok && v < 2; ++v) {
+    for (int l = 0; l < m->layers; ++l) side[l] = peak[2 * (size_t)l + v];
+    ok = fwrite(side.data(), 4, side.size(), fc.f) == side.size();
+  }
+  FILE *f = fc.f;
+  fc.f = nullptr;
+  if (fclose(f) != 0) ok = false;
+  return ok ? IGC_OKAY : IGC_FAIL_FORMAT;
+}
+
+extern "C" int igc_session_load(igc_session *s, const char *path, uint64_t *stamp_out, igc_keep_note *note_out,
+                                int *kind_out) { /* app_core.c:14076 */
+  if (!s || !path) return IGC_FAIL_ARGUMENT;
+  if (s->guess_count > 0) return IGC_FAIL_STATE;
+  if (stamp_out) *stamp_out = 0;
+  if (kind_out) *kind_out = IGC_KEEP_PROMPT;
+  if (note_out) memset(note_out, 0, sizeof(*note_out));
+  igc_model *m = s->m;
+  FileCloser fc{fopen(path, "rb")};
+  if (!fc.f) return IGC_FAIL_MISSING;
+  char text[16];
+  uint64_t head[7], runs = 0;
+  if (fread(text, 1, 16, fc.f) != 16 || memcmp(text, k_keep_text, 16) != 0 || fread(head, 8, 7, fc.f) != 7 ||
+      fread(&runs, 8, 1, fc.f) != 1)
+    return IGC_FAIL_FORMAT;
+  if (runs > (uint64_t)IGC_KEEP_RUNS) return IGC_FAIL_FORMAT;
+  igc_keep_note note;
+  memset(&note, 0, sizeof(note));
+  note.run_count = (int)runs;
+  for (int i = 0; i < note.run_count; ++i) {
+    uint64_t run[3];
+    if (fread(run, 8, 3, fc.f) != 3) return IGC_FAIL_FORMAT;
+    note.from_list[i] = (int32_t)(uint32_t)run[0];
+    note.till_list[i] = (int32_t)(uint32_t)run[1];
+    note.mark_list[i] = run[2];
+  }
+  if (!note_sane(&note, m->window_limit)) return IGC_FAIL_FORMAT;
+  if (head[6] != IGC_KEEP_PROMPT && head[6] != IGC_KEEP_TALK) return IGC_FAIL_FORMAT;
+  // a cache belongs to the shapes it was written from (app_core.c:14127-14134)
+  if (head[0] != keep_mark(s) || head[4] != (uint64_t)m->layers || head[5] != (uint64_t)(int64_t)m->cache_bits)
+    return IGC_FAIL_STATE;
+  const int64_t fill = (int64_t)head[2], held = (int64_t)head[3];
+  if (fill < 0 || fill > m->window_limit || held < 0 || held > m->window_limit) return IGC_FAIL_FORMAT;
+
+  // whatever is read replaces what the session held; a read that stops half
+  // way leaves it cleared
+  igc_session_reset(s);
+  clear_stale("session load");
+  CK(cudaSetDevice(m->device));
+  std::vector<int32_t> ids((size_t)held);
+  bool ok = held == 0 || fread(ids.data(), 4, (size_t)held, fc.f) == (size_t)held;
+  std::vector<uint8_t> buf;
+  int floor = 0;
+  for (int l = 0; ok && l < m->layers; ++l) {
+    const DevLayer &L = m->layer[l];
+    if (L.share) continue;
+    const int n = (int)std::min<int64_t>(fill, L.span);
+    if (n < 1) continue;
+    const CacheStore cq = layer_store(m, l, nullptr);
+    const size_t kw = side_bytes(cq.kq) * L.kv_rows, vw = side_bytes(cq.vq) * L.kv_rows;
+    buf.resize((size_t)n * (kw + vw));
+    if (fread(buf.data(), 1, buf.size(), fc.f) != buf.size()) {
+      ok = false;
+      break;
+    }
+    const RingRuns rr = ring_runs((int)fill, L.span);
+    const uint8_t *ksrc = buf.data(), *vsrc = buf.data() + (size_t)n * kw;
+    for (int part = 0; part < 2; ++part) {
+      if (rr.count[part] == 0) continue;
+      uint8_t *kd = reinterpret_cast<uint8_t *>(s->kc[l]) + (size_t)rr.first[part] * kw;
+      uint8_t *vd = reinterpret_cast<uint8_t *>(s->vc[l]) + (size_t)rr.first[part] * vw;
+      CK(cudaMemcpyAsync(kd, ksrc, (size_t)rr.count[part] * kw, cudaMemcpyHostToDevice, s->st));
+      CK(cudaMemcpyAsync(vd, vsrc, (size_t)rr.count[part] * vw, cudaMemcpyHostToDevice, s->st));
+      ksrc += (size_t)rr.count[part] * kw;
+      vsrc += (size_t)rr.count[part] * vw;
+    }
+    // the pageable copies return once the source is consumed, so the buffer may be reused
+    if (fill > L.span) floor = std::max(floor, (int)fill - L.span);
+  }
+  std::vector<float> kpk((size_t)m->layers), vpk((size_t)m->layers);
+  if (ok)
+    ok = fread(kpk.data(), 4, kpk.size(), fc.f) == kpk.size() && fread(vpk.data(), 4, vpk.size(), fc.f) == vpk.size();
+  if (!ok) {
+    igc_session_reset(s);
+    return IGC_FAIL_FORMAT;
+  }
+  std::vector<float> peak(2 * (size_t)m->layers);
+  for (int l = 0; l < m->layers; ++l) {
+    peak[2 * (size_t)l] = kpk[l];
+    peak[2 * (size_t)l + 1] = vpk[l];
+  }
+  CK(cudaMemcpyAsync(s->d_peak, peak.data(), sizeof(float) * peak.size(), cudaMemcpyHostToDevice, s->st));
+  CK(cudaStreamSynchronize(s->st));
+  s->fill = (int)fill;
+  s->floor = floor;
+  s->echo.assign(ids.begin(), ids.end());
+  s->logit_lanes = 0;
+  if (stamp_out) *stamp_out = head[1];
+  if (note_out) *note_out = note;
+  if (kind_out) *kind_out = (int)head[6];
   return IGC_OKAY;
 }
 
@@ -1796,7 +2284,8 @@ struct igc_crowd {
   cudaStream_t st = nullptr;
   int cap = 0, k = 0, lanes = 0;
   LaneBuf B;
-  // device: [ids: lanes][pos: cap][kc: layers * cap][vc: layers * cap], mirrored in pinned host memory
+  // device: [ids: lanes][pos: cap] then per layer and session [caches: key, value][peaks][the float rows
+  // attention reads: key, value], mirrored in pinned host memory
   uint8_t *d_tab = nullptr, *h_tab = nullptr;
   size_t tab_bytes = 0;
   int32_t *d_top = nullptr;  // [lanes] argmax, then the kernels' error word
@@ -1808,8 +2297,14 @@ struct igc_crowd {
 
   int32_t *ids() { return reinterpret_cast<int32_t *>(d_tab); }
   int *pos() { return reinterpret_cast<int *>(d_tab + sizeof(int32_t) * lanes); }
-  float **kc() { return reinterpret_cast<float **>(d_tab + sizeof(int32_t) * lanes + sizeof(int) * cap); }
+  // the pointer tables start on a 16-byte boundary whatever the lane and
+  // session counts (a pointer load from a 4-byte boundary is misaligned)
+  size_t ptr_at() const { return (sizeof(int32_t) * lanes + sizeof(int) * cap + 15) / 16 * 16; }
+  float **kc() { return reinterpret_cast<float **>(d_tab + ptr_at()); }
   float **vc() { return kc() + (size_t)m->layers * cap; }
+  float **pk() { return vc() + (size_t)m->layers * cap; }
+  float **kf() { return pk() + (size_t)m->layers * cap; }
+  float **vf() { return kf() + (size_t)m->layers * cap; }
 
   ~igc_crowd() {
     cudaSetDevice(m->device);
@@ -1837,7 +2332,7 @@ extern "C" int igc_crowd_open(igc_model *m, int session_limit, int lanes_per_ses
   CK(cudaStreamCreateWithFlags(&cr->st, cudaStreamNonBlocking));
   int c = lane_buf_alloc(m, cr->B, cr->lanes, cr->lanes, cr->owned);
   if (c != IGC_OKAY) return c;
-  cr->tab_bytes = sizeof(int32_t) * cr->lanes + sizeof(int) * cr->cap + 2 * sizeof(float *) * m->layers * cr->cap;
+  cr->tab_bytes = cr->ptr_at() + 5 * sizeof(float *) * m->layers * cr->cap;
   void *v = nullptr;
   CK(cudaMalloc(&v, cr->tab_bytes));
   cr->owned.push_back(v);
@@ -1866,10 +2361,44 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
   auto attend = [&](int l, const DevLayer &L) -> int {
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
+    const int sliding = L.kind == 0 ? 1 : 0;
+    const size_t at = (size_t)l * cr->cap;
+    if (!layer_bytes(m, owner)) {
+      const CacheStore cq = layer_store(m, owner, nullptr, L.share ? nullptr : cr->pk() + at);
+      CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
+                               m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr,
+                               sliding, m->slide_span, cr->pos(), k, IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr,
+                               nullptr, cr->kc() + at, cr->vc() + at, cr->pos(), S, &cq, cr->st));
+      return IGC_OKAY;
+    }
+    // a byte cache: every session's new rows onto the grid, the rows each
+    // reads decoded to floats, then attention over those without overlap
+    // (it copies rows before its wait)
+    const CacheStore cq = layer_store(m, owner, nullptr);
+    igc_kernels_pdl(0);
+    if (!L.share)
+      CKL(igc_launch_lane_kv_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.k_norm, m->rope_cs[L.kind],
+                                  m->rope_sn[L.kind], m->eps, nullptr, S * k, nullptr, nullptr, &cq, cr->pos(),
+                                  cr->kc() + at, cr->vc() + at, cr->pk() + at, k, cr->st));
+    WidenArgs w;
+    memset(&w, 0, sizeof(w));
+    w.kc_tab = cr->kc() + at;
+    w.vc_tab = cr->vc() + at;
+    w.kf_tab = cr->kf() + at;
+    w.vf_tab = cr->vf() + at;
+    w.pos_tab = cr->pos();
+    w.kq = cq.kq;
+    w.vq = cq.vq;
+    w.kv_w = O.kv_rows;
+    w.lanes = k;
+    w.sliding = sliding;
+    w.span = m->slide_span;
+    CKL(igc_launch_lane_widen(&w, S, widen_rows_most(m, sliding, k), m->sm_count, cr->st));
     CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
-                             m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr, L.kind == 0 ? 1 : 0,
-                             m->slide_span, cr->pos(), k, IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr, nullptr,
-                             cr->kc() + (size_t)l * cr->cap, cr->vc() + (size_t)l * cr->cap, cr->pos(), S, cr->st));
+                             m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding, m->slide_span, cr->pos(), k,
+                             IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr, nullptr, cr->kf() + at, cr->vf() + at,
+                             cr->pos(), S, nullptr, cr->st));
+    igc_kernels_pdl(1);
     return IGC_OKAY;
   };
   return lane_stack(r, cr->ids(), attend, cr->d_top, rows ? cr->logits : nullptr);
@@ -1901,8 +2430,11 @@ extern "C" int igc_crowd_round(igc_crowd *cr, igc_session **sessions, int count,
   // the tables: ids, positions and every layer's (owner's) caches per session
   int32_t *h_ids = reinterpret_cast<int32_t *>(cr->h_tab);
   int *h_pos = reinterpret_cast<int *>(cr->h_tab + sizeof(int32_t) * cr->lanes);
-  float **h_kc = reinterpret_cast<float **>(cr->h_tab + sizeof(int32_t) * cr->lanes + sizeof(int) * cr->cap);
+  float **h_kc = reinterpret_cast<float **>(cr->h_tab + cr->ptr_at());
   float **h_vc = h_kc + (size_t)m->layers * cr->cap;
+  float **h_pk = h_vc + (size_t)m->layers * cr->cap;
+  float **h_kf = h_pk + (size_t)m->layers * cr->cap;
+  float **h_vf = h_kf + (size_t)m->layers * cr->cap;
   memcpy(h_ids, ids, sizeof(int32_t) * (size_t)count * k);
   for (int j = 0; j < count; ++j) {
     h_pos[j] = sessions[j]->fill;
@@ -1911,6 +2443,9 @@ extern "C" int igc_crowd_round(igc_crowd *cr, igc_session **sessions, int count,
       const int owner = L.share ? L.source : l;
       h_kc[(size_t)l * cr->cap + j] = sessions[j]->kc[owner];
       h_vc[(size_t)l * cr->cap + j] = sessions[j]->vc[owner];
+      h_pk[(size_t)l * cr->cap + j] = sessions[j]->d_peak + 2 * l;
+      h_kf[(size_t)l * cr->cap + j] = attn_rows(sessions[j], owner, 0);
+      h_vf[(size_t)l * cr->cap + j] = attn_rows(sessions[j], owner, 1);
     }
   }
   CK(cudaMemcpyAsync(cr->d_tab, cr->h_tab, cr->tab_bytes, cudaMemcpyHostToDevice, cr->st));

@@ -78,7 +78,10 @@ typedef struct fill_job {
 static void fill_range(const fill_job *j) {
   const float sigma = 0.02f;
   size_t i;
-  if (j->kind == IGC_SYNTH_CODE) {
+  if (j->kind == IGC_SYNTH_CONST) {
+    float *o = (float *)j->out;
+    for (i = j->from; i < j->upto; ++i) o[i - j->origin] = j->offset;
+  } else if (j->kind == IGC_SYNTH_CODE) {
     uint8_t *o = (uint8_t *)j->out;
     for (i = j->from; i < j->upto; ++i) o[i - j->origin] = (uint8_t)(value_hash(j->base, i) & 0xFFu);
   } else {
@@ -105,7 +108,7 @@ int igc_synth_fill(uint64_t seed, uint64_t stream, int kind, float offset, size_
   fill_job jobs[64];
   pthread_t tid[64];
   int n = threads < 1 ? 1 : (threads > 64 ? 64 : threads);
-  if (!out || kind < 0 || kind > 3) return IGC_FAIL_ARGUMENT;
+  if (!out || kind < 0 || kind > IGC_SYNTH_CONST) return IGC_FAIL_ARGUMENT;
   pthread_once(&table_once, table_build);
   if (count < ((size_t)1 << 20)) n = 1;
   for (int t = 0; t < n; ++t) {
@@ -133,11 +136,13 @@ static int layer_global(const igc_synth_spec *s, int l) {
   return s->global_every > 0 && ((l + 1) % s->global_every) == 0;
 }
 
+static size_t dtype_size(int dtype) { return dtype == 6 ? 1u : dtype == 1 ? 4u : 2u; }
+
 static void add(igc_synth_tensor *room, int room_count, int *n, const char *name, int dtype,
                 int64_t r, int64_t c, int rank, int kind, float offset) {
   if (room && *n < room_count) {
     igc_synth_tensor *t = &room[*n];
-    size_t el = dtype == 6 ? 1u : 2u;
+    size_t el = dtype_size(dtype);
     memset(t, 0, sizeof(*t));
     snprintf(t->name, sizeof(t->name), "%s", name);
     t->dtype = dtype;
@@ -191,6 +196,15 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
       add_plane(room, room_count, &n, stem, kvw, s->hidden);
       STEM("self_attn.k_norm.weight");
       add(room, room_count, &n, stem, 3, s->head_dim, 0, 1, IGC_SYNTH_OFFSET, no);
+      /* the export's static cache ranges (app_core.c:8596-8601), varied by layer */
+      if (s->cache_scale_k > 0.0f) {
+        STEM("self_attn.k_cache_scale");
+        add(room, room_count, &n, stem, 1, 1, 0, 1, IGC_SYNTH_CONST, s->cache_scale_k * (1.0f + (float)(l % 4) / 8.0f));
+      }
+      if (s->cache_scale_v > 0.0f) {
+        STEM("self_attn.v_cache_scale");
+        add(room, room_count, &n, stem, 1, 1, 0, 1, IGC_SYNTH_CONST, s->cache_scale_v * (1.0f + (float)(l % 4) / 8.0f));
+      }
     }
     STEM("self_attn.o_proj");
     add_plane(room, room_count, &n, stem, s->hidden, qw);
@@ -229,7 +243,7 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
 
 int igc_synth_tensor_fill(const igc_synth_spec *spec, const igc_synth_tensor *t, void *out,
                           int threads) {
-  size_t count = t->dtype == 6 ? t->bytes : t->bytes / 2;
+  size_t count = t->bytes / dtype_size(t->dtype);
   return igc_synth_fill(spec->seed, igc_synth_stream(t->name), t->kind, t->offset, count, out,
                         threads);
 }
@@ -349,7 +363,7 @@ int igc_synth_write(const igc_synth_spec *spec, const char *folder, int threads)
   if (!buf) { fclose(f); free(list); return IGC_FAIL_MEMORY; }
   for (int i = 0; i < n && code == IGC_OKAY; ++i) {
     const igc_synth_tensor *t = &list[i];
-    size_t el = t->dtype == 6 ? 1u : 2u, count = t->bytes / el, per = chunk / el;
+    size_t el = dtype_size(t->dtype), count = t->bytes / el, per = chunk / el;
     uint64_t base_stream = igc_synth_stream(t->name);
     for (size_t from = 0; from < count; from += per) {
       size_t take = count - from < per ? count - from : per;

@@ -25,6 +25,7 @@ extern "C" {
 #define IGC_SYNTH_SCALE 1  /* f16 |N(0,0.02)| */
 #define IGC_SYNTH_NORMAL 2 /* bf16 N(0,0.02) */
 #define IGC_SYNTH_OFFSET 3 /* bf16 offset + N(0,0.02) */
+#define IGC_SYNTH_CONST 4  /* f32, every value the offset */
 
 /* One tensor of a synthetic checkpoint, in the layout the reference binds
  * (app_core.c:7886 plane_bind_gemma for U8 codes with F16 scales). */

@@ -56,7 +56,8 @@ typedef struct igc_setup {
   int device;
   int window_limit;
   int verbose_level;
-  int cache_bits; /* 0 only: caches are float, as app_setup.cache_bits = 0 */
+  int cache_bits; /* 8 stores a cache side as e4m3 bytes where the export ships
+                    its scale (app_core.c:14270-14284); anything else keeps floats */
 } igc_setup;
 
 /* app_core.c:60-67 app_taste, field for field. */
@@ -149,7 +150,10 @@ int igc_session_open(igc_model *model, igc_session **session_out);
 void igc_session_close(igc_session *session);
 void igc_session_reset(igc_session *session);
 /* app_core.c:13935 session_hold.  Caches are full length, so no ring turns
- * over and the APP_FAIL_SUPPORT refusal never arises. */
+ * over and the reference's IGC_FAIL_SUPPORT refusal does not arise from one;
+ * it does arise after igc_session_load of a file written from a ring that had
+ * turned over, for a keep_count whose sliding window reaches rows the file
+ * did not carry. */
 int igc_session_hold(igc_session *session, int keep_count);
 /* app_core.c:14443 session_prime: every id but the last, 16 lanes a pass. */
 int igc_session_prime(igc_session *session, const int32_t *id_list, int id_count);
@@ -194,6 +198,54 @@ int igc_session_round(igc_session *session, const int32_t *id_list, int id_count
  * steps and blocks (app_core.c:70-77 app_tally serve_seconds/serve_tokens). */
 double igc_session_serve_seconds(const igc_session *session);
 size_t igc_session_serve_tokens(const igc_session *session);
+
+/* ---- cache files and the cache's storage (app_core.c:320-425) -----------
+ *
+ * igc_session_save / igc_session_load write and read the reference's cache
+ * file (app_core.c:14010 session_save, :14076 session_load, layout "igllm
+ * cache 4"): the ids the session holds and the rows of its caches that carry
+ * anything, float or e4m3 bytes as the session stores them, in the order the
+ * reference's rings hold them.  A file written by either engine loads into
+ * the other for the same checkpoint, window and cache_bits; one written for
+ * other shapes is refused with IGC_FAIL_STATE, a damaged one with
+ * IGC_FAIL_FORMAT (the session is then left cleared).  `stamp_value`, the
+ * note and `kind_mark` are the caller's, written beside the cache and handed
+ * back unread.  Refused with IGC_FAIL_STATE while a block is in flight.
+ *
+ * igc_session_ids: the ids the session holds (app_core.c:14183); returns
+ * their count, and copies them only when `id_limit` has room.
+ *
+ * igc_keep_note_share: app_core.c:13991 keep_note_share, how much of
+ * `same_count` shared ids the two notes' runs leave reusable.
+ *
+ * igc_model_cache_scale / igc_session_cache_peak: a layer's calibrated range
+ * (0 when the export ships none) and the largest magnitude the session has
+ * written to that cache side (app_core.c:14515, :14540).
+ * igc_session_cache_room(_at): bytes this session's caches occupy (at
+ * `cache_bits` storage); every owner layer is held full length here, so the
+ * figure exceeds the reference's rings (app_core.c:14522).
+ * igc_model_memory_bytes: app_core.c:12667 model_memory_bytes, the bytes of
+ * the checkpoint's tensors the text stack binds. */
+#define IGC_KEEP_PROMPT 0 /* app_core.c:367 */
+#define IGC_KEEP_TALK 1   /* app_core.c:368 */
+#define IGC_KEEP_RUNS 16  /* app_core.c:385 */
+typedef struct igc_keep_note { /* app_core.c:387-392 app_keep_note */
+  int run_count;
+  int32_t from_list[IGC_KEEP_RUNS];
+  int32_t till_list[IGC_KEEP_RUNS];
+  uint64_t mark_list[IGC_KEEP_RUNS];
+} igc_keep_note;
+int igc_session_save(const igc_session *session, const char *path_text, uint64_t stamp_value,
+                     const igc_keep_note *note_in, int kind_mark);
+int igc_session_load(igc_session *session, const char *path_text, uint64_t *stamp_out, igc_keep_note *note_out,
+                     int *kind_out);
+int igc_session_ids(const igc_session *session, int32_t *id_list, int id_limit);
+int igc_keep_note_share(const igc_keep_note *held, const igc_keep_note *now, int same_count);
+float igc_model_cache_scale(const igc_model *model, int layer_index, int value_side);
+float igc_session_cache_peak(const igc_session *session, int layer_index, int value_side);
+size_t igc_session_cache_room(const igc_session *session);
+size_t igc_session_cache_room_at(const igc_session *session, int cache_bits);
+size_t igc_model_memory_bytes(const igc_model *model);
 
 /* ---- the crowd: many sessions' blocks in one pass (no counterpart in the
  * reference, which serialises sessions, app_core.c:7789-7793 and
@@ -302,12 +354,16 @@ typedef struct igc_synth_spec {
   float norm_offset;   /* 0: norms N(0,0.02); 1: norms 1+N(0,0.02) */
   int with_layer_scalar; /* write layer_scalar = 1+N(0,0.02); 0 leaves it out (gain 1) */
   uint64_t seed;
+  /* > 0: write each owner layer's self_attn.k_cache_scale / v_cache_scale as
+   * an F32 scalar, this value times (1 + (layer mod 4) / 8); 0 writes none */
+  float cache_scale_k, cache_scale_v;
 } igc_synth_spec;
 
 /* Fill `out` with `count` values of stream `stream` of the spec's seed.
  * kind 0: packed int4 bytes (two uniform codes a byte, low nibble first);
  * kind 1: f16 |N(0,0.02)| bits; kind 2: bf16 N(0,0.02) bits;
- * kind 3: bf16 offset + N(0,0.02) bits (offset = norm_offset). */
+ * kind 3: bf16 offset + N(0,0.02) bits (offset = norm_offset);
+ * kind 4: f32, every value `offset`. */
 int igc_synth_fill(uint64_t seed, uint64_t stream, int kind, float offset, size_t count, void *out,
                    int threads);
 /* Write config.json, tokenizer.json and model.safetensors for the spec under

@@ -23,6 +23,32 @@
 
 /* ---- scalar conversions ------------------------------------------------ */
 
+/* app_core.c:10980 cache_pack8 + :11008 cache_code8, from the format: field
+ * 0 counts steps of 2^-9 (a value that rounds to no step is code 0 whatever
+ * its sign); a value in [2^e, 2^(e+1)), e >= -6, has steps of
+ * 2^(e-3), and its rounded step count q (8..16) is the code ((e+7) << 3) +
+ * q - 8, carrying into the next exponent at q = 16. */
+uint8_t igo_cache_code8(float x) {
+  uint8_t sign = x < 0.0f ? 0x80u : 0u;
+  float a = fabsf(x);
+  int e;
+  if (!(a < 448.0f)) return (uint8_t)(sign | 0x7Eu);
+  if (a < 1.0f / 64.0f) { /* a value that rounds to zero keeps no sign */
+    uint8_t q = (uint8_t)nearbyintf(a * 512.0f);
+    return q ? (uint8_t)(sign | q) : 0u;
+  }
+  frexpf(a, &e); /* a in [2^(e-1), 2^e) */
+  e -= 1;
+  return (uint8_t)(sign | (uint8_t)(((e + 7) << 3) + (int)nearbyintf(ldexpf(a, 3 - e)) - 8));
+}
+
+/* app_core.c:11025 cache_real8 */
+float igo_cache_real8(uint8_t code) {
+  int f = (code >> 3) & 15, m = code & 7;
+  float a = f == 0 ? (float)m / 512.0f : ldexpf((float)(8 + m), f - 10);
+  return (code & 0x80u) ? -a : a;
+}
+
 static float bf16_to_f32(uint16_t h) { /* app_core.c:1689 real_from_bf16 */
   union { uint32_t u; float f; } c;
   c.u = (uint32_t)h << 16;

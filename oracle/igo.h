@@ -95,6 +95,13 @@ int32_t igo_session_pick(igo_session *s, const float *logits, const igo_taste *t
 /* Kept echo history (ids fed), for checking the host/device agree. */
 int igo_session_echo(const igo_session *s, int32_t *out, int limit);
 
+/* The byte cache's e4m3 grid (app_core.c:10975-11035 cache_pack8 /
+ * cache_code8 / cache_real8): a value (already divided by its layer's scale)
+ * to its code, rounding to nearest with ties to even and saturating at
+ * +-448 (a NaN to +448), and a code back to its value. */
+uint8_t igo_cache_code8(float x);
+float igo_cache_real8(uint8_t code);
+
 /* Kernel-level restatements, exported for known-answer tests. */
 float igo_row_code(const igo_plane *p, int row, const float *act);           /* kern_row_code :3688 */
 void igo_mat_mat(const igo_plane *p, const float *act, int act_stride, int lanes, float *out,

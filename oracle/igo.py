@@ -102,6 +102,11 @@ class IgoModel(ctypes.Structure):
                 ("layer", ctypes.POINTER(IgoLayer))]
 
 
+class KeepNote(ctypes.Structure):  # app_core.c:387-392 app_keep_note
+    _fields_ = [("run_count", ctypes.c_int), ("from_list", ctypes.c_int32 * 16), ("till_list", ctypes.c_int32 * 16),
+                ("mark_list", ctypes.c_uint64 * 16)]
+
+
 class Taste(ctypes.Structure):  # app_core.c:60-67
     _fields_ = [("heat", ctypes.c_float), ("top_count", ctypes.c_int), ("top_portion", ctypes.c_float),
                 ("echo_penalty", ctypes.c_float), ("echo_window", ctypes.c_int), ("seed", ctypes.c_uint64)]
@@ -148,6 +153,8 @@ def igo_lib():
             ("igo_pick_shape", i, [f, i, ctypes.POINTER(Taste), i32p, i, i32p, f]),
             ("igo_guess_draw_state", ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_uint64]),
             ("igo_draw_unit", ctypes.c_float, [ctypes.POINTER(ctypes.c_uint64)]),
+            ("igo_cache_code8", ctypes.c_uint8, [ctypes.c_float]),
+            ("igo_cache_real8", ctypes.c_float, [ctypes.c_uint8]),
         ]:
             fn = getattr(lib, name)
             fn.restype = res
@@ -417,6 +424,18 @@ def _bind_ref(lib):
         ("ref_session_pick", ctypes.c_int32, [vp, f, ctypes.POINTER(Taste)]),
         ("ref_session_serve_seconds", ctypes.c_double, [vp]),
         ("ref_session_serve_tokens", ctypes.c_size_t, [vp]),
+        ("ref_model_load_bits", i, [ctypes.c_char_p, i, i, i, ctypes.POINTER(vp)]),
+        ("ref_model_memory_bytes", ctypes.c_size_t, [vp]),
+        ("ref_model_cache_scale", ctypes.c_float, [vp, i, i]),
+        ("ref_session_cache_peak", ctypes.c_float, [vp, i, i]),
+        ("ref_session_cache_room", ctypes.c_size_t, [vp]),
+        ("ref_session_save", i, [vp, ctypes.c_char_p, ctypes.c_uint64, ctypes.POINTER(KeepNote), i]),
+        ("ref_session_load", i, [vp, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(KeepNote),
+                                 ctypes.POINTER(ctypes.c_int)]),
+        ("ref_session_ids", i, [vp, i32p, i]),
+        ("ref_keep_note_share", i, [ctypes.POINTER(KeepNote), ctypes.POINTER(KeepNote), i]),
+        ("ref_cache_code8", None, [f, i, ctypes.POINTER(ctypes.c_uint8)]),
+        ("ref_cache_real8", None, [ctypes.POINTER(ctypes.c_uint8), i, f]),
     ]:
         fn = getattr(lib, name)
         fn.restype = res
@@ -428,11 +447,12 @@ class RefModel:
     """The reference's model_load; with `cuda_device` set, the build whose
     backend table is libigllm_cuda's (its products on that GPU)."""
 
-    def __init__(self, folder, threads=8, window_limit=0, cuda_device=None):
+    def __init__(self, folder, threads=8, window_limit=0, cuda_device=None, cache_bits=0):
         self.h = ctypes.c_void_p()
         if cuda_device is None:
             self.lib = ref_lib()
-            code = self.lib.ref_model_load(str(folder).encode(), threads, window_limit, ctypes.byref(self.h))
+            code = self.lib.ref_model_load_bits(str(folder).encode(), threads, window_limit, int(cache_bits),
+                                                ctypes.byref(self.h))
         else:
             self.lib = ref_cuda_lib()
             code = self.lib.ref_model_load_cuda(str(folder).encode(), threads, window_limit, int(cuda_device),
@@ -443,6 +463,12 @@ class RefModel:
 
     def decode_bytes(self):
         return self.lib.ref_model_decode_bytes(self.h)
+
+    def memory_bytes(self):
+        return self.lib.ref_model_memory_bytes(self.h)
+
+    def cache_scale(self, layer, value_side):
+        return self.lib.ref_model_cache_scale(self.h, int(layer), int(value_side))
 
     def close(self):
         if self.h:
@@ -511,3 +537,38 @@ class RefSession:
 
     def serve_seconds(self):
         return self.lib.ref_session_serve_seconds(self.h)
+
+    def cache_peak(self, layer, value_side):
+        return self.lib.ref_session_cache_peak(self.h, int(layer), int(value_side))
+
+    def save(self, path, stamp=0, note=None, kind=0):
+        return self.lib.ref_session_save(self.h, str(path).encode(), int(stamp),
+                                         ctypes.byref(note) if note is not None else None, int(kind))
+
+    def load(self, path):
+        """(code, stamp, note, kind) of app_core.c:14076 session_load."""
+        stamp, note, kind = ctypes.c_uint64(), KeepNote(), ctypes.c_int()
+        code = self.lib.ref_session_load(self.h, str(path).encode(), ctypes.byref(stamp), ctypes.byref(note),
+                                         ctypes.byref(kind))
+        return code, stamp.value, note, kind.value
+
+    def ids(self):
+        n = self.lib.ref_session_ids(self.h, None, 0)
+        out = np.zeros(max(n, 1), np.int32)
+        self.lib.ref_session_ids(self.h, iptr(out), len(out))
+        return out[:n]
+
+
+def ref_cache_code8(x):
+    """The reference's own cache_code8 (app_core.c:11008) over an array."""
+    a = np.ascontiguousarray(x, np.float32)
+    out = np.zeros(len(a), np.uint8)
+    ref_lib().ref_cache_code8(fptr(a), len(a), out.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)))
+    return out
+
+
+def ref_cache_real8(codes):
+    c = np.ascontiguousarray(codes, np.uint8)
+    out = np.zeros(len(c), np.float32)
+    ref_lib().ref_cache_real8(c.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), len(c), fptr(out))
+    return out

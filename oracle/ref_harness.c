@@ -88,3 +88,43 @@ int32_t ref_session_pick(app_session *s, const float *logits, const ref_taste *t
 
 double ref_session_serve_seconds(const app_session *s) { return session_tally(s).serve_seconds; }
 size_t ref_session_serve_tokens(const app_session *s) { return session_tally(s).serve_tokens; }
+
+/* model_load with the setup's cache_bits (8: byte caches where the export
+ * ships scales, app_core.c:14270-14284). */
+int ref_model_load_bits(const char *folder, int threads, int window_limit, int cache_bits, app_model **out) {
+  app_setup setup = app_setup_plain();
+  setup.thread_count = threads;
+  setup.window_limit = window_limit;
+  setup.cache_bits = cache_bits;
+  return (int)model_load(folder, &setup, out);
+}
+
+size_t ref_model_memory_bytes(const app_model *m) { return model_memory_bytes(m); }
+float ref_model_cache_scale(const app_model *m, int layer, int value_side) {
+  return model_cache_scale(m, layer, value_side);
+}
+float ref_session_cache_peak(const app_session *s, int layer, int value_side) {
+  return session_cache_peak(s, layer, value_side);
+}
+size_t ref_session_cache_room(const app_session *s) { return session_cache_room(s); }
+
+int ref_session_save(const app_session *s, const char *path, uint64_t stamp, const app_keep_note *note, int kind) {
+  return (int)session_save(s, path, stamp, note, kind);
+}
+int ref_session_load(app_session *s, const char *path, uint64_t *stamp, app_keep_note *note, int *kind) {
+  return (int)session_load(s, path, stamp, note, kind);
+}
+int ref_session_ids(const app_session *s, int32_t *ids, int limit) { return session_ids(s, ids, limit); }
+int ref_keep_note_share(const app_keep_note *held, const app_keep_note *now, int same_count) {
+  return keep_note_share(held, now, same_count);
+}
+
+/* The cache grid's own conversions (app_core.c:10980-11035), over arrays. */
+void ref_cache_code8(const float *x, int n, uint8_t *out) {
+  int i;
+  for (i = 0; i < n; ++i) out[i] = cache_code8(x[i]);
+}
+void ref_cache_real8(const uint8_t *c, int n, float *out) {
+  int i;
+  for (i = 0; i < n; ++i) out[i] = cache_real8(c[i]);
+}

@@ -52,6 +52,16 @@ LITERAL = dict(TINY, norm_offset=0.0, with_layer_scalar=0, seed=3)
 WIDE = dict(TINY, inner=4096, seed=13)
 
 
+# The export's head width (256) and 8:1 grouping at a size the reference
+# primes in seconds, with every owner's key and value cache scales written
+# (1/32 x 1, 1.125, 1.25, 1.375 by layer) for the 8-bit cache.  Layers 0-3
+# are sliding owners with 64-row rings, 4 the global owner, 5 the last
+# sliding owner (held full length for its sharers 6-8), 9 a global sharer.
+CACHED = dict(vocab=8192, hidden=512, layers=10, heads=8, kv_heads=1, head_dim=256, inner=1024, ple_dim=64,
+              slide_span=64, share_count=4, global_every=5, window_limit=1024, norm_offset=1.0,
+              with_layer_scalar=1, seed=17, cache_scale_k=1.0 / 32, cache_scale_v=1.0 / 32)
+
+
 def make_checkpoint(lib, folder, cfg):
     spec = lib.SynthSpec(**cfg)
     if not os.path.exists(os.path.join(folder, "model.safetensors")):
@@ -84,4 +94,11 @@ def literal_dir(tmp_path_factory, igc_lib):
 def wide_dir(tmp_path_factory, igc_lib):
     d = str(tmp_path_factory.mktemp("wide"))
     make_checkpoint(igc_lib, d, WIDE)
+    return d
+
+
+@pytest.fixture(scope="session")
+def cached_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("cached"))
+    make_checkpoint(igc_lib, d, CACHED)
     return d

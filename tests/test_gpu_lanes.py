@@ -147,8 +147,8 @@ def test_crowd_round_matches_each_session_alone(igc_lib, small_dir):
 def test_crowd_refuses_what_it_cannot_run(igc_lib, small_dir, tiny_dir):
     """A crowd round refuses, before anything runs and leaving every session
     as it was: a session named twice, a session with a block in flight, a
-    session of another model, a full window, more sessions than the crowd
-    holds, and lanes a session that do not split into attention groups."""
+    session of another model, a full window and more sessions than the crowd
+    holds; a crowd is refused blocks past 16 lanes or 512 lanes in all."""
     from conftest import SMALL, TINY
     m = igc_lib.Model(folder=small_dir, window_limit=SMALL["window_limit"])
     other = igc_lib.Model(folder=tiny_dir, window_limit=TINY["window_limit"])
@@ -177,6 +177,33 @@ def test_crowd_refuses_what_it_cannot_run(igc_lib, small_dir, tiny_dir):
     take, made, _ = crowd.round([a, b], blk)  # the same sessions, unrefused, still run
     assert a.fill == 26 + take[0] + 1 and b.fill == 26 + take[1] + 1  # primed to 26, then take + 1 kept
     crowd.close()
-    with pytest.raises(igc_lib.IgcError) as e:
-        igc_lib.Crowd(m, 4, 6)
-    assert e.value.code == igc_lib.FAIL_SUPPORT
+    for limit, k in ((4, 17), (64, 16), (0, 4)):  # a block past 16 lanes, past 512 lanes in all, no room
+        with pytest.raises(igc_lib.IgcError) as e:
+            igc_lib.Crowd(m, limit, k)
+        assert e.value.code == igc_lib.FAIL_ARGUMENT
+
+
+def test_crowd_of_any_size(igc_lib, small_dir):
+    """Crowds whose lane and session counts put their tables at odd offsets
+    (3 sessions of 5 lanes, 5 of 3) run, and each session's rows are the same
+    bits shared or alone."""
+    from conftest import SMALL
+    m = igc_lib.Model(folder=small_dir, window_limit=SMALL["window_limit"])
+    rng = np.random.default_rng(7)
+    for n, k in ((3, 5), (5, 3)):
+        prompts = [rng.integers(0, SMALL["vocab"], 30 + 11 * j).astype(np.int32) for j in range(n)]
+        shared = [igc_lib.Session(m) for _ in range(n)]
+        alone = [igc_lib.Session(m) for _ in range(n)]
+        for a, b, p in zip(shared, alone, prompts):
+            a.prime(p)
+            b.prime(p)
+        blocks = np.stack([np.concatenate([p[-1:], rng.integers(0, SMALL["vocab"], k - 1)]) for p in prompts])
+        crowd = igc_lib.Crowd(m, n, k)
+        _, _, rows = crowd.round(shared, blocks.astype(np.int32), want_logits=True)
+        for j in range(n):
+            _, _, one = crowd.round([alone[j]], blocks[j:j + 1].astype(np.int32), want_logits=True)
+            assert np.array_equal(one, rows[j * k:(j + 1) * k])
+        crowd.close()
+        for x in shared + alone:
+            x.close()
+    m.close()
