@@ -66,7 +66,8 @@ class SynthSpec(ctypes.Structure):
                 ("share_count", ctypes.c_int), ("global_every", ctypes.c_int),
                 ("window_limit", ctypes.c_int), ("norm_offset", ctypes.c_float),
                 ("with_layer_scalar", ctypes.c_int), ("seed", ctypes.c_uint64),
-                ("cache_scale_k", ctypes.c_float), ("cache_scale_v", ctypes.c_float)]
+                ("cache_scale_k", ctypes.c_float), ("cache_scale_v", ctypes.c_float),
+                ("double_wide", ctypes.c_int), ("global_head_dim", ctypes.c_int)]
 
 
 def spec_e2b(norm_offset=0.0, seed=1, window_limit=32768):

@@ -509,13 +509,19 @@ constexpr int AT_MAX_CLUSTER = 16;
 
 template <int HD>
 struct AttnLayout {                  // offsets in floats
+  // A head of 512 (the export's global layers) keeps two tiles in flight and
+  // reads the pass's new rows through the tiles like any cached row (they are
+  // in the cache before it runs, written by lane_kv_kernel); narrower heads
+  // keep three and hold the pass's new rows apart, computed here.
+  static constexpr int DEPTH = HD > 256 ? 2 : AT_DEPTH;
+  static constexpr bool NEW_ROWS = HD <= 256;
   static constexpr int KS = HD + 8;  // key rows: a half-warp's float2 reads meet 32 banks
   static constexpr int VS = HD + 4;  // value rows: a warp's scalar reads meet 32 banks
   static constexpr int QS = HD + 4;
   static constexpr int TILE = AT_POS * (KS + VS);  // a slot: 16 key rows, then 16 value rows
-  static constexpr int O_NEWK = AT_DEPTH * TILE;
-  static constexpr int O_NEWV = O_NEWK + AT_POS * KS;
-  static constexpr int O_Q = O_NEWV + AT_POS * VS;
+  static constexpr int O_NEWK = DEPTH * TILE;
+  static constexpr int O_NEWV = O_NEWK + (NEW_ROWS ? AT_POS * KS : 0);
+  static constexpr int O_Q = O_NEWV + (NEW_ROWS ? AT_POS * VS : 0);
   static constexpr int O_ZERO = O_Q + AT_ROWS * QS;
   static constexpr int O_SRED = O_ZERO + KS;                    // [8 warps][16][AT_SRED]
   static constexpr int O_P = O_SRED + 8 * AT_ROWS * AT_SRED;    // hi, lo weights: 2 x [16][AT_SRED] halves
@@ -707,8 +713,8 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   const int cp_col = 4 * (tid % CP_C4), cp_r0 = tid / CP_C4;
   auto issue = [&](int i) {
     const int tb = (t0 + i * CX) * AT_POS;
-    const int a = max(tb, lo_all), b = min(tb + AT_POS, p0);
-    float *slot = ring + (i % AT_DEPTH) * LY::TILE;
+    const int a = max(tb, lo_all), b = min(tb + AT_POS, LY::NEW_ROWS ? p0 : hi_all);
+    float *slot = ring + (i % LY::DEPTH) * LY::TILE;
 #pragma unroll
     for (int row = cp_r0; row < AT_POS; row += CP_RPP) {
       const int pos = tb + row;
@@ -720,7 +726,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     }
   };
   for (int i = tid; i < KS; i += blockDim.x) zrow[i] = 0.0f;
-  for (int i = 0; i < AT_DEPTH; ++i) {
+  for (int i = 0; i < LY::DEPTH; ++i) {
     if (i < n_tiles) issue(i);
     cp_async_commit();
   }
@@ -751,7 +757,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   // block; on a sharing layer read back from the owner's cache).  Three at
   // a time: all three rows' loads issue before any row's arithmetic.
   {
-    const int n_items = 2 + (2 * lanes - warp + 7) / 8;
+    const int n_items = LY::NEW_ROWS ? 2 + (2 * lanes - warp + 7) / 8 : 2;
     for (int k0 = 0; k0 < n_items; k0 += 3) {
       HeadRow<DPL> R[3];
       bool live[3], norm[3], turn[3];
@@ -817,7 +823,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     }
   }
 
-  cp_async_wait<AT_DEPTH - 1>();  // this thread's copies of tile 0
+  cp_async_wait<LY::DEPTH - 1>();  // this thread's copies of tile 0
   __syncthreads();
   // the query A fragments of this warp's k-steps (warp w: 16 columns from
   // 16 (w + 8 i)); warps past the head's last k-step hold unused copies
@@ -847,14 +853,16 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   // place: one commit group a step keeps the count regular) the values
   for (int i = 0; i < n_tiles; ++i) {
     const int tb = (t0 + i * CX) * AT_POS;
-    const float *slot = ring + (i % AT_DEPTH) * LY::TILE;
+    const float *slot = ring + (i % LY::DEPTH) * LY::TILE;
     // a position's key and value rows: new, cached, or zeros outside the pass's span
     auto krow = [&](int pos) -> const float * {
-      return (pos < lo_all || pos >= hi_all) ? zrow : pos >= p0 ? newk + (pos - p0) * KS : slot + (pos - tb) * KS;
+      return (pos < lo_all || pos >= hi_all)   ? zrow
+             : (LY::NEW_ROWS && pos >= p0) ? newk + (pos - p0) * KS
+                                           : slot + (pos - tb) * KS;
     };
     auto vrow = [&](int pos) -> const float * {
       return (pos < lo_all || pos >= hi_all) ? zrow
-             : pos >= p0                      ? newv + (pos - p0) * VS
+             : (LY::NEW_ROWS && pos >= p0)    ? newv + (pos - p0) * VS
                                               : slot + AT_POS * KS + (pos - tb) * VS;
     };
     // scores: this warp's k-steps of the 16 x 16 tile, into the partials;
@@ -887,7 +895,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     }
     __syncthreads();  // the partials are written, and every warp is past tile i - 1
     if (i >= 1) {
-      if (i - 1 + AT_DEPTH < n_tiles) issue(i - 1 + AT_DEPTH);
+      if (i - 1 + LY::DEPTH < n_tiles) issue(i - 1 + LY::DEPTH);
       cp_async_commit();
     }
     // online softmax of row sr, one thread a position; the warps' partials
@@ -913,7 +921,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     ph[sr * AT_SRED + sp] = eh;
     pl[sr * AT_SRED + sp] = __float2half_rn(e - __half2float(eh));
     if (sp == 0) fsc[sr] = fct;
-    cp_async_wait<1>();  // this thread's copies of tile i + 1
+    cp_async_wait<LY::DEPTH - 2>();  // this thread's copies of tile i + 1 (all but the newest group)
     __syncthreads();     // the weights and factors are written; tile i + 1 is in place
     // weighted values: this warp's 8-dimension tiles n = warp + 8 i
     {
@@ -1411,7 +1419,8 @@ extern "C" {
 extern "C++" {
 template <int HD>
 static cudaError_t allow_attn(int bytes) {
-  cudaError_t e = allow_smem_fn(attn_kernel<HD, 8>, bytes);
+  cudaError_t e = cudaSuccess;
+  if constexpr (HD <= 256) e = allow_smem_fn(attn_kernel<HD, 8>, bytes);  // a 512 head runs in clusters of 16 only
   if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 16>, bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<HD, 16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
@@ -1435,6 +1444,7 @@ cudaError_t igc_kernels_configure(int bytes) {
   if (e == cudaSuccess) e = allow_attn<64>(bytes);
   if (e == cudaSuccess) e = allow_attn<128>(bytes);
   if (e == cudaSuccess) e = allow_attn<256>(bytes);
+  if (e == cudaSuccess) e = allow_attn<512>(bytes);
   if (e == cudaSuccess) e = allow_smem_fn(topk_stage2_kernel, bytes);
   return e;
 }
@@ -1528,6 +1538,7 @@ size_t igc_attn_smem(int hd) {
     case 64: return sizeof(float) * AttnLayout<64>::FLOATS;
     case 128: return sizeof(float) * AttnLayout<128>::FLOATS;
     case 256: return sizeof(float) * AttnLayout<256>::FLOATS;
+    case 512: return sizeof(float) * AttnLayout<512>::FLOATS;
     default: return 0;
   }
 }
@@ -1586,6 +1597,7 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
   const size_t smem = igc_attn_smem(hd);
   const int G = heads / kv_heads;
   const dim3 grid(cluster, kv_heads * ((lanes * G + AT_ROWS - 1) / AT_ROWS), batch);
+  const dim3 grid16(16, grid.y, batch);
 #define IGC_ATT(HD)                                                                                              \
   return cluster == 8 ? launch_attn<HD, 8>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
                                            sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,   \
@@ -1598,6 +1610,13 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
     case 64: IGC_ATT(64)
     case 128: IGC_ATT(128)
     case 256: IGC_ATT(256)
+    case 512:
+      // a 512-wide head: clusters of 16 always (the merge takes 32 dimensions
+      // a block), and the pass's new rows must already be in the cache
+      if (owner) return cudaErrorInvalidValue;
+      return launch_attn<512, 16>(grid16, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
+                                  owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp, kc_tab,
+                                  vc_tab, pos_tab, cq);
     default: return cudaErrorInvalidValue;
   }
 #undef IGC_ATT

@@ -584,9 +584,9 @@ __global__ void __launch_bounds__(256) lane_kv_kernel(const float *qkv, int qkv_
     const float q = is_v ? cq.vq : cq.kq;  // a byte side's scale, else 0
     float *dst = (is_v ? vc : kc) + at;
     uint8_t *dstb = reinterpret_cast<uint8_t *>(is_v ? vc : kc) + at;
-    float lo[4], hi[4], ss = 0.0f, mx = 0.0f;
+    float lo[8], hi[8], ss = 0.0f, mx = 0.0f;  // heads up to 512: d = lane + 32 e < 256
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+    for (int e = 0; e < 8; ++e) {
       const int d = l + 32 * e;
       lo[e] = d < half ? src[d] : 0.0f;
       hi[e] = d < half ? src[d + half] : 0.0f;
@@ -594,7 +594,7 @@ __global__ void __launch_bounds__(256) lane_kv_kernel(const float *qkv, int qkv_
     }
     const float sh = rms_shrink(warp_sum(ss), hd, eps);  // app_core.c:4667 kern_norm_rms
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
+    for (int e = 0; e < 8; ++e) {
       const int d = l + 32 * e;
       if (d >= half) continue;
       float x = lo[e] * sh, y = hi[e] * sh;
@@ -794,7 +794,7 @@ cudaError_t igc_launch_lane_kv_many(const float *qkv, int qkv_stride, int heads,
                                     int lanes, float *kc, float *vc, const CacheStore *store, const int *pos_tab,
                                     float *const *kc_tab, float *const *vc_tab, float *const *peak_tab, int per,
                                     cudaStream_t st) {
-  if (lanes < 1 || hd % 32 || hd > 256 || kv_heads < 1) return cudaErrorInvalidValue;
+  if (lanes < 1 || hd % 32 || hd > 512 || kv_heads < 1) return cudaErrorInvalidValue;
   if (pos_tab ? (!kc_tab || !vc_tab || per < 1 || lanes % per) : (!p0 || !kc || !vc)) return cudaErrorInvalidValue;
   CacheStore cq = {};
   if (store) cq = *store;

@@ -675,7 +675,7 @@ static int bind_model(igc_model *m, Source &src) {
     if (c != IGC_OKAY) return c;
     L.q_rows = q.rows;
     L.hd = q.rows / m->heads;
-    if (L.hd * m->heads != q.rows || L.hd % 16 || L.hd > 256) return IGC_FAIL_SUPPORT;
+    if (L.hd * m->heads != q.rows || L.hd % 16 || L.hd > 512) return IGC_FAIL_SUPPORT;
     if (!L.share) {
       c = b.code_view(STEM("self_attn.k_proj"), m->hidden, k);
       if (c != IGC_OKAY) return c;
@@ -981,6 +981,15 @@ static size_t side_bytes(float q) { return q > 0.0f ? 1u : sizeof(float); }
 static bool layer_bytes(const igc_model *m, int owner) {
   const CacheStore cq = layer_store(m, owner, nullptr);
   return cq.kq > 0.0f || cq.vq > 0.0f;
+}
+
+// Whether layer l's attention runs as separate launches (new rows written
+// first, then attention reading every row from the cache): a byte side, or a
+// head wider than 256 (the export's global layers), whose attention kernel
+// has no room to hold the pass's new rows apart.
+static bool layer_split(const igc_model *m, int l) {
+  const DevLayer &L = m->layer[l];
+  return layer_bytes(m, L.share ? L.source : l) || L.hd > 256;
 }
 
 // The float rows a layer's attention reads from: its owner's cache on a float
@@ -1377,7 +1386,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
     const DevLayer &O = m->layer[owner];
     prof_mark(s, PROF_ATTN, 0.0);
     const int sliding = L.kind == 0 ? 1 : 0;
-    if (!layer_bytes(m, owner)) {
+    if (!layer_split(m, l)) {
       // queries, an owner's new rows and the attention in one kernel
       const CacheStore cq = layer_store(m, owner, L.share ? nullptr : s->d_peak + 2 * l);
       CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
@@ -1385,24 +1394,27 @@ static int enqueue_pass(igc_session *s, int K, int want) {
                           m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
                           next_stamp(s, PROF_ATTN, 0.0), &cq, s->st));
     } else {
-      // a byte cache: an owner's new rows onto the grid, the rows the pass
-      // reads decoded to floats, then the attention over those (as a sharing
-      // layer reads).  No overlap: attention copies rows before its wait.
+      // an owner's new rows written first (onto the grid on a byte side),
+      // a byte side's rows the pass reads decoded to floats, then the
+      // attention over those (as a sharing layer reads).  No overlap:
+      // attention copies rows before its wait.
       const CacheStore cq = layer_store(m, owner, s->d_peak + 2 * l);
       igc_kernels_pdl(0);
       if (!L.share)
         CKL(igc_launch_lane_kv(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.k_norm, m->rope_cs[L.kind],
                                m->rope_sn[L.kind], m->eps, d_p0, K, s->kc[owner], s->vc[owner], &cq, s->st));
-      WidenArgs w = widen_of(s, owner, sliding, K);
-      w.p0 = d_p0;
-      CKL(igc_launch_lane_widen(&w, 1, widen_rows_most(m, sliding, K), m->sm_count, s->st));
+      if (layer_bytes(m, owner)) {
+        WidenArgs w = widen_of(s, owner, sliding, K);
+        w.p0 = d_p0;
+        CKL(igc_launch_lane_widen(&w, 1, widen_rows_most(m, sliding, K), m->sm_count, s->st));
+      }
       CKL(igc_launch_attn(s->qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                           m->rope_sn[L.kind], m->eps, 0, attn_rows(s, owner, 0), attn_rows(s, owner, 1), sliding,
                           m->slide_span, d_p0, K, s->attn_cluster, s->attn, L.q_rows, mags ? ma.buf : nullptr,
                           next_stamp(s, PROF_ATTN, 0.0), nullptr, s->st));
       igc_kernels_pdl(s->use_pdl != 0);
     }
-    ma.parts = m->heads * s->attn_cluster;
+    ma.parts = m->heads * (L.hd > 256 ? 16 : s->attn_cluster);  // a 512 head runs in clusters of 16
     c = gemv(s, L.o, K, PRO_F32, EPI_STORE, s->attn, L.q_rows, nullptr, nullptr, 1.0f, nullptr, nullptr, s->obuf, H,
              1.0f, nullptr, 0, nullptr, &so, ma_in);
     if (c != IGC_OKAY) return c;
@@ -2363,7 +2375,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
     const DevLayer &O = m->layer[owner];
     const int sliding = L.kind == 0 ? 1 : 0;
     const size_t at = (size_t)l * cr->cap;
-    if (!layer_bytes(m, owner)) {
+    if (!layer_split(m, l)) {
       const CacheStore cq = layer_store(m, owner, nullptr, L.share ? nullptr : cr->pk() + at);
       CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr,
@@ -2371,15 +2383,23 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
                                nullptr, cr->kc() + at, cr->vc() + at, cr->pos(), S, &cq, cr->st));
       return IGC_OKAY;
     }
-    // a byte cache: every session's new rows onto the grid, the rows each
-    // reads decoded to floats, then attention over those without overlap
-    // (it copies rows before its wait)
+    // every session's new rows written first (onto the grid on a byte
+    // side), a byte side's rows each reads decoded to floats, then attention
+    // over those without overlap (it copies rows before its wait)
     const CacheStore cq = layer_store(m, owner, nullptr);
     igc_kernels_pdl(0);
     if (!L.share)
       CKL(igc_launch_lane_kv_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.k_norm, m->rope_cs[L.kind],
                                   m->rope_sn[L.kind], m->eps, nullptr, S * k, nullptr, nullptr, &cq, cr->pos(),
                                   cr->kc() + at, cr->vc() + at, cr->pk() + at, k, cr->st));
+    if (!layer_bytes(m, owner)) {
+      CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
+                               m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding,
+                               m->slide_span, cr->pos(), k, IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr, nullptr,
+                               cr->kc() + at, cr->vc() + at, cr->pos(), S, nullptr, cr->st));
+      igc_kernels_pdl(1);
+      return IGC_OKAY;
+    }
     WidenArgs w;
     memset(&w, 0, sizeof(w));
     w.kc_tab = cr->kc() + at;

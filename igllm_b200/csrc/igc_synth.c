@@ -170,7 +170,7 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
   char name[128];
   int n = 0;
   int first_share = s->layers - s->share_count;
-  int qw = s->heads * s->head_dim, kvw = s->kv_heads * s->head_dim, PS = s->layers * s->ple_dim;
+  int PS = s->layers * s->ple_dim;
   float no = s->norm_offset;
   snprintf(name, sizeof(name), "%sembed_tokens.weight", P);
   add(room, room_count, &n, name, 3, s->vocab, s->hidden, 2, IGC_SYNTH_NORMAL, 0.0f);
@@ -186,6 +186,11 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
   for (int l = 0; l < s->layers; ++l) {
     char stem[128];
     int share = s->share_count > 0 && l >= first_share;
+    /* a global layer's head width (global_head_dim), and the doubled
+     * feed-forward of the layers that share another's cache */
+    int hd = layer_global(s, l) && s->global_head_dim > 0 ? s->global_head_dim : s->head_dim;
+    int qw = s->heads * hd, kvw = s->kv_heads * hd;
+    int inner = share && s->double_wide ? 2 * s->inner : s->inner;
 #define STEM(fmt) snprintf(stem, sizeof(stem), "%slayers.%d." fmt, P, l)
     STEM("self_attn.q_proj");
     add_plane(room, room_count, &n, stem, qw, s->hidden);
@@ -195,7 +200,7 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
       STEM("self_attn.v_proj");
       add_plane(room, room_count, &n, stem, kvw, s->hidden);
       STEM("self_attn.k_norm.weight");
-      add(room, room_count, &n, stem, 3, s->head_dim, 0, 1, IGC_SYNTH_OFFSET, no);
+      add(room, room_count, &n, stem, 3, hd, 0, 1, IGC_SYNTH_OFFSET, no);
       /* the export's static cache ranges (app_core.c:8596-8601), varied by layer */
       if (s->cache_scale_k > 0.0f) {
         STEM("self_attn.k_cache_scale");
@@ -209,13 +214,13 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
     STEM("self_attn.o_proj");
     add_plane(room, room_count, &n, stem, s->hidden, qw);
     STEM("self_attn.q_norm.weight");
-    add(room, room_count, &n, stem, 3, s->head_dim, 0, 1, IGC_SYNTH_OFFSET, no);
+    add(room, room_count, &n, stem, 3, hd, 0, 1, IGC_SYNTH_OFFSET, no);
     STEM("mlp.gate_proj");
-    add_plane(room, room_count, &n, stem, s->inner, s->hidden);
+    add_plane(room, room_count, &n, stem, inner, s->hidden);
     STEM("mlp.up_proj");
-    add_plane(room, room_count, &n, stem, s->inner, s->hidden);
+    add_plane(room, room_count, &n, stem, inner, s->hidden);
     STEM("mlp.down_proj");
-    add_plane(room, room_count, &n, stem, s->hidden, s->inner);
+    add_plane(room, room_count, &n, stem, s->hidden, inner);
     STEM("input_layernorm.weight");
     add(room, room_count, &n, stem, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
     STEM("post_attention_layernorm.weight");
@@ -278,12 +283,13 @@ char *igc_synth_config_text(const igc_synth_spec *s) {
   tb_add(&b, "    \"hidden_size\": %d,\n    \"intermediate_size\": %d,\n", s->hidden, s->inner);
   tb_add(&b, "    \"num_hidden_layers\": %d,\n    \"num_attention_heads\": %d,\n", s->layers, s->heads);
   tb_add(&b, "    \"num_key_value_heads\": %d,\n    \"head_dim\": %d,\n    \"global_head_dim\": %d,\n",
-         s->kv_heads, s->head_dim, s->head_dim);
+         s->kv_heads, s->head_dim, s->global_head_dim > 0 ? s->global_head_dim : s->head_dim);
   tb_add(&b, "    \"hidden_size_per_layer_input\": %d,\n    \"num_kv_shared_layers\": %d,\n",
          s->ple_dim, s->share_count);
   tb_add(&b, "    \"sliding_window\": %d,\n    \"max_position_embeddings\": %d,\n", s->slide_span,
          s->window_limit);
-  tb_add(&b, "    \"use_double_wide_mlp\": false,\n    \"attention_k_eq_v\": false,\n");
+  tb_add(&b, "    \"use_double_wide_mlp\": %s,\n    \"attention_k_eq_v\": false,\n",
+         s->double_wide ? "true" : "false");
   tb_add(&b, "    \"enable_moe_block\": false,\n    \"rms_norm_eps\": 1e-06,\n");
   tb_add(&b, "    \"final_logit_softcapping\": 30.0,\n    \"hidden_activation\": \"gelu_pytorch_tanh\",\n");
   tb_add(&b, "    \"bos_token_id\": 2,\n    \"eos_token_id\": 1,\n    \"pad_token_id\": 0,\n");

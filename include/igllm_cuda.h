@@ -357,6 +357,11 @@ typedef struct igc_synth_spec {
   /* > 0: write each owner layer's self_attn.k_cache_scale / v_cache_scale as
    * an F32 scalar, this value times (1 + (layer mod 4) / 8); 0 writes none */
   float cache_scale_k, cache_scale_v;
+  /* 1: the layers that share another's cache get a feed-forward twice
+   * `inner` wide (use_double_wide_mlp); 0: every layer `inner` */
+  int double_wide;
+  /* > 0: global layers' head width (global_head_dim); 0: head_dim */
+  int global_head_dim;
 } igc_synth_spec;
 
 /* Fill `out` with `count` values of stream `stream` of the spec's seed.
