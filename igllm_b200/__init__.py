@@ -67,7 +67,9 @@ class SynthSpec(ctypes.Structure):
                 ("window_limit", ctypes.c_int), ("norm_offset", ctypes.c_float),
                 ("with_layer_scalar", ctypes.c_int), ("seed", ctypes.c_uint64),
                 ("cache_scale_k", ctypes.c_float), ("cache_scale_v", ctypes.c_float),
-                ("double_wide", ctypes.c_int), ("global_head_dim", ctypes.c_int)]
+                ("double_wide", ctypes.c_int), ("global_head_dim", ctypes.c_int),
+                ("late_mlp_bits", ctypes.c_int), ("group", ctypes.c_int), ("bf16_scales", ctypes.c_int),
+                ("embed_bits", ctypes.c_int), ("ple_embed_bits", ctypes.c_int), ("tied_head", ctypes.c_int)]
 
 
 def spec_e2b(norm_offset=0.0, seed=1, window_limit=32768):

@@ -73,13 +73,23 @@ bool grow(DeskState *s, size_t floats) {
   return true;
 }
 
-// app_core.c:1775 plane, restricted to what the kernels read: 4-bit codes,
-// no flip, no zero points, groups of 32, f16 scales.
+// app_core.c:1775 plane, restricted to what the kernels read: offset codes of
+// 1, 2 or 4 bits, no flip, no zero points, groups a multiple of 32 columns,
+// scales of any float type that f16 holds exactly.
 const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
   auto it = s->planes.find(p->code_data);
   if (it != s->planes.end()) return &it->second;
-  if (p->form != 2 || p->bit_count != 4 || p->code_flip != 0 || p->bias_data || p->group_size != 32 ||
-      p->gain_type != 2 || p->code_bias != 8) {
+  const int bits = p->bit_count;
+  if (p->form != 2 || (bits != 1 && bits != 2 && bits != 4) || p->code_flip != 0 || p->bias_data ||
+      p->group_size < 32 || p->group_size % 32 || p->group_count * p->group_size < p->col_count ||
+      p->code_bias != (1 << (bits - 1))) {
+    note(s, IGC_FAIL_SUPPORT);
+    return nullptr;
+  }
+  const int g32 = (p->col_count + 31) / 32;
+  std::vector<uint16_t> sc((size_t)p->row_count * g32);
+  if (igc_scales_f16(p->gain_data, p->gain_type, p->row_count, p->group_count, p->group_size, p->col_count,
+                     sc.data()) != 0) {
     note(s, IGC_FAIL_SUPPORT);
     return nullptr;
   }
@@ -88,7 +98,7 @@ const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
   dp.cols = p->col_count;
   dp.n_rb = (p->row_count + 15) / 16;
   dp.n_cc = (p->col_count + 63) / 64;
-  size_t cb = (size_t)p->row_count * p->row_stride, sb = (size_t)p->row_count * p->group_count * 2;
+  size_t cb = (size_t)p->row_count * p->row_stride, sb = sizeof(uint16_t) * sc.size();
   uint8_t *dc = nullptr;
   uint16_t *ds = nullptr;
   if (!ok(s, cudaMalloc(&dp.tiles, (size_t)dp.n_rb * dp.n_cc * 512)) ||
@@ -96,8 +106,8 @@ const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
       !ok(s, cudaMalloc(&ds, sb)))
     return nullptr;
   bool good = ok(s, cudaMemcpy(dc, p->code_data, cb, cudaMemcpyHostToDevice)) &&
-              ok(s, cudaMemcpy(ds, p->gain_data, sb, cudaMemcpyHostToDevice)) &&
-              ok(s, igc_launch_repack(dc, p->row_stride, ds, p->group_count, p->row_count, p->col_count, dp.n_rb,
+              ok(s, cudaMemcpy(ds, sc.data(), sb, cudaMemcpyHostToDevice)) &&
+              ok(s, igc_launch_repack(dc, p->row_stride, bits, ds, g32, p->row_count, p->col_count, dp.n_rb,
                                       dp.n_cc, 1, 0, dp.tiles, dp.scales, s->st)) &&
               ok(s, cudaStreamSynchronize(s->st));
   cudaFree(dc);

@@ -239,6 +239,27 @@ __device__ __forceinline__ float cache_real8(uint32_t code) {
   return (code & 0x80u) ? -a : a;
 }
 
+// A quantized embedding table as the export stores it (app_core.c:7886
+// plane_bind_gemma, `embedding_quantized` + `embedding_scale`): codes of
+// `bits` bits packed from the low bit, `stride` bytes a row, a value being
+// the code minus 2^(bits-1), times the f16 scale of its 32-column group
+// (`scales` [rows][g32]).  `codes` null: the table is bf16 instead.
+struct EmbedCodes {
+  const uint8_t *codes;
+  size_t stride;
+  int bits;
+  const uint16_t *scales;
+  int g32;
+};
+
+// The value of column c of row r of a code table (app_core.c:1826 plane_row).
+__device__ __forceinline__ float embed_code(const EmbedCodes &t, size_t r, int c) {
+  const size_t bit = (size_t)c * t.bits;  // 1, 2 or 4 bits: never across a byte
+  const uint32_t v = (uint32_t)(t.codes[r * t.stride + (bit >> 3)] >> (bit & 7)) & ((1u << t.bits) - 1u);
+  const float scale = __half2float(__ushort_as_half(t.scales[r * t.g32 + (c >> 5)]));
+  return (float)((int)v - (1 << (t.bits - 1))) * scale;
+}
+
 // How a layer's key and value caches are stored, and where the largest
 // magnitudes written go.  A side whose scale is 0 holds float rows; a
 // positive scale makes it e4m3 bytes of value / scale (written by

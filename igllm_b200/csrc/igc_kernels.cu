@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <float.h>
 #include <stdint.h>
+#include <string.h>
 
 #include "igc_gemv.cuh"
 #include "igc_kernels.h"
@@ -10,11 +11,14 @@
 namespace igc {
 
 // ---------------------------------------------------------------------------
-// upload repack: raw U8 codes (two a byte, low nibble first, row_stride bytes a
-// row) and f16 scales [rows][groups] into the tile layout of igc_gemv.cuh.
+// upload repack: raw U8 codes of `bits` (1, 2 or 4) bits, packed from the low
+// bit up (app_core.c:1757 pack_read: code c at bits [c*bits, (c+1)*bits) of
+// its row, row_stride bytes a row), each the value plus 2^(bits-1), and f16
+// scales [rows][groups of 32 columns] into the tile layout of igc_gemv.cuh,
+// where every code is a 4-bit value + 8 (a 1- or 2-bit value fits exactly).
 // One thread writes one thread-slot (16 bytes) of one tile and, for t == 0,
 // that slot group's 8-byte scale record.
-__global__ void repack_kernel(const uint8_t *code, size_t row_stride, const uint16_t *scale,
+__global__ void repack_kernel(const uint8_t *code, size_t row_stride, int bits, const uint16_t *scale,
                               int groups, int rows, int cols, int n_rb, int n_cc, int out_mul, int out_add,
                               uint4 *tiles, uint2 *scales) {
   long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -29,8 +33,9 @@ __global__ void repack_kernel(const uint8_t *code, size_t row_stride, const uint
   long out_tile = (long)(rb * out_mul + out_add) * n_cc + cc;
   auto nib = [&](int r, int c) -> uint32_t {
     if (r >= rows || c >= cols) return 8u;  // zero weight
-    uint8_t byte = code[(size_t)r * row_stride + (size_t)(c >> 1)];
-    return (c & 1) ? (uint32_t)(byte >> 4) : (uint32_t)(byte & 15u);
+    const size_t bit = (size_t)c * bits;  // a code of 1, 2 or 4 bits never straddles a byte
+    const uint32_t v = (uint32_t)(code[(size_t)r * row_stride + (bit >> 3)] >> (bit & 7)) & ((1u << bits) - 1u);
+    return v + 8u - (1u << (bits - 1));
   };
   uint32_t word[4];
 #pragma unroll
@@ -410,7 +415,7 @@ __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embe
                              float embed_gain, const uint16_t *ple_embed, int ple_vocab,
                              int ple_width, float ple_gain, float *x_out, float *seed_out,
                              unsigned long long *stamp, int stamp_n, const float *peak, float *peak_saved,
-                             int peak_n) {
+                             int peak_n, EmbedCodes eq, EmbedCodes pq) {
   pdl_release();
   // the pass's launch stamps start over (every later kernel of the pass
   // stamps only after its wait, so after this kernel has finished)
@@ -427,15 +432,25 @@ __global__ void embed_kernel(const int32_t *ids, int lanes, const uint16_t *embe
   if (j >= lanes) return;
   const int id = ids[j];
   const int step = gridDim.y * blockDim.x, first = blockIdx.y * blockDim.x + threadIdx.x;
-  const uint4 *row = reinterpret_cast<const uint4 *>(embed + (size_t)id * hidden);
-  float4 *xo = reinterpret_cast<float4 *>(x_out + (size_t)j * hidden);
-  for (int i = first; i < hidden / 8; i += step) {
-    float4 a, b;
-    bf16x8_scaled(row[i], embed_gain, a, b);
-    xo[2 * i] = a;
-    xo[2 * i + 1] = b;
+  if (eq.codes) {
+    // a quantized table: each value decoded, then scaled as a bf16 row is
+    float *xo = x_out + (size_t)j * hidden;
+    for (int c = first; c < hidden; c += step) xo[c] = embed_code(eq, (size_t)id, c) * embed_gain;
+  } else {
+    const uint4 *row = reinterpret_cast<const uint4 *>(embed + (size_t)id * hidden);
+    float4 *xo = reinterpret_cast<float4 *>(x_out + (size_t)j * hidden);
+    for (int i = first; i < hidden / 8; i += step) {
+      float4 a, b;
+      bf16x8_scaled(row[i], embed_gain, a, b);
+      xo[2 * i] = a;
+      xo[2 * i + 1] = b;
+    }
   }
-  if (ple_embed) {
+  if (pq.codes) {
+    float *so = seed_out + (size_t)j * ple_width;
+    const size_t pr = (size_t)(id % ple_vocab);
+    for (int c = first; c < ple_width; c += step) so[c] = embed_code(pq, pr, c) * ple_gain;
+  } else if (ple_embed) {
     const uint4 *srow = reinterpret_cast<const uint4 *>(ple_embed + (size_t)(id % ple_vocab) * ple_width);
     float4 *so = reinterpret_cast<float4 *>(seed_out + (size_t)j * ple_width);
     for (int i = first; i < ple_width / 8; i += step) {
@@ -1449,14 +1464,55 @@ cudaError_t igc_kernels_configure(int bytes) {
   return e;
 }
 
-cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint16_t *scale, int groups,
+cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, int bits, const uint16_t *scale, int groups,
                               int rows, int cols, int n_rb, int n_cc, int out_mul, int out_add, uint4 *tiles,
                               uint2 *scales, cudaStream_t st) {
+  if (bits != 1 && bits != 2 && bits != 4) return cudaErrorInvalidValue;
   long total = (long)n_rb * n_cc * 32;
   int blocks = (int)((total + 255) / 256);
-  repack_kernel<<<blocks, 256, 0, st>>>(code, row_stride, scale, groups, rows, cols, n_rb, n_cc, out_mul,
+  repack_kernel<<<blocks, 256, 0, st>>>(code, row_stride, bits, scale, groups, rows, cols, n_rb, n_cc, out_mul,
                                         out_add, tiles, scales);
   return cudaGetLastError();
+}
+
+// A plane's group scales as f16 [rows][ceil(cols / 32)]: each group of
+// `group_size` columns (a multiple of 32) spreads its scale over its 32-column
+// groups, converted from F32 (1), F16 (2) or BF16 (3) storage.  Refused (-1)
+// unless every scale survives the conversion exactly, since the products use
+// it as stored.
+int igc_scales_f16(const void *src, int dtype, int rows, int groups, int group_size, int cols, uint16_t *out) {
+  if (rows < 1 || groups < 1 || group_size < 32 || group_size % 32 || cols < 1) return -1;
+  const int g32 = (cols + 31) / 32, per = group_size / 32;
+  for (int r = 0; r < rows; ++r)
+    for (int g = 0; g < groups; ++g) {
+      float v;
+      const size_t i = (size_t)r * groups + g;
+      if (dtype == 1) {
+        memcpy(&v, (const uint8_t *)src + 4 * i, 4);
+      } else if (dtype == 2 || dtype == 3) {
+        uint16_t h;
+        memcpy(&h, (const uint8_t *)src + 2 * i, 2);
+        if (dtype == 2) {
+          __half hh;
+          memcpy(&hh, &h, 2);
+          v = __half2float(hh);
+        } else {
+          const uint32_t u = (uint32_t)h << 16;
+          memcpy(&v, &u, 4);
+        }
+      } else {
+        return -1;
+      }
+      const __half h16 = __float2half_rn(v);
+      if (__half2float(h16) != v && !(v != v)) return -1;
+      uint16_t bits16;
+      memcpy(&bits16, &h16, 2);
+      for (int k = 0; k < per; ++k) {
+        const int c32 = g * per + k;
+        if (c32 < g32) out[(size_t)r * g32 + c32] = bits16;
+      }
+    }
+  return 0;
 }
 
 void igc_kernels_pdl(int on) { g_pdl = on; }
@@ -1518,11 +1574,18 @@ size_t igc_gemv_smem_min(const GemvArgs *a, int pair) {
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
                              float *x_out, float *seed_out, unsigned long long *stamp, int stamp_n,
-                             const float *peak, float *peak_saved, int peak_n, cudaStream_t st) {
+                             const float *peak, float *peak_saved, int peak_n, const EmbedCodes *embed_q,
+                             const EmbedCodes *ple_q, cudaStream_t st) {
   if ((hidden & 7) || (ple_embed && (ple_width & 7)) || (peak_saved && (!peak || peak_n < 0)))
     return cudaErrorInvalidValue;
+  EmbedCodes eq = {}, pq = {};
+  if (embed_q) eq = *embed_q;
+  if (ple_q) pq = *ple_q;
+  if ((!eq.codes && !embed) || (eq.codes && eq.bits != 1 && eq.bits != 2 && eq.bits != 4) ||
+      (pq.codes && pq.bits != 1 && pq.bits != 2 && pq.bits != 4))
+    return cudaErrorInvalidValue;
   embed_kernel<<<dim3(lanes, 8), 256, 0, st>>>(ids, lanes, embed, hidden, embed_gain, ple_embed, ple_vocab, ple_width,
-                                      ple_gain, x_out, seed_out, stamp, stamp_n, peak, peak_saved, peak_n);
+                                      ple_gain, x_out, seed_out, stamp, stamp_n, peak, peak_saved, peak_n, eq, pq);
   return cudaGetLastError();
 }
 

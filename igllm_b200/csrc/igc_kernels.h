@@ -10,9 +10,12 @@ extern "C" {
 
 cudaError_t igc_kernels_configure(int bytes);
 
-cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, const uint16_t *scale, int groups,
+cudaError_t igc_launch_repack(const uint8_t *code, size_t row_stride, int bits, const uint16_t *scale, int groups,
                               int rows, int cols, int n_rb, int n_cc, int out_mul, int out_add, uint4 *tiles,
                               uint2 *scales, cudaStream_t st);
+// Host: a plane's scales as f16 per 32-column group (see igc_kernels.cu); 0, or
+// -1 when a group is not a multiple of 32 columns or a scale is not exact in f16.
+int igc_scales_f16(const void *src, int dtype, int rows, int groups, int group_size, int cols, uint16_t *out);
 
 // Launches from the calling thread may overlap the kernel ahead of them
 // (programmatic dependent launch) while `on` is set.
@@ -31,7 +34,8 @@ size_t igc_gemv_smem_min(const igc::GemvArgs *a, int pair);
 cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embed, int hidden, float embed_gain,
                              const uint16_t *ple_embed, int ple_vocab, int ple_width, float ple_gain,
                              float *x_out, float *seed_out, unsigned long long *stamp, int stamp_n,
-                             const float *peak, float *peak_saved, int peak_n, cudaStream_t st);
+                             const float *peak, float *peak_saved, int peak_n, const igc::EmbedCodes *embed_q,
+                             const igc::EmbedCodes *ple_q, cudaStream_t st);
 cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes, int layers, int ple_dim,
                                   const float *w, float eps, float blend, float *out, cudaStream_t st);
 size_t igc_attn_smem(int hd);

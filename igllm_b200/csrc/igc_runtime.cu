@@ -314,6 +314,10 @@ struct igc_model {
   int rope_hd[2] = {0, 0};
   float *rope_cs[2] = {nullptr, nullptr}, *rope_sn[2] = {nullptr, nullptr};
   uint16_t *embed = nullptr, *ple_embed = nullptr;
+  // the embedding tables when the export stores them quantized
+  // (`embedding_quantized` + `embedding_scale`): codes as stored, f16 scales
+  // per 32-column group; `codes` null for a bf16 table
+  EmbedCodes embed_q = {}, ple_q = {};
   DevPlane ple_lift, head;
   float *ple_norm = nullptr, *final_norm = nullptr;
   std::vector<DevLayer> layer;
@@ -410,7 +414,8 @@ static int read_config(igc_model *m, const std::string &text, const igc_setup *s
 static std::string pick_prefix(Source &src) {
   const char *cands[] = {"model.language_model.", "language_model.model.", "model.", ""};
   for (const char *c : cands) {
-    if (src.find(std::string(c) + "embed_tokens.weight")) return c;
+    if (src.find(std::string(c) + "embed_tokens.weight") || src.find(std::string(c) + "embed_tokens.embedding_quantized"))
+      return c;
   }
   return "#";
 }
@@ -455,19 +460,27 @@ struct Binder {
     return v;
   }
 
-  // app_core.c:7886 plane_bind_gemma, 4-bit U8 codes with F16 group scales.
+  // app_core.c:7886 plane_bind_gemma: offset codes of 1, 2 or 4 bits packed in
+  // U8 bytes (the width fixed by `col_hint` and the row's byte count), group
+  // scales of any float type with groups a multiple of 32 columns.  8-bit
+  // codes (an I8 tensor, or U8 a byte a code) are refused: the tiles hold
+  // 4-bit values.
   struct CodeView {
     const Tensor *code = nullptr, *scale = nullptr;
-    int rows = 0, cols = 0, groups = 0;
-    std::string name;
+    int rows = 0, cols = 0, groups = 0, bits = 4, group_size = 32;
+    std::string name, code_name, scale_name;
   };
-  int code_view(const std::string &stem, int col_hint, CodeView &v) {
+  int code_view(const std::string &stem, int col_hint, CodeView &v, const char *leaf = "weight",
+                const char *scale_leaf = "weight_scale") {
     v.name = stem;
-    v.code = src.find(stem + ".weight");
+    v.code_name = stem + "." + leaf;
+    v.scale_name = stem + "." + scale_leaf;
+    v.code = src.find(v.code_name);
     if (!v.code) return IGC_FAIL_MISSING;
-    v.scale = src.find(stem + ".weight_scale");
-    if (v.code->dtype != T_U8 || !v.scale) return IGC_FAIL_SUPPORT;
+    v.scale = src.find(v.scale_name);
+    if (!v.scale || (v.code->dtype != T_U8 && v.code->dtype != T_I8)) return IGC_FAIL_SUPPORT;
     if (v.code->rank != 2) return IGC_FAIL_FORMAT;
+    if (v.code->dtype == T_I8) return IGC_FAIL_SUPPORT;
     int rows = (int)v.code->shape[0], bytes = (int)v.code->shape[1];
     int cols = col_hint;
     int bits = 0;
@@ -475,14 +488,55 @@ struct Binder {
     for (int w : widths)
       if (((int64_t)cols * w + 7) / 8 == bytes) { bits = w; break; }
     if (bits == 0) return IGC_FAIL_FORMAT;
-    if (bits != 4) return IGC_FAIL_SUPPORT;
+    if (bits == 8) return IGC_FAIL_SUPPORT;
     int groups = v.scale->rank >= 2 ? (int)v.scale->shape[v.scale->rank - 1] : 1;
     if (groups < 1 || cols % groups) return IGC_FAIL_FORMAT;
-    if (cols / groups != 32 || v.scale->dtype != T_F16) return IGC_FAIL_SUPPORT;
+    if ((cols / groups) % 32) return IGC_FAIL_SUPPORT;
+    if (v.scale->dtype != T_F16 && v.scale->dtype != T_BF16 && v.scale->dtype != T_F32) return IGC_FAIL_SUPPORT;
     if ((int)v.scale->shape[0] != rows) return IGC_FAIL_FORMAT;
     v.rows = rows;
     v.cols = cols;
     v.groups = groups;
+    v.bits = bits;
+    v.group_size = cols / groups;
+    return IGC_OKAY;
+  }
+
+  // A code view's scales as f16 per 32-column group; IGC_FAIL_SUPPORT when a
+  // scale is not exact in f16.
+  int scales_f16(const CodeView &p, std::vector<uint16_t> &out) {
+    const int g32 = (p.cols + 31) / 32;
+    out.assign((size_t)p.rows * g32, 0);
+    return igc_scales_f16(p.scale->data, p.scale->dtype, p.rows, p.groups, p.group_size, p.cols, out.data()) == 0
+               ? IGC_OKAY
+               : IGC_FAIL_SUPPORT;
+  }
+
+  // A quantized embedding table (`stem.embedding_quantized` and
+  // `stem.embedding_scale`) kept as stored for row lookups; `cols` the row's
+  // values.  The view is left for a tied head to upload as a plane.
+  int code_table(const std::string &stem, int cols, EmbedCodes &out, int *rows_out, CodeView &v) {
+    int c = code_view(stem, cols, v, "embedding_quantized", "embedding_scale");
+    if (c != IGC_OKAY) return c;
+    std::vector<uint16_t> sc;
+    c = scales_f16(v, sc);
+    if (c != IGC_OKAY) return c;
+    uint8_t *codes = nullptr;
+    uint16_t *scales = nullptr;
+    c = m->alloc(&codes, v.code->bytes);
+    if (c == IGC_OKAY) c = m->alloc(&scales, sc.size());
+    if (c != IGC_OKAY) return c;
+    CK(cudaMemcpy(codes, v.code->data, v.code->bytes, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(scales, sc.data(), sizeof(uint16_t) * sc.size(), cudaMemcpyHostToDevice));
+    out.codes = codes;
+    out.stride = (size_t)v.code->shape[1];
+    out.bits = v.bits;
+    out.scales = scales;
+    out.g32 = (v.cols + 31) / 32;
+    *rows_out = v.rows;
+    // app_core.c:1880 plane_row_bytes: a row's codes and scales
+    m->decode_bytes += out.stride + (size_t)v.groups * dtype_bytes(v.scale->dtype);
+    m->weight_bytes += v.code->bytes + v.scale->bytes;
     return IGC_OKAY;
   }
 
@@ -515,14 +569,17 @@ struct Binder {
       uint8_t *dc = nullptr;
       uint16_t *ds = nullptr;
       size_t cb = p.code->bytes, sb = p.scale->bytes;
+      std::vector<uint16_t> sc;
+      int c = scales_f16(p, sc);
+      if (c != IGC_OKAY) return c;
       CK(cudaMalloc(&dc, cb));
-      CK(cudaMalloc(&ds, sb));
+      CK(cudaMalloc(&ds, sizeof(uint16_t) * sc.size()));
       CK(cudaMemcpy(dc, p.code->data, cb, cudaMemcpyHostToDevice));
-      CK(cudaMemcpy(ds, p.scale->data, sb, cudaMemcpyHostToDevice));
+      CK(cudaMemcpy(ds, sc.data(), sizeof(uint16_t) * sc.size(), cudaMemcpyHostToDevice));
       int prb = (p.rows + 15) / 16;
       int mul = pair ? 2 : 1, add = pair ? (int)k : rb_at;
-      cudaError_t e = igc_launch_repack(dc, (size_t)p.code->shape[1], ds, p.groups, p.rows, p.cols, prb, n_cc, mul,
-                                        add, out.tiles, out.scales, st);
+      cudaError_t e = igc_launch_repack(dc, (size_t)p.code->shape[1], p.bits, ds, (p.cols + 31) / 32, p.rows, p.cols,
+                                        prb, n_cc, mul, add, out.tiles, out.scales, st);
       cudaError_t e2 = cudaStreamSynchronize(st);
       cudaFree(dc);
       cudaFree(ds);
@@ -533,8 +590,8 @@ struct Binder {
       m->decode_bytes += cb + sb;
       m->weight_bytes += cb + sb;
       out.bytes += (double)(cb + sb);
-      src.release(p.name + ".weight");
-      src.release(p.name + ".weight_scale");
+      src.release(p.code_name);
+      src.release(p.scale_name);
     }
     plan(out);
     out.tm_ok = igc_lane_tmaps(out.tiles, out.scales, out.n_rb, out.n_cc, &out.tm_codes, &out.tm_scales) == 0;
@@ -629,14 +686,30 @@ static int bind_model(igc_model *m, Source &src) {
   } guard{st};
   Binder b(m, src, P, st);
   int c, rows = 0;
-  c = b.table(P + "embed_tokens", 0, &m->embed, &rows);
+  // the embedding: bf16 rows, or the export's quantized table (whose view a
+  // tied head then uploads as its plane, app_core.c:8527-8538)
+  Binder::CodeView embed_view;
+  const bool embed_codes = src.find(P + "embed_tokens.embedding_quantized") != nullptr;
+  if (embed_codes)
+    c = b.code_table(P + "embed_tokens", m->hidden, m->embed_q, &rows, embed_view);
+  else
+    c = b.table(P + "embed_tokens", 0, &m->embed, &rows);
   if (c != IGC_OKAY) return c;
   m->vocab = rows;
   // the embedding table's width is the state size (app_core.c:8505)
   {
     int ple_rows = 0;
     if (m->ple_dim > 0) {
-      c = b.table(P + "embed_tokens_per_layer", m->ple_dim * m->layers, &m->ple_embed, &ple_rows);
+      if (src.find(P + "embed_tokens_per_layer.embedding_quantized")) {
+        Binder::CodeView pv;
+        c = b.code_table(P + "embed_tokens_per_layer", m->ple_dim * m->layers, m->ple_q, &ple_rows, pv);
+        if (c == IGC_OKAY) {
+          src.release(pv.code_name);
+          src.release(pv.scale_name);
+        }
+      } else {
+        c = b.table(P + "embed_tokens_per_layer", m->ple_dim * m->layers, &m->ple_embed, &ple_rows);
+      }
       if (c != IGC_OKAY) return c;
       m->ple_vocab = ple_rows;
       c = b.plane(P + "per_layer_model_projection", m->hidden, m->ple_lift);
@@ -654,6 +727,17 @@ static int bind_model(igc_model *m, Source &src) {
       if (!src.find(std::string(h) + ".weight")) continue;
       c = b.plane(h, m->hidden, m->head);
       break;
+    }
+    if (c == IGC_FAIL_MISSING && embed_codes) {
+      // no head of its own: the quantized embedding is the head (tied); its
+      // bytes were counted once, with the table
+      const size_t wb = m->weight_bytes, db = m->decode_bytes;
+      c = b.upload({embed_view}, false, m->head);
+      m->weight_bytes = wb;
+      m->decode_bytes = db + (size_t)(m->head.bytes);
+    } else if (embed_codes) {
+      src.release(embed_view.code_name);
+      src.release(embed_view.scale_name);
     }
     if (c != IGC_OKAY) return c; /* a tied head over a bf16 table is not supported */
   }
@@ -1342,7 +1426,7 @@ static int enqueue_pass(igc_session *s, int K, int want) {
   prof_mark(s, PROF_OTHER, 0.0);
   CKL(igc_launch_embed(d_ids, K, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
                        PS, (float)sqrt((double)m->ple_dim), s->x0, s->seed, s->use_stamps ? s->d_stamp : nullptr,
-                       IGC_STAMP_LIMIT, s->d_peak, s->d_peak_saved, 2 * m->layers, s->st));
+                       IGC_STAMP_LIMIT, s->d_peak, s->d_peak_saved, 2 * m->layers, &m->embed_q, &m->ple_q, s->st));
   if (m->ple_dim > 0) {
     int c = gemv(s, m->ple_lift, K, PRO_F32, EPI_STORE, s->x0, H, nullptr, nullptr, 1.0f, nullptr, nullptr,
                  s->ple_raw, PS, (float)(1.0 / sqrt((double)H)));
@@ -1654,7 +1738,8 @@ static int lane_stack(LaneRun &r, const int32_t *d_ids, Attend attend, int32_t *
   const int H = m->hidden, PS = m->layers * m->ple_dim, M = r.M;
   int c, split = 1;
   CKL(igc_launch_embed(d_ids, M, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
-                       PS, (float)sqrt((double)m->ple_dim), B.x0, B.seed, nullptr, 0, nullptr, nullptr, 0, r.st));
+                       PS, (float)sqrt((double)m->ple_dim), B.x0, B.seed, nullptr, 0, nullptr, nullptr, 0, &m->embed_q,
+                       &m->ple_q, r.st));
   if (m->ple_dim > 0) {
     LaneStageArgs sa = stage_of(LS_PLAIN, B.x0, H);
     sa.out_scale = (float)(1.0 / sqrt((double)H));

@@ -90,6 +90,8 @@ static void fill_range(const fill_job *j) {
       double q = quantile_table[value_hash(j->base, i) >> 48];
       if (j->kind == IGC_SYNTH_SCALE)
         o[i - j->origin] = f32_to_f16((float)fabs((double)sigma * q));
+      else if (j->kind == IGC_SYNTH_SCALE_BF16) /* not below f16's smallest normal, 2^-14 */
+        o[i - j->origin] = f32_to_bf16((float)fmax(fabs((double)sigma * q), 1.0 / 16384.0));
       else if (j->kind == IGC_SYNTH_NORMAL)
         o[i - j->origin] = f32_to_bf16((float)((double)sigma * q));
       else
@@ -108,7 +110,7 @@ int igc_synth_fill(uint64_t seed, uint64_t stream, int kind, float offset, size_
   fill_job jobs[64];
   pthread_t tid[64];
   int n = threads < 1 ? 1 : (threads > 64 ? 64 : threads);
-  if (!out || kind < 0 || kind > IGC_SYNTH_CONST) return IGC_FAIL_ARGUMENT;
+  if (!out || kind < 0 || kind > IGC_SYNTH_SCALE_BF16) return IGC_FAIL_ARGUMENT;
   pthread_once(&table_once, table_build);
   if (count < ((size_t)1 << 20)) n = 1;
   for (int t = 0; t < n; ++t) {
@@ -156,13 +158,29 @@ static void add(igc_synth_tensor *room, int room_count, int *n, const char *name
   *n += 1;
 }
 
-static void add_plane(igc_synth_tensor *room, int room_count, int *n, const char *stem, int64_t rows,
-                      int64_t cols) {
+/* A code plane as the export stores it (app_core.c:7886 plane_bind_gemma):
+ * `bits`-bit codes packed from the low bit in U8 rows, and a scale for every
+ * `group` columns (F16, or BF16 when `bf16`), under `leaf` / `scale_leaf`. */
+static void add_codes(igc_synth_tensor *room, int room_count, int *n, const char *stem, int64_t rows,
+                      int64_t cols, int bits, int group, int bf16, const char *leaf, const char *scale_leaf) {
   char name[128];
-  snprintf(name, sizeof(name), "%s.weight", stem);
-  add(room, room_count, n, name, 6, rows, cols / 2, 2, IGC_SYNTH_CODE, 0.0f);
-  snprintf(name, sizeof(name), "%s.weight_scale", stem);
-  add(room, room_count, n, name, 2, rows, cols / 32, 2, IGC_SYNTH_SCALE, 0.0f);
+  snprintf(name, sizeof(name), "%s.%s", stem, leaf);
+  add(room, room_count, n, name, 6, rows, (cols * bits + 7) / 8, 2, IGC_SYNTH_CODE, 0.0f);
+  snprintf(name, sizeof(name), "%s.%s", stem, scale_leaf);
+  add(room, room_count, n, name, bf16 ? 3 : 2, rows, cols / group, 2, bf16 ? IGC_SYNTH_SCALE_BF16 : IGC_SYNTH_SCALE,
+      0.0f);
+}
+
+static int spec_group(const igc_synth_spec *s) { return s->group > 0 ? s->group : 32; }
+
+static void add_plane_bits(igc_synth_tensor *room, int room_count, int *n, const igc_synth_spec *s,
+                           const char *stem, int64_t rows, int64_t cols, int bits) {
+  add_codes(room, room_count, n, stem, rows, cols, bits, spec_group(s), s->bf16_scales, "weight", "weight_scale");
+}
+
+static void add_plane(igc_synth_tensor *room, int room_count, int *n, const igc_synth_spec *s, const char *stem,
+                      int64_t rows, int64_t cols) {
+  add_plane_bits(room, room_count, n, s, stem, rows, cols, 4);
 }
 
 int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_count) {
@@ -172,17 +190,29 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
   int first_share = s->layers - s->share_count;
   int PS = s->layers * s->ple_dim;
   float no = s->norm_offset;
-  snprintf(name, sizeof(name), "%sembed_tokens.weight", P);
-  add(room, room_count, &n, name, 3, s->vocab, s->hidden, 2, IGC_SYNTH_NORMAL, 0.0f);
-  snprintf(name, sizeof(name), "%sembed_tokens_per_layer.weight", P);
-  add(room, room_count, &n, name, 3, s->vocab, PS, 2, IGC_SYNTH_NORMAL, 0.0f);
+  if (s->embed_bits > 0) { /* the export's quantized tables (app_core.c:7968) */
+    snprintf(name, sizeof(name), "%sembed_tokens", P);
+    add_codes(room, room_count, &n, name, s->vocab, s->hidden, s->embed_bits, spec_group(s), s->bf16_scales,
+              "embedding_quantized", "embedding_scale");
+  } else {
+    snprintf(name, sizeof(name), "%sembed_tokens.weight", P);
+    add(room, room_count, &n, name, 3, s->vocab, s->hidden, 2, IGC_SYNTH_NORMAL, 0.0f);
+  }
+  if (s->ple_embed_bits > 0) {
+    snprintf(name, sizeof(name), "%sembed_tokens_per_layer", P);
+    add_codes(room, room_count, &n, name, s->vocab, PS, s->ple_embed_bits, spec_group(s), s->bf16_scales,
+              "embedding_quantized", "embedding_scale");
+  } else {
+    snprintf(name, sizeof(name), "%sembed_tokens_per_layer.weight", P);
+    add(room, room_count, &n, name, 3, s->vocab, PS, 2, IGC_SYNTH_NORMAL, 0.0f);
+  }
   snprintf(name, sizeof(name), "%sper_layer_model_projection", P);
-  add_plane(room, room_count, &n, name, PS, s->hidden);
+  add_plane(room, room_count, &n, s, name, PS, s->hidden);
   snprintf(name, sizeof(name), "%sper_layer_projection_norm.weight", P);
   add(room, room_count, &n, name, 3, s->ple_dim, 0, 1, IGC_SYNTH_OFFSET, no);
   snprintf(name, sizeof(name), "%snorm.weight", P);
   add(room, room_count, &n, name, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
-  add_plane(room, room_count, &n, "lm_head", s->vocab, s->hidden);
+  if (!s->tied_head) add_plane(room, room_count, &n, s, "lm_head", s->vocab, s->hidden);
   for (int l = 0; l < s->layers; ++l) {
     char stem[128];
     int share = s->share_count > 0 && l >= first_share;
@@ -193,12 +223,12 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
     int inner = share && s->double_wide ? 2 * s->inner : s->inner;
 #define STEM(fmt) snprintf(stem, sizeof(stem), "%slayers.%d." fmt, P, l)
     STEM("self_attn.q_proj");
-    add_plane(room, room_count, &n, stem, qw, s->hidden);
+    add_plane(room, room_count, &n, s, stem, qw, s->hidden);
     if (!share) {
       STEM("self_attn.k_proj");
-      add_plane(room, room_count, &n, stem, kvw, s->hidden);
+      add_plane(room, room_count, &n, s, stem, kvw, s->hidden);
       STEM("self_attn.v_proj");
-      add_plane(room, room_count, &n, stem, kvw, s->hidden);
+      add_plane(room, room_count, &n, s, stem, kvw, s->hidden);
       STEM("self_attn.k_norm.weight");
       add(room, room_count, &n, stem, 3, hd, 0, 1, IGC_SYNTH_OFFSET, no);
       /* the export's static cache ranges (app_core.c:8596-8601), varied by layer */
@@ -212,15 +242,19 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
       }
     }
     STEM("self_attn.o_proj");
-    add_plane(room, room_count, &n, stem, s->hidden, qw);
+    add_plane(room, room_count, &n, s, stem, s->hidden, qw);
     STEM("self_attn.q_norm.weight");
     add(room, room_count, &n, stem, 3, hd, 0, 1, IGC_SYNTH_OFFSET, no);
-    STEM("mlp.gate_proj");
-    add_plane(room, room_count, &n, stem, inner, s->hidden);
-    STEM("mlp.up_proj");
-    add_plane(room, room_count, &n, stem, inner, s->hidden);
-    STEM("mlp.down_proj");
-    add_plane(room, room_count, &n, stem, s->hidden, inner);
+    {
+      /* the export codes the sharing layers' feed-forward narrower */
+      const int mb = share && s->late_mlp_bits > 0 ? s->late_mlp_bits : 4;
+      STEM("mlp.gate_proj");
+      add_plane_bits(room, room_count, &n, s, stem, inner, s->hidden, mb);
+      STEM("mlp.up_proj");
+      add_plane_bits(room, room_count, &n, s, stem, inner, s->hidden, mb);
+      STEM("mlp.down_proj");
+      add_plane_bits(room, room_count, &n, s, stem, s->hidden, inner, mb);
+    }
     STEM("input_layernorm.weight");
     add(room, room_count, &n, stem, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
     STEM("post_attention_layernorm.weight");
@@ -231,9 +265,9 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
     add(room, room_count, &n, stem, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
     if (s->ple_dim > 0) {
       STEM("per_layer_input_gate");
-      add_plane(room, room_count, &n, stem, s->ple_dim, s->hidden);
+      add_plane(room, room_count, &n, s, stem, s->ple_dim, s->hidden);
       STEM("per_layer_projection");
-      add_plane(room, room_count, &n, stem, s->hidden, s->ple_dim);
+      add_plane(room, room_count, &n, s, stem, s->hidden, s->ple_dim);
       STEM("post_per_layer_input_norm.weight");
       add(room, room_count, &n, stem, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
     }

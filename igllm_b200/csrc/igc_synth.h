@@ -26,6 +26,7 @@ extern "C" {
 #define IGC_SYNTH_NORMAL 2 /* bf16 N(0,0.02) */
 #define IGC_SYNTH_OFFSET 3 /* bf16 offset + N(0,0.02) */
 #define IGC_SYNTH_CONST 4  /* f32, every value the offset */
+#define IGC_SYNTH_SCALE_BF16 5 /* bf16 |N(0,0.02)|, raised to 2^-14 where smaller */
 
 /* One tensor of a synthetic checkpoint, in the layout the reference binds
  * (app_core.c:7886 plane_bind_gemma for U8 codes with F16 scales). */

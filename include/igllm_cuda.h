@@ -362,13 +362,20 @@ typedef struct igc_synth_spec {
   int double_wide;
   /* > 0: global layers' head width (global_head_dim); 0: head_dim */
   int global_head_dim;
+  /* the export's stored forms (0 keeps the benchmark's): the sharing layers'
+   * feed-forward codes `late_mlp_bits` wide (2 or 4); a scale every `group`
+   * columns (a multiple of 32; 0: 32), BF16 when `bf16_scales`; the embedding
+   * tables quantized to `embed_bits` / `ple_embed_bits` (2 or 4; 0: bf16
+   * rows); no lm_head when `tied_head` (the quantized embedding is the head) */
+  int late_mlp_bits, group, bf16_scales, embed_bits, ple_embed_bits, tied_head;
 } igc_synth_spec;
 
 /* Fill `out` with `count` values of stream `stream` of the spec's seed.
  * kind 0: packed int4 bytes (two uniform codes a byte, low nibble first);
  * kind 1: f16 |N(0,0.02)| bits; kind 2: bf16 N(0,0.02) bits;
  * kind 3: bf16 offset + N(0,0.02) bits (offset = norm_offset);
- * kind 4: f32, every value `offset`. */
+ * kind 4: f32, every value `offset`; kind 5: bf16 |N(0,0.02)| bits, raised
+ * to 2^-14 where smaller (scales f16 holds exactly). */
 int igc_synth_fill(uint64_t seed, uint64_t stream, int kind, float offset, size_t count, void *out,
                    int threads);
 /* Write config.json, tokenizer.json and model.safetensors for the spec under

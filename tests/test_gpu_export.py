@@ -1,13 +1,24 @@
-"""The real export's shape on the GPU, against the reference engine.
+"""The real export's shape and stored forms on the GPU, against the reference.
 
-The shipped Gemma-4-E2B export (its config.json) differs from the benchmark's
-shape in two ways this build covers: global layers with a head of 512
-(`global_head_dim`: q 8 x 512, k and v 512 on the global owner) and the
-doubled feed-forward of the layers that read another's cache
-(`use_double_wide_mlp`).  A checkpoint of that form at a size the reference
-primes in seconds: the prime (tcgen05 chunks), blocks of 1, 4 and 16 lanes,
-the 8-bit cache on the same shape, and a crowd, each against the reference's
-logits within 2e-2 (the crowd against lone rounds).
+The shipped Gemma-4-E2B export (its config.json and quantization_config)
+differs from the benchmark's checkpoint in ways this build covers:
+
+  * global layers with a head of 512 (`global_head_dim`: q 8 x 512, k and v
+    512 on the global owner) and the doubled feed-forward of the layers that
+    read another's cache (`use_double_wide_mlp`);
+  * its stored forms (app_core.c:7886 plane_bind_gemma): 2-bit codes where
+    the export codes narrower (the sharing layers' feed-forward), scales per
+    64 columns stored as BF16, the embedding tables quantized
+    (`embedding_quantized` 2-bit and 4-bit, `embedding_scale`), and no
+    lm_head: the quantized embedding is the head.
+
+Checkpoints of those forms at a size the reference primes in seconds: the
+prime (tcgen05 chunks), blocks of 1, 4 and 16 lanes, the 8-bit cache on the
+same shape, and a crowd, each against the reference's logits within 2e-2
+(the crowd against lone rounds).  Not covered here: the export's 8-bit
+planes (the per-layer input gate and projection), its unquantized
+per_layer_model_projection and its activation grids (`quant_step`); a
+checkpoint carrying them is refused (IGC_FAIL_SUPPORT).
 """
 
 import numpy as np
@@ -19,6 +30,8 @@ pytestmark = pytest.mark.gpu
 
 ATOL = 2e-2
 EXPORT = dict(CACHED, global_head_dim=512, double_wide=1, seed=29)
+STORED = dict(EXPORT, late_mlp_bits=2, group=64, bf16_scales=1, embed_bits=2, ple_embed_bits=4, tied_head=1,
+              seed=31)
 WINDOW = EXPORT["window_limit"]
 VOCAB = EXPORT["vocab"]
 
@@ -34,10 +47,18 @@ def export_dir(tmp_path_factory, igc_lib):
     return d
 
 
-@pytest.mark.parametrize("bits", [0, 8])
-def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, bits):
-    m = igc_lib.Model(folder=export_dir, window_limit=WINDOW, cache_bits=bits)
-    rm = igo_mod.RefModel(export_dir, threads=8, window_limit=WINDOW, cache_bits=bits)
+@pytest.fixture(scope="module")
+def stored_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("stored"))
+    igc_lib.synth_write(igc_lib.SynthSpec(**STORED), d, 8)
+    return d
+
+
+@pytest.mark.parametrize("form,bits", [("shape", 0), ("shape", 8), ("stored", 0)])
+def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, stored_dir, form, bits):
+    folder = export_dir if form == "shape" else stored_dir
+    m = igc_lib.Model(folder=folder, window_limit=WINDOW, cache_bits=bits)
+    rm = igo_mod.RefModel(folder, threads=8, window_limit=WINDOW, cache_bits=bits)
     assert m.memory_bytes() == rm.memory_bytes()
     s, rs = igc_lib.Session(m), igo_mod.RefSession(rm)
     ids = _ids(201, 3)
@@ -63,7 +84,7 @@ def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, bits):
         s.guess_keep(k)
         assert rs.keep(k) == 0
         tok = int(want[-1].argmax())
-    print(f"export shape, cache bits {bits}: worst |logit diff| vs the reference {worst:.3e}")
+    print(f"export {form}, cache bits {bits}: worst |logit diff| vs the reference {worst:.3e}")
     assert worst < ATOL
     s.close()
     rs.close()
