@@ -69,7 +69,9 @@ class SynthSpec(ctypes.Structure):
                 ("cache_scale_k", ctypes.c_float), ("cache_scale_v", ctypes.c_float),
                 ("double_wide", ctypes.c_int), ("global_head_dim", ctypes.c_int),
                 ("late_mlp_bits", ctypes.c_int), ("group", ctypes.c_int), ("bf16_scales", ctypes.c_int),
-                ("embed_bits", ctypes.c_int), ("ple_embed_bits", ctypes.c_int), ("tied_head", ctypes.c_int)]
+                ("embed_bits", ctypes.c_int), ("ple_embed_bits", ctypes.c_int), ("tied_head", ctypes.c_int),
+                ("ple_bits8", ctypes.c_int), ("dense_ple_lift", ctypes.c_int), ("grid_in", ctypes.c_float),
+                ("grid_out", ctypes.c_float)]
 
 
 def spec_e2b(norm_offset=0.0, seed=1, window_limit=32768):
@@ -604,7 +606,7 @@ class SynthTensor(ctypes.Structure):
                 ("bytes", ctypes.c_size_t)]
 
 
-_DTYPE_NAME = {1: "F32", 2: "F16", 3: "BF16", 6: "U8"}
+_DTYPE_NAME = {1: "F32", 2: "F16", 3: "BF16", 5: "I8", 6: "U8"}
 
 
 def synth_tensors(spec, threads=8):
@@ -621,7 +623,7 @@ def synth_tensors(spec, threads=8):
     out = {}
     for t in room:
         shape = [t.shape[0], t.shape[1]] if t.rank == 2 else [t.shape[0]]
-        arr = np.empty(shape, {6: np.uint8, 1: np.float32}.get(t.dtype, np.uint16))
+        arr = np.empty(shape, {6: np.uint8, 5: np.int8, 1: np.float32}.get(t.dtype, np.uint16))
         _check(lib.igc_synth_tensor_fill(ctypes.byref(spec), ctypes.byref(t), arr.ctypes.data_as(ctypes.c_void_p),
                                          threads), "synth_tensor_fill")
         out[t.name.decode()] = (_DTYPE_NAME[t.dtype], arr)

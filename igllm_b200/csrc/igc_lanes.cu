@@ -480,6 +480,9 @@ __global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
     for (int i = tid; i < n; i += nt) y[i] = y[i] * sh * a.w_in[i];
   }
   __syncthreads();
+  if (a.row_out)
+    for (int i = tid; i < n; i += nt) a.row_out[(size_t)j * a.row_stride + i] = y[i];
+  if (!a.a_tiles) return;
   float mx = 0.0f;
   for (int i = tid; i < n; i += nt) mx = fmaxf(mx, fabsf(y[i]));
   const float sc = lane_scale(block_max(mx, red));
@@ -653,6 +656,105 @@ __global__ void __launch_bounds__(256) lane_widen_kernel(WidenArgs w) {
   }
 }
 
+// app_core.c:1930 quant_step: a value onto the signed 8-bit grid of `step`,
+// rounding ties to even
+__device__ __forceinline__ float grid_step(float v, float step) {
+  const float level = fminf(fmaxf(rintf(__fdiv_rn(v, step)), -128.0f), 127.0f);
+  return level * step;
+}
+
+__device__ __forceinline__ float plain_weight(const PlainArgs &a, int r, int c) {
+  if (a.codes) {
+    const size_t bit = (size_t)c * a.bits;
+    const uint8_t *row = a.codes + (size_t)r * a.stride;
+    uint32_t w = row[bit >> 3] >> (bit & 7);
+    if ((int)(bit & 7) + a.bits > 8) w |= (uint32_t)row[(bit >> 3) + 1] << (8 - (bit & 7));
+    const int code = (int)((w & ((1u << a.bits) - 1u)) ^ a.flip);
+    return (float)(code - a.bias) * a.scales[(size_t)r * a.groups + c / a.group_size];
+  }
+  const size_t i = (size_t)r * a.cols + c;
+  if (a.dense_type == 1) return reinterpret_cast<const float *>(a.dense)[i];
+  const uint16_t h = reinterpret_cast<const uint16_t *>(a.dense)[i];
+  return a.dense_type == 2 ? __half2float(__ushort_as_half(h)) : __uint_as_float((uint32_t)h << 16);
+}
+
+// A warp a row at a time (the block's rows r0 + warp, + 8, ...), 16 lanes at
+// a time: thread t the columns t, t + 32, ..., then each lane's sum by one
+// fixed shuffle tree.  The head keeps, per lane, the largest of the block's
+// values (first row on a tie, app_main.c:482).
+constexpr int PL_ROWS = 128, PL_LANES = 16;
+__global__ void __launch_bounds__(256) plain_product_kernel(PlainArgs a) {
+  __shared__ float best_v[8][PL_LANES];
+  __shared__ int best_i[8][PL_LANES];
+  pdl_release();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
+  const int r0 = blockIdx.x * PL_ROWS, r1 = min(r0 + PL_ROWS, a.rows);
+  for (int g0 = 0; g0 < a.lanes; g0 += PL_LANES) {
+    const int gl = min(PL_LANES, a.lanes - g0);
+    float keep_v[PL_LANES];
+    int keep_i[PL_LANES];
+#pragma unroll
+    for (int j = 0; j < PL_LANES; ++j) {
+      keep_v[j] = -FLT_MAX;
+      keep_i[j] = 0x7fffffff;
+    }
+    for (int r = r0 + warp; r < r1; r += 8) {
+      float acc[PL_LANES];
+#pragma unroll
+      for (int j = 0; j < PL_LANES; ++j) acc[j] = 0.0f;
+      for (int c = l; c < a.cols; c += 32) {
+        const float w = plain_weight(a, r, c);
+#pragma unroll
+        for (int j = 0; j < PL_LANES; ++j)
+          if (j < gl) {
+            float x = a.x[(size_t)(g0 + j) * a.x_stride + c];
+            if (a.enter > 0.0f) x = grid_step(x, a.enter);
+            acc[j] = fmaf(w, x, acc[j]);
+          }
+      }
+#pragma unroll
+      for (int j = 0; j < PL_LANES; ++j) {
+        float v = warp_sum(acc[j]);
+        if (j >= gl) continue;
+        if (a.leave > 0.0f) v = grid_step(v, a.leave);
+        v *= a.out_scale;
+        if (a.cap > 0.0f) v = logit_cap(v, a.cap);
+        if (l == 0 && a.out) {
+          const int orow = a.pair_half >= 0 ? (r >> 4) * 32 + a.pair_half * 16 + (r & 15) : a.out_row0 + r;
+          a.out[(size_t)(g0 + j) * a.out_stride + orow] = v;
+        }
+        if (v > keep_v[j]) {  // rows rise, so the first row wins a tie
+          keep_v[j] = v;
+          keep_i[j] = r;
+        }
+      }
+    }
+    if (a.arg_val) {
+      if (l == 0)
+#pragma unroll
+        for (int j = 0; j < PL_LANES; ++j) {
+          best_v[warp][j] = keep_v[j];
+          best_i[warp][j] = keep_i[j];
+        }
+      __syncthreads();
+      if (threadIdx.x < gl) {
+        const int j = threadIdx.x;
+        float v = best_v[0][j];
+        int i = best_i[0][j];
+        for (int w = 1; w < 8; ++w)
+          if (best_v[w][j] > v || (best_v[w][j] == v && best_i[w][j] < i)) {
+            v = best_v[w][j];
+            i = best_i[w][j];
+          }
+        a.arg_val[(size_t)blockIdx.x * a.lanes + g0 + j] = v;
+        a.arg_idx[(size_t)blockIdx.x * a.lanes + g0 + j] = i;
+      }
+      __syncthreads();
+    }
+  }
+}
+
 // K-slice partials added in order: out[j][i] = sum_z p[z][j][i].
 __global__ void lane_sum_kernel(const float *p, int splits, int lanes, int cols, int p_stride, float *out,
                                 int out_stride) {
@@ -704,7 +806,8 @@ cudaError_t igc_lanes_configure(void) {
 }
 
 cudaError_t igc_launch_lane_stage(const LaneStageArgs *a, cudaStream_t st) {
-  if (a->lanes < 1 || a->cols < 1 || a->cols > a->n_cc * 64) return cudaErrorInvalidValue;
+  if (a->lanes < 1 || a->cols < 1) return cudaErrorInvalidValue;
+  if (a->a_tiles ? a->cols > a->n_cc * 64 : (!a->row_out || a->row_stride < a->cols)) return cudaErrorInvalidValue;
   const size_t smem = igc_lane_stage_smem(a->mode, a->cols);
   if (smem > LS_SMEM_LIMIT) return cudaErrorInvalidValue;
   return lane_launch(lane_stage_kernel, dim3(a->lanes), dim3(256), smem, st, *a);
@@ -802,6 +905,18 @@ cudaError_t igc_launch_lane_kv_many(const float *qkv, int qkv_stride, int heads,
   KvTables tab = {pos_tab, kc_tab, vc_tab, peak_tab, per};
   return lane_launch(lane_kv_kernel, dim3(lanes), dim3(256), 0, st, qkv, qkv_stride, heads, kv_heads, hd, k_norm, cs,
                      sn, eps, p0, kc, vc, cq, tab);
+}
+
+cudaError_t igc_launch_plain_product(const PlainArgs *a, int sm_count, int *blocks_out, cudaStream_t st) {
+  (void)sm_count;
+  if (!a || a->rows < 1 || a->cols < 1 || a->lanes < 1 || !a->x) return cudaErrorInvalidValue;
+  if (a->codes ? (a->bits < 1 || a->bits > 8 || !a->scales || a->groups < 1 || a->group_size < 1)
+               : (!a->dense || a->dense_type < 1 || a->dense_type > 3))
+    return cudaErrorInvalidValue;
+  if (a->arg_val && !a->arg_idx) return cudaErrorInvalidValue;
+  const int blocks = (a->rows + PL_ROWS - 1) / PL_ROWS;
+  if (blocks_out) *blocks_out = blocks;
+  return lane_launch(plain_product_kernel, dim3(blocks), dim3(256), 0, st, *a);
 }
 
 cudaError_t igc_launch_lane_widen(const WidenArgs *w, int batch, int rows_most, int sm_count, cudaStream_t st) {

@@ -37,9 +37,39 @@ struct LaneStageArgs {
   const float *aux;       // GELU_MUL: [lanes][aux_stride]
   int aux_stride;
   float out_scale;        // folded into the lane's factor
-  void *a_tiles;          // out: [lane tile][n_cc][hi, lo][16 KB] f16 operand blocks
+  void *a_tiles;          // out: [lane tile][n_cc][hi, lo][16 KB] f16 operand blocks (null: none)
   int n_cc;               // 64-column steps of the next product
   float *factor;          // out: [lanes] the factor undoing the staging scale (times out_scale)
+  float *row_out;         // out (nullable): [lanes][row_stride] the staged rows as f32, unscaled
+  int row_stride;
+};
+
+// One product of a plane the tiles do not hold, on the CUDA cores
+// (igc_launch_plain_product): offset codes of 1-8 bits packed from the low bit
+// (app_core.c:1757 pack_read), a value being (code ^ flip) - bias times the
+// f32 scale of its group, or a dense float plane; the input taken through its
+// activation grid and the output put through its own (app_core.c:1930
+// quant_step, :7814 plane_lift_many).
+struct PlainArgs {
+  const uint8_t *codes;   // [rows][stride] (null: dense)
+  size_t stride;
+  int bits;
+  uint32_t flip;
+  int bias;
+  const float *scales;    // [rows][groups]
+  int groups, group_size;
+  const void *dense;      // [rows][cols] of dense_type: 1 F32, 2 F16, 3 BF16
+  int dense_type;
+  int rows, cols;
+  float enter, leave;     // grid steps of the input and the output (0: none)
+  const float *x;         // [lanes][x_stride] the staged input rows
+  int x_stride, lanes;
+  float *out;             // [lanes][out_stride] at row out_row0 + r, or for pair_half >= 0 the
+  int out_stride, out_row0, pair_half;  // 16-row blocks of a gate|up pair (gate 0, up 1)
+  float out_scale;        // applied after the output grid
+  float cap;              // > 0: the head's soft cap, then argmax partials
+  float *arg_val;         // [block][lanes] the largest value of each block's rows, and its row
+  int *arg_idx;
 };
 
 struct LaneGemmArgs {
@@ -110,6 +140,10 @@ cudaError_t igc_launch_lane_kv_many(const float *qkv, int qkv_stride, int heads,
 // a global one).  `rows_most` bounds the rows any launch of this shape sees
 // (it sizes the grid); kv_w, a row's values, is a multiple of 16.
 cudaError_t igc_launch_lane_widen(const igc::WidenArgs *w, int batch, int rows_most, int sm_count, cudaStream_t st);
+// A plain plane's product for `lanes` lanes; with the head's cap, one block
+// of 8 warps a 128 rows (so `ceil(rows / 128)` argmax partials).  Returns the
+// blocks launched in *blocks_out when it is not null.
+cudaError_t igc_launch_plain_product(const igc::PlainArgs *a, int sm_count, int *blocks_out, cudaStream_t st);
 // out[i] = *p0 + 16 i for i < groups (a prefill chunk's attention groups).
 cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st);
 // Per lane the largest of `parts` argmax partials [part][lanes] (first index

@@ -285,8 +285,15 @@ struct DevPlane {
   int split = 1, grid = 1;
   bool pair = false;
   double bytes = 0.0;  // codes and scales a product streams (app_core.c:1860 plane_bytes)
+  // a plane of a model the tiles do not hold (8-bit codes, dense planes,
+  // activation grids): its parts as stored, one product each on the CUDA
+  // cores (igc_launch_plain_product), writing the rows the tiles would
+  std::vector<PlainArgs> plain;
   GemvPlane view() const { return GemvPlane{tiles, scales, n_rb, n_cc, rows, cols}; }
 };
+
+// Bind-time verdict that a model needs the plain planes (igc_model::plain).
+constexpr int IGC_NEED_PLAIN = -100;
 
 struct DevLayer {
   int kind = 0, share = 0, source = -1, hd = 0, kv_heads = 1, inner = 0;
@@ -325,6 +332,11 @@ struct igc_model {
   // bytes of every checkpoint tensor the text stack binds (app_core.c:12667
   // model_memory_bytes, the reference's model->weight_bytes)
   size_t weight_bytes = 0;
+  // every projection as stored, on the CUDA cores, and every pass through the
+  // lane stages (explicit norms, grids): set when a plane has 8-bit codes, is
+  // dense, has scales f16 cannot hold, or carries activation grids
+  bool plain = false;
+  int plain_cols = 0;  // the widest input row a plain product reads
   // app_setup.cache_bits: 8 stores a cache side as e4m3 bytes wherever the
   // export ships that side's scale (app_core.c:14270-14284)
   int cache_bits = 0;
@@ -466,8 +478,10 @@ struct Binder {
   // codes (an I8 tensor, or U8 a byte a code) are refused: the tiles hold
   // 4-bit values.
   struct CodeView {
-    const Tensor *code = nullptr, *scale = nullptr;
+    const Tensor *code = nullptr, *scale = nullptr, *dense = nullptr;
     int rows = 0, cols = 0, groups = 0, bits = 4, group_size = 32;
+    bool signed_codes = false;  // I8: app_core.c:7935 code_flip
+    float enter = 0.0f, leave = 0.0f;  // the plane's activation grids (app_core.c:7941-7948)
     std::string name, code_name, scale_name;
   };
   int code_view(const std::string &stem, int col_hint, CodeView &v, const char *leaf = "weight",
@@ -478,20 +492,40 @@ struct Binder {
     v.code = src.find(v.code_name);
     if (!v.code) return IGC_FAIL_MISSING;
     v.scale = src.find(v.scale_name);
+    // the grids are read, not counted (app_core.c:7941-7948)
+    if (const Tensor *g = src.find(stem + ".input_activation_scale")) v.enter = real_at(*g, 0);
+    if (const Tensor *g = src.find(stem + ".output_activation_scale")) v.leave = real_at(*g, 0);
+    if (!(v.enter > 0.0f)) v.enter = 0.0f;
+    if (!(v.leave > 0.0f)) v.leave = 0.0f;
+    if (!v.scale && (v.code->dtype == T_F32 || v.code->dtype == T_F16 || v.code->dtype == T_BF16)) {
+      // a dense plane (app_core.c:7980-7998)
+      if (v.code->rank != 2 || (col_hint > 0 && v.code->shape[1] != col_hint)) return IGC_FAIL_FORMAT;
+      if (!m->plain) return IGC_NEED_PLAIN;
+      v.dense = v.code;
+      v.code = nullptr;
+      v.rows = (int)v.dense->shape[0];
+      v.cols = (int)v.dense->shape[1];
+      v.code_name = stem + "." + leaf;
+      return IGC_OKAY;
+    }
     if (!v.scale || (v.code->dtype != T_U8 && v.code->dtype != T_I8)) return IGC_FAIL_SUPPORT;
     if (v.code->rank != 2) return IGC_FAIL_FORMAT;
-    if (v.code->dtype == T_I8) return IGC_FAIL_SUPPORT;
     int rows = (int)v.code->shape[0], bytes = (int)v.code->shape[1];
     int cols = col_hint;
     int bits = 0;
-    const int widths[] = {8, 4, 2, 1};
-    for (int w : widths)
-      if (((int64_t)cols * w + 7) / 8 == bytes) { bits = w; break; }
-    if (bits == 0) return IGC_FAIL_FORMAT;
-    if (bits == 8) return IGC_FAIL_SUPPORT;
+    if (v.code->dtype == T_I8) {
+      bits = 8;
+      v.signed_codes = true;
+      if (cols > 0 && bytes != cols) return IGC_FAIL_FORMAT;
+      cols = bytes;
+    } else {
+      const int widths[] = {8, 4, 2, 1};
+      for (int w : widths)
+        if (((int64_t)cols * w + 7) / 8 == bytes) { bits = w; break; }
+      if (bits == 0) return IGC_FAIL_FORMAT;
+    }
     int groups = v.scale->rank >= 2 ? (int)v.scale->shape[v.scale->rank - 1] : 1;
     if (groups < 1 || cols % groups) return IGC_FAIL_FORMAT;
-    if ((cols / groups) % 32) return IGC_FAIL_SUPPORT;
     if (v.scale->dtype != T_F16 && v.scale->dtype != T_BF16 && v.scale->dtype != T_F32) return IGC_FAIL_SUPPORT;
     if ((int)v.scale->shape[0] != rows) return IGC_FAIL_FORMAT;
     v.rows = rows;
@@ -499,6 +533,12 @@ struct Binder {
     v.groups = groups;
     v.bits = bits;
     v.group_size = cols / groups;
+    if (!m->plain) {
+      // what the 4-bit tiles cannot hold sends the model to the plain planes
+      if (bits == 8 || v.group_size % 32 || v.enter > 0.0f || v.leave > 0.0f) return IGC_NEED_PLAIN;
+      std::vector<uint16_t> sc;
+      if (scales_f16(v, sc) != IGC_OKAY) return IGC_NEED_PLAIN;
+    }
     return IGC_OKAY;
   }
 
@@ -518,6 +558,8 @@ struct Binder {
   int code_table(const std::string &stem, int cols, EmbedCodes &out, int *rows_out, CodeView &v) {
     int c = code_view(stem, cols, v, "embedding_quantized", "embedding_scale");
     if (c != IGC_OKAY) return c;
+    // the row reads take 1, 2 or 4-bit codes with f16 scales per 32 columns
+    if (v.bits == 8 || v.group_size % 32) return IGC_FAIL_SUPPORT;
     std::vector<uint16_t> sc;
     c = scales_f16(v, sc);
     if (c != IGC_OKAY) return c;
@@ -543,6 +585,63 @@ struct Binder {
   // Uploads one or more code planes of the same width into one tile array:
   // `parts` are stacked by row block (q|k|v) or, for a pair, interleaved
   // block by block (gate, up).
+  // A plane's parts as stored for the plain products: codes, their scales as
+  // f32, or the dense values; each part's rows at its place in the plane's
+  // output (stacked, or a gate|up pair's interleaved 16-row blocks).
+  int upload_plain(std::vector<CodeView> &parts, bool pair, DevPlane &out) {
+    int rb_at = 0;
+    for (size_t k = 0; k < parts.size(); ++k) {
+      CodeView &p = parts[k];
+      PlainArgs a;
+      memset(&a, 0, sizeof(a));
+      a.rows = p.rows;
+      a.cols = p.cols;
+      a.enter = p.enter;
+      a.leave = p.leave;
+      a.out_row0 = pair ? 0 : rb_at * 16;
+      a.pair_half = pair ? (int)k : -1;
+      size_t counted = 0;
+      if (p.dense) {
+        void *d = nullptr;
+        int c = m->alloc(reinterpret_cast<uint8_t **>(&d), p.dense->bytes);
+        if (c != IGC_OKAY) return c;
+        CK(cudaMemcpy(d, p.dense->data, p.dense->bytes, cudaMemcpyHostToDevice));
+        a.dense = d;
+        a.dense_type = p.dense->dtype;  // the reference's store types: 1 F32, 2 F16, 3 BF16
+        counted = p.dense->bytes;
+        src.release(p.code_name);
+      } else {
+        std::vector<float> sc((size_t)p.rows * p.groups);
+        for (size_t i = 0; i < sc.size(); ++i) sc[i] = real_at(*p.scale, i);
+        uint8_t *codes = nullptr;
+        float *scales = nullptr;
+        int c = m->alloc(&codes, p.code->bytes);
+        if (c == IGC_OKAY) c = m->alloc(&scales, sc.size());
+        if (c != IGC_OKAY) return c;
+        CK(cudaMemcpy(codes, p.code->data, p.code->bytes, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(scales, sc.data(), sizeof(float) * sc.size(), cudaMemcpyHostToDevice));
+        a.codes = codes;
+        a.stride = (size_t)p.code->shape[1];
+        a.bits = p.bits;
+        a.bias = 1 << (p.bits - 1);
+        a.flip = p.signed_codes ? (uint32_t)a.bias : 0u;
+        a.scales = scales;
+        a.groups = p.groups;
+        a.group_size = p.group_size;
+        counted = p.code->bytes + p.scale->bytes;
+        src.release(p.code_name);
+        src.release(p.scale_name);
+      }
+      m->decode_bytes += counted;  // app_core.c:1860 plane_bytes
+      m->weight_bytes += counted;
+      out.bytes += (double)counted;
+      if (p.cols > m->plain_cols) m->plain_cols = p.cols;
+      out.plain.push_back(a);
+      rb_at += (p.rows + 15) / 16;
+    }
+    return IGC_OKAY;
+  }
+
   int upload(std::vector<CodeView> parts, bool pair, DevPlane &out) {
     int cols = parts[0].cols;
     int n_cc = (cols + 63) / 64;
@@ -559,6 +658,7 @@ struct Binder {
     out.rows = pair ? parts[0].rows : n_rb * 16;
     if (!pair && parts.size() == 1) out.rows = parts[0].rows;
     out.pair = pair;
+    if (m->plain) return upload_plain(parts, pair, out);
     int c = m->alloc(&out.tiles, (size_t)n_rb * n_cc * 32);
     if (c != IGC_OKAY) return c;
     c = m->alloc(&out.scales, (size_t)n_rb * n_cc * 8);
@@ -867,18 +967,25 @@ extern "C" int igc_model_load(const char *folder, const igc_setup *setup, igc_mo
   *model_out = nullptr;
   std::string text;
   if (!slurp(std::string(folder) + "/config.json", text)) return IGC_FAIL_MISSING;
-  auto m = std::make_unique<igc_model>();
-  int c = model_prepare(m.get(), setup);
-  if (c != IGC_OKAY) return c;
-  c = read_config(m.get(), text, setup);
-  if (c != IGC_OKAY) return c;
   SafeSource src;
-  c = src.open(folder);
+  int c = src.open(folder);
   if (c != IGC_OKAY) return c;
-  c = bind_model(m.get(), src);
-  if (c != IGC_OKAY) return c;
-  *model_out = m.release();
-  return IGC_OKAY;
+  // the tiles first; a plane they cannot hold binds the whole model again
+  // as plain planes
+  for (int plain = 0; plain < 2; ++plain) {
+    auto m = std::make_unique<igc_model>();
+    m->plain = plain != 0;
+    c = model_prepare(m.get(), setup);
+    if (c != IGC_OKAY) return c;
+    c = read_config(m.get(), text, setup);
+    if (c != IGC_OKAY) return c;
+    c = bind_model(m.get(), src);
+    if (c == IGC_NEED_PLAIN && !plain) continue;
+    if (c != IGC_OKAY) return c == IGC_NEED_PLAIN ? IGC_FAIL_SUPPORT : c;
+    *model_out = m.release();
+    return IGC_OKAY;
+  }
+  return IGC_FAIL_SUPPORT;
 }
 
 extern "C" int igc_model_synth(const igc_synth_spec *spec, const igc_setup *setup, igc_model **model_out) {
@@ -888,16 +995,21 @@ extern "C" int igc_model_synth(const igc_synth_spec *spec, const igc_setup *setu
   if (!text) return IGC_FAIL_MEMORY;
   std::string t(text);
   free(text);
-  auto m = std::make_unique<igc_model>();
-  int c = model_prepare(m.get(), setup);
-  if (c != IGC_OKAY) return c;
-  c = read_config(m.get(), t, setup);
-  if (c != IGC_OKAY) return c;
   SynthSource src(*spec);
-  c = bind_model(m.get(), src);
-  if (c != IGC_OKAY) return c;
-  *model_out = m.release();
-  return IGC_OKAY;
+  for (int plain = 0; plain < 2; ++plain) {
+    auto m = std::make_unique<igc_model>();
+    m->plain = plain != 0;
+    int c = model_prepare(m.get(), setup);
+    if (c != IGC_OKAY) return c;
+    c = read_config(m.get(), t, setup);
+    if (c != IGC_OKAY) return c;
+    c = bind_model(m.get(), src);
+    if (c == IGC_NEED_PLAIN && !plain) continue;
+    if (c != IGC_OKAY) return c == IGC_NEED_PLAIN ? IGC_FAIL_SUPPORT : c;
+    *model_out = m.release();
+    return IGC_OKAY;
+  }
+  return IGC_FAIL_SUPPORT;
 }
 
 extern "C" void igc_model_free(igc_model *model) { delete model; }
@@ -911,7 +1023,9 @@ extern "C" size_t igc_model_device_bytes(const igc_model *m) { return m ? m->dev
 // columns, both halves of a gate|up pair): half the FLOPs of a lane.
 extern "C" size_t igc_model_weight_count(const igc_model *m) {
   if (!m) return 0;
-  auto n = [](const DevPlane &p) -> size_t { return p.tiles ? (size_t)p.rows * p.cols * (p.pair ? 2 : 1) : 0; };
+  auto n = [](const DevPlane &p) -> size_t {
+    return p.tiles || !p.plain.empty() ? (size_t)p.rows * p.cols * (p.pair ? 2 : 1) : 0;
+  };
   size_t t = n(m->ple_lift) + n(m->head);
   for (auto &L : m->layer) t += n(L.qkv) + n(L.o) + n(L.gateup) + n(L.down) + n(L.ple_gate) + n(L.ple_proj);
   return t;
@@ -929,6 +1043,7 @@ struct LaneBuf {
   int cap = 0, split_lanes = 0;
   float *x0 = nullptr, *xa = nullptr, *xb = nullptr, *seed = nullptr, *ple_raw = nullptr, *ple = nullptr;
   float *qkv = nullptr, *attn = nullptr, *part = nullptr, *factor = nullptr;
+  float *rows = nullptr;  // a plain model's staged input rows, [cap][model plain_cols]
   float *arg_val = nullptr;
   int *arg_idx = nullptr;
   void *a_tiles = nullptr;
@@ -1545,12 +1660,17 @@ static int enqueue_pass(igc_session *s, int K, int want) {
 
 // Runs one pass: ids and position in, argmax ids out (when want), with a
 // captured graph per (K, want) after the first pass of that shape.
+static int run_chunk(igc_session *s, const int32_t *ids, int M, bool head, bool want);
+
 static int run_pass(igc_session *s, const int32_t *ids, int K, int want) {
   igc_model *m = s->m;
   if (K < 1 || K > IGC_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
   if (s->fill + K > m->window_limit) return IGC_FAIL_STATE;
   for (int j = 0; j < K; ++j)
     if (ids[j] < 0 || ids[j] >= m->vocab) return IGC_FAIL_ARGUMENT;
+  // a plain model's passes run through the lane stages (explicit norms and
+  // grids) and its planes' CUDA-core products, the head included
+  if (m->plain) return run_chunk(s, ids, K, true, want != 0);
   clear_stale("pass");
   CK(cudaSetDevice(m->device));
   s->h_io[0] = s->fill;
@@ -1619,8 +1739,10 @@ static int lane_buf_alloc(igc_model *m, LaneBuf &B, int cap, int split_lanes, st
   size_t part = 0;
   int max_cc = 1;
   auto see = [&](const DevPlane &pl) {
-    if (!pl.tiles) return;
-    if (split_lanes > 0)
+    if (!pl.tiles && pl.plain.empty()) return;
+    if (m->plain)
+      part = std::max(part, (size_t)cap * pl.n_rb * 16);  // one slice: the products write whole sums
+    else if (split_lanes > 0)
       part = std::max(part, (size_t)igc_lane_gemm_split(split_lanes, pl.n_rb, pl.n_cc, m->sm_count) * cap * pl.n_rb * 16);
     else
       for (int lanes = 1; lanes <= cap; ++lanes)
@@ -1656,6 +1778,7 @@ static int lane_buf_alloc(igc_model *m, LaneBuf &B, int cap, int split_lanes, st
   if (c == IGC_OKAY) c = grab(&B.attn, (size_t)cap * m->max_q);
   if (c == IGC_OKAY) c = grab(&B.part, part);
   if (c == IGC_OKAY) c = grab(&B.factor, (size_t)cap);
+  if (c == IGC_OKAY && m->plain) c = grab(&B.rows, (size_t)cap * std::max(m->plain_cols, H));
   if (c == IGC_OKAY) c = grab((uint8_t **)&B.a_tiles, (size_t)((cap + LG_M - 1) / LG_M) * max_cc * LG_A_STEP_BYTES);
   const size_t head_tiles = (size_t)(m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16);
   if (c == IGC_OKAY) c = grab(&B.arg_val, head_tiles * cap);
@@ -1673,6 +1796,9 @@ struct LaneRun {
   LaneBuf *B;
   int *d_err;
   int M;  // lanes
+  // a session's cache peaks, copied by the embedding kernel before a block
+  // that may be undone (a plain model's steps and blocks)
+  float *peak = nullptr, *peak_saved = nullptr;
 };
 
 static LaneStageArgs stage_of(int mode, const float *x, int x_stride) {
@@ -1690,8 +1816,44 @@ static LaneStageArgs stage_of(int mode, const float *x, int x_stride) {
 // and steps), then the product: K-slice partials into B.part, or with `head`
 // set the output head's argmax partials (and logits into `logits` when given).
 static int lane_product(LaneRun &r, const DevPlane &pl, LaneStageArgs sa, int *split_out, bool head = false,
-                        float *logits = nullptr) {
+                        float *logits = nullptr, int *head_parts = nullptr) {
   LaneBuf &B = *r.B;
+  if (!pl.plain.empty()) {
+    // a plain plane: the staged rows as f32, then one CUDA-core product a
+    // part, each writing whole sums into its rows of the plane's output
+    const int stride = std::max(r.m->plain_cols, r.m->hidden);
+    sa.lanes = r.M;
+    sa.cols = pl.cols;
+    sa.n_cc = 0;
+    sa.a_tiles = nullptr;
+    sa.factor = B.factor;
+    sa.eps = r.m->eps;
+    sa.row_out = B.rows;
+    sa.row_stride = stride;
+    CKL(igc_launch_lane_stage(&sa, r.st));
+    for (const PlainArgs &part : pl.plain) {
+      PlainArgs a = part;
+      a.x = B.rows;
+      a.x_stride = stride;
+      a.lanes = r.M;
+      a.out_scale = sa.out_scale;
+      if (head) {
+        a.out = logits;
+        a.out_stride = pl.rows;
+        a.cap = r.m->softcap;
+        a.arg_val = B.arg_val;
+        a.arg_idx = B.arg_idx;
+      } else {
+        a.out = B.part;
+        a.out_stride = pl.n_rb * 16;
+      }
+      int blocks = 0;
+      CKL(igc_launch_plain_product(&a, r.m->sm_count, &blocks, r.st));
+      if (head_parts) *head_parts = blocks;
+    }
+    *split_out = 1;
+    return IGC_OKAY;
+  }
   sa.lanes = r.M;
   sa.cols = pl.cols;
   sa.n_cc = pl.n_cc;
@@ -1738,8 +1900,8 @@ static int lane_stack(LaneRun &r, const int32_t *d_ids, Attend attend, int32_t *
   const int H = m->hidden, PS = m->layers * m->ple_dim, M = r.M;
   int c, split = 1;
   CKL(igc_launch_embed(d_ids, M, m->embed, H, (float)sqrt((double)H), m->ple_embed, m->ple_vocab ? m->ple_vocab : 1,
-                       PS, (float)sqrt((double)m->ple_dim), B.x0, B.seed, nullptr, 0, nullptr, nullptr, 0, &m->embed_q,
-                       &m->ple_q, r.st));
+                       PS, (float)sqrt((double)m->ple_dim), B.x0, B.seed, nullptr, 0, r.peak, r.peak_saved,
+                       r.peak_saved ? 2 * m->layers : 0, &m->embed_q, &m->ple_q, r.st));
   if (m->ple_dim > 0) {
     LaneStageArgs sa = stage_of(LS_PLAIN, B.x0, H);
     sa.out_scale = (float)(1.0 / sqrt((double)H));
@@ -1834,9 +1996,10 @@ static int lane_stack(LaneRun &r, const int32_t *d_ids, Attend attend, int32_t *
     LaneStageArgs sa = stage_of(pend ? LS_RESID_NORM : LS_NORM, cur, H);
     sa.w_in = m->final_norm;
     if (pend) resid(sa);
-    c = lane_product(r, m->head, sa, &split, true, logits);
+    int parts = (m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16);
+    c = lane_product(r, m->head, sa, &split, true, logits, &parts);
     if (c != IGC_OKAY) return c;
-    CKL(igc_launch_lane_argmax(B.arg_val, B.arg_idx, (m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16), M, top, r.st));
+    CKL(igc_launch_lane_argmax(B.arg_val, B.arg_idx, parts, M, top, r.st));
   }
   return IGC_OKAY;
 }
@@ -1869,7 +2032,7 @@ static int chunks_ready(igc_session *s) {
 
 // One chunk of M lanes at the position in ch.d_ids[0], ids in ch.d_ids[1..M]
 // (app_core.c:11843 session_pass without the head: a prime keeps no logits).
-static int enqueue_chunk(igc_session *s, int M) {
+static int enqueue_chunk(igc_session *s, int M, bool head, bool want) {
   igc_model *m = s->m;
   auto &C = s->ch;
   // kernels overlap the one ahead (each waits before reading its results),
@@ -1914,12 +2077,19 @@ static int enqueue_chunk(igc_session *s, int M) {
     igc_kernels_pdl(s->use_pdl != 0);
     return IGC_OKAY;
   };
+  if (head) {
+    r.peak = s->d_peak;
+    r.peak_saved = s->d_peak_saved;
+    return lane_stack(r, C.d_ids + 1, attend, s->d_top, want ? s->logits : nullptr);
+  }
   return lane_stack(r, C.d_ids + 1, attend);
 }
 
-// One chunk of M lanes (64 <= M <= chunk_lanes()), kept, with a captured
-// graph per chunk length.
-static int run_chunk(igc_session *s, const int32_t *ids, int M) {
+// One chunk of M lanes (64 <= M <= chunk_lanes(); any M for a plain model),
+// kept, with a captured graph per chunk shape.  With `head` (a plain model's
+// step or block, M <= 16) it ends in each lane's argmax, and with `want` the
+// lanes' logits too.
+static int run_chunk(igc_session *s, const int32_t *ids, int M, bool head = false, bool want = false) {
   igc_model *m = s->m;
   auto &C = s->ch;
   int c = chunks_ready(s);
@@ -1929,13 +2099,14 @@ static int run_chunk(igc_session *s, const int32_t *ids, int M) {
   C.h_ids[0] = s->fill;
   memcpy(C.h_ids + 1, ids, sizeof(int32_t) * (size_t)M);
   CK(cudaMemcpyAsync(C.d_ids, C.h_ids, sizeof(int32_t) * (size_t)(1 + M), cudaMemcpyHostToDevice, s->st));
+  const int key = 4 * M + (head ? 2 : 0) + (want ? 1 : 0);
   if (s->use_graphs) {
-    auto it = C.graph.find(M);
+    auto it = C.graph.find(key);
     if (it == C.graph.end()) {
       cudaGraph_t g;
       long before = g_launches;
       CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
-      c = enqueue_chunk(s, M);
+      c = enqueue_chunk(s, M, head, want);
       cudaError_t e = cudaStreamEndCapture(s->st, &g);
       if (c != IGC_OKAY) return c;
       if (e != cudaSuccess) return fail_device(e, "capture");
@@ -1943,14 +2114,14 @@ static int run_chunk(igc_session *s, const int32_t *ids, int M) {
       e = cudaGraphInstantiate(&ex, g, 0);
       cudaGraphDestroy(g);
       if (e != cudaSuccess) return fail_device(e, "graph instantiate");
-      it = C.graph.emplace(M, ex).first;
-      s->kernels_per_chunk[M] = g_launches - before;
+      it = C.graph.emplace(key, ex).first;
+      s->kernels_per_chunk[key] = g_launches - before;
       g_launches = before;
     }
     CK(cudaGraphLaunch(it->second, s->st));
-    g_launches += s->kernels_per_chunk[M];
+    g_launches += s->kernels_per_chunk[key];
   } else {
-    c = enqueue_chunk(s, M);
+    c = enqueue_chunk(s, M, head, want);
     if (c != IGC_OKAY) return c;
   }
   CK(cudaMemcpyAsync(s->h_top, s->d_top, sizeof(int32_t) * (IGC_LANE_LIMIT + 1), cudaMemcpyDeviceToHost, s->st));
@@ -1959,7 +2130,7 @@ static int run_chunk(igc_session *s, const int32_t *ids, int M) {
   s->fill += M;
   for (int j = 0; j < M; ++j)
     if ((int)s->echo.size() < m->window_limit) s->echo.push_back(ids[j]);
-  s->logit_lanes = 0;
+  s->logit_lanes = head && want ? M : 0;
   return IGC_OKAY;
 }
 
@@ -1974,7 +2145,7 @@ extern "C" int igc_session_prime(igc_session *s, const int32_t *ids, int n) { /*
   // passes of at most 16 lanes (the reference's chunking, app_core.c:14443)
   for (int i = 0; i + 1 < n;) {
     int left = n - 1 - i, c;
-    if (s->use_chunks && left >= IGC_CHUNK_MIN) {
+    if (s->m->plain || (s->use_chunks && left >= IGC_CHUNK_MIN)) {
       const int lanes = left < chunk_lanes() ? left : chunk_lanes();
       c = run_chunk(s, ids + i, lanes);
       i += lanes;
@@ -2849,6 +3020,7 @@ extern "C" int igc_session_bench(igc_session *s, const int32_t *blocks, int roun
   if (!s || !blocks || rounds < 1 || k < 1 || k > IGC_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
   if (s->guess_count > 0) return IGC_FAIL_STATE;
   igc_model *m = s->m;
+  if (m->plain) return IGC_FAIL_SUPPORT;  // measures the decode GEMV passes
   if (s->fill + rounds * k > m->window_limit) return IGC_FAIL_STATE;
   for (int i = 0; i < rounds * k; ++i)
     if (blocks[i] < 0 || blocks[i] >= m->vocab) return IGC_FAIL_ARGUMENT;
@@ -2924,6 +3096,7 @@ extern "C" int igc_session_profile(igc_session *s, const int32_t *ids, int k, in
   if (!s || !ids || k < 1 || k > IGC_LANE_LIMIT) return IGC_FAIL_ARGUMENT;
   if (s->guess_count > 0) return IGC_FAIL_STATE;
   igc_model *m = s->m;
+  if (m->plain) return IGC_FAIL_SUPPORT;
   if (s->fill + k > m->window_limit) return IGC_FAIL_STATE;
   clear_stale("profile");
   CK(cudaSetDevice(m->device));
@@ -2962,6 +3135,7 @@ extern "C" int igc_session_profile(igc_session *s, const int32_t *ids, int k, in
 extern "C" int igc_session_stamps(igc_session *s, int k, int *cls_out, double *bytes_out, double *ns_out,
                                   int capacity, int reset) {
   if (!s || k < 1 || k > IGC_LANE_LIMIT || capacity < 0) return IGC_FAIL_ARGUMENT;
+  if (s->m->plain) return IGC_FAIL_SUPPORT;
   clear_stale("stamps");
   CK(cudaSetDevice(s->m->device));
   std::vector<unsigned long long> sum(IGC_STAMP_LIMIT);

@@ -138,7 +138,7 @@ static int layer_global(const igc_synth_spec *s, int l) {
   return s->global_every > 0 && ((l + 1) % s->global_every) == 0;
 }
 
-static size_t dtype_size(int dtype) { return dtype == 6 ? 1u : dtype == 1 ? 4u : 2u; }
+static size_t dtype_size(int dtype) { return dtype == 6 || dtype == 5 ? 1u : dtype == 1 ? 4u : 2u; }
 
 static void add(igc_synth_tensor *room, int room_count, int *n, const char *name, int dtype,
                 int64_t r, int64_t c, int rank, int kind, float offset) {
@@ -173,9 +173,33 @@ static void add_codes(igc_synth_tensor *room, int room_count, int *n, const char
 
 static int spec_group(const igc_synth_spec *s) { return s->group > 0 ? s->group : 32; }
 
+/* The export's activation grids of a projection (app_core.c:7941-7948): F32
+ * scalars, varied by a hash of the stem so planes differ. */
+static void add_grids(igc_synth_tensor *room, int room_count, int *n, const igc_synth_spec *s, const char *stem) {
+  char name[160];
+  const float vary = 1.0f + (float)(igc_synth_stream(stem) % 4) / 4.0f;
+  if (s->grid_in > 0.0f) {
+    snprintf(name, sizeof(name), "%s.input_activation_scale", stem);
+    add(room, room_count, n, name, 1, 1, 0, 1, IGC_SYNTH_CONST, s->grid_in * vary);
+  }
+  if (s->grid_out > 0.0f) {
+    snprintf(name, sizeof(name), "%s.output_activation_scale", stem);
+    add(room, room_count, n, name, 1, 1, 0, 1, IGC_SYNTH_CONST, s->grid_out * vary);
+  }
+}
+
 static void add_plane_bits(igc_synth_tensor *room, int room_count, int *n, const igc_synth_spec *s,
                            const char *stem, int64_t rows, int64_t cols, int bits) {
-  add_codes(room, room_count, n, stem, rows, cols, bits, spec_group(s), s->bf16_scales, "weight", "weight_scale");
+  if (bits == 8) { /* signed bytes, a scale a row (app_core.c:7910-7912) */
+    char name[128];
+    snprintf(name, sizeof(name), "%s.weight", stem);
+    add(room, room_count, n, name, 5, rows, cols, 2, IGC_SYNTH_CODE, 0.0f);
+    snprintf(name, sizeof(name), "%s.weight_scale", stem);
+    add(room, room_count, n, name, 2, rows, 1, 2, IGC_SYNTH_SCALE, 0.0f);
+  } else {
+    add_codes(room, room_count, n, stem, rows, cols, bits, spec_group(s), s->bf16_scales, "weight", "weight_scale");
+  }
+  add_grids(room, room_count, n, s, stem);
 }
 
 static void add_plane(igc_synth_tensor *room, int room_count, int *n, const igc_synth_spec *s, const char *stem,
@@ -207,12 +231,20 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
     add(room, room_count, &n, name, 3, s->vocab, PS, 2, IGC_SYNTH_NORMAL, 0.0f);
   }
   snprintf(name, sizeof(name), "%sper_layer_model_projection", P);
-  add_plane(room, room_count, &n, s, name, PS, s->hidden);
+  if (s->dense_ple_lift) { /* left unquantized by the export: bf16 N(0, 0.02) */
+    char wname[160];
+    snprintf(wname, sizeof(wname), "%s.weight", name);
+    add(room, room_count, &n, wname, 3, PS, s->hidden, 2, IGC_SYNTH_NORMAL, 0.0f);
+  } else {
+    add_plane(room, room_count, &n, s, name, PS, s->hidden);
+  }
   snprintf(name, sizeof(name), "%sper_layer_projection_norm.weight", P);
   add(room, room_count, &n, name, 3, s->ple_dim, 0, 1, IGC_SYNTH_OFFSET, no);
   snprintf(name, sizeof(name), "%snorm.weight", P);
   add(room, room_count, &n, name, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
-  if (!s->tied_head) add_plane(room, room_count, &n, s, "lm_head", s->vocab, s->hidden);
+  if (!s->tied_head) /* the head carries no activation grids in the export */
+    add_codes(room, room_count, &n, "lm_head", s->vocab, s->hidden, 4, spec_group(s), s->bf16_scales, "weight",
+              "weight_scale");
   for (int l = 0; l < s->layers; ++l) {
     char stem[128];
     int share = s->share_count > 0 && l >= first_share;
@@ -265,9 +297,9 @@ int igc_synth_list(const igc_synth_spec *s, igc_synth_tensor *room, int room_cou
     add(room, room_count, &n, stem, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
     if (s->ple_dim > 0) {
       STEM("per_layer_input_gate");
-      add_plane(room, room_count, &n, s, stem, s->ple_dim, s->hidden);
+      add_plane_bits(room, room_count, &n, s, stem, s->ple_dim, s->hidden, s->ple_bits8 ? 8 : 4);
       STEM("per_layer_projection");
-      add_plane(room, room_count, &n, s, stem, s->hidden, s->ple_dim);
+      add_plane_bits(room, room_count, &n, s, stem, s->hidden, s->ple_dim, s->ple_bits8 ? 8 : 4);
       STEM("post_per_layer_input_norm.weight");
       add(room, room_count, &n, stem, 3, s->hidden, 0, 1, IGC_SYNTH_OFFSET, no);
     }
@@ -354,6 +386,7 @@ static const char *dtype_name(int dtype) {
     case 1: return "F32";
     case 2: return "F16";
     case 3: return "BF16";
+    case 5: return "I8";
     case 6: return "U8";
     default: return "?";
   }

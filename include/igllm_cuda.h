@@ -368,6 +368,14 @@ typedef struct igc_synth_spec {
    * tables quantized to `embed_bits` / `ple_embed_bits` (2 or 4; 0: bf16
    * rows); no lm_head when `tied_head` (the quantized embedding is the head) */
   int late_mlp_bits, group, bf16_scales, embed_bits, ple_embed_bits, tied_head;
+  /* the forms the 4-bit tiles do not hold (a model with any of them runs its
+   * projections as stored on the CUDA cores): the per-layer input gate and
+   * projection as signed 8-bit codes with a scale a row (`ple_bits8`), the
+   * per-layer model projection left dense bf16 (`dense_ple_lift`), and every
+   * projection's activation grids, input and output steps `grid_in` /
+   * `grid_out` times 1, 1.25, 1.5 or 1.75 by plane (0: none) */
+  int ple_bits8, dense_ple_lift;
+  float grid_in, grid_out;
 } igc_synth_spec;
 
 /* Fill `out` with `count` values of stream `stream` of the spec's seed.

@@ -15,10 +15,15 @@ differs from the benchmark's checkpoint in ways this build covers:
 Checkpoints of those forms at a size the reference primes in seconds: the
 prime (tcgen05 chunks), blocks of 1, 4 and 16 lanes, the 8-bit cache on the
 same shape, and a crowd, each against the reference's logits within 2e-2
-(the crowd against lone rounds).  Not covered here: the export's 8-bit
-planes (the per-layer input gate and projection), its unquantized
-per_layer_model_projection and its activation grids (`quant_step`); a
-checkpoint carrying them is refused (IGC_FAIL_SUPPORT).
+(the crowd against lone rounds).
+
+A third checkpoint adds what the 4-bit tiles do not hold: the per-layer
+input gate and projection as signed 8-bit codes with a scale a row, the
+per-layer model projection left dense bf16, and activation grids on every
+projection (app_core.c:1930 quant_step, :7814 plane_lift_many).  Such a
+model binds every projection as stored and runs its passes through the lane
+stages (explicit norms, grids on the products' inputs and outputs) and
+CUDA-core products; it is checked the same way.
 """
 
 import numpy as np
@@ -32,6 +37,9 @@ ATOL = 2e-2
 EXPORT = dict(CACHED, global_head_dim=512, double_wide=1, seed=29)
 STORED = dict(EXPORT, late_mlp_bits=2, group=64, bf16_scales=1, embed_bits=2, ple_embed_bits=4, tied_head=1,
               seed=31)
+# and the forms the tiles do not hold: 8-bit per-layer input planes, a dense
+# per-layer model projection, activation grids on every projection
+PLAIN = dict(STORED, ple_bits8=1, dense_ple_lift=1, grid_in=0.05, grid_out=0.02, seed=37)
 WINDOW = EXPORT["window_limit"]
 VOCAB = EXPORT["vocab"]
 
@@ -54,9 +62,16 @@ def stored_dir(tmp_path_factory, igc_lib):
     return d
 
 
-@pytest.mark.parametrize("form,bits", [("shape", 0), ("shape", 8), ("stored", 0)])
-def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, stored_dir, form, bits):
-    folder = export_dir if form == "shape" else stored_dir
+@pytest.fixture(scope="module")
+def plain_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("plain"))
+    igc_lib.synth_write(igc_lib.SynthSpec(**PLAIN), d, 8)
+    return d
+
+
+@pytest.mark.parametrize("form,bits", [("shape", 0), ("shape", 8), ("stored", 0), ("plain", 0)])
+def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, stored_dir, plain_dir, form, bits):
+    folder = {"shape": export_dir, "stored": stored_dir, "plain": plain_dir}[form]
     m = igc_lib.Model(folder=folder, window_limit=WINDOW, cache_bits=bits)
     rm = igo_mod.RefModel(folder, threads=8, window_limit=WINDOW, cache_bits=bits)
     assert m.memory_bytes() == rm.memory_bytes()
@@ -92,8 +107,9 @@ def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, stored_dir
     rm.close()
 
 
-def test_export_shape_crowd(igc_lib, export_dir):
-    m = igc_lib.Model(folder=export_dir, window_limit=WINDOW)
+@pytest.mark.parametrize("form", ["shape", "plain"])
+def test_export_shape_crowd(igc_lib, export_dir, plain_dir, form):
+    m = igc_lib.Model(folder=export_dir if form == "shape" else plain_dir, window_limit=WINDOW)
     k = 4
     prompts = [_ids(90 + 23 * j, 60 + j) for j in range(3)]
     shared, lone = [], []
