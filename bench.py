@@ -424,6 +424,7 @@ def run_ours(args):
     crowd = crowd_bench(ig, model) if not args.no_crowd else None
     long_ctx = long_context_bench(ig) if not args.no_crowd else None
     cache8 = cache8_bench(ig, model) if not args.no_crowd else None
+    export = export_bench(ig) if not args.no_crowd else None
 
     # the projection kernels against the HBM roofline, from the timed
     # region's own graphed passes: every projection and attention launch
@@ -475,6 +476,7 @@ def run_ours(args):
         "crowd": crowd,
         "long_context": long_ctx,
         "cache8": cache8,
+        "export": export,
         "roofline": {"bound": "hbm", "kernel": "int4 skinny GEMM (layer projections)",
                      "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4) if achieved else None, "traffic": traffic,
@@ -595,6 +597,56 @@ def cache8_bench(ig, float_model):
     out["workload"] = ("config 0's prompt and weights, --cache 8 (key scale 1/2048, value 1/64, x1-1.375 by layer), "
                        "64 always-right --guess 4 rounds on the device; owner layers write e4m3 codes, each layer "
                        "decodes the rows it reads, then attends")
+    return out
+
+
+def export_bench(ig):
+    """The shipped export's form at full size (its config.json and
+    quantization_config, app_core.c:7886): 512-wide global heads, the doubled
+    feed-forward of the sharing layers (12288 wide) coded in 2 bits, the
+    embedding a 2-bit table that is also the head, the per-layer table in 4
+    bits.  Greedy --guess 4 rounds of always-right blocks after config 0's
+    prompt, on the device.  Then the forms the tiles do not hold on top (8-bit
+    per-layer input planes, a dense per-layer model projection, activation
+    grids on every projection): that model runs its plain path, timed through
+    igc_session_round (host ids in and out)."""
+    out = {}
+    prompt = make_prompt(0)
+    blocks = np.random.default_rng(6).integers(0, VOCAB, (32, GUESS)).astype(np.int32)
+    spec = ig.spec_e2b(seed=1, window_limit=4096)
+    spec.global_head_dim, spec.double_wide, spec.late_mlp_bits = 512, 1, 2
+    spec.embed_bits, spec.ple_embed_bits, spec.tied_head = 2, 4, 1
+    model = ig.Model(spec=spec, device=0, window_limit=4096)
+    s = ig.Session(model)
+    s.prime(prompt)
+    base = s.fill
+    s.bench(blocks[:2], GUESS)
+    s.hold(base)
+    ms, _ = s.bench(blocks, GUESS)
+    out["tiles"] = {"round_us": round(1000 * ms / len(blocks), 1), "tok_s": round(len(blocks) * GUESS / (ms / 1e3), 1),
+                    "decode_mb": round(model.decode_bytes() / 1e6, 1)}
+    s.close()
+    model.close()
+    spec.ple_bits8, spec.dense_ple_lift, spec.grid_in, spec.grid_out = 1, 1, 0.05, 0.02
+    model = ig.Model(spec=spec, device=0, window_limit=4096)
+    s = ig.Session(model)
+    short = prompt[:128]  # the plain path primes slowly: a short prompt
+    s.prime(short)
+    base = s.fill
+    seq = np.concatenate([[int(short[-1])], blocks.ravel()]).astype(np.int32)
+    s.round(seq[:GUESS])  # captures the pass
+    s.hold(base)
+    rounds = 8
+    t0 = time.perf_counter()
+    for r in range(rounds):
+        s.round(seq[r * GUESS: r * GUESS + GUESS])
+    wall = time.perf_counter() - t0
+    out["plain"] = {"round_ms": round(1000 * wall / rounds, 2), "rounds": rounds}
+    s.close()
+    model.close()
+    out["workload"] = ("the export's form at E2B size, config 0's prompt, --guess 4: 'tiles' 32 always-right rounds on the "
+                       "device (every lane counted); 'plain' adds 8-bit per-layer input planes, a dense per-layer model "
+                       "projection and activation grids, a 128-id prompt, 8 rounds through igc_session_round")
     return out
 
 

@@ -193,6 +193,14 @@ __device__ __forceinline__ float fmax4(float4 v) { return fmaxf(fmaxf(fabsf(v.x)
 //   [1600, 2112)  per-thread stripes of the residual's sums of squares
 constexpr int SCR_FACTOR = 0, SCR_SCALE = 16, SCR_SHRINK_P = 32, SCR_SSQ = 64, SCR_AMAX = 832, SCR_STRIPE = 1600;
 constexpr int SCR_FLOATS = 2112;
+// A plane wider than 6144 columns (the doubled feed-forward's 12288-column
+// down projection) keeps the sums of its parts 48-95 after the rest:
+//   [2112, 2880)  per-(lane, part) sums of squares of parts 48-95
+// and only its launches take those 3 KB.
+constexpr int SCR_SSQ_FAR = SCR_FLOATS, SCR_FLOATS_WIDE = SCR_FLOATS + 16 * 48;
+__host__ __device__ __forceinline__ int scr_ssq(int j, int part) {
+  return part < 48 ? SCR_SSQ + j * 48 + part : SCR_SSQ_FAR + j * 48 + (part - 48);
+}
 
 // float4 columns a thread loads before computing on them: as many as keep
 // the register file in bounds for the arrays the prologue reads.
@@ -210,7 +218,7 @@ struct ProBatch {
 // chunks further on per part, so each thread computes its four word offsets
 // once and then only adds.  The producer partials and the first batch of
 // activations are loaded before anything waits on either.
-constexpr int GEMV_MAX_PARTS = 48;  // 6144 columns
+constexpr int GEMV_MAX_PARTS = 96;  // 12288 columns
 
 // The unnormed prologue when the producer left the magnitudes of x: the
 // lanes' staging scales are known before any activation arrives, so each
@@ -419,7 +427,7 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
         }
         if (NRM) {  // a norm's sum of squares: one fixed tree per part
           ssq = warp_sum(ssq);
-          if (l32 == 0) scr[SCR_SSQ + j * GEMV_MAX_PARTS + w_local + wpl * i] = ssq;
+          if (l32 == 0) scr[scr_ssq(j, w_local + wpl * i)] = ssq;
         }
       }
     }
@@ -487,8 +495,11 @@ __device__ void gemv_prologue(const GemvArgs &a, uint32_t *stage, float *scr) {
     if (w_local == 0) {
       float s_ = 0.0f;
       if (NRM) {
-        const float *ps = scr + SCR_SSQ + j * GEMV_MAX_PARTS;
-        s_ = warp_sum((l32 < nparts ? ps[l32] : 0.0f) + (l32 + 32 < nparts ? ps[l32 + 32] : 0.0f));
+        // a fixed tree: parts l32, l32 + 32 and l32 + 64 a lane (the third is
+        // 0 below 65 parts, which leaves narrower planes' sums as they were)
+        s_ = warp_sum(((l32 < nparts ? scr[scr_ssq(j, l32)] : 0.0f) +
+                       (l32 + 32 < nparts ? scr[scr_ssq(j, l32 + 32)] : 0.0f)) +
+                      (l32 + 64 < nparts ? scr[scr_ssq(j, l32 + 64)] : 0.0f));
       }
       if (l32 == 0) {
         const float shrink = NRM ? rms_shrink(s_, cols, a.eps) : 1.0f;

@@ -1319,7 +1319,7 @@ struct GemvLayout {
 static GemvLayout gemv_layout(const GemvArgs &a, int pair, int W, int P, int D) {
   const int MODE = gemv_mode(a.lanes), H = pair + 1;
   GemvLayout L;
-  L.red = align128(gemv_stage_bytes(a.pl.n_cc, MODE) + SCR_FLOATS * 4);
+  L.red = align128(gemv_stage_bytes(a.pl.n_cc, MODE) + (a.pl.cols > 48 * 128 ? SCR_FLOATS_WIDE : SCR_FLOATS) * 4);
   size_t red_floats = a.split > 1 ? (size_t)W * 32 * H * gemv_acc_floats(MODE) : 0;
   if (red_floats < (size_t)W * 16) red_floats = (size_t)W * 16;
   L.bars = align128(L.red + red_floats * 4);

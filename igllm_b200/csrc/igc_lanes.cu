@@ -663,14 +663,30 @@ __device__ __forceinline__ float grid_step(float v, float step) {
   return level * step;
 }
 
-__device__ __forceinline__ float plain_weight(const PlainArgs &a, int r, int c) {
-  if (a.codes) {
-    const size_t bit = (size_t)c * a.bits;
-    const uint8_t *row = a.codes + (size_t)r * a.stride;
-    uint32_t w = row[bit >> 3] >> (bit & 7);
-    if ((int)(bit & 7) + a.bits > 8) w |= (uint32_t)row[(bit >> 3) + 1] << (8 - (bit & 7));
+// A plain plane's row r: where its codes, scales or dense values start, and
+// how a column finds its scale (a shift for groups of a power of two).
+struct PlainRow {
+  const uint8_t *codes;
+  const float *scales;
+  int shift;  // log2 of the group size, or -1 (divide), or -2 (one group)
+};
+
+__device__ __forceinline__ PlainRow plain_row(const PlainArgs &a, int r) {
+  PlainRow p;
+  p.codes = a.codes ? a.codes + (size_t)r * a.stride : nullptr;
+  p.scales = a.codes ? a.scales + (size_t)r * a.groups : nullptr;
+  p.shift = a.groups == 1 ? -2 : ((a.group_size & (a.group_size - 1)) == 0 ? __ffs(a.group_size) - 1 : -1);
+  return p;
+}
+
+__device__ __forceinline__ float plain_weight(const PlainArgs &a, const PlainRow &p, int r, int c) {
+  if (p.codes) {
+    const int bit = c * a.bits;
+    uint32_t w = p.codes[bit >> 3] >> (bit & 7);
+    if ((bit & 7) + a.bits > 8) w |= (uint32_t)p.codes[(bit >> 3) + 1] << (8 - (bit & 7));
     const int code = (int)((w & ((1u << a.bits) - 1u)) ^ a.flip);
-    return (float)(code - a.bias) * a.scales[(size_t)r * a.groups + c / a.group_size];
+    const int g = p.shift == -2 ? 0 : (p.shift >= 0 ? c >> p.shift : c / a.group_size);
+    return (float)(code - a.bias) * p.scales[g];
   }
   const size_t i = (size_t)r * a.cols + c;
   if (a.dense_type == 1) return reinterpret_cast<const float *>(a.dense)[i];
@@ -678,35 +694,40 @@ __device__ __forceinline__ float plain_weight(const PlainArgs &a, int r, int c) 
   return a.dense_type == 2 ? __half2float(__ushort_as_half(h)) : __uint_as_float((uint32_t)h << 16);
 }
 
-// A warp a row at a time (the block's rows r0 + warp, + 8, ...), 16 lanes at
-// a time: thread t the columns t, t + 32, ..., then each lane's sum by one
-// fixed shuffle tree.  The head keeps, per lane, the largest of the block's
-// values (first row on a tie, app_main.c:482).
-constexpr int PL_ROWS = 128, PL_LANES = 16;
+// A warp a row at a time (the block's rows r0 + warp, + 8, ...; 32 rows a
+// block, so even a small plane spreads over the SMs), LN lanes at a time:
+// thread t the columns t, t + 32, ... (four in flight), then each lane's sum
+// by one fixed shuffle tree.  A lane's sum does not depend on LN or on the
+// other lanes.  The head keeps, per lane, the largest of the block's values
+// (first row on a tie, app_main.c:482).
+constexpr int PL_ROWS = 32;
+template <int LN>
 __global__ void __launch_bounds__(256) plain_product_kernel(PlainArgs a) {
-  __shared__ float best_v[8][PL_LANES];
-  __shared__ int best_i[8][PL_LANES];
+  __shared__ float best_v[8][LN];
+  __shared__ int best_i[8][LN];
   pdl_release();
   pdl_wait();
   const int warp = threadIdx.x >> 5, l = threadIdx.x & 31;
   const int r0 = blockIdx.x * PL_ROWS, r1 = min(r0 + PL_ROWS, a.rows);
-  for (int g0 = 0; g0 < a.lanes; g0 += PL_LANES) {
-    const int gl = min(PL_LANES, a.lanes - g0);
-    float keep_v[PL_LANES];
-    int keep_i[PL_LANES];
+  for (int g0 = 0; g0 < a.lanes; g0 += LN) {
+    const int gl = min(LN, a.lanes - g0);
+    float keep_v[LN];
+    int keep_i[LN];
 #pragma unroll
-    for (int j = 0; j < PL_LANES; ++j) {
+    for (int j = 0; j < LN; ++j) {
       keep_v[j] = -FLT_MAX;
       keep_i[j] = 0x7fffffff;
     }
     for (int r = r0 + warp; r < r1; r += 8) {
-      float acc[PL_LANES];
+      const PlainRow pr = plain_row(a, r);
+      float acc[LN];
 #pragma unroll
-      for (int j = 0; j < PL_LANES; ++j) acc[j] = 0.0f;
+      for (int j = 0; j < LN; ++j) acc[j] = 0.0f;
+#pragma unroll 4
       for (int c = l; c < a.cols; c += 32) {
-        const float w = plain_weight(a, r, c);
+        const float w = plain_weight(a, pr, r, c);
 #pragma unroll
-        for (int j = 0; j < PL_LANES; ++j)
+        for (int j = 0; j < LN; ++j)
           if (j < gl) {
             float x = a.x[(size_t)(g0 + j) * a.x_stride + c];
             if (a.enter > 0.0f) x = grid_step(x, a.enter);
@@ -714,7 +735,7 @@ __global__ void __launch_bounds__(256) plain_product_kernel(PlainArgs a) {
           }
       }
 #pragma unroll
-      for (int j = 0; j < PL_LANES; ++j) {
+      for (int j = 0; j < LN; ++j) {
         float v = warp_sum(acc[j]);
         if (j >= gl) continue;
         if (a.leave > 0.0f) v = grid_step(v, a.leave);
@@ -733,7 +754,7 @@ __global__ void __launch_bounds__(256) plain_product_kernel(PlainArgs a) {
     if (a.arg_val) {
       if (l == 0)
 #pragma unroll
-        for (int j = 0; j < PL_LANES; ++j) {
+        for (int j = 0; j < LN; ++j) {
           best_v[warp][j] = keep_v[j];
           best_i[warp][j] = keep_i[j];
         }
@@ -914,10 +935,13 @@ cudaError_t igc_launch_plain_product(const PlainArgs *a, int sm_count, int *bloc
                : (!a->dense || a->dense_type < 1 || a->dense_type > 3))
     return cudaErrorInvalidValue;
   if (a->arg_val && !a->arg_idx) return cudaErrorInvalidValue;
-  const int blocks = (a->rows + PL_ROWS - 1) / PL_ROWS;
+  const int blocks = igc_plain_blocks(a->rows);
   if (blocks_out) *blocks_out = blocks;
-  return lane_launch(plain_product_kernel, dim3(blocks), dim3(256), 0, st, *a);
+  if (a->lanes <= 4) return lane_launch(plain_product_kernel<4>, dim3(blocks), dim3(256), 0, st, *a);
+  return lane_launch(plain_product_kernel<16>, dim3(blocks), dim3(256), 0, st, *a);
 }
+
+int igc_plain_blocks(int rows) { return (rows + PL_ROWS - 1) / PL_ROWS; }
 
 cudaError_t igc_launch_lane_widen(const WidenArgs *w, int batch, int rows_most, int sm_count, cudaStream_t st) {
   if (!w || batch < 1 || rows_most < 1 || w->kv_w < 16 || w->kv_w % 16 || w->lanes < 1) return cudaErrorInvalidValue;

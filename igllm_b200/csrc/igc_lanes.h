@@ -140,10 +140,12 @@ cudaError_t igc_launch_lane_kv_many(const float *qkv, int qkv_stride, int heads,
 // a global one).  `rows_most` bounds the rows any launch of this shape sees
 // (it sizes the grid); kv_w, a row's values, is a multiple of 16.
 cudaError_t igc_launch_lane_widen(const igc::WidenArgs *w, int batch, int rows_most, int sm_count, cudaStream_t st);
-// A plain plane's product for `lanes` lanes; with the head's cap, one block
-// of 8 warps a 128 rows (so `ceil(rows / 128)` argmax partials).  Returns the
-// blocks launched in *blocks_out when it is not null.
+// A plain plane's product for `lanes` lanes, one block of 8 warps a
+// igc_plain_blocks(rows)'th of the rows (with the head's cap, as many argmax
+// partials a lane).  Returns the blocks launched in *blocks_out when it is
+// not null.
 cudaError_t igc_launch_plain_product(const igc::PlainArgs *a, int sm_count, int *blocks_out, cudaStream_t st);
+int igc_plain_blocks(int rows);
 // out[i] = *p0 + 16 i for i < groups (a prefill chunk's attention groups).
 cudaError_t igc_launch_lane_positions(const int *p0, int groups, int *out, cudaStream_t st);
 // Per lane the largest of `parts` argmax partials [part][lanes] (first index

@@ -1471,7 +1471,16 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
     a.lanes = lb;
     a.lanes_total = K;
     a.batches = (K + lb - 1) / lb;
-    if (igc_gemv_smem_min(&a, pair) > (size_t)s->m->smem_limit) return IGC_FAIL_SUPPORT;
+    if (igc_gemv_smem_min(&a, pair) > (size_t)s->m->smem_limit) {
+      // too wide even for batches of four (the 12288-column down projection):
+      // the narrower launches below
+      a.lanes = K;
+      a.lanes_total = 0;
+      a.batches = 0;
+      lb = 0;
+    }
+  }
+  if (lb) {
     int g = pl.grid;
     if (wave_cap) {
       const int per = s->m->sm_count / a.batches;
@@ -1489,12 +1498,20 @@ static int gemv(igc_session *s, const DevPlane &pl, int K, int pro, int epi, con
     if (epi == EPI_LOGITS) s->head_parts = used;
     return IGC_OKAY;
   }
-  // Too wide to stage sixteen lanes at once (the 6144-column down
-  // projection): two launches of eight lanes, each lane independent.
-  if (K <= 8 || epi == EPI_LOGITS) return IGC_FAIL_SUPPORT;
-  for (int j0 = 0; j0 < K; j0 += 8) {
+  // Too wide to stage every lane at once (the 6144-column down projection
+  // at sixteen lanes, the doubled 12288-column one at four): launches of the
+  // most lanes that fit, 8, 4, 2 or 1, each lane independent.
+  if (epi == EPI_LOGITS) return IGC_FAIL_SUPPORT;
+  int sub = 8;
+  while (sub > 1) {
+    GemvArgs t = a;
+    t.lanes = K < sub ? K : sub;
+    if (t.lanes < K && igc_gemv_smem_min(&t, pair) <= (size_t)s->m->smem_limit) break;
+    sub /= 2;
+  }
+  for (int j0 = 0; j0 < K; j0 += sub) {
     GemvArgs b = a;
-    b.lanes = K - j0 < 8 ? K - j0 : 8;
+    b.lanes = K - j0 < sub ? K - j0 : sub;
     b.x = x + (size_t)j0 * x_stride;
     b.p = p ? p + (size_t)j0 * x_stride : nullptr;
     b.x_out = x_out ? x_out + (size_t)j0 * x_stride : nullptr;
@@ -1780,7 +1797,9 @@ static int lane_buf_alloc(igc_model *m, LaneBuf &B, int cap, int split_lanes, st
   if (c == IGC_OKAY) c = grab(&B.factor, (size_t)cap);
   if (c == IGC_OKAY && m->plain) c = grab(&B.rows, (size_t)cap * std::max(m->plain_cols, H));
   if (c == IGC_OKAY) c = grab((uint8_t **)&B.a_tiles, (size_t)((cap + LG_M - 1) / LG_M) * max_cc * LG_A_STEP_BYTES);
-  const size_t head_tiles = (size_t)(m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16);
+  // the head's argmax partials: one a 128-row tile, or a plain product's block
+  const size_t head_tiles = m->plain ? (size_t)igc_plain_blocks(m->head.rows)
+                                     : (size_t)(m->head.n_rb + LG_N / 16 - 1) / (LG_N / 16);
   if (c == IGC_OKAY) c = grab(&B.arg_val, head_tiles * cap);
   if (c == IGC_OKAY) c = grab(&B.arg_idx, head_tiles * cap);
   if (c != IGC_OKAY) return c;

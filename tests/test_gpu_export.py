@@ -40,6 +40,9 @@ STORED = dict(EXPORT, late_mlp_bits=2, group=64, bf16_scales=1, embed_bits=2, pl
 # and the forms the tiles do not hold: 8-bit per-layer input planes, a dense
 # per-layer model projection, activation grids on every projection
 PLAIN = dict(STORED, ple_bits8=1, dense_ple_lift=1, grid_in=0.05, grid_out=0.02, seed=37)
+# the export's own feed-forward width: 6144, doubled to 12288 on the sharing
+# layers (the decode projection then stages its lanes in narrower launches)
+WIDE = dict(EXPORT, inner=6144, seed=41)
 WINDOW = EXPORT["window_limit"]
 VOCAB = EXPORT["vocab"]
 
@@ -63,15 +66,23 @@ def stored_dir(tmp_path_factory, igc_lib):
 
 
 @pytest.fixture(scope="module")
+def wide_ff_dir(tmp_path_factory, igc_lib):
+    d = str(tmp_path_factory.mktemp("wideff"))
+    igc_lib.synth_write(igc_lib.SynthSpec(**WIDE), d, 8)
+    return d
+
+
+@pytest.fixture(scope="module")
 def plain_dir(tmp_path_factory, igc_lib):
     d = str(tmp_path_factory.mktemp("plain"))
     igc_lib.synth_write(igc_lib.SynthSpec(**PLAIN), d, 8)
     return d
 
 
-@pytest.mark.parametrize("form,bits", [("shape", 0), ("shape", 8), ("stored", 0), ("plain", 0)])
-def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, stored_dir, plain_dir, form, bits):
-    folder = {"shape": export_dir, "stored": stored_dir, "plain": plain_dir}[form]
+@pytest.mark.parametrize("form,bits", [("shape", 0), ("shape", 8), ("stored", 0), ("plain", 0), ("wide", 0)])
+def test_export_shape_matches_reference(igc_lib, igo_mod, export_dir, stored_dir, plain_dir, wide_ff_dir, form,
+                                        bits):
+    folder = {"shape": export_dir, "stored": stored_dir, "plain": plain_dir, "wide": wide_ff_dir}[form]
     m = igc_lib.Model(folder=folder, window_limit=WINDOW, cache_bits=bits)
     rm = igo_mod.RefModel(folder, threads=8, window_limit=WINDOW, cache_bits=bits)
     assert m.memory_bytes() == rm.memory_bytes()
