@@ -694,12 +694,56 @@ __device__ __forceinline__ float plain_weight(const PlainArgs &a, const PlainRow
   return a.dense_type == 2 ? __half2float(__ushort_as_half(h)) : __uint_as_float((uint32_t)h << 16);
 }
 
+// Eight weights of a row from column c0 (a multiple of 8) in one load: the
+// codes of 1, 2, 4 or 8 bits (1-8 bytes) and their group's scale, or eight
+// dense values.
+__device__ __forceinline__ void plain_weight8(const PlainArgs &a, const PlainRow &p, int r, int c0, float (&w)[8]) {
+  if (p.codes) {
+    const uint8_t *at = p.codes + (c0 * a.bits >> 3);
+    uint64_t v;
+    switch (a.bits) {
+      case 1: v = *at; break;
+      case 2: v = *reinterpret_cast<const uint16_t *>(at); break;
+      case 4: v = *reinterpret_cast<const uint32_t *>(at); break;
+      default: v = *reinterpret_cast<const uint64_t *>(at); break;
+    }
+    const int g = p.shift == -2 ? 0 : (p.shift >= 0 ? c0 >> p.shift : c0 / a.group_size);
+    const float sc = p.scales[g];
+    const uint32_t mask = (1u << a.bits) - 1u;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int code = (int)(((uint32_t)(v >> (k * a.bits)) & mask) ^ a.flip);
+      w[k] = (float)(code - a.bias) * sc;
+    }
+    return;
+  }
+  const size_t i = (size_t)r * a.cols + c0;
+  if (a.dense_type == 1) {
+    const float4 x0 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.dense) + i);
+    const float4 x1 = *reinterpret_cast<const float4 *>(reinterpret_cast<const float *>(a.dense) + i + 4);
+    w[0] = x0.x; w[1] = x0.y; w[2] = x0.z; w[3] = x0.w;
+    w[4] = x1.x; w[5] = x1.y; w[6] = x1.z; w[7] = x1.w;
+    return;
+  }
+  const uint4 h = *reinterpret_cast<const uint4 *>(reinterpret_cast<const uint16_t *>(a.dense) + i);
+  const uint32_t hw[4] = {h.x, h.y, h.z, h.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint16_t lo = (uint16_t)(hw[k] & 0xFFFFu), hi = (uint16_t)(hw[k] >> 16);
+    w[2 * k] = a.dense_type == 2 ? __half2float(__ushort_as_half(lo)) : __uint_as_float((uint32_t)lo << 16);
+    w[2 * k + 1] = a.dense_type == 2 ? __half2float(__ushort_as_half(hi)) : __uint_as_float((uint32_t)hi << 16);
+  }
+}
+
 // A warp a row at a time (the block's rows r0 + warp, + 8, ...; 32 rows a
-// block, so even a small plane spreads over the SMs), LN lanes at a time:
-// thread t the columns t, t + 32, ... (four in flight), then each lane's sum
-// by one fixed shuffle tree.  A lane's sum does not depend on LN or on the
-// other lanes.  The head keeps, per lane, the largest of the block's values
-// (first row on a tie, app_main.c:482).
+// block, so even a small plane spreads over the SMs), LN lanes at a time.
+// Where the row allows (`vec`: columns in eights that share a scale, code
+// rows and input rows aligned for it) thread t takes eight columns at a time
+// from 8t, 8t + 256, ..., one load of weights and two of each lane's inputs;
+// otherwise, or for the columns past the last 256, the columns t, t + 32, ....
+// Each lane's sum then goes by one fixed shuffle tree; it depends neither on
+// LN nor on the other lanes.  The head keeps, per lane, the largest of the
+// block's values (first row on a tie, app_main.c:482).
 constexpr int PL_ROWS = 32;
 template <int LN>
 __global__ void __launch_bounds__(256) plain_product_kernel(PlainArgs a) {
@@ -723,8 +767,34 @@ __global__ void __launch_bounds__(256) plain_product_kernel(PlainArgs a) {
       float acc[LN];
 #pragma unroll
       for (int j = 0; j < LN; ++j) acc[j] = 0.0f;
+      int c_from = l;
+      if (a.vec) {
+        const int n8 = a.cols >> 3;
+#pragma unroll 2
+        for (int q = l; q < n8; q += 32) {
+          const int c0 = q << 3;
+          float w[8];
+          plain_weight8(a, pr, r, c0, w);
+#pragma unroll
+          for (int j = 0; j < LN; ++j)
+            if (j < gl) {
+              const float *xr = a.x + (size_t)(g0 + j) * a.x_stride + c0;
+              const float4 x0 = *reinterpret_cast<const float4 *>(xr);
+              const float4 x1 = *reinterpret_cast<const float4 *>(xr + 4);
+              float xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+              if (a.enter > 0.0f)
+#pragma unroll
+                for (int k = 0; k < 8; ++k) xv[k] = grid_step(xv[k], a.enter);
+              float t = acc[j];
+#pragma unroll
+              for (int k = 0; k < 8; ++k) t = fmaf(w[k], xv[k], t);
+              acc[j] = t;
+            }
+        }
+        c_from = (n8 << 3) + l;
+      }
 #pragma unroll 4
-      for (int c = l; c < a.cols; c += 32) {
+      for (int c = c_from; c < a.cols; c += 32) {
         const float w = plain_weight(a, pr, r, c);
 #pragma unroll
         for (int j = 0; j < LN; ++j)
@@ -937,6 +1007,13 @@ cudaError_t igc_launch_plain_product(const PlainArgs *a, int sm_count, int *bloc
   if (a->arg_val && !a->arg_idx) return cudaErrorInvalidValue;
   const int blocks = igc_plain_blocks(a->rows);
   if (blocks_out) *blocks_out = blocks;
+  PlainArgs v = *a;
+  // eight columns a load where the rows and groups line up for it
+  v.vec = (a->x_stride % 4 == 0) && (a->cols % 8 == 0) && ((size_t)a->x % 16 == 0) &&
+          (a->codes ? ((a->bits == 1 || a->bits == 2 || a->bits == 4 || a->bits == 8) && a->group_size % 8 == 0 &&
+                       a->stride % (size_t)a->bits == 0 && (size_t)a->codes % 8 == 0)
+                    : ((size_t)a->dense % 16 == 0)) ? 1 : 0;
+  a = &v;
   if (a->lanes <= 4) return lane_launch(plain_product_kernel<4>, dim3(blocks), dim3(256), 0, st, *a);
   return lane_launch(plain_product_kernel<16>, dim3(blocks), dim3(256), 0, st, *a);
 }

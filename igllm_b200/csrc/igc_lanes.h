@@ -70,6 +70,7 @@ struct PlainArgs {
   float cap;              // > 0: the head's soft cap, then argmax partials
   float *arg_val;         // [block][lanes] the largest value of each block's rows, and its row
   int *arg_idx;
+  int vec;                // set by the launcher: eight columns a load
 };
 
 struct LaneGemmArgs {
