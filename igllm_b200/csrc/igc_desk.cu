@@ -27,6 +27,12 @@ struct DeskPlane {
   uint4 *tiles = nullptr;
   uint2 *scales = nullptr;
   int n_rb = 0, n_cc = 0, rows = 0, cols = 0, split = 1, grid = 1;
+  // a plane the tiles do not hold (8-bit codes, a dense plane, scales f16
+  // cannot hold): kept as stored for the CUDA-core product (`plain.codes` or
+  // `plain.dense` set), its device copies freed with the desk
+  bool is_plain = false;
+  PlainArgs plain = {};
+  void *plain_data = nullptr, *plain_scales = nullptr;
 };
 
 struct DeskState {
@@ -73,26 +79,92 @@ bool grow(DeskState *s, size_t floats) {
   return true;
 }
 
-// app_core.c:1775 plane, restricted to what the kernels read: offset codes of
-// 1, 2 or 4 bits, no flip, no zero points, groups a multiple of 32 columns,
-// scales of any float type that f16 holds exactly.
+// A plane the tiles do not hold, kept as stored for the CUDA-core product:
+// offset codes of 1-8 bits (signed bytes through their flip) with scales of
+// any float type widened to f32, or a dense F32/F16/BF16 plane
+// (app_core.c:1775-1797).  Zero points are refused.  The reference applies a
+// plane's activation grids itself around the table's product
+// (app_core.c:7814 plane_lift_many), so the product here takes none.
+const DeskPlane *plain_plane_of(DeskState *s, const igc_plane *p, const void *key) {
+  DeskPlane dp;
+  dp.is_plain = true;
+  dp.rows = p->row_count;
+  dp.cols = p->col_count;
+  PlainArgs &a = dp.plain;
+  memset(&a, 0, sizeof(a));
+  a.rows = p->row_count;
+  a.cols = p->col_count;
+  a.pair_half = -1;
+  a.out_scale = 1.0f;
+  auto type_bytes = [](int t) -> size_t { return t == 1 ? 4u : (t == 2 || t == 3) ? 2u : 0u; };
+  if (p->form == 1) {
+    const size_t tb = type_bytes(p->real_type);
+    if (!tb || !p->real_data) return void(note(s, IGC_FAIL_SUPPORT)), nullptr;
+    const size_t bytes = (size_t)p->row_count * p->col_count * tb;
+    if (!ok(s, cudaMalloc(&dp.plain_data, bytes)) ||
+        !ok(s, cudaMemcpy(dp.plain_data, p->real_data, bytes, cudaMemcpyHostToDevice)))
+      return nullptr;
+    a.dense = dp.plain_data;
+    a.dense_type = p->real_type;
+  } else {
+    const int bits = p->bit_count;
+    const size_t gb = type_bytes(p->gain_type);
+    if (p->form != 2 || bits < 1 || bits > 8 || p->code_bias != (1 << (bits - 1)) ||
+        (p->code_flip != 0 && p->code_flip != p->code_bias) || p->bias_data || !gb || p->group_count < 1 ||
+        p->group_size < 1 || (size_t)p->group_count * p->group_size < (size_t)p->col_count)
+      return void(note(s, IGC_FAIL_SUPPORT)), nullptr;
+    std::vector<float> sc((size_t)p->row_count * p->group_count);
+    for (size_t i = 0; i < sc.size(); ++i) {
+      const uint8_t *g = static_cast<const uint8_t *>(p->gain_data) + i * gb;
+      if (p->gain_type == 1) {
+        memcpy(&sc[i], g, 4);
+      } else {
+        uint16_t h;
+        memcpy(&h, g, 2);
+        if (p->gain_type == 2) {
+          __half hh;
+          memcpy(&hh, &h, 2);
+          sc[i] = __half2float(hh);
+        } else {
+          const uint32_t u = (uint32_t)h << 16;
+          memcpy(&sc[i], &u, 4);
+        }
+      }
+    }
+    const size_t cb = (size_t)p->row_count * p->row_stride;
+    if (!ok(s, cudaMalloc(&dp.plain_data, cb)) || !ok(s, cudaMalloc(&dp.plain_scales, sizeof(float) * sc.size())) ||
+        !ok(s, cudaMemcpy(dp.plain_data, p->code_data, cb, cudaMemcpyHostToDevice)) ||
+        !ok(s, cudaMemcpy(dp.plain_scales, sc.data(), sizeof(float) * sc.size(), cudaMemcpyHostToDevice)))
+      return nullptr;
+    a.codes = static_cast<const uint8_t *>(dp.plain_data);
+    a.stride = p->row_stride;
+    a.bits = bits;
+    a.flip = (uint32_t)p->code_flip;
+    a.bias = p->code_bias;
+    a.scales = static_cast<const float *>(dp.plain_scales);
+    a.groups = p->group_count;
+    a.group_size = p->group_size;
+  }
+  return &(s->planes[key] = dp);
+}
+
+// app_core.c:1775 plane: offset codes of 1, 2 or 4 bits, no flip, no zero
+// points, groups a multiple of 32 columns, scales of any float type that f16
+// holds exactly go to the tiles; anything else to plain_plane_of.
 const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
-  auto it = s->planes.find(p->code_data);
+  const void *key = p->code_data ? (const void *)p->code_data : p->real_data;
+  auto it = s->planes.find(key);
   if (it != s->planes.end()) return &it->second;
   const int bits = p->bit_count;
   if (p->form != 2 || (bits != 1 && bits != 2 && bits != 4) || p->code_flip != 0 || p->bias_data ||
       p->group_size < 32 || p->group_size % 32 || p->group_count * p->group_size < p->col_count ||
-      p->code_bias != (1 << (bits - 1))) {
-    note(s, IGC_FAIL_SUPPORT);
-    return nullptr;
-  }
+      p->code_bias != (1 << (bits - 1)))
+    return plain_plane_of(s, p, key);
   const int g32 = (p->col_count + 31) / 32;
   std::vector<uint16_t> sc((size_t)p->row_count * g32);
   if (igc_scales_f16(p->gain_data, p->gain_type, p->row_count, p->group_count, p->group_size, p->col_count,
-                     sc.data()) != 0) {
-    note(s, IGC_FAIL_SUPPORT);
-    return nullptr;
-  }
+                     sc.data()) != 0)
+    return plain_plane_of(s, p, key);
   DeskPlane dp;
   dp.rows = p->row_count;
   dp.cols = p->col_count;
@@ -119,7 +191,7 @@ const DeskPlane *plane_of(DeskState *s, const igc_plane *p) {
   dp.grid = (dp.n_rb + per_iter - 1) / per_iter;
   if (dp.grid > s->sm_count * 4) dp.grid = s->sm_count * 4;
   dp.tm_ok = igc_lane_tmaps(dp.tiles, dp.scales, dp.n_rb, dp.n_cc, &dp.tm_codes, &dp.tm_scales) == 0;
-  return &(s->planes[p->code_data] = dp);
+  return &(s->planes[key] = dp);
 }
 
 // A device buffer of at least `bytes`, grown (never shrunk) on demand.
@@ -138,6 +210,33 @@ bool room(DeskState *s, T **p, size_t *have, size_t bytes) {
 // reference never passes more than 16; a caller batching many lanes - a
 // prefill chunk, or many streams' blocks - does).
 constexpr int DESK_LANE_GEMM = 64;
+
+// A plain plane's product, 16 lanes a launch: the activations in, one
+// CUDA-core product, the rows out.
+void desk_mat_mat_plain(DeskState *s, const DeskPlane *p, const float *act, int act_stride, int lanes, float *out,
+                        int out_stride) {
+  for (int done = 0; done < lanes;) {
+    const int k = lanes - done < IGC_LANE_LIMIT ? lanes - done : IGC_LANE_LIMIT;
+    if (!grow(s, (size_t)IGC_LANE_LIMIT * (size_t)(p->cols > p->rows ? p->cols : p->rows))) return;
+    for (int j = 0; j < k; ++j)
+      if (!ok(s, cudaMemcpyAsync(s->buf_a + (size_t)j * p->cols, act + (size_t)(done + j) * act_stride,
+                                 sizeof(float) * p->cols, cudaMemcpyHostToDevice, s->st)))
+        return;
+    PlainArgs a = p->plain;
+    a.x = s->buf_a;
+    a.x_stride = p->cols;
+    a.lanes = k;
+    a.out = s->buf_b;
+    a.out_stride = p->rows;
+    if (!ok(s, igc_launch_plain_product(&a, s->sm_count, nullptr, s->st))) return;
+    for (int j = 0; j < k; ++j)
+      if (!ok(s, cudaMemcpyAsync(out + (size_t)(done + j) * out_stride, s->buf_b + (size_t)j * p->rows,
+                                 sizeof(float) * p->rows, cudaMemcpyDeviceToHost, s->st)))
+        return;
+    if (!ok(s, cudaStreamSynchronize(s->st))) return;
+    done += k;
+  }
+}
 
 void desk_mat_mat_lanes(DeskState *s, const DeskPlane *p, const float *act, int act_stride, int lanes, float *out,
                         int out_stride) {
@@ -200,6 +299,7 @@ void desk_mat_mat(igc_desk *d, const igc_plane *sheet, const float *act, int act
   if (cudaSetDevice(s->device) != cudaSuccess) return void(note(s, IGC_FAIL_DEVICE));
   const DeskPlane *p = plane_of(s, sheet);
   if (!p) return;
+  if (p->is_plain) return desk_mat_mat_plain(s, p, act, act_stride, lanes, out, out_stride);
   if (lanes >= DESK_LANE_GEMM) return desk_mat_mat_lanes(s, p, act, act_stride, lanes, out, out_stride);
   for (int done = 0; done < lanes;) {  // app_core.c:5250: chunks of 16 lanes
     int k = lanes - done < IGC_LANE_LIMIT ? lanes - done : IGC_LANE_LIMIT;
@@ -332,6 +432,8 @@ extern "C" void igc_back_close(igc_desk *desk) {
   for (auto &kv : s->planes) {
     cudaFree(kv.second.tiles);
     cudaFree(kv.second.scales);
+    cudaFree(kv.second.plain_data);
+    cudaFree(kv.second.plain_scales);
   }
   cudaFree(s->buf_a);
   cudaFree(s->buf_b);

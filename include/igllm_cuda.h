@@ -114,7 +114,10 @@ struct igc_desk {
 
 /* Replaces app_core.c:5415 back_open.  Each code plane is uploaded to HBM the
  * first time a product names it (keyed by its code pointer) and stays there
- * until igc_back_close.  Unsupported plane forms make the entry return
+ * until igc_back_close.  Codes of 1, 2 or 4 bits with groups of 32k columns
+ * and f16-exact gains go to the int4 tiles; other code planes (8-bit, signed
+ * through their flip, any group) and dense planes stay as stored for a
+ * CUDA-core product.  A plane with zero points makes the entry return
  * without writing and set igc_desk_status to IGC_FAIL_SUPPORT. */
 int igc_back_open(igc_desk *desk, int device);
 /* Replaces app_core.c:5445 back_close. */

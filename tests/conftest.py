@@ -60,6 +60,16 @@ WIDE = dict(TINY, inner=4096, seed=13)
 CACHED = dict(vocab=8192, hidden=512, layers=10, heads=8, kv_heads=1, head_dim=256, inner=1024, ple_dim=64,
               slide_span=64, share_count=4, global_every=5, window_limit=1024, norm_offset=1.0,
               with_layer_scalar=1, seed=17, cache_scale_k=1.0 / 32, cache_scale_v=1.0 / 32)
+# the shipped export's shape: global layers with a head of 512 and the doubled
+# feed-forward on the sharing layers
+EXPORT = dict(CACHED, global_head_dim=512, double_wide=1, seed=29)
+# its stored forms: 2-bit late feed-forward codes, BF16 scales per 64
+# columns, quantized embeddings, the embedding as the head
+STORED = dict(EXPORT, late_mlp_bits=2, group=64, bf16_scales=1, embed_bits=2, ple_embed_bits=4, tied_head=1,
+              seed=31)
+# and the forms the tiles do not hold: 8-bit per-layer input planes, a dense
+# per-layer model projection, activation grids on every projection
+PLAIN = dict(STORED, ple_bits8=1, dense_ple_lift=1, grid_in=0.05, grid_out=0.02, seed=37)
 
 
 def make_checkpoint(lib, folder, cfg):

@@ -29,17 +29,11 @@ CUDA-core products; it is checked the same way.
 import numpy as np
 import pytest
 
-from conftest import CACHED
+from conftest import EXPORT, PLAIN, STORED
 
 pytestmark = pytest.mark.gpu
 
 ATOL = 2e-2
-EXPORT = dict(CACHED, global_head_dim=512, double_wide=1, seed=29)
-STORED = dict(EXPORT, late_mlp_bits=2, group=64, bf16_scales=1, embed_bits=2, ple_embed_bits=4, tied_head=1,
-              seed=31)
-# and the forms the tiles do not hold: 8-bit per-layer input planes, a dense
-# per-layer model projection, activation grids on every projection
-PLAIN = dict(STORED, ple_bits8=1, dense_ple_lift=1, grid_in=0.05, grid_out=0.02, seed=37)
 # the export's own feed-forward width: 6144, doubled to 12288 on the sharing
 # layers (the decode projection then stages its lanes in narrower launches)
 WIDE = dict(EXPORT, inner=6144, seed=41)
