@@ -1003,11 +1003,11 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   }
   __syncthreads();
   // block r merges dimensions [r * DS, (r + 1) * DS) of every row, a thread a
-  // pair of them, blocks in rank order
+  // pair of them (in passes of the block where a block merges more than 32
+  // dimensions), blocks in rank order
   constexpr int DP = DS / 2;
-  static_assert(AT_ROWS * DP <= 256, "one pass of the block");
-  if (tid < AT_ROWS * DP) {
-    const int row = tid / DP, dd = 2 * (tid - row * DP), d = r * DS + dd;
+  for (int it = tid; it < AT_ROWS * DP; it += 256) {
+    const int row = it / DP, dd = 2 * (it - row * DP), d = r * DS + dd;
     float o0 = 0.0f, o1 = 0.0f;
 #pragma unroll
     for (int q = 0; q < CX; ++q) {
@@ -1435,7 +1435,12 @@ extern "C++" {
 template <int HD>
 static cudaError_t allow_attn(int bytes) {
   cudaError_t e = cudaSuccess;
-  if constexpr (HD <= 256) e = allow_smem_fn(attn_kernel<HD, 8>, bytes);  // a 512 head runs in clusters of 16 only
+  if constexpr (HD <= 256) {  // a 512 head runs in clusters of 16 only
+    e = allow_smem_fn(attn_kernel<HD, 1>, bytes);
+    if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 2>, bytes);
+    if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 4>, bytes);
+    if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 8>, bytes);
+  }
   if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 16>, bytes);
   if (e == cudaSuccess) e = cudaFuncSetAttribute(attn_kernel<HD, 16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   return e;
@@ -1650,8 +1655,9 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
                                  int cluster, float *out, int out_stride, float *out_amax, unsigned long long *stamp,
                                  float *const *kc_tab, float *const *vc_tab, const int *pos_tab, int batch,
                                  const igc::CacheStore *store, cudaStream_t st) {
-  if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads || (cluster != 8 && cluster != 16) ||
-      batch < 1 || (batch > 1 && !kc_tab))
+  if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads ||
+      (cluster != 1 && cluster != 2 && cluster != 4 && cluster != 8 && cluster != 16) || batch < 1 ||
+      (batch > 1 && !kc_tab))
     return cudaErrorInvalidValue;
   igc::CacheStore cq = {};
   if (store) cq = *store;
@@ -1661,13 +1667,15 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
   const int G = heads / kv_heads;
   const dim3 grid(cluster, kv_heads * ((lanes * G + AT_ROWS - 1) / AT_ROWS), batch);
   const dim3 grid16(16, grid.y, batch);
-#define IGC_ATT(HD)                                                                                              \
-  return cluster == 8 ? launch_attn<HD, 8>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
-                                           sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,   \
-                                           out_amax, stamp, kc_tab, vc_tab, pos_tab, cq)                          \
-                      : launch_attn<HD, 16>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, \
-                                            sn, eps, owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride,  \
-                                            out_amax, stamp, kc_tab, vc_tab, pos_tab, cq);
+#define IGC_ATT_CX(HD, CX)                                                                                  \
+  launch_attn<HD, CX>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps, owner, kc, vc, \
+                      sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp, kc_tab, vc_tab, pos_tab, cq)
+#define IGC_ATT(HD)                                                                      \
+  return cluster == 1   ? IGC_ATT_CX(HD, 1)                                              \
+         : cluster == 2 ? IGC_ATT_CX(HD, 2)                                              \
+         : cluster == 4 ? IGC_ATT_CX(HD, 4)                                              \
+         : cluster == 8 ? IGC_ATT_CX(HD, 8)                                              \
+                        : IGC_ATT_CX(HD, 16);
   switch (hd) {
     case 32: IGC_ATT(32)
     case 64: IGC_ATT(64)
@@ -1683,6 +1691,7 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
     default: return cudaErrorInvalidValue;
   }
 #undef IGC_ATT
+#undef IGC_ATT_CX
 }
 
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,

@@ -1049,6 +1049,26 @@ struct LaneBuf {
   void *a_tiles = nullptr;
 };
 
+// An attention cluster size from the environment (1, 2, 4, 8 or 16; for
+// comparisons), else `fallback` (0: chosen per launch, attn_cluster_for).
+static int cluster_env(const char *name, int fallback) {
+  const char *v = getenv(name);
+  const int c = v ? atoi(v) : 0;
+  return c == 1 || c == 2 || c == 4 || c == 8 || c == 16 ? c : fallback;
+}
+
+// Blocks a cluster for a lane pass's attention (a prime chunk or a crowd)
+// of `units` clusters (16 query rows of one key/value head each): the fewest
+// that still give about a wave of the SMs.  Each block then walks more tiles
+// and pays its fixed cost (its query rows, the cluster merge) fewer times;
+// measured on a 4096-id prime at E2B widths, 187 ms at 16 blocks a cluster
+// and 115 ms at 1 or 2, and a 64-session crowd round 11.1 ms at 8 and 9.0 at 1.
+static int attn_cluster_for(long units, int sm_count) {
+  int cx = 1;
+  while (cx < 16 && units * cx * 4 < (long)sm_count * 3) cx *= 2;
+  return cx;
+}
+
 struct igc_session {
   igc_model *m = nullptr;
   cudaStream_t st = nullptr;
@@ -1088,6 +1108,9 @@ struct igc_session {
   int *h_top_i = nullptr;
   int logit_lanes = 0;  // rows the last pass left in `logits`
   int attn_cluster = 16;  // attention blocks a cluster, fixed for the session
+  // blocks a cluster of a prime chunk's attention on sliding and on global
+  // layers (0: attn_cluster_for)
+  int chunk_cluster = 0, chunk_cluster_global = 0;
   int use_graphs = 1;
   int use_pdl = 1;
   int use_stamps = 1;  // IGC_NO_STAMPS=1 launches without launch stamps (for comparison)
@@ -1325,6 +1348,8 @@ extern "C" int igc_session_open(igc_model *m, igc_session **out) {
   // unless IGC_ATTN_CLUSTER=8 or the heads' magnitude partials would not fit
   const char *ac = getenv("IGC_ATTN_CLUSTER");
   s->attn_cluster = (ac && atoi(ac) == 8) || m->heads * 16 > GEMV_PART_LIMIT ? 8 : 16;
+  s->chunk_cluster = cluster_env("IGC_CHUNK_CLUSTER", 0);
+  s->chunk_cluster_global = cluster_env("IGC_CHUNK_CLUSTER_GLOBAL", s->chunk_cluster);
   *out = s.release();
   return IGC_OKAY;
 }
@@ -2071,6 +2096,10 @@ static int enqueue_chunk(igc_session *s, int M, bool head, bool want) {
     const int owner = L.share ? L.source : l;
     const DevLayer &O = m->layer[owner];
     const int full = M / 16, tail = M - 16 * full, sliding = L.kind == 0 ? 1 : 0;
+    const int G = m->heads / O.kv_heads;
+    const int cx_set = sliding ? s->chunk_cluster : s->chunk_cluster_global;
+    const int cx = cx_set ? cx_set : attn_cluster_for((long)(full > 0 ? full : 1) * O.kv_heads * ((16 * G + 15) / 16),
+                                                      m->sm_count);
     igc_kernels_pdl(0);
     const CacheStore kv = layer_store(m, owner, s->d_peak + 2 * owner);
     if (!L.share)
@@ -2085,13 +2114,13 @@ static int enqueue_chunk(igc_session *s, int M, bool head, bool want) {
     if (full > 0)
       CKL(igc_launch_attn_many(C.B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding,
-                               m->slide_span, C.d_pos, 16, s->attn_cluster, C.B.attn, L.q_rows, nullptr, nullptr,
+                               m->slide_span, C.d_pos, 16, cx, C.B.attn, L.q_rows, nullptr, nullptr,
                                C.kc_tab + (size_t)l * C.groups_cap, C.vc_tab + (size_t)l * C.groups_cap, C.d_pos,
                                full, nullptr, s->st));
     if (tail > 0)
       CKL(igc_launch_attn(C.B.qkv + (size_t)16 * full * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
                           L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, attn_rows(s, owner, 0),
-                          attn_rows(s, owner, 1), sliding, m->slide_span, C.d_pos + full, tail, s->attn_cluster,
+                          attn_rows(s, owner, 1), sliding, m->slide_span, C.d_pos + full, tail, cx,
                           C.B.attn + (size_t)16 * full * L.q_rows, L.q_rows, nullptr, nullptr, nullptr, s->st));
     igc_kernels_pdl(s->use_pdl != 0);
     return IGC_OKAY;
@@ -2564,12 +2593,12 @@ extern "C" int igc_session_load(igc_session *s, const char *path, uint64_t *stam
 
 // Attention blocks a cluster in a crowd round: with many sessions in one
 // launch, clusters of 8 take half the blocks (and waves) clusters of 16 do.
-constexpr int IGC_CROWD_CLUSTER = 8;
 
 struct igc_crowd {
   igc_model *m = nullptr;
   cudaStream_t st = nullptr;
   int cap = 0, k = 0, lanes = 0;
+  int cluster = 0;  // attention blocks a cluster (0: attn_cluster_for)
   LaneBuf B;
   // device: [ids: lanes][pos: cap] then per layer and session [caches: key, value][peaks][the float rows
   // attention reads: key, value], mirrored in pinned host memory
@@ -2615,6 +2644,7 @@ extern "C" int igc_crowd_open(igc_model *m, int session_limit, int lanes_per_ses
   cr->m = m;
   cr->cap = session_limit;
   cr->k = lanes_per_session;
+  cr->cluster = cluster_env("IGC_CROWD_CLUSTER", 0);
   cr->lanes = session_limit * lanes_per_session;
   CK(cudaStreamCreateWithFlags(&cr->st, cudaStreamNonBlocking));
   int c = lane_buf_alloc(m, cr->B, cr->lanes, cr->lanes, cr->owned);
@@ -2650,11 +2680,14 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
     const DevLayer &O = m->layer[owner];
     const int sliding = L.kind == 0 ? 1 : 0;
     const size_t at = (size_t)l * cr->cap;
+    const int cx = cr->cluster ? cr->cluster
+                               : attn_cluster_for((long)S * O.kv_heads * ((k * (m->heads / O.kv_heads) + 15) / 16),
+                                                  m->sm_count);
     if (!layer_split(m, l)) {
       const CacheStore cq = layer_store(m, owner, nullptr, L.share ? nullptr : cr->pk() + at);
       CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr,
-                               sliding, m->slide_span, cr->pos(), k, IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr,
+                               sliding, m->slide_span, cr->pos(), k, cx, cr->B.attn, L.q_rows, nullptr,
                                nullptr, cr->kc() + at, cr->vc() + at, cr->pos(), S, &cq, cr->st));
       return IGC_OKAY;
     }
@@ -2670,7 +2703,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
     if (!layer_bytes(m, owner)) {
       CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding,
-                               m->slide_span, cr->pos(), k, IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr, nullptr,
+                               m->slide_span, cr->pos(), k, cx, cr->B.attn, L.q_rows, nullptr, nullptr,
                                cr->kc() + at, cr->vc() + at, cr->pos(), S, nullptr, cr->st));
       igc_kernels_pdl(1);
       return IGC_OKAY;
@@ -2691,7 +2724,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
     CKL(igc_launch_lane_widen(&w, S, widen_rows_most(m, sliding, k), m->sm_count, cr->st));
     CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                              m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding, m->slide_span, cr->pos(), k,
-                             IGC_CROWD_CLUSTER, cr->B.attn, L.q_rows, nullptr, nullptr, cr->kf() + at, cr->vf() + at,
+                             cx, cr->B.attn, L.q_rows, nullptr, nullptr, cr->kf() + at, cr->vf() + at,
                              cr->pos(), S, nullptr, cr->st));
     igc_kernels_pdl(1);
     return IGC_OKAY;
