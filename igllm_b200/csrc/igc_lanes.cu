@@ -427,12 +427,8 @@ __device__ __forceinline__ float block_max(float v, float *red) {
   return t;
 }
 
-// The producer's output row of lane j: its K-slice partials added in order.
-__device__ __forceinline__ float slice_sum(const LaneStageArgs &a, int j, int i) {
-  float s = 0.0f;
-  for (int z = 0; z < a.p_splits; ++z) s += a.p[((size_t)z * a.lanes + j) * a.p_stride + i];
-  return s;
-}
+// Columns a thread of the stage takes a step (see lane_stage_kernel).
+constexpr int LS_U = 4;
 
 __global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
   extern __shared__ float ls_row[];  // the lane's staged values (cols floats), then the residual's
@@ -442,34 +438,114 @@ __global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
   const int j = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   float *y = ls_row;
   const int n = a.cols;
+  // Each thread takes columns tid, tid + nt, ... as before, LS_U of them a
+  // step with every global load of the step issued before any is used (the
+  // loads of one lane's row are independent; issuing them together keeps
+  // several in flight instead of one).  The order of every sum is unchanged.
+  constexpr int U = LS_U;
   if (a.mode == LS_PLAIN || a.mode == LS_NORM) {
-    for (int i = tid; i < n; i += nt) y[i] = a.x[(size_t)j * a.x_stride + i];
+    const float *xr = a.x + (size_t)j * a.x_stride;
+    for (int i0 = tid; i0 < n; i0 += U * nt) {
+      float v[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) v[k] = i0 + k * nt < n ? xr[i0 + k * nt] : 0.0f;
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (i0 + k * nt < n) y[i0 + k * nt] = v[k];
+    }
   } else if (a.mode == LS_GELU_PAIR) {
     // app_core.c:11673 gelu(gate) * up: the pair plane interleaves 16-row
     // blocks of gate and up rows
-    for (int i = tid; i < n; i += nt) {
-      const int gi = (i >> 4) * 32 + (i & 15);
-      y[i] = gelu_tanh(slice_sum(a, j, gi)) * slice_sum(a, j, gi + 16);
+    for (int i0 = tid; i0 < n; i0 += U * nt) {
+      float g[U], u[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) g[k] = u[k] = 0.0f;
+      for (int z = 0; z < a.p_splits; ++z) {
+        const float *pz = a.p + ((size_t)z * a.lanes + j) * a.p_stride;
+        float gv[U], uv[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          const int i = i0 + k * nt, gi = (i >> 4) * 32 + (i & 15);
+          gv[k] = i < n ? pz[gi] : 0.0f;
+          uv[k] = i < n ? pz[gi + 16] : 0.0f;
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+          g[k] += gv[k];
+          u[k] += uv[k];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (i0 + k * nt < n) y[i0 + k * nt] = gelu_tanh(g[k]) * u[k];
     }
   } else if (a.mode == LS_GELU_MUL) {
     // app_core.c:11723: gelu(gate) times the layer's per-layer input
-    for (int i = tid; i < n; i += nt) y[i] = gelu_tanh(slice_sum(a, j, i)) * a.aux[(size_t)j * a.aux_stride + i];
+    const float *ar = a.aux + (size_t)j * a.aux_stride;
+    for (int i0 = tid; i0 < n; i0 += U * nt) {
+      float g[U], m[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        g[k] = 0.0f;
+        m[k] = i0 + k * nt < n ? ar[i0 + k * nt] : 0.0f;
+      }
+      for (int z = 0; z < a.p_splits; ++z) {
+        const float *pz = a.p + ((size_t)z * a.lanes + j) * a.p_stride;
+        float gv[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) gv[k] = i0 + k * nt < n ? pz[i0 + k * nt] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < U; ++k) g[k] += gv[k];
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (i0 + k * nt < n) y[i0 + k * nt] = gelu_tanh(g[k]) * m[k];
+    }
   } else {
     // LS_RESID, LS_RESID_NORM (app_core.c:11690-11740): x += norm(p) * w_res,
     // then the layer gain; the new stream is written back
     float *pr = ls_row + n;
     float ss = 0.0f;
-    for (int i = tid; i < n; i += nt) {
-      const float v = slice_sum(a, j, i);
-      pr[i] = v;
-      ss += v * v;
+    for (int i0 = tid; i0 < n; i0 += U * nt) {
+      float v[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) v[k] = 0.0f;
+      for (int z = 0; z < a.p_splits; ++z) {
+        const float *pz = a.p + ((size_t)z * a.lanes + j) * a.p_stride;
+        float pv[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) pv[k] = i0 + k * nt < n ? pz[i0 + k * nt] : 0.0f;
+#pragma unroll
+        for (int k = 0; k < U; ++k) v[k] += pv[k];
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k)
+        if (i0 + k * nt < n) {
+          pr[i0 + k * nt] = v[k];
+          ss += v[k] * v[k];
+        }
     }
     const float sp = rms_shrink(block_sum(ss, red), n, a.eps);
-    for (int i = tid; i < n; i += nt) {
-      float v = a.x[(size_t)j * a.x_stride + i] + pr[i] * sp * a.w_res[i];
-      if (a.gain != 1.0f) v *= a.gain;
-      y[i] = v;
-      a.x_out[(size_t)j * a.x_stride + i] = v;
+    const float *xr = a.x + (size_t)j * a.x_stride;
+    float *xo = a.x_out + (size_t)j * a.x_stride;
+    for (int i0 = tid; i0 < n; i0 += U * nt) {
+      float xv[U], wv[U];
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const bool in = i0 + k * nt < n;
+        xv[k] = in ? xr[i0 + k * nt] : 0.0f;
+        wv[k] = in ? a.w_res[i0 + k * nt] : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < U; ++k) {
+        const int i = i0 + k * nt;
+        if (i < n) {
+          float v = xv[k] + pr[i] * sp * wv[k];
+          if (a.gain != 1.0f) v *= a.gain;
+          y[i] = v;
+          xo[i] = v;
+        }
+      }
     }
   }
   if (a.mode == LS_NORM || a.mode == LS_RESID_NORM) {
