@@ -522,14 +522,19 @@ constexpr int AT_DEPTH = 3;        // tiles in flight a block
 constexpr int AT_SRED = 24;        // row stride of the score partials and weights
 constexpr int AT_MAX_CLUSTER = 16;
 
-template <int HD>
+template <int HD, bool LITE = false>
 struct AttnLayout {                  // offsets in floats
   // A head of 512 (the export's global layers) keeps two tiles in flight and
   // reads the pass's new rows through the tiles like any cached row (they are
   // in the cache before it runs, written by lane_kv_kernel); narrower heads
-  // keep three and hold the pass's new rows apart, computed here.
-  static constexpr int DEPTH = HD > 256 ? 2 : AT_DEPTH;
-  static constexpr bool NEW_ROWS = HD <= 256;
+  // keep three and hold the pass's new rows apart, computed here.  The light
+  // layout (lane passes, whose new rows are all in the cache before the
+  // launch) reads them through the tiles too, keeps two tiles in flight and
+  // puts the cluster's pushed values in the ring once every block of the
+  // cluster is past its tiles: about 100 KB at a head of 256, so two blocks
+  // share an SM.
+  static constexpr int DEPTH = (HD > 256 || LITE) ? 2 : AT_DEPTH;
+  static constexpr bool NEW_ROWS = HD <= 256 && !LITE;
   static constexpr int KS = HD + 8;  // key rows: a half-warp's float2 reads meet 32 banks
   static constexpr int VS = HD + 4;  // value rows: a warp's scalar reads meet 32 banks
   static constexpr int QS = HD + 4;
@@ -541,12 +546,13 @@ struct AttnLayout {                  // offsets in floats
   static constexpr int O_SRED = O_ZERO + KS;                    // [8 warps][16][AT_SRED]
   static constexpr int O_P = O_SRED + 8 * AT_ROWS * AT_SRED;    // hi, lo weights: 2 x [16][AT_SRED] halves
   static constexpr int O_F = O_P + AT_ROWS * AT_SRED;
-  static constexpr int O_RO = O_F + AT_ROWS;              // pushed values: [sender][16][hd / CX]
-  static constexpr int O_RML = O_RO + AT_ROWS * HD;         // pushed maxima, totals: [sender][16][2]
+  static constexpr int O_RO = LITE ? 0 : O_F + AT_ROWS;   // pushed values: [sender][16][hd / CX]
+  static constexpr int O_RML = LITE ? O_F + AT_ROWS : O_RO + AT_ROWS * HD;  // pushed maxima, totals: [sender][16][2]
   static constexpr int O_W = O_RML + 2 * AT_ROWS * AT_MAX_CLUSTER;  // merge weights [16][16]
   static constexpr int O_LINV = O_W + AT_ROWS * AT_MAX_CLUSTER;
   static constexpr int O_AMX = O_LINV + AT_ROWS;
   static constexpr int FLOATS = O_AMX + AT_ROWS;
+  static_assert(!LITE || AT_ROWS * HD <= DEPTH * TILE, "pushed values fit the ring");
 };
 
 template <int DPL>
@@ -675,7 +681,7 @@ __device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_
   lo = *reinterpret_cast<const uint32_t *>(&r);
 }
 
-template <int HD, int CX>
+template <int HD, int CX, bool LITE = false>
 __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_stride, int heads, int kv_heads,
                                                    const float *q_norm, const float *k_norm, const float *cs_tab,
                                                    const float *sn_tab, float eps, int owner, float *kc, float *vc,
@@ -683,7 +689,7 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
                                                    int out_stride, float *out_amax, unsigned long long *stamp,
                                                    float *const *kc_tab, float *const *vc_tab, const int *pos_tab,
                                                    CacheStore cq) {
-  using LY = AttnLayout<HD>;
+  using LY = AttnLayout<HD, LITE>;
   float *peak = cq.peak;
   if (kc_tab) {
     // one of many sessions' blocks (blockIdx.z): its caches, peaks and
@@ -867,6 +873,14 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   // i - 1 left and the softmax, then (barrier, after which tile i + 1 is in
   // place: one commit group a step keeps the count regular) the values
   for (int i = 0; i < n_tiles; ++i) {
+    if constexpr (LITE) {
+      // tile i, issued a step ago, in place (its copy ran under the values
+      // of tile i - 1)
+      if (i > 0) {
+        cp_async_wait<0>();
+        __syncthreads();
+      }
+    }
     const int tb = (t0 + i * CX) * AT_POS;
     const float *slot = ring + (i % LY::DEPTH) * LY::TILE;
     // a position's key and value rows: new, cached, or zeros outside the pass's span
@@ -936,8 +950,8 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
     ph[sr * AT_SRED + sp] = eh;
     pl[sr * AT_SRED + sp] = __float2half_rn(e - __half2float(eh));
     if (sp == 0) fsc[sr] = fct;
-    cp_async_wait<LY::DEPTH - 2>();  // this thread's copies of tile i + 1 (all but the newest group)
-    __syncthreads();     // the weights and factors are written; tile i + 1 is in place
+    if constexpr (!LITE) cp_async_wait<LY::DEPTH - 2>();  // this thread's copies of tile i + 1 (all but the newest group)
+    __syncthreads();     // the weights and factors are written; tile i + 1 is in place (light: in flight)
     // weighted values: this warp's 8-dimension tiles n = warp + 8 i
     {
       const uint32_t *h32 = reinterpret_cast<const uint32_t *>(ph), *l32 = reinterpret_cast<const uint32_t *>(pl);
@@ -972,6 +986,12 @@ __global__ void __launch_bounds__(256) attn_kernel(const float *qkv, int qkv_str
   // values of dimensions [q DS, (q + 1) DS) to block q, and every row's
   // maximum and total to every block (remote stores into buffers nothing
   // else uses, made visible by the cluster barrier)
+  if constexpr (LITE) {
+    // the pushed values land in the ring: every block of the cluster first
+    // finishes with its tiles
+    cp_async_wait<0>();
+    cluster_sync();
+  }
 #pragma unroll
   for (int i2 = 0; i2 < NPW; ++i2) {
     const int nt = warp + 8 * i2;
@@ -1436,7 +1456,10 @@ template <int HD>
 static cudaError_t allow_attn(int bytes) {
   cudaError_t e = cudaSuccess;
   if constexpr (HD <= 256) {  // a 512 head runs in clusters of 16 only
-    e = allow_smem_fn(attn_kernel<HD, 1>, bytes);
+    e = allow_smem_fn(attn_kernel<HD, 1, true>, bytes);
+    if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 2, true>, bytes);
+    if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 4, true>, bytes);
+    if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 1>, bytes);
     if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 2>, bytes);
     if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 4>, bytes);
     if (e == cudaSuccess) e = allow_smem_fn(attn_kernel<HD, 8>, bytes);
@@ -1600,6 +1623,16 @@ cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes
                   blend, out);
 }
 
+size_t igc_attn_smem_light(int hd) {
+  switch (hd) {
+    case 32: return sizeof(float) * AttnLayout<32, true>::FLOATS;
+    case 64: return sizeof(float) * AttnLayout<64, true>::FLOATS;
+    case 128: return sizeof(float) * AttnLayout<128, true>::FLOATS;
+    case 256: return sizeof(float) * AttnLayout<256, true>::FLOATS;
+    default: return 0;
+  }
+}
+
 size_t igc_attn_smem(int hd) {
   switch (hd) {
     case 32: return sizeof(float) * AttnLayout<32>::FLOATS;
@@ -1612,7 +1645,7 @@ size_t igc_attn_smem(int hd) {
 }
 
 extern "C++" {
-template <int HD, int CX>
+template <int HD, int CX, bool LITE = false>
 static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const float *qkv, int qkv_stride, int heads,
                                int kv_heads, const float *q_norm, const float *k_norm, const float *cs,
                                const float *sn, float eps, int owner, float *kc, float *vc, int sliding, int span,
@@ -1633,7 +1666,7 @@ static cudaError_t launch_attn(dim3 grid, size_t smem, cudaStream_t st, const fl
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = g_pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, CX>, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
+  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, CX, LITE>, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps,
                             owner, kc, vc, sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp, kc_tab,
                             vc_tab, pos_tab, cq);
 }
@@ -1643,10 +1676,10 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
                             int out_stride, float *out_amax, unsigned long long *stamp, const igc::CacheStore *store,
-                            cudaStream_t st) {
+                            cudaStream_t st, int light) {
   return igc_launch_attn_many(qkv, qkv_stride, heads, kv_heads, hd, q_norm, k_norm, cs, sn, eps, owner, kc, vc, sliding,
                               span, d_p0, lanes, cluster, out, out_stride, out_amax, stamp, nullptr, nullptr, nullptr, 1,
-                              store, st);
+                              store, st, light);
 }
 
 cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
@@ -1654,7 +1687,7 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
                                  int owner, float *kc, float *vc, int sliding, int span, const int *d_p0, int lanes,
                                  int cluster, float *out, int out_stride, float *out_amax, unsigned long long *stamp,
                                  float *const *kc_tab, float *const *vc_tab, const int *pos_tab, int batch,
-                                 const igc::CacheStore *store, cudaStream_t st) {
+                                 const igc::CacheStore *store, cudaStream_t st, int light) {
   if (lanes < 1 || lanes > AT_POS || kv_heads < 1 || heads % kv_heads ||
       (cluster != 1 && cluster != 2 && cluster != 4 && cluster != 8 && cluster != 16) || batch < 1 ||
       (batch > 1 && !kc_tab))
@@ -1663,19 +1696,27 @@ cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, in
   if (store) cq = *store;
   // float caches only: a byte side is decoded into float rows first (igc_launch_lane_widen)
   if (cq.kq != 0.0f || cq.vq != 0.0f || (cq.peak_tab && !kc_tab)) return cudaErrorInvalidValue;
-  const size_t smem = igc_attn_smem(hd);
+  // the light layout (two blocks an SM) where asked for and possible: no
+  // new rows to write (every row of the pass already in the cache), a head
+  // of at most 256, clusters of at most 4
+  const bool lite = light && !owner && hd <= 256 && cluster <= 4;
+  const size_t smem = lite ? igc_attn_smem_light(hd) : igc_attn_smem(hd);
   const int G = heads / kv_heads;
   const dim3 grid(cluster, kv_heads * ((lanes * G + AT_ROWS - 1) / AT_ROWS), batch);
   const dim3 grid16(16, grid.y, batch);
-#define IGC_ATT_CX(HD, CX)                                                                                  \
-  launch_attn<HD, CX>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps, owner, kc, vc, \
-                      sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp, kc_tab, vc_tab, pos_tab, cq)
+#define IGC_ATT_CX(HD, CX, L)                                                                                  \
+  launch_attn<HD, CX, L>(grid, smem, st, qkv, qkv_stride, heads, kv_heads, q_norm, k_norm, cs, sn, eps, owner, kc, vc, \
+                         sliding, span, d_p0, lanes, out, out_stride, out_amax, stamp, kc_tab, vc_tab, pos_tab, cq)
 #define IGC_ATT(HD)                                                                      \
-  return cluster == 1   ? IGC_ATT_CX(HD, 1)                                              \
-         : cluster == 2 ? IGC_ATT_CX(HD, 2)                                              \
-         : cluster == 4 ? IGC_ATT_CX(HD, 4)                                              \
-         : cluster == 8 ? IGC_ATT_CX(HD, 8)                                              \
-                        : IGC_ATT_CX(HD, 16);
+  if (lite)                                                                              \
+    return cluster == 1 ? IGC_ATT_CX(HD, 1, true)                                        \
+           : cluster == 2 ? IGC_ATT_CX(HD, 2, true)                                      \
+                          : IGC_ATT_CX(HD, 4, true);                                     \
+  return cluster == 1   ? IGC_ATT_CX(HD, 1, false)                                       \
+         : cluster == 2 ? IGC_ATT_CX(HD, 2, false)                                       \
+         : cluster == 4 ? IGC_ATT_CX(HD, 4, false)                                       \
+         : cluster == 8 ? IGC_ATT_CX(HD, 8, false)                                       \
+                        : IGC_ATT_CX(HD, 16, false);
   switch (hd) {
     case 32: IGC_ATT(32)
     case 64: IGC_ATT(64)

@@ -39,6 +39,8 @@ cudaError_t igc_launch_embed(const int32_t *ids, int lanes, const uint16_t *embe
 cudaError_t igc_launch_ple_finish(const float *raw, const float *seed, int lanes, int layers, int ple_dim,
                                   const float *w, float eps, float blend, float *out, cudaStream_t st);
 size_t igc_attn_smem(int hd);
+// The light layout's (igc_launch_attn_many with `light`): heads of at most 256.
+size_t igc_attn_smem_light(int hd);
 // Attention for one layer in one kernel (query norm and rope, an owner
 // layer's cache writes, scores, softmax and values over 16-position tiles,
 // and the merge of the cluster's partials); `cluster` (8 or 16) blocks a
@@ -50,17 +52,20 @@ cudaError_t igc_launch_attn(const float *qkv, int qkv_stride, int heads, int kv_
                             const float *k_norm, const float *cs, const float *sn, float eps, int owner, float *kc,
                             float *vc, int sliding, int span, const int *d_p0, int lanes, int cluster, float *out,
                             int out_stride, float *out_amax, unsigned long long *stamp, const igc::CacheStore *store,
-                            cudaStream_t st);
+                            cudaStream_t st, int light = 0);
 // The same for `batch` sessions' blocks of `lanes` lanes each in one launch
 // (blockIdx.z the session): session z's caches are kc_tab[z] / vc_tab[z],
 // its first position pos_tab[z], its rows of q|k|v and of the output follow
-// the sessions before it.
+// the sessions before it.  `light` asks for the layout with two tiles in
+// flight and no room for new rows (two blocks an SM), taken where no new
+// rows are written (owner 0), the head is at most 256 wide and clusters are
+// of at most 4 blocks; otherwise ignored.
 cudaError_t igc_launch_attn_many(const float *qkv, int qkv_stride, int heads, int kv_heads, int hd,
                                  const float *q_norm, const float *k_norm, const float *cs, const float *sn, float eps,
                                  int owner, float *kc, float *vc, int sliding, int span, const int *d_p0, int lanes,
                                  int cluster, float *out, int out_stride, float *out_amax, unsigned long long *stamp,
                                  float *const *kc_tab, float *const *vc_tab, const int *pos_tab, int batch,
-                                 const igc::CacheStore *store, cudaStream_t st);
+                                 const igc::CacheStore *store, cudaStream_t st, int light = 0);
 // `stamp_sum`, when given, gets each of the pass's `stamp_n` stamped launches'
 // spans added (igc_device.cuh stamp_begin / stamp_end).
 cudaError_t igc_launch_argmax(const float *part_val, const int *part_idx, int parts, int lanes, int32_t *top,

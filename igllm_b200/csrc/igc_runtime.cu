@@ -1063,6 +1063,14 @@ static int cluster_env(const char *name, int fallback) {
 // and pays its fixed cost (its query rows, the cluster merge) fewer times;
 // measured on a 4096-id prime at E2B widths, 187 ms at 16 blocks a cluster
 // and 115 ms at 1 or 2, and a 64-session crowd round 11.1 ms at 8 and 9.0 at 1.
+// Whether lane passes ask for the light attention layout (two blocks an SM
+// where a pass writes no new rows; IGC_NO_LIGHT=1 leaves it out, for
+// comparison).
+static int attn_light() {
+  static const char *off = getenv("IGC_NO_LIGHT");
+  return off && off[0] == '1' ? 0 : 1;
+}
+
 static int attn_cluster_for(long units, int sm_count) {
   int cx = 1;
   while (cx < 16 && units * cx * 4 < (long)sm_count * 3) cx *= 2;
@@ -2116,12 +2124,13 @@ static int enqueue_chunk(igc_session *s, int M, bool head, bool want) {
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding,
                                m->slide_span, C.d_pos, 16, cx, C.B.attn, L.q_rows, nullptr, nullptr,
                                C.kc_tab + (size_t)l * C.groups_cap, C.vc_tab + (size_t)l * C.groups_cap, C.d_pos,
-                               full, nullptr, s->st));
+                               full, nullptr, s->st, attn_light()));
     if (tail > 0)
       CKL(igc_launch_attn(C.B.qkv + (size_t)16 * full * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
                           L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, attn_rows(s, owner, 0),
                           attn_rows(s, owner, 1), sliding, m->slide_span, C.d_pos + full, tail, cx,
-                          C.B.attn + (size_t)16 * full * L.q_rows, L.q_rows, nullptr, nullptr, nullptr, s->st));
+                          C.B.attn + (size_t)16 * full * L.q_rows, L.q_rows, nullptr, nullptr, nullptr, s->st,
+                          attn_light()));
     igc_kernels_pdl(s->use_pdl != 0);
     return IGC_OKAY;
   };
@@ -2688,7 +2697,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
       CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, L.share ? 0 : 1, nullptr, nullptr,
                                sliding, m->slide_span, cr->pos(), k, cx, cr->B.attn, L.q_rows, nullptr,
-                               nullptr, cr->kc() + at, cr->vc() + at, cr->pos(), S, &cq, cr->st));
+                               nullptr, cr->kc() + at, cr->vc() + at, cr->pos(), S, &cq, cr->st, attn_light()));
       return IGC_OKAY;
     }
     // every session's new rows written first (onto the grid on a byte
@@ -2704,7 +2713,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
       CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
                                m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding,
                                m->slide_span, cr->pos(), k, cx, cr->B.attn, L.q_rows, nullptr, nullptr,
-                               cr->kc() + at, cr->vc() + at, cr->pos(), S, nullptr, cr->st));
+                               cr->kc() + at, cr->vc() + at, cr->pos(), S, nullptr, cr->st, attn_light()));
       igc_kernels_pdl(1);
       return IGC_OKAY;
     }
@@ -2725,7 +2734,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
     CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm, m->rope_cs[L.kind],
                              m->rope_sn[L.kind], m->eps, 0, nullptr, nullptr, sliding, m->slide_span, cr->pos(), k,
                              cx, cr->B.attn, L.q_rows, nullptr, nullptr, cr->kf() + at, cr->vf() + at,
-                             cr->pos(), S, nullptr, cr->st));
+                             cr->pos(), S, nullptr, cr->st, attn_light()));
     igc_kernels_pdl(1);
     return IGC_OKAY;
   };
