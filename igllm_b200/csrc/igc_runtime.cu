@@ -1057,12 +1057,6 @@ static int cluster_env(const char *name, int fallback) {
   return c == 1 || c == 2 || c == 4 || c == 8 || c == 16 ? c : fallback;
 }
 
-// Blocks a cluster for a lane pass's attention (a prime chunk or a crowd)
-// of `units` clusters (16 query rows of one key/value head each): the fewest
-// that still give about a wave of the SMs.  Each block then walks more tiles
-// and pays its fixed cost (its query rows, the cluster merge) fewer times;
-// measured on a 4096-id prime at E2B widths, 187 ms at 16 blocks a cluster
-// and 115 ms at 1 or 2, and a 64-session crowd round 11.1 ms at 8 and 9.0 at 1.
 // Whether lane passes ask for the light attention layout (two blocks an SM
 // where a pass writes no new rows; IGC_NO_LIGHT=1 leaves it out, for
 // comparison).
@@ -1071,9 +1065,17 @@ static int attn_light() {
   return off && off[0] == '1' ? 0 : 1;
 }
 
-static int attn_cluster_for(long units, int sm_count) {
+// Blocks a cluster for a lane pass's attention (a prime chunk or a crowd)
+// of `units` clusters (16 query rows of one key/value head each): the fewest
+// that still give about a wave of `slots` blocks (the SMs, twice over where
+// the light layout lets two blocks share an SM).  Each block then walks more
+// tiles and pays its fixed cost (its query rows, the cluster merge) fewer
+// times.  Measured at E2B widths: a 4096-id prime took 187 ms at 16 blocks a
+// cluster and 115 ms at 1 or 2; a 64-session crowd round took 11.1 ms at 8
+// and 9.0 at 1, and with the light layout 7.9 at 1 and 7.7 at 2.
+static int attn_cluster_for(long units, int slots) {
   int cx = 1;
-  while (cx < 16 && units * cx * 4 < (long)sm_count * 3) cx *= 2;
+  while (cx < 16 && units * cx * 4 < (long)slots * 3) cx *= 2;
   return cx;
 }
 
@@ -2107,7 +2109,7 @@ static int enqueue_chunk(igc_session *s, int M, bool head, bool want) {
     const int G = m->heads / O.kv_heads;
     const int cx_set = sliding ? s->chunk_cluster : s->chunk_cluster_global;
     const int cx = cx_set ? cx_set : attn_cluster_for((long)(full > 0 ? full : 1) * O.kv_heads * ((16 * G + 15) / 16),
-                                                      m->sm_count);
+                                                      m->sm_count * (attn_light() ? 2 : 1));
     igc_kernels_pdl(0);
     const CacheStore kv = layer_store(m, owner, s->d_peak + 2 * owner);
     if (!L.share)
@@ -2691,7 +2693,7 @@ static int enqueue_crowd(igc_crowd *cr, int S, bool rows) {
     const size_t at = (size_t)l * cr->cap;
     const int cx = cr->cluster ? cr->cluster
                                : attn_cluster_for((long)S * O.kv_heads * ((k * (m->heads / O.kv_heads) + 15) / 16),
-                                                  m->sm_count);
+                                                  m->sm_count * (attn_light() ? 2 : 1));
     if (!layer_split(m, l)) {
       const CacheStore cq = layer_store(m, owner, nullptr, L.share ? nullptr : cr->pk() + at);
       CKL(igc_launch_attn_many(cr->B.qkv, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm, L.k_norm,
