@@ -438,10 +438,11 @@ __global__ void __launch_bounds__(256) lane_stage_kernel(LaneStageArgs a) {
   const int j = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
   float *y = ls_row;
   const int n = a.cols;
-  // Each thread takes columns tid, tid + nt, ... as before, LS_U of them a
-  // step with every global load of the step issued before any is used (the
+  // Each thread takes columns tid, tid + nt, tid + 2 nt, ..., LS_U of them a
+  // step, with every global load of the step issued before any is used (the
   // loads of one lane's row are independent; issuing them together keeps
-  // several in flight instead of one).  The order of every sum is unchanged.
+  // several in flight).  Each thread still adds its columns in increasing
+  // order, so every sum is the one a column-at-a-time loop forms.
   constexpr int U = LS_U;
   if (a.mode == LS_PLAIN || a.mode == LS_NORM) {
     const float *xr = a.x + (size_t)j * a.x_stride;
