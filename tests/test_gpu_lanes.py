@@ -97,6 +97,33 @@ def test_chunked_prime_matches_the_checker(igc_lib, igo_mod, which, tiny_dir, sm
     close(row, o.step(9))
 
 
+def test_prime_attention_at_every_cluster_size(igc_lib, igo_mod, small_dir, monkeypatch):
+    """A prime chunk's attention splits each 16-row block's positions over a
+    cluster of 1, 2, 4, 8 or 16 blocks (the light layout, two blocks an SM,
+    at up to 4); every size must leave caches that give the checker's logits
+    within 2e-2 and 2e-4 of the row's magnitude.  Only the split of the sums
+    over positions changes with the size."""
+    from conftest import SMALL
+    cfg = SMALL
+    m = igc_lib.Model(folder=small_dir, window_limit=cfg["window_limit"])
+    om = igo_mod.OracleModel(small_dir, window_limit=cfg["window_limit"])
+    o = igo_mod.OracleSession(om, threads=8)
+    rng = np.random.default_rng(47)
+    n = min(cfg["window_limit"] - 8, 300)
+    ids = rng.integers(0, cfg["vocab"], n).astype(np.int32)
+    o.prime(ids)
+    want = o.step(ids[-1])
+    for cx in (1, 2, 4, 8, 16):
+        monkeypatch.setenv("IGC_CHUNK_CLUSTER", str(cx))
+        monkeypatch.setenv("IGC_CHUNK_CLUSTER_GLOBAL", str(cx))
+        s = igc_lib.Session(m)  # the sizes are read when a session opens
+        s.prime(ids)
+        _, row = s.step(ids[-1])
+        err = float(np.abs(row - want).max())
+        assert err <= 2e-2 and err <= 2e-4 * max(1.0, float(np.abs(want).max())), (cx, err)
+        s.close()
+
+
 def test_crowd_round_matches_each_session_alone(igc_lib, small_dir):
     """Five sessions at different positions verify a block of four in one
     crowd round: every lane's logits agree with the session's own guess (the
