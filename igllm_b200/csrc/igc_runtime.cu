@@ -2108,8 +2108,10 @@ static int enqueue_chunk(igc_session *s, int M, bool head, bool want) {
     const int full = M / 16, tail = M - 16 * full, sliding = L.kind == 0 ? 1 : 0;
     const int G = m->heads / O.kv_heads;
     const int cx_set = sliding ? s->chunk_cluster : s->chunk_cluster_global;
-    const int cx = cx_set ? cx_set : attn_cluster_for((long)(full > 0 ? full : 1) * O.kv_heads * ((16 * G + 15) / 16),
-                                                      m->sm_count * (attn_light() ? 2 : 1));
+    const int slots = m->sm_count * (attn_light() ? 2 : 1);
+    const int cx = cx_set ? cx_set : attn_cluster_for((long)(full > 0 ? full : 1) * O.kv_heads * ((16 * G + 15) / 16), slots);
+    // the ragged last group runs alone, so it takes clusters sized for its own few blocks
+    const int cx_tail = cx_set ? cx_set : attn_cluster_for((long)O.kv_heads * ((tail * G + 15) / 16), slots);
     igc_kernels_pdl(0);
     const CacheStore kv = layer_store(m, owner, s->d_peak + 2 * owner);
     if (!L.share)
@@ -2130,7 +2132,7 @@ static int enqueue_chunk(igc_session *s, int M, bool head, bool want) {
     if (tail > 0)
       CKL(igc_launch_attn(C.B.qkv + (size_t)16 * full * L.qkv_rows, L.qkv_rows, m->heads, O.kv_heads, L.hd, L.q_norm,
                           L.k_norm, m->rope_cs[L.kind], m->rope_sn[L.kind], m->eps, 0, attn_rows(s, owner, 0),
-                          attn_rows(s, owner, 1), sliding, m->slide_span, C.d_pos + full, tail, cx,
+                          attn_rows(s, owner, 1), sliding, m->slide_span, C.d_pos + full, tail, cx_tail,
                           C.B.attn + (size_t)16 * full * L.q_rows, L.q_rows, nullptr, nullptr, nullptr, s->st,
                           attn_light()));
     igc_kernels_pdl(s->use_pdl != 0);
